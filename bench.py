@@ -1,0 +1,409 @@
+#!/usr/bin/env python
+"""Benchmark: accepted tok/s of the speculative draft -> verify -> accept loop.
+
+Workload: Llama-2-7B-architecture Q4_0 target (seed 0) + TinyLlama-1.1B-
+architecture Q4_0 draft (seed 2), weights N(0, 0.02) -> Q4_0, one 512-token uniform random
+prompt, k = 5, 256 committed tokens, T = 0.  Synthetic GGUF files are written once per box.
+
+A step is one generation of 256 tokens from a fresh prefill.  `value` is committed tokens of
+all ranks / the slowest rank's device time of the generation phase (CUDA events on the
+engine's stream; prefill reported separately); `e2e` is the same count over host wall time of
+the public API call (prompt copied in, tokens copied out, prefill included).  With N GPUs each
+rank decodes its own sequence (replicas, no collective: the single-sequence workload does not
+shard), so scaling is weak.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "universal-loader_b200")
+for p in (ROOT, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "accepted tok/s (Llama-2-7B-arch Q4_0, k=5) at 1-8 B200; verify HBM GB/s vs peak"
+TARGET = dict(n_layer=32, d_model=4096, n_head=32, n_head_kv=32, d_ff=11008, n_vocab=32000, rms_eps=1e-5,
+              rope_base=1e4, wtype="q4_0", seed=0, ctx_len=4096, name="llama2-7b-arch-q4_0-s0")
+DRAFT = dict(n_layer=22, d_model=2048, n_head=32, n_head_kv=4, d_ff=5632, n_vocab=32000, rms_eps=1e-5,
+             rope_base=1e4, wtype="q4_0", seed=2, ctx_len=2048, name="tinyllama-1.1b-arch-q4_0-s2")
+PROMPT_LEN, K_SPEC, NEW_TOKENS = 512, 5, 256
+WORKLOAD = ("C2: Llama-2-7B-arch Q4_0 target + TinyLlama-1.1B-arch Q4_0 draft, B=1 per GPU, "
+            "prompt 512, k=5, 256 new tokens, T=0")
+
+
+def q4_0_bytes(n):
+    return n // 32 * 18
+
+
+def linear_weights(s):
+    hd = s["d_model"] // s["n_head"]
+    d, f = s["d_model"], s["d_ff"]
+    per_layer = d * s["n_head"] * hd * 2 + d * s["n_head_kv"] * hd * 2 + 3 * d * f
+    return s["n_layer"] * per_layer + d * s["n_vocab"]
+
+
+def kv_bytes_per_token(s):
+    hd = s["d_model"] // s["n_head"]
+    return s["n_layer"] * s["n_head_kv"] * hd * 2 * 2
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def model_paths():
+    d = os.environ.get("ULB_BENCH_CACHE", "/tmp/ulb_bench_models")
+    os.makedirs(d, exist_ok=True)
+    return os.path.join(d, TARGET["name"] + ".gguf"), os.path.join(d, DRAFT["name"] + ".gguf")
+
+
+def ensure_models(rank, barrier):
+    import vulkangguf as vg
+    tp, dp = model_paths()
+    if rank == 0:
+        for path, spec in ((tp, TARGET), (dp, DRAFT)):
+            if not os.path.exists(path):
+                t0 = time.time()
+                vg.write_synthetic_gguf(path, spec)
+                print("[bench] wrote %s in %.1fs" % (path, time.time() - t0), file=sys.stderr)
+    barrier()
+    return tp, dp
+
+
+def prompt_for(rank):
+    import numpy as np
+    return np.random.default_rng(1 + 1000 * rank).integers(0, 32000, PROMPT_LEN).astype(np.int32).tolist()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+
+        def barrier():
+            dist.barrier()
+
+        def allmax(x):
+            import torch
+            t = torch.tensor([float(x)], dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        def allsum(x):
+            import torch
+            t = torch.tensor([float(x)], dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            return float(t.item())
+
+        def done():
+            dist.destroy_process_group()
+    else:
+        def barrier():
+            pass
+
+        def allmax(x):
+            return float(x)
+
+        def allsum(x):
+            return float(x)
+
+        def done():
+            pass
+    return world, rank, local, barrier, allmax, allsum, done
+
+
+def gpu_smi_index(local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# ---------------------------------------------------------------- roofline of the GEMV kernel
+def qgemv_roofline(device, reps=10):
+    """Time ulb_qgemm (the fused Q4_0 dequant-GEMV) on the 7B verify shapes (M = k+1 = 6 rows)
+    with CUDA events on the library's stream; 4 layers of distinct matrices (456 MB) are cycled
+    so every launch streams its weights from HBM (working set > L2)."""
+    import numpy as np
+    import ulb_capi as U
+    ctx = U.Context(device)
+    d, f, V = TARGET["d_model"], TARGET["d_ff"], TARGET["n_vocab"]
+    shapes = [(3 * d, d), (d, d), (2 * f, d), (d, f)]
+    rng = np.random.default_rng(0)
+    mats = []
+    try:
+        for _layer in range(4):
+            for (N, K) in shapes:
+                raw = rng.integers(0, 256, (N, K // 32, 18), dtype=np.uint8)
+                raw[:, :, 0:2] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+                mats.append((ctx.upload_tensor(U.T_Q4_0, (K, N), raw.reshape(N, -1)), N, K))
+        M = K_SPEC + 1
+        xb = ctx.buffer(rng.standard_normal((M, f)).astype(np.float16))
+        yb = ctx.buffer(nbytes=M * 2 * f * 4)
+        evs = [(ctx.event(), ctx.event()) for _ in mats]
+        times = {s: [] for s in shapes}
+        for it in range(reps + 2):
+            for (h, N, K), (a, b) in zip(mats, evs):
+                ctx.record(a)
+                U.check(U.lib().ulb_qgemm(ctx.h, h, xb.ptr, M, yb.ptr, N))
+                ctx.record(b)
+            ctx.sync()
+            if it >= 2:
+                for (h, N, K), (a, b) in zip(mats, evs):
+                    times[(N, K)].append(ctx.elapsed_ms(a, b))
+        per = {}
+        tot_b = tot_t = 0.0
+        for (N, K) in shapes:
+            ms = statistics.mean(times[(N, K)])
+            alg = q4_0_bytes(N * K) + M * K * 2 + M * N * 4
+            per["%dx%d" % (N, K)] = {"ms": ms, "gbs": alg / ms / 1e6}
+            tot_b += alg
+            tot_t += ms
+        for h, _, _ in mats:
+            ctx.free_tensor(h)
+        xb.free()
+        yb.free()
+        return {"achieved_gbs": tot_b / tot_t / 1e6, "bytes_per_layer": tot_b, "ms_per_layer": tot_t, "shapes": per}
+    finally:
+        ctx.close()
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_port_rounds(tp, dp, rounds, warp=(0.0, 0, 1.0)):
+    from oracle import ulb_oracle as orc
+    t, d = orc.Model(tp), orc.Model(dp)
+    t0 = time.perf_counter()
+    n, stats = orc.bench_rounds(t, d, PROMPT_LEN, K_SPEC, rounds, warp, seed=0)
+    dt = time.perf_counter() - t0
+    t.close()
+    d.close()
+    return n, dt, stats
+
+
+def cpu_baseline(tp, dp, budget_s=20.0):
+    n, dt, _ = cpu_port_rounds(tp, dp, 1)
+    rounds = 1
+    if dt < budget_s / 3:
+        extra = max(1, int(budget_s / dt) - 1)
+        n2, dt2, _ = cpu_port_rounds(tp, dp, extra)
+        n, dt, rounds = n + n2, dt + dt2, 1 + extra
+    return {"value": n / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": "%d speculative round(s) of the C2 models at context %d (KV caches pre-filled), k=%d, T=0, "
+                      "oracle/oracle.c with OpenMP; %.1f s" % (rounds, PROMPT_LEN, K_SPEC, dt)}
+
+
+def run_reference(args):
+    world, rank, local, barrier, allmax, allsum, done = dist_setup()
+    if rank != 0:
+        done()
+        return 0
+    tp, dp = ensure_models(0, lambda: None)
+    for _ in range(args.warmup):
+        cpu_port_rounds(tp, dp, 1)
+    toks, tsum = 0, 0.0
+    for _ in range(args.steps):
+        n, dt, _ = cpu_port_rounds(tp, dp, 1)
+        toks += n
+        tsum += dt
+    value = toks / tsum
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": tsum / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0xf16->f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "step": "one speculative round at context 512 on the host cores"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": "one round per step of the C2 workload at context %d (KV pre-filled); the "
+                                       "reference's own CPU path cannot run this loop (its engine computes only "
+                                       "Q/K/V and its AVX2 GEMM/dequant are not valid), so the oracle port "
+                                       "stands in" % PROMPT_LEN},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    done()
+    return 0
+
+
+def run_ours(args):
+    world, rank, local, barrier, allmax, allsum, done = dist_setup()
+    smi_index = gpu_smi_index(local)
+    if world > 1:  # one GPU per rank, chosen before CUDA initialises in this process
+        os.environ["CUDA_VISIBLE_DEVICES"] = str(smi_index)
+    import vulkangguf as vg
+    tp, dp = ensure_models(rank, barrier)
+    api = vg.InferenceAPI()
+    if not api.load_model(tp) or not api.load_draft_model(dp):
+        print("[bench] model load failed", file=sys.stderr)
+        return 1
+    api.enable_speculative_decoding(True)
+    api.set_speculation_length(K_SPEC)
+    cfg = vg.GenerationConfig()
+    cfg.max_tokens = NEW_TOKENS
+    cfg.temperature = 0.0
+    cfg.do_sample = False
+    cfg.seed = 0
+    prompt = prompt_for(rank)
+    for _ in range(args.warmup):
+        api.generate_tokens(prompt, cfg)
+    barrier()
+    clocks = ClockSampler(smi_index)
+    clocks.start()
+    t0 = time.perf_counter()
+    toks = 0
+    dec_ms = pre_ms = 0.0
+    launches = 0
+    accepted = drafted = rounds = 0
+    h2d = d2h = 0.0
+    outs = []
+    for _ in range(args.steps):
+        out = api.generate_tokens(prompt, cfg)
+        st = api.get_last_stats()
+        outs.append(out)
+        toks += len(out)
+        dec_ms += st["decode_ms"]
+        pre_ms += st["prefill_ms"]
+        launches += st["launches"]
+        accepted += st["accepted"]
+        drafted += st["drafted"]
+        rounds += st["rounds"]
+        h2d = st["h2d_bytes"]
+        d2h = st["d2h_bytes"]
+    wall = time.perf_counter() - t0
+    barrier()
+    clk = clocks.stop()
+    assert all(o == outs[0] for o in outs), "greedy generation is not deterministic"
+    prof = api.profile_round()
+    tot_toks = allsum(toks)
+    max_dec = allmax(dec_ms)
+    max_wall = allmax(wall)
+    max_step = allmax((dec_ms + pre_ms) / args.steps)
+    tot_launch = allsum(launches)
+    value = tot_toks / (max_dec / 1e3)
+    e2e = tot_toks / max_wall
+    if rank != 0:
+        done()
+        return 0
+    peak, peak_src = load_peaks()
+    ctx_len = PROMPT_LEN + NEW_TOKENS
+    verify_bytes = (q4_0_bytes(linear_weights(TARGET)) + kv_bytes_per_token(TARGET) * ctx_len
+                    + (K_SPEC + 1) * kv_bytes_per_token(TARGET) + (K_SPEC + 1) * TARGET["n_vocab"] * 4)
+    verify_gbs = verify_bytes / (prof["verify_ms"] / 1e3) / 1e9
+    rl = qgemv_roofline(0)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": max_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_0xf16->f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "parallelism": "replicas (one sequence per GPU, no collective)",
+                   "l2": "inputs larger than L2 (3.7 GB of target weights per verify)",
+                   "timed": "generation phase, CUDA events on the engine stream; prefill reported separately"},
+        "acceptance_rate": accepted / drafted if drafted else 0.0,
+        "rounds_per_step": rounds / args.steps,
+        "prefill_ms": pre_ms / args.steps,
+        "decode_ms": dec_ms / args.steps,
+        "round_profile_ms": prof,
+        "verify": {"bytes": verify_bytes, "ms": prof["verify_ms"], "gbs": verify_gbs,
+                   "frac": verify_gbs / peak, "peak": peak, "peak_source": peak_src,
+                   "frac_of_8tbs": verify_gbs / 8000.0},
+        "roofline": {"bound": "hbm", "achieved": rl["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": rl["achieved_gbs"] / peak, "traffic": None,
+                     "kernel": "qgemv_q40_kernel<NT=1> (fused Q4_0 dequant-GEMV, 7B verify shapes, M=6)",
+                     "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
+                     "shapes": rl["shapes"]},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "note": "public API generate_tokens (host prompt in, host tokens out), prefill included"},
+        "gpu_launches": int(tot_launch),
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(tp, dp)
+    print(json.dumps(line), flush=True)
+    done()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,256 @@
+/*
+ * ulb.h — C ABI of libulb_cuda.so, the sm_100a replacement for Universal-Loader's
+ * Vulkan backend (src/vulkan_backend) and its dequantize / gemm / attention shaders
+ * (src/shaders/{dequantize,gemm,attention}) on the speculative draft -> verify ->
+ * accept path.
+ *
+ * Conventions
+ *  - Every function returns ULB_OK (0) or a negative ULB_E* code; no C++ exception
+ *    crosses this boundary.  ulb_last_error() returns the calling thread's message for
+ *    the most recent failure.
+ *  - Pointers named dev_* are device pointers on the context's device; host_* are host
+ *    pointers borrowed for the duration of the call.  Outputs are caller-allocated unless
+ *    a function says otherwise.
+ *  - All work is enqueued on the context's stream (ulb_stream); calls on one context must
+ *    be serialised by the caller (one context per device, one host thread at a time).
+ *  - There is no CPU fallback: without a usable CUDA device ulb_init fails with ULB_ECUDA.
+ */
+#ifndef ULB_H
+#define ULB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ULB_API __attribute__((visibility("default")))
+#else
+#define ULB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status codes */
+#define ULB_OK 0
+#define ULB_EINVAL (-1)      /* bad argument, shape or state                        */
+#define ULB_ENOMEM (-2)      /* device or host allocation failed                    */
+#define ULB_ECUDA (-3)       /* CUDA runtime error                                  */
+#define ULB_ENCCL (-4)       /* NCCL error (tensor-parallel helpers)                */
+#define ULB_ETIMEOUT (-5)    /* a bounded device-side wait gave up                   */
+#define ULB_EFORMAT (-6)     /* malformed GGUF bytes / unsupported tensor layout     */
+#define ULB_EUNSUPPORTED (-7)
+
+/* GGML tensor type ids, as in the reference's ggml::GGMLType (src/core/gguf_types.h:6-33). */
+#define ULB_TYPE_F32 0
+#define ULB_TYPE_F16 1
+#define ULB_TYPE_Q4_0 2
+#define ULB_TYPE_Q4_K 12
+
+typedef struct ulb_ctx ulb_ctx;
+typedef struct ulb_tensor ulb_tensor;
+typedef struct ulb_model ulb_model;
+typedef struct ulb_kv ulb_kv;
+typedef struct ulb_spec ulb_spec;
+
+/* ------------------------------------------------------------------ errors / info */
+/* Replaces the reference's std::cerr + bool returns (vulkan_backend/context.cpp). */
+ULB_API const char* ulb_last_error(void);
+ULB_API const char* ulb_version(void);
+
+/* ------------------------------------------------------------------ context */
+/* Replaces vulkan::VulkanContext construction (src/vulkan_backend/context.cpp) and the
+ * engine's initialize() GPU branch (src/inference/inference_engine.cpp:48-148). */
+ULB_API int ulb_init(int device, ulb_ctx** out);
+ULB_API int ulb_destroy(ulb_ctx* ctx);
+/* The context's cudaStream_t (as void*). */
+ULB_API void* ulb_stream(ulb_ctx* ctx);
+/* Replaces ComputeDispatcher::wait_for_completion (src/vulkan_backend/compute.cpp:82-121). */
+ULB_API int ulb_stream_sync(ulb_ctx* ctx);
+/* Device bytes currently held by the context (weights, caches, workspaces). */
+ULB_API int ulb_mem_used(ulb_ctx* ctx, size_t* out_bytes);
+
+/* Device buffers and copies for callers of the kernels below.  Replaces VulkanMemory::
+ * create_buffer / destroy_buffer and TransferEngine (src/vulkan_backend/memory.cpp,
+ * transfer.cpp).  The copies are synchronous with respect to the host. */
+ULB_API int ulb_malloc(ulb_ctx* ctx, size_t bytes, void** out_dev);
+ULB_API int ulb_free(ulb_ctx* ctx, void* dev);
+ULB_API int ulb_memcpy_h2d(ulb_ctx* ctx, void* dev_dst, const void* host_src, size_t bytes);
+ULB_API int ulb_memcpy_d2h(ulb_ctx* ctx, void* host_dst, const void* dev_src, size_t bytes);
+
+/* CUDA-event timing on the context's stream (replaces vulkan::Profiler timestamp queries,
+ * src/vulkan_backend/profiler.cpp:174-230). */
+ULB_API int ulb_event_create(ulb_ctx* ctx, void** out_event);
+ULB_API int ulb_event_record(ulb_ctx* ctx, void* event);
+ULB_API int ulb_event_elapsed_ms(void* start, void* end, float* out_ms);
+ULB_API int ulb_event_destroy(void* event);
+
+/* ------------------------------------------------------------------ weights */
+/*
+ * Upload one GGUF tensor and repack it into the device layout used by the kernels.
+ * Replaces the reference's repack_q4k_tensor + upload_to_gpu
+ * (src/inference/inference_engine.cpp:536-548, 891-927) and VulkanMemory::create_buffer.
+ *   ggml_type  ULB_TYPE_F32 / F16 / Q4_0 / Q4_K
+ *   ne         GGUF dims, ne[0] = innermost (K for a weight matrix, ne[1] = rows N)
+ *   gguf_bytes host pointer to the tensor's bytes exactly as stored in the GGUF file
+ *   nbytes     must equal the GGUF size of the tensor (18 B / 32 weights for Q4_0,
+ *              144 B / 256 weights for Q4_K) -- ULB_EFORMAT otherwise
+ */
+ULB_API int ulb_tensor_upload(ulb_ctx* ctx, int ggml_type, const uint64_t ne[4],
+                      const void* gguf_bytes, size_t nbytes, ulb_tensor** out);
+ULB_API int ulb_tensor_free(ulb_tensor* t);
+ULB_API int ulb_tensor_info(const ulb_tensor* t, int* out_type, uint64_t out_ne[4], size_t* out_device_bytes);
+
+/* ------------------------------------------------------------------ kernels */
+/*
+ * Bit-exact dequantisation of a whole tensor to fp32, row-major [ne1][ne0].  Parity
+ * helper; replaces dequantize_q4_0.glsl / dequantize_q4_k(_flattened).glsl
+ * (src/shaders/dequantize) and cpu::dequantize_q4_0_f32 / q4_k_f32
+ * (src/cpu_backend/dequantize_cpu.cpp:6-74).
+ */
+ULB_API int ulb_dequant(ulb_ctx* ctx, const ulb_tensor* w, float* dev_out);
+
+/*
+ * Fused dequant-GEMM  y[m*ldy + n] = sum_k W[n][k] * x[m][k]   (fp32 accumulate)
+ *   W      Q4_0 or Q4_K tensor from ulb_tensor_upload, N = ne[1] rows, K = ne[0]
+ *   dev_x  fp16 activations, row-major [M][K]
+ *   dev_y  fp32 output rows with leading dimension ldy >= N
+ * Replaces run_linear_q4k = dequantize_q4_k_flattened + gemm_transposed_b_v2
+ * (src/inference/inference_engine.cpp:532-570) and gemm_dequant_q4_0.glsl /
+ * gemm_coop_dequant_q4_0.glsl (src/shaders/gemm).  Every output row is computed with the
+ * same arithmetic whatever M is, so batching never changes a row's result.
+ */
+ULB_API int ulb_qgemm(ulb_ctx* ctx, const ulb_tensor* w, const uint16_t* dev_x, int M,
+              float* dev_y, int ldy);
+
+/*
+ * Block-causal attention of M query rows against an fp16 KV cache.
+ *   dev_q       fp32 [M][n_head][head_dim] (RoPE already applied)
+ *   dev_k/v     fp16 [n_seq][n_head_kv][capacity][head_dim]
+ *   dev_row_seq int32 [M] sequence of each row;  dev_row_pos int32 [M] its position
+ *   Row m attends keys 0..row_pos[m] of its sequence (GQA: head h reads kv head
+ *   h / (n_head / n_head_kv)).  Rows of one sequence must be consecutive, rows_per_seq each.
+ *   dev_out     fp16 [M][n_head][head_dim]
+ * Replaces flash_attention.glsl and the flash_attention_v2_fused/_v3 feature set
+ * (src/shaders/attention, inference_engine.cpp:628-630).
+ */
+typedef struct ulb_attn_desc {
+  int n_head, n_head_kv, head_dim, capacity, n_seq;
+  float scale; /* usually 1/sqrt(head_dim) */
+} ulb_attn_desc;
+ULB_API int ulb_attention(ulb_ctx* ctx, const ulb_attn_desc* desc, const float* dev_q,
+                  const uint16_t* dev_k, const uint16_t* dev_v, const int32_t* dev_row_seq,
+                  const int32_t* dev_row_pos, int M, int rows_per_seq, uint16_t* dev_out);
+
+/*
+ * Logit warping shared by the draft sampler and the rejection sampler.  Replaces the
+ * intent of TextGenerator::apply_temperature / apply_top_k / apply_top_p
+ * (src/api/gguf_loader.cpp:90-155) and InferenceEngine::sample_token
+ * (src/inference/inference_engine.cpp:340-367).
+ *   temperature <= 0  -> greedy (argmax, lowest index on ties)
+ *   top_k <= 0 or >= V -> off;  top_p <= 0 or >= 1 -> off
+ * Order: logits / T -> keep logits >= k-th largest -> softmax -> keep tokens whose
+ * strictly-more-probable mass is < top_p -> renormalise.
+ */
+typedef struct ulb_warp {
+  float temperature;
+  int top_k;
+  float top_p;
+} ulb_warp;
+
+/* Sample one token per row: u = Philox uniform (seed; round, seq=row, slot, tag). */
+ULB_API int ulb_sample(ulb_ctx* ctx, const float* dev_logits, int rows, int V, int ld,
+               const ulb_warp* warp, uint64_t seed, uint32_t round, uint32_t slot,
+               uint32_t tag, int32_t* dev_out_tokens);
+
+/*
+ * Single-pass speculative rejection sampling (Leviathan et al. 2023; Chen et al. 2023),
+ * replacing SpeculativeDecoder::verify_speculation (src/inference/speculative_decoder.cpp:89-110).
+ *   p_logits [B][k+1][V] target logits, q_logits [B][k][V] draft logits,
+ *   draft_tokens [B][k].  For i = 0..k-1: accept draft i iff u_i * q_i(x_i) < p_i(x_i);
+ *   at the first rejection sample from norm(max(0, p_i - q_i)); if all k are accepted
+ *   sample a bonus from p_k.  Greedy warp: accept iff x_i == argmax p_i, correction /
+ *   bonus = argmax.  Uniforms: tag ULB_RNG_ACCEPT slot i, tag ULB_RNG_RESID slot n.
+ *   out_tokens [B][k+1]: the n accepted drafts followed by the correction/bonus token.
+ *   out_n_accepted [B]: n in 0..k (tokens committed = n + 1).
+ */
+ULB_API int ulb_spec_accept(ulb_ctx* ctx, const float* dev_p_logits, const float* dev_q_logits,
+                    const int32_t* dev_draft_tokens, int B, int k, int V, const ulb_warp* warp,
+                    uint64_t seed, uint32_t round, int32_t* dev_out_tokens,
+                    int32_t* dev_out_n_accepted);
+
+/* ------------------------------------------------------------------ models */
+/*
+ * A LLaMA-family model resident in HBM.  Replaces Model / LayerWeights / KVCache
+ * (src/inference/model.h:37-115, model.cpp:154-254) on the device side.  Tensors are
+ * given by their GGUF names (token_embd.weight, blk.N.attn_q.weight, ..., output.weight).
+ */
+typedef struct ulb_model_desc {
+  int n_layer, d_model, n_head, n_head_kv, head_dim, d_ff, n_vocab;
+  float rms_eps, rope_base;
+  int max_rows; /* largest number of query rows one forward may carry */
+} ulb_model_desc;
+
+ULB_API int ulb_model_create(ulb_ctx* ctx, const ulb_model_desc* desc, ulb_model** out);
+ULB_API int ulb_model_set_weight(ulb_model* m, const char* gguf_name, int ggml_type,
+                         const uint64_t ne[4], const void* gguf_bytes, size_t nbytes);
+/* Check every tensor is present and build the fused device layouts. */
+ULB_API int ulb_model_finalize(ulb_model* m);
+ULB_API int ulb_model_free(ulb_model* m);
+ULB_API int ulb_model_weight_bytes(const ulb_model* m, size_t* out_bytes);
+
+/* KV cache: fp16 [n_layer][n_seq][n_head_kv][capacity][head_dim] for K and for V. */
+ULB_API int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* m, int n_seq, int capacity, ulb_kv** out);
+ULB_API int ulb_kv_free(ulb_kv* kv);
+
+/*
+ * One forward pass of M rows (rows_per_seq consecutive rows per sequence).
+ *   dev_tokens/dev_row_seq/dev_row_pos int32 [M].  K/V of every row are written at
+ *   (seq, pos); row m attends positions 0..pos of its sequence.
+ *   logits_mode 0: logits for all M rows -> dev_logits[m*ld + v]
+ *   logits_mode 1: logits only for the last row of each sequence -> dev_logits[s*ld + v]
+ */
+ULB_API int ulb_model_forward(ulb_ctx* ctx, ulb_model* m, ulb_kv* kv, int M, int rows_per_seq,
+                      const int32_t* dev_tokens, const int32_t* dev_row_seq,
+                      const int32_t* dev_row_pos, int logits_mode, float* dev_logits, int ld);
+
+/* ------------------------------------------------------------------ speculative loop */
+/*
+ * Device-resident draft -> verify -> accept loop.  Replaces SpeculativeDecoder
+ * (src/inference/speculative_decoder.h:24-60, .cpp:25-116) and the engine's decode loop
+ * (src/inference/inference_engine.cpp:273-328).  With draft == NULL (or k == 0) each round
+ * is one target step (plain decoding) through the same code.
+ */
+typedef struct ulb_spec_desc {
+  int n_seq;        /* sequences decoded together                           */
+  int k;            /* draft tokens per round (speculation length)          */
+  int max_prompt;   /* longest prompt                                       */
+  int max_new;      /* tokens to commit per sequence                        */
+  ulb_warp warp;    /* applied identically to target and draft               */
+  uint64_t seed;    /* Philox key                                           */
+  int use_graphs;   /* 1: capture each round into a CUDA graph              */
+} ulb_spec_desc;
+
+ULB_API int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft,
+                    const ulb_spec_desc* desc, ulb_spec** out);
+/* Copy prompts (host int32 [n_seq][max_prompt], lengths [n_seq]) and prefill both models;
+ * commits the first generated token of every sequence. */
+ULB_API int ulb_spec_prefill(ulb_spec* s, const int32_t* host_prompts, const int32_t* host_prompt_lens);
+/* Run rounds until every sequence has max_new tokens or max_rounds rounds ran. */
+ULB_API int ulb_spec_run(ulb_spec* s, int max_rounds, int* out_rounds);
+/* host_tokens int32 [n_seq][max_new], host_counts [n_seq];
+ * stats: [0] rounds, [1] drafted tokens, [2] accepted drafts, [3] committed tokens. */
+ULB_API int ulb_spec_read(ulb_spec* s, int32_t* host_tokens, int32_t* host_counts, uint64_t stats[4]);
+ULB_API int ulb_spec_free(ulb_spec* s);
+/* Run one round outside any CUDA graph with events between its phases:
+ * ms[0] draft steps, ms[1] verify forward, ms[2] accept.  Sequences already done are computed
+ * but nothing is committed for them.  Replaces the reference's never-constructed
+ * vulkan::Profiler timestamps (src/vulkan_backend/profiler.cpp:174-230). */
+ULB_API int ulb_spec_profile_round(ulb_spec* s, float ms[3]);
+/* Kernels this loop launched since its last prefill (prefill and every round included). */
+ULB_API int ulb_spec_launch_count(ulb_spec* s, uint64_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ULB_H */

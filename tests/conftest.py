@@ -1,0 +1,84 @@
+"""Shared fixtures.  GPU tests are marked `gpu`; everything else runs on the CPU."""
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "universal-loader_b200")
+for p in (ROOT, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+# The tiny speculative pair of the CPU-runnable configuration: LLaMA d=512, 8 heads (hd 64),
+# SwiGLU 1408, vocab 32000, eps 1e-5, theta 1e4; target 8 layers, draft 2 layers, both from
+# seed 0 so the draft shares the target's first two blocks, embeddings and head.
+TINY_TARGET = dict(n_layer=8, d_model=512, n_head=8, n_head_kv=8, d_ff=1408, n_vocab=32000,
+                   rms_eps=1e-5, rope_base=1e4, wtype="q4_0", seed=0, name="tiny-target")
+TINY_DRAFT = dict(TINY_TARGET, n_layer=2, name="tiny-draft")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
+
+
+def _build():
+    from oracle import build as obuild
+    obuild.build()
+    sys.path.insert(0, PKG)
+    import build as pbuild  # universal-loader_b200/build.py
+    pbuild.build()
+
+
+@pytest.fixture(scope="session", autouse=True)
+def built():
+    _build()
+    return True
+
+
+@pytest.fixture(scope="session")
+def model_dir(tmp_path_factory):
+    return tmp_path_factory.mktemp("models")
+
+
+def _synth(model_dir, spec, name):
+    import vulkangguf as vg
+    path = os.path.join(str(model_dir), name)
+    if not os.path.exists(path):
+        vg.write_synthetic_gguf(path, spec)
+    return path
+
+
+@pytest.fixture(scope="session")
+def tiny_target(model_dir):
+    return _synth(model_dir, TINY_TARGET, "tiny_target.gguf")
+
+
+@pytest.fixture(scope="session")
+def tiny_draft(model_dir):
+    return _synth(model_dir, TINY_DRAFT, "tiny_draft.gguf")
+
+
+@pytest.fixture(scope="session")
+def tiny_gqa_q4k(model_dir):
+    spec = dict(n_layer=3, d_model=512, n_head=8, n_head_kv=2, d_ff=1536, n_vocab=4096,
+                rms_eps=1e-5, rope_base=5e5, wtype="q4_k", seed=3, name="tiny-gqa-q4k")
+    return _synth(model_dir, spec, "tiny_gqa_q4k.gguf")
+
+
+def has_gpu():
+    try:
+        import ulb_capi
+        ctx = ulb_capi.Context(0)
+        ctx.close()
+        return True
+    except Exception:
+        return False
+
+
+@pytest.fixture(scope="session")
+def ctx():
+    import ulb_capi
+    c = ulb_capi.Context(0)
+    yield c
+    c.close()

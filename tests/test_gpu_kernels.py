@@ -1,0 +1,224 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle, through the C ABI.
+
+Bars: dequantised weights bit-exact; GEMM relative error <= 1e-2 of the fp32-accumulate
+oracle (observed ~1e-6: both apply each block's scale to an exact integer dot product);
+attention within 2e-3 absolute on fp16 outputs; identical accept/reject decisions and
+sampled tokens when both sides get the same logits and Philox uniforms."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import gguf
+from oracle import ulb_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+GEMM_RTOL = 1e-2  # GEMM outputs within 1e-2 relative error (fp32 accumulate)
+
+
+def _q40(rng, N, K):
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    return gguf.quants.quantize(w, gguf.GGMLQuantizationType.Q4_0)
+
+
+def _q4k(rng, N, K):
+    b = rng.integers(0, 256, (N * K // 256, 144), dtype=np.uint8)
+    d = (np.abs(rng.standard_normal(N * K // 256)) * 0.002 + 1e-4).astype(np.float16)
+    dm = (np.abs(rng.standard_normal(N * K // 256)) * 0.002).astype(np.float16)
+    b[:, 0:2] = d.view(np.uint8).reshape(-1, 2)
+    b[:, 2:4] = dm.view(np.uint8).reshape(-1, 2)
+    return b.reshape(N, -1)
+
+
+def _rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.mark.parametrize("qt,N,K", [("q4_0", 48, 256), ("q4_0", 4096, 4096), ("q4_k", 32, 512),
+                                    ("q4_k", 11008, 4096), ("q4_0", 1000, 1408)])
+def test_dequant_bit_exact(ctx, qt, N, K):
+    rng = np.random.default_rng(N + K)
+    raw = _q40(rng, N, K) if qt == "q4_0" else _q4k(rng, N, K)
+    t = orc.T_Q4_0 if qt == "q4_0" else orc.T_Q4_K
+    h = ctx.upload_tensor(t, (K, N), raw)
+    try:
+        got = ctx.dequant(h, N, K)
+    finally:
+        ctx.free_tensor(h)
+    want = orc.dequant(t, raw, N * K).reshape(N, K)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    ref = gguf.quants.dequantize(raw.reshape(-1, 18 if qt == "q4_0" else 144),
+                                 gguf.GGMLQuantizationType.Q4_0 if qt == "q4_0" else
+                                 gguf.GGMLQuantizationType.Q4_K).reshape(N, K)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
+@pytest.mark.parametrize("M", [1, 2, 5, 8, 13, 16, 33, 64, 70])
+def test_qgemm_matches_oracle_small(ctx, qt, M):
+    rng = np.random.default_rng(100 + M)
+    N, K = 208, 1024
+    raw = _q40(rng, N, K) if qt == "q4_0" else _q4k(rng, N, K)
+    t = orc.T_Q4_0 if qt == "q4_0" else orc.T_Q4_K
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    h = ctx.upload_tensor(t, (K, N), raw)
+    try:
+        y = ctx.qgemm(h, x, N)
+    finally:
+        ctx.free_tensor(h)
+    ref = orc.qgemv(t, raw, N, K, x)
+    assert _rel(y, ref) < 1e-5, _rel(y, ref)
+
+
+@pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
+@pytest.mark.parametrize("NK", [(4096, 4096), (11008, 4096), (4096, 11008)])
+@pytest.mark.parametrize("M", [1, 5, 8, 16, 64, 256])
+def test_qgemm_op_sweep(ctx, qt, NK, M):
+    """Config-3 op sweep shapes: every (N, K) x M, Q4_0 and Q4_K, x ~ fp16 N(0,1)."""
+    N, K = NK
+    rng = np.random.default_rng(N * 7 + K + M)
+    raw = _q40(rng, N, K) if qt == "q4_0" else _q4k(rng, N, K)
+    t = orc.T_Q4_0 if qt == "q4_0" else orc.T_Q4_K
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    h = ctx.upload_tensor(t, (K, N), raw)
+    try:
+        y = ctx.qgemm(h, x, N)
+        y_last = ctx.qgemm(h, x[M - 1:M], N)[0]
+    finally:
+        ctx.free_tensor(h)
+    rows = min(M, 8)  # the oracle checks a subset of rows at the large shapes
+    ref = orc.qgemv(t, raw, N, K, x[:rows])
+    assert _rel(y[:rows], ref) < GEMM_RTOL
+    assert _rel(y[:rows], ref) < 1e-4
+    # every row is computed with the same arithmetic whatever M is
+    assert np.array_equal(y_last, y[M - 1])
+
+
+def test_qgemm_rows_independent_of_batch(ctx):
+    rng = np.random.default_rng(1)
+    N, K = 512, 2048
+    raw = _q40(rng, N, K)
+    x = rng.standard_normal((6, K)).astype(np.float16)
+    h = ctx.upload_tensor(orc.T_Q4_0, (K, N), raw)
+    try:
+        y6 = ctx.qgemm(h, x, N)
+        for m in range(6):
+            assert np.array_equal(ctx.qgemm(h, x[m:m + 1], N)[0], y6[m])
+    finally:
+        ctx.free_tensor(h)
+
+
+def _attn_case(ctx, H, Hkv, hd, S, rps, positions, seed):
+    import ulb_capi as U
+    rng = np.random.default_rng(seed)
+    cap = max(max(p) for p in positions) + 3
+    M = S * rps
+    q = rng.standard_normal((M, H * hd)).astype(np.float32)
+    k = (rng.standard_normal((S, Hkv, cap, hd))).astype(np.float16)
+    v = (rng.standard_normal((S, Hkv, cap, hd))).astype(np.float16)
+    row_seq = np.repeat(np.arange(S, dtype=np.int32), rps)
+    row_pos = np.concatenate([np.asarray(p, np.int32) for p in positions])
+    want = orc.attention(H, Hkv, hd, cap, 1.0 / np.sqrt(hd), q, k.view(np.uint16), v.view(np.uint16),
+                         row_seq, row_pos)
+    bufs = [ctx.buffer(a) for a in (q, k, v, row_seq, row_pos)]
+    out = ctx.buffer(nbytes=M * H * hd * 2)
+    d = U.AttnDesc(H, Hkv, hd, cap, S, 1.0 / np.sqrt(hd))
+    U.check(U.lib().ulb_attention(ctx.h, C.byref(d), bufs[0].ptr, bufs[1].ptr, bufs[2].ptr, bufs[3].ptr,
+                                  bufs[4].ptr, M, rps, out.ptr))
+    got = out.download(np.float16, (M, H * hd))
+    for b in bufs + [out]:
+        b.free()
+    return got.astype(np.float32), want.astype(np.float32)
+
+
+@pytest.mark.parametrize("H,Hkv,hd,S,rps,positions", [
+    (32, 32, 128, 1, 6, [[639, 640, 641, 642, 643, 644]]),        # 7B verify rows (k=5)
+    (32, 4, 64, 1, 2, [[700, 701]]),                               # TinyLlama draft step 0
+    (32, 4, 64, 1, 1, [[63]]),                                     # single chunk
+    (8, 8, 64, 3, 5, [[10, 11, 12, 13, 14], [127, 128, 129, 130, 131], [0, 1, 2, 3, 4]]),
+    (32, 8, 128, 2, 9, [list(range(300, 309)), list(range(4000, 4009))]),  # Llama-3 GQA k=8
+    (8, 8, 64, 1, 64, [list(range(0, 64))]),                       # prefill chunk
+])
+def test_attention_matches_oracle(ctx, H, Hkv, hd, S, rps, positions):
+    got, want = _attn_case(ctx, H, Hkv, hd, S, rps, positions, seed=H + hd + S)
+    assert np.abs(got - want).max() < 2e-3
+
+
+def _sample_gpu(ctx, logits, warp, seed, rnd, slot, tag):
+    import ulb_capi as U
+    rows, V = logits.shape
+    lb = ctx.buffer(np.ascontiguousarray(logits, np.float32))
+    ob = ctx.buffer(nbytes=rows * 4)
+    w = U.Warp(*warp)
+    U.check(U.lib().ulb_sample(ctx.h, lb.ptr, rows, V, V, C.byref(w), seed, rnd, slot, tag, ob.ptr))
+    out = ob.download(np.int32, (rows,))
+    lb.free(); ob.free()
+    return out
+
+
+@pytest.mark.parametrize("warp", [(0.0, 0, 1.0), (0.8, 40, 1.0), (1.0, 0, 1.0), (0.8, 0, 0.9),
+                                  (1.2, 100, 0.5)])
+def test_sample_matches_oracle(ctx, warp):
+    rng = np.random.default_rng(4)
+    rows, V = 24, 32000
+    logits = (rng.standard_normal((rows, V)) * 3).astype(np.float32)
+    got = _sample_gpu(ctx, logits, warp, seed=77, rnd=3, slot=1, tag=1)
+    want = [orc.sample(logits[r], orc.uniform(77, 3, r, 1, 1), *warp) for r in range(rows)]
+    assert got.tolist() == want
+
+
+def test_sample_top_p_large_vocab(ctx):
+    rng = np.random.default_rng(8)
+    rows, V = 6, 128256
+    logits = (rng.standard_normal((rows, V)) * 2).astype(np.float32)
+    warp = (0.8, 0, 0.9)
+    got = _sample_gpu(ctx, logits, warp, seed=5, rnd=0, slot=0, tag=1)
+    want = [orc.sample(logits[r], orc.uniform(5, 0, r, 0, 1), *warp) for r in range(rows)]
+    assert got.tolist() == want
+
+
+def _accept_gpu(ctx, pl, ql, draft, warp, seed, rnd):
+    import ulb_capi as U
+    B, k = draft.shape
+    V = pl.shape[-1]
+    bufs = [ctx.buffer(np.ascontiguousarray(a)) for a in (pl, ql if k else np.zeros(4, np.float32),
+                                                          draft if k else np.zeros(4, np.int32))]
+    ot = ctx.buffer(nbytes=B * (k + 1) * 4)
+    on = ctx.buffer(nbytes=B * 4)
+    w = U.Warp(*warp)
+    U.check(U.lib().ulb_spec_accept(ctx.h, bufs[0].ptr, bufs[1].ptr, bufs[2].ptr, B, k, V, C.byref(w),
+                                    seed, rnd, ot.ptr, on.ptr))
+    out = ot.download(np.int32, (B, k + 1))
+    n = on.download(np.int32, (B,))
+    for b in bufs + [ot, on]:
+        b.free()
+    return out, n
+
+
+@pytest.mark.parametrize("warp", [(0.0, 0, 1.0), (1.0, 0, 1.0), (0.8, 40, 1.0), (0.8, 0, 0.9)])
+def test_spec_accept_matches_oracle(ctx, warp):
+    """Config-3 rejection shapes: p [64, 9, 32000], q [64, 8, 32000] ~ N(0, 3); draft ~ q."""
+    rng = np.random.default_rng(12)
+    B, k, V = 64, 8, 32000
+    pl = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
+    ql = (rng.standard_normal((B, k, V)) * 3).astype(np.float32)
+    # make some drafts agree with the target so accept paths are exercised
+    ql[: B // 2] = pl[: B // 2, :k] + 0.3 * ql[: B // 2]
+    draft = np.array([[orc.sample(ql[b, i], orc.uniform(9, 0, b, i, 1), *warp) for i in range(k)]
+                      for b in range(B)], np.int32)
+    got_t, got_n = _accept_gpu(ctx, pl, ql, draft, warp, seed=9, rnd=4)
+    want_t, want_n = orc.spec_accept(pl, ql, draft, warp, seed=9, rnd=4)
+    assert got_n.tolist() == want_n.tolist()
+    for b in range(B):
+        assert got_t[b, :want_n[b] + 1].tolist() == want_t[b, :want_n[b] + 1].tolist()
+    assert want_n.max() > 0 and want_n.min() < k  # both branches covered
+
+
+def test_spec_accept_k0_is_plain_sampling(ctx):
+    rng = np.random.default_rng(2)
+    pl = (rng.standard_normal((4, 1, 1000))).astype(np.float32)
+    got_t, got_n = _accept_gpu(ctx, pl, None, np.zeros((4, 0), np.int32), (1.0, 0, 1.0), 3, 7)
+    want_t, want_n = orc.spec_accept(pl, np.zeros((4, 0, 1000), np.float32), np.zeros((4, 0), np.int32),
+                                     (1.0, 0, 1.0), 3, 7)
+    assert (got_n == 0).all() and got_t[:, 0].tolist() == want_t[:, 0].tolist()

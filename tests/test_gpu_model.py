@@ -1,0 +1,174 @@
+"""GPU parity of whole forwards and of the speculative loop against the CPU oracle.
+
+The tiny configuration (target d=512, 8 layers; draft 2 layers sharing the target's first
+blocks) runs on both sides from the same GGUF files.  Greedy (T=0) token streams of 256
+tokens must be identical; the oracle also reports the smallest top-2 logit margin it saw, so
+a mismatch can be told apart from a near-tie."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle import ulb_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _prompt(n, seed=1, vocab=32000):
+    return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int32)
+
+
+class GpuModel:
+    """ulb_model_* through the C ABI, fed from a GGUF file read by the oracle's reader."""
+
+    def __init__(self, ctx, path):
+        import ulb_capi as U
+        self.U, self.ctx = U, ctx
+        om = orc.Model(path)
+        d = om.desc
+        self.desc = d
+        md = U.ModelDesc(d.n_layer, d.d_model, d.n_head, d.n_head_kv, d.head_dim, d.d_ff, d.n_vocab,
+                         d.rms_eps, d.rope_base, 64)
+        h = C.c_void_p()
+        U.check(U.lib().ulb_model_create(ctx.h, C.byref(md), C.byref(h)))
+        self.h = h
+        names = ["token_embd.weight", "output_norm.weight", "output.weight"]
+        for l in range(d.n_layer):
+            names += ["blk.%d.%s.weight" % (l, s) for s in
+                      ("attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm", "ffn_gate",
+                       "ffn_up", "ffn_down")]
+        for nm in names:
+            t, ne, raw = om.tensor(nm)
+            ne4 = (C.c_uint64 * 4)(*ne)
+            U.check(U.lib().ulb_model_set_weight(h, nm.encode(), t, ne4, raw.ctypes.data_as(C.c_void_p),
+                                                 raw.nbytes))
+        U.check(U.lib().ulb_model_finalize(h))
+        self.om = om
+
+    def kv(self, n_seq, cap):
+        kv = C.c_void_p()
+        self.U.check(self.U.lib().ulb_kv_alloc(self.ctx.h, self.h, n_seq, cap, C.byref(kv)))
+        return kv
+
+    def forward(self, kv, tokens, seq, pos, rps, logits_mode=0):
+        M = len(tokens)
+        V = self.desc.n_vocab
+        bt, bs, bp = (self.ctx.buffer(np.asarray(a, np.int32)) for a in (tokens, seq, pos))
+        n_out = M // rps if logits_mode == 1 else M
+        bl = self.ctx.buffer(nbytes=n_out * V * 4)
+        self.U.check(self.U.lib().ulb_model_forward(self.ctx.h, self.h, kv, M, rps, bt.ptr, bs.ptr, bp.ptr,
+                                                    logits_mode, bl.ptr, V))
+        out = bl.download(np.float32, (n_out, V))
+        for b in (bt, bs, bp, bl):
+            b.free()
+        return out
+
+    def close(self):
+        self.U.lib().ulb_model_free(self.h)
+
+
+def test_forward_matches_oracle(ctx, tiny_target):
+    gm = GpuModel(ctx, tiny_target)
+    try:
+        cap = 200
+        kvg = gm.kv(2, cap)
+        kvo = orc.KV(gm.om, 2, cap)
+        # prefill 64 rows of sequence 0 and 40 rows of sequence 1, then a 5-row verify block
+        for s, n in ((0, 64), (1, 40)):
+            toks = _prompt(n, seed=10 + s)
+            g = gm.forward(kvg, toks, [s] * n, range(n), n, logits_mode=1)
+            o = orc.forward(gm.om, kvo, toks, [s] * n, list(range(n)), n, logits_mode=1)
+            assert np.abs(g - o).max() / np.abs(o).max() < 1e-4
+        toks = np.concatenate([_prompt(5, 20), _prompt(5, 21)])
+        seq = [0] * 5 + [1] * 5
+        pos = list(range(64, 69)) + list(range(40, 45))
+        g = gm.forward(kvg, toks, seq, pos, 5)
+        o = orc.forward(gm.om, kvo, toks, seq, pos, 5)
+        assert np.abs(g - o).max() / np.abs(o).max() < 1e-4
+        assert (g.argmax(1) == o.argmax(1)).all()
+        gm.U.lib().ulb_kv_free(kvg)
+    finally:
+        gm.close()
+
+
+def _api(target, draft=None, k=4):
+    import vulkangguf as vg
+    api = vg.InferenceAPI()
+    assert api.load_model(target)
+    if draft:
+        assert api.load_draft_model(draft)
+        api.enable_speculative_decoding(True)
+        api.set_speculation_length(k)
+    return api
+
+
+def _cfg(n, temperature=0.0, top_k=0, top_p=1.0, seed=0):
+    import vulkangguf as vg
+    c = vg.GenerationConfig()
+    c.max_tokens = n
+    c.temperature = temperature
+    c.top_k = top_k
+    c.top_p = top_p
+    c.do_sample = temperature > 0
+    c.seed = seed
+    return c
+
+
+def test_greedy_spec_stream_matches_oracle(tiny_target, tiny_draft):
+    """Config 1 shapes at T=0: 128-token prompt, k=4, 256 tokens, identical to the oracle."""
+    prompt = _prompt(128, seed=1)
+    api = _api(tiny_target, tiny_draft, k=4)
+    got = api.generate_tokens(prompt.tolist(), _cfg(256))
+    st = api.get_last_stats()
+    t, d = orc.Model(tiny_target), orc.Model(tiny_draft)
+    want, cnt, stats, margin = orc.spec_generate(t, d, [prompt], 256, 4, (0.0, 0, 1.0), seed=0)
+    assert len(got) == 256
+    assert got == want[0].tolist(), "first mismatch at %d (oracle min top-2 margin %.3g)" % (
+        next(i for i in range(256) if got[i] != want[0][i]), margin)
+    assert st["rounds"] == stats[0] and st["accepted"] == stats[2]
+
+
+def test_sampled_spec_stream_matches_oracle(tiny_target, tiny_draft):
+    """Config 1 exactly: T=0.8, top_k=40, Philox seed 0, 256 tokens."""
+    prompt = _prompt(128, seed=1)
+    api = _api(tiny_target, tiny_draft, k=4)
+    got = api.generate_tokens(prompt.tolist(), _cfg(256, 0.8, 40, 1.0, seed=0))
+    t, d = orc.Model(tiny_target), orc.Model(tiny_draft)
+    want, cnt, stats, _ = orc.spec_generate(t, d, [prompt], 256, 4, (0.8, 40, 1.0), seed=0)
+    assert got == want[0].tolist()
+    assert api.get_acceptance_rate() == pytest.approx(stats[2] / stats[1])
+
+
+def test_spec_equals_plain_greedy(tiny_target, tiny_draft):
+    """Speculative decoding at T=0 commits exactly the target's greedy stream."""
+    prompt = _prompt(100, seed=3)
+    spec = _api(tiny_target, tiny_draft, k=5).generate_tokens(prompt.tolist(), _cfg(200))
+    plain = _api(tiny_target).generate_tokens(prompt.tolist(), _cfg(200))
+    assert spec == plain
+
+
+def test_batch_of_sequences_matches_oracle(tiny_target, tiny_draft):
+    prompts = [_prompt(n, seed=30 + n) for n in (17, 64, 90)]
+    api = _api(tiny_target, tiny_draft, k=3)
+    got = api.generate_tokens([p.tolist() for p in prompts], _cfg(48, 1.0, 0, 0.9, seed=5))
+    t, d = orc.Model(tiny_target), orc.Model(tiny_draft)
+    want, cnt, stats, _ = orc.spec_generate(t, d, prompts, 48, 3, (1.0, 0, 0.9), seed=5)
+    assert [g for g in got] == [w.tolist() for w in want]
+
+
+def test_gqa_q4k_model_matches_oracle(tiny_gqa_q4k):
+    prompt = _prompt(70, seed=4, vocab=4096)
+    api = _api(tiny_gqa_q4k)
+    got = api.generate_tokens(prompt.tolist(), _cfg(64))
+    t = orc.Model(tiny_gqa_q4k)
+    want, _, _, margin = orc.spec_generate(t, None, [prompt], 64, 0, (0.0, 0, 1.0), seed=0)
+    assert got == want[0].tolist(), margin
+
+
+def test_token_logits_api(tiny_target):
+    api = _api(tiny_target)
+    toks = _prompt(70, seed=2)
+    got = np.array(api.get_token_logits(toks.tolist()), np.float32)
+    om = orc.Model(tiny_target)
+    want = orc.forward(om, orc.KV(om, 1, 70), toks, [0] * 70, list(range(70)), 70, logits_mode=1)[0]
+    assert np.abs(got - want).max() / np.abs(want).max() < 1e-4

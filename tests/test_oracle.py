@@ -1,0 +1,224 @@
+"""CPU tests of the oracle: pinned against the GGUF format oracle (the `gguf` package),
+published Philox4x32-10 known-answer vectors, hand-built blocks and mathematical known
+answers.  The oracle is the checker of the CUDA path, so it is checked first."""
+import numpy as np
+import pytest
+
+import gguf
+from oracle import ulb_oracle as orc
+
+
+# ---------------------------------------------------------------- Philox4x32-10
+# Known-answer vectors of the Random123 distribution (kat_vectors, philox4x32_10).
+PHILOX_KAT = [
+    ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+    ((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2, (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+    ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+     (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+]
+
+
+@pytest.mark.parametrize("ctr,key,want", PHILOX_KAT)
+def test_philox_known_answers(ctr, key, want):
+    assert tuple(int(x) for x in orc.philox(ctr, key)) == want
+
+
+def _philox_py(ctr, key):
+    """independent pure-Python restatement for cross-checking random counters"""
+    c = list(ctr)
+    k = list(key)
+    for _ in range(10):
+        p0 = 0xD2511F53 * c[0]
+        p1 = 0xCD9E8D57 * c[2]
+        c = [((p1 >> 32) ^ c[1] ^ k[0]) & 0xFFFFFFFF, p1 & 0xFFFFFFFF,
+             ((p0 >> 32) ^ c[3] ^ k[1]) & 0xFFFFFFFF, p0 & 0xFFFFFFFF]
+        k = [(k[0] + 0x9E3779B9) & 0xFFFFFFFF, (k[1] + 0xBB67AE85) & 0xFFFFFFFF]
+    return tuple(c)
+
+
+def test_philox_random_counters():
+    rng = np.random.default_rng(7)
+    for _ in range(200):
+        ctr = tuple(int(x) for x in rng.integers(0, 2**32, 4))
+        key = tuple(int(x) for x in rng.integers(0, 2**32, 2))
+        assert tuple(int(x) for x in orc.philox(ctr, key)) == _philox_py(ctr, key)
+
+
+def test_uniform_is_top24_bits():
+    seed = 0x1234_5678_9ABC_DEF0
+    o = _philox_py((3, 1, 2, 2), (seed & 0xFFFFFFFF, seed >> 32))
+    assert orc.uniform(seed, 3, 1, 2, 2) == (o[0] >> 8) / 16777216.0
+
+
+# ---------------------------------------------------------------- block formats
+def _q4_0_block(d_bits, nibbles):
+    """hand-built GGUF Q4_0 block: fp16 d then 16 bytes (low nibble = w[j], high = w[j+16])"""
+    b = np.zeros(18, np.uint8)
+    b[0:2] = np.frombuffer(np.uint16(d_bits).tobytes(), np.uint8)
+    for j in range(16):
+        b[2 + j] = nibbles[j] | (nibbles[j + 16] << 4)
+    return b
+
+
+def test_q4_0_hand_built_block():
+    nib = np.arange(32) % 16
+    blk = _q4_0_block(0x3C00, nib)  # d = 1.0
+    out = orc.dequant(orc.T_Q4_0, blk, 32)
+    np.testing.assert_array_equal(out, (nib - 8).astype(np.float32))
+    ref = gguf.quants.dequantize(blk.reshape(1, 18), gguf.GGMLQuantizationType.Q4_0).ravel()
+    np.testing.assert_array_equal(out, ref)
+
+
+def test_q4_0_subnormal_and_negative_scale():
+    nib = (np.arange(32) * 7) % 16
+    for d_bits in (0x0001, 0x03FF, 0x8001, 0xBC00, 0x7BFF):  # subnormals, -1, max
+        blk = _q4_0_block(d_bits, nib)
+        out = orc.dequant(orc.T_Q4_0, blk, 32)
+        ref = gguf.quants.dequantize(blk.reshape(1, 18), gguf.GGMLQuantizationType.Q4_0).ravel()
+        assert np.array_equal(out.view(np.uint32), ref.view(np.uint32)), hex(d_bits)
+
+
+def _random_q4k_blocks(n, seed):
+    rng = np.random.default_rng(seed)
+    b = rng.integers(0, 256, (n, 144), dtype=np.uint8)
+    # finite, mixed-sign fp16 d / dmin including subnormals
+    d = rng.choice(np.array([0x3C00, 0x2E66, 0x0001, 0x03FF, 0x1800, 0xB400], np.uint16), n)
+    dm = rng.choice(np.array([0x3800, 0x2A00, 0x0002, 0x0000, 0x1C00], np.uint16), n)
+    b[:, 0:2] = d.view(np.uint8).reshape(n, 2)
+    b[:, 2:4] = dm.view(np.uint8).reshape(n, 2)
+    return b
+
+
+def test_q4_k_decode_matches_gguf_bit_exact():
+    blocks = _random_q4k_blocks(64, 11)
+    out = orc.dequant(orc.T_Q4_K, blocks, 64 * 256)
+    ref = gguf.quants.dequantize(blocks, gguf.GGMLQuantizationType.Q4_K).ravel()
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+def test_q4_k_scale_min_corner_cases():
+    # all 6-bit scale / min bits set, d = dmin = 1: sc = m = 63 for every sub-block
+    b = np.zeros((1, 144), np.uint8)
+    b[0, 0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+    b[0, 2:4] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+    b[0, 4:16] = 0xFF
+    b[0, 16:] = 0x5F  # low nibble 15, high nibble 5
+    out = orc.dequant(orc.T_Q4_K, b, 256)
+    ref = gguf.quants.dequantize(b, gguf.GGMLQuantizationType.Q4_K).ravel()
+    np.testing.assert_array_equal(out, ref)
+    assert set(np.unique(out)) == {63 * 15 - 63.0, 63 * 5 - 63.0}
+
+
+def test_q4_0_random_tensor_bit_exact():
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((64, 256)) * 0.02).astype(np.float32)
+    q = gguf.quants.quantize(x, gguf.GGMLQuantizationType.Q4_0)
+    out = orc.dequant(orc.T_Q4_0, q, x.size)
+    ref = gguf.quants.dequantize(q, gguf.GGMLQuantizationType.Q4_0).ravel()
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+def test_oracle_quantizer_matches_gguf():
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal((16, 512)) * 0.02).astype(np.float32)
+    x[0, :32] = 0.0  # all-zero block
+    q = gguf.quants.quantize(x, gguf.GGMLQuantizationType.Q4_0).ravel()
+    assert np.array_equal(orc.quantize_q4_0(x), q)
+
+
+# ---------------------------------------------------------------- GEMV structure
+@pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
+@pytest.mark.parametrize("M", [1, 5, 8])
+def test_qgemv_matches_float64_dot(qt, M):
+    rng = np.random.default_rng(M)
+    N, K = 48, 512
+    if qt == "q4_0":
+        t = orc.T_Q4_0
+        w = gguf.quants.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32),
+                                 gguf.GGMLQuantizationType.Q4_0)
+        wf = gguf.quants.dequantize(w, gguf.GGMLQuantizationType.Q4_0).reshape(N, K)
+    else:
+        t = orc.T_Q4_K
+        w = _random_q4k_blocks(N * K // 256, M)
+        wf = gguf.quants.dequantize(w, gguf.GGMLQuantizationType.Q4_K).reshape(N, K)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    y = orc.qgemv(t, w, N, K, x)
+    ref = x.astype(np.float64) @ wf.astype(np.float64).T
+    rel = np.abs(y - ref).max() / np.abs(ref).max()
+    assert rel < 1e-5, rel
+
+
+# ---------------------------------------------------------------- sampling known answers
+def test_warp_probs_greedy_and_topk():
+    logits = np.array([0.5, 3.0, -1.0, 3.0, 2.0], np.float32)
+    p = orc.warp_probs(logits, temperature=0.0)
+    np.testing.assert_array_equal(p, [0, 1, 0, 0, 0])  # lowest index on ties
+    p = orc.warp_probs(logits, temperature=1.0, top_k=2)
+    assert p[1] == p[3] and p[0] == p[2] == p[4] == 0 and abs(p.sum() - 1) < 1e-15
+    p = orc.warp_probs(logits, temperature=1.0, top_k=3)
+    assert (p > 0).sum() == 3 and p[4] > 0
+
+
+def test_warp_probs_top_p():
+    logits = np.log(np.array([0.5, 0.3, 0.15, 0.05], np.float64)).astype(np.float32)
+    p = orc.warp_probs(logits, temperature=1.0, top_p=0.7)  # keeps 0.5 and 0.3
+    assert (p > 0).tolist() == [True, True, False, False]
+    p = orc.warp_probs(logits, temperature=1.0, top_p=0.5)  # first token alone reaches 0.5
+    assert (p > 0).tolist() == [True, False, False, False]
+
+
+def test_accept_p_equals_q_accepts_all():
+    rng = np.random.default_rng(0)
+    B, k, V = 3, 4, 64
+    pl = rng.standard_normal((B, k + 1, V)).astype(np.float32)
+    ql = pl[:, :k].copy()
+    draft = rng.integers(0, V, (B, k)).astype(np.int32)
+    out, n = orc.spec_accept(pl, ql, draft, (1.0, 0, 1.0), seed=1, rnd=0)
+    assert (n == k).all()
+    assert (out[:, :k] == draft).all()
+
+
+def test_accept_one_hot_rejects_at_first():
+    B, k, V = 2, 3, 16
+    pl = np.full((B, k + 1, V), -30.0, np.float32)
+    pl[:, :, 7] = 30.0  # target puts all mass on token 7
+    ql = np.zeros((B, k, V), np.float32)
+    draft = np.full((B, k), 3, np.int32)
+    out, n = orc.spec_accept(pl, ql, draft, (1.0, 0, 1.0), seed=5, rnd=2)
+    assert (n == 0).all() and (out[:, 0] == 7).all()
+
+
+def test_accept_greedy_rules():
+    B, k, V = 1, 4, 10
+    pl = np.zeros((B, k + 1, V), np.float32)
+    am = [2, 5, 5, 1, 9]
+    for i, a in enumerate(am):
+        pl[0, i, a] = 1.0
+    draft = np.array([[2, 5, 4, 1]], np.int32)
+    out, n = orc.spec_accept(pl, np.zeros((B, k, V), np.float32), draft, (0.0, 0, 1.0), 0, 0)
+    assert n[0] == 2 and out[0, :3].tolist() == [2, 5, 5]
+    draft = np.array([[2, 5, 5, 1]], np.int32)
+    out, n = orc.spec_accept(pl, np.zeros((B, k, V), np.float32), draft, (0.0, 0, 1.0), 0, 0)
+    assert n[0] == 4 and out[0].tolist() == [2, 5, 5, 1, 9]
+
+
+def test_spec_sampling_is_lossless_chi2():
+    """The committed first token of a round is distributed as p (Leviathan et al. 2023)."""
+    V = 6
+    rng = np.random.default_rng(3)
+    p_log = rng.standard_normal(V).astype(np.float32) * 1.5
+    q_log = rng.standard_normal(V).astype(np.float32) * 1.5
+    p = orc.warp_probs(p_log, 1.0)
+    q = orc.warp_probs(q_log, 1.0)
+    n_trials = 6000
+    counts = np.zeros(V)
+    pl = np.broadcast_to(p_log, (1, 2, V)).copy()
+    ql = q_log.reshape(1, 1, V)
+    for r in range(n_trials):
+        x = orc.sample(q_log, orc.uniform(11, r, 0, 0, 1), 1.0)
+        out, n = orc.spec_accept(pl, ql, np.array([[x]], np.int32), (1.0, 0, 1.0), 11, r)
+        counts[out[0, 0]] += 1
+    exp = p * n_trials
+    chi2 = ((counts - exp) ** 2 / exp).sum()
+    assert chi2 < 25.0, (chi2, counts, exp)  # 5 dof, p ~ 1e-4
+    assert not np.allclose(p, q)

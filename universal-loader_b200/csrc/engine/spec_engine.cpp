@@ -1,0 +1,235 @@
+/*
+ * spec_engine.cpp — see spec_engine.h.
+ */
+#include "spec_engine.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+
+#include "gguf.h"
+
+namespace ulbe {
+
+Engine::Engine(int device) {
+  if (ulb_init(device, &ctx_) != ULB_OK) {
+    err_ = ulb_last_error();
+    ctx_ = nullptr;
+  }
+}
+
+Engine::~Engine() {
+  drop_spec();
+  if (draft_) ulb_model_free(draft_);
+  if (target_) ulb_model_free(target_);
+  if (ctx_) ulb_destroy(ctx_);
+}
+
+bool Engine::fail(const std::string& m) {
+  err_ = m;
+  return false;
+}
+
+void Engine::drop_spec() {
+  if (spec_) ulb_spec_free(spec_);
+  spec_ = nullptr;
+}
+
+void Engine::unload(bool draft) {
+  std::lock_guard<std::mutex> lk(mu_);
+  drop_spec();
+  ulb_model*& m = draft ? draft_ : target_;
+  if (m) ulb_model_free(m);
+  m = nullptr;
+  (draft ? dinfo_ : tinfo_) = ModelInfo();
+}
+
+bool Engine::load(const std::string& path, bool draft) {
+  std::lock_guard<std::mutex> lk(mu_);
+  if (!ctx_) return fail("no CUDA device: " + err_);
+  GGUFFile f;
+  std::string e;
+  if (!f.open(path, &e)) return fail(e);
+  ModelInfo mi;
+  mi.path = path;
+  mi.file_bytes = f.file_bytes;
+  mi.name = f.str("general.name", "llama");
+  mi.n_layer = (int)f.num("llama.block_count", 0);
+  mi.d_model = (int)f.num("llama.embedding_length", 0);
+  mi.n_head = (int)f.num("llama.attention.head_count", 0);
+  mi.n_head_kv = (int)f.num("llama.attention.head_count_kv", mi.n_head);
+  mi.d_ff = (int)f.num("llama.feed_forward_length", 0);
+  mi.ctx_len = (int)f.num("llama.context_length", 2048);
+  mi.rms_eps = (float)f.num("llama.attention.layer_norm_rms_epsilon", 1e-5);
+  mi.rope_base = (float)f.num("llama.rope.freq_base", 10000.0);
+  const GGUFTensor* emb = f.find("token_embd.weight");
+  mi.n_vocab = (int)f.num("llama.vocab_size", emb ? (double)emb->ne[1] : 0.0);
+  if (mi.n_layer <= 0 || mi.d_model <= 0 || mi.n_head <= 0 || mi.d_ff <= 0 || mi.n_vocab <= 0)
+    return fail(path + ": missing llama.* metadata");
+  const GGUFTensor* q = f.find("blk.0.attn_q.weight");
+  mi.wtype = q ? q->type : 0;
+  ulb_model_desc d{};
+  d.n_layer = mi.n_layer;
+  d.d_model = mi.d_model;
+  d.n_head = mi.n_head;
+  d.n_head_kv = mi.n_head_kv;
+  d.head_dim = mi.d_model / mi.n_head;
+  d.d_ff = mi.d_ff;
+  d.n_vocab = mi.n_vocab;
+  d.rms_eps = mi.rms_eps;
+  d.rope_base = mi.rope_base;
+  d.max_rows = 64;
+  ulb_model* m = nullptr;
+  if (ulb_model_create(ctx_, &d, &m) != ULB_OK) return fail(ulb_last_error());
+  for (const GGUFTensor& t : f.tensors) {
+    if (ulb_model_set_weight(m, t.name.c_str(), t.type, t.ne, t.data, t.nbytes) != ULB_OK) {
+      std::string msg = ulb_last_error();
+      ulb_model_free(m);
+      return fail(msg);
+    }
+  }
+  if (ulb_model_finalize(m) != ULB_OK) {
+    std::string msg = ulb_last_error();
+    ulb_model_free(m);
+    return fail(msg);
+  }
+  ulb_model_weight_bytes(m, &mi.weight_bytes);
+  drop_spec();
+  ulb_model*& slot = draft ? draft_ : target_;
+  if (slot) ulb_model_free(slot);
+  slot = m;
+  (draft ? dinfo_ : tinfo_) = mi;
+  return true;
+}
+
+bool Engine::generate(const std::vector<std::vector<int32_t>>& prompts, const GenParams& p,
+                      std::vector<std::vector<int32_t>>* out, GenStats* st) {
+  std::lock_guard<std::mutex> lk(mu_);
+  if (!target_) return fail("no model loaded");
+  out->assign(prompts.size(), {});
+  if (prompts.empty() || p.max_new == 0) return true;
+  const auto t0 = std::chrono::steady_clock::now();
+  int max_prompt = 0;
+  for (const auto& pr : prompts) {
+    if (pr.empty()) return fail("empty prompt");
+    max_prompt = std::max(max_prompt, (int)pr.size());
+  }
+  const bool use_draft = draft_ != nullptr && p.k > 0;
+  ulb_spec_desc sd{};
+  sd.n_seq = (int)prompts.size();
+  sd.k = use_draft ? p.k : 0;
+  sd.max_prompt = max_prompt;
+  sd.max_new = (int)p.max_new;
+  sd.warp.temperature = p.greedy ? 0.f : p.temperature;
+  sd.warp.top_k = p.top_k;
+  sd.warp.top_p = p.top_p;
+  sd.seed = p.seed;
+  sd.use_graphs = p.use_graphs ? 1 : 0;
+  const bool same = spec_ && spec_has_draft_ == use_draft && !memcmp(&sd, &spec_desc_, sizeof sd);
+  if (!same) {
+    drop_spec();
+    if (ulb_spec_create(ctx_, target_, use_draft ? draft_ : nullptr, &sd, &spec_) != ULB_OK) {
+      spec_ = nullptr;
+      return fail(ulb_last_error());
+    }
+    spec_desc_ = sd;
+    spec_has_draft_ = use_draft;
+  }
+  std::vector<int32_t> flat((size_t)sd.n_seq * max_prompt, 0), lens(sd.n_seq);
+  for (int s = 0; s < sd.n_seq; ++s) {
+    lens[s] = (int32_t)prompts[s].size();
+    std::copy(prompts[s].begin(), prompts[s].end(), flat.begin() + (size_t)s * max_prompt);
+  }
+  void *e0 = nullptr, *e1 = nullptr, *e2 = nullptr;
+  ulb_event_create(ctx_, &e0);
+  ulb_event_create(ctx_, &e1);
+  ulb_event_create(ctx_, &e2);
+  ulb_event_record(ctx_, e0);
+  int rc = ulb_spec_prefill(spec_, flat.data(), lens.data());
+  ulb_event_record(ctx_, e1);
+  int rounds = 0;
+  if (rc == ULB_OK) rc = ulb_spec_run(spec_, 0, &rounds);
+  ulb_event_record(ctx_, e2);
+  std::vector<int32_t> toks((size_t)sd.n_seq * sd.max_new), counts(sd.n_seq);
+  uint64_t stats[4] = {0, 0, 0, 0}, launches = 0;
+  if (rc == ULB_OK) rc = ulb_spec_read(spec_, toks.data(), counts.data(), stats);
+  if (rc == ULB_OK) rc = ulb_spec_launch_count(spec_, &launches);
+  float pms = 0, dms = 0;
+  if (rc == ULB_OK) {
+    ulb_event_elapsed_ms(e0, e1, &pms);
+    ulb_event_elapsed_ms(e1, e2, &dms);
+  }
+  ulb_event_destroy(e0);
+  ulb_event_destroy(e1);
+  ulb_event_destroy(e2);
+  if (rc != ULB_OK) {
+    std::string msg = ulb_last_error();
+    drop_spec();
+    return fail(msg);
+  }
+  uint64_t gen = 0;
+  for (int s = 0; s < sd.n_seq; ++s) {
+    (*out)[s].assign(toks.begin() + (size_t)s * sd.max_new, toks.begin() + (size_t)s * sd.max_new + counts[s]);
+    gen += (uint64_t)counts[s];
+  }
+  if (st) {
+    st->rounds = stats[0];
+    st->drafted = stats[1];
+    st->accepted = stats[2];
+    st->committed = stats[3];
+    st->generated = gen;
+    st->prefill_ms = pms;
+    st->decode_ms = dms;
+    st->total_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    st->h2d_bytes = (double)(flat.size() + lens.size()) * 4.0;
+    st->d2h_bytes = (double)(toks.size() + counts.size()) * 4.0;
+    st->launches = launches;
+  }
+  return true;
+}
+
+bool Engine::profile_round(float ms[3]) {
+  std::lock_guard<std::mutex> lk(mu_);
+  if (!spec_) return fail("no generation to profile");
+  if (ulb_spec_profile_round(spec_, ms) != ULB_OK) return fail(ulb_last_error());
+  return true;
+}
+
+bool Engine::last_logits(const std::vector<int32_t>& tokens, std::vector<float>* out) {
+  std::lock_guard<std::mutex> lk(mu_);
+  if (!target_) return fail("no model loaded");
+  if (tokens.empty()) return fail("empty token list");
+  const int n = (int)tokens.size(), V = tinfo_.n_vocab;
+  ulb_kv* kv = nullptr;
+  if (ulb_kv_alloc(ctx_, target_, 1, n, &kv) != ULB_OK) return fail(ulb_last_error());
+  std::vector<int32_t> seq(n, 0), pos(n);
+  for (int i = 0; i < n; ++i) pos[i] = i;
+  bool ok = true;
+  out->assign(V, 0.f);
+  /* rows are fed in chunks of 64 (the model workspace); logits of the last chunk's last row */
+  const int chunk = 64;
+  int32_t *dt = nullptr, *ds = nullptr, *dp = nullptr;
+  float* dl = nullptr;
+  if (ulb_malloc(ctx_, chunk * 4, (void**)&dt) || ulb_malloc(ctx_, chunk * 4, (void**)&ds) ||
+      ulb_malloc(ctx_, chunk * 4, (void**)&dp) ||
+      ulb_malloc(ctx_, (size_t)V * 4, (void**)&dl))
+    ok = fail(ulb_last_error());
+  for (int c0 = 0; ok && c0 < n; c0 += chunk) {
+    const int m = std::min(chunk, n - c0);
+    if (ulb_memcpy_h2d(ctx_, dt, tokens.data() + c0, m * 4) ||
+        ulb_memcpy_h2d(ctx_, ds, seq.data() + c0, m * 4) ||
+        ulb_memcpy_h2d(ctx_, dp, pos.data() + c0, m * 4) ||
+        ulb_model_forward(ctx_, target_, kv, m, m, dt, ds, dp, 1, dl, V))
+      ok = fail(ulb_last_error());
+  }
+  if (ok && ulb_memcpy_d2h(ctx_, out->data(), dl, (size_t)V * 4)) ok = fail(ulb_last_error());
+  ulb_free(ctx_, dt);
+  ulb_free(ctx_, ds);
+  ulb_free(ctx_, dp);
+  ulb_free(ctx_, dl);
+  ulb_kv_free(kv);
+  return ok;
+}
+
+}  // namespace ulbe

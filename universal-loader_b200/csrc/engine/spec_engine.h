@@ -1,0 +1,82 @@
+/*
+ * spec_engine.h — host engine above the C ABI.
+ *
+ * Plays the role of the reference's InferenceEngine (src/inference/inference_engine.h) on the
+ * speculative path: owns the device context, the target and draft models loaded from GGUF
+ * files, and drives the device-resident draft -> verify -> accept loop (ulb_spec_*).
+ */
+#pragma once
+#include <cstdint>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "ulb.h"
+
+namespace ulbe {
+
+struct ModelInfo {
+  int n_layer = 0, d_model = 0, n_head = 0, n_head_kv = 0, d_ff = 0, n_vocab = 0, ctx_len = 0;
+  float rms_eps = 1e-5f, rope_base = 10000.f;
+  int wtype = 0;
+  size_t file_bytes = 0, weight_bytes = 0;
+  std::string name, path;
+};
+
+struct GenParams {
+  uint32_t max_new = 0;
+  float temperature = 0.f;
+  int top_k = 0;
+  float top_p = 1.f;
+  bool greedy = true;
+  uint64_t seed = 0;
+  int k = 0;              /* speculation length; 0 = plain decoding */
+  bool use_graphs = true;
+};
+
+struct GenStats {
+  uint64_t rounds = 0, drafted = 0, accepted = 0, committed = 0, generated = 0;
+  double prefill_ms = 0, decode_ms = 0, total_ms = 0;
+  double h2d_bytes = 0, d2h_bytes = 0;
+  uint64_t launches = 0; /* kernels launched by the library for this generation */
+};
+
+class Engine {
+ public:
+  explicit Engine(int device = 0);
+  ~Engine();
+  bool ok() const { return ctx_ != nullptr; }
+  const std::string& error() const { return err_; }
+
+  bool load(const std::string& path, bool draft);
+  void unload(bool draft);
+  bool has_model(bool draft) const { return draft ? draft_ != nullptr : target_ != nullptr; }
+  const ModelInfo& info(bool draft) const { return draft ? dinfo_ : tinfo_; }
+
+  /* prompts: token ids.  Returns committed tokens per prompt (max_new each). */
+  bool generate(const std::vector<std::vector<int32_t>>& prompts, const GenParams& p,
+                std::vector<std::vector<int32_t>>* out, GenStats* st);
+  /* logits of the last position after feeding `tokens` to the target from an empty cache */
+  bool last_logits(const std::vector<int32_t>& tokens, std::vector<float>* out);
+  /* time one extra round of the last generation's loop by phase: draft, verify, accept (ms) */
+  bool profile_round(float ms[3]);
+
+  ulb_ctx* ctx() { return ctx_; }
+
+ private:
+  bool fail(const std::string& m);
+  void drop_spec();
+  ulb_ctx* ctx_ = nullptr;
+  ulb_model* target_ = nullptr;
+  ulb_model* draft_ = nullptr;
+  ModelInfo tinfo_, dinfo_;
+  std::string err_;
+  /* cached loop for repeated calls with the same shape */
+  ulb_spec* spec_ = nullptr;
+  ulb_spec_desc spec_desc_{};
+  bool spec_has_draft_ = false;
+  std::mutex mu_;
+};
+
+}  // namespace ulbe

@@ -1,0 +1,533 @@
+/*
+ * model.cu — LLaMA-family model resident in HBM, KV cache, and one forward pass.
+ *
+ * Replaces Model / LayerWeights / KVCache (src/inference/model.h:37-115,
+ * model.cpp:11-131,154-254) and the per-layer GPU forward
+ * (src/inference/inference_engine.cpp:475-692), keeping its op order
+ *   norm -> Q,K,V -> RoPE -> attention -> o -> +res -> norm -> gate,up -> SiLU*mul -> down -> +res
+ * with each op given its LLaMA meaning and fused as:
+ *   rmsnorm(fp16 out) | QKV-GEMV (+RoPE, K/V -> cache) | attention | O-GEMV (+residual)
+ *   | rmsnorm | gate/up-GEMV (+SiLU*up) | down-GEMV (+residual)
+ * Tensors are named as in GGUF (the reference maps only a subset and misses the
+ * blk.N.ffn_* names, model.cpp:232-245).
+ */
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+
+#include "ulb_internal.h"
+
+namespace ulb {
+
+struct RawW {
+  int type = 0;
+  uint64_t ne[4] = {1, 1, 1, 1};
+  void* dev = nullptr;
+  size_t bytes = 0;
+};
+
+struct Layer {
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  Tensor qkv, o, gateup, down;
+};
+
+struct Model {
+  Ctx* c = nullptr;
+  ulb_model_desc d{};
+  int nq = 0, nkv = 0;
+  std::map<std::string, RawW> raw;
+  bool finalized = false;
+  int embd_type = ULB_TYPE_F16;
+  void* embd = nullptr;
+  size_t embd_bytes = 0;
+  std::vector<Layer> layers;
+  float* out_norm = nullptr;
+  Tensor out;
+  size_t weight_bytes = 0;
+  /* workspace */
+  int ws_rows = 0;
+  float* x = nullptr;
+  __half* x16 = nullptr;
+  float* qb = nullptr;
+  __half* att = nullptr;
+  __half* h16 = nullptr;
+  size_t ws_bytes = 0;
+};
+
+struct KV {
+  Model* m = nullptr;
+  int n_seq = 0, cap = 0;
+  __half* k = nullptr;
+  __half* v = nullptr;
+  size_t layer_elems = 0;
+  size_t bytes = 0;
+  float2* rope = nullptr;
+  size_t rope_bytes = 0;
+  float* attn_scratch = nullptr;
+  size_t attn_floats = 0;
+  int* attn_counters = nullptr;
+  int n_counters = 0;
+};
+
+namespace {
+
+__global__ void embed_kernel(const void* __restrict__ table, int table_type, int d, int V,
+                             const int* __restrict__ tokens, float* __restrict__ x, int* err) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x;
+  int t = tokens[m];
+  if (t < 0 || t >= V) {
+    if (threadIdx.x == 0) atomicOr(err, 1);
+    t = t < 0 ? 0 : V - 1;
+  }
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float v;
+    if (table_type == ULB_TYPE_F16) v = __half2float(reinterpret_cast<const __half*>(table)[(size_t)t * d + i]);
+    else v = reinterpret_cast<const float*>(table)[(size_t)t * d + i];
+    x[(size_t)m * d + i] = v;
+  }
+}
+
+/* out[s] = fp16((x[row] * r) * g), r = 1 / sqrt(mean(x^2) + eps); row = s*sel + sel-1 if sel */
+__global__ void rmsnorm_kernel(const float* __restrict__ x, int ldx, const float* __restrict__ g, int d, float eps,
+                               int sel, __half* __restrict__ out, int ldo) {
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
+  const int s = blockIdx.x;
+  const int row = sel > 0 ? s * sel + sel - 1 : s;
+  const float* xv = x + (size_t)row * ldx;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) ss = __fmaf_rn(xv[i], xv[i], ss);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    out[(size_t)s * ldo + i] = __float2half_rn(__fmul_rn(__fmul_rn(xv[i], r), g[i]));
+}
+
+}  // namespace
+
+int launch_embed_t(Ctx* c, const void* table, int type, int d, int V, const int* tokens, int M, float* x, int* err) {
+  if (M == 0) return ULB_OK;
+  cudaError_t e = launch_k(c, embed_kernel, dim3(M), dim3(256), 0, table, type, d, V, tokens, x, err);
+  if (e != cudaSuccess) return cuda_error(e, "embed launch", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
+int launch_rmsnorm_sel(Ctx* c, const float* x, int ldx, const float* g, int n_out, int d, float eps, int sel,
+                       __half* out, int ldo) {
+  if (n_out == 0) return ULB_OK;
+  cudaError_t e = launch_k(c, rmsnorm_kernel, dim3(n_out), dim3(256), 0, x, ldx, g, d, eps, sel, out, ldo);
+  if (e != cudaSuccess) return cuda_error(e, "rmsnorm launch", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
+static int ensure_ws(Model* m, int rows) {
+  if (rows <= m->ws_rows) return ULB_OK;
+  Ctx* c = m->c;
+  dev_free(c, m->x, 0); dev_free(c, m->x16, 0); dev_free(c, m->qb, 0); dev_free(c, m->att, 0); dev_free(c, m->h16, 0);
+  c->bytes_live -= m->ws_bytes;
+  m->ws_bytes = 0;
+  m->ws_rows = 0;
+  const ulb_model_desc& d = m->d;
+  const size_t R = (size_t)rows;
+  const size_t bx = R * d.d_model * 4, bx16 = R * d.d_model * 2, bq = R * m->nq * 4, ba = R * m->nq * 2,
+               bh = R * d.d_ff * 2;
+  ULB_TRY(dev_alloc(c, (void**)&m->x, bx));
+  ULB_TRY(dev_alloc(c, (void**)&m->x16, bx16));
+  ULB_TRY(dev_alloc(c, (void**)&m->qb, bq));
+  ULB_TRY(dev_alloc(c, (void**)&m->att, ba));
+  ULB_TRY(dev_alloc(c, (void**)&m->h16, bh));
+  m->ws_bytes = bx + bx16 + bq + ba + bh;
+  m->ws_rows = rows;
+  return ULB_OK;
+}
+
+static int ensure_attn(KV* kv, int M, int rps) {
+  const ulb_model_desc& d = kv->m->d;
+  ulb_attn_desc ad{d.n_head, d.n_head_kv, d.head_dim, kv->cap, kv->n_seq, 1.0f / std::sqrt((float)d.head_dim)};
+  int nc = 0;
+  const size_t nf = attention_scratch_floats(&ad, M, rps, kv->cap - 1, &nc);
+  if (nf <= kv->attn_floats && nc <= kv->n_counters) return ULB_OK;
+  Ctx* c = kv->m->c;
+  dev_free(c, kv->attn_scratch, kv->attn_floats * 4);
+  dev_free(c, kv->attn_counters, (size_t)kv->n_counters * 4);
+  kv->attn_scratch = nullptr; kv->attn_counters = nullptr; kv->attn_floats = 0; kv->n_counters = 0;
+  const size_t f2 = nf > kv->attn_floats ? nf : kv->attn_floats;
+  ULB_TRY(dev_alloc(c, (void**)&kv->attn_scratch, f2 * 4));
+  kv->attn_floats = f2;
+  ULB_TRY(dev_alloc(c, (void**)&kv->attn_counters, (size_t)nc * 4));
+  kv->n_counters = nc;
+  ULB_CUDA(cudaMemsetAsync(kv->attn_counters, 0, (size_t)nc * 4, c->stream));
+  return ULB_OK;
+}
+
+/* Make workspaces large enough for a forward of M rows (rps per sequence).  Must be called
+ * before a forward is captured into a CUDA graph. */
+int model_prepare(Model* m, KV* kv, int M, int rps) {
+  ULB_TRY(ensure_ws(m, M));
+  ULB_TRY(ensure_attn(kv, M, rps));
+  return ULB_OK;
+}
+
+int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos, int logits_mode,
+                  float* logits, int ld, int* err) {
+  Ctx* c = m->c;
+  const ulb_model_desc& d = m->d;
+  ULB_CHECK(m->finalized, ULB_EINVAL, "forward: model not finalized");
+  ULB_CHECK(kv && kv->m == m, ULB_EINVAL, "forward: KV cache belongs to another model");
+  ULB_CHECK(M > 0 && rps > 0 && M % rps == 0, ULB_EINVAL, "forward: M=%d rows_per_seq=%d", M, rps);
+  ULB_CHECK(M <= m->ws_rows, ULB_EINVAL, "forward: M=%d exceeds prepared workspace (%d rows)", M, m->ws_rows);
+  ULB_CHECK(ld >= d.n_vocab, ULB_EINVAL, "forward: ld %d < n_vocab %d", ld, d.n_vocab);
+  ulb_attn_desc ad{d.n_head, d.n_head_kv, d.head_dim, kv->cap, kv->n_seq, 1.0f / std::sqrt((float)d.head_dim)};
+  ULB_TRY(launch_embed_t(c, m->embd, m->embd_type, d.d_model, d.n_vocab, tok, M, m->x, err));
+  for (int l = 0; l < d.n_layer; ++l) {
+    Layer& L = m->layers[l];
+    __half* kc = kv->k + (size_t)l * kv->layer_elems;
+    __half* vc = kv->v + (size_t)l * kv->layer_elems;
+    ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, L.attn_norm, M, d.d_model, d.rms_eps, 0, m->x16, d.d_model));
+    EpiArgs a;
+    a.q = m->qb; a.ldq = m->nq; a.kc = kc; a.vc = vc;
+    a.nq = m->nq; a.nkv = m->nkv; a.hd = d.head_dim; a.cap = kv->cap; a.n_head_kv = d.n_head_kv; a.n_seq = kv->n_seq;
+    a.row_seq = seq; a.row_pos = pos; a.rope = kv->rope;
+    ULB_TRY(launch_qgemv(c, &L.qkv, m->x16, M, d.d_model, EPI_QKV, a));
+    ULB_TRY(launch_attention(c, &ad, m->qb, m->nq, kc, vc, seq, pos, M, rps, m->att, kv->attn_scratch,
+                             kv->attn_counters, kv->attn_floats, kv->n_counters));
+    EpiArgs r;
+    r.y = m->x; r.ldy = d.d_model;
+    ULB_TRY(launch_qgemv(c, &L.o, m->att, M, m->nq, EPI_RESID, r));
+    ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, L.ffn_norm, M, d.d_model, d.rms_eps, 0, m->x16, d.d_model));
+    EpiArgs s;
+    s.h = m->h16; s.ldh = d.d_ff;
+    ULB_TRY(launch_qgemv(c, &L.gateup, m->x16, M, d.d_model, EPI_SWIGLU, s));
+    ULB_TRY(launch_qgemv(c, &L.down, m->h16, M, d.d_ff, EPI_RESID, r));
+  }
+  const int n_out = logits_mode == 1 ? M / rps : M;
+  ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, m->out_norm, n_out, d.d_model, d.rms_eps,
+                             logits_mode == 1 ? rps : 0, m->x16, d.d_model));
+  EpiArgs o;
+  o.y = logits; o.ldy = ld;
+  return launch_qgemv(c, &m->out, m->x16, n_out, d.d_model, EPI_STORE, o);
+}
+
+}  // namespace ulb
+
+struct ulb_model {
+  ulb::Model m;
+};
+struct ulb_kv {
+  ulb::KV kv;
+};
+
+namespace ulb {
+Model* model_of(ulb_model* m) { return &m->m; }
+KV* kv_of(ulb_kv* kv) { return &kv->kv; }
+int model_vocab(const Model* m) { return m->d.n_vocab; }
+}  // namespace ulb
+
+using namespace ulb;
+
+namespace {
+
+int upload_plain(Ctx* c, const RawW& r, void** out, size_t* bytes) {
+  *bytes = r.bytes;
+  ULB_TRY(dev_alloc(c, out, r.bytes));
+  ULB_CUDA(cudaMemcpyAsync(*out, r.dev, r.bytes, cudaMemcpyDeviceToDevice, c->stream));
+  return ULB_OK;
+}
+
+/* concatenate raw rows of several same-type matrices and repack with a row map */
+int build_fused(Ctx* c, const std::vector<const RawW*>& parts, const std::vector<int>& map, Tensor* out) {
+  const int type = parts[0]->type;
+  const int K = (int)parts[0]->ne[0];
+  size_t total = 0;
+  int rows = 0;
+  for (const RawW* p : parts) {
+    ULB_CHECK(p->type == type, ULB_EFORMAT, "fused weights must share one quant type");
+    ULB_CHECK((int)p->ne[0] == K, ULB_EFORMAT, "fused weights must share K");
+    total += p->bytes;
+    rows += (int)p->ne[1];
+  }
+  void* cat = nullptr;
+  ULB_TRY(dev_alloc(c, &cat, total));
+  size_t off = 0;
+  for (const RawW* p : parts) {
+    cudaError_t e = cudaMemcpyAsync((uint8_t*)cat + off, p->dev, p->bytes, cudaMemcpyDeviceToDevice, c->stream);
+    if (e != cudaSuccess) { dev_free(c, cat, total); return cuda_error(e, "concat", __FILE__, __LINE__); }
+    off += p->bytes;
+  }
+  int rc = repack_q4(c, type, cat, rows, K, map.data(), (int)map.size(), out);
+  dev_free(c, cat, total);
+  if (rc) return rc;
+  out->N = (int)map.size();
+  out->ne[0] = (uint64_t)K;
+  out->ne[1] = (uint64_t)out->N;
+  return ULB_OK;
+}
+
+int build_plain(Ctx* c, const RawW& r, Tensor* out) {
+  const int N = (int)r.ne[1], K = (int)r.ne[0];
+  const int rows = (N + 15) / 16 * 16;
+  std::vector<int> map(rows);
+  for (int i = 0; i < rows; ++i) map[i] = i < N ? i : -1;
+  ULB_TRY(repack_q4(c, r.type, r.dev, N, K, map.data(), rows, out));
+  out->N = N;
+  out->ne[0] = (uint64_t)K;
+  out->ne[1] = (uint64_t)N;
+  return ULB_OK;
+}
+
+void free_tensor(Ctx* c, Tensor& t) {
+  dev_free(c, t.dev, t.bytes);
+  t.dev = nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ulb_model_create(ulb_ctx* ctx, const ulb_model_desc* d, ulb_model** out) {
+  ULB_CHECK(ctx && d && out, ULB_EINVAL, "ulb_model_create: NULL argument");
+  ULB_CHECK(d->n_layer > 0 && d->d_model > 0 && d->n_head > 0 && d->n_head_kv > 0 && d->head_dim > 0 && d->d_ff > 0 &&
+                d->n_vocab > 0,
+            ULB_EINVAL, "ulb_model_create: non-positive dimension");
+  ULB_CHECK(d->n_head % d->n_head_kv == 0, ULB_EINVAL, "n_head %d not a multiple of n_head_kv %d", d->n_head, d->n_head_kv);
+  ULB_CHECK(d->head_dim % 16 == 0, ULB_EUNSUPPORTED, "head_dim %d must be a multiple of 16", d->head_dim);
+  ULB_CHECK(d->d_ff % 8 == 0 && d->d_model % 8 == 0, ULB_EUNSUPPORTED, "d_model/d_ff must be multiples of 8");
+  std::unique_ptr<ulb_model> m(new ulb_model());
+  m->m.c = &ctx->c;
+  m->m.d = *d;
+  m->m.nq = d->n_head * d->head_dim;
+  m->m.nkv = d->n_head_kv * d->head_dim;
+  m->m.layers.resize(d->n_layer);
+  *out = m.release();
+  return ULB_OK;
+}
+
+int ulb_model_set_weight(ulb_model* mm, const char* name, int type, const uint64_t ne[4], const void* bytes,
+                         size_t nbytes) {
+  ULB_CHECK(mm && name && ne && bytes, ULB_EINVAL, "ulb_model_set_weight: NULL argument");
+  Model* m = &mm->m;
+  ULB_CHECK(!m->finalized, ULB_EINVAL, "ulb_model_set_weight: model already finalized");
+  const uint64_t n = ne[0] * ne[1] * ne[2] * ne[3];
+  size_t want = 0;
+  switch (type) {
+    case ULB_TYPE_F32: want = n * 4; break;
+    case ULB_TYPE_F16: want = n * 2; break;
+    case ULB_TYPE_Q4_0: want = ne[0] % 32 ? 0 : n / 32 * 18; break;
+    case ULB_TYPE_Q4_K: want = ne[0] % 256 ? 0 : n / 256 * 144; break;
+    default: return set_error(ULB_EUNSUPPORTED, "%s: tensor type %d not supported", name, type);
+  }
+  ULB_CHECK(want && want == nbytes, ULB_EFORMAT, "%s: %zu bytes, GGUF size is %zu", name, nbytes, want);
+  Ctx* c = m->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  auto it = m->raw.find(name);
+  if (it != m->raw.end()) {
+    dev_free(c, it->second.dev, it->second.bytes);
+    m->raw.erase(it);
+  }
+  RawW r;
+  r.type = type;
+  memcpy(r.ne, ne, sizeof r.ne);
+  r.bytes = nbytes;
+  ULB_TRY(dev_alloc(c, &r.dev, nbytes));
+  cudaError_t e = cudaMemcpyAsync(r.dev, bytes, nbytes, cudaMemcpyHostToDevice, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) { dev_free(c, r.dev, nbytes); return cuda_error(e, "upload", __FILE__, __LINE__); }
+  m->raw[name] = r;
+  return ULB_OK;
+}
+
+int ulb_model_finalize(ulb_model* mm) {
+  ULB_CHECK(mm, ULB_EINVAL, "ulb_model_finalize: NULL model");
+  Model* m = &mm->m;
+  if (m->finalized) return ULB_OK;
+  Ctx* c = m->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  const ulb_model_desc& d = m->d;
+  auto get = [&](const std::string& nm, const RawW** out) -> int {
+    auto it = m->raw.find(nm);
+    if (it == m->raw.end()) return set_error(ULB_EFORMAT, "missing tensor %s", nm.c_str());
+    *out = &it->second;
+    return ULB_OK;
+  };
+  auto expect = [&](const RawW* r, const char* nm, uint64_t ne0, uint64_t ne1) -> int {
+    if (r->ne[0] != ne0 || r->ne[1] != ne1)
+      return set_error(ULB_EFORMAT, "%s: shape [%llu, %llu], expected [%llu, %llu]", nm, (unsigned long long)r->ne[0],
+                       (unsigned long long)r->ne[1], (unsigned long long)ne0, (unsigned long long)ne1);
+    return ULB_OK;
+  };
+  auto is_q4 = [](int t) { return t == ULB_TYPE_Q4_0 || t == ULB_TYPE_Q4_K; };
+  const RawW* r;
+  ULB_TRY(get("token_embd.weight", &r));
+  ULB_TRY(expect(r, "token_embd.weight", d.d_model, d.n_vocab));
+  ULB_CHECK(r->type == ULB_TYPE_F16 || r->type == ULB_TYPE_F32, ULB_EUNSUPPORTED, "token_embd must be F16 or F32");
+  m->embd_type = r->type;
+  ULB_TRY(upload_plain(c, *r, &m->embd, &m->embd_bytes));
+  const int nq = m->nq, nkv = m->nkv;
+  for (int l = 0; l < d.n_layer; ++l) {
+    Layer& L = m->layers[l];
+    const std::string p = "blk." + std::to_string(l) + ".";
+    const RawW *an, *fn, *q, *k, *v, *o, *g, *u, *dn;
+    ULB_TRY(get(p + "attn_norm.weight", &an));
+    ULB_TRY(get(p + "ffn_norm.weight", &fn));
+    ULB_TRY(get(p + "attn_q.weight", &q));
+    ULB_TRY(get(p + "attn_k.weight", &k));
+    ULB_TRY(get(p + "attn_v.weight", &v));
+    ULB_TRY(get(p + "attn_output.weight", &o));
+    ULB_TRY(get(p + "ffn_gate.weight", &g));
+    ULB_TRY(get(p + "ffn_up.weight", &u));
+    ULB_TRY(get(p + "ffn_down.weight", &dn));
+    ULB_CHECK(an->type == ULB_TYPE_F32 && fn->type == ULB_TYPE_F32, ULB_EUNSUPPORTED, "%snorms must be F32", p.c_str());
+    ULB_CHECK(an->ne[0] == (uint64_t)d.d_model && fn->ne[0] == (uint64_t)d.d_model, ULB_EFORMAT, "%snorm size", p.c_str());
+    ULB_TRY(expect(q, "attn_q", d.d_model, nq));
+    ULB_TRY(expect(k, "attn_k", d.d_model, nkv));
+    ULB_TRY(expect(v, "attn_v", d.d_model, nkv));
+    ULB_TRY(expect(o, "attn_output", nq, d.d_model));
+    ULB_TRY(expect(g, "ffn_gate", d.d_model, d.d_ff));
+    ULB_TRY(expect(u, "ffn_up", d.d_model, d.d_ff));
+    ULB_TRY(expect(dn, "ffn_down", d.d_ff, d.d_model));
+    for (const RawW* w : {q, k, v, o, g, u, dn})
+      ULB_CHECK(is_q4(w->type), ULB_EUNSUPPORTED, "%s linear weights must be Q4_0 or Q4_K", p.c_str());
+    size_t b;
+    ULB_TRY(upload_plain(c, *an, (void**)&L.attn_norm, &b));
+    ULB_TRY(upload_plain(c, *fn, (void**)&L.ffn_norm, &b));
+    /* QKV: q and k rows paired for RoPE (strip row i = feature 2i, row i+8 = 2i+1), v as is */
+    std::vector<int> map(nq + 2 * nkv);
+    for (int s = 0; s < (nq + 2 * nkv) / 16; ++s)
+      for (int i = 0; i < 16; ++i) {
+        const int f0 = s * 16;
+        map[f0 + i] = f0 < nq + nkv ? (i < 8 ? f0 + 2 * i : f0 + 2 * (i - 8) + 1) : f0 + i;
+      }
+    ULB_TRY(build_fused(c, {q, k, v}, map, &L.qkv));
+    ULB_TRY(build_plain(c, *o, &L.o));
+    /* gate/up interleaved in strips: rows 0..7 gate 8s.., rows 8..15 up 8s.. */
+    std::vector<int> gm(2 * d.d_ff);
+    for (int s = 0; s < d.d_ff / 8; ++s)
+      for (int i = 0; i < 16; ++i) gm[s * 16 + i] = i < 8 ? s * 8 + i : d.d_ff + s * 8 + (i - 8);
+    ULB_TRY(build_fused(c, {g, u}, gm, &L.gateup));
+    ULB_TRY(build_plain(c, *dn, &L.down));
+    m->weight_bytes += L.qkv.bytes + L.o.bytes + L.gateup.bytes + L.down.bytes;
+  }
+  ULB_TRY(get("output_norm.weight", &r));
+  ULB_CHECK(r->type == ULB_TYPE_F32 && r->ne[0] == (uint64_t)d.d_model, ULB_EFORMAT, "output_norm");
+  size_t b;
+  ULB_TRY(upload_plain(c, *r, (void**)&m->out_norm, &b));
+  ULB_TRY(get("output.weight", &r));
+  ULB_TRY(expect(r, "output.weight", d.d_model, d.n_vocab));
+  ULB_CHECK(is_q4(r->type), ULB_EUNSUPPORTED, "output.weight must be Q4_0 or Q4_K");
+  ULB_TRY(build_plain(c, *r, &m->out));
+  m->weight_bytes += m->out.bytes;
+  for (auto& kv : m->raw) dev_free(c, kv.second.dev, kv.second.bytes);
+  m->raw.clear();
+  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  m->finalized = true;
+  return ULB_OK;
+}
+
+int ulb_model_free(ulb_model* mm) {
+  if (!mm) return ULB_OK;
+  Model* m = &mm->m;
+  Ctx* c = m->c;
+  cudaSetDevice(c->device);
+  for (auto& kv : m->raw) dev_free(c, kv.second.dev, kv.second.bytes);
+  dev_free(c, m->embd, m->embd_bytes);
+  for (Layer& L : m->layers) {
+    dev_free(c, L.attn_norm, (size_t)m->d.d_model * 4);
+    dev_free(c, L.ffn_norm, (size_t)m->d.d_model * 4);
+    free_tensor(c, L.qkv); free_tensor(c, L.o); free_tensor(c, L.gateup); free_tensor(c, L.down);
+  }
+  dev_free(c, m->out_norm, (size_t)m->d.d_model * 4);
+  free_tensor(c, m->out);
+  dev_free(c, m->x, 0); dev_free(c, m->x16, 0); dev_free(c, m->qb, 0); dev_free(c, m->att, 0); dev_free(c, m->h16, 0);
+  c->bytes_live -= m->ws_bytes;
+  cudaStreamSynchronize(c->stream);
+  delete mm;
+  return ULB_OK;
+}
+
+int ulb_model_weight_bytes(const ulb_model* mm, size_t* out) {
+  ULB_CHECK(mm && out, ULB_EINVAL, "ulb_model_weight_bytes: NULL argument");
+  *out = mm->m.weight_bytes;
+  return ULB_OK;
+}
+
+int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* mm, int n_seq, int cap, ulb_kv** out) {
+  ULB_CHECK(ctx && mm && out, ULB_EINVAL, "ulb_kv_alloc: NULL argument");
+  ULB_CHECK(n_seq > 0 && cap > 0, ULB_EINVAL, "ulb_kv_alloc: n_seq %d cap %d", n_seq, cap);
+  Ctx* c = &ctx->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  std::unique_ptr<ulb_kv> kvh(new ulb_kv());
+  KV* kv = &kvh->kv;
+  kv->m = const_cast<Model*>(&mm->m);
+  const ulb_model_desc& d = mm->m.d;
+  kv->n_seq = n_seq;
+  kv->cap = cap;
+  kv->layer_elems = (size_t)n_seq * d.n_head_kv * cap * d.head_dim;
+  kv->bytes = kv->layer_elems * d.n_layer * 2;
+  ULB_TRY(dev_alloc(c, (void**)&kv->k, kv->bytes));
+  ULB_TRY(dev_alloc(c, (void**)&kv->v, kv->bytes));
+  ULB_CUDA(cudaMemsetAsync(kv->k, 0, kv->bytes, c->stream));
+  ULB_CUDA(cudaMemsetAsync(kv->v, 0, kv->bytes, c->stream));
+  /* RoPE table: theta = pos * base^(-2i/hd) in fp64, cos/sin rounded to fp32 */
+  const int half = d.head_dim / 2;
+  std::vector<float2> tab((size_t)cap * half);
+  for (int p = 0; p < cap; ++p)
+    for (int i = 0; i < half; ++i) {
+      const double th = (double)p * std::pow((double)d.rope_base, -2.0 * (double)i / (double)d.head_dim);
+      tab[(size_t)p * half + i] = make_float2((float)std::cos(th), (float)std::sin(th));
+    }
+  kv->rope_bytes = tab.size() * sizeof(float2);
+  ULB_TRY(dev_alloc(c, (void**)&kv->rope, kv->rope_bytes));
+  ULB_CUDA(cudaMemcpyAsync(kv->rope, tab.data(), kv->rope_bytes, cudaMemcpyHostToDevice, c->stream));
+  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  *out = kvh.release();
+  return ULB_OK;
+}
+
+int ulb_kv_free(ulb_kv* kvh) {
+  if (!kvh) return ULB_OK;
+  KV* kv = &kvh->kv;
+  Ctx* c = kv->m->c;
+  cudaSetDevice(c->device);
+  dev_free(c, kv->k, kv->bytes);
+  dev_free(c, kv->v, kv->bytes);
+  dev_free(c, kv->rope, kv->rope_bytes);
+  dev_free(c, kv->attn_scratch, kv->attn_floats * 4);
+  dev_free(c, kv->attn_counters, (size_t)kv->n_counters * 4);
+  cudaStreamSynchronize(c->stream);
+  delete kvh;
+  return ULB_OK;
+}
+
+int ulb_model_forward(ulb_ctx* ctx, ulb_model* mm, ulb_kv* kvh, int M, int rps, const int32_t* tok,
+                      const int32_t* seq, const int32_t* pos, int logits_mode, float* logits, int ld) {
+  ULB_CHECK(ctx && mm && kvh && tok && seq && pos && logits, ULB_EINVAL, "ulb_model_forward: NULL argument");
+  ULB_CHECK(&ctx->c == mm->m.c, ULB_EINVAL, "ulb_model_forward: model belongs to another context");
+  Ctx* c = &ctx->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  ULB_TRY(model_prepare(&mm->m, &kvh->kv, M, rps));
+  int* err = nullptr;
+  ULB_TRY(dev_alloc(c, (void**)&err, sizeof(int)));
+  ULB_CUDA(cudaMemsetAsync(err, 0, sizeof(int), c->stream));
+  int rc = model_forward(&mm->m, &kvh->kv, M, rps, tok, seq, pos, logits_mode, logits, ld, err);
+  int herr = 0;
+  if (rc == ULB_OK) {
+    cudaError_t e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) rc = cuda_error(e, "forward", __FILE__, __LINE__);
+  }
+  dev_free(c, err, sizeof(int));
+  if (rc == ULB_OK && herr) rc = set_error(ULB_EINVAL, "ulb_model_forward: token id out of range");
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,586 @@
+/*
+ * qgemv.cu — fused Q4_0 / Q4_K dequant-GEMM for the HBM-bound regime (M <= 64 rows),
+ * plus the load-time repack and the bit-exact dequant kernel.
+ *
+ * Replaces the reference's run_linear_q4k path (src/inference/inference_engine.cpp:532-570:
+ * dequantize_q4_k_flattened.glsl materialising an fp32 [N][K] matrix, then the scalar
+ * gemm_transposed_b_v2.glsl) and the unused gemm_dequant_q4_0 / gemm_coop_dequant_q4_0
+ * shaders (src/shaders/gemm).
+ *
+ * Design (B200):
+ *  - one CTA per 16-row strip; its 8 warps split the strip's K-tiles; the strip is one
+ *    contiguous range of packed bytes which thread 0 hands to the L2 with a single
+ *    cp.async.bulk.prefetch.L2 before griddepcontrol.wait, so weight streaming overlaps
+ *    the tail of the previous kernel (programmatic dependent launch);
+ *  - every lane fetches its share of a tile with 128-bit loads that bypass L1;
+ *  - nibbles become exact fp16 integers with one LOP3 + one HSUB2/HFMA2 per pair
+ *    (0x6400 magic) and feed mma.sync.m16n8k16 (weights = A, activations = B, so M <= 8
+ *    tokens fill one n-tile); each 32-weight block's scale is applied in fp32 to that
+ *    block's integer dot product, so weights are never rounded;
+ *  - the fused epilogues write RoPE'd Q / K / V (K and V straight into the fp16 KV cache),
+ *    SiLU(gate)*up in fp16, or the fp32 residual add.
+ * The tensor pipe is idle in this regime (<= 3.6 flop/B at M = 1); mma.sync is used as the
+ * cheapest-to-issue dot product engine.  The reduction order of a row never depends on M.
+ */
+#include "ulb_internal.h"
+
+namespace ulb {
+
+namespace {
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+/* D = A(16x16 f16, row) * B(16x8 f16, col) + C (f32) */
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1, const float (&c)[4]) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+        "f"(c[3]));
+}
+
+/*
+ * Word v holds nibbles n0..n7 at bit positions {0,16,4,20,8,24,12,28}.  Produces the four
+ * fp16x2 pairs (n0,n1) (n2,n3) (n4,n5) (n6,n7) minus `bias` exactly.
+ *   (v & 0x000F000F) | 0x6400_6400 = (1024 + n0, 1024 + n1)
+ *   (v & 0x00F000F0) | 0x6400_6400 = (1024 + 16 n2, 1024 + 16 n3) -> x/16 - (64 + bias)
+ */
+template <int BIAS>
+__device__ __forceinline__ void nib_pairs(uint32_t v, uint32_t& p01, uint32_t& p23, uint32_t& p45,
+                                          uint32_t& p67) {
+  constexpr uint32_t MAGIC = 0x64006400u;
+  /* fp16 of 1024 + BIAS and of -(64 + BIAS), duplicated */
+  constexpr uint32_t SUB = BIAS == 8 ? 0x64086408u : 0x64006400u;
+  constexpr uint32_t NEG = BIAS == 8 ? 0xD480D480u : 0xD400D400u;
+  constexpr uint32_t SIXTEENTH = 0x2C002C00u;
+  uint32_t v8 = v >> 8;
+  p01 = hsub2u((v & 0x000F000Fu) | MAGIC, SUB);
+  p23 = hfma2u((v & 0x00F000F0u) | MAGIC, SIXTEENTH, NEG);
+  p45 = hsub2u((v8 & 0x000F000Fu) | MAGIC, SUB);
+  p67 = hfma2u((v8 & 0x00F000F0u) | MAGIC, SIXTEENTH, NEG);
+}
+
+/* One 32-weight block for rows (g, g+8): integer dot products with NT n-tiles of x. */
+template <int BIAS, int NT>
+__device__ __forceinline__ void block_mma(uint32_t vg, uint32_t vg8, const __half* __restrict__ x,
+                                          int ldx, int M, int g, int kofs, float (&s)[NT][4]) {
+  uint32_t a01, a23, a45, a67, b01, b23, b45, b67;
+  nib_pairs<BIAS>(vg, a01, a23, a45, a67);
+  nib_pairs<BIAS>(vg8, b01, b23, b45, b67);
+  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int n = nt * 8 + g;
+    uint4 bx = make_uint4(0u, 0u, 0u, 0u);
+    if (n < M) bx = __ldg(reinterpret_cast<const uint4*>(x + (size_t)n * ldx + kofs));
+    float tmp[4];
+    mma16816(tmp, a01, b01, a23, b23, bx.x, bx.y, zero);
+    mma16816(s[nt], a45, b45, a67, b67, bx.z, bx.w, tmp);
+  }
+}
+
+/* Column sums of x over one 32-wide block, via MMA with an all-ones A. */
+template <int NT>
+__device__ __forceinline__ void block_colsum(const __half* __restrict__ x, int ldx, int M, int g,
+                                             int kofs, float (&s)[NT][4]) {
+  const uint32_t ONES = 0x3C003C00u;
+  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int n = nt * 8 + g;
+    uint4 bx = make_uint4(0u, 0u, 0u, 0u);
+    if (n < M) bx = __ldg(reinterpret_cast<const uint4*>(x + (size_t)n * ldx + kofs));
+    float tmp[4];
+    mma16816(tmp, ONES, ONES, ONES, ONES, bx.x, bx.y, zero);
+    mma16816(s[nt], ONES, ONES, ONES, ONES, bx.z, bx.w, tmp);
+  }
+}
+
+/* Q4_K 6-bit (scale, min) of sub-block J from the 12 packed bytes (3 little-endian words). */
+template <int J>
+__device__ __forceinline__ void q4k_sm(uint32_t w0, uint32_t w1, uint32_t w2, float& sc, float& mn) {
+  uint32_t s, m;
+  if (J < 4) {
+    s = (w0 >> (8 * J)) & 63u;
+    m = (w1 >> (8 * J)) & 63u;
+  } else {
+    s = ((w2 >> (8 * (J - 4))) & 0x0Fu) | (((w0 >> (8 * (J - 4) + 6)) & 3u) << 4);
+    m = ((w2 >> (8 * (J - 4) + 4)) & 0x0Fu) | (((w1 >> (8 * (J - 4) + 6)) & 3u) << 4);
+  }
+  sc = (float)s;
+  mn = (float)m;
+}
+
+/* ------------------------------------------------------------------ epilogues */
+template <int EPI>
+__device__ __forceinline__ void epilogue(const EpiArgs& e, int strip, int nt, int g, int t, int M,
+                                         int N, const float4& v) {
+  const int tok0 = nt * 8 + 2 * t, tok1 = tok0 + 1;
+  if (EPI == EPI_STORE || EPI == EPI_RESID) {
+    const int r0 = strip * 16 + g, r1 = r0 + 8;
+    float vals[4] = {v.x, v.y, v.z, v.w};
+    int rows[4] = {r0, r0, r1, r1}, toks[4] = {tok0, tok1, tok0, tok1};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (toks[i] < M && rows[i] < N) {
+        float* p = e.y + (size_t)toks[i] * e.ldy + rows[i];
+        if (EPI == EPI_RESID) *p = *p + vals[i];
+        else *p = vals[i];
+      }
+    }
+  } else if (EPI == EPI_SWIGLU) {
+    const int f = strip * 8 + g;
+    if (tok0 < M) {
+      float gt = v.x, up = v.z;
+      float sg = gt / (1.0f + expf(-gt));
+      e.h[(size_t)tok0 * e.ldh + f] = __float2half_rn(__fmul_rn(sg, up));
+    }
+    if (tok1 < M) {
+      float gt = v.y, up = v.w;
+      float sg = gt / (1.0f + expf(-gt));
+      e.h[(size_t)tok1 * e.ldh + f] = __float2half_rn(__fmul_rn(sg, up));
+    }
+  } else if (EPI == EPI_QKV) {
+    const int f0 = strip * 16;
+    const int toks[2] = {tok0, tok1};
+    if (f0 < e.nq + e.nkv) {
+      /* RoPE-permuted strip: row g = feature f0 + 2g, row g + 8 = feature f0 + 2g + 1 */
+      const int f = f0 + 2 * g;
+      const int pair = (f % e.hd) >> 1;
+      const float ev[2] = {v.x, v.y}, od[2] = {v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int tok = toks[i];
+        if (tok >= M) continue;
+        const int pos = e.row_pos[tok];
+        const int seq = e.row_seq[tok];
+        if ((unsigned)pos >= (unsigned)e.cap || (unsigned)seq >= (unsigned)e.n_seq) continue; /* never write outside the cache */
+        const float2 cs = e.rope[(size_t)pos * (e.hd >> 1) + pair];
+        const float x0 = ev[i], x1 = od[i];
+        const float y0 = __fmaf_rn(x0, cs.x, -__fmul_rn(x1, cs.y));
+        const float y1 = __fmaf_rn(x0, cs.y, __fmul_rn(x1, cs.x));
+        if (f < e.nq) {
+          float* q = e.q + (size_t)tok * e.ldq + f;
+          q[0] = y0;
+          q[1] = y1;
+        } else {
+          const int fk = f - e.nq, kvh = fk / e.hd, d = fk % e.hd;
+          __half2* kp = reinterpret_cast<__half2*>(
+              e.kc + (((size_t)seq * e.n_head_kv + kvh) * e.cap + pos) * e.hd + d);
+          *kp = __halves2half2(__float2half_rn(y0), __float2half_rn(y1));
+        }
+      }
+    } else {
+      /* V strip, identity rows */
+      const float vals[4] = {v.x, v.y, v.z, v.w};
+      const int rows[4] = {g, g, g + 8, g + 8};
+      const int tk[4] = {tok0, tok1, tok0, tok1};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (tk[i] >= M) continue;
+        const int fv = f0 + rows[i] - e.nq - e.nkv;
+        const int kvh = fv / e.hd, d = fv % e.hd;
+        const int seq = e.row_seq[tk[i]], pos = e.row_pos[tk[i]];
+        if ((unsigned)pos >= (unsigned)e.cap || (unsigned)seq >= (unsigned)e.n_seq) continue;
+        e.vc[(((size_t)seq * e.n_head_kv + kvh) * e.cap + pos) * e.hd + d] = __float2half_rn(vals[i]);
+      }
+    }
+  }
+}
+
+constexpr int kWarps = 8;
+
+template <int NT>
+__device__ __forceinline__ void reduce_and_finish_prep(float (&acc)[NT][4], float4* red, int warp, int lane) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+    red[(warp * NT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+}
+
+/* ------------------------------------------------------------------ Q4_0 kernel */
+template <int NT, int EPI>
+__global__ void __launch_bounds__(kWarps * 32) qgemv_q40_kernel(const uint8_t* __restrict__ w, int tiles,
+                                                                int N, const __half* __restrict__ x,
+                                                                int M, int ldx, EpiArgs ea) {
+  __shared__ float4 red[kWarps * NT * 32];
+  const int strip = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* sw = w + (size_t)strip * tiles * kQ40TileBytes;
+  if (warp == 0) {
+    const uint32_t total = (uint32_t)tiles * kQ40TileBytes;
+    for (uint32_t off = (uint32_t)lane * 32768u; off < total; off += 32u * 32768u) {
+      uint32_t n = total - off < 32768u ? total - off : 32768u;
+      prefetch_l2_bulk(sw + off, n);
+    }
+  }
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+
+  int tile = warp;
+  uint4 n01 = make_uint4(0, 0, 0, 0), n23 = n01, sc = n01;
+  if (tile < tiles) {
+    const uint8_t* tp = sw + (size_t)tile * kQ40TileBytes;
+    n01 = ld_stream(tp + lane * 16);
+    n23 = ld_stream(tp + 512 + lane * 16);
+    sc = ld_stream(tp + 1024 + g * 16);
+  }
+  pdl_wait();
+  pdl_trigger();
+  for (; tile < tiles; tile += kWarps) {
+    uint4 c01 = n01, c23 = n23, csc = sc;
+    const int nxt = tile + kWarps;
+    if (nxt < tiles) {
+      const uint8_t* tp = sw + (size_t)nxt * kQ40TileBytes;
+      n01 = ld_stream(tp + lane * 16);
+      n23 = ld_stream(tp + 512 + lane * 16);
+      sc = ld_stream(tp + 1024 + g * 16);
+    }
+    const uint32_t words[8] = {c01.x, c01.y, c01.z, c01.w, c23.x, c23.y, c23.z, c23.w};
+    const uint32_t scw[4] = {csc.x, csc.y, csc.z, csc.w};
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      float s[NT][4];
+      block_mma<8, NT>(words[2 * b], words[2 * b + 1], x, ldx, M, g, tile * 128 + b * 32 + t * 8, s);
+      __half2 d2 = *reinterpret_cast<const __half2*>(&scw[b]);
+      float2 dd = __half22float2(d2);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        acc[nt][0] = __fmaf_rn(dd.x, s[nt][0], acc[nt][0]);
+        acc[nt][1] = __fmaf_rn(dd.x, s[nt][1], acc[nt][1]);
+        acc[nt][2] = __fmaf_rn(dd.y, s[nt][2], acc[nt][2]);
+        acc[nt][3] = __fmaf_rn(dd.y, s[nt][3], acc[nt][3]);
+      }
+    }
+  }
+  reduce_and_finish_prep<NT>(acc, red, warp, lane);
+  __syncthreads();
+  for (int nt = warp; nt < NT; nt += kWarps) {
+    float4 s = red[nt * 32 + lane];
+#pragma unroll
+    for (int w2 = 1; w2 < kWarps; ++w2) {
+      float4 o = red[(w2 * NT + nt) * 32 + lane];
+      s.x += o.x; s.y += o.y; s.z += o.z; s.w += o.w;
+    }
+    epilogue<EPI>(ea, strip, nt, g, t, M, N, s);
+  }
+}
+
+/* ------------------------------------------------------------------ Q4_K kernel */
+template <int NT, int EPI>
+__global__ void __launch_bounds__(kWarps * 32) qgemv_q4k_kernel(const uint8_t* __restrict__ w, int tiles,
+                                                                int N, const __half* __restrict__ x,
+                                                                int M, int ldx, EpiArgs ea) {
+  __shared__ float4 red[kWarps * NT * 32];
+  const int strip = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* sw = w + (size_t)strip * tiles * kQ4KTileBytes;
+  if (warp == 0) {
+    const uint32_t total = (uint32_t)tiles * kQ4KTileBytes;
+    for (uint32_t off = (uint32_t)lane * 32768u; off < total; off += 32u * 32768u) {
+      uint32_t n = total - off < 32768u ? total - off : 32768u;
+      prefetch_l2_bulk(sw + off, n);
+    }
+  }
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  pdl_wait();
+  pdl_trigger();
+  for (int tile = warp; tile < tiles; tile += kWarps) {
+    const uint8_t* tp = sw + (size_t)tile * kQ4KTileBytes;
+    uint4 nb[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) nb[p] = ld_stream(tp + p * 512 + lane * 16);
+    const uint4 mg = ld_stream(tp + 2048 + g * 16);
+    const uint4 mg8 = ld_stream(tp + 2048 + (g + 8) * 16);
+    const float2 dg = __half22float2(*reinterpret_cast<const __half2*>(&mg.x));   /* (d, dmin) row g */
+    const float2 dg8 = __half22float2(*reinterpret_cast<const __half2*>(&mg8.x)); /* row g + 8 */
+    float t1[NT][4], t0[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) t1[nt][i] = t0[nt][i] = 0.f;
+#define ULB_Q4K_SUB(J)                                                                   \
+    {                                                                                    \
+      const uint32_t* wp = reinterpret_cast<const uint32_t*>(&nb[(J) >> 1]);            \
+      float s1[NT][4], s0[NT][4];                                                        \
+      const int kofs = tile * 256 + (J) * 32 + t * 8;                                    \
+      block_mma<0, NT>(wp[((J) & 1) * 2], wp[((J) & 1) * 2 + 1], x, ldx, M, g, kofs, s1); \
+      block_colsum<NT>(x, ldx, M, g, kofs, s0);                                          \
+      float scg, mng, scg8, mng8;                                                        \
+      q4k_sm<J>(mg.y, mg.z, mg.w, scg, mng);                                             \
+      q4k_sm<J>(mg8.y, mg8.z, mg8.w, scg8, mng8);                                        \
+      _Pragma("unroll") for (int nt = 0; nt < NT; ++nt) {                                \
+        t1[nt][0] = __fmaf_rn(scg, s1[nt][0], t1[nt][0]);                                \
+        t1[nt][1] = __fmaf_rn(scg, s1[nt][1], t1[nt][1]);                                \
+        t1[nt][2] = __fmaf_rn(scg8, s1[nt][2], t1[nt][2]);                               \
+        t1[nt][3] = __fmaf_rn(scg8, s1[nt][3], t1[nt][3]);                               \
+        t0[nt][0] = __fmaf_rn(mng, s0[nt][0], t0[nt][0]);                                \
+        t0[nt][1] = __fmaf_rn(mng, s0[nt][1], t0[nt][1]);                                \
+        t0[nt][2] = __fmaf_rn(mng8, s0[nt][2], t0[nt][2]);                               \
+        t0[nt][3] = __fmaf_rn(mng8, s0[nt][3], t0[nt][3]);                               \
+      }                                                                                  \
+    }
+    ULB_Q4K_SUB(0) ULB_Q4K_SUB(1) ULB_Q4K_SUB(2) ULB_Q4K_SUB(3)
+    ULB_Q4K_SUB(4) ULB_Q4K_SUB(5) ULB_Q4K_SUB(6) ULB_Q4K_SUB(7)
+#undef ULB_Q4K_SUB
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      acc[nt][0] = __fmaf_rn(-dg.y, t0[nt][0], __fmaf_rn(dg.x, t1[nt][0], acc[nt][0]));
+      acc[nt][1] = __fmaf_rn(-dg.y, t0[nt][1], __fmaf_rn(dg.x, t1[nt][1], acc[nt][1]));
+      acc[nt][2] = __fmaf_rn(-dg8.y, t0[nt][2], __fmaf_rn(dg8.x, t1[nt][2], acc[nt][2]));
+      acc[nt][3] = __fmaf_rn(-dg8.y, t0[nt][3], __fmaf_rn(dg8.x, t1[nt][3], acc[nt][3]));
+    }
+  }
+  reduce_and_finish_prep<NT>(acc, red, warp, lane);
+  __syncthreads();
+  for (int nt = warp; nt < NT; nt += kWarps) {
+    float4 s = red[nt * 32 + lane];
+#pragma unroll
+    for (int w2 = 1; w2 < kWarps; ++w2) {
+      float4 o = red[(w2 * NT + nt) * 32 + lane];
+      s.x += o.x; s.y += o.y; s.z += o.z; s.w += o.w;
+    }
+    epilogue<EPI>(ea, strip, nt, g, t, M, N, s);
+  }
+}
+
+/* ------------------------------------------------------------------ repack / dequant */
+__device__ __forceinline__ uint32_t place_nibbles(const uint8_t (&n)[8]) {
+  /* nibble i -> bit position {0,16,4,20,8,24,12,28}[i] */
+  return (uint32_t)n[0] | ((uint32_t)n[1] << 16) | ((uint32_t)n[2] << 4) | ((uint32_t)n[3] << 20) |
+         ((uint32_t)n[4] << 8) | ((uint32_t)n[5] << 24) | ((uint32_t)n[6] << 12) |
+         ((uint32_t)n[7] << 28);
+}
+__device__ __forceinline__ int unplace(uint32_t v, int i) {
+  const int pos[8] = {0, 16, 4, 20, 8, 24, 12, 28};
+  return (int)((v >> pos[i]) & 15u);
+}
+
+/* grid (tiles, strips), block 32 */
+__global__ void repack_q40_kernel(const uint8_t* __restrict__ raw, int K, const int* __restrict__ rmap,
+                                  uint8_t* __restrict__ out, int tiles) {
+  const int tile = blockIdx.x, strip = blockIdx.y, lane = threadIdx.x;
+  const int g = lane >> 2, t = lane & 3;
+  const size_t row_bytes = (size_t)K / 32 * 18;
+  uint8_t* tp = out + ((size_t)strip * tiles + tile) * kQ40TileBytes;
+  uint16_t d[2][4];
+  for (int b = 0; b < 4; ++b) {
+    for (int hr = 0; hr < 2; ++hr) {
+      const int raw_row = rmap[strip * 16 + g + 8 * hr];
+      uint32_t word = 0;
+      uint16_t dd = 0;
+      if (raw_row >= 0) {
+        const uint8_t* blk = raw + (size_t)raw_row * row_bytes + (size_t)(tile * 4 + b) * 18;
+        dd = (uint16_t)blk[0] | ((uint16_t)blk[1] << 8);
+        uint8_t n[8];
+        for (int i = 0; i < 8; ++i) {
+          const int wi = 8 * t + i;
+          n[i] = wi < 16 ? (blk[2 + wi] & 15) : (blk[2 + wi - 16] >> 4);
+        }
+        word = place_nibbles(n);
+      }
+      d[hr][b] = dd;
+      const int part = b >> 1;
+      reinterpret_cast<uint32_t*>(tp + part * 512 + lane * 16)[(b & 1) * 2 + hr] = word;
+    }
+  }
+  if (t == 0) {
+    for (int b = 0; b < 4; ++b)
+      reinterpret_cast<uint32_t*>(tp + 1024 + g * 16)[b] = (uint32_t)d[0][b] | ((uint32_t)d[1][b] << 16);
+  }
+}
+
+__global__ void repack_q4k_kernel(const uint8_t* __restrict__ raw, int K, const int* __restrict__ rmap,
+                                  uint8_t* __restrict__ out, int tiles) {
+  const int tile = blockIdx.x, strip = blockIdx.y, lane = threadIdx.x;
+  const int g = lane >> 2, t = lane & 3;
+  const size_t row_bytes = (size_t)K / 256 * 144;
+  uint8_t* tp = out + ((size_t)strip * tiles + tile) * kQ4KTileBytes;
+  for (int j = 0; j < 8; ++j) {
+    for (int hr = 0; hr < 2; ++hr) {
+      const int raw_row = rmap[strip * 16 + g + 8 * hr];
+      uint32_t word = 0;
+      if (raw_row >= 0) {
+        const uint8_t* qs = raw + (size_t)raw_row * row_bytes + (size_t)tile * 144 + 16;
+        uint8_t n[8];
+        for (int i = 0; i < 8; ++i) {
+          const uint8_t byte = qs[32 * (j >> 1) + 8 * t + i];
+          n[i] = (j & 1) ? (byte >> 4) : (byte & 15);
+        }
+        word = place_nibbles(n);
+      }
+      reinterpret_cast<uint32_t*>(tp + (j >> 1) * 512 + lane * 16)[(j & 1) * 2 + hr] = word;
+    }
+  }
+  if (lane < 16) {
+    const int raw_row = rmap[strip * 16 + lane];
+    uint8_t* m = tp + 2048 + lane * 16;
+    for (int i = 0; i < 16; ++i)
+      m[i] = raw_row >= 0 ? raw[(size_t)raw_row * row_bytes + (size_t)tile * 144 + i] : 0;
+  }
+}
+
+/* dequant: grid (tiles, strips), block 32; out[row][k] fp32, rows < N only */
+__global__ void dequant_q40_kernel(const uint8_t* __restrict__ w, int tiles, int N, int K, float* __restrict__ out) {
+  const int tile = blockIdx.x, strip = blockIdx.y, lane = threadIdx.x;
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* tp = w + ((size_t)strip * tiles + tile) * kQ40TileBytes;
+  for (int b = 0; b < 4; ++b)
+    for (int hr = 0; hr < 2; ++hr) {
+      const int row = strip * 16 + g + 8 * hr;
+      if (row >= N) continue;
+      const uint32_t word = reinterpret_cast<const uint32_t*>(tp + (b >> 1) * 512 + lane * 16)[(b & 1) * 2 + hr];
+      const uint16_t dh = (uint16_t)(reinterpret_cast<const uint32_t*>(tp + 1024 + g * 16)[b] >> (16 * hr));
+      const float d = __half2float(__ushort_as_half(dh));
+      for (int i = 0; i < 8; ++i)
+        out[(size_t)row * K + tile * 128 + b * 32 + 8 * t + i] = __fmul_rn(d, (float)(unplace(word, i) - 8));
+    }
+}
+
+__global__ void dequant_q4k_kernel(const uint8_t* __restrict__ w, int tiles, int N, int K, float* __restrict__ out) {
+  const int tile = blockIdx.x, strip = blockIdx.y, lane = threadIdx.x;
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* tp = w + ((size_t)strip * tiles + tile) * kQ4KTileBytes;
+  for (int hr = 0; hr < 2; ++hr) {
+    const int row = strip * 16 + g + 8 * hr;
+    if (row >= N) continue;
+    const uint8_t* m = tp + 2048 + (g + 8 * hr) * 16;
+    const float d = __half2float(__ushort_as_half((uint16_t)(m[0] | (m[1] << 8))));
+    const float dmin = __half2float(__ushort_as_half((uint16_t)(m[2] | (m[3] << 8))));
+    const uint8_t* s12 = m + 4;
+    for (int j = 0; j < 8; ++j) {
+      int sc, mn;
+      if (j < 4) { sc = s12[j] & 63; mn = s12[j + 4] & 63; }
+      else { sc = (s12[j + 4] & 0x0F) | ((s12[j - 4] >> 6) << 4); mn = (s12[j + 4] >> 4) | ((s12[j] >> 6) << 4); }
+      const float s = __fmul_rn(d, (float)sc), mm = __fmul_rn(dmin, (float)mn);
+      const uint32_t word = reinterpret_cast<const uint32_t*>(tp + (j >> 1) * 512 + lane * 16)[(j & 1) * 2 + hr];
+      for (int i = 0; i < 8; ++i)
+        out[(size_t)row * K + tile * 256 + j * 32 + 8 * t + i] = __fsub_rn(__fmul_rn(s, (float)unplace(word, i)), mm);
+    }
+  }
+}
+
+template <int NT, int EPI>
+int launch_nt(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a) {
+  dim3 grid(w->n_strips), block(kWarps * 32);
+  cudaError_t e;
+  if (w->type == ULB_TYPE_Q4_0)
+    e = launch_k(c, qgemv_q40_kernel<NT, EPI>, grid, block, 0, (const uint8_t*)w->dev, w->tiles, w->N, x, M, ldx, a);
+  else
+    e = launch_k(c, qgemv_q4k_kernel<NT, EPI>, grid, block, 0, (const uint8_t*)w->dev, w->tiles, w->N, x, M, ldx, a);
+  if (e != cudaSuccess) return cuda_error(e, "qgemv launch", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
+template <int EPI>
+int launch_epi(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a) {
+  if (M <= 8) return launch_nt<1, EPI>(c, w, x, M, ldx, a);
+  if (M <= 16) return launch_nt<2, EPI>(c, w, x, M, ldx, a);
+  if (M <= 32) return launch_nt<4, EPI>(c, w, x, M, ldx, a);
+  if (w->type == ULB_TYPE_Q4_0) return launch_nt<8, EPI>(c, w, x, M, ldx, a);
+  return set_error(ULB_EINVAL, "qgemv: Q4_K chunk of %d rows exceeds 32", M);
+}
+
+}  // namespace
+
+/* Max rows per launch (larger M is chunked by the caller of launch_qgemv). */
+static int max_rows_per_launch(int type) { return type == ULB_TYPE_Q4_0 ? 64 : 32; }
+
+int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
+  ULB_CHECK(w && (w->type == ULB_TYPE_Q4_0 || w->type == ULB_TYPE_Q4_K), ULB_EINVAL, "qgemv: weight is not Q4_0/Q4_K");
+  ULB_CHECK(M >= 0 && ldx % 8 == 0 && ldx >= w->K, ULB_EINVAL, "qgemv: bad M=%d / ldx=%d (K=%d)", M, ldx, w->K);
+  ULB_CHECK(((uintptr_t)x & 15) == 0, ULB_EINVAL, "qgemv: activations must be 16-byte aligned");
+  if (M == 0) return ULB_OK;
+  const int step = max_rows_per_launch(w->type);
+  for (int m0 = 0; m0 < M; m0 += step) {
+    const int mc = M - m0 < step ? M - m0 : step;
+    EpiArgs a = a0;
+    const __half* xc = x + (size_t)m0 * ldx;
+    if (a.y) a.y += (size_t)m0 * a.ldy;
+    if (a.h) a.h += (size_t)m0 * a.ldh;
+    if (a.q) a.q += (size_t)m0 * a.ldq;
+    if (a.row_seq) a.row_seq += m0;
+    if (a.row_pos) a.row_pos += m0;
+    int rc;
+    switch (epi) {
+      case EPI_STORE: rc = launch_epi<EPI_STORE>(c, w, xc, mc, ldx, a); break;
+      case EPI_RESID: rc = launch_epi<EPI_RESID>(c, w, xc, mc, ldx, a); break;
+      case EPI_SWIGLU: rc = launch_epi<EPI_SWIGLU>(c, w, xc, mc, ldx, a); break;
+      case EPI_QKV: rc = launch_epi<EPI_QKV>(c, w, xc, mc, ldx, a); break;
+      default: return set_error(ULB_EINVAL, "qgemv: bad epilogue %d", epi);
+    }
+    if (rc) return rc;
+  }
+  return ULB_OK;
+}
+
+int launch_dequant(Ctx* c, const Tensor* w, float* out) {
+  dim3 grid(w->tiles, w->n_strips), block(32);
+  if (w->type == ULB_TYPE_Q4_0)
+    dequant_q40_kernel<<<grid, block, 0, c->stream>>>((const uint8_t*)w->dev, w->tiles, w->N, w->K, out);
+  else if (w->type == ULB_TYPE_Q4_K)
+    dequant_q4k_kernel<<<grid, block, 0, c->stream>>>((const uint8_t*)w->dev, w->tiles, w->N, w->K, out);
+  else
+    return set_error(ULB_EINVAL, "dequant: tensor type %d is not quantised", w->type);
+  ULB_CUDA(cudaGetLastError());
+  return ULB_OK;
+}
+
+int repack_q4(Ctx* c, int type, const void* dev_raw, int raw_rows, int K, const int* host_row_map,
+              int packed_rows, Tensor* out) {
+  ULB_CHECK(type == ULB_TYPE_Q4_0 || type == ULB_TYPE_Q4_K, ULB_EINVAL, "repack: type %d", type);
+  const int tk = tile_k(type);
+  ULB_CHECK(K > 0 && K % tk == 0, ULB_EUNSUPPORTED, "repack: K=%d must be a multiple of %d", K, tk);
+  ULB_CHECK(packed_rows > 0 && packed_rows % kStripRows == 0, ULB_EINVAL, "repack: rows %d", packed_rows);
+  for (int i = 0; i < packed_rows; ++i)
+    ULB_CHECK(host_row_map[i] < raw_rows, ULB_EINVAL, "repack: row map out of range");
+  out->type = type;
+  out->K = K;
+  out->n_strips = packed_rows / kStripRows;
+  out->tiles = K / tk;
+  out->bytes = (size_t)out->n_strips * out->tiles * tile_bytes(type);
+  ULB_TRY(dev_alloc(c, &out->dev, out->bytes));
+  int* dmap = nullptr;
+  ULB_TRY(dev_alloc(c, (void**)&dmap, (size_t)packed_rows * sizeof(int)));
+  cudaError_t e = cudaMemcpyAsync(dmap, host_row_map, (size_t)packed_rows * sizeof(int), cudaMemcpyHostToDevice, c->stream);
+  if (e == cudaSuccess) {
+    dim3 grid(out->tiles, out->n_strips), block(32);
+    if (type == ULB_TYPE_Q4_0)
+      repack_q40_kernel<<<grid, block, 0, c->stream>>>((const uint8_t*)dev_raw, K, dmap, (uint8_t*)out->dev, out->tiles);
+    else
+      repack_q4k_kernel<<<grid, block, 0, c->stream>>>((const uint8_t*)dev_raw, K, dmap, (uint8_t*)out->dev, out->tiles);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  dev_free(c, dmap, (size_t)packed_rows * sizeof(int));
+  if (e != cudaSuccess) return cuda_error(e, "repack", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
+}  // namespace ulb

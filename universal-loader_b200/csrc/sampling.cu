@@ -1,0 +1,493 @@
+/*
+ * sampling.cu — logit warping, draft-token sampling and speculative rejection sampling.
+ *
+ * Replaces InferenceEngine::sample_token (src/inference/inference_engine.cpp:340-367: an
+ * unseeded inverse CDF over a zero logits vector), the intent of TextGenerator's
+ * apply_temperature / apply_top_k / apply_top_p (src/api/gguf_loader.cpp:90-155), and
+ * SpeculativeDecoder::verify_speculation (src/inference/speculative_decoder.cpp:89-110, a
+ * token-match heuristic) with standard speculative rejection sampling (Leviathan et al.
+ * 2023; Chen et al. 2023).
+ *
+ * Warp definition (identical in the CPU oracle): z = logit / T; keep z >= k-th largest z
+ * (top-k); e = exp(z - max z) in fp64; keep tokens whose strictly-more-probable mass is
+ * < top_p * sum(e) (top-p); p = e / sum over kept.  Keep sets are decided on exact
+ * comparisons of z (radix select on the order-preserving integer key of z), so the same
+ * logits give the same kept set on host and device.
+ *
+ * Kernels: row_stats (one CTA per row: max, keep threshold, normaliser, argmax) over all
+ * target and draft rows of a round in parallel; sample (stats + inverse CDF for the draft
+ * tokens); decide (one CTA per sequence: accept test, residual / bonus sampling, commit).
+ */
+#include "ulb_internal.h"
+
+namespace ulb {
+
+namespace {
+
+constexpr int ST = 256; /* threads per row CTA */
+
+struct RowStats {
+  float mx;    /* max z                                  */
+  float thr;   /* keep iff z >= thr                      */
+  double Z;    /* sum of exp(z - mx) over the kept set   */
+  int amax;    /* argmax of the raw logits (lowest index) */
+  int pad;
+};
+
+/* z = logit / T with -0 folded to +0, so key order and float order agree */
+__device__ __forceinline__ float zof(float x, float T) { return __fadd_rn(__fdiv_rn(x, T), 0.0f); }
+
+__device__ __forceinline__ uint32_t fkey(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float unkey(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+struct SmemRed {
+  float f[ST / 32];
+  int i[ST / 32];
+  double d[ST / 32];
+  unsigned int hist_u[256];
+  double hist_d[256];
+  double seg[ST];
+  uint32_t prefix;
+  int found;
+  double above;
+};
+
+__device__ float block_max(float v, SmemRed& s) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) s.f[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = s.f[0];
+#pragma unroll
+  for (int w = 1; w < ST / 32; ++w) r = fmaxf(r, s.f[w]);
+  return r;
+}
+
+/* deterministic fp64 sum: per-thread partials reduced in a fixed tree */
+__device__ double block_sum_d(double v, SmemRed& s) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) s.d[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double r = s.d[0];
+#pragma unroll
+  for (int w = 1; w < ST / 32; ++w) r += s.d[w];
+  return r;
+}
+
+/* argmax, lowest index on ties */
+__device__ int block_argmax(const float* l, int V, SmemRed& s) {
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += ST) {
+    const float x = l[i];
+    if (x > bv || (x == bv && i < bi)) { bv = x; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) { s.f[threadIdx.x >> 5] = bv; s.i[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  bv = s.f[0]; bi = s.i[0];
+  for (int w = 1; w < ST / 32; ++w)
+    if (s.f[w] > bv || (s.f[w] == bv && s.i[w] < bi)) { bv = s.f[w]; bi = s.i[w]; }
+  return bi == 0x7fffffff ? 0 : bi;
+}
+
+/* key of the k-th largest z (count based radix select, exact) */
+__device__ uint32_t kth_largest_key(const float* l, int V, float T, int k, SmemRed& s) {
+  uint32_t prefix = 0, mask = 0;
+  int need = k; /* rank within the current prefix class (1-based) */
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = threadIdx.x; b < 256; b += ST) s.hist_u[b] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < V; i += ST) {
+      const uint32_t key = fkey(zof(l[i], T));
+      if ((key & mask) == prefix) atomicAdd(&s.hist_u[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int cum = 0, b = 255;
+      for (; b > 0; --b) {
+        if (cum + (int)s.hist_u[b] >= need) break;
+        cum += s.hist_u[b];
+      }
+      s.prefix = prefix | ((uint32_t)b << shift);
+      s.found = need - cum;
+    }
+    __syncthreads();
+    prefix = s.prefix;
+    need = s.found;
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+/*
+ * key of the smallest z kept by top-p: the first element in descending z order whose
+ * inclusive cumulative mass reaches P (mass histograms in fp64).
+ */
+__device__ uint32_t topp_key(const float* l, int V, float T, float mx, uint32_t key_lo, double P, SmemRed& s) {
+  uint32_t prefix = 0, mask = 0;
+  double above = 0.0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = threadIdx.x; b < 256; b += ST) s.hist_d[b] = 0.0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < V; i += ST) {
+      const float z = zof(l[i], T);
+      const uint32_t key = fkey(z);
+      if (key >= key_lo && (key & mask) == prefix)
+        atomicAdd(&s.hist_d[(key >> shift) & 255u], exp((double)(z - mx)));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int b = 255, last_nonempty = -1;
+      double a = above;
+      for (; b >= 0; --b) {
+        if (s.hist_d[b] > 0.0) {
+          last_nonempty = b;
+          if (a + s.hist_d[b] >= P) break;
+          a += s.hist_d[b];
+        }
+      }
+      if (b < 0) { /* rounding left P just above the total: keep everything down to the last bin */
+        b = last_nonempty < 0 ? 0 : last_nonempty;
+        a = a - s.hist_d[b];
+      }
+      s.prefix = prefix | ((uint32_t)b << shift);
+      s.above = a;
+    }
+    __syncthreads();
+    prefix = s.prefix;
+    above = s.above;
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+__device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowStats& out, SmemRed& s) {
+  const int amax = block_argmax(l, V, s);
+  if (!(w.temperature > 0.f)) {
+    if (threadIdx.x == 0) { out.mx = l[amax]; out.thr = -INFINITY; out.Z = 1.0; out.amax = amax; }
+    return;
+  }
+  const float T = w.temperature;
+  const float mx = zof(l[amax], T); /* division is monotone: max z = z of the max logit */
+  uint32_t key_lo = 0;
+  if (w.top_k > 0 && w.top_k < V) key_lo = kth_largest_key(l, V, T, w.top_k, s);
+  if (w.top_p > 0.f && w.top_p < 1.f) {
+    double zs = 0.0;
+    for (int i = threadIdx.x; i < V; i += ST) {
+      const float z = zof(l[i], T);
+      if (fkey(z) >= key_lo) zs += exp((double)(z - mx));
+    }
+    const double Z0 = block_sum_d(zs, s);
+    key_lo = topp_key(l, V, T, mx, key_lo, (double)w.top_p * Z0, s);
+  }
+  double zs = 0.0;
+  for (int i = threadIdx.x; i < V; i += ST) {
+    const float z = zof(l[i], T);
+    if (fkey(z) >= key_lo) zs += exp((double)(z - mx));
+  }
+  const double Z = block_sum_d(zs, s);
+  if (threadIdx.x == 0) {
+    out.mx = mx;
+    out.thr = key_lo == 0 ? -INFINITY : unkey(key_lo);
+    out.Z = Z;
+    out.amax = amax;
+  }
+}
+
+/* warped probability weight e (unnormalised) of token i under stats st */
+__device__ __forceinline__ double warped_e(const float* l, int i, float T, const RowStats& st) {
+  const float z = zof(l[i], T);
+  if (!(z >= st.thr)) return 0.0;
+  return exp((double)(z - st.mx));
+}
+
+/*
+ * Inverse CDF in index order over weights produced by wfun(i) (fp64, >= 0): returns the
+ * smallest i whose cumulative weight exceeds target.  Fixed per-thread contiguous segments.
+ */
+template <typename WF>
+__device__ int block_inv_cdf(int V, double target, WF wfun, SmemRed& s) {
+  const int seg = (V + ST - 1) / ST;
+  const int b0 = threadIdx.x * seg, b1 = min(V, b0 + seg);
+  double sum = 0.0;
+  for (int i = b0; i < b1; ++i) sum += wfun(i);
+  __syncthreads();
+  s.seg[threadIdx.x] = sum;
+  if (threadIdx.x == 0) s.found = 0x7fffffff;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double c = 0.0;
+    for (int t = 0; t < ST; ++t) { const double v = s.seg[t]; s.seg[t] = c; c += v; }
+  }
+  __syncthreads();
+  double cum = s.seg[threadIdx.x];
+  if (b0 < b1 && cum + sum > target) {
+    for (int i = b0; i < b1; ++i) {
+      const double wv = wfun(i);
+      if (wv <= 0.0) continue;
+      cum += wv;
+      if (cum > target) { atomicMin(&s.found, i); break; }
+    }
+  }
+  __syncthreads();
+  int r = s.found;
+  if (r == 0x7fffffff) { /* target at/above the total through rounding: last positive weight */
+    __syncthreads();
+    int last = -1;
+    for (int i = threadIdx.x; i < V; i += ST)
+      if (wfun(i) > 0.0) last = max(last, i);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+    if ((threadIdx.x & 31) == 0) s.i[threadIdx.x >> 5] = last;
+    __syncthreads();
+    r = s.i[0];
+    for (int w2 = 1; w2 < ST / 32; ++w2) r = max(r, s.i[w2]);
+    if (r < 0) r = 0;
+  }
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ float rng_u(uint64_t seed, uint32_t round, uint32_t seq, uint32_t slot, uint32_t tag) {
+  return ulb_uniform(seed, round, seq, slot, tag);
+}
+
+/* ------------------------------------------------------------------ kernels */
+
+/* one CTA per row: draft / first-token sampling. out[row * out_stride] = token */
+__global__ void __launch_bounds__(ST) sample_kernel(const float* __restrict__ logits, int V, int ld, ulb_warp w,
+                                                    uint64_t seed, const uint32_t* dev_round, uint32_t round,
+                                                    uint32_t slot, uint32_t tag, uint32_t seq_base, int32_t* out,
+                                                    int out_stride) {
+  __shared__ SmemRed s;
+  __shared__ RowStats st;
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x;
+  const float* l = logits + (size_t)row * ld;
+  compute_row_stats(l, V, w, st, s);
+  __syncthreads();
+  int tok;
+  if (!(w.temperature > 0.f)) {
+    tok = st.amax;
+  } else {
+    const uint32_t seq = seq_base + (uint32_t)row;
+    const uint32_t r = dev_round ? dev_round[seq] : round;
+    const float u = rng_u(seed, r, seq, slot, tag);
+    const float T = w.temperature;
+    const RowStats stc = st;
+    tok = block_inv_cdf(V, (double)u * stc.Z, [&](int i) { return warped_e(l, i, T, stc); }, s);
+  }
+  if (threadIdx.x == 0) out[(size_t)row * out_stride] = tok;
+}
+
+/* stats for p rows [B][k+1] followed by q rows [B][k] */
+__global__ void __launch_bounds__(ST) stats_kernel(const float* __restrict__ p, const float* __restrict__ q, int B,
+                                                   int k, int V, ulb_warp w, RowStats* __restrict__ out) {
+  __shared__ SmemRed s;
+  __shared__ RowStats st;
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x;
+  const int np = B * (k + 1);
+  const float* l = row < np ? p + (size_t)row * V : q + (size_t)(row - np) * V;
+  compute_row_stats(l, V, w, st, s);
+  __syncthreads();
+  if (threadIdx.x == 0) out[row] = st;
+}
+
+struct SpecCommit {
+  int32_t* hist;     /* [B][hist_len] committed tokens (prompt first)      */
+  int hist_len;
+  int32_t* L;        /* [B] committed length                                 */
+  int32_t* done;     /* [B]                                                  */
+  const int32_t* prompt_len; /* [B]                                          */
+  int max_new;
+  uint32_t* round;   /* [B] per-sequence round counter, incremented here     */
+  unsigned long long* stats; /* [4] (unused), drafted, accepted, committed  */
+  int32_t* active;   /* [B] rounds in which the sequence was still decoding   */
+};
+
+/* one CTA per sequence */
+__global__ void __launch_bounds__(ST) decide_kernel(const float* __restrict__ p, const float* __restrict__ q,
+                                                    const int32_t* __restrict__ draft, const RowStats* __restrict__ rs,
+                                                    int B, int k, int V, ulb_warp w, uint64_t seed,
+                                                    const uint32_t* dev_round, uint32_t round,
+                                                    int32_t* out_tokens, int32_t* out_n, SpecCommit cm) {
+  __shared__ SmemRed s;
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x;
+  const bool greedy = !(w.temperature > 0.f);
+  const float T = greedy ? 1.f : w.temperature;
+  const uint32_t rnd = dev_round ? dev_round[b] : round;
+  const int np = B * (k + 1);
+  int n = 0, tok = -1;
+  for (int i = 0; i < k; ++i) {
+    const int x = draft[b * k + i];
+    const RowStats sp = rs[b * (k + 1) + i];
+    if (greedy) {
+      if (x == sp.amax) { ++n; continue; }
+      tok = sp.amax;
+      break;
+    }
+    const RowStats sq = rs[np + b * k + i];
+    const float* pl = p + ((size_t)b * (k + 1) + i) * V;
+    const float* ql = q + ((size_t)b * k + i) * V;
+    const bool in_vocab = (unsigned)x < (unsigned)V; /* a token outside the vocabulary is rejected */
+    const double px = in_vocab ? warped_e(pl, x, T, sp) / sp.Z : 0.0;
+    const double qx = in_vocab ? warped_e(ql, x, T, sq) / sq.Z : 0.0;
+    const float u = rng_u(seed, rnd, (uint32_t)b, (uint32_t)i, ULB_RNG_ACCEPT);
+    if ((double)u * qx < px) { ++n; continue; }
+    /* residual norm(max(0, p - q)) */
+    auto resid = [&](int v) {
+      const double r = warped_e(pl, v, T, sp) / sp.Z - warped_e(ql, v, T, sq) / sq.Z;
+      return r > 0.0 ? r : 0.0;
+    };
+    double part = 0.0;
+    for (int v = threadIdx.x; v < V; v += ST) part += resid(v);
+    const double R = block_sum_d(part, s);
+    const float u2 = rng_u(seed, rnd, (uint32_t)b, (uint32_t)i, ULB_RNG_RESID);
+    if (R > 0.0) tok = block_inv_cdf(V, (double)u2 * R, resid, s);
+    else tok = block_inv_cdf(V, (double)u2 * sp.Z, [&](int v) { return warped_e(pl, v, T, sp); }, s);
+    break;
+  }
+  if (tok < 0) {
+    const RowStats sp = rs[b * (k + 1) + k];
+    if (greedy) tok = sp.amax;
+    else {
+      const float* pl = p + ((size_t)b * (k + 1) + k) * V;
+      const float u2 = rng_u(seed, rnd, (uint32_t)b, (uint32_t)k, ULB_RNG_RESID);
+      tok = block_inv_cdf(V, (double)u2 * sp.Z, [&](int v) { return warped_e(pl, v, T, sp); }, s);
+    }
+  }
+  if (threadIdx.x != 0) return;
+  if (out_tokens) {
+    for (int i = 0; i < n; ++i) out_tokens[b * (k + 1) + i] = draft[b * k + i];
+    out_tokens[b * (k + 1) + n] = tok;
+    for (int i = n + 1; i <= k; ++i) out_tokens[b * (k + 1) + i] = -1;
+  }
+  if (out_n) out_n[b] = n;
+  if (cm.hist) {
+    if (!cm.done[b]) {
+      const int L = cm.L[b];
+      int32_t* h = cm.hist + (size_t)b * cm.hist_len;
+      for (int i = 0; i < n; ++i) h[L + i] = draft[b * k + i];
+      h[L + n] = tok;
+      cm.L[b] = L + n + 1;
+      if (L + n + 1 - cm.prompt_len[b] >= cm.max_new) cm.done[b] = 1;
+      atomicAdd(&cm.stats[1], (unsigned long long)k);
+      atomicAdd(&cm.stats[2], (unsigned long long)n);
+      atomicAdd(&cm.stats[3], (unsigned long long)(n + 1));
+      cm.active[b] += 1;
+    }
+    cm.round[b] = rnd + 1;
+  }
+}
+
+}  // namespace
+
+int launch_sample_seq(Ctx* c, const float* logits, int rows, int V, int ld, const ulb_warp* w, uint64_t seed,
+                      const uint32_t* dev_round, uint32_t round, uint32_t slot, uint32_t tag, uint32_t seq_base,
+                      int32_t* out, int out_stride);
+int launch_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* draft, int B, int k, int V,
+                       const ulb_warp* w, uint64_t seed, const uint32_t* dev_round, uint32_t round,
+                       int32_t* out_tokens, int32_t* out_n, void* stats_scratch, const void* commit);
+
+size_t sample_scratch_bytes(int, int) { return 0; }
+size_t accept_scratch_bytes(int B, int k, int) { return sizeof(RowStats) * (size_t)B * (2 * k + 1); }
+
+int launch_sample(Ctx* c, const float* logits, int rows, int V, int ld, const ulb_warp* w, uint64_t seed,
+                  const uint32_t* dev_round, uint32_t round, uint32_t slot, uint32_t tag, int32_t* out,
+                  int out_stride, float*) {
+  if (rows == 0) return ULB_OK;
+  return launch_sample_seq(c, logits, rows, V, ld, w, seed, dev_round, round, slot, tag, 0, out, out_stride);
+}
+
+int launch_sample_seq(Ctx* c, const float* logits, int rows, int V, int ld, const ulb_warp* w, uint64_t seed,
+                      const uint32_t* dev_round, uint32_t round, uint32_t slot, uint32_t tag, uint32_t seq_base,
+                      int32_t* out, int out_stride) {
+  if (rows == 0) return ULB_OK;
+  cudaError_t e = launch_k(c, sample_kernel, dim3(rows), dim3(ST), 0, logits, V, ld, *w, seed, dev_round, round,
+                           slot, tag, seq_base, out, out_stride);
+  if (e != cudaSuccess) return cuda_error(e, "sample launch", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
+int launch_accept_commit(Ctx* c, const float* p, const float* q, const int32_t* draft, int B, int k, int V,
+                         const ulb_warp* w, uint64_t seed, const uint32_t* dev_round, void* stats_scratch,
+                         int32_t* hist, int hist_len, int32_t* L, int32_t* done, const int32_t* plen, int max_new,
+                         uint32_t* round, unsigned long long* stats, int32_t* active) {
+  SpecCommit cm;
+  cm.hist = hist; cm.hist_len = hist_len; cm.L = L; cm.done = done; cm.prompt_len = plen;
+  cm.max_new = max_new; cm.round = round; cm.stats = stats; cm.active = active;
+  return launch_accept_impl(c, p, q, draft, B, k, V, w, seed, dev_round, 0, nullptr, nullptr, stats_scratch, &cm);
+}
+
+int launch_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* draft, int B, int k, int V,
+                       const ulb_warp* w, uint64_t seed, const uint32_t* dev_round, uint32_t round,
+                       int32_t* out_tokens, int32_t* out_n, void* stats_scratch, const void* commit) {
+  if (B == 0) return ULB_OK;
+  RowStats* rs = (RowStats*)stats_scratch;
+  const int rows = B * (k + 1) + B * k;
+  cudaError_t e = launch_k(c, stats_kernel, dim3(rows), dim3(ST), 0, p, q, B, k, V, *w, rs);
+  if (e != cudaSuccess) return cuda_error(e, "stats launch", __FILE__, __LINE__);
+  SpecCommit cm = {};
+  if (commit) cm = *(const SpecCommit*)commit;
+  e = launch_k(c, decide_kernel, dim3(B), dim3(ST), 0, p, q, draft, (const RowStats*)rs, B, k, V, *w, seed,
+               dev_round, round, out_tokens, out_n, cm);
+  if (e != cudaSuccess) return cuda_error(e, "decide launch", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
+int launch_spec_accept(Ctx* c, const float* p, const float* q, const int32_t* draft, int B, int k, int V,
+                       const ulb_warp* w, uint64_t seed, const uint32_t* dev_round, uint32_t round,
+                       int32_t* out_tokens, int32_t* out_n, double* scratch) {
+  return launch_accept_impl(c, p, q, draft, B, k, V, w, seed, dev_round, round, out_tokens, out_n, scratch, nullptr);
+}
+
+}  // namespace ulb
+
+using namespace ulb;
+
+extern "C" int ulb_sample(ulb_ctx* ctx, const float* logits, int rows, int V, int ld, const ulb_warp* w,
+                          uint64_t seed, uint32_t round, uint32_t slot, uint32_t tag, int32_t* out) {
+  ULB_CHECK(ctx && logits && w && out, ULB_EINVAL, "ulb_sample: NULL argument");
+  ULB_CHECK(rows >= 0 && V > 0 && ld >= V, ULB_EINVAL, "ulb_sample: bad shape");
+  ULB_CUDA(cudaSetDevice(ctx->c.device));
+  return launch_sample(&ctx->c, logits, rows, V, ld, w, seed, nullptr, round, slot, tag, out, 1, nullptr);
+}
+
+extern "C" int ulb_spec_accept(ulb_ctx* ctx, const float* p, const float* q, const int32_t* draft, int B, int k,
+                               int V, const ulb_warp* w, uint64_t seed, uint32_t round, int32_t* out_tokens,
+                               int32_t* out_n) {
+  ULB_CHECK(ctx && p && w && out_tokens && out_n, ULB_EINVAL, "ulb_spec_accept: NULL argument");
+  ULB_CHECK(B >= 0 && k >= 0 && V > 0, ULB_EINVAL, "ulb_spec_accept: bad shape");
+  ULB_CHECK(k == 0 || (q && draft), ULB_EINVAL, "ulb_spec_accept: draft logits/tokens required for k > 0");
+  Ctx* c = &ctx->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  void* scratch = nullptr;
+  const size_t bytes = accept_scratch_bytes(B, k, V);
+  ULB_TRY(dev_alloc(c, &scratch, bytes));
+  int rc = launch_spec_accept(c, p, q, draft, B, k, V, w, seed, nullptr, round, out_tokens, out_n, (double*)scratch);
+  dev_free(c, scratch, bytes);
+  return rc;
+}
