@@ -215,6 +215,33 @@ def test_spec_accept_matches_oracle(ctx, warp):
     assert want_n.max() > 0 and want_n.min() < k  # both branches covered
 
 
+def test_spec_accept_is_lossless_chi2(ctx):
+    """Committed first token of a round ~ p exactly (Leviathan et al. 2023): 6000 sequences
+    with the same p / q logits and independent Philox uniforms, drafts sampled on the GPU."""
+    import ulb_capi as U
+    B, V = 6000, 6
+    rng = np.random.default_rng(3)
+    p1 = (rng.standard_normal(V) * 1.5).astype(np.float32)
+    q1 = (rng.standard_normal(V) * 1.5).astype(np.float32)
+    pl = np.broadcast_to(p1, (B, 2, V)).copy()
+    ql = np.broadcast_to(q1, (B, 1, V)).copy()
+    qb = ctx.buffer(ql)
+    db = ctx.buffer(nbytes=B * 4)
+    w = U.Warp(1.0, 0, 1.0)
+    U.check(U.lib().ulb_sample(ctx.h, qb.ptr, B, V, V, C.byref(w), 11, 0, 0, U.RNG_DRAFT, db.ptr))
+    draft = db.download(np.int32, (B, 1))
+    qb.free(); db.free()
+    out, n = _accept_gpu(ctx, pl, ql, draft, (1.0, 0, 1.0), seed=11, rnd=0)
+    p = orc.warp_probs(p1, 1.0)
+    q = orc.warp_probs(q1, 1.0)
+    dcount = np.bincount(draft[:, 0], minlength=V)
+    assert ((dcount - q * B) ** 2 / (q * B)).sum() < 25.0  # drafts ~ q
+    counts = np.bincount(out[:, 0], minlength=V)
+    chi2 = ((counts - p * B) ** 2 / (p * B)).sum()
+    assert chi2 < 25.0, (chi2, counts, p * B)  # 5 dof: p-value ~ 1e-4
+    assert 0 < (n == 1).mean() < 1
+
+
 def test_spec_accept_k0_is_plain_sampling(ctx):
     rng = np.random.default_rng(2)
     pl = (rng.standard_normal((4, 1, 1000))).astype(np.float32)

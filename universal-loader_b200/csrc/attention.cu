@@ -8,12 +8,13 @@
  * 42-45, 153): GQA (kv head = q head / group), causal masking, online softmax over KV
  * blocks, KV read from the cache.
  *
- * Split-KV (flash-decoding): grid = (KV chunk of 64 keys, kv head, sequence x row block).
- * All q heads of one GQA group and all rows of the block share each K/V chunk staged in
- * shared memory, so the cache is read once per verify step.  A chunk's partial
- * (max, sum, unnormalised output) goes to scratch; the CTA that arrives last for its
- * (sequence, row block, kv head) merges the chunks in chunk order, so the result is
- * deterministic and a row's arithmetic depends only on its own position.
+ * grid = (key split of 512 positions, kv head, sequence x row block).  All q heads of a GQA
+ * group and all rows of the block share each 64-key K/V block, staged in shared memory with
+ * cp.async and double-buffered, so the cache is read once per step.  Inside a split the CTA
+ * keeps an online softmax (running max / sum, rescaled output).  Contexts up to 512 keys
+ * need no merge; longer ones write one partial per split and the CTA that arrives last for
+ * its (sequence, row block, kv head) merges them in split order.  The split structure depends
+ * only on a row's position, so a row's arithmetic never depends on what else is batched.
  */
 #include "ulb_internal.h"
 
@@ -21,27 +22,63 @@ namespace ulb {
 
 namespace {
 
-constexpr int ACH = 64;     /* keys per chunk */
-constexpr int AQMAX = 64;   /* queries (heads x rows) per CTA */
-constexpr int ATHREADS = 128;
+constexpr int BK = 64;       /* keys per staged block */
+constexpr int SPLIT = 64;    /* keys per CTA: many CTAs per (sequence, kv head) */
+constexpr int MAXSPLIT = 128; /* capacity <= 8192 */
+constexpr int MERGE_UNROLL = 8;
+constexpr int AQMAX = 64;    /* queries (heads x rows) per CTA */
+constexpr int ATHREADS = 256;
+constexpr int ANW = ATHREADS / 32;
+constexpr int MAXITEMS = AQMAX * 64 / ATHREADS; /* output (query, dim pair) items per thread, hd <= 128 */
 
 struct AttnParams {
-  int H, Hkv, hd, cap, G, rps, RB, n_rb, max_chunks, ldq, n_seq;
+  int H, Hkv, hd, cap, G, rps, RB, n_rb, max_splits, ldq, n_seq;
   float scale;
 };
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+struct Smem {
+  float* qs;     /* [AQMAX][hd]               */
+  float* ss;     /* [AQMAX][BK] scores / p    */
+  int* qpos;     /* [AQMAX]                   */
+  float* mrun;   /* [AQMAX] running max       */
+  float* lrun;   /* [AQMAX] running sum       */
+  float* scl;    /* [AQMAX] rescale of block  */
+  uint4* ks;     /* [2][BK][hd/8] swizzled    */
+  uint4* vs;     /* [2][BK][hd/8]             */
+};
+
+__device__ __forceinline__ Smem carve(float* base, int hd) {
+  Smem s;
+  s.qs = base;
+  s.ss = s.qs + AQMAX * hd;
+  s.qpos = reinterpret_cast<int*>(s.ss + AQMAX * BK);
+  s.mrun = reinterpret_cast<float*>(s.qpos + AQMAX);
+  s.lrun = s.mrun + AQMAX;
+  s.scl = s.lrun + AQMAX;
+  s.ks = reinterpret_cast<uint4*>(s.scl + AQMAX);
+  s.vs = s.ks + 2 * BK * (hd / 8);
+  return s;
+}
+
 __global__ void __launch_bounds__(ATHREADS) attn_kernel(AttnParams p, const float* __restrict__ q,
-                                                        const __half* __restrict__ kc,
-                                                        const __half* __restrict__ vc,
+                                                        const __half* __restrict__ kc, const __half* __restrict__ vc,
                                                         const int* __restrict__ row_seq,
-                                                        const int* __restrict__ row_pos,
-                                                        __half* __restrict__ out, float* scratch,
-                                                        int* counters) {
-  extern __shared__ float smem[];
-  const int chunk = blockIdx.x, kvh = blockIdx.y, gz = blockIdx.z;
+                                                        const int* __restrict__ row_pos, __half* __restrict__ out,
+                                                        float* scratch, int* counters) {
+  extern __shared__ __align__(16) float smem_raw[];
+  const int split = blockIdx.x, kvh = blockIdx.y, gz = blockIdx.z;
   const int gi = gz / p.n_rb, rb = gz % p.n_rb;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hd = p.hd, hd2 = hd >> 1;
+  const int hd = p.hd, hd2 = hd >> 1, vpr = hd / 8;
+  const Smem S = carve(smem_raw, hd);
   pdl_wait();
   pdl_trigger();
 
@@ -52,143 +89,224 @@ __global__ void __launch_bounds__(ATHREADS) attn_kernel(AttnParams p, const floa
   int last_pos = 0;
   for (int r = 0; r < nr; ++r) last_pos = max(last_pos, row_pos[m0 + r]);
   last_pos = min(last_pos, p.cap - 1); /* positions past the cache never index it */
-  const int n_valid = last_pos / ACH + 1;
-  if (chunk >= n_valid) return;
+  const int n_splits = last_pos / SPLIT + 1;
+  if (split >= n_splits) return;
   const int seq = row_seq[m0];
   if ((unsigned)seq >= (unsigned)p.n_seq) return;
-  const int k0 = chunk * ACH;
-  const int nk = min(ACH, last_pos + 1 - k0);
+  const int k_begin = split * SPLIT;
+  const int k_end = min(k_begin + SPLIT, last_pos + 1);
+  const int nblocks = (k_end - k_begin + BK - 1) / BK;
+  const size_t kvbase = (((size_t)seq * p.Hkv + kvh) * p.cap) * hd;
 
-  /* shared layout */
-  float* qs = smem;                                   /* [Q][hd]            */
-  float* ss = qs + AQMAX * hd;                        /* [Q][ACH]           */
-  int* qpos = reinterpret_cast<int*>(ss + AQMAX * ACH); /* [Q]              */
-  float* ml = reinterpret_cast<float*>(qpos + AQMAX); /* [Q][2] (m, l)      */
-  __half2* ks = reinterpret_cast<__half2*>(ml + 2 * AQMAX); /* [ACH][hd2 + 1] */
-  __half2* vs = ks + ACH * (hd2 + 1);                  /* [ACH][hd2]         */
+  auto stage = [&](int b, int buf) {
+    const int kb = k_begin + b * BK;
+    const int nk = min(BK, k_end - kb);
+    uint4* kd = S.ks + buf * BK * vpr;
+    uint4* vd = S.vs + buf * BK * vpr;
+    for (int i = tid; i < nk * vpr; i += ATHREADS) {
+      const int j = i / vpr, c = i % vpr;
+      const int cs = (c & ~7) | ((c ^ j) & 7); /* XOR swizzle inside each group of 8 chunks */
+      const size_t src = kvbase + (size_t)(kb + j) * hd + c * 8;
+      cp_async16(kd + j * vpr + cs, kc + src);
+      cp_async16(vd + j * vpr + c, vc + src);
+    }
+  };
 
-  for (int i = tid; i < Q * hd; i += ATHREADS) {
-    const int qi = i / hd, d = i % hd;
+  for (int i = tid; i < Q * (hd / 4); i += ATHREADS) {
+    const int qi = i / (hd / 4), c = i % (hd / 4);
     const int r = qi / p.G, gq = qi % p.G;
-    const int h = kvh * p.G + gq;
-    qs[i] = q[(size_t)(m0 + r) * p.ldq + h * hd + d];
+    cp_async16(S.qs + qi * hd + c * 4, q + (size_t)(m0 + r) * p.ldq + (kvh * p.G + gq) * hd + c * 4);
   }
-  for (int qi = tid; qi < Q; qi += ATHREADS) qpos[qi] = row_pos[m0 + qi / p.G];
-  const size_t kvbase = (((size_t)seq * p.Hkv + kvh) * p.cap + k0) * hd;
-  const int vec_per_row = hd / 8;
-  for (int i = tid; i < nk * vec_per_row; i += ATHREADS) {
-    const int j = i / vec_per_row, c = i % vec_per_row;
-    const uint4 kv4 = __ldg(reinterpret_cast<const uint4*>(kc + kvbase + (size_t)j * hd) + c);
-    const uint4 vv4 = __ldg(reinterpret_cast<const uint4*>(vc + kvbase + (size_t)j * hd) + c);
-    const uint32_t kw[4] = {kv4.x, kv4.y, kv4.z, kv4.w};
-    uint32_t* krow = reinterpret_cast<uint32_t*>(ks + j * (hd2 + 1));
-#pragma unroll
-    for (int e = 0; e < 4; ++e) krow[c * 4 + e] = kw[e];
-    reinterpret_cast<uint4*>(vs + j * hd2)[c] = vv4;
-  }
-  __syncthreads();
-
-  /* scores: warp per query, lanes over keys; sequential fma over d (same order as the CPU) */
-  for (int qi = warp; qi < Q; qi += ATHREADS / 32) {
-    const float2* qv = reinterpret_cast<const float2*>(qs + qi * hd);
-    for (int j = lane; j < ACH; j += 32) {
-      float s = -INFINITY;
-      if (j < nk && k0 + j <= qpos[qi]) {
-        const __half2* kr = ks + j * (hd2 + 1);
-        float a = 0.f;
-        for (int d2 = 0; d2 < hd2; ++d2) {
-          const float2 kf = __half22float2(kr[d2]);
-          const float2 qf = qv[d2];
-          a = __fmaf_rn(qf.x, kf.x, a);
-          a = __fmaf_rn(qf.y, kf.y, a);
-        }
-        s = __fmul_rn(a, p.scale);
-      }
-      ss[qi * ACH + j] = s;
-    }
-  }
-  __syncthreads();
-  /* per-query chunk softmax */
-  for (int qi = warp; qi < Q; qi += ATHREADS / 32) {
-    float m = -INFINITY;
-    for (int j = lane; j < ACH; j += 32) m = fmaxf(m, ss[qi * ACH + j]);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int j = lane; j < ACH; j += 32) {
-      const float s = ss[qi * ACH + j];
-      const float e = s == -INFINITY ? 0.f : expf(s - m);
-      ss[qi * ACH + j] = e;
-      l += e;
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) { ml[2 * qi] = m; ml[2 * qi + 1] = l; }
-  }
-  __syncthreads();
-
-  /* P.V: thread per (query, d pair); sequential over keys */
-  float* part = nullptr;
-  const int qstride = p.G * p.RB;
-  if (n_valid > 1)
-    part = scratch + (((size_t)gz * p.Hkv + kvh) * p.max_chunks + chunk) * (size_t)qstride * (hd + 2);
-  for (int it = tid; it < Q * hd2; it += ATHREADS) {
-    const int qi = it / hd2, d2 = it % hd2;
-    float ox = 0.f, oy = 0.f;
-    const float* pr = ss + qi * ACH;
-    for (int j = 0; j < nk; ++j) {
-      const float pj = pr[j];
-      const float2 vf = __half22float2(vs[j * hd2 + d2]);
-      ox = __fmaf_rn(pj, vf.x, ox);
-      oy = __fmaf_rn(pj, vf.y, oy);
-    }
-    if (n_valid == 1) {
-      const float l = ml[2 * qi + 1];
-      const int r = qi / p.G, gq = qi % p.G;
-      const int h = kvh * p.G + gq;
-      __half2* op = reinterpret_cast<__half2*>(out + (size_t)(m0 + r) * p.H * hd + h * hd) + d2;
-      *op = __halves2half2(__float2half_rn(ox / l), __float2half_rn(oy / l));
-    } else {
-      float* pq = part + (size_t)qi * (hd + 2);
-      pq[2 + 2 * d2] = ox;
-      pq[3 + 2 * d2] = oy;
-    }
-  }
-  if (n_valid == 1) return;
+  stage(0, 0);
+  cp_commit();
   for (int qi = tid; qi < Q; qi += ATHREADS) {
-    part[(size_t)qi * (hd + 2)] = ml[2 * qi];
-    part[(size_t)qi * (hd + 2) + 1] = ml[2 * qi + 1];
+    S.qpos[qi] = row_pos[m0 + qi / p.G];
+    S.mrun[qi] = -INFINITY;
+    S.lrun[qi] = 0.f;
+  }
+  const int n_items = Q * hd2;
+  float2 o[MAXITEMS];
+#pragma unroll
+  for (int k = 0; k < MAXITEMS; ++k) o[k] = make_float2(0.f, 0.f);
+
+  for (int b = 0; b < nblocks; ++b) {
+    const int buf = b & 1;
+    if (b + 1 < nblocks) {
+      stage(b + 1, buf ^ 1);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    const int kb = k_begin + b * BK;
+    const int nk = min(BK, k_end - kb);
+    const uint4* kbuf = S.ks + buf * BK * vpr;
+    /* scores: warp per query, lanes over keys; sequential fma over d (as the CPU oracle) */
+    for (int qi = warp; qi < Q; qi += ANW) {
+      const float4* qv = reinterpret_cast<const float4*>(S.qs + qi * hd);
+      const int qp = S.qpos[qi];
+      for (int j = lane; j < BK; j += 32) {
+        float s = -INFINITY;
+        if (j < nk && kb + j <= qp) {
+          const uint4* kr = kbuf + j * vpr;
+          float a = 0.f;
+          for (int c = 0; c < vpr; ++c) {
+            const uint4 kk = kr[(c & ~7) | ((c ^ j) & 7)];
+            const float4 qa = qv[2 * c], qb = qv[2 * c + 1];
+            const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kk.x));
+            const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kk.y));
+            const float2 k45 = __half22float2(*reinterpret_cast<const __half2*>(&kk.z));
+            const float2 k67 = __half22float2(*reinterpret_cast<const __half2*>(&kk.w));
+            a = __fmaf_rn(qa.x, k01.x, a);
+            a = __fmaf_rn(qa.y, k01.y, a);
+            a = __fmaf_rn(qa.z, k23.x, a);
+            a = __fmaf_rn(qa.w, k23.y, a);
+            a = __fmaf_rn(qb.x, k45.x, a);
+            a = __fmaf_rn(qb.y, k45.y, a);
+            a = __fmaf_rn(qb.z, k67.x, a);
+            a = __fmaf_rn(qb.w, k67.y, a);
+          }
+          s = __fmul_rn(a, p.scale);
+        }
+        S.ss[qi * BK + j] = s;
+      }
+      __syncwarp();
+      /* online softmax update of this query (the same warp wrote its scores) */
+      float mb = -INFINITY;
+      for (int j = lane; j < BK; j += 32) mb = fmaxf(mb, S.ss[qi * BK + j]);
+#pragma unroll
+      for (int off = 16; off; off >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+      const float mold = S.mrun[qi];
+      const float mnew = fmaxf(mold, mb);
+      float lb = 0.f;
+      for (int j = lane; j < BK; j += 32) {
+        const float s = S.ss[qi * BK + j];
+        const float e = s == -INFINITY ? 0.f : expf(s - mnew);
+        S.ss[qi * BK + j] = e;
+        lb += e;
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) lb += __shfl_xor_sync(0xffffffffu, lb, off);
+      __syncwarp();
+      if (lane == 0) {
+        const float sc = mold == -INFINITY ? 0.f : expf(mold - mnew);
+        S.scl[qi] = sc;
+        S.lrun[qi] = __fmaf_rn(S.lrun[qi], sc, lb);
+        S.mrun[qi] = mnew;
+      }
+    }
+    __syncthreads();
+    /* P.V: thread per (query, dim pair) items; sequential over keys */
+    const __half2* vbuf = reinterpret_cast<const __half2*>(S.vs + buf * BK * vpr);
+#pragma unroll
+    for (int k = 0; k < MAXITEMS; ++k) {
+      const int it = tid + k * ATHREADS;
+      if (it < n_items) {
+        const int qi = it / hd2, d2 = it % hd2;
+        const float sc = S.scl[qi];
+        float ox = o[k].x * sc, oy = o[k].y * sc;
+        const float* pr = S.ss + qi * BK;
+        for (int j = 0; j < nk; ++j) {
+          const float pj = pr[j];
+          const float2 vf = __half22float2(vbuf[j * hd2 + d2]);
+          ox = __fmaf_rn(pj, vf.x, ox);
+          oy = __fmaf_rn(pj, vf.y, oy);
+        }
+        o[k] = make_float2(ox, oy);
+      }
+    }
+    __syncthreads(); /* the next iteration restages this buffer */
+  }
+
+  auto out_ptr = [&](int qi) {
+    const int r = qi / p.G, gq = qi % p.G;
+    return reinterpret_cast<__half2*>(out + (size_t)(m0 + r) * p.H * hd + (kvh * p.G + gq) * hd);
+  };
+  if (n_splits == 1) {
+#pragma unroll
+    for (int k = 0; k < MAXITEMS; ++k) {
+      const int it = tid + k * ATHREADS;
+      if (it < n_items) {
+        const int qi = it / hd2, d2 = it % hd2;
+        const float l = S.lrun[qi];
+        out_ptr(qi)[d2] = __halves2half2(__float2half_rn(o[k].x / l), __float2half_rn(o[k].y / l));
+      }
+    }
+    return;
+  }
+  /* partial of this split: (m, l) then the unnormalised output */
+  const int qstride = p.G * p.RB;
+  const size_t pstride = (size_t)qstride * (hd + 2);
+  float* base = scratch + ((size_t)gz * p.Hkv + kvh) * p.max_splits * pstride;
+  float* part = base + split * pstride;
+#pragma unroll
+  for (int k = 0; k < MAXITEMS; ++k) {
+    const int it = tid + k * ATHREADS;
+    if (it < n_items) {
+      const int qi = it / hd2, d2 = it % hd2;
+      part[(size_t)qi * (hd + 2) + 2 + 2 * d2] = o[k].x;
+      part[(size_t)qi * (hd + 2) + 3 + 2 * d2] = o[k].y;
+    }
+  }
+  for (int qi = tid; qi < Q; qi += ATHREADS) {
+    part[(size_t)qi * (hd + 2)] = S.mrun[qi];
+    part[(size_t)qi * (hd + 2) + 1] = S.lrun[qi];
   }
   __threadfence();
   __syncthreads();
   __shared__ int is_last;
-  if (tid == 0) {
-    const int prev = atomicAdd(&counters[gz * p.Hkv + kvh], 1);
-    is_last = prev == n_valid - 1;
-  }
+  if (tid == 0) is_last = atomicAdd(&counters[gz * p.Hkv + kvh], 1) == n_splits - 1;
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  const float* base = scratch + (((size_t)gz * p.Hkv + kvh) * p.max_chunks) * (size_t)qstride * (hd + 2);
-  const size_t cstride = (size_t)qstride * (hd + 2);
-  for (int it = tid; it < Q * hd2; it += ATHREADS) {
-    const int qi = it / hd2, d2 = it % hd2;
+  /* merge in split order.  (1) every (query, split) max / sum is fetched in parallel into
+     shared memory; (2) a thread per query turns them into weights; (3) each output item
+     sums its splits with the loads of MERGE_UNROLL splits in flight at once. */
+  float* msm = S.qs; /* [Q][n_splits] (max, then weight)    */
+  float* lsm = S.ss; /* [Q][n_splits] sums                   */
+  for (int idx = tid; idx < Q * n_splits; idx += ATHREADS) {
+    const int qi = idx / n_splits, c = idx % n_splits;
+    msm[idx] = __ldcg(base + c * pstride + (size_t)qi * (hd + 2));
+    lsm[idx] = __ldcg(base + c * pstride + (size_t)qi * (hd + 2) + 1);
+  }
+  __syncthreads();
+  for (int qi = tid; qi < Q; qi += ATHREADS) {
     float M = -INFINITY;
-    for (int c = 0; c < n_valid; ++c) M = fmaxf(M, __ldcg(base + c * cstride + (size_t)qi * (hd + 2)));
-    float L = 0.f, ox = 0.f, oy = 0.f;
-    for (int c = 0; c < n_valid; ++c) {
-      const float* pc = base + c * cstride + (size_t)qi * (hd + 2);
-      const float mc = __ldcg(pc);
-      if (mc == -INFINITY) continue;
-      const float w = expf(mc - M);
-      L = __fmaf_rn(__ldcg(pc + 1), w, L);
-      ox = __fmaf_rn(__ldcg(pc + 2 + 2 * d2), w, ox);
-      oy = __fmaf_rn(__ldcg(pc + 3 + 2 * d2), w, oy);
+    for (int c = 0; c < n_splits; ++c) M = fmaxf(M, msm[qi * n_splits + c]);
+    float L = 0.f;
+    for (int c = 0; c < n_splits; ++c) {
+      const float mc = msm[qi * n_splits + c];
+      const float w = mc == -INFINITY ? 0.f : expf(mc - M);
+      msm[qi * n_splits + c] = w;
+      L = __fmaf_rn(lsm[qi * n_splits + c], w, L);
     }
-    const int r = qi / p.G, gq = qi % p.G;
-    const int h = kvh * p.G + gq;
-    __half2* op = reinterpret_cast<__half2*>(out + (size_t)(m0 + r) * p.H * hd + h * hd) + d2;
-    *op = __halves2half2(__float2half_rn(ox / L), __float2half_rn(oy / L));
+    S.lrun[qi] = L;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < MAXITEMS; ++k) {
+    const int it = tid + k * ATHREADS;
+    if (it < n_items) {
+      const int qi = it / hd2, d2 = it % hd2;
+      float ox = 0.f, oy = 0.f;
+      for (int c0 = 0; c0 < n_splits; c0 += MERGE_UNROLL) {
+        float2 oc[MERGE_UNROLL];
+#pragma unroll
+        for (int u = 0; u < MERGE_UNROLL; ++u)
+          if (c0 + u < n_splits)
+            oc[u] = __ldcg(reinterpret_cast<const float2*>(base + (c0 + u) * pstride + (size_t)qi * (hd + 2) + 2) + d2);
+#pragma unroll
+        for (int u = 0; u < MERGE_UNROLL; ++u)
+          if (c0 + u < n_splits) {
+            const float w = msm[qi * n_splits + c0 + u];
+            ox = __fmaf_rn(oc[u].x, w, ox);
+            oy = __fmaf_rn(oc[u].y, w, oy);
+          }
+      }
+      const float L = S.lrun[qi];
+      out_ptr(qi)[d2] = __halves2half2(__float2half_rn(ox / L), __float2half_rn(oy / L));
+    }
   }
   if (tid == 0) counters[gz * p.Hkv + kvh] = 0; /* ready for the next launch / graph replay */
 }
@@ -200,18 +318,21 @@ void attn_geometry(const ulb_attn_desc* d, int M, int rps, int max_pos, AttnPara
   p->cap = d->capacity;
   p->G = d->n_head / d->n_head_kv;
   p->rps = rps;
+  p->max_splits = max_pos / SPLIT + 1;
   p->RB = AQMAX / p->G < 1 ? 1 : AQMAX / p->G;
+  /* the merge stages (query, split) pairs in shared memory: at most AQMAX * BK of them */
+  const int rb_merge = (AQMAX * BK) / (p->G * p->max_splits);
+  if (p->RB > rb_merge) p->RB = rb_merge < 1 ? 1 : rb_merge;
   if (p->RB > rps) p->RB = rps;
   p->n_rb = (rps + p->RB - 1) / p->RB;
-  p->max_chunks = max_pos / ACH + 1;
   p->scale = d->scale;
   p->n_seq = d->n_seq;
   *n_groups = M / rps;
 }
 
 size_t attn_smem(int hd) {
-  return sizeof(float) * ((size_t)AQMAX * hd + AQMAX * ACH + 2 * AQMAX) + sizeof(int) * AQMAX +
-         sizeof(__half2) * ((size_t)ACH * (hd / 2 + 1) + (size_t)ACH * (hd / 2));
+  return sizeof(float) * ((size_t)AQMAX * hd + AQMAX * BK + 3 * AQMAX) + sizeof(int) * AQMAX +
+         sizeof(__half) * 4 * (size_t)BK * hd;
 }
 
 }  // namespace
@@ -221,16 +342,20 @@ size_t attention_scratch_floats(const ulb_attn_desc* d, int M, int rps, int max_
   int ng;
   attn_geometry(d, M, rps, max_pos, &p, &ng);
   *n_counters = ng * p.n_rb * p.Hkv;
-  return (size_t)ng * p.n_rb * p.Hkv * p.max_chunks * (size_t)(p.G * p.RB) * (p.hd + 2);
+  return (size_t)ng * p.n_rb * p.Hkv * p.max_splits * (size_t)(p.G * p.RB) * (p.hd + 2);
 }
 
 int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, const __half* k,
                      const __half* v, const int* row_seq, const int* row_pos, int M, int rps,
                      __half* out, float* scratch, int* counters, size_t scratch_floats, int n_counters) {
   ULB_CHECK(d->n_head % d->n_head_kv == 0, ULB_EINVAL, "attention: n_head %% n_head_kv != 0");
-  ULB_CHECK(d->head_dim % 8 == 0 && d->head_dim <= 256, ULB_EUNSUPPORTED, "attention: head_dim %d", d->head_dim);
+  ULB_CHECK(d->head_dim % 16 == 0 && d->head_dim <= 128, ULB_EUNSUPPORTED, "attention: head_dim %d", d->head_dim);
   ULB_CHECK(d->n_head / d->n_head_kv <= AQMAX, ULB_EUNSUPPORTED, "attention: GQA group > %d", AQMAX);
+  ULB_CHECK(d->capacity <= SPLIT * MAXSPLIT, ULB_EUNSUPPORTED, "attention: capacity %d > %d", d->capacity,
+            SPLIT * MAXSPLIT);
   ULB_CHECK(rps > 0 && M % rps == 0, ULB_EINVAL, "attention: M=%d not a multiple of rows_per_seq=%d", M, rps);
+  ULB_CHECK(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 && ldq % 4 == 0,
+            ULB_EINVAL, "attention: q / k / v must be 16-byte aligned (ldq a multiple of 4)");
   if (M == 0) return ULB_OK;
   AttnParams p;
   int ng;
@@ -238,16 +363,16 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
   p.ldq = ldq;
   int need_c = 0;
   const size_t need = attention_scratch_floats(d, M, rps, d->capacity - 1, &need_c);
-  ULB_CHECK(scratch_floats >= need && n_counters >= need_c, ULB_EINVAL,
+  ULB_CHECK(p.max_splits == 1 || (scratch_floats >= need && n_counters >= need_c), ULB_EINVAL,
             "attention: scratch %zu floats / %d counters, need %zu / %d", scratch_floats, n_counters, need, need_c);
-  const size_t smem = attn_smem(p.hd);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(256));
+    ULB_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(128)));
     attr_set = true;
   }
-  dim3 grid(p.max_chunks, p.Hkv, ng * p.n_rb), block(ATHREADS);
-  cudaError_t e = launch_k(c, attn_kernel, grid, block, smem, p, q, k, v, row_seq, row_pos, out, scratch, counters);
+  dim3 grid(p.max_splits, p.Hkv, ng * p.n_rb), block(ATHREADS);
+  cudaError_t e = launch_k(c, attn_kernel, grid, block, attn_smem(p.hd), p, q, k, v, row_seq, row_pos, out, scratch,
+                           counters);
   if (e != cudaSuccess) return cuda_error(e, "attention launch", __FILE__, __LINE__);
   return ULB_OK;
 }
@@ -275,6 +400,7 @@ extern "C" int ulb_attention(ulb_ctx* ctx, const ulb_attn_desc* d, const float* 
                                              row_seq, row_pos, M, rps, (__half*)out, scratch, counters, nf, nc)
                           : cuda_error(e, "memset", __FILE__, __LINE__);
   }
+  if (rc == ULB_OK) rc = check_device_errors(c);
   dev_free(c, counters, (size_t)nc * sizeof(int));
   dev_free(c, scratch, nf * sizeof(float));
   return rc;

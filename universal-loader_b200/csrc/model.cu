@@ -94,14 +94,33 @@ __global__ void embed_kernel(const void* __restrict__ table, int table_type, int
 /* out[s] = fp16((x[row] * r) * g), r = 1 / sqrt(mean(x^2) + eps); row = s*sel + sel-1 if sel */
 __global__ void rmsnorm_kernel(const float* __restrict__ x, int ldx, const float* __restrict__ g, int d, float eps,
                                int sel, __half* __restrict__ out, int ldo) {
+  /* the whole row is loaded with independent 128-bit loads before any arithmetic, so the
+     kernel pays one memory latency, not one per element (d <= 8192 with 256 threads) */
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
   const int s = blockIdx.x;
   const int row = sel > 0 ? s * sel + sel - 1 : s;
-  const float* xv = x + (size_t)row * ldx;
+  const float4* xv = reinterpret_cast<const float4*>(x + (size_t)row * ldx);
+  const float4* gv = reinterpret_cast<const float4*>(g);
+  const int n4 = d >> 2;
+  float4 v[8], gg[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = i * 256 + threadIdx.x;
+    if (j < n4) { v[i] = xv[j]; gg[i] = __ldg(gv + j); }
+  }
   float ss = 0.f;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) ss = __fmaf_rn(xv[i], xv[i], ss);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = i * 256 + threadIdx.x;
+    if (j < n4) {
+      ss = __fmaf_rn(v[i].x, v[i].x, ss);
+      ss = __fmaf_rn(v[i].y, v[i].y, ss);
+      ss = __fmaf_rn(v[i].z, v[i].z, ss);
+      ss = __fmaf_rn(v[i].w, v[i].w, ss);
+    }
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -109,8 +128,17 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, int ldx, const float
   float tot = 0.f;
   for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
-  for (int i = threadIdx.x; i < d; i += blockDim.x)
-    out[(size_t)s * ldo + i] = __float2half_rn(__fmul_rn(__fmul_rn(xv[i], r), g[i]));
+  __half2* o2 = reinterpret_cast<__half2*>(out + (size_t)s * ldo);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = i * 256 + threadIdx.x;
+    if (j < n4) {
+      o2[2 * j] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v[i].x, r), gg[i].x)),
+                                 __float2half_rn(__fmul_rn(__fmul_rn(v[i].y, r), gg[i].y)));
+      o2[2 * j + 1] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v[i].z, r), gg[i].z)),
+                                     __float2half_rn(__fmul_rn(__fmul_rn(v[i].w, r), gg[i].w)));
+    }
+  }
 }
 
 }  // namespace
@@ -157,16 +185,18 @@ static int ensure_attn(KV* kv, int M, int rps) {
   int nc = 0;
   const size_t nf = attention_scratch_floats(&ad, M, rps, kv->cap - 1, &nc);
   if (nf <= kv->attn_floats && nc <= kv->n_counters) return ULB_OK;
+  /* grow to the largest shape seen so far: every prepared shape must keep fitting */
+  const size_t f2 = nf > kv->attn_floats ? nf : kv->attn_floats;
+  const int c2 = nc > kv->n_counters ? nc : kv->n_counters;
   Ctx* c = kv->m->c;
   dev_free(c, kv->attn_scratch, kv->attn_floats * 4);
   dev_free(c, kv->attn_counters, (size_t)kv->n_counters * 4);
   kv->attn_scratch = nullptr; kv->attn_counters = nullptr; kv->attn_floats = 0; kv->n_counters = 0;
-  const size_t f2 = nf > kv->attn_floats ? nf : kv->attn_floats;
   ULB_TRY(dev_alloc(c, (void**)&kv->attn_scratch, f2 * 4));
   kv->attn_floats = f2;
-  ULB_TRY(dev_alloc(c, (void**)&kv->attn_counters, (size_t)nc * 4));
-  kv->n_counters = nc;
-  ULB_CUDA(cudaMemsetAsync(kv->attn_counters, 0, (size_t)nc * 4, c->stream));
+  ULB_TRY(dev_alloc(c, (void**)&kv->attn_counters, (size_t)c2 * 4));
+  kv->n_counters = c2;
+  ULB_CUDA(cudaMemsetAsync(kv->attn_counters, 0, (size_t)c2 * 4, c->stream));
   return ULB_OK;
 }
 
@@ -302,6 +332,7 @@ int ulb_model_create(ulb_ctx* ctx, const ulb_model_desc* d, ulb_model** out) {
   ULB_CHECK(d->n_head % d->n_head_kv == 0, ULB_EINVAL, "n_head %d not a multiple of n_head_kv %d", d->n_head, d->n_head_kv);
   ULB_CHECK(d->head_dim % 16 == 0, ULB_EUNSUPPORTED, "head_dim %d must be a multiple of 16", d->head_dim);
   ULB_CHECK(d->d_ff % 8 == 0 && d->d_model % 8 == 0, ULB_EUNSUPPORTED, "d_model/d_ff must be multiples of 8");
+  ULB_CHECK(d->d_model <= 8192, ULB_EUNSUPPORTED, "d_model %d > 8192 (rmsnorm keeps a row in registers)", d->d_model);
   std::unique_ptr<ulb_model> m(new ulb_model());
   m->m.c = &ctx->c;
   m->m.d = *d;
@@ -527,6 +558,7 @@ int ulb_model_forward(ulb_ctx* ctx, ulb_model* mm, ulb_kv* kvh, int M, int rps, 
   }
   dev_free(c, err, sizeof(int));
   if (rc == ULB_OK && herr) rc = set_error(ULB_EINVAL, "ulb_model_forward: token id out of range");
+  if (rc == ULB_OK) rc = check_device_errors(c);
   return rc;
 }
 

@@ -82,19 +82,31 @@ __device__ __forceinline__ void nib_pairs(uint32_t v, uint32_t& p01, uint32_t& p
   p67 = hfma2u((v8 & 0x00F000F0u) | MAGIC, SIXTEENTH, NEG);
 }
 
+/*
+ * Activation rows of the lane: xr[nt] = x row (nt*8 + g) + 8t, or a zero row for padding
+ * tokens >= M, so every B-fragment fetch is one unpredicated 128-bit load at an offset.
+ */
+template <int NT>
+__device__ __forceinline__ void activation_rows(const __half* __restrict__ x, const __half* __restrict__ xzero, int ldx,
+                                                int M, int g, int t, const __half* (&xr)[NT]) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int n = nt * 8 + g;
+    xr[nt] = (n < M ? x + (size_t)n * ldx : xzero) + t * 8;
+  }
+}
+
 /* One 32-weight block for rows (g, g+8): integer dot products with NT n-tiles of x. */
 template <int BIAS, int NT>
-__device__ __forceinline__ void block_mma(uint32_t vg, uint32_t vg8, const __half* __restrict__ x,
-                                          int ldx, int M, int g, int kofs, float (&s)[NT][4]) {
+__device__ __forceinline__ void block_mma(uint32_t vg, uint32_t vg8, const __half* const (&xr)[NT], int kofs,
+                                          float (&s)[NT][4]) {
   uint32_t a01, a23, a45, a67, b01, b23, b45, b67;
   nib_pairs<BIAS>(vg, a01, a23, a45, a67);
   nib_pairs<BIAS>(vg8, b01, b23, b45, b67);
   const float zero[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const int n = nt * 8 + g;
-    uint4 bx = make_uint4(0u, 0u, 0u, 0u);
-    if (n < M) bx = __ldg(reinterpret_cast<const uint4*>(x + (size_t)n * ldx + kofs));
+    const uint4 bx = __ldg(reinterpret_cast<const uint4*>(xr[nt] + kofs));
     float tmp[4];
     mma16816(tmp, a01, b01, a23, b23, bx.x, bx.y, zero);
     mma16816(s[nt], a45, b45, a67, b67, bx.z, bx.w, tmp);
@@ -103,15 +115,12 @@ __device__ __forceinline__ void block_mma(uint32_t vg, uint32_t vg8, const __hal
 
 /* Column sums of x over one 32-wide block, via MMA with an all-ones A. */
 template <int NT>
-__device__ __forceinline__ void block_colsum(const __half* __restrict__ x, int ldx, int M, int g,
-                                             int kofs, float (&s)[NT][4]) {
+__device__ __forceinline__ void block_colsum(const __half* const (&xr)[NT], int kofs, float (&s)[NT][4]) {
   const uint32_t ONES = 0x3C003C00u;
   const float zero[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const int n = nt * 8 + g;
-    uint4 bx = make_uint4(0u, 0u, 0u, 0u);
-    if (n < M) bx = __ldg(reinterpret_cast<const uint4*>(x + (size_t)n * ldx + kofs));
+    const uint4 bx = __ldg(reinterpret_cast<const uint4*>(xr[nt] + kofs));
     float tmp[4];
     mma16816(tmp, ONES, ONES, ONES, ONES, bx.x, bx.y, zero);
     mma16816(s[nt], ONES, ONES, ONES, ONES, bx.z, bx.w, tmp);
@@ -219,105 +228,225 @@ __device__ __forceinline__ void reduce_and_finish_prep(float (&acc)[NT][4], floa
     red[(warp * NT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
 }
 
-/* ------------------------------------------------------------------ Q4_0 kernel */
-template <int NT, int EPI>
-__global__ void __launch_bounds__(kWarps * 32) qgemv_q40_kernel(const uint8_t* __restrict__ w, int tiles,
-                                                                int N, const __half* __restrict__ x,
-                                                                int M, int ldx, EpiArgs ea) {
-  __shared__ float4 red[kWarps * NT * 32];
-  const int strip = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const uint8_t* sw = w + (size_t)strip * tiles * kQ40TileBytes;
-  if (warp == 0) {
-    const uint32_t total = (uint32_t)tiles * kQ40TileBytes;
-    for (uint32_t off = (uint32_t)lane * 32768u; off < total; off += 32u * 32768u) {
-      uint32_t n = total - off < 32768u ? total - off : 32768u;
-      prefetch_l2_bulk(sw + off, n);
-    }
-  }
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+/* ------------------------------------------------------------------ staged weight pipeline */
+/*
+ * A strip's packed bytes are copied global -> shared with cp.async.bulk in chunks of 27 KB
+ * (24 Q4_0 tiles or 12 Q4_K tiles) through a ring of 3 buffers, each guarded by an
+ * mbarrier.  The first three chunks are issued before griddepcontrol.wait, so the weight
+ * stream of this kernel overlaps the previous kernel in the stream.
+ */
+constexpr int kChunkBytes = 27648;
+constexpr int kNBuf = 3;
+constexpr int kMaxChunks = 32;
+template <int QT> struct QTraits;
+template <> struct QTraits<ULB_TYPE_Q4_0> { static constexpr int TB = kQ40TileBytes, CT = 24; };
+template <> struct QTraits<ULB_TYPE_Q4_K> { static constexpr int TB = kQ4KTileBytes, CT = 12; };
 
-  int tile = warp;
-  uint4 n01 = make_uint4(0, 0, 0, 0), n23 = n01, sc = n01;
-  if (tile < tiles) {
-    const uint8_t* tp = sw + (size_t)tile * kQ40TileBytes;
-    n01 = ld_stream(tp + lane * 16);
-    n23 = ld_stream(tp + 512 + lane * 16);
-    sc = ld_stream(tp + 1024 + g * 16);
-  }
-  pdl_wait();
-  pdl_trigger();
-  for (; tile < tiles; tile += kWarps) {
-    uint4 c01 = n01, c23 = n23, csc = sc;
-    const int nxt = tile + kWarps;
-    if (nxt < tiles) {
-      const uint8_t* tp = sw + (size_t)nxt * kQ40TileBytes;
-      n01 = ld_stream(tp + lane * 16);
-      n23 = ld_stream(tp + 512 + lane * 16);
-      sc = ld_stream(tp + 1024 + g * 16);
-    }
-    const uint32_t words[8] = {c01.x, c01.y, c01.z, c01.w, c23.x, c23.y, c23.z, c23.w};
-    const uint32_t scw[4] = {csc.x, csc.y, csc.z, csc.w};
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+/* try_wait with a 1 ms suspend hint: a waiting thread sleeps until the phase completes
+   instead of spinning on the issue slots the consumer warps need */
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+/* Wait for phase `parity`; gives up after `limit_ns` of wall time (returns false). */
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  while (!mbar_try(bar, parity))
+    if (gtimer() - t0 > limit_ns) return false;
+  return true;
+}
+
+template <int NT>
+__device__ __forceinline__ void q40_tile(const uint8_t* tp, int tile, const __half* const (&xr)[NT], int lane, int g,
+                                         float (&acc)[NT][4]) {
+  const uint4 c01 = *reinterpret_cast<const uint4*>(tp + lane * 16);
+  const uint4 c23 = *reinterpret_cast<const uint4*>(tp + 512 + lane * 16);
+  const uint4 csc = *reinterpret_cast<const uint4*>(tp + 1024 + g * 16);
+  const uint32_t words[8] = {c01.x, c01.y, c01.z, c01.w, c23.x, c23.y, c23.z, c23.w};
+  const uint32_t scw[4] = {csc.x, csc.y, csc.z, csc.w};
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      float s[NT][4];
-      block_mma<8, NT>(words[2 * b], words[2 * b + 1], x, ldx, M, g, tile * 128 + b * 32 + t * 8, s);
-      __half2 d2 = *reinterpret_cast<const __half2*>(&scw[b]);
-      float2 dd = __half22float2(d2);
+  for (int b = 0; b < 4; ++b) {
+    float s[NT][4];
+    block_mma<8, NT>(words[2 * b], words[2 * b + 1], xr, tile * 128 + b * 32, s);
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&scw[b]));
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        acc[nt][0] = __fmaf_rn(dd.x, s[nt][0], acc[nt][0]);
-        acc[nt][1] = __fmaf_rn(dd.x, s[nt][1], acc[nt][1]);
-        acc[nt][2] = __fmaf_rn(dd.y, s[nt][2], acc[nt][2]);
-        acc[nt][3] = __fmaf_rn(dd.y, s[nt][3], acc[nt][3]);
-      }
+    for (int nt = 0; nt < NT; ++nt) {
+      acc[nt][0] = __fmaf_rn(dd.x, s[nt][0], acc[nt][0]);
+      acc[nt][1] = __fmaf_rn(dd.x, s[nt][1], acc[nt][1]);
+      acc[nt][2] = __fmaf_rn(dd.y, s[nt][2], acc[nt][2]);
+      acc[nt][3] = __fmaf_rn(dd.y, s[nt][3], acc[nt][3]);
     }
-  }
-  reduce_and_finish_prep<NT>(acc, red, warp, lane);
-  __syncthreads();
-  for (int nt = warp; nt < NT; nt += kWarps) {
-    float4 s = red[nt * 32 + lane];
-#pragma unroll
-    for (int w2 = 1; w2 < kWarps; ++w2) {
-      float4 o = red[(w2 * NT + nt) * 32 + lane];
-      s.x += o.x; s.y += o.y; s.z += o.z; s.w += o.w;
-    }
-    epilogue<EPI>(ea, strip, nt, g, t, M, N, s);
   }
 }
 
-/* ------------------------------------------------------------------ Q4_K kernel */
-template <int NT, int EPI>
-__global__ void __launch_bounds__(kWarps * 32) qgemv_q4k_kernel(const uint8_t* __restrict__ w, int tiles,
-                                                                int N, const __half* __restrict__ x,
-                                                                int M, int ldx, EpiArgs ea) {
-  __shared__ float4 red[kWarps * NT * 32];
-  const int strip = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const uint8_t* sw = w + (size_t)strip * tiles * kQ4KTileBytes;
-  if (warp == 0) {
-    const uint32_t total = (uint32_t)tiles * kQ4KTileBytes;
-    for (uint32_t off = (uint32_t)lane * 32768u; off < total; off += 32u * 32768u) {
-      uint32_t n = total - off < 32768u ? total - off : 32768u;
-      prefetch_l2_bulk(sw + off, n);
+template <int NT>
+__device__ __forceinline__ void q4k_tile(const uint8_t* tp, int tile, const __half* const (&xr)[NT], int lane, int g,
+                                         float (&acc)[NT][4]);
+
+/*
+ * Persistent, warp-specialised form: one CTA per SM walks strips blockIdx.x, +gridDim.x, ...
+ * A producer warp streams the CTA's whole sequence of weight chunks (16 tiles each)
+ * through a ring of shared-memory slots with cp.async.bulk (full / empty mbarrier pairs),
+ * starting before griddepcontrol.wait; CW consumer warps dequantise + MMA one tile each
+ * per chunk and release the slot.  HBM never waits for compute and vice versa.
+ * Every wait has a deadline (2 s after kernel start): past it the CTA stops computing,
+ * raises bit 1 of *err and runs to completion without writing results.
+ */
+/* a chunk is ~36 KB of one strip; 2 ring slots per CTA; 2 CTAs per SM for NT <= 2 */
+template <int QT> struct PQ;
+template <> struct PQ<ULB_TYPE_Q4_0> { static constexpr int TB = kQ40TileBytes, CT = 32, NB = 2; };
+template <> struct PQ<ULB_TYPE_Q4_K> { static constexpr int TB = kQ4KTileBytes, CT = 16, NB = 2; };
+template <int NT> struct PQW {
+  static constexpr int CW = 8;               /* consumer warps; fixed so reduction order is too */
+  static constexpr int MINB = NT == 1 ? 2 : 1; /* resident CTAs per SM */
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, uint32_t parity, uint64_t deadline) {
+  while (!mbar_try(bar, parity))
+    if (gtimer() > deadline) return false;
+  return true;
+}
+
+template <int QT, int NT, int EPI>
+__global__ void __launch_bounds__((PQW<NT>::CW + 1) * 32, PQW<NT>::MINB)
+    qgemv_kernel(const uint8_t* __restrict__ w, int tiles, int n_strips, int N, const __half* __restrict__ x, int M,
+                 int ldx, EpiArgs ea, int* err, int nb, const __half* __restrict__ xzero) {
+  constexpr int TB = PQ<QT>::TB, CT = PQ<QT>::CT, NB = PQ<QT>::NB, CW = PQW<NT>::CW;
+  constexpr int CB = CT * TB;
+  /* tile i of a chunk always accumulates into slot i (of CT), and slots are summed in slot
+     order, so a row's arithmetic is the same whatever NT / the number of consumer warps */
+  constexpr int NSL = CT / CW;
+  extern __shared__ __align__(128) uint8_t ring[]; /* nb slots of CB bytes, then the slot sums */
+  float4* red = reinterpret_cast<float4*>(ring + (size_t)nb * CB);
+  __shared__ uint64_t full[NB], empty[NB];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nch = (tiles + CT - 1) / CT;
+  if (tid == 0) {
+    for (int i = 0; i < nb; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], CW);
     }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  __syncthreads();
+  const uint64_t deadline = gtimer() + 2000000000ull;
+  if (warp == CW) { /* ---------------- producer warp */
+    if (lane == 0) {
+      int seq = 0;
+      bool ok = true;
+      for (int s = blockIdx.x; s < n_strips && ok; s += gridDim.x)
+        for (int ch = 0; ch < nch; ++ch, ++seq) {
+          const int slot = seq % nb;
+          if (seq >= nb && !mbar_wait_deadline(&empty[slot], (uint32_t)((seq / nb) - 1) & 1u, deadline)) {
+            atomicOr(err, 2);
+            ok = false;
+            break;
+          }
+          const uint32_t bytes = (uint32_t)min(CT, tiles - ch * CT) * TB;
+          mbar_expect_tx(&full[slot], bytes);
+          bulk_g2s(ring + (size_t)slot * CB, w + ((size_t)s * tiles + (size_t)ch * CT) * TB, bytes, &full[slot]);
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
+  /* ---------------- consumer warps */
   pdl_wait();
   pdl_trigger();
-  for (int tile = warp; tile < tiles; tile += kWarps) {
-    const uint8_t* tp = sw + (size_t)tile * kQ4KTileBytes;
+  const int g = lane >> 2, t = lane & 3;
+  const __half* xr[NT];
+  activation_rows<NT>(x, xzero, ldx, M, g, t, xr);
+  int seq = 0;
+  bool ok = true;
+  for (int s = blockIdx.x; s < n_strips; s += gridDim.x) {
+    float acc[NSL][NT][4];
+#pragma unroll
+    for (int j = 0; j < NSL; ++j)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) acc[j][nt][0] = acc[j][nt][1] = acc[j][nt][2] = acc[j][nt][3] = 0.f;
+    for (int ch = 0; ch < nch; ++ch, ++seq) {
+      const int slot = seq % nb;
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait_deadline(&full[slot], (uint32_t)(seq / nb) & 1u, deadline));
+      if (ok) {
+        const uint8_t* base = ring + (size_t)slot * CB;
+        const int t0 = ch * CT, tn = min(tiles - t0, CT);
+#pragma unroll
+        for (int j = 0; j < NSL; ++j) {
+          const int i = warp + j * CW;
+          if (i < tn) {
+            if (QT == ULB_TYPE_Q4_0) q40_tile<NT>(base + i * TB, t0 + i, xr, lane, g, acc[j]);
+            else q4k_tile<NT>(base + i * TB, t0 + i, xr, lane, g, acc[j]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    /* slots w, w+CW, ... are summed in the warp, then warps in warp order: CW is the same
+       for every NT, so this order is fixed */
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float4 v = make_float4(acc[0][nt][0], acc[0][nt][1], acc[0][nt][2], acc[0][nt][3]);
+#pragma unroll
+      for (int j = 1; j < NSL; ++j) {
+        v.x += acc[j][nt][0]; v.y += acc[j][nt][1]; v.z += acc[j][nt][2]; v.w += acc[j][nt][3];
+      }
+      red[(warp * NT + nt) * 32 + lane] = v;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+    for (int nt = warp; nt < NT; nt += CW) {
+      float4 v = red[nt * 32 + lane];
+#pragma unroll
+      for (int w2 = 1; w2 < CW; ++w2) {
+        const float4 o = red[(w2 * NT + nt) * 32 + lane];
+        v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+      }
+      if (ok) epilogue<EPI>(ea, s, nt, g, t, M, N, v);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+  }
+  if (!ok && lane == 0) atomicOr(err, 2);
+}
+
+/* ------------------------------------------------------------------ Q4_K tile */
+template <int NT>
+__device__ __forceinline__ void q4k_tile(const uint8_t* tp, int tile, const __half* const (&xr)[NT], int lane, int g,
+                                         float (&acc)[NT][4]) {
+  {
     uint4 nb[4];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) nb[p] = ld_stream(tp + p * 512 + lane * 16);
-    const uint4 mg = ld_stream(tp + 2048 + g * 16);
-    const uint4 mg8 = ld_stream(tp + 2048 + (g + 8) * 16);
+    for (int p = 0; p < 4; ++p) nb[p] = *reinterpret_cast<const uint4*>(tp + p * 512 + lane * 16);
+    const uint4 mg = *reinterpret_cast<const uint4*>(tp + 2048 + g * 16);
+    const uint4 mg8 = *reinterpret_cast<const uint4*>(tp + 2048 + (g + 8) * 16);
     const float2 dg = __half22float2(*reinterpret_cast<const __half2*>(&mg.x));   /* (d, dmin) row g */
     const float2 dg8 = __half22float2(*reinterpret_cast<const __half2*>(&mg8.x)); /* row g + 8 */
     float t1[NT][4], t0[NT][4];
@@ -329,9 +458,9 @@ __global__ void __launch_bounds__(kWarps * 32) qgemv_q4k_kernel(const uint8_t* _
     {                                                                                    \
       const uint32_t* wp = reinterpret_cast<const uint32_t*>(&nb[(J) >> 1]);            \
       float s1[NT][4], s0[NT][4];                                                        \
-      const int kofs = tile * 256 + (J) * 32 + t * 8;                                    \
-      block_mma<0, NT>(wp[((J) & 1) * 2], wp[((J) & 1) * 2 + 1], x, ldx, M, g, kofs, s1); \
-      block_colsum<NT>(x, ldx, M, g, kofs, s0);                                          \
+      const int kofs = tile * 256 + (J) * 32;                                            \
+      block_mma<0, NT>(wp[((J) & 1) * 2], wp[((J) & 1) * 2 + 1], xr, kofs, s1);         \
+      block_colsum<NT>(xr, kofs, s0);                                                    \
       float scg, mng, scg8, mng8;                                                        \
       q4k_sm<J>(mg.y, mg.z, mg.w, scg, mng);                                             \
       q4k_sm<J>(mg8.y, mg8.z, mg8.w, scg8, mng8);                                        \
@@ -356,17 +485,6 @@ __global__ void __launch_bounds__(kWarps * 32) qgemv_q4k_kernel(const uint8_t* _
       acc[nt][2] = __fmaf_rn(-dg8.y, t0[nt][2], __fmaf_rn(dg8.x, t1[nt][2], acc[nt][2]));
       acc[nt][3] = __fmaf_rn(-dg8.y, t0[nt][3], __fmaf_rn(dg8.x, t1[nt][3], acc[nt][3]));
     }
-  }
-  reduce_and_finish_prep<NT>(acc, red, warp, lane);
-  __syncthreads();
-  for (int nt = warp; nt < NT; nt += kWarps) {
-    float4 s = red[nt * 32 + lane];
-#pragma unroll
-    for (int w2 = 1; w2 < kWarps; ++w2) {
-      float4 o = red[(w2 * NT + nt) * 32 + lane];
-      s.x += o.x; s.y += o.y; s.z += o.z; s.w += o.w;
-    }
-    epilogue<EPI>(ea, strip, nt, g, t, M, N, s);
   }
 }
 
@@ -486,31 +604,48 @@ __global__ void dequant_q4k_kernel(const uint8_t* __restrict__ w, int tiles, int
   }
 }
 
-template <int NT, int EPI>
-int launch_nt(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a) {
-  dim3 grid(w->n_strips), block(kWarps * 32);
-  cudaError_t e;
-  if (w->type == ULB_TYPE_Q4_0)
-    e = launch_k(c, qgemv_q40_kernel<NT, EPI>, grid, block, 0, (const uint8_t*)w->dev, w->tiles, w->N, x, M, ldx, a);
-  else
-    e = launch_k(c, qgemv_q4k_kernel<NT, EPI>, grid, block, 0, (const uint8_t*)w->dev, w->tiles, w->N, x, M, ldx, a);
+template <int QT, int NT, int EPI>
+int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a) {
+  constexpr int TB = PQ<QT>::TB, CT = PQ<QT>::CT, NB = PQ<QT>::NB, CW = PQW<NT>::CW;
+  const int nch = (w->tiles + CT - 1) / CT;
+  /* ring: as many slots as the CTA has chunks in flight, at most NB */
+  ULB_CHECK(w->K + 8 <= kZeroRowHalves, ULB_EUNSUPPORTED, "qgemv: K=%d too long", w->K);
+  const int ctas = c->n_sm * PQW<NT>::MINB;
+  const int per_cta = (w->n_strips + ctas - 1) / ctas;
+  const int grid = (w->n_strips + per_cta - 1) / per_cta; /* balanced: every CTA gets per_cta or per_cta-1 strips */
+  const int slots = min(NB, per_cta * nch);
+  const size_t red_bytes = (size_t)CW * NT * 32 * sizeof(float4);
+  const size_t smem = (size_t)slots * CT * TB + red_bytes;
+  static bool attr_set = false;
+  if (!attr_set) {
+    ULB_CUDA(cudaFuncSetAttribute(qgemv_kernel<QT, NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)((size_t)NB * CT * TB + red_bytes)));
+    attr_set = true;
+  }
+  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI>, dim3(grid), dim3((CW + 1) * 32), smem,
+                           (const uint8_t*)w->dev, w->tiles, w->n_strips, w->N, x, M, ldx, a, c->dev_err, slots,
+                           (const __half*)c->zero_row);
   if (e != cudaSuccess) return cuda_error(e, "qgemv launch", __FILE__, __LINE__);
   return ULB_OK;
+}
+
+template <int NT, int EPI>
+int launch_nt(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a) {
+  if (w->type == ULB_TYPE_Q4_0) return launch_q<ULB_TYPE_Q4_0, NT, EPI>(c, w, x, M, ldx, a);
+  return launch_q<ULB_TYPE_Q4_K, NT, EPI>(c, w, x, M, ldx, a);
 }
 
 template <int EPI>
 int launch_epi(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a) {
   if (M <= 8) return launch_nt<1, EPI>(c, w, x, M, ldx, a);
   if (M <= 16) return launch_nt<2, EPI>(c, w, x, M, ldx, a);
-  if (M <= 32) return launch_nt<4, EPI>(c, w, x, M, ldx, a);
-  if (w->type == ULB_TYPE_Q4_0) return launch_nt<8, EPI>(c, w, x, M, ldx, a);
-  return set_error(ULB_EINVAL, "qgemv: Q4_K chunk of %d rows exceeds 32", M);
+  return launch_nt<4, EPI>(c, w, x, M, ldx, a);
 }
 
 }  // namespace
 
 /* Max rows per launch (larger M is chunked by the caller of launch_qgemv). */
-static int max_rows_per_launch(int type) { return type == ULB_TYPE_Q4_0 ? 64 : 32; }
+static int max_rows_per_launch(int) { return 32; }
 
 int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
   ULB_CHECK(w && (w->type == ULB_TYPE_Q4_0 || w->type == ULB_TYPE_Q4_K), ULB_EINVAL, "qgemv: weight is not Q4_0/Q4_K");

@@ -50,6 +50,17 @@ void dev_free(Ctx* c, void* p, size_t bytes) {
   c->bytes_live -= bytes;
 }
 
+int check_device_errors(Ctx* c) {
+  int h = 0;
+  ULB_CUDA(cudaMemcpyAsync(&h, c->dev_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  if (h) {
+    ULB_CUDA(cudaMemsetAsync(c->dev_err, 0, sizeof(int), c->stream));
+    return set_error(ULB_ETIMEOUT, "a device-side bounded wait gave up (flags 0x%x); results of that launch are invalid", h);
+  }
+  return ULB_OK;
+}
+
 }  // namespace ulb
 
 using namespace ulb;
@@ -78,6 +89,10 @@ int ulb_init(int device, ulb_ctx** out) {
   c->c.device = device;
   c->c.n_sm = prop.multiProcessorCount;
   ULB_CUDA(cudaStreamCreateWithFlags(&c->c.stream, cudaStreamNonBlocking));
+  ULB_CUDA(cudaMalloc((void**)&c->c.dev_err, sizeof(int)));
+  ULB_CUDA(cudaMemset(c->c.dev_err, 0, sizeof(int)));
+  ULB_CUDA(cudaMalloc(&c->c.zero_row, kZeroRowHalves * sizeof(__half)));
+  ULB_CUDA(cudaMemset(c->c.zero_row, 0, kZeroRowHalves * sizeof(__half)));
   *out = c.release();
   return ULB_OK;
 }
@@ -86,6 +101,8 @@ int ulb_destroy(ulb_ctx* ctx) {
   if (!ctx) return ULB_OK;
   cudaSetDevice(ctx->c.device);
   cudaStreamSynchronize(ctx->c.stream);
+  cudaFree(ctx->c.dev_err);
+  cudaFree(ctx->c.zero_row);
   cudaStreamDestroy(ctx->c.stream);
   delete ctx;
   return ULB_OK;
@@ -95,8 +112,7 @@ void* ulb_stream(ulb_ctx* ctx) { return ctx ? (void*)ctx->c.stream : nullptr; }
 
 int ulb_stream_sync(ulb_ctx* ctx) {
   ULB_CHECK(ctx, ULB_EINVAL, "ulb_stream_sync: NULL context");
-  ULB_CUDA(cudaStreamSynchronize(ctx->c.stream));
-  return ULB_OK;
+  return check_device_errors(&ctx->c);
 }
 
 int ulb_mem_used(ulb_ctx* ctx, size_t* out) {

@@ -350,7 +350,7 @@ int ulb_spec_run(ulb_spec* h, int max_rounds, int* out_rounds) {
     }
     ran += r;
   }
-  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  ULB_TRY(check_device_errors(c));
   int herr = 0;
   ULB_CUDA(cudaMemcpy(&herr, sp->err, 4, cudaMemcpyDeviceToHost));
   ULB_CHECK(!herr, ULB_EINVAL, "ulb_spec_run: a token id fell outside the vocabulary");

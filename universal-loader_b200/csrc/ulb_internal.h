@@ -76,7 +76,13 @@ struct Ctx {
   bool pdl = true; /* programmatic dependent launch between consecutive kernels */
   std::map<void*, size_t> user_allocs; /* buffers handed out by ulb_malloc */
   uint64_t launches = 0;               /* kernels launched through launch_k (not graph replays) */
+  int* dev_err = nullptr;              /* device error word: bit 1 = a bounded wait gave up */
+  void* zero_row = nullptr;            /* kZeroRowHalves fp16 zeros: padding activation rows */
 };
+constexpr int kZeroRowHalves = 65536 + 64;
+
+/* read and clear the device error word (synchronises the stream) */
+int check_device_errors(Ctx* c);
 
 /* tracked device allocation */
 int dev_alloc(Ctx* c, void** p, size_t bytes);
