@@ -143,6 +143,30 @@ ULB_API int ulb_attention(ulb_ctx* ctx, const ulb_attn_desc* desc, const float* 
                   const int32_t* dev_row_pos, int M, int rows_per_seq, uint16_t* dev_out);
 
 /*
+ * ulb_attention without any device allocation.  This entry point has no counterpart in the
+ * reference.  It is for callers that must not call cudaMalloc / cudaFree: code that runs
+ * between the kernels of a latency-bound decode step (an allocation can synchronise the
+ * whole device), code whose device memory is already reserved by another allocator (a
+ * framework's caching allocator), and processes with no memory headroom left.
+ *   - Arguments, results and errors are those of ulb_attention.  The split-KV partials and
+ *     counters live in a static device array of 8 MiB + 32 KiB that every GPU loading this
+ *     library holds until the process exits; a shape needing more scratch than that (at most
+ *     2 Mi floats and 8192 counters, see ulb_attention's geometry) is rejected with
+ *     ULB_EINVAL before anything is launched.
+ *   - The first call on a device looks the array up (cudaGetSymbolAddress) on the current
+ *     device; make that first call before any stream capture.
+ *   - Every call shares the one array and its contents persist between calls (the counters
+ *     are cleared by each call): calls that overlap on the GPU — on two streams, or from two
+ *     contexts on the same device — race and give wrong results.  Calls on one context's
+ *     stream are ordered and safe.
+ *   - The call enqueues work and returns without synchronising; a device-side error is
+ *     reported by the next ulb_stream_sync.
+ */
+ULB_API int ulb_attention_noalloc(ulb_ctx* ctx, const ulb_attn_desc* desc, const float* dev_q,
+                          const uint16_t* dev_k, const uint16_t* dev_v, const int32_t* dev_row_seq,
+                          const int32_t* dev_row_pos, int M, int rows_per_seq, uint16_t* dev_out);
+
+/*
  * Logit warping shared by the draft sampler and the rejection sampler.  Replaces the
  * intent of TextGenerator::apply_temperature / apply_top_k / apply_top_p
  * (src/api/gguf_loader.cpp:90-155) and InferenceEngine::sample_token

@@ -16,13 +16,15 @@
  * its (sequence, row block, kv head) merges them in split order.  The split structure depends
  * only on a row's position, so a row's arithmetic never depends on what else is batched.
  */
+#include <mutex>
+
 #include "ulb_internal.h"
 
 namespace ulb {
 
 namespace {
 
-constexpr int BK = 64;       /* keys per staged block */
+constexpr int BK = 64;      /* keys per staged block */
 constexpr int SPLIT = 64;    /* keys per CTA: many CTAs per (sequence, kv head) */
 constexpr int MAXSPLIT = 128; /* capacity <= 8192 */
 constexpr int MERGE_UNROLL = 8;
@@ -377,9 +379,74 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
   return ULB_OK;
 }
 
+/* ------------------------------------------------------------------ allocation-free entry */
+/*
+ * Scratch of ulb_attention_noalloc lives in file-scope device arrays instead of memory the
+ * call allocates: every GPU that loads this library holds them (8 MiB + 32 KiB) until the
+ * process exits.  Host code cannot use the array names as device addresses; the addresses
+ * are looked up once per device with cudaGetSymbolAddress.
+ */
+constexpr size_t kNoAllocScratchFloats = (size_t)2 << 20; /* 2 Mi floats = 8 MiB */
+constexpr int kNoAllocCounters = 8192;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+static __device__ __align__(256) int g_noalloc_counters[kNoAllocCounters];
+
+namespace {
+struct NoAllocDevice {
+  bool ready = false;
+  float* scratch = nullptr;
+  int* counters = nullptr;
+};
+constexpr int kMaxDevices = 64;
+NoAllocDevice g_noalloc_dev[kMaxDevices];
+std::mutex g_noalloc_mu;
+}  // namespace
+
+/* device addresses of the static scratch on the current device (set up on first use) */
+static int noalloc_scratch(Ctx* c, float** scratch, int** counters) {
+  ULB_CHECK(c->device >= 0 && c->device < kMaxDevices, ULB_EUNSUPPORTED, "device id %d", c->device);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[c->device];
+  if (!d.ready) {
+    void* s = nullptr;
+    void* k = nullptr;
+    ULB_CUDA(cudaGetSymbolAddress(&s, g_noalloc_scratch));
+    ULB_CUDA(cudaGetSymbolAddress(&k, g_noalloc_counters));
+    d.scratch = (float*)s;
+    d.counters = (int*)k;
+    d.ready = true;
+  }
+  *scratch = d.scratch;
+  *counters = d.counters;
+  return ULB_OK;
+}
+
 }  // namespace ulb
 
 using namespace ulb;
+
+extern "C" int ulb_attention_noalloc(ulb_ctx* ctx, const ulb_attn_desc* d, const float* q, const uint16_t* k,
+                                     const uint16_t* v, const int32_t* row_seq, const int32_t* row_pos, int M,
+                                     int rps, uint16_t* out) {
+  ULB_CHECK(ctx && d && q && k && v && row_seq && row_pos && out, ULB_EINVAL, "ulb_attention_noalloc: NULL argument");
+  ULB_CHECK(d->capacity > 0 && d->n_seq > 0, ULB_EINVAL, "ulb_attention_noalloc: capacity / n_seq");
+  ULB_CHECK(rps > 0 && M >= 0 && M % rps == 0, ULB_EINVAL, "ulb_attention_noalloc: M=%d, rows_per_seq=%d", M, rps);
+  Ctx* c = &ctx->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  int nc = 0;
+  const size_t nf = attention_scratch_floats(d, M, rps, d->capacity - 1, &nc);
+  ULB_CHECK(nf <= kNoAllocScratchFloats && nc <= kNoAllocCounters, ULB_EINVAL,
+            "ulb_attention_noalloc: this shape needs %zu scratch floats and %d counters; the static scratch holds "
+            "%zu floats and %d counters (use ulb_attention)",
+            nf, nc, kNoAllocScratchFloats, kNoAllocCounters);
+  float* scratch = nullptr;
+  int* counters = nullptr;
+  ULB_TRY(noalloc_scratch(c, &scratch, &counters));
+  /* the arrays keep the previous call's contents: the split counters must start at zero */
+  ULB_CUDA(cudaMemsetAsync(counters, 0, (size_t)nc * sizeof(int), c->stream));
+  return launch_attention(c, d, q, d->n_head * d->head_dim, (const __half*)k, (const __half*)v, row_seq, row_pos, M,
+                          rps, (__half*)out, scratch, counters, kNoAllocScratchFloats, kNoAllocCounters);
+}
 
 extern "C" int ulb_attention(ulb_ctx* ctx, const ulb_attn_desc* d, const float* q, const uint16_t* k,
                              const uint16_t* v, const int32_t* row_seq, const int32_t* row_pos, int M,
