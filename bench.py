@@ -194,9 +194,10 @@ def gpu_smi_index(local_rank):
 
 # ---------------------------------------------------------------- roofline of the GEMV kernel
 def qgemv_roofline(device, reps=10):
-    """Time ulb_qgemm (the fused Q4_0 dequant-GEMV) on the 7B verify shapes (M = k+1 = 6 rows)
-    with CUDA events on the library's stream; 4 layers of distinct matrices (456 MB) are cycled
-    so every launch streams its weights from HBM (working set > L2)."""
+    """Time ulb_qgemm (the fused Q4_0 dequant-GEMV) on the 7B verify shapes (M = k+1 = 6 rows):
+    per shape, 4 layers' distinct copies are recorded in a CUDA graph and replayed, timed with
+    CUDA events on the library's stream; 456 MB of weights in all, so every launch streams its
+    weights from HBM (working set > L2)."""
     import numpy as np
     import ulb_capi as U
     ctx = U.Context(device)
@@ -213,21 +214,16 @@ def qgemv_roofline(device, reps=10):
         M = K_SPEC + 1
         xb = ctx.buffer(rng.standard_normal((M, f)).astype(np.float16))
         yb = ctx.buffer(nbytes=M * 2 * f * 4)
-        evs = [(ctx.event(), ctx.event()) for _ in mats]
-        times = {s: [] for s in shapes}
-        for it in range(reps + 2):
-            for (h, N, K), (a, b) in zip(mats, evs):
-                ctx.record(a)
-                U.check(U.lib().ulb_qgemm(ctx.h, h, xb.ptr, M, yb.ptr, N))
-                ctx.record(b)
-            ctx.sync()
-            if it >= 2:
-                for (h, N, K), (a, b) in zip(mats, evs):
-                    times[(N, K)].append(ctx.elapsed_ms(a, b))
+        for h, N, K in mats:
+            U.check(U.lib().ulb_qgemm(ctx.h, h, xb.ptr, M, yb.ptr, N))
         per = {}
         tot_b = tot_t = 0.0
         for (N, K) in shapes:
-            ms = statistics.mean(times[(N, K)])
+            # the 4 layers' copies of this matrix, recorded in a CUDA graph: back-to-back launches
+            mine = [(h, n, k) for (h, n, k) in mats if (n, k) == (N, K)]
+            g = ctx.capture(lambda: [U.check(U.lib().ulb_qgemm(ctx.h, h, xb.ptr, M, yb.ptr, n)) for h, n, k in mine])
+            ms = ctx.time_graph(g, reps) / len(mine)
+            U.lib().ulb_graph_free(g)
             alg = q4_0_bytes(N * K) + M * K * 2 + M * N * 4
             per["%dx%d" % (N, K)] = {"ms": ms, "gbs": alg / ms / 1e6}
             tot_b += alg
@@ -392,16 +388,131 @@ def run_ours(args):
     return 0
 
 
+def _rand_q4(rng, qt, N, K):
+    import numpy as np
+    if qt == "q4_0":
+        raw = rng.integers(0, 256, (N, K // 32, 18), dtype=np.uint8)
+        raw[:, :, 0:2] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+    else:
+        raw = rng.integers(0, 256, (N, K // 256, 144), dtype=np.uint8)
+        raw[:, :, 0:2] = np.frombuffer(np.float16(0.002).tobytes(), np.uint8)
+        raw[:, :, 2:4] = np.frombuffer(np.float16(0.001).tobytes(), np.uint8)
+    return raw.reshape(N, -1)
+
+
+def run_ops(args):
+    """Config-3 op sweep on one GPU: fused Q4_0 / Q4_K dequant-GEMM for (N, K) in
+    {(4096,4096), (11008,4096), (4096,11008)} x M in {1,5,8,16,64,256}, and the rejection
+    kernel at p [64, 9, 32000] / q [64, 8, 32000], and the attention kernel at the verify / draft
+    shapes.  Each case's launches are recorded in a CUDA graph and replayed, timed with CUDA
+    events on the library stream (so host call overhead is not in the figure); enough distinct
+    weight copies are cycled that every GEMM launch streams its weights from HBM."""
+    import ctypes as C
+    import numpy as np
+    import ulb_capi as U
+    peak, peak_src = load_peaks()
+    ctx = U.Context(0)
+    rng = np.random.default_rng(0)
+    cases = []
+    for qt in ("q4_0", "q4_k"):
+        for (N, K) in ((4096, 4096), (11008, 4096), (4096, 11008)):
+            for M in (1, 5, 8, 16, 64, 256):
+                name = "%s:%dx%d:m%d" % (qt, N, K, M)
+                if args.only and args.only != name and not name.startswith(args.only):
+                    continue
+                cases.append((qt, N, K, M, name))
+    results = {}
+    cache = {}
+    for qt, N, K, M, name in cases:
+        key = (qt, N, K)
+        if key not in cache:
+            copies = max(2, int(300e6 // (N * K * 0.5625)) + 1)  # > 2x L2 of weights
+            cache.clear()
+            cache[key] = [ctx.upload_tensor(U.T_Q4_0 if qt == "q4_0" else U.T_Q4_K, (K, N), _rand_q4(rng, qt, N, K))
+                          for _ in range(copies)]
+        mats = cache[key]
+        xb = ctx.buffer(rng.standard_normal((M, K)).astype(np.float16))
+        yb = ctx.buffer(nbytes=M * N * 4)
+        for h in mats[: max(1, args.warmup)]:
+            U.check(U.lib().ulb_qgemm(ctx.h, h, xb.ptr, M, yb.ptr, N))
+        # one launch per weight copy, recorded in a CUDA graph so the device runs them back to back
+        g = ctx.capture(lambda: [U.check(U.lib().ulb_qgemm(ctx.h, h, xb.ptr, M, yb.ptr, N)) for h in mats])
+        ms = ctx.time_graph(g, max(args.steps, 3)) / len(mats)
+        U.lib().ulb_graph_free(g)
+        alg = N * K * 0.5625 + 2 * M * K + 4 * M * N
+        results[name] = {"us": ms * 1e3, "gbs": alg / ms / 1e6, "hbm_frac": alg / ms / 1e6 / peak,
+                         "tflops": 2.0 * M * N * K / ms / 1e9}
+        xb.free()
+        yb.free()
+    for mats in cache.values():
+        for h in mats:
+            ctx.free_tensor(h)
+    # block-causal attention of the verify / draft rows against a KV cache (ulb_attention_noalloc:
+    # no allocation or synchronisation inside the timed loop); bytes = the K/V rows read
+    for (label, H, Hkv, hd, rps, L) in (("attn:7b_verify", 32, 32, 128, 6, 768), ("attn:tinyllama_draft", 32, 4, 64, 2, 768),
+                                        ("attn:7b_verify_4k", 32, 32, 128, 6, 4096)):
+        if args.only and not label.startswith(args.only):
+            continue
+        cap = L + 8
+        desc = U.AttnDesc(H, Hkv, hd, cap, 1, 1.0 / float(np.sqrt(hd)))
+        q = rng.standard_normal((rps, H * hd)).astype(np.float32)
+        kc = rng.standard_normal((1, Hkv, cap, hd)).astype(np.float16)
+        vc = rng.standard_normal((1, Hkv, cap, hd)).astype(np.float16)
+        rs = np.zeros(rps, np.int32)
+        rp = np.arange(L - rps, L, dtype=np.int32)
+        bufs = [ctx.buffer(a) for a in (q, kc, vc, rs, rp)]
+        out = ctx.buffer(nbytes=rps * H * hd * 2)
+        call = lambda: U.check(U.lib().ulb_attention_noalloc(ctx.h, C.byref(desc), bufs[0].ptr, bufs[1].ptr, bufs[2].ptr,
+                                                             bufs[3].ptr, bufs[4].ptr, rps, rps, out.ptr))
+        for _ in range(max(1, args.warmup)):
+            call()
+        ctx.sync()
+        g = ctx.capture(lambda: [call() for _ in range(20)])  # each call: counter reset + kernel
+        ms = ctx.time_graph(g, max(args.steps, 3)) / 20
+        U.lib().ulb_graph_free(g)
+        alg = 2 * L * Hkv * hd * 2 + q.nbytes + rps * H * hd * 2
+        results[label] = {"us": ms * 1e3, "gbs": alg / ms / 1e6, "hbm_frac": alg / ms / 1e6 / peak,
+                          "note": "K/V of one sequence (%.1f MB) fit in L2: a latency figure" % (2 * L * Hkv * hd * 2 / 1e6)}
+        for b in bufs + [out]:
+            b.free()
+    if not args.only or args.only.startswith("accept"):
+        B, k, V = 64, 8, 32000
+        pl = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
+        ql = (rng.standard_normal((B, k, V)) * 3).astype(np.float32)
+        draft = rng.integers(0, V, (B, k)).astype(np.int32)
+        bp, bq, bd = ctx.buffer(pl), ctx.buffer(ql), ctx.buffer(draft)
+        ot, on = ctx.buffer(nbytes=B * (k + 1) * 4), ctx.buffer(nbytes=B * 4)
+        for warp in ((1.0, 0, 1.0), (0.0, 0, 1.0)):
+            w = U.Warp(*warp)
+            for _ in range(max(1, args.warmup)):
+                U.check(U.lib().ulb_spec_accept(ctx.h, bp.ptr, bq.ptr, bd.ptr, B, k, V, C.byref(w), 1, 0, ot.ptr, on.ptr))
+            ctx.sync()
+            g = ctx.capture(lambda: [U.check(U.lib().ulb_spec_accept(ctx.h, bp.ptr, bq.ptr, bd.ptr, B, k, V, C.byref(w),
+                                                                      1, r, ot.ptr, on.ptr)) for r in range(4)])
+            ms = ctx.time_graph(g, max(args.steps, 3)) / 4
+            U.lib().ulb_graph_free(g)
+            alg = pl.nbytes + ql.nbytes
+            results["accept:T%g" % warp[0]] = {"us": ms * 1e3, "gbs": alg / ms / 1e6, "hbm_frac": alg / ms / 1e6 / peak}
+    ctx.close()
+    print(json.dumps({"mode": "ops", "peak_gbs": peak, "peak_source": peak_src, "results": results}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="spec", choices=["spec", "ops"],
+                    help="spec: the C2 speculative workload (default); ops: the config-3 kernel sweep")
+    ap.add_argument("--only", default="", help="ops mode: run one case, e.g. q4_0:11008x4096:m5 or accept")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.mode == "ops":
+        return run_ops(args)
     return run_ours(args)
 
 

@@ -85,6 +85,18 @@ ULB_API int ulb_event_record(ulb_ctx* ctx, void* event);
 ULB_API int ulb_event_elapsed_ms(void* start, void* end, float* out_ms);
 ULB_API int ulb_event_destroy(void* event);
 
+/* CUDA-graph capture of a fixed sequence of per-op calls on the context's stream, replayed
+ * with one launch (replaces re-recording the reference's command buffers per dispatch,
+ * src/vulkan_backend/compute.cpp:27-80).  Calls between begin and end are recorded, not
+ * run.  Capturable: ulb_qgemm, ulb_attention_noalloc, ulb_sample, ulb_spec_accept, once
+ * each has been called on the context outside a capture; not capturable: calls that
+ * synchronise with the host (ulb_attention, ulb_malloc, ulb_memcpy_*, ulb_model_forward). */
+typedef struct ulb_graph ulb_graph;
+ULB_API int ulb_capture_begin(ulb_ctx* ctx);
+ULB_API int ulb_capture_end(ulb_ctx* ctx, ulb_graph** out);
+ULB_API int ulb_graph_launch(ulb_ctx* ctx, const ulb_graph* g);
+ULB_API int ulb_graph_free(ulb_graph* g);
+
 /* ------------------------------------------------------------------ weights */
 /*
  * Upload one GGUF tensor and repack it into the device layout used by the kernels.

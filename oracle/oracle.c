@@ -631,20 +631,47 @@ static int argmax_f(const float* l, int V) {
 }
 
 /*
- * Warped distribution.  z = logits / T; top-k keeps z >= k-th largest z; e = exp(z - max)
- * in fp64; top-p keeps v iff (sum of e over z_u > z_v) < top_p * Z; probs = e / Z_kept.
- * Greedy (T <= 0): one-hot at the argmax.
+ * exp(x), x = z - max z <= 0, for the warp weights: the same sequence of IEEE binary32
+ * operations as ulb_warp_exp in universal-loader_b200/csrc/ulb_common.h, so the weights
+ * are bit-identical (this file is built with -ffp-contract=off; fmaf is the fused op).
+ * k = rint(x / ln 2); r = x - k*C1 - k*C2 with C1 = 355/512 (Cody & Waite two-part ln 2);
+ * exp(r) by its degree-7 Taylor polynomial in Horner form; times 2^k.  x < -87 gives 0.
  */
-int orc_warp_probs(const float* logits, int V, const orc_warp* w, double* probs) {
+float orc_warp_exp(float x) {
+  if (!(x >= -87.0f)) return 0.0f;
+  float kf = rintf(x * 1.44269504088896341f);
+  float r = fmaf(kf, -0.693359375f, x);
+  r = fmaf(kf, 2.12194440054690583e-4f, r);
+  float p = 1.98412698412698413e-4f;
+  p = fmaf(p, r, 1.38888888888888889e-3f);
+  p = fmaf(p, r, 8.33333333333333333e-3f);
+  p = fmaf(p, r, 4.16666666666666667e-2f);
+  p = fmaf(p, r, 1.66666666666666667e-1f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  uint32_t bits = (uint32_t)((int)kf + 127) << 23;
+  float two_k;
+  memcpy(&two_k, &bits, 4);
+  return p * two_k;
+}
+
+/*
+ * Warp weights.  z = logits * (1/T), 1/T rounded once; top-k keeps z >= k-th largest z; e = orc_warp_exp(z - max)
+ * as fp64; top-p keeps v iff (sum of e over z_u > z_v) < top_p * Z; *Zout = sum of kept e.
+ * Greedy (T <= 0): one-hot at the argmax, Z = 1.
+ */
+int orc_warp_weights(const float* logits, int V, const orc_warp* w, double* e, double* Zout) {
   if (!(w->temperature > 0.0f)) {
-    for (int i = 0; i < V; ++i) probs[i] = 0.0;
-    probs[argmax_f(logits, V)] = 1.0;
+    for (int i = 0; i < V; ++i) e[i] = 0.0;
+    e[argmax_f(logits, V)] = 1.0;
+    *Zout = 1.0;
     return 0;
   }
-  float T = w->temperature;
+  float iT = 1.0f / w->temperature; /* 1/T rounded once; z = logit * iT */
   float* z = (float*)malloc((size_t)V * 4);
   float mx = -INFINITY;
-  for (int i = 0; i < V; ++i) { z[i] = logits[i] / T + 0.0f; if (z[i] > mx) mx = z[i]; }
+  for (int i = 0; i < V; ++i) { z[i] = logits[i] * iT + 0.0f; if (z[i] > mx) mx = z[i]; }
   float thr_k = -INFINITY;
   if (w->top_k > 0 && w->top_k < V) {
     zi_t* s = (zi_t*)malloc((size_t)V * sizeof(zi_t));
@@ -655,35 +682,46 @@ int orc_warp_probs(const float* logits, int V, const orc_warp* w, double* probs)
   }
   double Z = 0.0;
   for (int i = 0; i < V; ++i) {
-    probs[i] = z[i] >= thr_k ? exp((double)(z[i] - mx)) : 0.0;
-    Z += probs[i];
+    e[i] = z[i] >= thr_k ? (double)orc_warp_exp(z[i] - mx) : 0.0;
+    Z += e[i];
   }
   if (w->top_p > 0.0f && w->top_p < 1.0f) {
     zi_t* s = (zi_t*)malloc((size_t)V * sizeof(zi_t));
     int n = 0;
-    for (int i = 0; i < V; ++i) if (probs[i] > 0.0) { s[n].z = z[i]; s[n].i = i; ++n; }
+    for (int i = 0; i < V; ++i) if (e[i] > 0.0) { s[n].z = z[i]; s[n].i = i; ++n; }
     qsort(s, n, sizeof(zi_t), cmp_zi_desc);
     double P = (double)w->top_p * Z, cum = 0.0;
     float thr_p = s[0].z;
     for (int j = 0; j < n; ++j) {
-      cum += probs[s[j].i];
+      cum += e[s[j].i];
       if (cum >= P) { thr_p = s[j].z; break; }
       thr_p = s[j].z;
     }
     free(s);
     Z = 0.0;
     for (int i = 0; i < V; ++i) {
-      if (z[i] < thr_p) probs[i] = 0.0;
-      Z += probs[i];
+      if (z[i] < thr_p) e[i] = 0.0;
+      Z += e[i];
     }
   }
-  for (int i = 0; i < V; ++i) probs[i] /= Z;
   free(z);
+  *Zout = Z;
   return 0;
 }
 
-/* inverse CDF in index order over fp64 weights w (not necessarily normalised) */
-static int inv_cdf(const double* w, int V, double total, float u) {
+/* normalised warped distribution: probs = e / Z */
+int orc_warp_probs(const float* logits, int V, const orc_warp* w, double* probs) {
+  double Z;
+  orc_warp_weights(logits, V, w, probs, &Z);
+  for (int i = 0; i < V; ++i) probs[i] /= Z;
+  return 0;
+}
+
+/* inverse CDF in index order over fp64 weights w: smallest i whose cumulative weight
+   exceeds u * (sum of w) */
+static int inv_cdf(const double* w, int V, float u) {
+  double total = 0.0;
+  for (int i = 0; i < V; ++i) total += w[i];
   double target = (double)u * total, cum = 0.0;
   int last = -1;
   for (int i = 0; i < V; ++i) {
@@ -697,10 +735,11 @@ static int inv_cdf(const double* w, int V, double total, float u) {
 
 int orc_sample(const float* logits, int V, const orc_warp* w, float u) {
   if (!(w->temperature > 0.0f)) return argmax_f(logits, V);
-  double* p = (double*)malloc((size_t)V * 8);
-  orc_warp_probs(logits, V, w, p);
-  int t = inv_cdf(p, V, 1.0, u);
-  free(p);
+  double* e = (double*)malloc((size_t)V * 8);
+  double Z;
+  orc_warp_weights(logits, V, w, e, &Z);
+  int t = inv_cdf(e, V, u);
+  free(e);
   return t;
 }
 
@@ -720,23 +759,26 @@ int orc_spec_accept(const float* pl, const float* ql, const int32_t* draft, int 
         if (x == a) { out_tokens[b * (k + 1) + n] = x; ++n; continue; }
         tok = a; break;
       }
-      orc_warp_probs(pi, V, w, p);
-      orc_warp_probs(qi, V, w, q);
+      double Zp, Zq;
+      orc_warp_weights(pi, V, w, p, &Zp);
+      orc_warp_weights(qi, V, w, q, &Zq);
       float u = orc_uniform(seed, round, (uint32_t)b, (uint32_t)i, 2);
-      if ((double)u * q[x] < p[x]) { out_tokens[b * (k + 1) + n] = x; ++n; continue; }
+      double px = (unsigned)x < (unsigned)V ? p[x] / Zp : 0.0, qx = (unsigned)x < (unsigned)V ? q[x] / Zq : 0.0;
+      if ((double)u * qx < px) { out_tokens[b * (k + 1) + n] = x; ++n; continue; }
+      /* residual norm(max(0, p - q)) as max(0, e_p Z_q - e_q Z_p) */
       double tot = 0.0;
-      for (int v = 0; v < V; ++v) { double r = p[v] - q[v]; p[v] = r > 0.0 ? r : 0.0; tot += p[v]; }
+      for (int v = 0; v < V; ++v) { double r = p[v] * Zq - q[v] * Zp; q[v] = r > 0.0 ? r : 0.0; tot += q[v]; }
       float u2 = orc_uniform(seed, round, (uint32_t)b, (uint32_t)i, 3);
-      if (tot > 0.0) tok = inv_cdf(p, V, tot, u2);
-      else { orc_warp_probs(pi, V, w, p); tok = inv_cdf(p, V, 1.0, u2); }
+      tok = tot > 0.0 ? inv_cdf(q, V, u2) : inv_cdf(p, V, u2);
       break;
     }
     if (tok < 0) { /* all k accepted: bonus from p_k */
       const float* pk = pl + ((size_t)b * (k + 1) + k) * V;
       if (greedy) tok = argmax_f(pk, V);
       else {
-        orc_warp_probs(pk, V, w, p);
-        tok = inv_cdf(p, V, 1.0, orc_uniform(seed, round, (uint32_t)b, (uint32_t)k, 3));
+        double Zp;
+        orc_warp_weights(pk, V, w, p, &Zp);
+        tok = inv_cdf(p, V, orc_uniform(seed, round, (uint32_t)b, (uint32_t)k, 3));
       }
     }
     out_tokens[b * (k + 1) + n] = tok;

@@ -86,7 +86,11 @@ int orc_forward(orc_model* m, orc_kv* kv, int M, int rows_per_seq, const int32_t
 float orc_uniform(uint64_t seed, uint32_t round, uint32_t seq, uint32_t slot, uint32_t tag);
 void orc_philox(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0, uint32_t k1,
                 uint32_t out[4]);
-/* warped probabilities (fp64, zero outside the kept set); returns 0 */
+/* exp of the warp weights (binary32, the same operations as the device's ulb_warp_exp) */
+float orc_warp_exp(float x);
+/* unnormalised warp weights e (fp64, zero outside the kept set) and their sum *Z; returns 0 */
+int orc_warp_weights(const float* logits, int V, const orc_warp* w, double* e, double* Z);
+/* warped probabilities e / Z; returns 0 */
 int orc_warp_probs(const float* logits, int V, const orc_warp* w, double* probs);
 int orc_sample(const float* logits, int V, const orc_warp* w, float u);
 int orc_spec_accept(const float* p_logits, const float* q_logits, const int32_t* draft, int B,

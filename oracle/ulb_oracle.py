@@ -55,6 +55,9 @@ def lib():
         L.orc_uniform.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]
         L.orc_philox.argtypes = [C.c_uint32] * 6 + [P]
         L.orc_warp_probs.argtypes = [P, C.c_int, C.POINTER(Warp), P]
+        L.orc_warp_exp.restype = C.c_float
+        L.orc_warp_exp.argtypes = [C.c_float]
+        L.orc_warp_weights.argtypes = [P, C.c_int, C.POINTER(Warp), P, C.POINTER(C.c_double)]
         L.orc_sample.argtypes = [P, C.c_int, C.POINTER(Warp), C.c_float]
         L.orc_spec_accept.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.POINTER(Warp),
                                       C.c_uint64, C.c_uint32, P, P]
@@ -133,6 +136,19 @@ def warp_probs(logits, temperature=1.0, top_k=0, top_p=1.0):
     w = Warp(temperature, top_k, top_p)
     lib().orc_warp_probs(_p(logits), logits.size, C.byref(w), _p(p))
     return p
+
+
+def warp_exp(x):
+    return float(lib().orc_warp_exp(float(x)))
+
+
+def warp_weights(logits, temperature=1.0, top_k=0, top_p=1.0):
+    logits = np.ascontiguousarray(logits, np.float32)
+    e = np.empty(logits.size, np.float64)
+    Z = C.c_double()
+    w = Warp(temperature, top_k, top_p)
+    lib().orc_warp_weights(_p(logits), logits.size, C.byref(w), _p(e), C.byref(Z))
+    return e, Z.value
 
 
 def sample(logits, u, temperature=1.0, top_k=0, top_p=1.0):

@@ -109,6 +109,30 @@ def test_qgemm_rows_independent_of_batch(ctx):
         ctx.free_tensor(h)
 
 
+def test_graph_capture_replays_per_op_calls(ctx):
+    """ulb_capture_begin / end record ulb_qgemm calls; a replay gives the direct result."""
+    import ulb_capi as U
+    rng = np.random.default_rng(2)
+    N, K, M = 256, 1024, 5
+    h = ctx.upload_tensor(orc.T_Q4_0, (K, N), _q40(rng, N, K))
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    xb = ctx.buffer(x)
+    yb = ctx.buffer(nbytes=M * N * 4)
+    try:
+        want = ctx.qgemm(h, x, N)
+        yb.upload(np.zeros((M, N), np.float32))
+        g = ctx.capture(lambda: U.check(U.lib().ulb_qgemm(ctx.h, h, xb.ptr, M, yb.ptr, N)))
+        assert not yb.download(np.float32, (M, N)).any()  # recorded, not run
+        U.check(U.lib().ulb_graph_launch(ctx.h, g))
+        ctx.sync()
+        assert np.array_equal(yb.download(np.float32, (M, N)), want)
+        U.lib().ulb_graph_free(g)
+    finally:
+        xb.free()
+        yb.free()
+        ctx.free_tensor(h)
+
+
 def _attn_case(ctx, H, Hkv, hd, S, rps, positions, seed):
     import ulb_capi as U
     rng = np.random.default_rng(seed)

@@ -148,6 +148,42 @@ def test_qgemv_matches_float64_dot(qt, M):
     assert rel < 1e-5, rel
 
 
+# ---------------------------------------------------------------- warp-weight exponential
+def test_warp_exp_accuracy_and_range():
+    """orc_warp_exp (Cody-Waite reduction + degree-7 Taylor) is within a few ulp of exp."""
+    rng = np.random.default_rng(3)
+    xs = np.concatenate([-rng.random(40000) * 87.0, -rng.random(2000) * 1e-3,
+                         np.array([0.0, -1e-30, -0.34657359, -0.34657360, -86.99999])]).astype(np.float32)
+    got = np.array([orc.warp_exp(x) for x in xs], np.float64)
+    want = np.exp(xs.astype(np.float64))
+    assert np.max(np.abs(got - want) / want) < 4e-7
+    assert orc.warp_exp(0.0) == 1.0
+    assert orc.warp_exp(-87.5) == 0.0 and orc.warp_exp(float("-inf")) == 0.0
+
+
+def test_warp_exp_header_matches_oracle(tmp_path):
+    """The device header's ulb_warp_exp, compiled for the host, is bit-identical to the
+    oracle's restatement (the device build compiles the same source with __fmaf_rn /
+    __fmul_rn / rintf, which are the same IEEE operations)."""
+    import ctypes as C
+    import os
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = tmp_path / "hx.c"
+    src.write_text('#include "ulb_common.h"\nfloat hx(float x) { return ulb_warp_exp(x); }\n')
+    so = tmp_path / "hx.so"
+    subprocess.run(["gcc", "-O2", "-ffp-contract=off", "-fPIC", "-shared", "-I",
+                    os.path.join(root, "universal-loader_b200", "csrc"), "-o", str(so), str(src), "-lm"], check=True)
+    lib = C.CDLL(str(so))
+    lib.hx.restype = C.c_float
+    lib.hx.argtypes = [C.c_float]
+    rng = np.random.default_rng(5)
+    xs = (-rng.random(30000) * 90.0).astype(np.float32)
+    for x in xs:
+        a, b = np.float32(lib.hx(x)), np.float32(orc.warp_exp(x))
+        assert a.view(np.uint32) == b.view(np.uint32), (float(x), float(a), float(b))
+
+
 # ---------------------------------------------------------------- sampling known answers
 def test_warp_probs_greedy_and_topk():
     logits = np.array([0.5, 3.0, -1.0, 3.0, 2.0], np.float32)

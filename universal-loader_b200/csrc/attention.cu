@@ -8,14 +8,23 @@
  * 42-45, 153): GQA (kv head = q head / group), causal masking, online softmax over KV
  * blocks, KV read from the cache.
  *
- * grid = (key split of 512 positions, kv head, sequence x row block).  All q heads of a GQA
- * group and all rows of the block share each 64-key K/V block, staged in shared memory with
- * cp.async and double-buffered, so the cache is read once per step.  Inside a split the CTA
- * keeps an online softmax (running max / sum, rescaled output).  Contexts up to 512 keys
- * need no merge; longer ones write one partial per split and the CTA that arrives last for
- * its (sequence, row block, kv head) merges them in split order.  The split structure depends
- * only on a row's position, so a row's arithmetic never depends on what else is batched.
+ * Tensor-core flash decoding (B200, mma.sync.m16n8k16 with fp32 accumulate):
+ *  - grid = (16-query tile x split of 256 keys, kv head, sequence); 4 warps per CTA, warp w
+ *    owns keys [split*256 + 64w, +64): it stages that K / V block in shared memory with
+ *    cp.async (XOR-swizzled 16-byte chunks, so ldmatrix reads are conflict-free), computes
+ *    S = Q.K^T with Q split into hi + lo fp16 parts (two MMAs, ~22 bits of q kept), masks
+ *    keys past each query's position, and accumulates O = P.V with P rounded to fp16 (the
+ *    score registers are reused as A fragments);
+ *  - a query tile packs the G heads of a GQA group times the rows of the sequence, so each
+ *    K / V block is read once for all of them;
+ *  - the 4 warp blocks merge in shared memory; with several splits each CTA writes a
+ *    partial (max, sum, output) and the CTA that arrives last for its (sequence, tile, kv
+ *    head) merges the splits in split order.
+ * A row's key blocks and merge order depend only on its own position: blocks or splits past
+ * it contribute exact zeros, so batching never changes a row's result.
+ * head_dim 64 and 128; capacity <= 8192.
  */
+#include <algorithm>
 #include <mutex>
 
 #include "ulb_internal.h"
@@ -24,293 +33,306 @@ namespace ulb {
 
 namespace {
 
-constexpr int BK = 64;      /* keys per staged block */
-constexpr int SPLIT = 64;    /* keys per CTA: many CTAs per (sequence, kv head) */
-constexpr int MAXSPLIT = 128; /* capacity <= 8192 */
-constexpr int MERGE_UNROLL = 8;
-constexpr int AQMAX = 64;    /* queries (heads x rows) per CTA */
-constexpr int ATHREADS = 256;
-constexpr int ANW = ATHREADS / 32;
-constexpr int MAXITEMS = AQMAX * 64 / ATHREADS; /* output (query, dim pair) items per thread, hd <= 128 */
+constexpr int KB = 64;              /* keys per warp block */
+constexpr int AW = 4;               /* warps per CTA */
+constexpr int SPLITK = KB * AW;     /* keys per CTA = one split */
+constexpr int MAXSPLIT = 32;        /* capacity <= 8192 */
+constexpr int QT = 16;              /* queries per CTA: one m16 tile */
+constexpr float kLog2e = 1.44269504088896340736f;
 
 struct AttnParams {
-  int H, Hkv, hd, cap, G, rps, RB, n_rb, max_splits, ldq, n_seq;
-  float scale;
+  int H, Hkv, hd, cap, G, rps, n_mt, max_splits, ldq, n_seq;
+  float scale2; /* softmax scale x log2(e): scores live in the base-2 domain */
 };
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+/* 16-byte async copy; zero-fills the destination when !valid (nothing is read then) */
+__device__ __forceinline__ void cp_async16z(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr(dst)), "l"(src), "r"(valid ? 16 : 0)
                : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-struct Smem {
-  float* qs;     /* [AQMAX][hd]               */
-  float* ss;     /* [AQMAX][BK] scores / p    */
-  int* qpos;     /* [AQMAX]                   */
-  float* mrun;   /* [AQMAX] running max       */
-  float* lrun;   /* [AQMAX] running sum       */
-  float* scl;    /* [AQMAX] rescale of block  */
-  uint4* ks;     /* [2][BK][hd/8] swizzled    */
-  uint4* vs;     /* [2][BK][hd/8]             */
-};
-
-__device__ __forceinline__ Smem carve(float* base, int hd) {
-  Smem s;
-  s.qs = base;
-  s.ss = s.qs + AQMAX * hd;
-  s.qpos = reinterpret_cast<int*>(s.ss + AQMAX * BK);
-  s.mrun = reinterpret_cast<float*>(s.qpos + AQMAX);
-  s.lrun = s.mrun + AQMAX;
-  s.scl = s.lrun + AQMAX;
-  s.ks = reinterpret_cast<uint4*>(s.scl + AQMAX);
-  s.vs = s.ks + 2 * BK * (hd / 8);
-  return s;
+__device__ __forceinline__ void ldsm4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a));
 }
+__device__ __forceinline__ void ldsm4t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a));
+}
+/* C += A(16x16 f16, row) * B(16x8 f16, col), fp32 accumulate */
+__device__ __forceinline__ void mma_acc(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};"
+               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+/* 16-byte chunk c of key row j is stored at chunk c ^ (j & 7): the 8 rows one ldmatrix
+   phase reads fall in 8 different bank groups */
+__device__ __forceinline__ int swz(int j, int c) { return c ^ (j & 7); }
 
-__global__ void __launch_bounds__(ATHREADS) attn_kernel(AttnParams p, const float* __restrict__ q,
-                                                        const __half* __restrict__ kc, const __half* __restrict__ vc,
-                                                        const int* __restrict__ row_seq,
-                                                        const int* __restrict__ row_pos, __half* __restrict__ out,
-                                                        float* scratch, int* counters) {
-  extern __shared__ __align__(16) float smem_raw[];
-  const int split = blockIdx.x, kvh = blockIdx.y, gz = blockIdx.z;
-  const int gi = gz / p.n_rb, rb = gz % p.n_rb;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hd = p.hd, hd2 = hd >> 1, vpr = hd / 8;
-  const Smem S = carve(smem_raw, hd);
+/*
+ * One CTA = one (sequence, kv head, 16-query tile, split of 256 keys); warp w scores the
+ * tile against keys [split*256 + 64w, +64) with tensor cores and keeps that block's softmax
+ * (max, sum, unnormalised output).  The 4 warp blocks merge in shared memory; with more
+ * than one split, the CTA that finishes last for its (sequence, tile, kv head) merges the
+ * splits in split order.  Queries: index qi = r * G + j is row r of the sequence, head
+ * kv_head * G + j.
+ */
+template <int HD>
+__global__ void __launch_bounds__(AW * 32, 1)
+    attn_mma_kernel(AttnParams p, const float* __restrict__ q, const __half* __restrict__ kc,
+                    const __half* __restrict__ vc, const int* __restrict__ row_seq, const int* __restrict__ row_pos,
+                    __half* __restrict__ out, float* scratch, int* counters) {
+  constexpr int NCH = HD / 8; /* 16-byte chunks per K / V row */
+  constexpr int KS = HD / 16; /* k-steps of Q.K^T */
+  constexpr int DN = HD / 8;  /* n-tiles of the output */
+  constexpr int PST = HD + 2; /* floats per query of a partial: m, l, o[HD] */
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int mt = blockIdx.x % p.n_mt, split = blockIdx.x / p.n_mt, kvh = blockIdx.y, gi = blockIdx.z;
   pdl_wait();
   pdl_trigger();
-
-  const int r0 = rb * p.RB;
-  const int nr = min(p.RB, p.rps - r0);
-  const int Q = p.G * nr;
-  const int m0 = gi * p.rps + r0;
-  int last_pos = 0;
-  for (int r = 0; r < nr; ++r) last_pos = max(last_pos, row_pos[m0 + r]);
-  last_pos = min(last_pos, p.cap - 1); /* positions past the cache never index it */
-  const int n_splits = last_pos / SPLIT + 1;
-  if (split >= n_splits) return;
+  const int Q = p.G * p.rps, q0 = mt * QT, nq = min(QT, Q - q0);
+  const int m0 = gi * p.rps;
+  /* every index load of the CTA is issued before any is used: the tile's last position (one
+     load per lane, lane < nq <= 16, then a warp max), the sequence, and the lane's two query
+     positions, so the CTA pays one memory latency here */
+  const int qa = q0 + g, qb = q0 + g + 8; /* the lane's two query rows of the tile: g, g + 8 */
+  const bool va = g < nq, vb = g + 8 < nq;
+  int last_pos = lane < nq ? row_pos[m0 + (q0 + lane) / p.G] : 0;
   const int seq = row_seq[m0];
+  const int pa = va ? row_pos[m0 + qa / p.G] : -1, pb = vb ? row_pos[m0 + qb / p.G] : -1;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) last_pos = max(last_pos, __shfl_xor_sync(0xffffffffu, last_pos, o));
+  last_pos = max(0, min(last_pos, p.cap - 1)); /* positions past the cache never index it */
+  const int n_splits = last_pos / SPLITK + 1;
+  if (split >= n_splits) return;
   if ((unsigned)seq >= (unsigned)p.n_seq) return;
-  const int k_begin = split * SPLIT;
-  const int k_end = min(k_begin + SPLIT, last_pos + 1);
-  const int nblocks = (k_end - k_begin + BK - 1) / BK;
-  const size_t kvbase = (((size_t)seq * p.Hkv + kvh) * p.cap) * hd;
 
-  auto stage = [&](int b, int buf) {
-    const int kb = k_begin + b * BK;
-    const int nk = min(BK, k_end - kb);
-    uint4* kd = S.ks + buf * BK * vpr;
-    uint4* vd = S.vs + buf * BK * vpr;
-    for (int i = tid; i < nk * vpr; i += ATHREADS) {
-      const int j = i / vpr, c = i % vpr;
-      const int cs = (c & ~7) | ((c ^ j) & 7); /* XOR swizzle inside each group of 8 chunks */
-      const size_t src = kvbase + (size_t)(kb + j) * hd + c * 8;
-      cp_async16(kd + j * vpr + cs, kc + src);
-      cp_async16(vd + j * vpr + c, vc + src);
+  const int kb0 = (split * AW + warp) * KB;
+  const int nk = min(KB, last_pos + 1 - kb0); /* keys of this warp's block (may be <= 0) */
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+  float o[DN][4];
+#pragma unroll
+  for (int d = 0; d < DN; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
+  __half* Ks = reinterpret_cast<__half*>(sm) + (size_t)warp * 2 * KB * HD;
+  __half* Vs = Ks + KB * HD;
+  if (nk > 0) {
+    const size_t kvoff = (((size_t)seq * p.Hkv + kvh) * p.cap + kb0) * HD;
+    const __half* kg = kc + kvoff;
+    const __half* vg = vc + kvoff;
+    for (int i = lane; i < KB * NCH; i += 32) {
+      const int j = i / NCH, c = i % NCH;
+      const bool ok = j < nk;
+      const size_t off = ok ? (size_t)j * HD + c * 8 : 0;
+      cp_async16z(Ks + j * HD + swz(j, c) * 8, kg + off, ok);
+      cp_async16z(Vs + j * HD + swz(j, c) * 8, vg + off, ok);
     }
-  };
-
-  for (int i = tid; i < Q * (hd / 4); i += ATHREADS) {
-    const int qi = i / (hd / 4), c = i % (hd / 4);
-    const int r = qi / p.G, gq = qi % p.G;
-    cp_async16(S.qs + qi * hd + c * 4, q + (size_t)(m0 + r) * p.ldq + (kvh * p.G + gq) * hd + c * 4);
+    cp_commit();
   }
-  stage(0, 0);
-  cp_commit();
-  for (int qi = tid; qi < Q; qi += ATHREADS) {
-    S.qpos[qi] = row_pos[m0 + qi / p.G];
-    S.mrun[qi] = -INFINITY;
-    S.lrun[qi] = 0.f;
-  }
-  const int n_items = Q * hd2;
-  float2 o[MAXITEMS];
+  const float* qpa = q + (size_t)(m0 + (va ? qa : q0) / p.G) * p.ldq + (kvh * p.G + (va ? qa : q0) % p.G) * HD;
+  const float* qpb = q + (size_t)(m0 + (vb ? qb : q0) / p.G) * p.ldq + (kvh * p.G + (vb ? qb : q0) % p.G) * HD;
+  /* Q as A fragments, split hi + lo into two fp16 parts so the scores keep ~22 bits of q */
+  uint32_t qh[KS][4], ql[KS][4];
 #pragma unroll
-  for (int k = 0; k < MAXITEMS; ++k) o[k] = make_float2(0.f, 0.f);
-
-  for (int b = 0; b < nblocks; ++b) {
-    const int buf = b & 1;
-    if (b + 1 < nblocks) {
-      stage(b + 1, buf ^ 1);
-      cp_commit();
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
+  for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const bool v = (r & 1) ? vb : va;
+      const float* src = ((r & 1) ? qpb : qpa) + ks * 16 + 2 * t + (r >> 1) * 8;
+      const float2 f = v ? *reinterpret_cast<const float2*>(src) : make_float2(0.f, 0.f);
+      const __half2 h = __floats2half2_rn(f.x, f.y);
+      const float2 hf = __half22float2(h);
+      qh[ks][r] = *reinterpret_cast<const uint32_t*>(&h);
+      ql[ks][r] = pack_h2(f.x - hf.x, f.y - hf.y);
     }
-    __syncthreads();
-    const int kb = k_begin + b * BK;
-    const int nk = min(BK, k_end - kb);
-    const uint4* kbuf = S.ks + buf * BK * vpr;
-    /* scores: warp per query, lanes over keys; sequential fma over d (as the CPU oracle) */
-    for (int qi = warp; qi < Q; qi += ANW) {
-      const float4* qv = reinterpret_cast<const float4*>(S.qs + qi * hd);
-      const int qp = S.qpos[qi];
-      for (int j = lane; j < BK; j += 32) {
-        float s = -INFINITY;
-        if (j < nk && kb + j <= qp) {
-          const uint4* kr = kbuf + j * vpr;
-          float a = 0.f;
-          for (int c = 0; c < vpr; ++c) {
-            const uint4 kk = kr[(c & ~7) | ((c ^ j) & 7)];
-            const float4 qa = qv[2 * c], qb = qv[2 * c + 1];
-            const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kk.x));
-            const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kk.y));
-            const float2 k45 = __half22float2(*reinterpret_cast<const __half2*>(&kk.z));
-            const float2 k67 = __half22float2(*reinterpret_cast<const __half2*>(&kk.w));
-            a = __fmaf_rn(qa.x, k01.x, a);
-            a = __fmaf_rn(qa.y, k01.y, a);
-            a = __fmaf_rn(qa.z, k23.x, a);
-            a = __fmaf_rn(qa.w, k23.y, a);
-            a = __fmaf_rn(qb.x, k45.x, a);
-            a = __fmaf_rn(qb.y, k45.y, a);
-            a = __fmaf_rn(qb.z, k67.x, a);
-            a = __fmaf_rn(qb.w, k67.y, a);
-          }
-          s = __fmul_rn(a, p.scale);
-        }
-        S.ss[qi * BK + j] = s;
-      }
-      __syncwarp();
-      /* online softmax update of this query (the same warp wrote its scores) */
-      float mb = -INFINITY;
-      for (int j = lane; j < BK; j += 32) mb = fmaxf(mb, S.ss[qi * BK + j]);
-#pragma unroll
-      for (int off = 16; off; off >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-      const float mold = S.mrun[qi];
-      const float mnew = fmaxf(mold, mb);
-      float lb = 0.f;
-      for (int j = lane; j < BK; j += 32) {
-        const float s = S.ss[qi * BK + j];
-        const float e = s == -INFINITY ? 0.f : expf(s - mnew);
-        S.ss[qi * BK + j] = e;
-        lb += e;
-      }
-#pragma unroll
-      for (int off = 16; off; off >>= 1) lb += __shfl_xor_sync(0xffffffffu, lb, off);
-      __syncwarp();
-      if (lane == 0) {
-        const float sc = mold == -INFINITY ? 0.f : expf(mold - mnew);
-        S.scl[qi] = sc;
-        S.lrun[qi] = __fmaf_rn(S.lrun[qi], sc, lb);
-        S.mrun[qi] = mnew;
-      }
-    }
-    __syncthreads();
-    /* P.V: thread per (query, dim pair) items; sequential over keys */
-    const __half2* vbuf = reinterpret_cast<const __half2*>(S.vs + buf * BK * vpr);
-#pragma unroll
-    for (int k = 0; k < MAXITEMS; ++k) {
-      const int it = tid + k * ATHREADS;
-      if (it < n_items) {
-        const int qi = it / hd2, d2 = it % hd2;
-        const float sc = S.scl[qi];
-        float ox = o[k].x * sc, oy = o[k].y * sc;
-        const float* pr = S.ss + qi * BK;
-        for (int j = 0; j < nk; ++j) {
-          const float pj = pr[j];
-          const float2 vf = __half22float2(vbuf[j * hd2 + d2]);
-          ox = __fmaf_rn(pj, vf.x, ox);
-          oy = __fmaf_rn(pj, vf.y, oy);
-        }
-        o[k] = make_float2(ox, oy);
-      }
-    }
-    __syncthreads(); /* the next iteration restages this buffer */
   }
 
+  if (nk > 0) {
+    cp_wait_all();
+    __syncwarp();
+    /* S = Q.K^T for 8 n-tiles of 8 keys */
+    float s[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+      s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+      const int key = nb * 8 + (lane & 7);
+#pragma unroll
+      for (int kp = 0; kp < KS / 2; ++kp) {
+        uint32_t b0, b1, b2, b3;
+        ldsm4(saddr(Ks + key * HD + swz(key, kp * 4 + (lane >> 3)) * 8), b0, b1, b2, b3);
+        mma_acc(s[nb], qh[2 * kp], b0, b1);
+        mma_acc(s[nb], ql[2 * kp], b0, b1);
+        mma_acc(s[nb], qh[2 * kp + 1], b2, b3);
+        mma_acc(s[nb], ql[2 * kp + 1], b2, b3);
+      }
+    }
+    /* causal mask (key <= the query's position) and the block's softmax */
+    float mxA = -INFINITY, mxB = -INFINITY;
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = kb0 + nb * 8 + 2 * t + e;
+        s[nb][e] = key <= pa ? s[nb][e] * p.scale2 : -INFINITY;
+        s[nb][2 + e] = key <= pb ? s[nb][2 + e] * p.scale2 : -INFINITY;
+        mxA = fmaxf(mxA, s[nb][e]);
+        mxB = fmaxf(mxB, s[nb][2 + e]);
+      }
+    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
+    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
+    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
+    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        s[nb][e] = mxA == -INFINITY ? 0.f : exp2f(s[nb][e] - mxA);
+        s[nb][2 + e] = mxB == -INFINITY ? 0.f : exp2f(s[nb][2 + e] - mxB);
+        lA += s[nb][e];
+        lB += s[nb][2 + e];
+      }
+    lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+    lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+    mA = mxA;
+    mB = mxB;
+    /* O = P.V: P (fp16) as A fragments straight from the score registers */
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t pf[4] = {pack_h2(s[2 * kk][0], s[2 * kk][1]), pack_h2(s[2 * kk][2], s[2 * kk][3]),
+                              pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]),
+                              pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3])};
+      const int key = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+      for (int dp = 0; dp < DN / 2; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        ldsm4t(saddr(Vs + key * HD + swz(key, dp * 2 + (lane >> 4)) * 8), b0, b1, b2, b3);
+        mma_acc(o[2 * dp], pf, b0, b1);
+        mma_acc(o[2 * dp + 1], pf, b2, b3);
+      }
+    }
+  }
+
+  /* merge the 4 warp blocks (shared memory, warp order) */
+  float* part = reinterpret_cast<float*>(sm); /* [AW][QT][PST], over the K / V staging */
+  __syncthreads();
+  {
+    float* pw = part + (size_t)warp * QT * PST;
+#pragma unroll
+    for (int d = 0; d < DN; ++d) {
+      pw[g * PST + 2 + d * 8 + 2 * t] = o[d][0];
+      pw[g * PST + 3 + d * 8 + 2 * t] = o[d][1];
+      pw[(g + 8) * PST + 2 + d * 8 + 2 * t] = o[d][2];
+      pw[(g + 8) * PST + 3 + d * 8 + 2 * t] = o[d][3];
+    }
+    if (t == 0) {
+      pw[g * PST] = mA;
+      pw[g * PST + 1] = lA;
+      pw[(g + 8) * PST] = mB;
+      pw[(g + 8) * PST + 1] = lB;
+    }
+  }
+  __syncthreads();
   auto out_ptr = [&](int qi) {
-    const int r = qi / p.G, gq = qi % p.G;
-    return reinterpret_cast<__half2*>(out + (size_t)(m0 + r) * p.H * hd + (kvh * p.G + gq) * hd);
+    const int qq = q0 + qi;
+    return reinterpret_cast<__half2*>(out + (size_t)(m0 + qq / p.G) * p.H * HD + (kvh * p.G + qq % p.G) * HD);
   };
-  if (n_splits == 1) {
+  const int ti = (gi * p.n_mt + mt) * p.Hkv + kvh;
+  float* gbase = scratch + (size_t)ti * p.max_splits * QT * PST;
+  for (int it = tid; it < QT * (HD / 2); it += AW * 32) {
+    const int qi = it / (HD / 2), d2 = it % (HD / 2);
+    float M = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < MAXITEMS; ++k) {
-      const int it = tid + k * ATHREADS;
-      if (it < n_items) {
-        const int qi = it / hd2, d2 = it % hd2;
-        const float l = S.lrun[qi];
-        out_ptr(qi)[d2] = __halves2half2(__float2half_rn(o[k].x / l), __float2half_rn(o[k].y / l));
+    for (int w = 0; w < AW; ++w) M = fmaxf(M, part[(w * QT + qi) * PST]);
+    float L = 0.f, ox = 0.f, oy = 0.f;
+#pragma unroll
+    for (int w = 0; w < AW; ++w) {
+      const float* pw = part + (size_t)(w * QT + qi) * PST;
+      const float e = pw[0] == -INFINITY ? 0.f : exp2f(pw[0] - M);
+      L = __fmaf_rn(pw[1], e, L);
+      ox = __fmaf_rn(pw[2 + 2 * d2], e, ox);
+      oy = __fmaf_rn(pw[3 + 2 * d2], e, oy);
+    }
+    if (n_splits == 1) {
+      if (qi < nq) {
+        const float inv = L > 0.f ? 1.0f / L : 0.f;
+        out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
       }
-    }
-    return;
-  }
-  /* partial of this split: (m, l) then the unnormalised output */
-  const int qstride = p.G * p.RB;
-  const size_t pstride = (size_t)qstride * (hd + 2);
-  float* base = scratch + ((size_t)gz * p.Hkv + kvh) * p.max_splits * pstride;
-  float* part = base + split * pstride;
-#pragma unroll
-  for (int k = 0; k < MAXITEMS; ++k) {
-    const int it = tid + k * ATHREADS;
-    if (it < n_items) {
-      const int qi = it / hd2, d2 = it % hd2;
-      part[(size_t)qi * (hd + 2) + 2 + 2 * d2] = o[k].x;
-      part[(size_t)qi * (hd + 2) + 3 + 2 * d2] = o[k].y;
+    } else {
+      float* gp = gbase + (size_t)split * QT * PST + (size_t)qi * PST;
+      if (d2 == 0) {
+        gp[0] = M;
+        gp[1] = L;
+      }
+      gp[2 + 2 * d2] = ox;
+      gp[3 + 2 * d2] = oy;
     }
   }
-  for (int qi = tid; qi < Q; qi += ATHREADS) {
-    part[(size_t)qi * (hd + 2)] = S.mrun[qi];
-    part[(size_t)qi * (hd + 2) + 1] = S.lrun[qi];
-  }
+  if (n_splits == 1) return;
   __threadfence();
   __syncthreads();
   __shared__ int is_last;
-  if (tid == 0) is_last = atomicAdd(&counters[gz * p.Hkv + kvh], 1) == n_splits - 1;
+  if (tid == 0) is_last = atomicAdd(&counters[ti], 1) == n_splits - 1;
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  /* merge in split order.  (1) every (query, split) max / sum is fetched in parallel into
-     shared memory; (2) a thread per query turns them into weights; (3) each output item
-     sums its splits with the loads of MERGE_UNROLL splits in flight at once. */
-  float* msm = S.qs; /* [Q][n_splits] (max, then weight)    */
-  float* lsm = S.ss; /* [Q][n_splits] sums                   */
-  for (int idx = tid; idx < Q * n_splits; idx += ATHREADS) {
+  /* merge of the splits in split order: (max, sum) of every (query, split) staged first */
+  float* msm = part;                   /* [QT][MAXSPLIT] max, then weight */
+  float* lsm = part + QT * MAXSPLIT;   /* [QT][MAXSPLIT] sum               */
+  float* Lq = part + 2 * QT * MAXSPLIT; /* [QT]                             */
+  for (int idx = tid; idx < QT * n_splits; idx += AW * 32) {
     const int qi = idx / n_splits, c = idx % n_splits;
-    msm[idx] = __ldcg(base + c * pstride + (size_t)qi * (hd + 2));
-    lsm[idx] = __ldcg(base + c * pstride + (size_t)qi * (hd + 2) + 1);
+    msm[qi * MAXSPLIT + c] = __ldcg(gbase + (size_t)c * QT * PST + (size_t)qi * PST);
+    lsm[qi * MAXSPLIT + c] = __ldcg(gbase + (size_t)c * QT * PST + (size_t)qi * PST + 1);
   }
   __syncthreads();
-  for (int qi = tid; qi < Q; qi += ATHREADS) {
+  for (int qi = tid; qi < QT; qi += AW * 32) {
     float M = -INFINITY;
-    for (int c = 0; c < n_splits; ++c) M = fmaxf(M, msm[qi * n_splits + c]);
+    for (int c = 0; c < n_splits; ++c) M = fmaxf(M, msm[qi * MAXSPLIT + c]);
     float L = 0.f;
     for (int c = 0; c < n_splits; ++c) {
-      const float mc = msm[qi * n_splits + c];
-      const float w = mc == -INFINITY ? 0.f : expf(mc - M);
-      msm[qi * n_splits + c] = w;
-      L = __fmaf_rn(lsm[qi * n_splits + c], w, L);
+      const float mc = msm[qi * MAXSPLIT + c];
+      const float w = mc == -INFINITY ? 0.f : exp2f(mc - M);
+      msm[qi * MAXSPLIT + c] = w;
+      L = __fmaf_rn(lsm[qi * MAXSPLIT + c], w, L);
     }
-    S.lrun[qi] = L;
+    Lq[qi] = L;
   }
   __syncthreads();
+  for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
+    const int qi = it / (HD / 2), d2 = it % (HD / 2);
+    float ox = 0.f, oy = 0.f;
+    for (int c0 = 0; c0 < n_splits; c0 += 8) {
+      float2 oc[8];
 #pragma unroll
-  for (int k = 0; k < MAXITEMS; ++k) {
-    const int it = tid + k * ATHREADS;
-    if (it < n_items) {
-      const int qi = it / hd2, d2 = it % hd2;
-      float ox = 0.f, oy = 0.f;
-      for (int c0 = 0; c0 < n_splits; c0 += MERGE_UNROLL) {
-        float2 oc[MERGE_UNROLL];
+      for (int u = 0; u < 8; ++u)
+        if (c0 + u < n_splits)
+          oc[u] = __ldcg(reinterpret_cast<const float2*>(gbase + (size_t)(c0 + u) * QT * PST + (size_t)qi * PST + 2) + d2);
 #pragma unroll
-        for (int u = 0; u < MERGE_UNROLL; ++u)
-          if (c0 + u < n_splits)
-            oc[u] = __ldcg(reinterpret_cast<const float2*>(base + (c0 + u) * pstride + (size_t)qi * (hd + 2) + 2) + d2);
-#pragma unroll
-        for (int u = 0; u < MERGE_UNROLL; ++u)
-          if (c0 + u < n_splits) {
-            const float w = msm[qi * n_splits + c0 + u];
-            ox = __fmaf_rn(oc[u].x, w, ox);
-            oy = __fmaf_rn(oc[u].y, w, oy);
-          }
-      }
-      const float L = S.lrun[qi];
-      out_ptr(qi)[d2] = __halves2half2(__float2half_rn(ox / L), __float2half_rn(oy / L));
+      for (int u = 0; u < 8; ++u)
+        if (c0 + u < n_splits) {
+          const float w = msm[qi * MAXSPLIT + c0 + u];
+          ox = __fmaf_rn(oc[u].x, w, ox);
+          oy = __fmaf_rn(oc[u].y, w, oy);
+        }
     }
+    const float L = Lq[qi];
+    const float inv = L > 0.f ? 1.0f / L : 0.f;
+    out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
   }
-  if (tid == 0) counters[gz * p.Hkv + kvh] = 0; /* ready for the next launch / graph replay */
+  if (tid == 0) counters[ti] = 0; /* ready for the next launch / graph replay */
 }
 
 void attn_geometry(const ulb_attn_desc* d, int M, int rps, int max_pos, AttnParams* p, int* n_groups) {
@@ -320,21 +342,18 @@ void attn_geometry(const ulb_attn_desc* d, int M, int rps, int max_pos, AttnPara
   p->cap = d->capacity;
   p->G = d->n_head / d->n_head_kv;
   p->rps = rps;
-  p->max_splits = max_pos / SPLIT + 1;
-  p->RB = AQMAX / p->G < 1 ? 1 : AQMAX / p->G;
-  /* the merge stages (query, split) pairs in shared memory: at most AQMAX * BK of them */
-  const int rb_merge = (AQMAX * BK) / (p->G * p->max_splits);
-  if (p->RB > rb_merge) p->RB = rb_merge < 1 ? 1 : rb_merge;
-  if (p->RB > rps) p->RB = rps;
-  p->n_rb = (rps + p->RB - 1) / p->RB;
-  p->scale = d->scale;
+  p->n_mt = (p->G * rps + QT - 1) / QT;
+  p->max_splits = max_pos / SPLITK + 1;
+  p->scale2 = d->scale * kLog2e;
   p->n_seq = d->n_seq;
   *n_groups = M / rps;
 }
 
 size_t attn_smem(int hd) {
-  return sizeof(float) * ((size_t)AQMAX * hd + AQMAX * BK + 3 * AQMAX) + sizeof(int) * AQMAX +
-         sizeof(__half) * 4 * (size_t)BK * hd;
+  const size_t kv = (size_t)AW * 2 * KB * hd * sizeof(__half);
+  const size_t part = (size_t)AW * QT * (hd + 2) * sizeof(float);
+  const size_t merge = ((size_t)2 * QT * MAXSPLIT + QT) * sizeof(float);
+  return std::max(kv, std::max(part, merge));
 }
 
 }  // namespace
@@ -343,18 +362,18 @@ size_t attention_scratch_floats(const ulb_attn_desc* d, int M, int rps, int max_
   AttnParams p;
   int ng;
   attn_geometry(d, M, rps, max_pos, &p, &ng);
-  *n_counters = ng * p.n_rb * p.Hkv;
-  return (size_t)ng * p.n_rb * p.Hkv * p.max_splits * (size_t)(p.G * p.RB) * (p.hd + 2);
+  *n_counters = ng * p.n_mt * p.Hkv;
+  return (size_t)ng * p.n_mt * p.Hkv * p.max_splits * QT * (size_t)(p.hd + 2);
 }
 
 int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, const __half* k,
                      const __half* v, const int* row_seq, const int* row_pos, int M, int rps,
                      __half* out, float* scratch, int* counters, size_t scratch_floats, int n_counters) {
-  ULB_CHECK(d->n_head % d->n_head_kv == 0, ULB_EINVAL, "attention: n_head %% n_head_kv != 0");
-  ULB_CHECK(d->head_dim % 16 == 0 && d->head_dim <= 128, ULB_EUNSUPPORTED, "attention: head_dim %d", d->head_dim);
-  ULB_CHECK(d->n_head / d->n_head_kv <= AQMAX, ULB_EUNSUPPORTED, "attention: GQA group > %d", AQMAX);
-  ULB_CHECK(d->capacity <= SPLIT * MAXSPLIT, ULB_EUNSUPPORTED, "attention: capacity %d > %d", d->capacity,
-            SPLIT * MAXSPLIT);
+  ULB_CHECK(d->n_head_kv > 0 && d->n_head % d->n_head_kv == 0, ULB_EINVAL, "attention: n_head %% n_head_kv != 0");
+  ULB_CHECK(d->head_dim == 64 || d->head_dim == 128, ULB_EUNSUPPORTED, "attention: head_dim %d (64 or 128)",
+            d->head_dim);
+  ULB_CHECK(d->capacity <= SPLITK * MAXSPLIT, ULB_EUNSUPPORTED, "attention: capacity %d > %d", d->capacity,
+            SPLITK * MAXSPLIT);
   ULB_CHECK(rps > 0 && M % rps == 0, ULB_EINVAL, "attention: M=%d not a multiple of rows_per_seq=%d", M, rps);
   ULB_CHECK(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 && ldq % 4 == 0,
             ULB_EINVAL, "attention: q / k / v must be 16-byte aligned (ldq a multiple of 4)");
@@ -369,12 +388,17 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
             "attention: scratch %zu floats / %d counters, need %zu / %d", scratch_floats, n_counters, need, need_c);
   static bool attr_set = false;
   if (!attr_set) {
-    ULB_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(128)));
+    ULB_CUDA(cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(64)));
+    ULB_CUDA(cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)attn_smem(128)));
     attr_set = true;
   }
-  dim3 grid(p.max_splits, p.Hkv, ng * p.n_rb), block(ATHREADS);
-  cudaError_t e = launch_k(c, attn_kernel, grid, block, attn_smem(p.hd), p, q, k, v, row_seq, row_pos, out, scratch,
-                           counters);
+  dim3 grid(p.n_mt * p.max_splits, p.Hkv, ng), block(AW * 32);
+  cudaError_t e = d->head_dim == 64
+                      ? launch_k(c, attn_mma_kernel<64>, grid, block, attn_smem(64), p, q, k, v, row_seq, row_pos,
+                                 out, scratch, counters)
+                      : launch_k(c, attn_mma_kernel<128>, grid, block, attn_smem(128), p, q, k, v, row_seq, row_pos,
+                                 out, scratch, counters);
   if (e != cudaSuccess) return cuda_error(e, "attention launch", __FILE__, __LINE__);
   return ULB_OK;
 }

@@ -8,11 +8,14 @@
  * shaders (src/shaders/gemm).
  *
  * Design (B200):
- *  - one CTA per 16-row strip; its 8 warps split the strip's K-tiles; the strip is one
- *    contiguous range of packed bytes which thread 0 hands to the L2 with a single
- *    cp.async.bulk.prefetch.L2 before griddepcontrol.wait, so weight streaming overlaps
- *    the tail of the previous kernel (programmatic dependent launch);
- *  - every lane fetches its share of a tile with 128-bit loads that bypass L1;
+ *  - persistent CTAs (2 per SM for M <= 8) walk 16-row strips; a strip is one contiguous
+ *    range of packed tiles, streamed global -> shared in ~36 KB chunks by cp.async.bulk
+ *    through a 2-slot mbarrier ring; the first chunks are issued before
+ *    griddepcontrol.wait, so the weight stream overlaps the previous kernel (programmatic
+ *    dependent launch), and the last warp done with a slot refills it (no producer warp,
+ *    so 8 warps x 2 CTAs leave 128 registers a thread);
+ *  - each warp owns tiles warp, warp + 8, ... of a chunk and loads tile j + 1 (weights
+ *    from shared memory, activations from L1) into registers before computing tile j;
  *  - nibbles become exact fp16 integers with one LOP3 + one HSUB2/HFMA2 per pair
  *    (0x6400 magic) and feed mma.sync.m16n8k16 (weights = A, activations = B, so M <= 8
  *    tokens fill one n-tile); each 32-weight block's scale is applied in fp32 to that
@@ -124,6 +127,19 @@ __device__ __forceinline__ void block_colsum(const __half* const (&xr)[NT], int 
     float tmp[4];
     mma16816(tmp, ONES, ONES, ONES, ONES, bx.x, bx.y, zero);
     mma16816(s[nt], ONES, ONES, ONES, ONES, bx.z, bx.w, tmp);
+  }
+}
+
+/* the same column sums from activation fragments already in registers */
+template <int NT>
+__device__ __forceinline__ void block_colsum_r(const uint4 (&bx)[NT], float (&s)[NT][4]) {
+  const uint32_t ONES = 0x3C003C00u;
+  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float tmp[4];
+    mma16816(tmp, ONES, ONES, ONES, ONES, bx[nt].x, bx[nt].y, zero);
+    mma16816(s[nt], ONES, ONES, ONES, ONES, bx[nt].z, bx[nt].w, tmp);
   }
 }
 
@@ -281,18 +297,83 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
+/*
+ * A tile's operands in registers.  The consumer loop loads tile j + 1 (shared-memory weight
+ * words, and for Q4_0 at NT = 1 also the activation fragments from L1) before it computes
+ * tile j, so the load latency hides behind a tile of dequant + MMA work.
+ *   Q4_0: 2 x 16 B of nibble words + 16 B of scales (rows g, g + 8) per lane.
+ *   Q4_K: 4 x 16 B of nibble words + the 16 B meta rows of g and g + 8.
+ */
+template <int QT, int NT> struct TileRegs;
+template <int NT> struct TileRegs<ULB_TYPE_Q4_0, NT> {
+  static constexpr bool PFX = NT == 1; /* activations prefetched with the weights */
+  uint4 w[2], sc;
+  uint4 x[PFX ? 4 : 1][NT];
+};
+template <int NT> struct TileRegs<ULB_TYPE_Q4_K, NT> {
+  static constexpr bool PFX = false;
+  uint4 w[4], mg, mg8;
+};
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
 template <int NT>
-__device__ __forceinline__ void q40_tile(const uint8_t* tp, int tile, const __half* const (&xr)[NT], int lane, int g,
-                                         float (&acc)[NT][4]) {
-  const uint4 c01 = *reinterpret_cast<const uint4*>(tp + lane * 16);
-  const uint4 c23 = *reinterpret_cast<const uint4*>(tp + 512 + lane * 16);
-  const uint4 csc = *reinterpret_cast<const uint4*>(tp + 1024 + g * 16);
-  const uint32_t words[8] = {c01.x, c01.y, c01.z, c01.w, c23.x, c23.y, c23.z, c23.w};
-  const uint32_t scw[4] = {csc.x, csc.y, csc.z, csc.w};
+__device__ __forceinline__ void tile_load(TileRegs<ULB_TYPE_Q4_0, NT>& r, const uint8_t* tp, int tile,
+                                          const __half* const (&xr)[NT], int lane, int g) {
+  r.w[0] = lds128(tp + lane * 16);
+  r.w[1] = lds128(tp + 512 + lane * 16);
+  r.sc = lds128(tp + 1024 + g * 16);
+  if (TileRegs<ULB_TYPE_Q4_0, NT>::PFX) {
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) r.x[b][nt] = __ldg(reinterpret_cast<const uint4*>(xr[nt] + tile * 128 + b * 32));
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void tile_load(TileRegs<ULB_TYPE_Q4_K, NT>& r, const uint8_t* tp, int, const __half* const (&)[NT],
+                                          int lane, int g) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p) r.w[p] = lds128(tp + p * 512 + lane * 16);
+  r.mg = lds128(tp + 2048 + g * 16);
+  r.mg8 = lds128(tp + 2048 + (g + 8) * 16);
+}
+
+/* dot products of one 32-weight block whose activation fragments are already in registers */
+template <int BIAS, int NT>
+__device__ __forceinline__ void block_mma_r(uint32_t vg, uint32_t vg8, const uint4 (&bx)[NT], float (&s)[NT][4]) {
+  uint32_t a01, a23, a45, a67, b01, b23, b45, b67;
+  nib_pairs<BIAS>(vg, a01, a23, a45, a67);
+  nib_pairs<BIAS>(vg8, b01, b23, b45, b67);
+  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float tmp[4];
+    mma16816(tmp, a01, b01, a23, b23, bx[nt].x, bx[nt].y, zero);
+    mma16816(s[nt], a45, b45, a67, b67, bx[nt].z, bx[nt].w, tmp);
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_0, NT>& r, int tile, const __half* const (&xr)[NT],
+                                             float (&acc)[NT][4]) {
+  const uint32_t words[8] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w, r.w[1].x, r.w[1].y, r.w[1].z, r.w[1].w};
+  const uint32_t scw[4] = {r.sc.x, r.sc.y, r.sc.z, r.sc.w};
+  uint4 xl[4][NT];
+  if (!TileRegs<ULB_TYPE_Q4_0, NT>::PFX) { /* all of the tile's activation loads first */
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) xl[b][nt] = __ldg(reinterpret_cast<const uint4*>(xr[nt] + tile * 128 + b * 32));
+  }
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
     float s[NT][4];
-    block_mma<8, NT>(words[2 * b], words[2 * b + 1], xr, tile * 128 + b * 32, s);
+    if (TileRegs<ULB_TYPE_Q4_0, NT>::PFX)
+      block_mma_r<8, NT>(words[2 * b], words[2 * b + 1], r.x[TileRegs<ULB_TYPE_Q4_0, NT>::PFX ? b : 0], s);
+    else
+      block_mma_r<8, NT>(words[2 * b], words[2 * b + 1], xl[b], s);
     const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&scw[b]));
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -305,8 +386,8 @@ __device__ __forceinline__ void q40_tile(const uint8_t* tp, int tile, const __ha
 }
 
 template <int NT>
-__device__ __forceinline__ void q4k_tile(const uint8_t* tp, int tile, const __half* const (&xr)[NT], int lane, int g,
-                                         float (&acc)[NT][4]);
+__device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_K, NT>& r, int tile, const __half* const (&xr)[NT],
+                                             float (&acc)[NT][4]);
 
 /*
  * Persistent, warp-specialised form: one CTA per SM walks strips blockIdx.x, +gridDim.x, ...
@@ -336,7 +417,7 @@ __device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, uint32_t parit
 }
 
 template <int QT, int NT, int EPI>
-__global__ void __launch_bounds__((PQW<NT>::CW + 1) * 32, PQW<NT>::MINB)
+__global__ void __launch_bounds__(PQW<NT>::CW * 32, PQW<NT>::MINB)
     qgemv_kernel(const uint8_t* __restrict__ w, int tiles, int n_strips, int N, const __half* __restrict__ x, int M,
                  int ldx, EpiArgs ea, int* err, int nb, const __half* __restrict__ xzero) {
   constexpr int TB = PQ<QT>::TB, CT = PQ<QT>::CT, NB = PQ<QT>::NB, CW = PQW<NT>::CW;
@@ -346,48 +427,39 @@ __global__ void __launch_bounds__((PQW<NT>::CW + 1) * 32, PQW<NT>::MINB)
   constexpr int NSL = CT / CW;
   extern __shared__ __align__(128) uint8_t ring[]; /* nb slots of CB bytes, then the slot sums */
   float4* red = reinterpret_cast<float4*>(ring + (size_t)nb * CB);
-  __shared__ uint64_t full[NB], empty[NB];
+  __shared__ uint64_t full[NB];
+  __shared__ uint32_t released[NB]; /* warps done with the slot's current chunk */
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nch = (tiles + CT - 1) / CT;
+  const int my_strips = (n_strips - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int total = my_strips * nch; /* chunks this CTA streams, in order */
+  /* chunk q of the CTA's sequence -> ring slot q % nb */
+  auto issue = [&](int q) {
+    const int s = blockIdx.x + (q / nch) * gridDim.x, ch = q % nch, slot = q % nb;
+    const uint32_t bytes = (uint32_t)min(CT, tiles - ch * CT) * TB;
+    mbar_expect_tx(&full[slot], bytes);
+    bulk_g2s(ring + (size_t)slot * CB, w + ((size_t)s * tiles + (size_t)ch * CT) * TB, bytes, &full[slot]);
+  };
   if (tid == 0) {
     for (int i = 0; i < nb; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], CW);
+      released[i] = 0;
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   const uint64_t deadline = gtimer() + 2000000000ull;
-  if (warp == CW) { /* ---------------- producer warp */
-    if (lane == 0) {
-      int seq = 0;
-      bool ok = true;
-      for (int s = blockIdx.x; s < n_strips && ok; s += gridDim.x)
-        for (int ch = 0; ch < nch; ++ch, ++seq) {
-          const int slot = seq % nb;
-          if (seq >= nb && !mbar_wait_deadline(&empty[slot], (uint32_t)((seq / nb) - 1) & 1u, deadline)) {
-            atomicOr(err, 2);
-            ok = false;
-            break;
-          }
-          const uint32_t bytes = (uint32_t)min(CT, tiles - ch * CT) * TB;
-          mbar_expect_tx(&full[slot], bytes);
-          bulk_g2s(ring + (size_t)slot * CB, w + ((size_t)s * tiles + (size_t)ch * CT) * TB, bytes, &full[slot]);
-        }
-    }
-    pdl_wait();
-    pdl_trigger();
-    return;
-  }
-  /* ---------------- consumer warps */
+  /* the weights do not depend on the previous kernel: start streaming before the wait */
+  if (tid == 0)
+    for (int q = 0; q < nb && q < total; ++q) issue(q);
   pdl_wait();
   pdl_trigger();
   const int g = lane >> 2, t = lane & 3;
   const __half* xr[NT];
   activation_rows<NT>(x, xzero, ldx, M, g, t, xr);
-  int seq = 0;
+  int seq = 0, iter = 0;
   bool ok = true;
-  for (int s = blockIdx.x; s < n_strips; s += gridDim.x) {
+  for (int s = blockIdx.x; s < n_strips; s += gridDim.x, ++iter) {
     float acc[NSL][NT][4];
 #pragma unroll
     for (int j = 0; j < NSL; ++j)
@@ -399,20 +471,40 @@ __global__ void __launch_bounds__((PQW<NT>::CW + 1) * 32, PQW<NT>::MINB)
       if (ok) {
         const uint8_t* base = ring + (size_t)slot * CB;
         const int t0 = ch * CT, tn = min(tiles - t0, CT);
+        /* software pipeline over the warp's tiles warp, warp + CW, ...: load j + 1, compute j */
+        TileRegs<QT, NT> tr[2]; /* indexed by j & 1: constant after unrolling, so no copies */
+        if (warp < tn) tile_load<NT>(tr[0], base + warp * TB, t0 + warp, xr, lane, g);
 #pragma unroll
         for (int j = 0; j < NSL; ++j) {
           const int i = warp + j * CW;
-          if (i < tn) {
-            if (QT == ULB_TYPE_Q4_0) q40_tile<NT>(base + i * TB, t0 + i, xr, lane, g, acc[j]);
-            else q4k_tile<NT>(base + i * TB, t0 + i, xr, lane, g, acc[j]);
-          }
+          if (j + 1 < NSL && i + CW < tn) tile_load<NT>(tr[(j + 1) & 1], base + (i + CW) * TB, t0 + i + CW, xr, lane, g);
+          if (i < tn) tile_compute<NT>(tr[j & 1], t0 + i, xr, acc[j]);
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (lane == 0) {
+        /* the last of the CW warps to be done with the slot refills it with chunk seq + nb:
+           acq_rel makes every warp's reads of the slot happen before the refill, and the
+           proxy fence orders them before the async-proxy write of the bulk copy */
+        uint32_t prev;
+        asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                     : "=r"(prev)
+                     : "r"(smem_u32(&released[slot]))
+                     : "memory");
+        if (prev == CW - 1) {
+          released[slot] = 0;
+          if (seq + nb < total) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(seq + nb);
+          }
+        }
+      }
     }
     /* slots w, w+CW, ... are summed in the warp, then warps in warp order: CW is the same
-       for every NT, so this order is fixed */
+       for every NT, so this order is fixed.  The partials alternate between two buffers, so
+       one barrier per strip suffices: a buffer is rewritten two strips later, after every
+       warp (its reader included) has passed the barrier of the strip in between. */
+    float4* rb = red + (size_t)(iter & 1) * CW * NT * 32;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       float4 v = make_float4(acc[0][nt][0], acc[0][nt][1], acc[0][nt][2], acc[0][nt][3]);
@@ -420,33 +512,31 @@ __global__ void __launch_bounds__((PQW<NT>::CW + 1) * 32, PQW<NT>::MINB)
       for (int j = 1; j < NSL; ++j) {
         v.x += acc[j][nt][0]; v.y += acc[j][nt][1]; v.z += acc[j][nt][2]; v.w += acc[j][nt][3];
       }
-      red[(warp * NT + nt) * 32 + lane] = v;
+      rb[(warp * NT + nt) * 32 + lane] = v;
     }
     asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
-    for (int nt = warp; nt < NT; nt += CW) {
-      float4 v = red[nt * 32 + lane];
+    /* n-tile nt of this strip is finished by warp (nt + iter) % CW: the epilogue work rotates
+       over the warps instead of stalling warp 0 on every strip */
+    for (int nt = (warp - iter % CW + CW) % CW; nt < NT; nt += CW) {
+      float4 v = rb[nt * 32 + lane];
 #pragma unroll
       for (int w2 = 1; w2 < CW; ++w2) {
-        const float4 o = red[(w2 * NT + nt) * 32 + lane];
+        const float4 o = rb[(w2 * NT + nt) * 32 + lane];
         v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
       }
       if (ok) epilogue<EPI>(ea, s, nt, g, t, M, N, v);
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
   }
   if (!ok && lane == 0) atomicOr(err, 2);
 }
 
 /* ------------------------------------------------------------------ Q4_K tile */
 template <int NT>
-__device__ __forceinline__ void q4k_tile(const uint8_t* tp, int tile, const __half* const (&xr)[NT], int lane, int g,
-                                         float (&acc)[NT][4]) {
+__device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_K, NT>& r, int tile, const __half* const (&xr)[NT],
+                                             float (&acc)[NT][4]) {
   {
-    uint4 nb[4];
-#pragma unroll
-    for (int p = 0; p < 4; ++p) nb[p] = *reinterpret_cast<const uint4*>(tp + p * 512 + lane * 16);
-    const uint4 mg = *reinterpret_cast<const uint4*>(tp + 2048 + g * 16);
-    const uint4 mg8 = *reinterpret_cast<const uint4*>(tp + 2048 + (g + 8) * 16);
+    const uint4(&nb)[4] = r.w;
+    const uint4 mg = r.mg, mg8 = r.mg8;
     const float2 dg = __half22float2(*reinterpret_cast<const __half2*>(&mg.x));   /* (d, dmin) row g */
     const float2 dg8 = __half22float2(*reinterpret_cast<const __half2*>(&mg8.x)); /* row g + 8 */
     float t1[NT][4], t0[NT][4];
@@ -459,8 +549,11 @@ __device__ __forceinline__ void q4k_tile(const uint8_t* tp, int tile, const __ha
       const uint32_t* wp = reinterpret_cast<const uint32_t*>(&nb[(J) >> 1]);            \
       float s1[NT][4], s0[NT][4];                                                        \
       const int kofs = tile * 256 + (J) * 32;                                            \
-      block_mma<0, NT>(wp[((J) & 1) * 2], wp[((J) & 1) * 2 + 1], xr, kofs, s1);         \
-      block_colsum<NT>(xr, kofs, s0);                                                    \
+      uint4 bx[NT];                                                                      \
+      _Pragma("unroll") for (int nt = 0; nt < NT; ++nt)                                  \
+        bx[nt] = __ldg(reinterpret_cast<const uint4*>(xr[nt] + kofs));                   \
+      block_mma_r<0, NT>(wp[((J) & 1) * 2], wp[((J) & 1) * 2 + 1], bx, s1);              \
+      block_colsum_r<NT>(bx, s0);                                                        \
       float scg, mng, scg8, mng8;                                                        \
       q4k_sm<J>(mg.y, mg.z, mg.w, scg, mng);                                             \
       q4k_sm<J>(mg8.y, mg8.z, mg8.w, scg8, mng8);                                        \
@@ -614,7 +707,7 @@ int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const Epi
   const int per_cta = (w->n_strips + ctas - 1) / ctas;
   const int grid = (w->n_strips + per_cta - 1) / per_cta; /* balanced: every CTA gets per_cta or per_cta-1 strips */
   const int slots = min(NB, per_cta * nch);
-  const size_t red_bytes = (size_t)CW * NT * 32 * sizeof(float4);
+  const size_t red_bytes = 2 * (size_t)CW * NT * 32 * sizeof(float4); /* two alternating partial buffers */
   const size_t smem = (size_t)slots * CT * TB + red_bytes;
   static bool attr_set = false;
   if (!attr_set) {
@@ -622,7 +715,7 @@ int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const Epi
                                   (int)((size_t)NB * CT * TB + red_bytes)));
     attr_set = true;
   }
-  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI>, dim3(grid), dim3((CW + 1) * 32), smem,
+  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI>, dim3(grid), dim3(CW * 32), smem,
                            (const uint8_t*)w->dev, w->tiles, w->n_strips, w->N, x, M, ldx, a, c->dev_err, slots,
                            (const __half*)c->zero_row);
   if (e != cudaSuccess) return cuda_error(e, "qgemv launch", __FILE__, __LINE__);

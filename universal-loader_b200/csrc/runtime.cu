@@ -10,6 +10,8 @@
 #include <memory>
 #include <mutex>
 
+#include <new>
+
 #include "ulb_internal.h"
 
 namespace ulb {
@@ -180,6 +182,57 @@ int ulb_event_elapsed_ms(void* a, void* b, float* ms) {
 }
 int ulb_event_destroy(void* ev) {
   if (ev) cudaEventDestroy((cudaEvent_t)ev);
+  return ULB_OK;
+}
+
+struct ulb_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+int ulb_capture_begin(ulb_ctx* ctx) {
+  ULB_CHECK(ctx, ULB_EINVAL, "ulb_capture_begin: NULL context");
+  ULB_CUDA(cudaSetDevice(ctx->c.device));
+  ULB_CUDA(cudaStreamBeginCapture(ctx->c.stream, cudaStreamCaptureModeThreadLocal));
+  return ULB_OK;
+}
+
+int ulb_capture_end(ulb_ctx* ctx, ulb_graph** out) {
+  ULB_CHECK(ctx && out, ULB_EINVAL, "ulb_capture_end: NULL argument");
+  *out = nullptr;
+  ULB_CUDA(cudaSetDevice(ctx->c.device));
+  cudaGraph_t g = nullptr;
+  ULB_CUDA(cudaStreamEndCapture(ctx->c.stream, &g));
+  cudaGraphExec_t x = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&x, g, 0);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(g);
+    return cuda_error(e, "graph instantiate", __FILE__, __LINE__);
+  }
+  ulb_graph* r = new (std::nothrow) ulb_graph;
+  if (!r) {
+    cudaGraphExecDestroy(x);
+    cudaGraphDestroy(g);
+    return set_error(ULB_ENOMEM, "ulb_capture_end: host allocation");
+  }
+  r->graph = g;
+  r->exec = x;
+  *out = r;
+  return ULB_OK;
+}
+
+int ulb_graph_launch(ulb_ctx* ctx, const ulb_graph* g) {
+  ULB_CHECK(ctx && g && g->exec, ULB_EINVAL, "ulb_graph_launch: NULL argument");
+  ULB_CUDA(cudaSetDevice(ctx->c.device));
+  ULB_CUDA(cudaGraphLaunch(g->exec, ctx->c.stream));
+  return ULB_OK;
+}
+
+int ulb_graph_free(ulb_graph* g) {
+  if (!g) return ULB_OK;
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  delete g;
   return ULB_OK;
 }
 

@@ -8,11 +8,13 @@
  * token-match heuristic) with standard speculative rejection sampling (Leviathan et al.
  * 2023; Chen et al. 2023).
  *
- * Warp definition (identical in the CPU oracle): z = logit / T; keep z >= k-th largest z
- * (top-k); e = exp(z - max z) in fp64; keep tokens whose strictly-more-probable mass is
- * < top_p * sum(e) (top-p); p = e / sum over kept.  Keep sets are decided on exact
- * comparisons of z (radix select on the order-preserving integer key of z), so the same
- * logits give the same kept set on host and device.
+ * Warp definition (identical in the CPU oracle): z = logit * iT with iT = 1/T rounded once;
+ * top-k keeps z >= the k-th largest z; e = ulb_warp_exp(z - max z) (binary32, bit-identical
+ * on host and device), summed in fp64; top-p keeps tokens whose strictly-more-probable mass
+ * is < top_p * sum(e); p = e / sum over the kept set.  Sampling is an inverse CDF over e in
+ * index order.  Keep sets are decided on exact comparisons of z (radix select on the
+ * order-preserving integer key of z), so the same logits give the same kept set on host and
+ * device.
  *
  * Kernels: row_stats (one CTA per row: max, keep threshold, normaliser, argmax) over all
  * target and draft rows of a round in parallel; sample (stats + inverse CDF for the draft
@@ -24,7 +26,8 @@ namespace ulb {
 
 namespace {
 
-constexpr int ST = 256; /* threads per row CTA */
+constexpr int ST = 256;  /* threads per row CTA (stats, draft sampling) */
+constexpr int DT = 1024; /* threads per sequence CTA (decide: residual / bonus sampling) */
 
 struct RowStats {
   float mx;    /* max z                                  */
@@ -34,8 +37,9 @@ struct RowStats {
   int pad;
 };
 
-/* z = logit / T with -0 folded to +0, so key order and float order agree */
-__device__ __forceinline__ float zof(float x, float T) { return __fadd_rn(__fdiv_rn(x, T), 0.0f); }
+/* z = logit * iT with -0 folded to +0, so key order and float order agree; iT is 1 / T
+   rounded once (a multiply per logit instead of a divide) */
+__device__ __forceinline__ float zof(float x, float iT) { return __fadd_rn(__fmul_rn(x, iT), 0.0f); }
 
 __device__ __forceinline__ uint32_t fkey(float f) {
   const uint32_t u = __float_as_uint(f);
@@ -46,19 +50,21 @@ __device__ __forceinline__ float unkey(uint32_t k) {
   return __uint_as_float(u);
 }
 
+template <int BT>
 struct SmemRed {
-  float f[ST / 32];
-  int i[ST / 32];
-  double d[ST / 32];
+  float f[BT / 32];
+  int i[BT / 32];
+  double d[BT / 32];
   unsigned int hist_u[256];
   double hist_d[256];
-  double seg[ST];
+  double seg[BT];
   uint32_t prefix;
   int found;
   double above;
 };
 
-__device__ float block_max(float v, SmemRed& s) {
+template <int BT>
+__device__ float block_max(float v, SmemRed<BT>& s) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   __syncthreads();
@@ -66,12 +72,13 @@ __device__ float block_max(float v, SmemRed& s) {
   __syncthreads();
   float r = s.f[0];
 #pragma unroll
-  for (int w = 1; w < ST / 32; ++w) r = fmaxf(r, s.f[w]);
+  for (int w = 1; w < BT / 32; ++w) r = fmaxf(r, s.f[w]);
   return r;
 }
 
 /* deterministic fp64 sum: per-thread partials reduced in a fixed tree */
-__device__ double block_sum_d(double v, SmemRed& s) {
+template <int BT>
+__device__ double block_sum_d(double v, SmemRed<BT>& s) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   __syncthreads();
@@ -79,15 +86,16 @@ __device__ double block_sum_d(double v, SmemRed& s) {
   __syncthreads();
   double r = s.d[0];
 #pragma unroll
-  for (int w = 1; w < ST / 32; ++w) r += s.d[w];
+  for (int w = 1; w < BT / 32; ++w) r += s.d[w];
   return r;
 }
 
 /* argmax, lowest index on ties */
-__device__ int block_argmax(const float* l, int V, SmemRed& s) {
+template <int BT>
+__device__ int block_argmax(const float* l, int V, SmemRed<BT>& s) {
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += ST) {
+  for (int i = threadIdx.x; i < V; i += BT) {
     const float x = l[i];
     if (x > bv || (x == bv && i < bi)) { bv = x; bi = i; }
   }
@@ -101,20 +109,21 @@ __device__ int block_argmax(const float* l, int V, SmemRed& s) {
   if ((threadIdx.x & 31) == 0) { s.f[threadIdx.x >> 5] = bv; s.i[threadIdx.x >> 5] = bi; }
   __syncthreads();
   bv = s.f[0]; bi = s.i[0];
-  for (int w = 1; w < ST / 32; ++w)
+  for (int w = 1; w < BT / 32; ++w)
     if (s.f[w] > bv || (s.f[w] == bv && s.i[w] < bi)) { bv = s.f[w]; bi = s.i[w]; }
   return bi == 0x7fffffff ? 0 : bi;
 }
 
 /* key of the k-th largest z (count based radix select, exact) */
-__device__ uint32_t kth_largest_key(const float* l, int V, float T, int k, SmemRed& s) {
+template <int BT>
+__device__ uint32_t kth_largest_key(const float* l, int V, float iT, int k, SmemRed<BT>& s) {
   uint32_t prefix = 0, mask = 0;
   int need = k; /* rank within the current prefix class (1-based) */
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = threadIdx.x; b < 256; b += ST) s.hist_u[b] = 0;
+    for (int b = threadIdx.x; b < 256; b += BT) s.hist_u[b] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < V; i += ST) {
-      const uint32_t key = fkey(zof(l[i], T));
+    for (int i = threadIdx.x; i < V; i += BT) {
+      const uint32_t key = fkey(zof(l[i], iT));
       if ((key & mask) == prefix) atomicAdd(&s.hist_u[(key >> shift) & 255u], 1u);
     }
     __syncthreads();
@@ -140,17 +149,18 @@ __device__ uint32_t kth_largest_key(const float* l, int V, float T, int k, SmemR
  * key of the smallest z kept by top-p: the first element in descending z order whose
  * inclusive cumulative mass reaches P (mass histograms in fp64).
  */
-__device__ uint32_t topp_key(const float* l, int V, float T, float mx, uint32_t key_lo, double P, SmemRed& s) {
+template <int BT>
+__device__ uint32_t topp_key(const float* l, int V, float iT, float mx, uint32_t key_lo, double P, SmemRed<BT>& s) {
   uint32_t prefix = 0, mask = 0;
   double above = 0.0;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = threadIdx.x; b < 256; b += ST) s.hist_d[b] = 0.0;
+    for (int b = threadIdx.x; b < 256; b += BT) s.hist_d[b] = 0.0;
     __syncthreads();
-    for (int i = threadIdx.x; i < V; i += ST) {
-      const float z = zof(l[i], T);
+    for (int i = threadIdx.x; i < V; i += BT) {
+      const float z = zof(l[i], iT);
       const uint32_t key = fkey(z);
       if (key >= key_lo && (key & mask) == prefix)
-        atomicAdd(&s.hist_d[(key >> shift) & 255u], exp((double)(z - mx)));
+        atomicAdd(&s.hist_d[(key >> shift) & 255u], (double)ulb_warp_exp(__fsub_rn(z, mx)));
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -179,29 +189,30 @@ __device__ uint32_t topp_key(const float* l, int V, float T, float mx, uint32_t 
   return prefix;
 }
 
-__device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowStats& out, SmemRed& s) {
+template <int BT>
+__device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowStats& out, SmemRed<BT>& s) {
   const int amax = block_argmax(l, V, s);
   if (!(w.temperature > 0.f)) {
     if (threadIdx.x == 0) { out.mx = l[amax]; out.thr = -INFINITY; out.Z = 1.0; out.amax = amax; }
     return;
   }
-  const float T = w.temperature;
-  const float mx = zof(l[amax], T); /* division is monotone: max z = z of the max logit */
+  const float iT = __fdiv_rn(1.0f, w.temperature); /* inverse temperature */
+  const float mx = zof(l[amax], iT); /* scaling by 1/T > 0 is monotone: max z = z of the max logit */
   uint32_t key_lo = 0;
-  if (w.top_k > 0 && w.top_k < V) key_lo = kth_largest_key(l, V, T, w.top_k, s);
+  if (w.top_k > 0 && w.top_k < V) key_lo = kth_largest_key(l, V, iT, w.top_k, s);
   if (w.top_p > 0.f && w.top_p < 1.f) {
     double zs = 0.0;
-    for (int i = threadIdx.x; i < V; i += ST) {
-      const float z = zof(l[i], T);
-      if (fkey(z) >= key_lo) zs += exp((double)(z - mx));
+    for (int i = threadIdx.x; i < V; i += BT) {
+      const float z = zof(l[i], iT);
+      if (fkey(z) >= key_lo) zs += (double)ulb_warp_exp(__fsub_rn(z, mx));
     }
     const double Z0 = block_sum_d(zs, s);
-    key_lo = topp_key(l, V, T, mx, key_lo, (double)w.top_p * Z0, s);
+    key_lo = topp_key(l, V, iT, mx, key_lo, (double)w.top_p * Z0, s);
   }
   double zs = 0.0;
-  for (int i = threadIdx.x; i < V; i += ST) {
-    const float z = zof(l[i], T);
-    if (fkey(z) >= key_lo) zs += exp((double)(z - mx));
+  for (int i = threadIdx.x; i < V; i += BT) {
+    const float z = zof(l[i], iT);
+    if (fkey(z) >= key_lo) zs += (double)ulb_warp_exp(__fsub_rn(z, mx));
   }
   const double Z = block_sum_d(zs, s);
   if (threadIdx.x == 0) {
@@ -213,19 +224,21 @@ __device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowS
 }
 
 /* warped probability weight e (unnormalised) of token i under stats st */
-__device__ __forceinline__ double warped_e(const float* l, int i, float T, const RowStats& st) {
-  const float z = zof(l[i], T);
+__device__ __forceinline__ double warped_e(const float* l, int i, float iT, const RowStats& st) {
+  const float z = zof(l[i], iT);
   if (!(z >= st.thr)) return 0.0;
-  return exp((double)(z - st.mx));
+  return (double)ulb_warp_exp(__fsub_rn(z, st.mx));
 }
 
 /*
- * Inverse CDF in index order over weights produced by wfun(i) (fp64, >= 0): returns the
- * smallest i whose cumulative weight exceeds target.  Fixed per-thread contiguous segments.
+ * Inverse CDF in index order over weights produced by wfun(i) (fp64, >= 0): with W the
+ * total weight (sum of per-thread contiguous segments, in segment order), returns the
+ * smallest i whose cumulative weight exceeds u * W, and W in *total.  One pass over the
+ * weights plus a scan of the one segment that holds the target.
  */
-template <typename WF>
-__device__ int block_inv_cdf(int V, double target, WF wfun, SmemRed& s) {
-  const int seg = (V + ST - 1) / ST;
+template <int BT, typename WF>
+__device__ int block_inv_cdf(int V, float u, WF wfun, SmemRed<BT>& s, double* total) {
+  const int seg = (V + BT - 1) / BT;
   const int b0 = threadIdx.x * seg, b1 = min(V, b0 + seg);
   double sum = 0.0;
   for (int i = b0; i < b1; ++i) sum += wfun(i);
@@ -235,9 +248,12 @@ __device__ int block_inv_cdf(int V, double target, WF wfun, SmemRed& s) {
   __syncthreads();
   if (threadIdx.x == 0) {
     double c = 0.0;
-    for (int t = 0; t < ST; ++t) { const double v = s.seg[t]; s.seg[t] = c; c += v; }
+    for (int t = 0; t < BT; ++t) { const double v = s.seg[t]; s.seg[t] = c; c += v; }
+    s.above = c;
   }
   __syncthreads();
+  const double W = s.above;
+  const double target = (double)u * W;
   double cum = s.seg[threadIdx.x];
   if (b0 < b1 && cum + sum > target) {
     for (int i = b0; i < b1; ++i) {
@@ -252,17 +268,18 @@ __device__ int block_inv_cdf(int V, double target, WF wfun, SmemRed& s) {
   if (r == 0x7fffffff) { /* target at/above the total through rounding: last positive weight */
     __syncthreads();
     int last = -1;
-    for (int i = threadIdx.x; i < V; i += ST)
+    for (int i = threadIdx.x; i < V; i += BT)
       if (wfun(i) > 0.0) last = max(last, i);
 #pragma unroll
     for (int o = 16; o; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
     if ((threadIdx.x & 31) == 0) s.i[threadIdx.x >> 5] = last;
     __syncthreads();
     r = s.i[0];
-    for (int w2 = 1; w2 < ST / 32; ++w2) r = max(r, s.i[w2]);
+    for (int w2 = 1; w2 < BT / 32; ++w2) r = max(r, s.i[w2]);
     if (r < 0) r = 0;
   }
   __syncthreads();
+  if (total) *total = W;
   return r;
 }
 
@@ -277,7 +294,7 @@ __global__ void __launch_bounds__(ST) sample_kernel(const float* __restrict__ lo
                                                     uint64_t seed, const uint32_t* dev_round, uint32_t round,
                                                     uint32_t slot, uint32_t tag, uint32_t seq_base, int32_t* out,
                                                     int out_stride) {
-  __shared__ SmemRed s;
+  __shared__ SmemRed<ST> s;
   __shared__ RowStats st;
   pdl_wait();
   pdl_trigger();
@@ -292,9 +309,9 @@ __global__ void __launch_bounds__(ST) sample_kernel(const float* __restrict__ lo
     const uint32_t seq = seq_base + (uint32_t)row;
     const uint32_t r = dev_round ? dev_round[seq] : round;
     const float u = rng_u(seed, r, seq, slot, tag);
-    const float T = w.temperature;
+    const float iT = __fdiv_rn(1.0f, w.temperature); /* inverse temperature */
     const RowStats stc = st;
-    tok = block_inv_cdf(V, (double)u * stc.Z, [&](int i) { return warped_e(l, i, T, stc); }, s);
+    tok = block_inv_cdf(V, u, [&](int i) { return warped_e(l, i, iT, stc); }, s, nullptr);
   }
   if (threadIdx.x == 0) out[(size_t)row * out_stride] = tok;
 }
@@ -302,7 +319,7 @@ __global__ void __launch_bounds__(ST) sample_kernel(const float* __restrict__ lo
 /* stats for p rows [B][k+1] followed by q rows [B][k] */
 __global__ void __launch_bounds__(ST) stats_kernel(const float* __restrict__ p, const float* __restrict__ q, int B,
                                                    int k, int V, ulb_warp w, RowStats* __restrict__ out) {
-  __shared__ SmemRed s;
+  __shared__ SmemRed<ST> s;
   __shared__ RowStats st;
   pdl_wait();
   pdl_trigger();
@@ -327,17 +344,17 @@ struct SpecCommit {
 };
 
 /* one CTA per sequence */
-__global__ void __launch_bounds__(ST) decide_kernel(const float* __restrict__ p, const float* __restrict__ q,
+__global__ void __launch_bounds__(DT) decide_kernel(const float* __restrict__ p, const float* __restrict__ q,
                                                     const int32_t* __restrict__ draft, const RowStats* __restrict__ rs,
                                                     int B, int k, int V, ulb_warp w, uint64_t seed,
                                                     const uint32_t* dev_round, uint32_t round,
                                                     int32_t* out_tokens, int32_t* out_n, SpecCommit cm) {
-  __shared__ SmemRed s;
+  __shared__ SmemRed<DT> s;
   pdl_wait();
   pdl_trigger();
   const int b = blockIdx.x;
   const bool greedy = !(w.temperature > 0.f);
-  const float T = greedy ? 1.f : w.temperature;
+  const float iT = greedy ? 1.f : __fdiv_rn(1.0f, w.temperature); /* inverse temperature */
   const uint32_t rnd = dev_round ? dev_round[b] : round;
   const int np = B * (k + 1);
   int n = 0, tok = -1;
@@ -353,21 +370,19 @@ __global__ void __launch_bounds__(ST) decide_kernel(const float* __restrict__ p,
     const float* pl = p + ((size_t)b * (k + 1) + i) * V;
     const float* ql = q + ((size_t)b * k + i) * V;
     const bool in_vocab = (unsigned)x < (unsigned)V; /* a token outside the vocabulary is rejected */
-    const double px = in_vocab ? warped_e(pl, x, T, sp) / sp.Z : 0.0;
-    const double qx = in_vocab ? warped_e(ql, x, T, sq) / sq.Z : 0.0;
+    const double px = in_vocab ? warped_e(pl, x, iT, sp) / sp.Z : 0.0;
+    const double qx = in_vocab ? warped_e(ql, x, iT, sq) / sq.Z : 0.0;
     const float u = rng_u(seed, rnd, (uint32_t)b, (uint32_t)i, ULB_RNG_ACCEPT);
     if ((double)u * qx < px) { ++n; continue; }
-    /* residual norm(max(0, p - q)) */
+    /* residual norm(max(0, p - q)), as max(0, e_p Z_q - e_q Z_p) = Z_p Z_q max(0, p - q) */
     auto resid = [&](int v) {
-      const double r = warped_e(pl, v, T, sp) / sp.Z - warped_e(ql, v, T, sq) / sq.Z;
+      const double r = warped_e(pl, v, iT, sp) * sq.Z - warped_e(ql, v, iT, sq) * sp.Z;
       return r > 0.0 ? r : 0.0;
     };
-    double part = 0.0;
-    for (int v = threadIdx.x; v < V; v += ST) part += resid(v);
-    const double R = block_sum_d(part, s);
     const float u2 = rng_u(seed, rnd, (uint32_t)b, (uint32_t)i, ULB_RNG_RESID);
-    if (R > 0.0) tok = block_inv_cdf(V, (double)u2 * R, resid, s);
-    else tok = block_inv_cdf(V, (double)u2 * sp.Z, [&](int v) { return warped_e(pl, v, T, sp); }, s);
+    double R = 0.0;
+    tok = block_inv_cdf(V, u2, resid, s, &R);
+    if (!(R > 0.0)) tok = block_inv_cdf(V, u2, [&](int v) { return warped_e(pl, v, iT, sp); }, s, nullptr);
     break;
   }
   if (tok < 0) {
@@ -376,7 +391,7 @@ __global__ void __launch_bounds__(ST) decide_kernel(const float* __restrict__ p,
     else {
       const float* pl = p + ((size_t)b * (k + 1) + k) * V;
       const float u2 = rng_u(seed, rnd, (uint32_t)b, (uint32_t)k, ULB_RNG_RESID);
-      tok = block_inv_cdf(V, (double)u2 * sp.Z, [&](int v) { return warped_e(pl, v, T, sp); }, s);
+      tok = block_inv_cdf(V, u2, [&](int v) { return warped_e(pl, v, iT, sp); }, s, nullptr);
     }
   }
   if (threadIdx.x != 0) return;
@@ -452,7 +467,7 @@ int launch_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* dr
   if (e != cudaSuccess) return cuda_error(e, "stats launch", __FILE__, __LINE__);
   SpecCommit cm = {};
   if (commit) cm = *(const SpecCommit*)commit;
-  e = launch_k(c, decide_kernel, dim3(B), dim3(ST), 0, p, q, draft, (const RowStats*)rs, B, k, V, *w, seed,
+  e = launch_k(c, decide_kernel, dim3(B), dim3(DT), 0, p, q, draft, (const RowStats*)rs, B, k, V, *w, seed,
                dev_round, round, out_tokens, out_n, cm);
   if (e != cudaSuccess) return cuda_error(e, "decide launch", __FILE__, __LINE__);
   return ULB_OK;

@@ -7,6 +7,7 @@
  *  - IEEE binary16 <-> binary32 conversion (round-to-nearest-even), matching the
  *    semantics of the reference's half_to_float (src/inference/inference_engine.cpp:15-37).
  *  - The counter layout used by the speculative loop for every uniform it draws.
+ *  - The exponential of the sampler's logit weights (ulb_warp_exp).
  */
 #ifndef ULB_COMMON_H
 #define ULB_COMMON_H
@@ -58,6 +59,45 @@ enum {
 ULB_HD float ulb_uniform(uint64_t seed, uint32_t round, uint32_t seq, uint32_t slot, uint32_t tag) {
   ulb_u32x4 r = ulb_philox4x32_10(round, seq, slot, tag, (uint32_t)seed, (uint32_t)(seed >> 32));
   return ulb_u01(r.v[0]);
+}
+
+/* ---------------------------------------------------------------- warp weights */
+#if defined(__CUDA_ARCH__)
+#define ULB_FMUL(a, b) __fmul_rn((a), (b))
+#define ULB_FMA(a, b, c) __fmaf_rn((a), (b), (c))
+#define ULB_RINT(a) rintf(a)
+#else
+#include <math.h>
+#define ULB_FMUL(a, b) ((a) * (b)) /* host builds use -ffp-contract=off */
+#define ULB_FMA(a, b, c) fmaf((a), (b), (c))
+#define ULB_RINT(a) rintf(a)
+#endif
+
+/*
+ * exp(x) for the sampler's weights, x = z - max z <= 0, in binary32.  Every step is one
+ * IEEE-rounded operation, so host and device give bit-identical weights:
+ *   k = rint(x / ln 2); r = x - k ln 2 with ln 2 split in two parts (Cody & Waite, 1980:
+ *   C1 = 355/512 has 9 significant bits, so k C1 is exact and x - k C1 has no rounding);
+ *   exp(r), |r| <= ln(2)/2, by its Taylor series to degree 7 in Horner form (truncation
+ *   below 2^-27 relative); result = exp(r) * 2^k.
+ * x < -87 (a weight below 2^-125 of the largest) gives 0.
+ */
+ULB_HD float ulb_warp_exp(float x) {
+  if (!(x >= -87.0f)) return 0.0f;
+  const float kf = ULB_RINT(ULB_FMUL(x, 1.44269504088896341f));
+  float r = ULB_FMA(kf, -0.693359375f, x);
+  r = ULB_FMA(kf, 2.12194440054690583e-4f, r);
+  float p = 1.98412698412698413e-4f;   /* 1/7! */
+  p = ULB_FMA(p, r, 1.38888888888888889e-3f); /* 1/6! */
+  p = ULB_FMA(p, r, 8.33333333333333333e-3f); /* 1/5! */
+  p = ULB_FMA(p, r, 4.16666666666666667e-2f); /* 1/4! */
+  p = ULB_FMA(p, r, 1.66666666666666667e-1f); /* 1/3! */
+  p = ULB_FMA(p, r, 0.5f);
+  p = ULB_FMA(p, r, 1.0f);
+  p = ULB_FMA(p, r, 1.0f);
+  union { uint32_t u; float f; } two_k;
+  two_k.u = (uint32_t)((int)kf + 127) << 23; /* k in [-126, 0] */
+  return ULB_FMUL(p, two_k.f);
 }
 
 /* ---------------------------------------------------------------- binary16 */

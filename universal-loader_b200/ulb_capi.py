@@ -59,6 +59,10 @@ _SIGS = {
     "ulb_event_record": (C.c_int, [P, P]),
     "ulb_event_elapsed_ms": (C.c_int, [P, P, C.POINTER(C.c_float)]),
     "ulb_event_destroy": (C.c_int, [P]),
+    "ulb_capture_begin": (C.c_int, [P]),
+    "ulb_capture_end": (C.c_int, [P, C.POINTER(P)]),
+    "ulb_graph_launch": (C.c_int, [P, P]),
+    "ulb_graph_free": (C.c_int, [P]),
     "ulb_tensor_upload": (C.c_int, [P, C.c_int, C.POINTER(C.c_uint64), P, C.c_size_t, C.POINTER(P)]),
     "ulb_tensor_free": (C.c_int, [P]),
     "ulb_tensor_info": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_uint64), C.POINTER(C.c_size_t)]),
@@ -218,6 +222,31 @@ class Context:
 
     def record(self, e):
         check(lib().ulb_event_record(self.h, e))
+
+    def capture(self, fn):
+        """Record the device work of fn() into a CUDA graph (returns the graph handle)."""
+        check(lib().ulb_capture_begin(self.h))
+        try:
+            fn()
+        finally:
+            g = P()
+            rc = lib().ulb_capture_end(self.h, C.byref(g))
+        check(rc)
+        return g
+
+    def time_graph(self, g, reps=10):
+        """Device milliseconds of one replay of g (CUDA events, after one warm replay)."""
+        check(lib().ulb_graph_launch(self.h, g))
+        a, b = self.event(), self.event()
+        self.record(a)
+        for _ in range(reps):
+            check(lib().ulb_graph_launch(self.h, g))
+        self.record(b)
+        self.sync()
+        ms = self.elapsed_ms(a, b) / reps
+        lib().ulb_event_destroy(a)
+        lib().ulb_event_destroy(b)
+        return ms
 
     def elapsed_ms(self, a, b):
         ms = C.c_float()
