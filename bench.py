@@ -35,6 +35,9 @@ TARGET = dict(n_layer=32, d_model=4096, n_head=32, n_head_kv=32, d_ff=11008, n_v
 DRAFT = dict(n_layer=22, d_model=2048, n_head=32, n_head_kv=4, d_ff=5632, n_vocab=32000, rms_eps=1e-5,
              rope_base=1e4, wtype="q4_0", seed=2, ctx_len=2048, name="tinyllama-1.1b-arch-q4_0-s2")
 PROMPT_LEN, K_SPEC, NEW_TOKENS = 512, 5, 256
+# ncu (dram__bytes_read.sum + dram__bytes_write.sum) / algorithmic bytes of one fused Q4_0 GEMV
+# launch (N=11008, K=4096, M=5: 25.44 MB measured vs 25.62 MB algorithmic)
+QGEMV_TRAFFIC_RATIO = 0.993
 WORKLOAD = ("C2: Llama-2-7B-arch Q4_0 target + TinyLlama-1.1B-arch Q4_0 draft, B=1 per GPU, "
             "prompt 512, k=5, 256 new tokens, T=0")
 
@@ -372,7 +375,11 @@ def run_ours(args):
                    "frac": verify_gbs / peak, "peak": peak, "peak_source": peak_src,
                    "frac_of_8tbs": verify_gbs / 8000.0},
         "roofline": {"bound": "hbm", "achieved": rl["achieved_gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": rl["achieved_gbs"] / peak, "traffic": None,
+                     "frac": rl["achieved_gbs"] / peak,
+                     "traffic": rl["bytes_per_layer"] / 4 * QGEMV_TRAFFIC_RATIO,
+                     "traffic_note": "bytes per average launch: algorithmic bytes x %.3f, the DRAM read+write / "
+                                     "algorithmic ratio of an ncu capture of the Q4_0 11008x4096 M=5 launch "
+                                     "(no re-reads)" % QGEMV_TRAFFIC_RATIO,
                      "kernel": "qgemv_q40_kernel<NT=1> (fused Q4_0 dequant-GEMV, 7B verify shapes, M=6)",
                      "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
                      "shapes": rl["shapes"]},

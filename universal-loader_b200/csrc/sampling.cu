@@ -20,6 +20,8 @@
  * target and draft rows of a round in parallel; sample (stats + inverse CDF for the draft
  * tokens); decide (one CTA per sequence: accept test, residual / bonus sampling, commit).
  */
+#include <algorithm>
+
 #include "ulb_internal.h"
 
 namespace ulb {
@@ -48,6 +50,33 @@ __device__ __forceinline__ uint32_t fkey(float f) {
 __device__ __forceinline__ float unkey(uint32_t k) {
   const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
   return __uint_as_float(u);
+}
+
+/* Visit every element of a logits row as f(i, x): 128-bit loads when the row is 16-byte
+   aligned and V % 4 == 0 (each thread walks float4s i = tid, tid + BT, ...), else scalar. */
+template <int BT, typename F>
+__device__ __forceinline__ void row_for_each(const float* __restrict__ l, int V, F f) {
+  if ((((uintptr_t)l) & 15) == 0 && (V & 3) == 0) {
+    const float4* l4 = reinterpret_cast<const float4*>(l);
+    const int V4 = V >> 2;
+    int i = threadIdx.x;
+    for (; i + 3 * BT < V4; i += 4 * BT) { /* four 16-byte loads in flight per thread */
+      float4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = __ldg(l4 + i + u * BT);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int b = 4 * (i + u * BT);
+        f(b, a[u].x); f(b + 1, a[u].y); f(b + 2, a[u].z); f(b + 3, a[u].w);
+      }
+    }
+    for (; i < V4; i += BT) {
+      const float4 a = __ldg(l4 + i);
+      f(4 * i, a.x); f(4 * i + 1, a.y); f(4 * i + 2, a.z); f(4 * i + 3, a.w);
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += BT) f(i, l[i]);
+  }
 }
 
 template <int BT>
@@ -95,10 +124,9 @@ template <int BT>
 __device__ int block_argmax(const float* l, int V, SmemRed<BT>& s) {
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += BT) {
-    const float x = l[i];
+  row_for_each<BT>(l, V, [&](int i, float x) {
     if (x > bv || (x == bv && i < bi)) { bv = x; bi = i; }
-  }
+  });
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -122,10 +150,10 @@ __device__ uint32_t kth_largest_key(const float* l, int V, float iT, int k, Smem
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int b = threadIdx.x; b < 256; b += BT) s.hist_u[b] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < V; i += BT) {
-      const uint32_t key = fkey(zof(l[i], iT));
+    row_for_each<BT>(l, V, [&](int, float x) {
+      const uint32_t key = fkey(zof(x, iT));
       if ((key & mask) == prefix) atomicAdd(&s.hist_u[(key >> shift) & 255u], 1u);
-    }
+    });
     __syncthreads();
     if (threadIdx.x == 0) {
       int cum = 0, b = 255;
@@ -156,12 +184,12 @@ __device__ uint32_t topp_key(const float* l, int V, float iT, float mx, uint32_t
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int b = threadIdx.x; b < 256; b += BT) s.hist_d[b] = 0.0;
     __syncthreads();
-    for (int i = threadIdx.x; i < V; i += BT) {
-      const float z = zof(l[i], iT);
+    row_for_each<BT>(l, V, [&](int, float x) {
+      const float z = zof(x, iT);
       const uint32_t key = fkey(z);
       if (key >= key_lo && (key & mask) == prefix)
         atomicAdd(&s.hist_d[(key >> shift) & 255u], (double)ulb_warp_exp(__fsub_rn(z, mx)));
-    }
+    });
     __syncthreads();
     if (threadIdx.x == 0) {
       int b = 255, last_nonempty = -1;
@@ -202,18 +230,18 @@ __device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowS
   if (w.top_k > 0 && w.top_k < V) key_lo = kth_largest_key(l, V, iT, w.top_k, s);
   if (w.top_p > 0.f && w.top_p < 1.f) {
     double zs = 0.0;
-    for (int i = threadIdx.x; i < V; i += BT) {
-      const float z = zof(l[i], iT);
+    row_for_each<BT>(l, V, [&](int, float x) {
+      const float z = zof(x, iT);
       if (fkey(z) >= key_lo) zs += (double)ulb_warp_exp(__fsub_rn(z, mx));
-    }
+    });
     const double Z0 = block_sum_d(zs, s);
     key_lo = topp_key(l, V, iT, mx, key_lo, (double)w.top_p * Z0, s);
   }
   double zs = 0.0;
-  for (int i = threadIdx.x; i < V; i += BT) {
-    const float z = zof(l[i], iT);
+  row_for_each<BT>(l, V, [&](int, float x) {
+    const float z = zof(x, iT);
     if (fkey(z) >= key_lo) zs += (double)ulb_warp_exp(__fsub_rn(z, mx));
-  }
+  });
   const double Z = block_sum_d(zs, s);
   if (threadIdx.x == 0) {
     out.mx = mx;
@@ -323,12 +351,16 @@ __global__ void __launch_bounds__(ST) stats_kernel(const float* __restrict__ p, 
   __shared__ RowStats st;
   pdl_wait();
   pdl_trigger();
-  const int row = blockIdx.x;
-  const int np = B * (k + 1);
-  const float* l = row < np ? p + (size_t)row * V : q + (size_t)(row - np) * V;
-  compute_row_stats(l, V, w, st, s);
-  __syncthreads();
-  if (threadIdx.x == 0) out[row] = st;
+  /* persistent: few rows in flight per SM, so a row read by the max pass is still in L2
+     when the sum pass reads it again */
+  const int np = B * (k + 1), rows = np + B * k;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* l = row < np ? p + (size_t)row * V : q + (size_t)(row - np) * V;
+    compute_row_stats(l, V, w, st, s);
+    __syncthreads();
+    if (threadIdx.x == 0) out[row] = st;
+    __syncthreads();
+  }
 }
 
 struct SpecCommit {
@@ -463,7 +495,10 @@ int launch_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* dr
   if (B == 0) return ULB_OK;
   RowStats* rs = (RowStats*)stats_scratch;
   const int rows = B * (k + 1) + B * k;
-  cudaError_t e = launch_k(c, stats_kernel, dim3(rows), dim3(ST), 0, p, q, B, k, V, *w, rs);
+  /* rows in flight (one per CTA): as many as keep ~60 MB of rows in L2, between 1 and 3 per SM */
+  const int fit = (int)std::min<long long>(3LL * c->n_sm, std::max<long long>(c->n_sm, 60000000LL / ((long long)V * 4)));
+  const int grid = std::min(rows, fit);
+  cudaError_t e = launch_k(c, stats_kernel, dim3(grid), dim3(ST), 0, p, q, B, k, V, *w, rs);
   if (e != cudaSuccess) return cuda_error(e, "stats launch", __FILE__, __LINE__);
   SpecCommit cm = {};
   if (commit) cm = *(const SpecCommit*)commit;
