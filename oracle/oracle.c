@@ -804,7 +804,8 @@ static double top2_margin(const float* l, int V) {
  */
 int orc_spec_generate(orc_model* tg, orc_model* dr, int S, const int32_t* prompts, const int32_t* plen,
                       int max_prompt, int max_new, int k, const orc_warp* w, uint64_t seed,
-                      int32_t* out_tokens, int32_t* out_counts, uint64_t stats[4], double* margin_min) {
+                      int32_t* out_tokens, int32_t* out_counts, uint64_t stats[4], double* margin_min,
+                      double* tok_margin) {
   if (!dr) k = 0;
   int V = tg->d.n_vocab;
   /* finished sequences keep being computed (not committed) until every sequence is done */
@@ -832,7 +833,7 @@ int orc_spec_generate(orc_model* tg, orc_model* dr, int S, const int32_t* prompt
     for (int i = 0; i < P; ++i) { hist[(size_t)s * hist_len + i] = prompts[(size_t)s * max_prompt + i]; tok[i] = prompts[(size_t)s * max_prompt + i]; seqv[i] = s; posv[i] = i; }
     orc_forward(tg, kvt, P, P, tok, seqv, posv, 1, lg, V);
     if (dr) orc_forward(dr, kvd, P, P, tok, seqv, posv, 1, qlg, V);
-    if (greedy) { double mg = top2_margin(lg, V); if (mg < mmin) mmin = mg; }
+    if (greedy) { double mg = top2_margin(lg, V); if (mg < mmin) mmin = mg; if (tok_margin) tok_margin[(size_t)s * max_new] = mg; }
     int t0 = orc_sample(lg, V, w, orc_uniform(seed, 0, (uint32_t)s, 0, 4));
     hist[(size_t)s * hist_len + P] = t0;
     L[s] = P + 1;
@@ -878,6 +879,12 @@ int orc_spec_generate(orc_model* tg, orc_model* dr, int S, const int32_t* prompt
       if (done[s]) continue;
       int n = on[s];
       for (int i = 0; i <= n; ++i) hist[(size_t)s * hist_len + L[s] + i] = otok[s * (k + 1) + i];
+      /* committed token i was decided by verify row i of this sequence */
+      if (greedy && tok_margin)
+        for (int i = 0; i <= n; ++i) {
+          int idx = L[s] - plen[s] + i;
+          if (idx < max_new) tok_margin[(size_t)s * max_new + idx] = top2_margin(lg + (size_t)(s * R + i) * V, V);
+        }
       L[s] += n + 1;
       stats[1] += (uint64_t)k; stats[2] += (uint64_t)n; stats[3] += (uint64_t)(n + 1);
       if (L[s] - plen[s] >= max_new) done[s] = 1;

@@ -101,7 +101,8 @@ int orc_spec_accept(const float* p_logits, const float* q_logits, const int32_t*
 int orc_spec_generate(orc_model* target, orc_model* draft, int n_seq, const int32_t* prompts,
                       const int32_t* prompt_lens, int max_prompt, int max_new, int k,
                       const orc_warp* w, uint64_t seed, int32_t* out_tokens, int32_t* out_counts,
-                      uint64_t stats[4], double* top2_margin_min);
+                      uint64_t stats[4], double* top2_margin_min,
+                      double* token_margins /* [n_seq][max_new] or NULL: top-2 margin deciding each token (greedy) */);
 
 /* CPU-baseline sample: `rounds` rounds at context ctx_len with pre-filled caches */
 int orc_bench_rounds(orc_model* target, orc_model* draft, int ctx_len, int k, int rounds,

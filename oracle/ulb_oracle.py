@@ -63,7 +63,7 @@ def lib():
                                       C.c_uint64, C.c_uint32, P, P]
         L.orc_spec_generate.argtypes = [P, P, C.c_int, P, P, C.c_int, C.c_int, C.c_int,
                                         C.POINTER(Warp), C.c_uint64, P, P, P,
-                                        C.POINTER(C.c_double)]
+                                        C.POINTER(C.c_double), P]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_bench_rounds.argtypes = [P, P, C.c_int, C.c_int, C.c_int, C.POINTER(Warp), C.c_uint64, P]
         _lib = L
@@ -238,8 +238,9 @@ def bench_rounds(target: Model, draft, ctx_len, k, rounds, warp, seed=0, threads
     return n, stats
 
 
-def spec_generate(target: Model, draft, prompts, max_new, k, warp, seed, threads=0):
-    """Returns (tokens [S][max_new], counts [S], stats[4], min top-2 margin (greedy))."""
+def spec_generate(target: Model, draft, prompts, max_new, k, warp, seed, threads=0, with_margins=False):
+    """Returns (tokens [S][max_new], counts [S], stats[4], min top-2 margin (greedy)), plus,
+    with_margins, the top-2 logit margin that decided each committed token [S][max_new]."""
     prompts = [np.asarray(p, np.int32) for p in prompts]
     S = len(prompts)
     P = max(p.size for p in prompts)
@@ -254,8 +255,11 @@ def spec_generate(target: Model, draft, prompts, max_new, k, warp, seed, threads
     if threads:
         lib().orc_set_threads(threads)
     w = Warp(*warp)
+    tm = np.full((S, max_new), np.inf)
     rc = lib().orc_spec_generate(target.h, draft.h if draft is not None else None, S, _p(pr),
                                  _p(plen), P, max_new, k, C.byref(w), seed, _p(out), _p(cnt),
-                                 _p(stats), C.byref(margin))
+                                 _p(stats), C.byref(margin), _p(tm))
     assert rc == 0, rc
+    if with_margins:
+        return out, cnt, stats, margin.value, tm
     return out, cnt, stats, margin.value

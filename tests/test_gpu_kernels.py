@@ -31,6 +31,9 @@ def _q4k(rng, N, K):
     return b.reshape(N, -1)
 
 
+TC_MIN_ROWS = 128  # rows from which ulb_qgemm runs the tensor-core GEMM
+
+
 def _rel(a, b):
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
@@ -55,7 +58,7 @@ def test_dequant_bit_exact(ctx, qt, N, K):
 
 
 @pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
-@pytest.mark.parametrize("M", [1, 2, 5, 8, 13, 16, 33, 64, 70])
+@pytest.mark.parametrize("M", [1, 2, 5, 8, 13, 16, 33, 64, 70, 100, 200, 576])
 def test_qgemm_matches_oracle_small(ctx, qt, M):
     rng = np.random.default_rng(100 + M)
     N, K = 208, 1024
@@ -73,7 +76,7 @@ def test_qgemm_matches_oracle_small(ctx, qt, M):
 
 @pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
 @pytest.mark.parametrize("NK", [(4096, 4096), (11008, 4096), (4096, 11008)])
-@pytest.mark.parametrize("M", [1, 5, 8, 16, 64, 256])
+@pytest.mark.parametrize("M", [1, 5, 8, 16, 64, 256, 576])
 def test_qgemm_op_sweep(ctx, qt, NK, M):
     """Config-3 op sweep shapes: every (N, K) x M, Q4_0 and Q4_K, x ~ fp16 N(0,1)."""
     N, K = NK
@@ -84,15 +87,22 @@ def test_qgemm_op_sweep(ctx, qt, NK, M):
     h = ctx.upload_tensor(t, (K, N), raw)
     try:
         y = ctx.qgemm(h, x, N)
-        y_last = ctx.qgemm(h, x[M - 1:M], N)[0]
+        # the same last row computed in a smaller batch of the same regime: M < 128 runs the
+        # mma.sync GEMV, M >= 128 the tcgen05 GEMM (K is never split)
+        y_last = ctx.qgemm(h, x[M - 1:M], N)[0] if M < TC_MIN_ROWS else ctx.qgemm(h, x[M - TC_MIN_ROWS:M], N)[-1]
+        y_gemv = ctx.qgemm(h, x[M - 1:M], N)[0]
     finally:
         ctx.free_tensor(h)
     rows = min(M, 8)  # the oracle checks a subset of rows at the large shapes
     ref = orc.qgemv(t, raw, N, K, x[:rows])
     assert _rel(y[:rows], ref) < GEMM_RTOL
     assert _rel(y[:rows], ref) < 1e-4
-    # every row is computed with the same arithmetic whatever M is
+    # within a regime every row is computed with the same arithmetic whatever M is
     assert np.array_equal(y_last, y[M - 1])
+    # across regimes (tensor-core GEMM vs GEMV) rows agree to fp32 accumulation order: the GEMM
+    # chains K/16 fp32 tensor-core accumulations over the whole row (a Q4_K weight d*sc*q - dmin*m
+    # is also rounded once to fp32 there); the GEMV sums scaled 32-weight blocks
+    assert _rel(y[M - 1], y_gemv) < 1e-4
 
 
 def test_qgemm_rows_independent_of_batch(ctx):

@@ -20,7 +20,7 @@ INCLUDE = os.path.join(ROOT, "include")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 CUDA_HOME = os.path.dirname(os.path.dirname(NVCC))
 
-CU_SOURCES = ["runtime.cu", "qgemv.cu", "attention.cu", "sampling.cu", "model.cu", "spec.cu"]
+CU_SOURCES = ["runtime.cu", "qgemv.cu", "qgemm_tc.cu", "attention.cu", "sampling.cu", "model.cu", "spec.cu"]
 CUDA_LIB = os.path.join(PKG, "libulb_cuda.so")
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",

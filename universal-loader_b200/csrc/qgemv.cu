@@ -25,7 +25,7 @@
  * The tensor pipe is idle in this regime (<= 3.6 flop/B at M = 1); mma.sync is used as the
  * cheapest-to-issue dot product engine.  The reduction order of a row never depends on M.
  */
-#include "ulb_internal.h"
+#include "epilogue.cuh"
 
 namespace ulb {
 
@@ -159,80 +159,13 @@ __device__ __forceinline__ void q4k_sm(uint32_t w0, uint32_t w1, uint32_t w2, fl
 }
 
 /* ------------------------------------------------------------------ epilogues */
+/* lane (g, t) holds, for n-tile nt, rows (g, g + 8) of tokens nt*8 + 2t and + 1 */
 template <int EPI>
 __device__ __forceinline__ void epilogue(const EpiArgs& e, int strip, int nt, int g, int t, int M,
                                          int N, const float4& v) {
-  const int tok0 = nt * 8 + 2 * t, tok1 = tok0 + 1;
-  if (EPI == EPI_STORE || EPI == EPI_RESID) {
-    const int r0 = strip * 16 + g, r1 = r0 + 8;
-    float vals[4] = {v.x, v.y, v.z, v.w};
-    int rows[4] = {r0, r0, r1, r1}, toks[4] = {tok0, tok1, tok0, tok1};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (toks[i] < M && rows[i] < N) {
-        float* p = e.y + (size_t)toks[i] * e.ldy + rows[i];
-        if (EPI == EPI_RESID) *p = *p + vals[i];
-        else *p = vals[i];
-      }
-    }
-  } else if (EPI == EPI_SWIGLU) {
-    const int f = strip * 8 + g;
-    if (tok0 < M) {
-      float gt = v.x, up = v.z;
-      float sg = gt / (1.0f + expf(-gt));
-      e.h[(size_t)tok0 * e.ldh + f] = __float2half_rn(__fmul_rn(sg, up));
-    }
-    if (tok1 < M) {
-      float gt = v.y, up = v.w;
-      float sg = gt / (1.0f + expf(-gt));
-      e.h[(size_t)tok1 * e.ldh + f] = __float2half_rn(__fmul_rn(sg, up));
-    }
-  } else if (EPI == EPI_QKV) {
-    const int f0 = strip * 16;
-    const int toks[2] = {tok0, tok1};
-    if (f0 < e.nq + e.nkv) {
-      /* RoPE-permuted strip: row g = feature f0 + 2g, row g + 8 = feature f0 + 2g + 1 */
-      const int f = f0 + 2 * g;
-      const int pair = (f % e.hd) >> 1;
-      const float ev[2] = {v.x, v.y}, od[2] = {v.z, v.w};
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int tok = toks[i];
-        if (tok >= M) continue;
-        const int pos = e.row_pos[tok];
-        const int seq = e.row_seq[tok];
-        if ((unsigned)pos >= (unsigned)e.cap || (unsigned)seq >= (unsigned)e.n_seq) continue; /* never write outside the cache */
-        const float2 cs = e.rope[(size_t)pos * (e.hd >> 1) + pair];
-        const float x0 = ev[i], x1 = od[i];
-        const float y0 = __fmaf_rn(x0, cs.x, -__fmul_rn(x1, cs.y));
-        const float y1 = __fmaf_rn(x0, cs.y, __fmul_rn(x1, cs.x));
-        if (f < e.nq) {
-          float* q = e.q + (size_t)tok * e.ldq + f;
-          q[0] = y0;
-          q[1] = y1;
-        } else {
-          const int fk = f - e.nq, kvh = fk / e.hd, d = fk % e.hd;
-          __half2* kp = reinterpret_cast<__half2*>(
-              e.kc + (((size_t)seq * e.n_head_kv + kvh) * e.cap + pos) * e.hd + d);
-          *kp = __halves2half2(__float2half_rn(y0), __float2half_rn(y1));
-        }
-      }
-    } else {
-      /* V strip, identity rows */
-      const float vals[4] = {v.x, v.y, v.z, v.w};
-      const int rows[4] = {g, g, g + 8, g + 8};
-      const int tk[4] = {tok0, tok1, tok0, tok1};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (tk[i] >= M) continue;
-        const int fv = f0 + rows[i] - e.nq - e.nkv;
-        const int kvh = fv / e.hd, d = fv % e.hd;
-        const int seq = e.row_seq[tk[i]], pos = e.row_pos[tk[i]];
-        if ((unsigned)pos >= (unsigned)e.cap || (unsigned)seq >= (unsigned)e.n_seq) continue;
-        e.vc[(((size_t)seq * e.n_head_kv + kvh) * e.cap + pos) * e.hd + d] = __float2half_rn(vals[i]);
-      }
-    }
-  }
+  const int tok0 = nt * 8 + 2 * t;
+  epilogue_token<EPI>(e, strip, g, tok0, M, N, v.x, v.z);
+  epilogue_token<EPI>(e, strip, g, tok0 + 1, M, N, v.y, v.w);
 }
 
 constexpr int kWarps = 8;
@@ -745,6 +678,8 @@ int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int e
   ULB_CHECK(M >= 0 && ldx % 8 == 0 && ldx >= w->K, ULB_EINVAL, "qgemv: bad M=%d / ldx=%d (K=%d)", M, ldx, w->K);
   ULB_CHECK(((uintptr_t)x & 15) == 0, ULB_EINVAL, "qgemv: activations must be 16-byte aligned");
   if (M == 0) return ULB_OK;
+  /* dense enough for the tensor cores: one tcgen05 GEMM instead of 32-row GEMV launches */
+  if (M >= kTcMinRows && w->K % 64 == 0) return launch_qgemm_tc(c, w, x, M, ldx, epi, a0);
   const int step = max_rows_per_launch(w->type);
   for (int m0 = 0; m0 < M; m0 += step) {
     const int mc = M - m0 < step ? M - m0 : step;

@@ -6,6 +6,7 @@
  * round trip of ComputeDispatcher (src/vulkan_backend/compute.cpp:29-121), which on this
  * path becomes a kernel launch on the context's stream with no host synchronisation.
  */
+#include <algorithm>
 #include <cstring>
 #include <memory>
 #include <mutex>

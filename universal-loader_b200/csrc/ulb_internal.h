@@ -107,6 +107,10 @@ struct EpiArgs {
 };
 
 int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a);
+/* tensor-core dequant-GEMM (M >= kTcMinRows); launch_qgemv routes there */
+constexpr int kTcMinRows = 128;
+int launch_qgemm_tc(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a);
+
 int launch_dequant(Ctx* c, const Tensor* w, float* out);
 
 int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, const __half* k,
