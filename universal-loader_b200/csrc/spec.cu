@@ -91,7 +91,8 @@ __global__ void stage_prefill_kernel(int s, int c0, int n, const int* __restrict
   rpos[i] = c0 + i;
 }
 
-constexpr int kPrefillChunk = 64;
+/* prompt rows per prefill forward: large enough for the tensor-core GEMM (>= 128 rows) */
+constexpr int kPrefillChunk = 256;
 
 }  // namespace
 
