@@ -85,6 +85,12 @@ ULB_API int ulb_event_record(ulb_ctx* ctx, void* event);
 ULB_API int ulb_event_elapsed_ms(void* start, void* end, float* out_ms);
 ULB_API int ulb_event_destroy(void* event);
 
+/* NCCL communicator of the context (one process per GPU; NVLink / NVSwitch inside a node).
+ * ulb_tp_unique_id writes the 128-byte ncclUniqueId on one rank; share it with the others
+ * (any host channel), then every rank calls ulb_tp_init on its own context. */
+ULB_API int ulb_tp_unique_id(void* out_id128);
+ULB_API int ulb_tp_init(ulb_ctx* ctx, int rank, int world, const void* id128);
+
 /* CUDA-graph capture of a fixed sequence of per-op calls on the context's stream, replayed
  * with one launch (replaces re-recording the reference's command buffers per dispatch,
  * src/vulkan_backend/compute.cpp:27-80).  Calls between begin and end are recorded, not
@@ -228,6 +234,19 @@ typedef struct ulb_model_desc {
 } ulb_model_desc;
 
 ULB_API int ulb_model_create(ulb_ctx* ctx, const ulb_model_desc* desc, ulb_model** out);
+/*
+ * Tensor parallelism (config 5).  Call after ulb_model_create and before the first
+ * ulb_model_set_weight, on a context that has joined a communicator (ulb_tp_init): rank r of
+ * `world` keeps heads [r H/world, (r+1) H/world) of Q / K / V and their KV cache, features
+ * [r F/world, ...) of gate / up, and the matching column (K) slices of attn_output and
+ * ffn_down, sliced on the host while the tensors are set; embeddings, norms and output.weight
+ * are replicated.  Every forward then sums the attn_output and ffn_down partial outputs
+ * across the ranks with an fp32 NCCL all-reduce before the residual add, so every rank holds
+ * the same residual stream and logits.  H, n_head_kv and d_ff must divide by `world`, and the
+ * K slices must be whole quantisation blocks.  Replaces the reference's unimplemented
+ * multi-GPU path (InferenceAPI::enable_multi_gpu, src/api/inference_api.cpp).
+ */
+ULB_API int ulb_model_set_tp(ulb_model* m, int rank, int world);
 ULB_API int ulb_model_set_weight(ulb_model* m, const char* gguf_name, int ggml_type,
                          const uint64_t ne[4], const void* gguf_bytes, size_t nbytes);
 /* Check every tensor is present and build the fused device layouts. */

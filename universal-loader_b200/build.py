@@ -64,7 +64,7 @@ def build_cuda(verbose=False):
                 print("== %s\n%s" % (src, out))
     if _newer(CUDA_LIB, objs):
         tmp = CUDA_LIB + ".tmp"
-        _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", tmp] + objs)
+        _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", tmp] + objs + ["-lnccl"])
         os.replace(tmp, CUDA_LIB)
     return CUDA_LIB
 

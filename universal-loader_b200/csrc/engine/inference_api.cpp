@@ -110,6 +110,22 @@ class InferenceAPI {
     config_.seed = 0;
   }
 
+  /* Tensor parallelism (addition; the reference's enable_multi_gpu is a flag with no effect):
+     join an NCCL communicator of `world` processes, one GPU each, before load_model; the
+     target is then split over the ranks and the draft replicated. */
+  bool init_tensor_parallel(int rank, int world, const py::bytes& nccl_id) {
+    std::lock_guard<std::mutex> lk(mu_);
+    const std::string id = nccl_id;
+    if (id.size() != 128) {
+      std::fprintf(stderr, "[InferenceAPI] init_tensor_parallel: the NCCL id must be 128 bytes\n");
+      return false;
+    }
+    if (!engine_) engine_.reset(new ulbe::Engine(0));
+    const bool ok = engine_->ok() && engine_->init_tp(rank, world, id.data());
+    if (!ok) std::fprintf(stderr, "[InferenceAPI] init_tensor_parallel: %s\n", engine_->error().c_str());
+    return ok;
+  }
+
   bool load_model(const std::string& path) { return load(path, false); }
   bool load_draft_model(const std::string& path) { return load(path, true); }
 
@@ -523,6 +539,8 @@ PYBIND11_MODULE(vulkangguf, m) {
            "Register custom shader compiler function")
       /* additions for the speculative path */
       .def("load_draft_model", &InferenceAPI::load_draft_model, "Load the GGUF draft model for speculative decoding")
+      .def("init_tensor_parallel", &InferenceAPI::init_tensor_parallel, py::arg("rank"), py::arg("world"),
+           py::arg("nccl_id"), "Join a tensor-parallel NCCL communicator before load_model (one GPU per process)")
       .def("unload_draft_model", &InferenceAPI::unload_draft_model, "Unload the draft model")
       .def("set_speculation_length", &InferenceAPI::set_speculation_length, "Draft tokens per round (k)")
       .def("set_seed", &InferenceAPI::set_seed, "Seed of the Philox sampler")
@@ -577,6 +595,11 @@ PYBIND11_MODULE(vulkangguf, m) {
       .value("NF4", QuantizationType::NF4);
 
   m.def("get_quantization_type_name", &quantization_type_name, "Get quantization type name");
+  m.def("nccl_unique_id", []() {
+    char id[128];
+    if (ulb_tp_unique_id(id) != 0) throw std::runtime_error(ulb_last_error());
+    return py::bytes(id, sizeof id);
+  }, "A new 128-byte NCCL unique id (create on one rank, share with the others)");
   m.def("write_synthetic_gguf", &write_synthetic, py::arg("path"), py::arg("spec"), py::arg("threads") = 0,
         "Write a synthetic LLaMA GGUF: Q4_0/Q4_K weights N(0, stddev), fp16 embeddings, unit norms");
   m.def("synth_normal", &ulbe::synth_normal, "Sample i of the synthetic N(0,1) stream keyed by (seed, name)");

@@ -45,6 +45,16 @@ void Engine::unload(bool draft) {
   (draft ? dinfo_ : tinfo_) = ModelInfo();
 }
 
+bool Engine::init_tp(int rank, int world, const void* nccl_id128) {
+  std::lock_guard<std::mutex> lk(mu_);
+  if (!ctx_) return fail("no CUDA device: " + err_);
+  if (target_) return fail("init_tp: call before loading the target model");
+  if (world > 1 && ulb_tp_init(ctx_, rank, world, nccl_id128) != ULB_OK) return fail(ulb_last_error());
+  tp_rank_ = rank;
+  tp_world_ = world;
+  return true;
+}
+
 bool Engine::load(const std::string& path, bool draft) {
   std::lock_guard<std::mutex> lk(mu_);
   if (!ctx_) return fail("no CUDA device: " + err_);
@@ -82,6 +92,11 @@ bool Engine::load(const std::string& path, bool draft) {
   d.max_rows = 64;
   ulb_model* m = nullptr;
   if (ulb_model_create(ctx_, &d, &m) != ULB_OK) return fail(ulb_last_error());
+  if (!draft && tp_world_ > 1 && ulb_model_set_tp(m, tp_rank_, tp_world_) != ULB_OK) {
+    std::string msg = ulb_last_error();
+    ulb_model_free(m);
+    return fail(msg);
+  }
   for (const GGUFTensor& t : f.tensors) {
     if (ulb_model_set_weight(m, t.name.c_str(), t.type, t.ne, t.data, t.nbytes) != ULB_OK) {
       std::string msg = ulb_last_error();

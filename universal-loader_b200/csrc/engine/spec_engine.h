@@ -50,6 +50,9 @@ class Engine {
   const std::string& error() const { return err_; }
 
   bool load(const std::string& path, bool draft);
+  /* join a tensor-parallel communicator: later target loads keep this rank's slice (the
+     draft stays replicated) */
+  bool init_tp(int rank, int world, const void* nccl_id128);
   void unload(bool draft);
   bool has_model(bool draft) const { return draft ? draft_ != nullptr : target_ != nullptr; }
   const ModelInfo& info(bool draft) const { return draft ? dinfo_ : tinfo_; }
@@ -68,6 +71,7 @@ class Engine {
   bool fail(const std::string& m);
   void drop_spec();
   ulb_ctx* ctx_ = nullptr;
+  int tp_rank_ = 0, tp_world_ = 1;
   ulb_model* target_ = nullptr;
   ulb_model* draft_ = nullptr;
   ModelInfo tinfo_, dinfo_;

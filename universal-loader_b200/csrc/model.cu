@@ -12,9 +12,11 @@
  * blk.N.ffn_* names, model.cpp:232-245).
  */
 #include <cmath>
+#include <algorithm>
 #include <cstring>
 #include <memory>
 #include <string>
+#include <vector>
 
 #include "ulb_internal.h"
 
@@ -35,7 +37,9 @@ struct Layer {
 
 struct Model {
   Ctx* c = nullptr;
-  ulb_model_desc d{};
+  ulb_model_desc d{};   /* this rank's shapes (heads, d_ff divided by tp_world) */
+  ulb_model_desc gd{};  /* the whole model's shapes */
+  int tp_rank = 0, tp_world = 1;
   int nq = 0, nkv = 0;
   std::map<std::string, RawW> raw;
   bool finalized = false;
@@ -53,6 +57,7 @@ struct Model {
   float* qb = nullptr;
   __half* att = nullptr;
   __half* h16 = nullptr;
+  float* tp_part = nullptr; /* [rows][d] partial attn_output / ffn_down sums (tensor parallel) */
   size_t ws_bytes = 0;
 };
 
@@ -162,6 +167,8 @@ static int ensure_ws(Model* m, int rows) {
   if (rows <= m->ws_rows) return ULB_OK;
   Ctx* c = m->c;
   dev_free(c, m->x, 0); dev_free(c, m->x16, 0); dev_free(c, m->qb, 0); dev_free(c, m->att, 0); dev_free(c, m->h16, 0);
+  dev_free(c, m->tp_part, 0);
+  m->tp_part = nullptr;
   c->bytes_live -= m->ws_bytes;
   m->ws_bytes = 0;
   m->ws_rows = 0;
@@ -175,6 +182,10 @@ static int ensure_ws(Model* m, int rows) {
   ULB_TRY(dev_alloc(c, (void**)&m->att, ba));
   ULB_TRY(dev_alloc(c, (void**)&m->h16, bh));
   m->ws_bytes = bx + bx16 + bq + ba + bh;
+  if (m->tp_world > 1) {
+    ULB_TRY(dev_alloc(c, (void**)&m->tp_part, bx));
+    m->ws_bytes += bx;
+  }
   m->ws_rows = rows;
   return ULB_OK;
 }
@@ -208,6 +219,24 @@ int model_prepare(Model* m, KV* kv, int M, int rps) {
   return ULB_OK;
 }
 
+/* x += part, elementwise (the residual add after a tensor-parallel all-reduce) */
+__global__ void add_inplace_kernel(float* __restrict__ x, const float* __restrict__ part, size_t n) {
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    x[i] = x[i] + part[i];
+}
+
+static int tp_reduce_add(Model* m, int M) {
+  Ctx* c = m->c;
+  const size_t n = (size_t)M * m->d.d_model;
+  ULB_TRY(tp_allreduce_sum(c, m->tp_part, n));
+  const int grid = (int)std::min<size_t>((n + 255) / 256, (size_t)c->n_sm * 4);
+  cudaError_t e = launch_k(c, add_inplace_kernel, dim3(grid), dim3(256), 0, m->x, (const float*)m->tp_part, n);
+  if (e != cudaSuccess) return cuda_error(e, "residual add", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
 int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos, int logits_mode,
                   float* logits, int ld, int* err) {
   Ctx* c = m->c;
@@ -233,12 +262,19 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
                              kv->attn_counters, kv->attn_floats, kv->n_counters));
     EpiArgs r;
     r.y = m->x; r.ldy = d.d_model;
-    ULB_TRY(launch_qgemv(c, &L.o, m->att, M, m->nq, EPI_RESID, r));
+    /* tensor parallel: this rank's heads / features give a partial sum of attn_output and
+       ffn_down; the ranks' partials are summed (NCCL, fp32) before the residual add */
+    EpiArgs pr;
+    pr.y = m->tp_part; pr.ldy = d.d_model;
+    const bool tp = m->tp_world > 1;
+    ULB_TRY(launch_qgemv(c, &L.o, m->att, M, m->nq, tp ? EPI_STORE : EPI_RESID, tp ? pr : r));
+    if (tp) ULB_TRY(tp_reduce_add(m, M));
     ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, L.ffn_norm, M, d.d_model, d.rms_eps, 0, m->x16, d.d_model));
     EpiArgs s;
     s.h = m->h16; s.ldh = d.d_ff;
     ULB_TRY(launch_qgemv(c, &L.gateup, m->x16, M, d.d_model, EPI_SWIGLU, s));
-    ULB_TRY(launch_qgemv(c, &L.down, m->h16, M, d.d_ff, EPI_RESID, r));
+    ULB_TRY(launch_qgemv(c, &L.down, m->h16, M, d.d_ff, tp ? EPI_STORE : EPI_RESID, tp ? pr : r));
+    if (tp) ULB_TRY(tp_reduce_add(m, M));
   }
   const int n_out = logits_mode == 1 ? M / rps : M;
   ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, m->out_norm, n_out, d.d_model, d.rms_eps,
@@ -322,6 +358,58 @@ void free_tensor(Ctx* c, Tensor& t) {
 
 }  // namespace
 
+namespace ulb {
+namespace {
+/* GGUF bytes of one row of ne0 elements */
+size_t gguf_row_bytes(int type, uint64_t ne0) {
+  switch (type) {
+    case ULB_TYPE_F32: return ne0 * 4;
+    case ULB_TYPE_F16: return ne0 * 2;
+    case ULB_TYPE_Q4_0: return ne0 / 32 * 18;
+    case ULB_TYPE_Q4_K: return ne0 / 256 * 144;
+    default: return 0;
+  }
+}
+/* this rank's part of a tensor: rows [r0, r0 + nr) or, with kslice, columns [k0, k0 + nk) of every row */
+int tp_slice(Model* m, const std::string& nm, int type, const uint64_t ne[4], const uint8_t* src,
+             std::vector<uint8_t>* out, uint64_t ne_out[4]) {
+  const ulb_model_desc& l = m->d;
+  const int hd = l.head_dim, r = m->tp_rank;
+  uint64_t rows = 0, kcols = 0;
+  bool ks = false;
+  auto ends = [&](const char* suf) { return nm.size() > strlen(suf) && nm.compare(nm.size() - strlen(suf), strlen(suf), suf) == 0; };
+  if (ends(".attn_q.weight")) rows = (uint64_t)l.n_head * hd;
+  else if (ends(".attn_k.weight") || ends(".attn_v.weight")) rows = (uint64_t)l.n_head_kv * hd;
+  else if (ends(".ffn_gate.weight") || ends(".ffn_up.weight")) rows = (uint64_t)l.d_ff;
+  else if (ends(".attn_output.weight")) { kcols = (uint64_t)l.n_head * hd; ks = true; }
+  else if (ends(".ffn_down.weight")) { kcols = (uint64_t)l.d_ff; ks = true; }
+  else return 1; /* replicated */
+  memcpy(ne_out, ne, 4 * sizeof(uint64_t));
+  const size_t rb = gguf_row_bytes(type, ne[0]);
+  ULB_CHECK(rb > 0, ULB_EUNSUPPORTED, "%s: tensor type %d cannot be sliced", nm.c_str(), type);
+  if (!ks) {
+    ULB_CHECK(ne[1] == rows * m->tp_world, ULB_EFORMAT, "%s: %llu rows, expected %llu", nm.c_str(),
+              (unsigned long long)ne[1], (unsigned long long)(rows * m->tp_world));
+    out->assign(src + (size_t)r * rows * rb, src + (size_t)(r + 1) * rows * rb);
+    ne_out[1] = rows;
+  } else {
+    ULB_CHECK(ne[0] == kcols * m->tp_world, ULB_EFORMAT, "%s: K = %llu, expected %llu", nm.c_str(),
+              (unsigned long long)ne[0], (unsigned long long)(kcols * m->tp_world));
+    const size_t kb = gguf_row_bytes(type, kcols);
+    /* each rank's K slice must be whole packed K-tiles (128 weights for Q4_0, 256 for Q4_K) */
+    ULB_CHECK(kb > 0 && gguf_row_bytes(type, kcols) * m->tp_world == rb && kcols % (uint64_t)tile_k(type) == 0,
+              ULB_EUNSUPPORTED, "%s: a K slice of %llu per rank is not a multiple of the %d-weight tile", nm.c_str(),
+              (unsigned long long)kcols, tile_k(type));
+    out->resize((size_t)ne[1] * kb);
+    for (uint64_t i = 0; i < ne[1]; ++i) memcpy(out->data() + i * kb, src + i * rb + (size_t)r * kb, kb);
+    ne_out[0] = kcols;
+  }
+  return ULB_OK;
+}
+}  // namespace
+
+}  // namespace ulb
+
 extern "C" {
 
 int ulb_model_create(ulb_ctx* ctx, const ulb_model_desc* d, ulb_model** out) {
@@ -336,6 +424,7 @@ int ulb_model_create(ulb_ctx* ctx, const ulb_model_desc* d, ulb_model** out) {
   std::unique_ptr<ulb_model> m(new ulb_model());
   m->m.c = &ctx->c;
   m->m.d = *d;
+  m->m.gd = *d;
   m->m.nq = d->n_head * d->head_dim;
   m->m.nkv = d->n_head_kv * d->head_dim;
   m->m.layers.resize(d->n_layer);
@@ -343,11 +432,53 @@ int ulb_model_create(ulb_ctx* ctx, const ulb_model_desc* d, ulb_model** out) {
   return ULB_OK;
 }
 
-int ulb_model_set_weight(ulb_model* mm, const char* name, int type, const uint64_t ne[4], const void* bytes,
-                         size_t nbytes) {
-  ULB_CHECK(mm && name && ne && bytes, ULB_EINVAL, "ulb_model_set_weight: NULL argument");
+int ulb_model_set_tp(ulb_model* mm, int rank, int world) {
+  ULB_CHECK(mm, ULB_EINVAL, "ulb_model_set_tp: NULL model");
+  Model* m = &mm->m;
+  ULB_CHECK(!m->finalized && m->raw.empty(), ULB_EINVAL, "ulb_model_set_tp: call before the first ulb_model_set_weight");
+  ULB_CHECK(world >= 1 && rank >= 0 && rank < world, ULB_EINVAL, "ulb_model_set_tp: rank %d of %d", rank, world);
+  if (world > 1)
+    ULB_CHECK(m->c->nccl && m->c->tp_rank == rank && m->c->tp_world == world, ULB_EINVAL,
+              "ulb_model_set_tp: the context's communicator (ulb_tp_init) is not rank %d of %d", rank, world);
+  const ulb_model_desc& g = m->gd;
+  ULB_CHECK(g.n_head % world == 0 && g.n_head_kv % world == 0 && g.d_ff % world == 0, ULB_EUNSUPPORTED,
+            "tensor parallel: n_head %d, n_head_kv %d and d_ff %d must divide by %d", g.n_head, g.n_head_kv, g.d_ff,
+            world);
+  ULB_CHECK((g.d_ff / world) % 8 == 0, ULB_EUNSUPPORTED, "tensor parallel: d_ff / world = %d not a multiple of 8",
+            g.d_ff / world);
+  m->tp_rank = rank;
+  m->tp_world = world;
+  m->d = g;
+  m->d.n_head = g.n_head / world;
+  m->d.n_head_kv = g.n_head_kv / world;
+  m->d.d_ff = g.d_ff / world;
+  m->nq = m->d.n_head * m->d.head_dim;
+  m->nkv = m->d.n_head_kv * m->d.head_dim;
+  return ULB_OK;
+}
+
+int ulb_model_set_weight(ulb_model* mm, const char* name, int type, const uint64_t ne_in[4], const void* bytes_in,
+                         size_t nbytes_in) {
+  ULB_CHECK(mm && name && ne_in && bytes_in, ULB_EINVAL, "ulb_model_set_weight: NULL argument");
   Model* m = &mm->m;
   ULB_CHECK(!m->finalized, ULB_EINVAL, "ulb_model_set_weight: model already finalized");
+  const uint64_t* ne = ne_in;
+  const void* bytes = bytes_in;
+  size_t nbytes = nbytes_in;
+  std::vector<uint8_t> part;
+  uint64_t ne_part[4];
+  if (m->tp_world > 1) {
+    const uint64_t n_in = ne_in[0] * ne_in[1] * ne_in[2] * ne_in[3];
+    ULB_CHECK(gguf_row_bytes(type, ne_in[0]) * (n_in / std::max<uint64_t>(ne_in[0], 1)) == nbytes_in, ULB_EFORMAT,
+              "%s: %zu bytes do not match its shape", name, nbytes_in);
+    const int rc = tp_slice(m, name, type, ne_in, (const uint8_t*)bytes_in, &part, ne_part);
+    if (rc < 0) return rc;
+    if (rc == ULB_OK) {
+      ne = ne_part;
+      bytes = part.data();
+      nbytes = part.size();
+    }
+  }
   const uint64_t n = ne[0] * ne[1] * ne[2] * ne[3];
   size_t want = 0;
   switch (type) {

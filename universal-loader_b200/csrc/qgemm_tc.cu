@@ -9,7 +9,7 @@
  * for batched rows.
  *
  * One CTA computes a 128-weight-row x NT-token tile of y = W x^T over the whole of K, fed by
- * TMA (no cluster multicast): one 3-D tensor-map load per packed K-tile brings the 8 strips'
+ * TMA (each copy to this CTA only): one 3-D tensor-map load per packed K-tile brings the 8 strips'
  * raw Q4 bytes, one 2-D load per 64-k stage brings the activation tile already in the
  * 128-byte-swizzled K-major layout; 8 warps dequantise each stage into fp16 hi and lo parts
  * (hi = fp16(w), lo = fp16(w - hi): a Q4_0 weight d (q - 8) has <= 15 significant bits, so
@@ -174,7 +174,7 @@ struct TcArgs {
   int* err;
 };
 
-/* TMA tile loads (no multicast): dst, tensor map, coordinates (innermost first) */
+/* TMA tile loads into this CTA: dst, tensor map, coordinates (innermost first) */
 __device__ __forceinline__ void tma2(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

@@ -13,6 +13,8 @@
 
 #include <new>
 
+#include <nccl.h>
+
 #include "ulb_internal.h"
 
 namespace ulb {
@@ -64,6 +66,13 @@ int check_device_errors(Ctx* c) {
   return ULB_OK;
 }
 
+int tp_allreduce_sum(Ctx* c, float* buf, size_t n) {
+  ULB_CHECK(c->nccl, ULB_EINVAL, "tensor parallelism: the context has no communicator (ulb_tp_init)");
+  const ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, (ncclComm_t)c->nccl, c->stream);
+  ULB_CHECK(r == ncclSuccess, ULB_ENCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
+  return ULB_OK;
+}
+
 }  // namespace ulb
 
 using namespace ulb;
@@ -100,10 +109,37 @@ int ulb_init(int device, ulb_ctx** out) {
   return ULB_OK;
 }
 
+int ulb_tp_unique_id(void* out_id128) {
+  ULB_CHECK(out_id128, ULB_EINVAL, "ulb_tp_unique_id: NULL argument");
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+  ncclUniqueId id;
+  const ncclResult_t r = ncclGetUniqueId(&id);
+  ULB_CHECK(r == ncclSuccess, ULB_ENCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+  memcpy(out_id128, &id, sizeof id);
+  return ULB_OK;
+}
+
+int ulb_tp_init(ulb_ctx* ctx, int rank, int world, const void* id128) {
+  ULB_CHECK(ctx && id128, ULB_EINVAL, "ulb_tp_init: NULL argument");
+  ULB_CHECK(world >= 1 && rank >= 0 && rank < world, ULB_EINVAL, "ulb_tp_init: rank %d of %d", rank, world);
+  ULB_CHECK(!ctx->c.nccl, ULB_EINVAL, "ulb_tp_init: the context already has a communicator");
+  ULB_CUDA(cudaSetDevice(ctx->c.device));
+  ncclUniqueId id;
+  memcpy(&id, id128, sizeof id);
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = ncclCommInitRank(&comm, world, id, rank);
+  ULB_CHECK(r == ncclSuccess, ULB_ENCCL, "ncclCommInitRank(rank %d of %d): %s", rank, world, ncclGetErrorString(r));
+  ctx->c.nccl = comm;
+  ctx->c.tp_rank = rank;
+  ctx->c.tp_world = world;
+  return ULB_OK;
+}
+
 int ulb_destroy(ulb_ctx* ctx) {
   if (!ctx) return ULB_OK;
   cudaSetDevice(ctx->c.device);
   cudaStreamSynchronize(ctx->c.stream);
+  if (ctx->c.nccl) ncclCommDestroy((ncclComm_t)ctx->c.nccl);
   cudaFree(ctx->c.dev_err);
   cudaFree(ctx->c.zero_row);
   cudaStreamDestroy(ctx->c.stream);

@@ -78,7 +78,11 @@ struct Ctx {
   uint64_t launches = 0;               /* kernels launched through launch_k (not graph replays) */
   int* dev_err = nullptr;              /* device error word: bit 1 = a bounded wait gave up */
   void* zero_row = nullptr;            /* kZeroRowHalves fp16 zeros: padding activation rows */
+  void* nccl = nullptr;                /* ncclComm_t of ulb_tp_init (tensor parallelism) */
+  int tp_rank = 0, tp_world = 1;
 };
+/* fp32 sum over the communicator's ranks, in place, on the context stream */
+int tp_allreduce_sum(Ctx* c, float* buf, size_t n);
 constexpr int kZeroRowHalves = 65536 + 64;
 
 /* read and clear the device error word (synchronises the stream) */

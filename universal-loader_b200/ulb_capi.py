@@ -59,6 +59,9 @@ _SIGS = {
     "ulb_event_record": (C.c_int, [P, P]),
     "ulb_event_elapsed_ms": (C.c_int, [P, P, C.POINTER(C.c_float)]),
     "ulb_event_destroy": (C.c_int, [P]),
+    "ulb_tp_unique_id": (C.c_int, [P]),
+    "ulb_tp_init": (C.c_int, [P, C.c_int, C.c_int, P]),
+    "ulb_model_set_tp": (C.c_int, [P, C.c_int, C.c_int]),
     "ulb_capture_begin": (C.c_int, [P]),
     "ulb_capture_end": (C.c_int, [P, C.POINTER(P)]),
     "ulb_graph_launch": (C.c_int, [P, P]),
