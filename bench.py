@@ -409,6 +409,114 @@ def run_ours(args):
     return 0
 
 
+# Llama-2-70B-arch Q4_0 target (N(0, 0.02), seed 0), tensor-parallel over the GPUs with an
+# all-reduce after attn-out and FFN-down; Llama-2-7B-arch Q4_0 draft replicated per GPU; batch 8, 2048-token
+# prompts, k = 6, T = 0
+C5_TARGET = dict(n_layer=80, d_model=8192, n_head=64, n_head_kv=8, d_ff=28672, n_vocab=32000, rms_eps=1e-5,
+                 rope_base=1e4, wtype="q4_0", seed=0, ctx_len=4096, name="llama2-70b-arch-q4_0-s0")
+C5_SEQS, C5_PROMPT, C5_K, C5_NEW = 8, 2048, 6, 256
+C5_WORKLOAD = ("C5: Llama-2-70B-arch Q4_0 target tensor-parallel over the GPUs (all-reduce after attn-out and "
+               "FFN-down) + Llama-2-7B-arch Q4_0 draft replicated per GPU, batch 8, 2048-token prompts, k=6, "
+               "256 new tokens, T=0")
+
+
+def run_c5(args):
+    """Config 5: every rank holds 1/N of the 70B target's heads and FFN features and all of the
+    7B draft; all ranks decode the same 8 sequences in lock step (NCCL all-reduces inside each
+    target forward), so tokens are counted once."""
+    world, rank, local, barrier, allmax, allsum, done = dist_setup()
+    smi_index = gpu_smi_index(local)
+    if world > 1:
+        os.environ["CUDA_VISIBLE_DEVICES"] = str(smi_index)
+    import numpy as np
+    import vulkangguf as vg
+    tp, dp = ensure_models(rank, barrier, C5_TARGET, TARGET)
+    api = vg.InferenceAPI()
+    if world > 1:
+        import torch.distributed as dist
+        box = [vg.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        if not api.init_tensor_parallel(rank, world, box[0]):
+            print("[bench] tensor-parallel init failed", file=sys.stderr)
+            return 1
+    if not api.load_model(tp) or not api.load_draft_model(dp):
+        print("[bench] model load failed", file=sys.stderr)
+        return 1
+    api.enable_speculative_decoding(True)
+    api.set_speculation_length(C5_K)
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, C5_TARGET["n_vocab"], C5_PROMPT).astype(np.int32).tolist() for _ in range(C5_SEQS)]
+    cfg = vg.GenerationConfig()
+    cfg.max_tokens, cfg.temperature, cfg.do_sample, cfg.seed = C5_NEW, 0.0, False, 0
+    for _ in range(args.warmup):
+        api.generate_tokens(prompts, cfg)
+    barrier()
+    clocks = ClockSampler(smi_index)
+    clocks.start()
+    t0 = time.perf_counter()
+    toks = 0
+    dec_ms = pre_ms = 0.0
+    launches = accepted = drafted = rounds = 0
+    h2d = d2h = 0.0
+    outs = []
+    for _ in range(args.steps):
+        out = api.generate_tokens(prompts, cfg)
+        st = api.get_last_stats()
+        outs.append(out)
+        toks += sum(len(o) for o in out)
+        dec_ms += st["decode_ms"]
+        pre_ms += st["prefill_ms"]
+        launches += st["launches"]
+        accepted += st["accepted"]
+        drafted += st["drafted"]
+        rounds += st["rounds"]
+        h2d, d2h = st["h2d_bytes"], st["d2h_bytes"]
+    wall = time.perf_counter() - t0
+    barrier()
+    clk = clocks.stop()
+    prof = api.profile_round()
+    max_dec = allmax(dec_ms)
+    max_wall = allmax(wall)
+    max_step = allmax((dec_ms + pre_ms) / args.steps)
+    tot_launch = allsum(launches)
+    verify_ms = allmax(prof["verify_ms"])
+    if rank != 0:
+        done()
+        return 0
+    peak, peak_src = load_peaks()
+    ctx_len = C5_PROMPT + C5_NEW // 2
+    w_bytes = q4_0_bytes(linear_weights(C5_TARGET))
+    hd = C5_TARGET["d_model"] // C5_TARGET["n_head"]
+    kv_tok = C5_TARGET["n_layer"] * C5_TARGET["n_head_kv"] * hd * 2 * 2
+    # per GPU and verify: the rank's weight slice (the LM head is replicated) + its KV heads
+    lm_head = q4_0_bytes(C5_TARGET["d_model"] * C5_TARGET["n_vocab"])
+    verify_bytes = (w_bytes - lm_head) / world + lm_head + C5_SEQS * ctx_len * kv_tok / world
+    gbs = verify_bytes / (verify_ms / 1e3) / 1e9
+    line = {
+        "metric": "accepted tok/s (Llama-2-70B-arch Q4_0 tensor-parallel, batch 8, k=6)",
+        "value": toks / (max_dec / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": max_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "q4_0xf16->f32", "data": "synthetic",
+        "config": {"workload": C5_WORKLOAD, "parallelism": "tp%d (NCCL all-reduce, fp32 partial sums)" % world,
+                   "l2": "inputs larger than L2 (38.6 GB of target weights)",
+                   "timed": "generation phase, CUDA events, max over ranks; prefill separate"},
+        "acceptance_rate": accepted / drafted if drafted else 0.0,
+        "rounds_per_step": rounds / args.steps,
+        "prefill_ms": pre_ms / args.steps, "decode_ms": dec_ms / args.steps,
+        "round_profile_ms": prof,
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "traffic": None, "kernel": "target verify forward of one round per GPU (weights slice + KV)",
+                     "peak_source": peak_src},
+        "e2e": {"value": toks / max_wall, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "note": "public API generate_tokens, prefill included"},
+        "gpu_launches": int(tot_launch),
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    done()
+    return 0
+
+
 def c4_prompts():
     """The 64 config-4 prompts (lengths U[256, 4096], ids U[0, vocab), seed 1)."""
     import numpy as np
@@ -637,9 +745,10 @@ def main():
     ap.add_argument("--mode", default="spec", choices=["spec", "ops"],
                     help="spec: the C2 speculative workload (default); ops: the config-3 kernel sweep")
     ap.add_argument("--only", default="", help="ops mode: run one case, e.g. q4_0:11008x4096:m5 or accept")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c4"],
+    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"],
                     help="c2: 7B + TinyLlama, B=1 (default, the headline); c4: Llama-3-8B + 3.2-1B, 64 sequences "
-                         "sharded data-parallel over the GPUs")
+                         "sharded data-parallel over the GPUs; c5: 70B target tensor-parallel over the GPUs + "
+                         "replicated 7B draft, batch 8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -648,6 +757,8 @@ def main():
         return run_ops(args)
     if args.workload == "c4":
         return run_c4(args)
+    if args.workload == "c5":
+        return run_c5(args)
     return run_ours(args)
 
 
