@@ -31,7 +31,14 @@ def _q4k(rng, N, K):
     return b.reshape(N, -1)
 
 
-TC_MIN_ROWS = 128  # rows from which ulb_qgemm runs the tensor-core GEMM
+# ulb_qgemm's regimes by row count: the mma.sync GEMV up to 32 rows, the tcgen05 GEMM with
+# 64-token tiles and K split a fixed number of ways per matrix for 33 ... 255 rows, the
+# tcgen05 GEMM without a K split from 256 rows; a row's arithmetic is fixed within a regime
+REGIME_FIRST_ROW = (1, 33, 256)
+
+
+def _regime_first(M):
+    return max(r for r in REGIME_FIRST_ROW if r <= M)
 
 
 def _rel(a, b):
@@ -58,7 +65,7 @@ def test_dequant_bit_exact(ctx, qt, N, K):
 
 
 @pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
-@pytest.mark.parametrize("M", [1, 2, 5, 8, 13, 16, 33, 64, 70, 100, 200, 576])
+@pytest.mark.parametrize("M", [1, 2, 5, 8, 13, 16, 32, 33, 64, 70, 100, 200, 255, 256, 576])
 def test_qgemm_matches_oracle_small(ctx, qt, M):
     rng = np.random.default_rng(100 + M)
     N, K = 208, 1024
@@ -87,9 +94,9 @@ def test_qgemm_op_sweep(ctx, qt, NK, M):
     h = ctx.upload_tensor(t, (K, N), raw)
     try:
         y = ctx.qgemm(h, x, N)
-        # the same last row computed in a smaller batch of the same regime: M < 128 runs the
-        # mma.sync GEMV, M >= 128 the tcgen05 GEMM (K is never split)
-        y_last = ctx.qgemm(h, x[M - 1:M], N)[0] if M < TC_MIN_ROWS else ctx.qgemm(h, x[M - TC_MIN_ROWS:M], N)[-1]
+        # the same last row computed in the smallest batch of the same regime
+        lo = _regime_first(M)
+        y_last = ctx.qgemm(h, x[M - lo:M], N)[-1]
         y_gemv = ctx.qgemm(h, x[M - 1:M], N)[0]
     finally:
         ctx.free_tensor(h)
@@ -103,6 +110,30 @@ def test_qgemm_op_sweep(ctx, qt, NK, M):
     # chains K/16 fp32 tensor-core accumulations over the whole row (a Q4_K weight d*sc*q - dmin*m
     # is also rounded once to fp32 there); the GEMV sums scaled 32-weight blocks
     assert _rel(y[M - 1], y_gemv) < 1e-4
+
+
+@pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
+def test_qgemm_split_regime_in_several_launches(ctx, qt):
+    """250 rows of an 11008 x 4096 matrix: the K-split partial sums of all 64-token tiles do
+    not fit the context workspace at once, so the token tiles go in several launches; every
+    row still matches the oracle and the same row computed in a 33-row batch, bit for bit."""
+    N, K, M = 11008, 4096, 250
+    rng = np.random.default_rng(7)
+    raw = _q40(rng, N, K) if qt == "q4_0" else _q4k(rng, N, K)
+    t = orc.T_Q4_0 if qt == "q4_0" else orc.T_Q4_K
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    h = ctx.upload_tensor(t, (K, N), raw)
+    try:
+        y = ctx.qgemm(h, x, N)
+        y33 = ctx.qgemm(h, x[M - 33:M], N)
+        y_again = ctx.qgemm(h, x, N)
+    finally:
+        ctx.free_tensor(h)
+    pick = [0, 63, 64, 191, 192, 249]  # rows on both sides of the launch boundaries
+    ref = orc.qgemv(t, raw, N, K, x[pick])
+    assert _rel(y[pick], ref) < 1e-4
+    assert np.array_equal(y[M - 33:], y33)
+    assert np.array_equal(y, y_again)
 
 
 def test_qgemm_rows_independent_of_batch(ctx):

@@ -111,6 +111,26 @@ def test_forward_matches_oracle(ctx, tiny_target):
         gm.close()
 
 
+def test_fused_rmsnorm_rows_equal_separate_rmsnorm(ctx, tiny_target):
+    """Up to 8 rows (here d = 512, so <= 16 KB of fp16 activations) the QKV and gate/up GEMVs
+    normalise their input themselves; larger batches run rmsnorm_kernel first.  A row must get
+    the same bits either way: one token decoded alone (fused) equals the same token at the same
+    position as the first row of a 10-row block (separate), on a cache prefilled identically."""
+    gm = GpuModel(ctx, tiny_target)
+    try:
+        kvg = gm.kv(2, 64)
+        pre = _prompt(20, seed=30)
+        for s in (0, 1):
+            gm.forward(kvg, pre, [s] * 20, range(20), 20, logits_mode=1)
+        nxt = _prompt(10, seed=31)
+        alone = gm.forward(kvg, nxt[:1], [0], [20], 1)[0]
+        block = gm.forward(kvg, nxt, [1] * 10, range(20, 30), 10)
+        assert np.array_equal(alone.view(np.uint32), block[0].view(np.uint32))
+        gm.U.lib().ulb_kv_free(kvg)
+    finally:
+        gm.close()
+
+
 def _api(target, draft=None, k=4):
     import vulkangguf as vg
     api = vg.InferenceAPI()

@@ -96,54 +96,16 @@ __global__ void embed_kernel(const void* __restrict__ table, int table_type, int
   }
 }
 
-/* out[s] = fp16((x[row] * r) * g), r = 1 / sqrt(mean(x^2) + eps); row = s*sel + sel-1 if sel */
+/* out[s] = fp16((x[row] * r) * g), r = 1 / sqrt(mean(x^2) + eps); row = s*sel + sel-1 if sel.
+   256 threads (rms_row_256). */
 __global__ void rmsnorm_kernel(const float* __restrict__ x, int ldx, const float* __restrict__ g, int d, float eps,
                                int sel, __half* __restrict__ out, int ldo) {
-  /* the whole row is loaded with independent 128-bit loads before any arithmetic, so the
-     kernel pays one memory latency, not one per element (d <= 8192 with 256 threads) */
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
   const int s = blockIdx.x;
   const int row = sel > 0 ? s * sel + sel - 1 : s;
-  const float4* xv = reinterpret_cast<const float4*>(x + (size_t)row * ldx);
-  const float4* gv = reinterpret_cast<const float4*>(g);
-  const int n4 = d >> 2;
-  float4 v[8], gg[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int j = i * 256 + threadIdx.x;
-    if (j < n4) { v[i] = xv[j]; gg[i] = __ldg(gv + j); }
-  }
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int j = i * 256 + threadIdx.x;
-    if (j < n4) {
-      ss = __fmaf_rn(v[i].x, v[i].x, ss);
-      ss = __fmaf_rn(v[i].y, v[i].y, ss);
-      ss = __fmaf_rn(v[i].z, v[i].z, ss);
-      ss = __fmaf_rn(v[i].w, v[i].w, ss);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
-  __half2* o2 = reinterpret_cast<__half2*>(out + (size_t)s * ldo);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int j = i * 256 + threadIdx.x;
-    if (j < n4) {
-      o2[2 * j] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v[i].x, r), gg[i].x)),
-                                 __float2half_rn(__fmul_rn(__fmul_rn(v[i].y, r), gg[i].y)));
-      o2[2 * j + 1] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v[i].z, r), gg[i].z)),
-                                     __float2half_rn(__fmul_rn(__fmul_rn(v[i].w, r), gg[i].w)));
-    }
-  }
+  rms_row_256(x + (size_t)row * ldx, g, d, eps, out + (size_t)s * ldo, red);
 }
 
 }  // namespace
@@ -252,12 +214,11 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     Layer& L = m->layers[l];
     __half* kc = kv->k + (size_t)l * kv->layer_elems;
     __half* vc = kv->v + (size_t)l * kv->layer_elems;
-    ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, L.attn_norm, M, d.d_model, d.rms_eps, 0, m->x16, d.d_model));
     EpiArgs a;
     a.q = m->qb; a.ldq = m->nq; a.kc = kc; a.vc = vc;
     a.nq = m->nq; a.nkv = m->nkv; a.hd = d.head_dim; a.cap = kv->cap; a.n_head_kv = d.n_head_kv; a.n_seq = kv->n_seq;
     a.row_seq = seq; a.row_pos = pos; a.rope = kv->rope;
-    ULB_TRY(launch_qgemv(c, &L.qkv, m->x16, M, d.d_model, EPI_QKV, a));
+    ULB_TRY(launch_qgemv_rms(c, &L.qkv, m->x, d.d_model, L.attn_norm, d.rms_eps, m->x16, M, EPI_QKV, a));
     ULB_TRY(launch_attention(c, &ad, m->qb, m->nq, kc, vc, seq, pos, M, rps, m->att, kv->attn_scratch,
                              kv->attn_counters, kv->attn_floats, kv->n_counters));
     EpiArgs r;
@@ -269,10 +230,9 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     const bool tp = m->tp_world > 1;
     ULB_TRY(launch_qgemv(c, &L.o, m->att, M, m->nq, tp ? EPI_STORE : EPI_RESID, tp ? pr : r));
     if (tp) ULB_TRY(tp_reduce_add(m, M));
-    ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, L.ffn_norm, M, d.d_model, d.rms_eps, 0, m->x16, d.d_model));
     EpiArgs s;
     s.h = m->h16; s.ldh = d.d_ff;
-    ULB_TRY(launch_qgemv(c, &L.gateup, m->x16, M, d.d_model, EPI_SWIGLU, s));
+    ULB_TRY(launch_qgemv_rms(c, &L.gateup, m->x, d.d_model, L.ffn_norm, d.rms_eps, m->x16, M, EPI_SWIGLU, s));
     ULB_TRY(launch_qgemv(c, &L.down, m->h16, M, d.d_ff, tp ? EPI_STORE : EPI_RESID, tp ? pr : r));
     if (tp) ULB_TRY(tp_reduce_add(m, M));
   }

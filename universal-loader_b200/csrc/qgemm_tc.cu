@@ -16,8 +16,10 @@
  * hi + lo == w exactly) in the same layout; one lane issues tcgen05.mma (M = 128, N = NT,
  * K = 16, fp16 x fp16 -> fp32 in TMEM) twice per k-step (hi, lo) and commits each stage to
  * the mbarriers that free its slots; the 8 warps then read TMEM and run the epilogue.
- * Parallelism comes from the token tile (64 ... 256 tokens, the largest that still gives a CTA
- * per SM), never from splitting K, so a row's summation order does not depend on M.
+ * From kTcWideRows rows on, parallelism comes from the token tile (64 ... 256 tokens, the
+ * largest that still gives a CTA per SM) and K is never split; below that (33 ... 255 rows)
+ * the tile is 64 tokens and K is split S ways, S fixed per matrix (tc_splits), with the
+ * partials added in split order.  Either way a row's summation order does not depend on M.
  * Every mbarrier wait has a deadline (2 s): past it the CTA raises bit 3 of the device error
  * word, stops issuing work and still waits (bounded) for its MMAs before freeing TMEM.
  */
@@ -161,8 +163,8 @@ struct TcCfg {
      raw-weight ring (K-tiles of 2 or 4 stages) the several-microsecond latency of weight
      tiles streamed by every SM at once */
   static constexpr int SA = NT <= 128 ? 3 : 2;
-  static constexpr int SB = NT == 64 ? 4 : 3;
-  static constexpr int RT = QT == ULB_TYPE_Q4_0 ? (NT == 64 || NT == 192 ? 8 : 6) : (NT == 64 || NT == 192 ? 4 : 3);
+  static constexpr int SB = NT == 64 ? 8 : 3;
+  static constexpr int RT = QT == ULB_TYPE_Q4_0 ? (NT == 192 ? 8 : 6) : (NT == 192 ? 4 : 3);
   static constexpr int SMEM = SA * A_BYTES + SB * B_BYTES + RT * RAW_BYTES + 1024; /* + alignment slack */
   static constexpr int TMEM_COLS = NT <= 64 ? 64 : NT <= 128 ? 128 : 256;
   static_assert(SMEM <= 227 * 1024, "shared memory");
@@ -170,7 +172,10 @@ struct TcCfg {
 
 struct TcArgs {
   int tiles, n_strips, N, M;
-  int n_kstages;
+  int splits; /* K splits (grid z): split s covers packed K-tiles [s T / S, (s + 1) T / S) */
+  int tt0;    /* first token tile of this launch */
+  float* ws;  /* splits > 1: partial sums [tile of the launch][split][NT][128] */
+  int* cnt;   /* splits > 1: arrivals per tile of the launch (zero between launches) */
   int* err;
 };
 
@@ -219,11 +224,13 @@ __global__ void __launch_bounds__(TCW * 32, 1)
   uint8_t* const b_ring = smem + SA * C::A_BYTES;
   uint8_t* const raw_ring = b_ring + SB * C::B_BYTES;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int wt = blockIdx.x, tt = blockIdx.y;
+  const int wt = blockIdx.x, tt = a.tt0 + (int)blockIdx.y, split = blockIdx.z;
   const int strip0 = wt * 8;
   const int tok0 = tt * NT;
-  const int nk = a.n_kstages;
-  const int ntiles = nk / SPT;
+  const int kt0 = (int)((long long)split * a.tiles / a.splits);
+  const int ntiles = (int)((long long)(split + 1) * a.tiles / a.splits) - kt0; /* packed K-tiles of this CTA */
+  const int nk = ntiles * SPT;                                                 /* its 64-k stages */
+  const int ks0 = kt0 * SPT;
 
   if (tid == 0) {
     for (int i = 0; i < RT; ++i) { mb_init(&full_raw[i], 1); mb_init(&free_raw[i], 8); }
@@ -253,8 +260,8 @@ __global__ void __launch_bounds__(TCW * 32, 1)
         if (t >= RT && !mb_wait(&free_raw[r], (uint32_t)((t / RT) - 1) & 1u, deadline)) { ok = false; break; }
         uint8_t* raw = raw_ring + r * C::RAW_BYTES;
         mb_expect_tx(&full_raw[r], (uint32_t)C::RAW_BYTES);
-        tma3(raw, &tw, 0, t, strip0, &full_raw[r]);
-        if (QT == ULB_TYPE_Q4_K) tma3(raw + 8 * kTmaBox * 8, &tw, kTmaBox, t, strip0, &full_raw[r]);
+        tma3(raw, &tw, 0, kt0 + t, strip0, &full_raw[r]);
+        if (QT == ULB_TYPE_Q4_K) tma3(raw + 8 * kTmaBox * 8, &tw, kTmaBox, kt0 + t, strip0, &full_raw[r]);
       }
     }
     __syncwarp();
@@ -269,7 +276,7 @@ __global__ void __launch_bounds__(TCW * 32, 1)
         const int b = i % SB;
         if (i >= SB && !mb_wait(&free_b[b], (uint32_t)((i / SB) - 1) & 1u, deadline)) { ok = false; break; }
         mb_expect_tx(&full_b[b], (uint32_t)C::B_BYTES);
-        tma2(b_ring + b * C::B_BYTES, &tx, i * KS, tok0, &full_b[b]);
+        tma2(b_ring + b * C::B_BYTES, &tx, (ks0 + i) * KS, tok0, &full_b[b]);
       }
     }
     __syncwarp();
@@ -376,24 +383,67 @@ __global__ void __launch_bounds__(TCW * 32, 1)
   }
 
   /* ------------------------------------------------ epilogue (warps 2-9): TMEM -> registers ->
-     the fused epilogue; lanes g and g + 8 of a strip meet through a shuffle */
+     the fused epilogue; lanes g and g + 8 of a strip meet through a shuffle.  With K split,
+     every CTA stores its partial tile, and the CTA that arrives last for the tile adds the
+     partials in split order (0, 1, ..., S - 1, whichever CTA that is) and runs the epilogue. */
   bool acc_ok = true;
+  __shared__ int last_arrival;
   if (warp >= 2 && warp <= 9) {
     acc_ok = mb_wait(&acc_full, 0, deadline + 1000000000ull);
     tc_fence_after();
     const int q4 = warp & 3;                        /* TMEM lane quarter this warp may access */
     const int col0 = ((warp - 2) >> 2) * (NT / 2);  /* its half of the token columns */
-    const int n = wt * BM + q4 * 32 + lane;         /* packed row */
-    if (acc_ok && ok) {
-#pragma unroll 1
-      for (int c0 = col0; c0 < col0 + NT / 2; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+    const int row = q4 * 32 + lane;                 /* row of the 128-row tile = TMEM lane */
+    const int n = wt * BM + row;                    /* packed row */
+    auto finish = [&](int c0, const float (&v)[32]) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float v8 = __shfl_down_sync(0xffffffffu, v[c], 8);
-          if ((lane & 15) < 8) epilogue_token<EPI>(ea, n >> 4, lane & 7, tok0 + c0 + c, a.M, a.N, v[c], v8);
+      for (int c = 0; c < 32; ++c) {
+        const float v8 = __shfl_down_sync(0xffffffffu, v[c], 8);
+        if ((lane & 15) < 8) epilogue_token<EPI>(ea, n >> 4, lane & 7, tok0 + c0 + c, a.M, a.N, v[c], v8);
+      }
+    };
+    if (a.splits == 1) {
+      if (acc_ok && ok) {
+#pragma unroll 1
+        for (int c0 = col0; c0 < col0 + NT / 2; c0 += 32) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+          finish(c0, v);
         }
+      }
+    } else {
+      const int tile = (int)(blockIdx.y * gridDim.x + blockIdx.x);
+      float* const wtile = a.ws + (size_t)tile * a.splits * NT * BM;
+      if (acc_ok && ok) {
+        float* const wp = wtile + (size_t)split * NT * BM;
+#pragma unroll 1
+        for (int c0 = col0; c0 < col0 + NT / 2; c0 += 32) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) __stcg(wp + (size_t)(c0 + c) * BM + row, v[c]);
+        }
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (tid == 64) last_arrival = atomicAdd(&a.cnt[tile], 1) == a.splits - 1;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (last_arrival) {
+        __threadfence();
+#pragma unroll 1
+        for (int c0 = col0; c0 < col0 + NT / 2; c0 += 32) {
+          float v[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = __ldcg(wtile + (size_t)(c0 + c) * BM + row);
+#pragma unroll 1
+          for (int sp = 1; sp < a.splits; ++sp) {
+            const float* wp = wtile + (size_t)sp * NT * BM;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) v[c] += __ldcg(wp + (size_t)(c0 + c) * BM + row);
+          }
+          finish(c0, v);
+        }
+        if (tid == 64) a.cnt[tile] = 0; /* ready for the next launch */
       }
     }
   }
@@ -415,6 +465,29 @@ inline int tc_ntile(const Ctx* c, const Tensor* w, int M) {
   for (int i = 0; i < 4; ++i)
     if ((long long)n_wt * ((M + cand[i] - 1) / cand[i]) >= c->n_sm) return cand[i];
   return 64;
+}
+
+/*
+ * K splits for the 64-token tiles of the narrow regime (kGemvMaxRows < M < kTcWideRows): the
+ * count that minimises (waves of weight tiles x splits) x (stages per split + fill), plus a
+ * fixed cost for the partial-sum pass.  It depends on the matrix and the SM count only, never
+ * on M, so every row of the regime is summed in the same order.
+ */
+inline int tc_splits(const Ctx* c, const Tensor* w) {
+  const int n_wt = (w->n_strips + 7) / 8, T = w->tiles;
+  const int spt = (w->type == ULB_TYPE_Q4_0 ? kQ40TileK : kQ4KTileK) / KS;
+  int best_s = 1;
+  long long best = -1;
+  for (int s = 1; s <= std::min(16, T); ++s) {
+    if ((size_t)n_wt * s * 64 * BM > c->tc_ws_floats || (s > 1 && n_wt > kTcCounters)) break;
+    const long long waves = ((long long)n_wt * s + c->n_sm - 1) / c->n_sm;
+    const long long cost = waves * ((long long)((T + s - 1) / s) * spt + 4) + (s > 1 ? 4 : 0);
+    if (best < 0 || cost < best) {
+      best = cost;
+      best_s = s;
+    }
+  }
+  return best_s;
 }
 
 /* cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link) */
@@ -439,7 +512,7 @@ int encode_fn(EncodeTiledFn* out) {
 }
 
 template <int QT, int NT, int EPI>
-int launch_tc3(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& ea) {
+int launch_tc3(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& ea, int splits) {
   using Cf = TcCfg<QT, NT>;
   static bool attr = false;
   if (!attr) {
@@ -472,22 +545,35 @@ int launch_tc3(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const E
   a.n_strips = w->n_strips;
   a.N = w->N;
   a.M = M;
-  a.n_kstages = w->K / KS;
+  a.splits = splits;
+  a.ws = c->tc_ws;
+  a.cnt = c->tc_cnt;
   a.err = c->dev_err;
   const int n_wt = (w->n_strips + 7) / 8, n_tt = (M + NT - 1) / NT;
-  cudaError_t e =
-      launch_k(c, qgemm_tc_kernel<QT, NT, EPI>, dim3(n_wt, n_tt), dim3(TCW * 32), Cf::SMEM, tw, tx, a, ea);
-  if (e != cudaSuccess) return cuda_error(e, "tensor-core GEMM launch", __FILE__, __LINE__);
+  /* with K split, the token tiles go in launches whose partial sums fit the context's workspace */
+  int per = n_tt;
+  if (splits > 1) {
+    per = (int)std::min<size_t>((size_t)n_tt, c->tc_ws_floats / ((size_t)n_wt * splits * NT * BM));
+    per = std::min(per, kTcCounters / n_wt);
+    ULB_CHECK(per >= 1, ULB_EUNSUPPORTED, "qgemm_tc: split workspace too small for %d x %d tiles", n_wt, splits);
+  }
+  for (int tt0 = 0; tt0 < n_tt; tt0 += per) {
+    a.tt0 = tt0;
+    cudaError_t e = launch_k(c, qgemm_tc_kernel<QT, NT, EPI>, dim3(n_wt, std::min(per, n_tt - tt0), splits),
+                             dim3(TCW * 32), Cf::SMEM, tw, tx, a, ea);
+    if (e != cudaSuccess) return cuda_error(e, "tensor-core GEMM launch", __FILE__, __LINE__);
+  }
   return ULB_OK;
 }
 
 template <int QT, int EPI>
 int launch_tc2(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& ea) {
+  if (M < kTcWideRows) return launch_tc3<QT, 64, EPI>(c, w, x, M, ldx, ea, tc_splits(c, w));
   switch (tc_ntile(c, w, M)) {
-    case 64: return launch_tc3<QT, 64, EPI>(c, w, x, M, ldx, ea);
-    case 128: return launch_tc3<QT, 128, EPI>(c, w, x, M, ldx, ea);
-    case 192: return launch_tc3<QT, 192, EPI>(c, w, x, M, ldx, ea);
-    default: return launch_tc3<QT, 256, EPI>(c, w, x, M, ldx, ea);
+    case 64: return launch_tc3<QT, 64, EPI>(c, w, x, M, ldx, ea, 1);
+    case 128: return launch_tc3<QT, 128, EPI>(c, w, x, M, ldx, ea, 1);
+    case 192: return launch_tc3<QT, 192, EPI>(c, w, x, M, ldx, ea, 1);
+    default: return launch_tc3<QT, 256, EPI>(c, w, x, M, ldx, ea, 1);
   }
 }
 

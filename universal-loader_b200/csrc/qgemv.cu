@@ -99,35 +99,15 @@ __device__ __forceinline__ void activation_rows(const __half* __restrict__ x, co
   }
 }
 
-/* One 32-weight block for rows (g, g+8): integer dot products with NT n-tiles of x. */
-template <int BIAS, int NT>
-__device__ __forceinline__ void block_mma(uint32_t vg, uint32_t vg8, const __half* const (&xr)[NT], int kofs,
-                                          float (&s)[NT][4]) {
-  uint32_t a01, a23, a45, a67, b01, b23, b45, b67;
-  nib_pairs<BIAS>(vg, a01, a23, a45, a67);
-  nib_pairs<BIAS>(vg8, b01, b23, b45, b67);
-  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const uint4 bx = __ldg(reinterpret_cast<const uint4*>(xr[nt] + kofs));
-    float tmp[4];
-    mma16816(tmp, a01, b01, a23, b23, bx.x, bx.y, zero);
-    mma16816(s[nt], a45, b45, a67, b67, bx.z, bx.w, tmp);
-  }
-}
-
-/* Column sums of x over one 32-wide block, via MMA with an all-ones A. */
-template <int NT>
-__device__ __forceinline__ void block_colsum(const __half* const (&xr)[NT], int kofs, float (&s)[NT][4]) {
-  const uint32_t ONES = 0x3C003C00u;
-  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const uint4 bx = __ldg(reinterpret_cast<const uint4*>(xr[nt] + kofs));
-    float tmp[4];
-    mma16816(tmp, ONES, ONES, ONES, ONES, bx.x, bx.y, zero);
-    mma16816(s[nt], ONES, ONES, ONES, ONES, bx.z, bx.w, tmp);
-  }
+/*
+ * One 16-byte activation fragment.  XS: x is this CTA's normalised copy in shared memory
+ * (padding rows still point at the global zero row), so the load is generic; otherwise x is
+ * global and read-only for the kernel's lifetime.
+ */
+template <bool XS>
+__device__ __forceinline__ uint4 xld(const __half* p) {
+  if (XS) return *reinterpret_cast<const uint4*>(p);
+  return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
 /* the same column sums from activation fragments already in registers */
@@ -250,7 +230,7 @@ template <int NT> struct TileRegs<ULB_TYPE_Q4_K, NT> {
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
-template <int NT>
+template <bool XS, int NT>
 __device__ __forceinline__ void tile_load(TileRegs<ULB_TYPE_Q4_0, NT>& r, const uint8_t* tp, int tile,
                                           const __half* const (&xr)[NT], int lane, int g) {
   r.w[0] = lds128(tp + lane * 16);
@@ -260,11 +240,11 @@ __device__ __forceinline__ void tile_load(TileRegs<ULB_TYPE_Q4_0, NT>& r, const 
 #pragma unroll
     for (int b = 0; b < 4; ++b)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) r.x[b][nt] = __ldg(reinterpret_cast<const uint4*>(xr[nt] + tile * 128 + b * 32));
+      for (int nt = 0; nt < NT; ++nt) r.x[b][nt] = xld<XS>(xr[nt] + tile * 128 + b * 32);
   }
 }
 
-template <int NT>
+template <bool XS, int NT>
 __device__ __forceinline__ void tile_load(TileRegs<ULB_TYPE_Q4_K, NT>& r, const uint8_t* tp, int, const __half* const (&)[NT],
                                           int lane, int g) {
 #pragma unroll
@@ -288,7 +268,7 @@ __device__ __forceinline__ void block_mma_r(uint32_t vg, uint32_t vg8, const uin
   }
 }
 
-template <int NT>
+template <bool XS, int NT>
 __device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_0, NT>& r, int tile, const __half* const (&xr)[NT],
                                              float (&acc)[NT][4]) {
   const uint32_t words[8] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w, r.w[1].x, r.w[1].y, r.w[1].z, r.w[1].w};
@@ -298,7 +278,7 @@ __device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_0, NT>& 
 #pragma unroll
     for (int b = 0; b < 4; ++b)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) xl[b][nt] = __ldg(reinterpret_cast<const uint4*>(xr[nt] + tile * 128 + b * 32));
+      for (int nt = 0; nt < NT; ++nt) xl[b][nt] = xld<XS>(xr[nt] + tile * 128 + b * 32);
   }
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
@@ -318,7 +298,7 @@ __device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_0, NT>& 
   }
 }
 
-template <int NT>
+template <bool XS, int NT>
 __device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_K, NT>& r, int tile, const __half* const (&xr)[NT],
                                              float (&acc)[NT][4]);
 
@@ -349,10 +329,18 @@ __device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, uint32_t parit
   return true;
 }
 
-template <int QT, int NT, int EPI>
+/* RMSNorm fused into the GEMV (XS): the fp32 rows, the norm weights and eps */
+struct NormIn {
+  const float* x = nullptr;
+  int ldx = 0;
+  const float* g = nullptr;
+  float eps = 0.f;
+};
+
+template <int QT, int NT, int EPI, bool XS>
 __global__ void __launch_bounds__(PQW<NT>::CW * 32, PQW<NT>::MINB)
-    qgemv_kernel(const uint8_t* __restrict__ w, int tiles, int n_strips, int N, const __half* __restrict__ x, int M,
-                 int ldx, EpiArgs ea, int* err, int nb, const __half* __restrict__ xzero) {
+    qgemv_kernel(const uint8_t* __restrict__ w, int tiles, int n_strips, int N, const __half* x, int M,
+                 int ldx, EpiArgs ea, int* err, int nb, const __half* __restrict__ xzero, NormIn nin) {
   constexpr int TB = PQ<QT>::TB, CT = PQ<QT>::CT, NB = PQ<QT>::NB, CW = PQW<NT>::CW;
   constexpr int CB = CT * TB;
   /* tile i of a chunk always accumulates into slot i (of CT), and slots are summed in slot
@@ -387,6 +375,17 @@ __global__ void __launch_bounds__(PQW<NT>::CW * 32, PQW<NT>::MINB)
     for (int q = 0; q < nb && q < total; ++q) issue(q);
   pdl_wait();
   pdl_trigger();
+  if (XS) {
+    /* every CTA normalises the M input rows into its own shared-memory copy, with the
+       arithmetic of rmsnorm_kernel (so the fused and the separate paths give the same bits) */
+    __shared__ float nred[32];
+    __half* xs = reinterpret_cast<__half*>(ring + (size_t)nb * CB + 2 * (size_t)CW * NT * 32 * sizeof(float4));
+    const int K = tiles * (QT == ULB_TYPE_Q4_0 ? kQ40TileK : kQ4KTileK);
+    for (int m = 0; m < M; ++m) rms_row_256(nin.x + (size_t)m * nin.ldx, nin.g, K, nin.eps, xs + (size_t)m * K, nred);
+    __syncthreads();
+    x = xs;
+    ldx = K;
+  }
   const int g = lane >> 2, t = lane & 3;
   const __half* xr[NT];
   activation_rows<NT>(x, xzero, ldx, M, g, t, xr);
@@ -406,12 +405,13 @@ __global__ void __launch_bounds__(PQW<NT>::CW * 32, PQW<NT>::MINB)
         const int t0 = ch * CT, tn = min(tiles - t0, CT);
         /* software pipeline over the warp's tiles warp, warp + CW, ...: load j + 1, compute j */
         TileRegs<QT, NT> tr[2]; /* indexed by j & 1: constant after unrolling, so no copies */
-        if (warp < tn) tile_load<NT>(tr[0], base + warp * TB, t0 + warp, xr, lane, g);
+        if (warp < tn) tile_load<XS, NT>(tr[0], base + warp * TB, t0 + warp, xr, lane, g);
 #pragma unroll
         for (int j = 0; j < NSL; ++j) {
           const int i = warp + j * CW;
-          if (j + 1 < NSL && i + CW < tn) tile_load<NT>(tr[(j + 1) & 1], base + (i + CW) * TB, t0 + i + CW, xr, lane, g);
-          if (i < tn) tile_compute<NT>(tr[j & 1], t0 + i, xr, acc[j]);
+          if (j + 1 < NSL && i + CW < tn)
+            tile_load<XS, NT>(tr[(j + 1) & 1], base + (i + CW) * TB, t0 + i + CW, xr, lane, g);
+          if (i < tn) tile_compute<XS, NT>(tr[j & 1], t0 + i, xr, acc[j]);
         }
       }
       __syncwarp();
@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(PQW<NT>::CW * 32, PQW<NT>::MINB)
 }
 
 /* ------------------------------------------------------------------ Q4_K tile */
-template <int NT>
+template <bool XS, int NT>
 __device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_K, NT>& r, int tile, const __half* const (&xr)[NT],
                                              float (&acc)[NT][4]) {
   {
@@ -484,7 +484,7 @@ __device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_K, NT>& 
       const int kofs = tile * 256 + (J) * 32;                                            \
       uint4 bx[NT];                                                                      \
       _Pragma("unroll") for (int nt = 0; nt < NT; ++nt)                                  \
-        bx[nt] = __ldg(reinterpret_cast<const uint4*>(xr[nt] + kofs));                   \
+        bx[nt] = xld<XS>(xr[nt] + kofs);                                                 \
       block_mma_r<0, NT>(wp[((J) & 1) * 2], wp[((J) & 1) * 2 + 1], bx, s1);              \
       block_colsum_r<NT>(bx, s0);                                                        \
       float scg, mng, scg8, mng8;                                                        \
@@ -630,8 +630,8 @@ __global__ void dequant_q4k_kernel(const uint8_t* __restrict__ w, int tiles, int
   }
 }
 
-template <int QT, int NT, int EPI>
-int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a) {
+template <int QT, int NT, int EPI, bool XS = false>
+int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a, const NormIn& nin = NormIn()) {
   constexpr int TB = PQ<QT>::TB, CT = PQ<QT>::CT, NB = PQ<QT>::NB, CW = PQW<NT>::CW;
   const int nch = (w->tiles + CT - 1) / CT;
   /* ring: as many slots as the CTA has chunks in flight, at most NB */
@@ -641,16 +641,17 @@ int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const Epi
   const int grid = (w->n_strips + per_cta - 1) / per_cta; /* balanced: every CTA gets per_cta or per_cta-1 strips */
   const int slots = min(NB, per_cta * nch);
   const size_t red_bytes = 2 * (size_t)CW * NT * 32 * sizeof(float4); /* two alternating partial buffers */
-  const size_t smem = (size_t)slots * CT * TB + red_bytes;
+  const size_t xs_bytes = XS ? (size_t)kNormSmemBytes : 0; /* normalised x (fused RMSNorm) */
+  const size_t smem = (size_t)slots * CT * TB + red_bytes + xs_bytes;
   static bool attr_set = false;
   if (!attr_set) {
-    ULB_CUDA(cudaFuncSetAttribute(qgemv_kernel<QT, NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)((size_t)NB * CT * TB + red_bytes)));
+    ULB_CUDA(cudaFuncSetAttribute(qgemv_kernel<QT, NT, EPI, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)((size_t)NB * CT * TB + red_bytes + xs_bytes)));
     attr_set = true;
   }
-  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI>, dim3(grid), dim3(CW * 32), smem,
+  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI, XS>, dim3(grid), dim3(CW * 32), smem,
                            (const uint8_t*)w->dev, w->tiles, w->n_strips, w->N, x, M, ldx, a, c->dev_err, slots,
-                           (const __half*)c->zero_row);
+                           (const __half*)c->zero_row, nin);
   if (e != cudaSuccess) return cuda_error(e, "qgemv launch", __FILE__, __LINE__);
   return ULB_OK;
 }
@@ -671,7 +672,7 @@ int launch_epi(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const E
 }  // namespace
 
 /* Max rows per launch (larger M is chunked by the caller of launch_qgemv). */
-static int max_rows_per_launch(int) { return 32; }
+static int max_rows_per_launch(int) { return kGemvMaxRows; }
 
 int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
   ULB_CHECK(w && (w->type == ULB_TYPE_Q4_0 || w->type == ULB_TYPE_Q4_K), ULB_EINVAL, "qgemv: weight is not Q4_0/Q4_K");
@@ -679,7 +680,7 @@ int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int e
   ULB_CHECK(((uintptr_t)x & 15) == 0, ULB_EINVAL, "qgemv: activations must be 16-byte aligned");
   if (M == 0) return ULB_OK;
   /* dense enough for the tensor cores: one tcgen05 GEMM instead of 32-row GEMV launches */
-  if (M >= kTcMinRows && w->K % 64 == 0) return launch_qgemm_tc(c, w, x, M, ldx, epi, a0);
+  if (M > kGemvMaxRows && w->K % 64 == 0) return launch_qgemm_tc(c, w, x, M, ldx, epi, a0);
   const int step = max_rows_per_launch(w->type);
   for (int m0 = 0; m0 < M; m0 += step) {
     const int mc = M - m0 < step ? M - m0 : step;
@@ -701,6 +702,30 @@ int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int e
     if (rc) return rc;
   }
   return ULB_OK;
+}
+
+int launch_qgemv_rms(Ctx* c, const Tensor* w, const float* x32, int ldx32, const float* g, float eps, __half* x16,
+                     int M, int epi, const EpiArgs& a) {
+  ULB_CHECK(w && (w->type == ULB_TYPE_Q4_0 || w->type == ULB_TYPE_Q4_K), ULB_EINVAL, "qgemv: weight is not Q4_0/Q4_K");
+  if (M == 0) return ULB_OK;
+  const bool fuse = M <= 8 && (size_t)M * w->K * sizeof(__half) <= (size_t)kNormSmemBytes && w->K <= 8192 &&
+                    w->K % 8 == 0 && ldx32 % 4 == 0 && ((uintptr_t)x32 & 15) == 0 && ((uintptr_t)g & 15) == 0 &&
+                    (epi == EPI_QKV || epi == EPI_SWIGLU);
+  if (!fuse) {
+    ULB_TRY(launch_rmsnorm_sel(c, x32, ldx32, g, M, w->K, eps, 0, x16, w->K));
+    return launch_qgemv(c, w, x16, M, w->K, epi, a);
+  }
+  NormIn nin;
+  nin.x = x32;
+  nin.ldx = ldx32;
+  nin.g = g;
+  nin.eps = eps;
+  const bool q40 = w->type == ULB_TYPE_Q4_0;
+  if (epi == EPI_QKV)
+    return q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_QKV, true>(c, w, nullptr, M, w->K, a, nin)
+               : launch_q<ULB_TYPE_Q4_K, 1, EPI_QKV, true>(c, w, nullptr, M, w->K, a, nin);
+  return q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_SWIGLU, true>(c, w, nullptr, M, w->K, a, nin)
+             : launch_q<ULB_TYPE_Q4_K, 1, EPI_SWIGLU, true>(c, w, nullptr, M, w->K, a, nin);
 }
 
 int launch_dequant(Ctx* c, const Tensor* w, float* out) {

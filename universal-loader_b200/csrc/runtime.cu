@@ -105,6 +105,10 @@ int ulb_init(int device, ulb_ctx** out) {
   ULB_CUDA(cudaMemset(c->c.dev_err, 0, sizeof(int)));
   ULB_CUDA(cudaMalloc(&c->c.zero_row, kZeroRowHalves * sizeof(__half)));
   ULB_CUDA(cudaMemset(c->c.zero_row, 0, kZeroRowHalves * sizeof(__half)));
+  ULB_CUDA(cudaMalloc((void**)&c->c.tc_ws, kTcWsFloats * sizeof(float)));
+  c->c.tc_ws_floats = kTcWsFloats;
+  ULB_CUDA(cudaMalloc((void**)&c->c.tc_cnt, kTcCounters * sizeof(int)));
+  ULB_CUDA(cudaMemset(c->c.tc_cnt, 0, kTcCounters * sizeof(int)));
   *out = c.release();
   return ULB_OK;
 }
@@ -142,6 +146,8 @@ int ulb_destroy(ulb_ctx* ctx) {
   if (ctx->c.nccl) ncclCommDestroy((ncclComm_t)ctx->c.nccl);
   cudaFree(ctx->c.dev_err);
   cudaFree(ctx->c.zero_row);
+  cudaFree(ctx->c.tc_ws);
+  cudaFree(ctx->c.tc_cnt);
   cudaStreamDestroy(ctx->c.stream);
   delete ctx;
   return ULB_OK;

@@ -79,6 +79,9 @@ struct Ctx {
   int* dev_err = nullptr;              /* device error word: bit 1 = a bounded wait gave up */
   void* zero_row = nullptr;            /* kZeroRowHalves fp16 zeros: padding activation rows */
   void* nccl = nullptr;                /* ncclComm_t of ulb_tp_init (tensor parallelism) */
+  float* tc_ws = nullptr;              /* split-K partial sums of the tensor-core GEMM */
+  size_t tc_ws_floats = 0;
+  int* tc_cnt = nullptr;               /* kTcCounters arrival counters, zero between launches */
   int tp_rank = 0, tp_world = 1;
 };
 /* fp32 sum over the communicator's ranks, in place, on the context stream */
@@ -111,8 +114,24 @@ struct EpiArgs {
 };
 
 int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a);
-/* tensor-core dequant-GEMM (M >= kTcMinRows); launch_qgemv routes there */
-constexpr int kTcMinRows = 128;
+/* y = W . rmsnorm(x32) with the fused epilogue `epi`.  Small batches (M <= 8 rows whose fp16
+   copy fits kNormSmemBytes) normalise inside the GEMV, each CTA into its own shared memory;
+   otherwise rmsnorm_kernel writes x16 [M][K] first.  Both give the same bits. */
+constexpr int kNormSmemBytes = 16384;
+/* out[s] = rmsnorm(x[row]) (row = s*sel + sel - 1 when sel > 0, else s), 256 threads a row */
+int launch_rmsnorm_sel(Ctx* c, const float* x, int ldx, const float* g, int n_out, int d, float eps, int sel,
+                       __half* out, int ldo);
+int launch_qgemv_rms(Ctx* c, const Tensor* w, const float* x32, int ldx32, const float* g, float eps, __half* x16,
+                     int M, int epi, const EpiArgs& a);
+/* GEMM regimes by row count M (a row's summation order is fixed within each):
+     M <= kGemvMaxRows            mma.sync GEMV (qgemv.cu), fixed lane / warp tree
+     kGemvMaxRows < M < kTcWideRows  tcgen05 GEMM, 64-token tiles, K split S(matrix) ways
+     M >= kTcWideRows             tcgen05 GEMM, 64..256-token tiles, K not split
+   launch_qgemv routes M > kGemvMaxRows to launch_qgemm_tc. */
+constexpr int kGemvMaxRows = 32;
+constexpr int kTcWideRows = 256;
+constexpr size_t kTcWsFloats = (size_t)8 << 20; /* 32 MiB of split partial sums per context */
+constexpr int kTcCounters = 4096;
 int launch_qgemm_tc(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a);
 
 int launch_dequant(Ctx* c, const Tensor* w, float* out);
@@ -174,6 +193,58 @@ namespace ulb {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 /* Allow the next kernel in the stream to begin launching its CTAs. */
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+/*
+ * RMSNorm of one row by a block of exactly 256 threads (all of them call it; d % 4 == 0,
+ * d <= 8192): out = fp16((x * r) * g), r = 1 / sqrt(sum(x^2) / d + eps).  The whole row is
+ * loaded with independent 128-bit loads before any arithmetic (one memory latency), and the
+ * sum has one fixed order (per-thread fmaf chains over float4 j = i*256 + tid, a warp xor
+ * tree, the 8 warps in order), so every caller produces the same bits.  `red` is 8 floats
+ * of shared memory; `out` may be global or shared.
+ */
+__device__ __forceinline__ void rms_row_256(const float* __restrict__ x, const float* __restrict__ g, int d, float eps,
+                                            __half* out, float* red) {
+  const float4* xv = reinterpret_cast<const float4*>(x);
+  const float4* gv = reinterpret_cast<const float4*>(g);
+  const int n4 = d >> 2, tid = threadIdx.x;
+  float4 v[8], gg[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = i * 256 + tid;
+    if (j < n4) { v[i] = xv[j]; gg[i] = __ldg(gv + j); }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = i * 256 + tid;
+    if (j < n4) {
+      ss = __fmaf_rn(v[i].x, v[i].x, ss);
+      ss = __fmaf_rn(v[i].y, v[i].y, ss);
+      ss = __fmaf_rn(v[i].z, v[i].z, ss);
+      ss = __fmaf_rn(v[i].w, v[i].w, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) tot += red[w];
+  __syncthreads(); /* red is free for the next row */
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
+  __half2* o2 = reinterpret_cast<__half2*>(out);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = i * 256 + tid;
+    if (j < n4) {
+      o2[2 * j] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v[i].x, r), gg[i].x)),
+                                 __float2half_rn(__fmul_rn(__fmul_rn(v[i].y, r), gg[i].y)));
+      o2[2 * j + 1] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v[i].z, r), gg[i].z)),
+                                     __float2half_rn(__fmul_rn(__fmul_rn(v[i].w, r), gg[i].w)));
+    }
+  }
+}
 }  // namespace ulb
 #endif
 
