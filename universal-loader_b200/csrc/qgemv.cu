@@ -8,36 +8,31 @@
  * shaders (src/shaders/gemm).
  *
  * Design (B200):
- *  - persistent CTAs (2 per SM for M <= 8) walk 16-row strips; a strip is one contiguous
- *    range of packed tiles, streamed global -> shared in ~36 KB chunks by cp.async.bulk
- *    through a 2-slot mbarrier ring; the first chunks are issued before
+ *  - one CTA of 16 warps per SM; the matrix is one stream of 16-row x K-tile tiles in layout
+ *    order, split into equal contiguous ranges per SM and per warp, so every SM streams the
+ *    same bytes to within one tile and every warp one contiguous range;
+ *  - each warp loads its tiles with 128-bit L1-bypassing loads straight into a ring of D
+ *    tiles of registers (~74 KB in flight per SM); the first D tiles are requested before
  *    griddepcontrol.wait, so the weight stream overlaps the previous kernel (programmatic
- *    dependent launch), and the last warp done with a slot refills it (no producer warp,
- *    so 8 warps x 2 CTAs leave 128 registers a thread);
- *  - each warp owns tiles warp, warp + 8, ... of a chunk and loads tile j + 1 (weights
- *    from shared memory, activations from L1) into registers before computing tile j;
+ *    dependent launch), and there are no shared-memory staging, mbarriers or waits;
  *  - nibbles become exact fp16 integers with one LOP3 + one HSUB2/HFMA2 per pair
  *    (0x6400 magic) and feed mma.sync.m16n8k16 (weights = A, activations = B, so M <= 8
  *    tokens fill one n-tile); each 32-weight block's scale is applied in fp32 to that
  *    block's integer dot product, so weights are never rounded;
+ *  - a strip split between warps is summed in a fixed two-level order (warps of a CTA in
+ *    shared memory, then CTAs through global memory), the last arriving warp running the
+ *    epilogue; the split depends on (N, K, SM count) only, so a row's arithmetic never
+ *    depends on M;
  *  - the fused epilogues write RoPE'd Q / K / V (K and V straight into the fp16 KV cache),
  *    SiLU(gate)*up in fp16, or the fp32 residual add.
  * The tensor pipe is idle in this regime (<= 3.6 flop/B at M = 1); mma.sync is used as the
- * cheapest-to-issue dot product engine.  The reduction order of a row never depends on M.
+ * cheapest-to-issue dot product engine.
  */
 #include "epilogue.cuh"
 
 namespace ulb {
 
 namespace {
-
-__device__ __forceinline__ uint4 ld_stream(const void* p) {
-  uint4 r;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-      : "l"(p));
-  return r;
-}
 
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -70,19 +65,33 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
  *   (v & 0x000F000F) | 0x6400_6400 = (1024 + n0, 1024 + n1)
  *   (v & 0x00F000F0) | 0x6400_6400 = (1024 + 16 n2, 1024 + 16 n3) -> x/16 - (64 + bias)
  */
+/* (v & MASK) | m in one LOP3: m comes in a register (two immediates would cost two ops) */
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t and_or(uint32_t v, uint32_t m) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(v), "n"(MASK), "r"(m));
+  return r;
+}
+/* the fp16 magic 0x6400 (1024.0) twice, in a register the compiler cannot fold */
+__device__ __forceinline__ uint32_t magic_1024x2() {
+  uint32_t r;
+  asm("mov.b32 %0, 0x64006400;" : "=r"(r));
+  return r;
+}
+
 template <int BIAS>
 __device__ __forceinline__ void nib_pairs(uint32_t v, uint32_t& p01, uint32_t& p23, uint32_t& p45,
                                           uint32_t& p67) {
-  constexpr uint32_t MAGIC = 0x64006400u;
+  const uint32_t MAGIC = magic_1024x2();
   /* fp16 of 1024 + BIAS and of -(64 + BIAS), duplicated */
   constexpr uint32_t SUB = BIAS == 8 ? 0x64086408u : 0x64006400u;
   constexpr uint32_t NEG = BIAS == 8 ? 0xD480D480u : 0xD400D400u;
   constexpr uint32_t SIXTEENTH = 0x2C002C00u;
   uint32_t v8 = v >> 8;
-  p01 = hsub2u((v & 0x000F000Fu) | MAGIC, SUB);
-  p23 = hfma2u((v & 0x00F000F0u) | MAGIC, SIXTEENTH, NEG);
-  p45 = hsub2u((v8 & 0x000F000Fu) | MAGIC, SUB);
-  p67 = hfma2u((v8 & 0x00F000F0u) | MAGIC, SIXTEENTH, NEG);
+  p01 = hsub2u(and_or<0x000F000Fu>(v, MAGIC), SUB);
+  p23 = hfma2u(and_or<0x00F000F0u>(v, MAGIC), SIXTEENTH, NEG);
+  p45 = hsub2u(and_or<0x000F000Fu>(v8, MAGIC), SUB);
+  p67 = hfma2u(and_or<0x00F000F0u>(v8, MAGIC), SIXTEENTH, NEG);
 }
 
 /*
@@ -110,17 +119,13 @@ __device__ __forceinline__ uint4 xld(const __half* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
-/* the same column sums from activation fragments already in registers */
-template <int NT>
-__device__ __forceinline__ void block_colsum_r(const uint4 (&bx)[NT], float (&s)[NT][4]) {
+/* column sums of one n-tile of activation fragments over a 32-weight block (an all-ones A) */
+__device__ __forceinline__ void block_colsum(const uint4& bx, float (&s)[4]) {
   const uint32_t ONES = 0x3C003C00u;
   const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    float tmp[4];
-    mma16816(tmp, ONES, ONES, ONES, ONES, bx[nt].x, bx[nt].y, zero);
-    mma16816(s[nt], ONES, ONES, ONES, ONES, bx[nt].z, bx[nt].w, tmp);
-  }
+  float tmp[4];
+  mma16816(tmp, ONES, ONES, ONES, ONES, bx.x, bx.y, zero);
+  mma16816(s, ONES, ONES, ONES, ONES, bx.z, bx.w, tmp);
 }
 
 /* Q4_K 6-bit (scale, min) of sub-block J from the 12 packed bytes (3 little-endian words). */
@@ -148,186 +153,180 @@ __device__ __forceinline__ void epilogue(const EpiArgs& e, int strip, int nt, in
   epilogue_token<EPI>(e, strip, g, tok0 + 1, M, N, v.y, v.w);
 }
 
-constexpr int kWarps = 8;
-
-template <int NT>
-__device__ __forceinline__ void reduce_and_finish_prep(float (&acc)[NT][4], float4* red, int warp, int lane) {
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-    red[(warp * NT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-}
-
-/* ------------------------------------------------------------------ staged weight pipeline */
-/*
- * A strip's packed bytes are copied global -> shared with cp.async.bulk in chunks of 27 KB
- * (24 Q4_0 tiles or 12 Q4_K tiles) through a ring of 3 buffers, each guarded by an
- * mbarrier.  The first three chunks are issued before griddepcontrol.wait, so the weight
- * stream of this kernel overlaps the previous kernel in the stream.
- */
-constexpr int kChunkBytes = 27648;
-constexpr int kNBuf = 3;
-constexpr int kMaxChunks = 32;
-template <int QT> struct QTraits;
-template <> struct QTraits<ULB_TYPE_Q4_0> { static constexpr int TB = kQ40TileBytes, CT = 24; };
-template <> struct QTraits<ULB_TYPE_Q4_K> { static constexpr int TB = kQ4KTileBytes, CT = 12; };
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-/* try_wait with a 1 ms suspend hint: a waiting thread sleeps until the phase completes
-   instead of spinning on the issue slots the consumer warps need */
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t gtimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-/* Wait for phase `parity`; gives up after `limit_ns` of wall time (returns false). */
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-  if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = gtimer();
-  while (!mbar_try(bar, parity))
-    if (gtimer() - t0 > limit_ns) return false;
-  return true;
+/* 128-bit weight load: read once, so it neither allocates in L1 (kept for the activations)
+   nor waits for the previous kernel (weights are constant) */
+__device__ __forceinline__ uint4 ldw(const uint8_t* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
 }
 
 /*
- * A tile's operands in registers.  The consumer loop loads tile j + 1 (shared-memory weight
- * words, and for Q4_0 at NT = 1 also the activation fragments from L1) before it computes
- * tile j, so the load latency hides behind a tile of dequant + MMA work.
+ * A tile's weight operands in registers, straight from global memory.
  *   Q4_0: 2 x 16 B of nibble words + 16 B of scales (rows g, g + 8) per lane.
  *   Q4_K: 4 x 16 B of nibble words + the 16 B meta rows of g and g + 8.
  */
-template <int QT, int NT> struct TileRegs;
-template <int NT> struct TileRegs<ULB_TYPE_Q4_0, NT> {
-  static constexpr bool PFX = NT == 1; /* activations prefetched with the weights */
+template <int QT> struct WTile;
+template <> struct WTile<ULB_TYPE_Q4_0> {
+  static constexpr int TB = kQ40TileBytes, TK = kQ40TileK;
   uint4 w[2], sc;
-  uint4 x[PFX ? 4 : 1][NT];
+  __device__ __forceinline__ void load(const uint8_t* tp, int lane, int g) {
+    w[0] = ldw(tp + lane * 16);
+    w[1] = ldw(tp + 512 + lane * 16);
+    sc = ldw(tp + 1024 + g * 16);
+  }
 };
-template <int NT> struct TileRegs<ULB_TYPE_Q4_K, NT> {
-  static constexpr bool PFX = false;
+template <> struct WTile<ULB_TYPE_Q4_K> {
+  static constexpr int TB = kQ4KTileBytes, TK = kQ4KTileK;
   uint4 w[4], mg, mg8;
+  __device__ __forceinline__ void load(const uint8_t* tp, int lane, int g) {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) w[p] = ldw(tp + p * 512 + lane * 16);
+    mg = ldw(tp + 2048 + g * 16);
+    mg8 = ldw(tp + 2048 + (g + 8) * 16);
+  }
 };
 
-__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-
-template <bool XS, int NT>
-__device__ __forceinline__ void tile_load(TileRegs<ULB_TYPE_Q4_0, NT>& r, const uint8_t* tp, int tile,
-                                          const __half* const (&xr)[NT], int lane, int g) {
-  r.w[0] = lds128(tp + lane * 16);
-  r.w[1] = lds128(tp + 512 + lane * 16);
-  r.sc = lds128(tp + 1024 + g * 16);
-  if (TileRegs<ULB_TYPE_Q4_0, NT>::PFX) {
-#pragma unroll
-    for (int b = 0; b < 4; ++b)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) r.x[b][nt] = xld<XS>(xr[nt] + tile * 128 + b * 32);
-  }
+/* the exact fp16 integer weights of one 32-weight block, rows g (w[0..3]) and g + 8 (w[4..7]) */
+template <int BIAS>
+__device__ __forceinline__ void block_weights(uint32_t vg, uint32_t vg8, uint32_t (&w)[8]) {
+  nib_pairs<BIAS>(vg, w[0], w[1], w[2], w[3]);
+  nib_pairs<BIAS>(vg8, w[4], w[5], w[6], w[7]);
 }
-
-template <bool XS, int NT>
-__device__ __forceinline__ void tile_load(TileRegs<ULB_TYPE_Q4_K, NT>& r, const uint8_t* tp, int, const __half* const (&)[NT],
-                                          int lane, int g) {
-#pragma unroll
-  for (int p = 0; p < 4; ++p) r.w[p] = lds128(tp + p * 512 + lane * 16);
-  r.mg = lds128(tp + 2048 + g * 16);
-  r.mg8 = lds128(tp + 2048 + (g + 8) * 16);
-}
-
-/* dot products of one 32-weight block whose activation fragments are already in registers */
-template <int BIAS, int NT>
-__device__ __forceinline__ void block_mma_r(uint32_t vg, uint32_t vg8, const uint4 (&bx)[NT], float (&s)[NT][4]) {
-  uint32_t a01, a23, a45, a67, b01, b23, b45, b67;
-  nib_pairs<BIAS>(vg, a01, a23, a45, a67);
-  nib_pairs<BIAS>(vg8, b01, b23, b45, b67);
+/* integer dot products of one block with one n-tile of activation fragments */
+__device__ __forceinline__ void block_dot(const uint32_t (&w)[8], const uint4& bx, float (&s)[4]) {
   const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    float tmp[4];
-    mma16816(tmp, a01, b01, a23, b23, bx[nt].x, bx[nt].y, zero);
-    mma16816(s[nt], a45, b45, a67, b67, bx[nt].z, bx[nt].w, tmp);
-  }
+  float tmp[4];
+  mma16816(tmp, w[0], w[4], w[1], w[5], bx.x, bx.y, zero);
+  mma16816(s, w[2], w[6], w[3], w[7], bx.z, bx.w, tmp);
 }
 
+constexpr int kGW = 16; /* warps per CTA (one CTA per SM) */
+
+/* GEMV configuration per weight type and n-tile count:
+     W    warps per CTA (one CTA per SM; the split of the weight stream depends on it, so it is
+          the same for every NT of a weight type)
+     D    weight tiles in flight per warp (the register ring) */
+template <int QT, int NT> struct GemvCfg {
+  static constexpr int W = kGW;
+  static constexpr int D = QT == ULB_TYPE_Q4_0 ? (NT == 4 ? 2 : 4) : (NT == 4 ? 1 : 2);
+};
+
+/* one Q4_0 tile: xp[nt] points at the tile's first activation of n-tile nt (this lane's row) */
 template <bool XS, int NT>
-__device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_0, NT>& r, int tile, const __half* const (&xr)[NT],
+__device__ __forceinline__ void tile_compute(const WTile<ULB_TYPE_Q4_0>& r, const __half* const (&xp)[NT],
                                              float (&acc)[NT][4]) {
   const uint32_t words[8] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w, r.w[1].x, r.w[1].y, r.w[1].z, r.w[1].w};
   const uint32_t scw[4] = {r.sc.x, r.sc.y, r.sc.z, r.sc.w};
-  uint4 xl[4][NT];
-  if (!TileRegs<ULB_TYPE_Q4_0, NT>::PFX) { /* all of the tile's activation loads first */
+  /* block b's activation fragments are loaded one block ahead (NT <= 2) or just before use
+     (NT = 4, for the registers) */
+  constexpr int LA = NT <= 2 ? 1 : 0;
+  uint4 xl[2][NT];
+  if (LA) {
 #pragma unroll
-    for (int b = 0; b < 4; ++b)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) xl[b][nt] = xld<XS>(xr[nt] + tile * 128 + b * 32);
+    for (int nt = 0; nt < NT; ++nt) xl[0][nt] = xld<XS>(xp[nt]);
   }
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
-    float s[NT][4];
-    if (TileRegs<ULB_TYPE_Q4_0, NT>::PFX)
-      block_mma_r<8, NT>(words[2 * b], words[2 * b + 1], r.x[TileRegs<ULB_TYPE_Q4_0, NT>::PFX ? b : 0], s);
-    else
-      block_mma_r<8, NT>(words[2 * b], words[2 * b + 1], xl[b], s);
-    const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&scw[b]));
+    if (b + LA < 4) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) xl[(b + LA) & 1][nt] = xld<XS>(xp[nt] + (b + LA) * 32);
+    }
+    uint32_t wq[8];
+    block_weights<8>(words[2 * b], words[2 * b + 1], wq);
+    float2 dd; /* the block scales of rows g and g + 8 */
+    asm("{.reg .b16 l, h; mov.b32 {l, h}, %2; cvt.f32.f16 %0, l; cvt.f32.f16 %1, h;}"
+        : "=f"(dd.x), "=f"(dd.y)
+        : "r"(scw[b]));
+    /* one n-tile at a time: the scaled block sum goes into acc before the next n-tile's MMA */
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      acc[nt][0] = __fmaf_rn(dd.x, s[nt][0], acc[nt][0]);
-      acc[nt][1] = __fmaf_rn(dd.x, s[nt][1], acc[nt][1]);
-      acc[nt][2] = __fmaf_rn(dd.y, s[nt][2], acc[nt][2]);
-      acc[nt][3] = __fmaf_rn(dd.y, s[nt][3], acc[nt][3]);
+      float s[4];
+      block_dot(wq, xl[b & 1][nt], s);
+      acc[nt][0] = __fmaf_rn(dd.x, s[0], acc[nt][0]);
+      acc[nt][1] = __fmaf_rn(dd.x, s[1], acc[nt][1]);
+      acc[nt][2] = __fmaf_rn(dd.y, s[2], acc[nt][2]);
+      acc[nt][3] = __fmaf_rn(dd.y, s[3], acc[nt][3]);
     }
   }
 }
 
 template <bool XS, int NT>
-__device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_K, NT>& r, int tile, const __half* const (&xr)[NT],
-                                             float (&acc)[NT][4]);
+__device__ __forceinline__ void tile_compute(const WTile<ULB_TYPE_Q4_K>& r, const __half* const (&xp)[NT],
+                                             float (&acc)[NT][4]) {
+  const uint4(&nb)[4] = r.w;
+  const uint4 mg = r.mg, mg8 = r.mg8;
+  const float2 dg = __half22float2(*reinterpret_cast<const __half2*>(&mg.x));   /* (d, dmin) row g */
+  const float2 dg8 = __half22float2(*reinterpret_cast<const __half2*>(&mg8.x)); /* row g + 8 */
+  float t1[NT][4], t0[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) t1[nt][i] = t0[nt][i] = 0.f;
+#define ULB_Q4K_SUB(J)                                                                   \
+  {                                                                                      \
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(&nb[(J) >> 1]);              \
+    uint32_t wq[8];                                                                      \
+    block_weights<0>(wp[((J) & 1) * 2], wp[((J) & 1) * 2 + 1], wq);                     \
+    float scg, mng, scg8, mng8;                                                          \
+    q4k_sm<J>(mg.y, mg.z, mg.w, scg, mng);                                               \
+    q4k_sm<J>(mg8.y, mg8.z, mg8.w, scg8, mng8);                                          \
+    _Pragma("unroll") for (int nt = 0; nt < NT; ++nt) {                                  \
+      const uint4 bx = xld<XS>(xp[nt] + (J) * 32);                                       \
+      float s1[4], s0[4];                                                                \
+      block_dot(wq, bx, s1);                                                             \
+      block_colsum(bx, s0);                                                              \
+      t1[nt][0] = __fmaf_rn(scg, s1[0], t1[nt][0]);                                      \
+      t1[nt][1] = __fmaf_rn(scg, s1[1], t1[nt][1]);                                      \
+      t1[nt][2] = __fmaf_rn(scg8, s1[2], t1[nt][2]);                                     \
+      t1[nt][3] = __fmaf_rn(scg8, s1[3], t1[nt][3]);                                     \
+      t0[nt][0] = __fmaf_rn(mng, s0[0], t0[nt][0]);                                      \
+      t0[nt][1] = __fmaf_rn(mng, s0[1], t0[nt][1]);                                      \
+      t0[nt][2] = __fmaf_rn(mng8, s0[2], t0[nt][2]);                                     \
+      t0[nt][3] = __fmaf_rn(mng8, s0[3], t0[nt][3]);                                     \
+    }                                                                                    \
+  }
+  ULB_Q4K_SUB(0) ULB_Q4K_SUB(1) ULB_Q4K_SUB(2) ULB_Q4K_SUB(3)
+  ULB_Q4K_SUB(4) ULB_Q4K_SUB(5) ULB_Q4K_SUB(6) ULB_Q4K_SUB(7)
+#undef ULB_Q4K_SUB
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    acc[nt][0] = __fmaf_rn(-dg.y, t0[nt][0], __fmaf_rn(dg.x, t1[nt][0], acc[nt][0]));
+    acc[nt][1] = __fmaf_rn(-dg.y, t0[nt][1], __fmaf_rn(dg.x, t1[nt][1], acc[nt][1]));
+    acc[nt][2] = __fmaf_rn(-dg8.y, t0[nt][2], __fmaf_rn(dg8.x, t1[nt][2], acc[nt][2]));
+    acc[nt][3] = __fmaf_rn(-dg8.y, t0[nt][3], __fmaf_rn(dg8.x, t1[nt][3], acc[nt][3]));
+  }
+}
 
 /*
- * Persistent, warp-specialised form: one CTA per SM walks strips blockIdx.x, +gridDim.x, ...
- * A producer warp streams the CTA's whole sequence of weight chunks (16 tiles each)
- * through a ring of shared-memory slots with cp.async.bulk (full / empty mbarrier pairs),
- * starting before griddepcontrol.wait; CW consumer warps dequantise + MMA one tile each
- * per chunk and release the slot.  HBM never waits for compute and vice versa.
- * Every wait has a deadline (2 s after kernel start): past it the CTA stops computing,
- * raises bit 1 of *err and runs to completion without writing results.
+ * Split of the weight stream.  The matrix is one stream of T = n_strips * tiles tiles in layout
+ * order (strip-major).  CTA c of G takes tiles [c*T/G, (c+1)*T/G) and warp w of its Wn working
+ * warps an equal contiguous share of those, so every warp streams one contiguous byte range
+ * and every SM gets the same bytes to within one tile.  A strip split between warps is summed
+ * in two levels with one fixed order: the warps of a CTA in warp order (shared memory), then
+ * the CTAs in CTA order (global memory, only for the strips that cross a CTA boundary).  The
+ * split depends on (N, K, G) only, never on M, so a row's arithmetic does not depend on what
+ * else is batched.  All quantities fit 32 bits (T * G < 2^31, checked by the launcher).
  */
-/* a chunk is ~36 KB of one strip; 2 ring slots per CTA; 2 CTAs per SM for NT <= 2 */
-template <int QT> struct PQ;
-template <> struct PQ<ULB_TYPE_Q4_0> { static constexpr int TB = kQ40TileBytes, CT = 32, NB = 2; };
-template <> struct PQ<ULB_TYPE_Q4_K> { static constexpr int TB = kQ4KTileBytes, CT = 16, NB = 2; };
-template <int NT> struct PQW {
-  static constexpr int CW = 8;               /* consumer warps; fixed so reduction order is too */
-  static constexpr int MINB = NT == 1 ? 2 : 1; /* resident CTAs per SM */
+struct Split {
+  uint32_t T;     /* tiles in the matrix */
+  uint32_t G;     /* CTAs */
+  uint32_t Wn;    /* working warps per CTA (<= 16, <= T / G): every working warp has >= 1 tile */
+  uint32_t tiles; /* tiles per strip */
 };
+__device__ __forceinline__ uint32_t cta_begin(const Split& s, uint32_t c) { return c * s.T / s.G; }
+__device__ __forceinline__ uint32_t cta_of(const Split& s, uint32_t i) { return ((i + 1) * s.G - 1) / s.T; }
+/* first tile of warp w of a CTA starting at c0 with tc tiles; the warp holding local tile l */
+__device__ __forceinline__ uint32_t warp_begin(uint32_t c0, uint32_t tc, uint32_t Wn, uint32_t w) {
+  return c0 + w * tc / Wn;
+}
+__device__ __forceinline__ uint32_t warp_in_cta(uint32_t tc, uint32_t Wn, uint32_t l) { return ((l + 1) * Wn - 1) / tc; }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, uint32_t parity, uint64_t deadline) {
-  while (!mbar_try(bar, parity))
-    if (gtimer() > deadline) return false;
-  return true;
-}
+
 
 /* RMSNorm fused into the GEMV (XS): the fp32 rows, the norm weights and eps */
 struct NormIn {
@@ -337,181 +336,208 @@ struct NormIn {
   float eps = 0.f;
 };
 
+/* bytes of the per-warp strip partials in shared memory: W warps x {first, last strip} */
+template <int QT, int NT> constexpr size_t warp_part_bytes() {
+  return (size_t)GemvCfg<QT, NT>::W * 2 * NT * 32 * sizeof(float4);
+}
+
+/*
+ * Warp-streamed fused dequant-GEMV, one CTA of 16 warps per SM.  Each working warp streams its
+ * own contiguous range of tiles with 128-bit loads straight into a ring of D tiles of
+ * registers: the first D tiles (all of a small matrix) are requested before
+ * griddepcontrol.wait, overlapping the previous kernel, and a tile's registers are refilled
+ * with tile j + D as soon as tile j is computed.  No warp ever waits for another.
+ * A strip finished inside one warp goes straight to the epilogue.  A strip split between warps
+ * leaves each warp's partial in shared memory (slot 0: the warp's first strip, 1: its last);
+ * the last of the CTA's warps to count itself in wcnt[first warp] sums them in warp order.
+ * If the strip also crosses a CTA boundary, that CTA sum goes to `part` (two slots per CTA,
+ * same rule) and the last CTA to count itself in cnt[first CTA] sums the CTAs' partials in
+ * CTA order, runs the epilogue and zeroes the counter for the next launch.
+ */
 template <int QT, int NT, int EPI, bool XS>
-__global__ void __launch_bounds__(PQW<NT>::CW * 32, PQW<NT>::MINB)
-    qgemv_kernel(const uint8_t* __restrict__ w, int tiles, int n_strips, int N, const __half* x, int M,
-                 int ldx, EpiArgs ea, int* err, int nb, const __half* __restrict__ xzero, NormIn nin) {
-  constexpr int TB = PQ<QT>::TB, CT = PQ<QT>::CT, NB = PQ<QT>::NB, CW = PQW<NT>::CW;
-  constexpr int CB = CT * TB;
-  /* tile i of a chunk always accumulates into slot i (of CT), and slots are summed in slot
-     order, so a row's arithmetic is the same whatever NT / the number of consumer warps */
-  constexpr int NSL = CT / CW;
-  extern __shared__ __align__(128) uint8_t ring[]; /* nb slots of CB bytes, then the slot sums */
-  float4* red = reinterpret_cast<float4*>(ring + (size_t)nb * CB);
-  __shared__ uint64_t full[NB];
-  __shared__ uint32_t released[NB]; /* warps done with the slot's current chunk */
+__global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
+    qgemv_kernel(const uint8_t* __restrict__ w, Split sp, int N, const __half* x, int M, int ldx, EpiArgs ea,
+                 const __half* __restrict__ xzero, NormIn nin, float4* __restrict__ part, int* __restrict__ cnt,
+                 const uint8_t* __restrict__ pf, uint32_t pf_bytes) {
+  constexpr int TB = WTile<QT>::TB, D = GemvCfg<QT, NT>::D, W = GemvCfg<QT, NT>::W;
+  /* dynamic shared memory: [W][2][NT][32] warp partials | normalised rows (XS) */
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint32_t wcnt[W];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nch = (tiles + CT - 1) / CT;
-  const int my_strips = (n_strips - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-  const int total = my_strips * nch; /* chunks this CTA streams, in order */
-  /* chunk q of the CTA's sequence -> ring slot q % nb */
-  auto issue = [&](int q) {
-    const int s = blockIdx.x + (q / nch) * gridDim.x, ch = q % nch, slot = q % nb;
-    const uint32_t bytes = (uint32_t)min(CT, tiles - ch * CT) * TB;
-    mbar_expect_tx(&full[slot], bytes);
-    bulk_g2s(ring + (size_t)slot * CB, w + ((size_t)s * tiles + (size_t)ch * CT) * TB, bytes, &full[slot]);
-  };
-  if (tid == 0) {
-    for (int i = 0; i < nb; ++i) {
-      mbar_init(&full[i], 1);
-      released[i] = 0;
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t c = blockIdx.x;
+  const uint32_t c0 = cta_begin(sp, c), c1 = cta_begin(sp, c + 1), tc = c1 - c0;
+  uint32_t a = 0, b = 0;
+  const uint32_t u = c * sp.Wn + warp; /* working-warp index (when warp < Wn) */
+  if ((uint32_t)warp < sp.Wn) {
+    a = warp_begin(c0, tc, sp.Wn, warp);
+    b = warp_begin(c0, tc, sp.Wn, warp + 1);
   }
-  __syncthreads();
-  const uint64_t deadline = gtimer() + 2000000000ull;
+  const int n = (int)(b - a);
+  const uint8_t* src = w + (size_t)a * TB;
+  float4* wpart = reinterpret_cast<float4*>(smem);
   /* the weights do not depend on the previous kernel: start streaming before the wait */
-  if (tid == 0)
-    for (int q = 0; q < nb && q < total; ++q) issue(q);
+  WTile<QT> ring[D];
+#pragma unroll
+  for (int u = 0; u < D; ++u)
+    if (u < n) ring[u].load(src + (size_t)u * TB, lane, g);
+  if (tid < W) wcnt[tid] = 0;
   pdl_wait();
   pdl_trigger();
   if (XS) {
-    /* every CTA normalises the M input rows into its own shared-memory copy, with the
-       arithmetic of rmsnorm_kernel (so the fused and the separate paths give the same bits) */
-    __shared__ float nred[32];
-    __half* xs = reinterpret_cast<__half*>(ring + (size_t)nb * CB + 2 * (size_t)CW * NT * 32 * sizeof(float4));
-    const int K = tiles * (QT == ULB_TYPE_Q4_0 ? kQ40TileK : kQ4KTileK);
-    for (int m = 0; m < M; ++m) rms_row_256(nin.x + (size_t)m * nin.ldx, nin.g, K, nin.eps, xs + (size_t)m * K, nred);
-    __syncthreads();
+    /* the CTA normalises the M input rows into its own shared-memory copy with the arithmetic
+       of rmsnorm_kernel (same bits as the separate path): threads 0-255 take rows 0, 2, ...,
+       threads 256-511 rows 1, 3, ..., each half on its own named barrier */
+    static_assert(!XS || W == 16, "the fused RMSNorm runs as two 256-thread halves");
+    __shared__ float nred[2][8];
+    __half* xs = reinterpret_cast<__half*>(smem + warp_part_bytes<QT, NT>());
+    const int K = (int)sp.tiles * WTile<QT>::TK;
+    const int hf = tid >> 8;
+    for (int m = hf; m < M; m += 2)
+      rms_row_256(nin.x + (size_t)m * nin.ldx, nin.g, K, nin.eps, xs + (size_t)m * K, nred[hf], tid & 255, 1 + hf);
     x = xs;
     ldx = K;
   }
-  const int g = lane >> 2, t = lane & 3;
+  __syncthreads(); /* wcnt zeroed, normalised rows written */
+  if (n == 0) return;
   const __half* xr[NT];
   activation_rows<NT>(x, xzero, ldx, M, g, t, xr);
-  int seq = 0, iter = 0;
-  bool ok = true;
-  for (int s = blockIdx.x; s < n_strips; s += gridDim.x, ++iter) {
-    float acc[NSL][NT][4];
+  const uint32_t tiles = sp.tiles;
+  const uint32_t first_strip = a / tiles;
+  float acc[NT][4];
 #pragma unroll
-    for (int j = 0; j < NSL; ++j)
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+
+  /* the warp's part of strip s is in acc */
+  auto flush = [&](uint32_t s) {
+    const uint32_t s0 = s * tiles, s1 = s0 + tiles;
+    float4 v[NT];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) acc[j][nt][0] = acc[j][nt][1] = acc[j][nt][2] = acc[j][nt][3] = 0.f;
-    for (int ch = 0; ch < nch; ++ch, ++seq) {
-      const int slot = seq % nb;
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait_deadline(&full[slot], (uint32_t)(seq / nb) & 1u, deadline));
-      if (ok) {
-        const uint8_t* base = ring + (size_t)slot * CB;
-        const int t0 = ch * CT, tn = min(tiles - t0, CT);
-        /* software pipeline over the warp's tiles warp, warp + CW, ...: load j + 1, compute j */
-        TileRegs<QT, NT> tr[2]; /* indexed by j & 1: constant after unrolling, so no copies */
-        if (warp < tn) tile_load<XS, NT>(tr[0], base + warp * TB, t0 + warp, xr, lane, g);
+    for (int nt = 0; nt < NT; ++nt) v[nt] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+    if (s0 < a || s1 > b) {
+      /* level 1: the warps of this CTA holding part of s, in warp order */
+      const uint32_t lo = max(s0, c0), hi = min(s1, c1);
+      const uint32_t wa = warp_in_cta(tc, sp.Wn, lo - c0), wb = warp_in_cta(tc, sp.Wn, hi - 1 - c0);
+      if (wa != wb) {
+        float4* mine = wpart + ((size_t)(warp * 2 + (s == first_strip ? 0 : 1)) * NT) * 32 + lane;
 #pragma unroll
-        for (int j = 0; j < NSL; ++j) {
-          const int i = warp + j * CW;
-          if (j + 1 < NSL && i + CW < tn)
-            tile_load<XS, NT>(tr[(j + 1) & 1], base + (i + CW) * TB, t0 + i + CW, xr, lane, g);
-          if (i < tn) tile_compute<XS, NT>(tr[j & 1], t0 + i, xr, acc[j]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) {
-        /* the last of the CW warps to be done with the slot refills it with chunk seq + nb:
-           acq_rel makes every warp's reads of the slot happen before the refill, and the
-           proxy fence orders them before the async-proxy write of the bulk copy */
-        uint32_t prev;
-        asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
-                     : "=r"(prev)
-                     : "r"(smem_u32(&released[slot]))
-                     : "memory");
-        if (prev == CW - 1) {
-          released[slot] = 0;
-          if (seq + nb < total) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(seq + nb);
+        for (int nt = 0; nt < NT; ++nt) mine[nt * 32] = v[nt];
+        __syncwarp();
+        uint32_t prev = 0;
+        if (lane == 0)
+          asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                       : "=r"(prev)
+                       : "r"(smem_u32(&wcnt[wa]))
+                       : "memory");
+        if (__shfl_sync(0xffffffffu, prev, 0) != wb - wa) return;
+        __syncwarp();
+        if (lane == 0) wcnt[wa] = 0;
+        /* warp wa holds s as its first strip iff it starts at or after s0; later warps start
+           inside s */
+        const int sa = warp_begin(c0, tc, sp.Wn, wa) >= s0 ? 0 : 1;
+        for (uint32_t ww = wa; ww <= wb; ++ww) {
+          const float4* q = wpart + ((size_t)(ww * 2 + (ww == wa ? sa : 0)) * NT) * 32 + lane;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const float4 o = q[nt * 32];
+            if (ww == wa) {
+              v[nt] = o;
+            } else {
+              v[nt].x += o.x; v[nt].y += o.y; v[nt].z += o.z; v[nt].w += o.w;
+            }
           }
         }
       }
-    }
-    /* slots w, w+CW, ... are summed in the warp, then warps in warp order: CW is the same
-       for every NT, so this order is fixed.  The partials alternate between two buffers, so
-       one barrier per strip suffices: a buffer is rewritten two strips later, after every
-       warp (its reader included) has passed the barrier of the strip in between. */
-    float4* rb = red + (size_t)(iter & 1) * CW * NT * 32;
+      if (s0 < c0 || s1 > c1) {
+        /* level 2: the CTAs holding part of s, in CTA order */
+        float4* mine = part + ((size_t)(c * 2 + (s == c0 / tiles ? 0 : 1)) * NT) * 32 + lane;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      float4 v = make_float4(acc[0][nt][0], acc[0][nt][1], acc[0][nt][2], acc[0][nt][3]);
+        for (int nt = 0; nt < NT; ++nt) __stcg(mine + nt * 32, v[nt]);
+        __threadfence();
+        __syncwarp();
+        const uint32_t ca = cta_of(sp, s0), cb = cta_of(sp, s1 - 1);
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&cnt[ca], 1) == (int)(cb - ca);
+        if (!__shfl_sync(0xffffffffu, last, 0)) return;
+        __threadfence();
+        const int sa = cta_begin(sp, ca) >= s0 ? 0 : 1;
+        for (uint32_t cc = ca; cc <= cb; cc += 2) {
+          float4 o[2][NT]; /* two CTAs' partials in flight at once */
 #pragma unroll
-      for (int j = 1; j < NSL; ++j) {
-        v.x += acc[j][nt][0]; v.y += acc[j][nt][1]; v.z += acc[j][nt][2]; v.w += acc[j][nt][3];
+          for (int i = 0; i < 2; ++i)
+            if (cc + i <= cb) {
+              const float4* q = part + ((size_t)((cc + i) * 2 + (cc + i == ca ? sa : 0)) * NT) * 32 + lane;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) o[i][nt] = __ldcg(q + nt * 32);
+            }
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            if (cc + i <= cb) {
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                if (cc + i == ca) {
+                  v[nt] = o[i][nt];
+                } else {
+                  v[nt].x += o[i][nt].x; v[nt].y += o[i][nt].y; v[nt].z += o[i][nt].z; v[nt].w += o[i][nt].w;
+                }
+              }
+            }
+        }
+        if (lane == 0) cnt[ca] = 0;
       }
-      rb[(warp * NT + nt) * 32 + lane] = v;
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
-    /* n-tile nt of this strip is finished by warp (nt + iter) % CW: the epilogue work rotates
-       over the warps instead of stalling warp 0 on every strip */
-    for (int nt = (warp - iter % CW + CW) % CW; nt < NT; nt += CW) {
-      float4 v = rb[nt * 32 + lane];
 #pragma unroll
-      for (int w2 = 1; w2 < CW; ++w2) {
-        const float4 o = rb[(w2 * NT + nt) * 32 + lane];
-        v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-      }
-      if (ok) epilogue<EPI>(ea, s, nt, g, t, M, N, v);
-    }
-  }
-  if (!ok && lane == 0) atomicOr(err, 2);
-}
+    for (int nt = 0; nt < NT; ++nt) epilogue<EPI>(ea, (int)s, nt, g, t, M, N, v[nt]);
+  };
 
-/* ------------------------------------------------------------------ Q4_K tile */
-template <bool XS, int NT>
-__device__ __forceinline__ void tile_compute(const TileRegs<ULB_TYPE_Q4_K, NT>& r, int tile, const __half* const (&xr)[NT],
-                                             float (&acc)[NT][4]) {
-  {
-    const uint4(&nb)[4] = r.w;
-    const uint4 mg = r.mg, mg8 = r.mg8;
-    const float2 dg = __half22float2(*reinterpret_cast<const __half2*>(&mg.x));   /* (d, dmin) row g */
-    const float2 dg8 = __half22float2(*reinterpret_cast<const __half2*>(&mg8.x)); /* row g + 8 */
-    float t1[NT][4], t0[NT][4];
+  uint32_t s = first_strip;
+  uint32_t kt = a - first_strip * tiles;
+  constexpr int TK = WTile<QT>::TK;
+  const __half* xp[NT]; /* activations of the current tile */
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+  for (int nt = 0; nt < NT; ++nt) xp[nt] = xr[nt] + kt * TK;
+  const uint8_t* wp = src + (size_t)D * TB; /* the refill of the tile being computed */
+  /* after tile j: refill its ring slot with tile j + D, step the activations, finish the strip */
+#define ULB_GEMV_NEXT(u, j)                                                                  \
+  {                                                                                          \
+    if ((j) + D < n) ring[u].load(wp, lane, g);                                              \
+    wp += TB;                                                                                \
+    if (++kt == tiles) {                                                                     \
+      flush(s);                                                                              \
+      _Pragma("unroll") for (int nt = 0; nt < NT; ++nt) {                                    \
+        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;                             \
+        xp[nt] = xr[nt];                                                                     \
+      }                                                                                      \
+      ++s;                                                                                   \
+      kt = 0;                                                                                \
+    } else {                                                                                 \
+      _Pragma("unroll") for (int nt = 0; nt < NT; ++nt) xp[nt] += TK;                        \
+    }                                                                                        \
+  }
+  int j = 0;
+  for (; j + D <= n; j += D) { /* full groups: tile j + u is in ring slot u */
 #pragma unroll
-      for (int i = 0; i < 4; ++i) t1[nt][i] = t0[nt][i] = 0.f;
-#define ULB_Q4K_SUB(J)                                                                   \
-    {                                                                                    \
-      const uint32_t* wp = reinterpret_cast<const uint32_t*>(&nb[(J) >> 1]);            \
-      float s1[NT][4], s0[NT][4];                                                        \
-      const int kofs = tile * 256 + (J) * 32;                                            \
-      uint4 bx[NT];                                                                      \
-      _Pragma("unroll") for (int nt = 0; nt < NT; ++nt)                                  \
-        bx[nt] = xld<XS>(xr[nt] + kofs);                                                 \
-      block_mma_r<0, NT>(wp[((J) & 1) * 2], wp[((J) & 1) * 2 + 1], bx, s1);              \
-      block_colsum_r<NT>(bx, s0);                                                        \
-      float scg, mng, scg8, mng8;                                                        \
-      q4k_sm<J>(mg.y, mg.z, mg.w, scg, mng);                                             \
-      q4k_sm<J>(mg8.y, mg8.z, mg8.w, scg8, mng8);                                        \
-      _Pragma("unroll") for (int nt = 0; nt < NT; ++nt) {                                \
-        t1[nt][0] = __fmaf_rn(scg, s1[nt][0], t1[nt][0]);                                \
-        t1[nt][1] = __fmaf_rn(scg, s1[nt][1], t1[nt][1]);                                \
-        t1[nt][2] = __fmaf_rn(scg8, s1[nt][2], t1[nt][2]);                               \
-        t1[nt][3] = __fmaf_rn(scg8, s1[nt][3], t1[nt][3]);                               \
-        t0[nt][0] = __fmaf_rn(mng, s0[nt][0], t0[nt][0]);                                \
-        t0[nt][1] = __fmaf_rn(mng, s0[nt][1], t0[nt][1]);                                \
-        t0[nt][2] = __fmaf_rn(mng8, s0[nt][2], t0[nt][2]);                               \
-        t0[nt][3] = __fmaf_rn(mng8, s0[nt][3], t0[nt][3]);                               \
-      }                                                                                  \
-    }
-    ULB_Q4K_SUB(0) ULB_Q4K_SUB(1) ULB_Q4K_SUB(2) ULB_Q4K_SUB(3)
-    ULB_Q4K_SUB(4) ULB_Q4K_SUB(5) ULB_Q4K_SUB(6) ULB_Q4K_SUB(7)
-#undef ULB_Q4K_SUB
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      acc[nt][0] = __fmaf_rn(-dg.y, t0[nt][0], __fmaf_rn(dg.x, t1[nt][0], acc[nt][0]));
-      acc[nt][1] = __fmaf_rn(-dg.y, t0[nt][1], __fmaf_rn(dg.x, t1[nt][1], acc[nt][1]));
-      acc[nt][2] = __fmaf_rn(-dg8.y, t0[nt][2], __fmaf_rn(dg8.x, t1[nt][2], acc[nt][2]));
-      acc[nt][3] = __fmaf_rn(-dg8.y, t0[nt][3], __fmaf_rn(dg8.x, t1[nt][3], acc[nt][3]));
+    for (int u = 0; u < D; ++u) {
+      tile_compute<XS, NT>(ring[u], xp, acc);
+      ULB_GEMV_NEXT(u, j + u)
     }
   }
+#pragma unroll
+  for (int u = 0; u < D - 1; ++u) /* the last n % D tiles */
+    if (j + u < n) {
+      tile_compute<XS, NT>(ring[u], xp, acc);
+      ULB_GEMV_NEXT(u, j + u)
+    }
+#undef ULB_GEMV_NEXT
+  if (pf_bytes && lane == 0) {
+    /* this warp's loads are all issued: start the next kernel's weights on their way to L2,
+       an equal share per warp, so HBM stays busy through this kernel's tail and the next one's
+       start */
+    const uint64_t nw = (uint64_t)sp.G * sp.Wn;
+    const uint64_t lo = (uint64_t)pf_bytes * u / nw & ~15ull, hi = (uint64_t)pf_bytes * (u + 1) / nw & ~15ull;
+    for (uint64_t o = lo; o < hi; o += 32768) prefetch_l2_bulk(pf + o, hi - o < 32768 ? (uint32_t)(hi - o) : 32768u);
+  }
+  if (kt != 0) flush(s); /* the range ends inside strip s */
 }
 
 /* ------------------------------------------------------------------ repack / dequant */
@@ -632,26 +658,29 @@ __global__ void dequant_q4k_kernel(const uint8_t* __restrict__ w, int tiles, int
 
 template <int QT, int NT, int EPI, bool XS = false>
 int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a, const NormIn& nin = NormIn()) {
-  constexpr int TB = PQ<QT>::TB, CT = PQ<QT>::CT, NB = PQ<QT>::NB, CW = PQW<NT>::CW;
-  const int nch = (w->tiles + CT - 1) / CT;
-  /* ring: as many slots as the CTA has chunks in flight, at most NB */
   ULB_CHECK(w->K + 8 <= kZeroRowHalves, ULB_EUNSUPPORTED, "qgemv: K=%d too long", w->K);
-  const int ctas = c->n_sm * PQW<NT>::MINB;
-  const int per_cta = (w->n_strips + ctas - 1) / ctas;
-  const int grid = (w->n_strips + per_cta - 1) / per_cta; /* balanced: every CTA gets per_cta or per_cta-1 strips */
-  const int slots = min(NB, per_cta * nch);
-  const size_t red_bytes = 2 * (size_t)CW * NT * 32 * sizeof(float4); /* two alternating partial buffers */
-  const size_t xs_bytes = XS ? (size_t)kNormSmemBytes : 0; /* normalised x (fused RMSNorm) */
-  const size_t smem = (size_t)slots * CT * TB + red_bytes + xs_bytes;
+  const long long T = (long long)w->n_strips * w->tiles;
+  ULB_CHECK(T * c->n_sm < (1ll << 31), ULB_EUNSUPPORTED, "qgemv: %lld tiles is too many", T);
+  Split sp;
+  sp.T = (uint32_t)T;
+  sp.G = (uint32_t)std::min<long long>(c->n_sm, T);
+  sp.Wn = (uint32_t)std::max<long long>(1, std::min<long long>(GemvCfg<QT, NT>::W, T / sp.G));
+  sp.tiles = (uint32_t)w->tiles;
+  ULB_CHECK(sp.G <= (uint32_t)kGemvCounters && (size_t)sp.G * 2 * 4 * 32 <= (size_t)c->n_sm * kGemvPartPerSm,
+            ULB_EUNSUPPORTED, "qgemv: grid of %u CTAs", sp.G);
+  const size_t xs_bytes = XS ? ((size_t)M * w->K * sizeof(__half) + 15) / 16 * 16 : 0; /* normalised rows */
+  const size_t smem = warp_part_bytes<QT, NT>() + xs_bytes;
+  ULB_CHECK(smem <= kGemvSmemBytes, ULB_EUNSUPPORTED, "qgemv: %zu B of normalised rows", xs_bytes);
   static bool attr_set = false;
   if (!attr_set) {
     ULB_CUDA(cudaFuncSetAttribute(qgemv_kernel<QT, NT, EPI, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)((size_t)NB * CT * TB + red_bytes + xs_bytes)));
+                                  (int)kGemvSmemBytes));
     attr_set = true;
   }
-  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI, XS>, dim3(grid), dim3(CW * 32), smem,
-                           (const uint8_t*)w->dev, w->tiles, w->n_strips, w->N, x, M, ldx, a, c->dev_err, slots,
-                           (const __half*)c->zero_row, nin);
+  const uint32_t pf_bytes = (uint32_t)std::min<size_t>(c->pf_bytes, kPrefetchMaxBytes) & ~15u;
+  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI, XS>, dim3(sp.G), dim3(GemvCfg<QT, NT>::W * 32), smem,
+                           (const uint8_t*)w->dev, sp, w->N, x, M, ldx, a, (const __half*)c->zero_row, nin,
+                           c->gemv_part, c->gemv_cnt, (const uint8_t*)c->pf_ptr, c->pf_ptr ? pf_bytes : 0u);
   if (e != cudaSuccess) return cuda_error(e, "qgemv launch", __FILE__, __LINE__);
   return ULB_OK;
 }
@@ -674,7 +703,16 @@ int launch_epi(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const E
 /* Max rows per launch (larger M is chunked by the caller of launch_qgemv). */
 static int max_rows_per_launch(int) { return kGemvMaxRows; }
 
+static int launch_qgemv_impl(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0);
+
 int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
+  const int rc = launch_qgemv_impl(c, w, x, M, ldx, epi, a0);
+  c->pf_ptr = nullptr; /* the prefetch hint is for the launch that follows it only */
+  c->pf_bytes = 0;
+  return rc;
+}
+
+static int launch_qgemv_impl(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
   ULB_CHECK(w && (w->type == ULB_TYPE_Q4_0 || w->type == ULB_TYPE_Q4_K), ULB_EINVAL, "qgemv: weight is not Q4_0/Q4_K");
   ULB_CHECK(M >= 0 && ldx % 8 == 0 && ldx >= w->K, ULB_EINVAL, "qgemv: bad M=%d / ldx=%d (K=%d)", M, ldx, w->K);
   ULB_CHECK(((uintptr_t)x & 15) == 0, ULB_EINVAL, "qgemv: activations must be 16-byte aligned");
@@ -721,11 +759,16 @@ int launch_qgemv_rms(Ctx* c, const Tensor* w, const float* x32, int ldx32, const
   nin.g = g;
   nin.eps = eps;
   const bool q40 = w->type == ULB_TYPE_Q4_0;
+  int rc;
   if (epi == EPI_QKV)
-    return q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_QKV, true>(c, w, nullptr, M, w->K, a, nin)
-               : launch_q<ULB_TYPE_Q4_K, 1, EPI_QKV, true>(c, w, nullptr, M, w->K, a, nin);
-  return q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_SWIGLU, true>(c, w, nullptr, M, w->K, a, nin)
+    rc = q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_QKV, true>(c, w, nullptr, M, w->K, a, nin)
+             : launch_q<ULB_TYPE_Q4_K, 1, EPI_QKV, true>(c, w, nullptr, M, w->K, a, nin);
+  else
+    rc = q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_SWIGLU, true>(c, w, nullptr, M, w->K, a, nin)
              : launch_q<ULB_TYPE_Q4_K, 1, EPI_SWIGLU, true>(c, w, nullptr, M, w->K, a, nin);
+  c->pf_ptr = nullptr;
+  c->pf_bytes = 0;
+  return rc;
 }
 
 int launch_dequant(Ctx* c, const Tensor* w, float* out) {

@@ -82,8 +82,16 @@ struct Ctx {
   float* tc_ws = nullptr;              /* split-K partial sums of the tensor-core GEMM */
   size_t tc_ws_floats = 0;
   int* tc_cnt = nullptr;               /* kTcCounters arrival counters, zero between launches */
+  float4* gemv_part = nullptr;         /* GEMV partials of strips shared by CTAs: n_sm x kGemvPartPerSm */
+  int* gemv_cnt = nullptr;             /* kGemvCounters arrival counters, zero between launches */
   int tp_rank = 0, tp_world = 1;
+  /* hint: the weights the next GEMV on the stream will read (set just before it by the
+     forward pass); the GEMV launched after the hint prefetches them into L2 from its tail.
+     Every GEMV launch clears it. */
+  const void* pf_ptr = nullptr;
+  size_t pf_bytes = 0;
 };
+constexpr size_t kPrefetchMaxBytes = (size_t)48 << 20;
 /* fp32 sum over the communicator's ranks, in place, on the context stream */
 int tp_allreduce_sum(Ctx* c, float* buf, size_t n);
 constexpr int kZeroRowHalves = 65536 + 64;
@@ -118,6 +126,11 @@ int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int e
    copy fits kNormSmemBytes) normalise inside the GEMV, each CTA into its own shared memory;
    otherwise rmsnorm_kernel writes x16 [M][K] first.  Both give the same bits. */
 constexpr int kNormSmemBytes = 16384;
+/* GEMV (M <= kGemvMaxRows): dynamic shared memory per CTA at most, arrival counters (one per
+   CTA), cross-CTA partial slots per SM ({first, last strip} x up to 4 n-tiles x 32 lanes) */
+constexpr size_t kGemvSmemBytes = 230400;
+constexpr int kGemvCounters = 16384;
+constexpr size_t kGemvPartPerSm = 2 * 4 * 32;
 /* out[s] = rmsnorm(x[row]) (row = s*sel + sel - 1 when sel > 0, else s), 256 threads a row */
 int launch_rmsnorm_sel(Ctx* c, const float* x, int ldx, const float* g, int n_out, int d, float eps, int sel,
                        __half* out, int ldo);
@@ -194,19 +207,29 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 /* Allow the next kernel in the stream to begin launching its CTAs. */
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+/* barrier of a 256-thread group: the whole block (bar == 0, a 256-thread block) or named
+   barrier `bar` of 256 threads inside a larger block */
+__device__ __forceinline__ void sync256(int bar) {
+  if (bar == 0)
+    __syncthreads();
+  else
+    asm volatile("bar.sync %0, 256;" ::"r"(bar) : "memory");
+}
+
 /*
- * RMSNorm of one row by a block of exactly 256 threads (all of them call it; d % 4 == 0,
- * d <= 8192): out = fp16((x * r) * g), r = 1 / sqrt(sum(x^2) / d + eps).  The whole row is
- * loaded with independent 128-bit loads before any arithmetic (one memory latency), and the
- * sum has one fixed order (per-thread fmaf chains over float4 j = i*256 + tid, a warp xor
- * tree, the 8 warps in order), so every caller produces the same bits.  `red` is 8 floats
- * of shared memory; `out` may be global or shared.
+ * RMSNorm of one row by a group of exactly 256 threads (all of them call it, tid = 0..255;
+ * d % 4 == 0, d <= 8192): out = fp16((x * r) * g), r = 1 / sqrt(sum(x^2) / d + eps).  The
+ * whole row is loaded with independent 128-bit loads before any arithmetic (one memory
+ * latency), and the sum has one fixed order (per-thread fmaf chains over float4
+ * j = i*256 + tid, a warp xor tree, the 8 warps in order), so every caller produces the same
+ * bits.  `red` is 8 floats of shared memory private to the group; `out` may be global or
+ * shared; `bar` as for sync256.
  */
 __device__ __forceinline__ void rms_row_256(const float* __restrict__ x, const float* __restrict__ g, int d, float eps,
-                                            __half* out, float* red) {
+                                            __half* out, float* red, int tid = threadIdx.x, int bar = 0) {
   const float4* xv = reinterpret_cast<const float4*>(x);
   const float4* gv = reinterpret_cast<const float4*>(g);
-  const int n4 = d >> 2, tid = threadIdx.x;
+  const int n4 = d >> 2;
   float4 v[8], gg[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -227,11 +250,11 @@ __device__ __forceinline__ void rms_row_256(const float* __restrict__ x, const f
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((tid & 31) == 0) red[tid >> 5] = ss;
-  __syncthreads();
+  sync256(bar);
   float tot = 0.f;
 #pragma unroll
   for (int w = 0; w < 8; ++w) tot += red[w];
-  __syncthreads(); /* red is free for the next row */
+  sync256(bar); /* red is free for the next row */
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
   __half2* o2 = reinterpret_cast<__half2*>(out);
 #pragma unroll
