@@ -66,6 +66,14 @@ def tiny_gqa_q4k(model_dir):
     return _synth(model_dir, spec, "tiny_gqa_q4k.gguf")
 
 
+@pytest.fixture(scope="session")
+def mid_q40(model_dir):
+    """Large enough that every GEMV spans all SMs (d = 1024, FFN 2816, 2 layers)."""
+    spec = dict(n_layer=2, d_model=1024, n_head=8, n_head_kv=8, d_ff=2816, n_vocab=4096,
+                rms_eps=1e-5, rope_base=1e4, wtype="q4_0", seed=5, name="mid-q40")
+    return _synth(model_dir, spec, "mid_q40.gguf")
+
+
 def has_gpu():
     try:
         import ulb_capi

@@ -131,6 +131,26 @@ def test_fused_rmsnorm_rows_equal_separate_rmsnorm(ctx, tiny_target):
         gm.close()
 
 
+def test_mid_model_matches_oracle(ctx, mid_q40):
+    """d = 1024, FFN 2816: every GEMV spans all SMs with strips shared between warps; a 6-row
+    verify block after a 20-row prefill matches the oracle."""
+    gm = GpuModel(ctx, mid_q40)
+    try:
+        kvg = gm.kv(1, 64)
+        kvo = orc.KV(gm.om, 1, 64)
+        toks = _prompt(20, seed=43, vocab=4096)
+        gm.forward(kvg, toks, [0] * 20, range(20), 20, logits_mode=1)
+        orc.forward(gm.om, kvo, toks, [0] * 20, list(range(20)), 20, logits_mode=1)
+        toks = _prompt(6, seed=44, vocab=4096)
+        g = gm.forward(kvg, toks, [0] * 6, range(20, 26), 6)
+        o = orc.forward(gm.om, kvo, toks, [0] * 6, list(range(20, 26)), 6)
+        assert np.abs(g - o).max() / np.abs(o).max() < FWD_RTOL
+        assert (g.argmax(1) == o.argmax(1)).all()
+        gm.U.lib().ulb_kv_free(kvg)
+    finally:
+        gm.close()
+
+
 def _api(target, draft=None, k=4):
     import vulkangguf as vg
     api = vg.InferenceAPI()

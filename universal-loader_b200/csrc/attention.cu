@@ -25,6 +25,7 @@
  * head_dim 64 and 128; capacity <= 8192.
  */
 #include <algorithm>
+#include <climits>
 #include <mutex>
 
 #include "ulb_internal.h"
@@ -100,20 +101,27 @@ __global__ void __launch_bounds__(AW * 32, 1)
   extern __shared__ __align__(128) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int mt = blockIdx.x % p.n_mt, split = blockIdx.x / p.n_mt, kvh = blockIdx.y, gi = blockIdx.z;
-  pdl_wait();
-  pdl_trigger();
+  /* Rows' sequences and positions, and the cache rows before this forward's, were written
+     before the previous kernel (the QKV GEMV) started: they are read, and those K / V rows
+     requested, before griddepcontrol.wait; the rows this forward appended wait for it. */
   const int Q = p.G * p.rps, q0 = mt * QT, nq = min(QT, Q - q0);
   const int m0 = gi * p.rps;
   /* every index load of the CTA is issued before any is used: the tile's last position (one
-     load per lane, lane < nq <= 16, then a warp max), the sequence, and the lane's two query
+     load per lane, lane < nq <= 16, then a warp max), the sequence, the lane's two query
      positions, so the CTA pays one memory latency here */
   const int qa = q0 + g, qb = q0 + g + 8; /* the lane's two query rows of the tile: g, g + 8 */
   const bool va = g < nq, vb = g + 8 < nq;
   int last_pos = lane < nq ? row_pos[m0 + (q0 + lane) / p.G] : 0;
   const int seq = row_seq[m0];
   const int pa = va ? row_pos[m0 + qa / p.G] : -1, pb = vb ? row_pos[m0 + qb / p.G] : -1;
+  /* and the first position this forward wrote for the sequence (rows m0 .. m0 + rps - 1) */
+  int first_new = lane < p.rps ? row_pos[m0 + lane] : INT_MAX;
+  for (int r = lane + 32; r < p.rps; r += 32) first_new = min(first_new, row_pos[m0 + r]);
 #pragma unroll
-  for (int o = 16; o; o >>= 1) last_pos = max(last_pos, __shfl_xor_sync(0xffffffffu, last_pos, o));
+  for (int o = 16; o; o >>= 1) {
+    last_pos = max(last_pos, __shfl_xor_sync(0xffffffffu, last_pos, o));
+    first_new = min(first_new, __shfl_xor_sync(0xffffffffu, first_new, o));
+  }
   last_pos = max(0, min(last_pos, p.cap - 1)); /* positions past the cache never index it */
   const int n_splits = last_pos / SPLITK + 1;
   if (split >= n_splits) return;
@@ -127,17 +135,26 @@ __global__ void __launch_bounds__(AW * 32, 1)
   for (int d = 0; d < DN; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
   __half* Ks = reinterpret_cast<__half*>(sm) + (size_t)warp * 2 * KB * HD;
   __half* Vs = Ks + KB * HD;
-  if (nk > 0) {
-    const size_t kvoff = (((size_t)seq * p.Hkv + kvh) * p.cap + kb0) * HD;
-    const __half* kg = kc + kvoff;
-    const __half* vg = vc + kvoff;
+  const size_t kvoff = (((size_t)seq * p.Hkv + kvh) * p.cap + max(kb0, 0)) * HD;
+  const __half* kg = kc + kvoff;
+  const __half* vg = vc + kvoff;
+  /* keys [0, n_old) of the block predate this forward, keys [n_old, nk) were just written */
+  const int n_old = max(0, min(nk, first_new - kb0));
+  auto stage = [&](int j0, int j1) {
     for (int i = lane; i < KB * NCH; i += 32) {
       const int j = i / NCH, c = i % NCH;
+      if (j < j0 || j >= j1) continue;
       const bool ok = j < nk;
       const size_t off = ok ? (size_t)j * HD + c * 8 : 0;
       cp_async16z(Ks + j * HD + swz(j, c) * 8, kg + off, ok);
       cp_async16z(Vs + j * HD + swz(j, c) * 8, vg + off, ok);
     }
+  };
+  if (nk > 0) stage(0, n_old);
+  pdl_wait();
+  pdl_trigger();
+  if (nk > 0) {
+    stage(n_old, KB); /* the new keys, and zero fill past the last key */
     cp_commit();
   }
   const float* qpa = q + (size_t)(m0 + (va ? qa : q0) / p.G) * p.ldq + (kvh * p.G + (va ? qa : q0) % p.G) * HD;

@@ -24,11 +24,11 @@ __device__ __forceinline__ void epilogue_token(const EpiArgs& e, int strip, int 
     const int r0 = strip * 16 + g, r1 = r0 + 8;
     if (r0 < N) {
       float* p = e.y + (size_t)tok * e.ldy + r0;
-      *p = EPI == EPI_RESID ? *p + vg : vg;
+      *p = EPI == EPI_RESID ? __ldcg(p) + vg : vg;
     }
     if (r1 < N) {
       float* p = e.y + (size_t)tok * e.ldy + r1;
-      *p = EPI == EPI_RESID ? *p + vg8 : vg8;
+      *p = EPI == EPI_RESID ? __ldcg(p) + vg8 : vg8;
     }
   } else if (EPI == EPI_SWIGLU) {
     const int f = strip * 8 + g;

@@ -199,6 +199,19 @@ static int tp_reduce_add(Model* m, int M) {
   return ULB_OK;
 }
 
+/* final RMSNorm (of every row, or of each sequence's last row) and the LM head */
+static int forward_head(Model* m, int M, int rps, int logits_mode, float* logits, int ld) {
+  Ctx* c = m->c;
+  const ulb_model_desc& d = m->d;
+  const int n_out = logits_mode == 1 ? M / rps : M;
+  ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, m->out_norm, n_out, d.d_model, d.rms_eps,
+                             logits_mode == 1 ? rps : 0, m->x16, d.d_model));
+  EpiArgs o;
+  o.y = logits;
+  o.ldy = ld;
+  return launch_qgemv(c, &m->out, m->x16, n_out, d.d_model, EPI_STORE, o);
+}
+
 int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos, int logits_mode,
                   float* logits, int ld, int* err) {
   Ctx* c = m->c;
@@ -245,12 +258,7 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     ULB_TRY(launch_qgemv(c, &L.down, m->h16, M, d.d_ff, tp ? EPI_STORE : EPI_RESID, tp ? pr : r));
     if (tp) ULB_TRY(tp_reduce_add(m, M));
   }
-  const int n_out = logits_mode == 1 ? M / rps : M;
-  ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, m->out_norm, n_out, d.d_model, d.rms_eps,
-                             logits_mode == 1 ? rps : 0, m->x16, d.d_model));
-  EpiArgs o;
-  o.y = logits; o.ldy = ld;
-  return launch_qgemv(c, &m->out, m->x16, n_out, d.d_model, EPI_STORE, o);
+  return forward_head(m, M, rps, logits_mode, logits, ld);
 }
 
 }  // namespace ulb

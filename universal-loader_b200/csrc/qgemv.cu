@@ -9,8 +9,8 @@
  *
  * Design (B200):
  *  - one CTA of 16 warps per SM; the matrix is one stream of 16-row x K-tile tiles in layout
- *    order, split into equal contiguous ranges per SM and per warp, so every SM streams the
- *    same bytes to within one tile and every warp one contiguous range;
+ *    order, split into whole strips per SM and equal contiguous ranges per warp, so every SM
+ *    streams the same bytes to within one strip and every warp one contiguous range;
  *  - each warp loads its tiles with 128-bit L1-bypassing loads straight into a ring of D
  *    tiles of registers (~74 KB in flight per SM); the first D tiles are requested before
  *    griddepcontrol.wait, so the weight stream overlaps the previous kernel (programmatic
@@ -19,10 +19,9 @@
  *    (0x6400 magic) and feed mma.sync.m16n8k16 (weights = A, activations = B, so M <= 8
  *    tokens fill one n-tile); each 32-weight block's scale is applied in fp32 to that
  *    block's integer dot product, so weights are never rounded;
- *  - a strip split between warps is summed in a fixed two-level order (warps of a CTA in
- *    shared memory, then CTAs through global memory), the last arriving warp running the
- *    epilogue; the split depends on (N, K, SM count) only, so a row's arithmetic never
- *    depends on M;
+ *  - CTAs take whole strips; a strip split between warps is summed in warp order in shared
+ *    memory by the last warp to finish its part, which runs the epilogue; the split depends
+ *    on (N, K, SM count) only, so a row's arithmetic never depends on M;
  *  - the fused epilogues write RoPE'd Q / K / V (K and V straight into the fp16 KV cache),
  *    SiLU(gate)*up in fp16, or the fp32 residual add.
  * The tensor pipe is idle in this regime (<= 3.6 flop/B at M = 1); mma.sync is used as the
@@ -154,6 +153,11 @@ __device__ __forceinline__ void epilogue(const EpiArgs& e, int strip, int nt, in
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 /* 128-bit weight load: read once, so it neither allocates in L1 (kept for the activations)
    nor waits for the previous kernel (weights are constant) */
@@ -303,23 +307,23 @@ __device__ __forceinline__ void tile_compute(const WTile<ULB_TYPE_Q4_K>& r, cons
 }
 
 /*
- * Split of the weight stream.  The matrix is one stream of T = n_strips * tiles tiles in layout
- * order (strip-major).  CTA c of G takes tiles [c*T/G, (c+1)*T/G) and warp w of its Wn working
- * warps an equal contiguous share of those, so every warp streams one contiguous byte range
- * and every SM gets the same bytes to within one tile.  A strip split between warps is summed
- * in two levels with one fixed order: the warps of a CTA in warp order (shared memory), then
- * the CTAs in CTA order (global memory, only for the strips that cross a CTA boundary).  The
- * split depends on (N, K, G) only, never on M, so a row's arithmetic does not depend on what
- * else is batched.  All quantities fit 32 bits (T * G < 2^31, checked by the launcher).
+ * Split of the weight stream.  The matrix is one stream of n_strips * tiles tiles in layout
+ * order (strip-major).  CTA c of G takes the whole strips [c*S/G, (c+1)*S/G) (S = n_strips),
+ * and warp w of its Wn working warps an equal contiguous share of that CTA's tiles, so every
+ * warp streams one contiguous byte range and no strip is split between CTAs: a CTA streams
+ * at most one strip (16 rows x K) more than the average, less than the latency of a cross-CTA
+ * reduction it saves.  A strip split between warps is summed in warp order in shared memory.
+ * The split depends on (N, K, G) only, never on M, so a row's arithmetic does not depend on
+ * what else is batched.  All quantities fit 32 bits.
  */
 struct Split {
-  uint32_t T;     /* tiles in the matrix */
-  uint32_t G;     /* CTAs */
-  uint32_t Wn;    /* working warps per CTA (<= 16, <= T / G): every working warp has >= 1 tile */
+  uint32_t S;     /* strips in the matrix */
+  uint32_t G;     /* CTAs (<= S) */
+  uint32_t Wn;    /* working warps per CTA (<= 16, <= the tiles of a CTA) */
   uint32_t tiles; /* tiles per strip */
 };
-__device__ __forceinline__ uint32_t cta_begin(const Split& s, uint32_t c) { return c * s.T / s.G; }
-__device__ __forceinline__ uint32_t cta_of(const Split& s, uint32_t i) { return ((i + 1) * s.G - 1) / s.T; }
+/* first tile of CTA c (c = G gives the end of the matrix) */
+__device__ __forceinline__ uint32_t cta_begin(const Split& s, uint32_t c) { return c * s.S / s.G * s.tiles; }
 /* first tile of warp w of a CTA starting at c0 with tc tiles; the warp holding local tile l */
 __device__ __forceinline__ uint32_t warp_begin(uint32_t c0, uint32_t tc, uint32_t Wn, uint32_t w) {
   return c0 + w * tc / Wn;
@@ -328,7 +332,7 @@ __device__ __forceinline__ uint32_t warp_in_cta(uint32_t tc, uint32_t Wn, uint32
 
 
 
-/* RMSNorm fused into the GEMV (XS): the fp32 rows, the norm weights and eps */
+/* RMSNorm fused into the GEMV: the fp32 rows, the norm weights and eps */
 struct NormIn {
   const float* x = nullptr;
   int ldx = 0;
@@ -341,28 +345,140 @@ template <int QT, int NT> constexpr size_t warp_part_bytes() {
   return (size_t)GemvCfg<QT, NT>::W * 2 * NT * 32 * sizeof(float4);
 }
 
+/* one GEMV of a launch: y (by its epilogue) = W . activations */
+struct GemvStep {
+  const uint8_t* w = nullptr; /* packed strips */
+  Split sp{};
+  int N = 0, M = 0;
+  const __half* x = nullptr; /* activations [M][ldx] fp16, unless nin.x: rmsnorm(nin.x) */
+  int ldx = 0;
+  NormIn nin;
+  EpiArgs ea;
+  const uint8_t* pf = nullptr; /* weights of the next GEMV: prefetched into L2 from the tail */
+  uint32_t pf_bytes = 0;
+};
+
+/* shared-memory layout of a GEMV CTA: warp partials | activations (fp16 [M][K]) | fp32 rows
+   being normalised ([M][K]) */
+template <int QT, int NT> __device__ __forceinline__ __half* smem_x(uint8_t* smem) {
+  return reinterpret_cast<__half*>(smem + warp_part_bytes<QT, NT>());
+}
+__device__ __forceinline__ size_t align16(size_t b) { return (b + 15) / 16 * 16; }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+/* copy rows [0, M) of `bytes_per_row` from global (row stride ld_bytes) into shared memory
+   (packed), through L2 (cp.async.cg: coherent with writes of other CTAs before a barrier) */
+__device__ __forceinline__ void stage_rows(void* dst, const void* src, size_t ld_bytes, int M, int bytes_per_row) {
+  const int per = bytes_per_row / 16, tot = per * M;
+  for (int i = threadIdx.x; i < tot; i += blockDim.x) {
+    const int m = i / per, k = i - m * per;
+    cp_async16(reinterpret_cast<uint8_t*>(dst) + (size_t)m * bytes_per_row + k * 16,
+               reinterpret_cast<const uint8_t*>(src) + (size_t)m * ld_bytes + k * 16);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+}
+
 /*
- * Warp-streamed fused dequant-GEMV, one CTA of 16 warps per SM.  Each working warp streams its
- * own contiguous range of tiles with 128-bit loads straight into a ring of D tiles of
- * registers: the first D tiles (all of a small matrix) are requested before
- * griddepcontrol.wait, overlapping the previous kernel, and a tile's registers are refilled
- * with tile j + D as soon as tile j is computed.  No warp ever waits for another.
+ * xs[m] = fp16((x[m] * r_m) * g), r_m = 1 / sqrt(sum(x[m]^2) / d + eps) for rows m < M held in
+ * shared memory (fp32 [M][d]), by all warps of the CTA at once, with exactly the arithmetic of
+ * rms_row_256 (rmsnorm_kernel): row m's sum is eight virtual 256-thread blocks' per-thread fmaf
+ * chains over float4 j = i*256 + vt, a warp xor tree, and the eight virtual warps in order.
+ * Real warp w takes virtual warps w, w + NW, ... of the M * 8.
+ */
+template <int NW>
+__device__ __forceinline__ void norm_rows(const float* stg, const float* __restrict__ gw, int d, float eps, int M,
+                                          __half* xs, float* red /* [8 * 8 + 8] */) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n4 = d >> 2;
+  for (int vwi = warp; vwi < M * 8; vwi += NW) {
+    const int m = vwi >> 3, vt = (vwi & 7) * 32 + lane;
+    const float4* xv = reinterpret_cast<const float4*>(stg + (size_t)m * d);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int j = i * 256 + vt;
+      if (j < n4) {
+        const float4 v = xv[j];
+        ss = __fmaf_rn(v.x, v.x, ss);
+        ss = __fmaf_rn(v.y, v.y, ss);
+        ss = __fmaf_rn(v.z, v.z, ss);
+        ss = __fmaf_rn(v.w, v.w, ss);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[vwi] = ss;
+  }
+  __syncthreads();
+  if (threadIdx.x < M) { /* the row scales, over red[64 + m] */
+    const int m = threadIdx.x;
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += red[m * 8 + w];
+    red[64 + m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
+  }
+  __syncthreads();
+  const float4* gv = reinterpret_cast<const float4*>(gw);
+  for (int idx = threadIdx.x; idx < M * n4; idx += NW * 32) {
+    const int m = idx / n4, j = idx - m * n4;
+    const float r = red[64 + m];
+    const float4 v = reinterpret_cast<const float4*>(stg + (size_t)m * d)[j];
+    const float4 gg = __ldg(gv + j);
+    __half2* o2 = reinterpret_cast<__half2*>(xs + (size_t)m * d) + 2 * j;
+    o2[0] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v.x, r), gg.x)),
+                           __float2half_rn(__fmul_rn(__fmul_rn(v.y, r), gg.y)));
+    o2[1] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v.z, r), gg.z)),
+                           __float2half_rn(__fmul_rn(__fmul_rn(v.w, r), gg.w)));
+  }
+  __syncthreads();
+}
+
+/* where a step's activation rows are: fp16 [M][ldx] */
+struct XIn {
+  const __half* x;
+  int ldx;
+};
+
+/* the normalised activations of a step (its nin rows), in shared memory: fp16 [M][K] */
+template <int QT, int NT>
+__device__ __forceinline__ XIn prep_norm(const GemvStep& S, uint8_t* smem, float* red) {
+  const int K = (int)S.sp.tiles * WTile<QT>::TK;
+  __half* xs = smem_x<QT, NT>(smem);
+  float* stg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + align16((size_t)S.M * K * sizeof(__half)));
+  stage_rows(stg, S.nin.x, (size_t)S.nin.ldx * sizeof(float), S.M, K * (int)sizeof(float));
+  norm_rows<GemvCfg<QT, NT>::W>(stg, S.nin.g, K, S.nin.eps, S.M, xs, red);
+  return XIn{xs, K};
+}
+
+/*
+ * Warp-streamed fused dequant-GEMV body, run by a CTA of 16 warps (one per SM).  Each working
+ * warp streams its own contiguous range of tiles with 128-bit loads straight into a ring of D
+ * tiles of registers: the first D tiles (all of a small matrix) are requested before `sync`
+ * (griddepcontrol.wait, or the wait of a grid barrier), so the weight stream overlaps what
+ * came before, and a tile's registers are refilled with tile j + D as soon as tile j is
+ * computed.  No warp ever waits for another while streaming.
  * A strip finished inside one warp goes straight to the epilogue.  A strip split between warps
  * leaves each warp's partial in shared memory (slot 0: the warp's first strip, 1: its last);
- * the last of the CTA's warps to count itself in wcnt[first warp] sums them in warp order.
- * If the strip also crosses a CTA boundary, that CTA sum goes to `part` (two slots per CTA,
- * same rule) and the last CTA to count itself in cnt[first CTA] sums the CTAs' partials in
- * CTA order, runs the epilogue and zeroes the counter for the next launch.
+ * the last of the CTA's warps to count itself in wcnt[first warp] sums them in warp order and
+ * runs the epilogue.
+ * sync(): every thread calls it once; false = abandon the step.  prep(): every thread; returns
+ * the activation rows and ends with a CTA barrier.  XS: the rows are read with generic loads
+ * (shared memory, or global memory written earlier in the same launch); otherwise with
+ * read-only loads.
  */
-template <int QT, int NT, int EPI, bool XS>
-__global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
-    qgemv_kernel(const uint8_t* __restrict__ w, Split sp, int N, const __half* x, int M, int ldx, EpiArgs ea,
-                 const __half* __restrict__ xzero, NormIn nin, float4* __restrict__ part, int* __restrict__ cnt,
-                 const uint8_t* __restrict__ pf, uint32_t pf_bytes) {
+template <int QT, int NT, int EPI, bool XS, class Sync, class Prep>
+__device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint32_t* wcnt,
+                                          const __half* __restrict__ xzero, Sync sync, Prep prep) {
   constexpr int TB = WTile<QT>::TB, D = GemvCfg<QT, NT>::D, W = GemvCfg<QT, NT>::W;
-  /* dynamic shared memory: [W][2][NT][32] warp partials | normalised rows (XS) */
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint32_t wcnt[W];
+  const Split sp = S.sp;
+  const int M = S.M, N = S.N;
+  const EpiArgs& ea = S.ea;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t c = blockIdx.x;
@@ -374,40 +490,24 @@ __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
     b = warp_begin(c0, tc, sp.Wn, warp + 1);
   }
   const int n = (int)(b - a);
-  const uint8_t* src = w + (size_t)a * TB;
+  const uint8_t* src = S.w + (size_t)a * TB;
   float4* wpart = reinterpret_cast<float4*>(smem);
-  /* the weights do not depend on the previous kernel: start streaming before the wait */
+  /* the weights do not depend on what came before: start streaming before the wait */
   WTile<QT> ring[D];
 #pragma unroll
-  for (int u = 0; u < D; ++u)
-    if (u < n) ring[u].load(src + (size_t)u * TB, lane, g);
+  for (int i = 0; i < D; ++i)
+    if (i < n) ring[i].load(src + (size_t)i * TB, lane, g);
   if (tid < W) wcnt[tid] = 0;
-  pdl_wait();
-  pdl_trigger();
-  if (XS) {
-    /* the CTA normalises the M input rows into its own shared-memory copy with the arithmetic
-       of rmsnorm_kernel (same bits as the separate path): threads 0-255 take rows 0, 2, ...,
-       threads 256-511 rows 1, 3, ..., each half on its own named barrier */
-    static_assert(!XS || W == 16, "the fused RMSNorm runs as two 256-thread halves");
-    __shared__ float nred[2][8];
-    __half* xs = reinterpret_cast<__half*>(smem + warp_part_bytes<QT, NT>());
-    const int K = (int)sp.tiles * WTile<QT>::TK;
-    const int hf = tid >> 8;
-    for (int m = hf; m < M; m += 2)
-      rms_row_256(nin.x + (size_t)m * nin.ldx, nin.g, K, nin.eps, xs + (size_t)m * K, nred[hf], tid & 255, 1 + hf);
-    x = xs;
-    ldx = K;
-  }
-  __syncthreads(); /* wcnt zeroed, normalised rows written */
+  if (!sync()) return;
+  const XIn xin = prep();
   if (n == 0) return;
   const __half* xr[NT];
-  activation_rows<NT>(x, xzero, ldx, M, g, t, xr);
+  activation_rows<NT>(xin.x, xzero, xin.ldx, M, g, t, xr);
   const uint32_t tiles = sp.tiles;
   const uint32_t first_strip = a / tiles;
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-
   /* the warp's part of strip s is in acc */
   auto flush = [&](uint32_t s) {
     const uint32_t s0 = s * tiles, s1 = s0 + tiles;
@@ -415,10 +515,9 @@ __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) v[nt] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
     if (s0 < a || s1 > b) {
-      /* level 1: the warps of this CTA holding part of s, in warp order */
-      const uint32_t lo = max(s0, c0), hi = min(s1, c1);
-      const uint32_t wa = warp_in_cta(tc, sp.Wn, lo - c0), wb = warp_in_cta(tc, sp.Wn, hi - 1 - c0);
-      if (wa != wb) {
+      /* the warps of this CTA holding part of s, in warp order (strips never cross CTAs) */
+      const uint32_t wa = warp_in_cta(tc, sp.Wn, s0 - c0), wb = warp_in_cta(tc, sp.Wn, s1 - 1 - c0);
+      {
         float4* mine = wpart + ((size_t)(warp * 2 + (s == first_strip ? 0 : 1)) * NT) * 32 + lane;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mine[nt * 32] = v[nt];
@@ -447,43 +546,6 @@ __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
             }
           }
         }
-      }
-      if (s0 < c0 || s1 > c1) {
-        /* level 2: the CTAs holding part of s, in CTA order */
-        float4* mine = part + ((size_t)(c * 2 + (s == c0 / tiles ? 0 : 1)) * NT) * 32 + lane;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) __stcg(mine + nt * 32, v[nt]);
-        __threadfence();
-        __syncwarp();
-        const uint32_t ca = cta_of(sp, s0), cb = cta_of(sp, s1 - 1);
-        int last = 0;
-        if (lane == 0) last = atomicAdd(&cnt[ca], 1) == (int)(cb - ca);
-        if (!__shfl_sync(0xffffffffu, last, 0)) return;
-        __threadfence();
-        const int sa = cta_begin(sp, ca) >= s0 ? 0 : 1;
-        for (uint32_t cc = ca; cc <= cb; cc += 2) {
-          float4 o[2][NT]; /* two CTAs' partials in flight at once */
-#pragma unroll
-          for (int i = 0; i < 2; ++i)
-            if (cc + i <= cb) {
-              const float4* q = part + ((size_t)((cc + i) * 2 + (cc + i == ca ? sa : 0)) * NT) * 32 + lane;
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) o[i][nt] = __ldcg(q + nt * 32);
-            }
-#pragma unroll
-          for (int i = 0; i < 2; ++i)
-            if (cc + i <= cb) {
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) {
-                if (cc + i == ca) {
-                  v[nt] = o[i][nt];
-                } else {
-                  v[nt].x += o[i][nt].x; v[nt].y += o[i][nt].y; v[nt].z += o[i][nt].z; v[nt].w += o[i][nt].w;
-                }
-              }
-            }
-        }
-        if (lane == 0) cnt[ca] = 0;
       }
     }
 #pragma unroll
@@ -529,15 +591,38 @@ __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
       ULB_GEMV_NEXT(u, j + u)
     }
 #undef ULB_GEMV_NEXT
-  if (pf_bytes && lane == 0) {
+  if (S.pf_bytes && lane == 0) {
     /* this warp's loads are all issued: start the next kernel's weights on their way to L2,
        an equal share per warp, so HBM stays busy through this kernel's tail and the next one's
        start */
     const uint64_t nw = (uint64_t)sp.G * sp.Wn;
-    const uint64_t lo = (uint64_t)pf_bytes * u / nw & ~15ull, hi = (uint64_t)pf_bytes * (u + 1) / nw & ~15ull;
-    for (uint64_t o = lo; o < hi; o += 32768) prefetch_l2_bulk(pf + o, hi - o < 32768 ? (uint32_t)(hi - o) : 32768u);
+    const uint64_t lo = (uint64_t)S.pf_bytes * u / nw & ~15ull, hi = (uint64_t)S.pf_bytes * (u + 1) / nw & ~15ull;
+    for (uint64_t o = lo; o < hi; o += 32768) prefetch_l2_bulk(S.pf + o, hi - o < 32768 ? (uint32_t)(hi - o) : 32768u);
   }
   if (kt != 0) flush(s); /* the range ends inside strip s */
+}
+
+
+/* one GEMV per launch: activations from global memory (through L1), or normalised in shared
+   memory (XS: the step's nin rows) */
+template <int QT, int NT, int EPI, bool XS>
+__global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
+    qgemv_kernel(GemvStep S, const __half* __restrict__ xzero) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint32_t wcnt[GemvCfg<QT, NT>::W];
+  __shared__ float red[72];
+  gemv_body<QT, NT, EPI, XS>(
+      S, smem, wcnt, xzero,
+      [] {
+        pdl_wait();
+        pdl_trigger();
+        return true;
+      },
+      [&]() -> XIn {
+        if (XS) return prep_norm<QT, NT>(S, smem, red);
+        __syncthreads();
+        return XIn{S.x, S.ldx};
+      });
 }
 
 /* ------------------------------------------------------------------ repack / dequant */
@@ -656,31 +741,55 @@ __global__ void dequant_q4k_kernel(const uint8_t* __restrict__ w, int tiles, int
   }
 }
 
+/* the split of a matrix over the SMs (see Split) */
+template <int QT, int NT>
+static int make_split(Ctx* c, const Tensor* w, Split* sp) {
+  const long long S = w->n_strips;
+  ULB_CHECK(S > 0 && (long long)w->tiles * S * c->n_sm < (1ll << 31), ULB_EUNSUPPORTED, "qgemv: %lld strips of %d tiles",
+            S, w->tiles);
+  sp->S = (uint32_t)S;
+  sp->G = (uint32_t)std::min<long long>(c->n_sm, S);
+  sp->tiles = (uint32_t)w->tiles;
+  sp->Wn = (uint32_t)std::min<long long>(GemvCfg<QT, NT>::W, S / sp->G * w->tiles);
+  return ULB_OK;
+}
+
+/* the next-GEMV prefetch hint of the context, as kernel arguments */
+static void take_hint(Ctx* c, GemvStep* S) {
+  S->pf = (const uint8_t*)c->pf_ptr;
+  S->pf_bytes = c->pf_ptr ? (uint32_t)(std::min<size_t>(c->pf_bytes, kPrefetchMaxBytes) & ~(size_t)15) : 0u;
+}
+
+/* shared memory of a step whose activations are staged (raw: M x K fp16; normalised: plus the
+   fp32 rows) */
+static size_t staged_bytes(int M, int K, bool norm) {
+  const size_t xs = ((size_t)M * K * sizeof(__half) + 15) / 16 * 16;
+  return xs + (norm ? (size_t)M * K * sizeof(float) : 0);
+}
+
 template <int QT, int NT, int EPI, bool XS = false>
 int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a, const NormIn& nin = NormIn()) {
   ULB_CHECK(w->K + 8 <= kZeroRowHalves, ULB_EUNSUPPORTED, "qgemv: K=%d too long", w->K);
-  const long long T = (long long)w->n_strips * w->tiles;
-  ULB_CHECK(T * c->n_sm < (1ll << 31), ULB_EUNSUPPORTED, "qgemv: %lld tiles is too many", T);
-  Split sp;
-  sp.T = (uint32_t)T;
-  sp.G = (uint32_t)std::min<long long>(c->n_sm, T);
-  sp.Wn = (uint32_t)std::max<long long>(1, std::min<long long>(GemvCfg<QT, NT>::W, T / sp.G));
-  sp.tiles = (uint32_t)w->tiles;
-  ULB_CHECK(sp.G <= (uint32_t)kGemvCounters && (size_t)sp.G * 2 * 4 * 32 <= (size_t)c->n_sm * kGemvPartPerSm,
-            ULB_EUNSUPPORTED, "qgemv: grid of %u CTAs", sp.G);
-  const size_t xs_bytes = XS ? ((size_t)M * w->K * sizeof(__half) + 15) / 16 * 16 : 0; /* normalised rows */
-  const size_t smem = warp_part_bytes<QT, NT>() + xs_bytes;
-  ULB_CHECK(smem <= kGemvSmemBytes, ULB_EUNSUPPORTED, "qgemv: %zu B of normalised rows", xs_bytes);
+  GemvStep S;
+  S.w = (const uint8_t*)w->dev;
+  ULB_TRY((make_split<QT, NT>(c, w, &S.sp)));
+  S.N = w->N;
+  S.M = M;
+  S.x = x;
+  S.ldx = ldx;
+  S.nin = nin;
+  S.ea = a;
+  take_hint(c, &S);
+  const size_t smem = warp_part_bytes<QT, NT>() + (XS ? staged_bytes(M, w->K, true) : 0);
+  ULB_CHECK(smem <= kGemvSmemBytes, ULB_EUNSUPPORTED, "qgemv: %d normalised rows of %d", M, w->K);
   static bool attr_set = false;
   if (!attr_set) {
     ULB_CUDA(cudaFuncSetAttribute(qgemv_kernel<QT, NT, EPI, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)kGemvSmemBytes));
     attr_set = true;
   }
-  const uint32_t pf_bytes = (uint32_t)std::min<size_t>(c->pf_bytes, kPrefetchMaxBytes) & ~15u;
-  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI, XS>, dim3(sp.G), dim3(GemvCfg<QT, NT>::W * 32), smem,
-                           (const uint8_t*)w->dev, sp, w->N, x, M, ldx, a, (const __half*)c->zero_row, nin,
-                           c->gemv_part, c->gemv_cnt, (const uint8_t*)c->pf_ptr, c->pf_ptr ? pf_bytes : 0u);
+  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI, XS>, dim3(S.sp.G), dim3(GemvCfg<QT, NT>::W * 32), smem, S,
+                           (const __half*)c->zero_row);
   if (e != cudaSuccess) return cuda_error(e, "qgemv launch", __FILE__, __LINE__);
   return ULB_OK;
 }

@@ -61,8 +61,7 @@ int check_device_errors(Ctx* c) {
   ULB_CUDA(cudaStreamSynchronize(c->stream));
   if (h) {
     ULB_CUDA(cudaMemsetAsync(c->dev_err, 0, sizeof(int), c->stream));
-    /* a launch that gave up may have left arrival counters of unfinished strips set */
-    ULB_CUDA(cudaMemsetAsync(c->gemv_cnt, 0, kGemvCounters * sizeof(int), c->stream));
+
     return set_error(ULB_ETIMEOUT, "a device-side bounded wait gave up (flags 0x%x); results of that launch are invalid", h);
   }
   return ULB_OK;
@@ -111,9 +110,7 @@ int ulb_init(int device, ulb_ctx** out) {
   c->c.tc_ws_floats = kTcWsFloats;
   ULB_CUDA(cudaMalloc((void**)&c->c.tc_cnt, kTcCounters * sizeof(int)));
   ULB_CUDA(cudaMemset(c->c.tc_cnt, 0, kTcCounters * sizeof(int)));
-  ULB_CUDA(cudaMalloc((void**)&c->c.gemv_part, (size_t)c->c.n_sm * kGemvPartPerSm * sizeof(float4)));
-  ULB_CUDA(cudaMalloc((void**)&c->c.gemv_cnt, kGemvCounters * sizeof(int)));
-  ULB_CUDA(cudaMemset(c->c.gemv_cnt, 0, kGemvCounters * sizeof(int)));
+
   *out = c.release();
   return ULB_OK;
 }
@@ -153,8 +150,7 @@ int ulb_destroy(ulb_ctx* ctx) {
   cudaFree(ctx->c.zero_row);
   cudaFree(ctx->c.tc_ws);
   cudaFree(ctx->c.tc_cnt);
-  cudaFree(ctx->c.gemv_part);
-  cudaFree(ctx->c.gemv_cnt);
+
   cudaStreamDestroy(ctx->c.stream);
   delete ctx;
   return ULB_OK;

@@ -82,8 +82,6 @@ struct Ctx {
   float* tc_ws = nullptr;              /* split-K partial sums of the tensor-core GEMM */
   size_t tc_ws_floats = 0;
   int* tc_cnt = nullptr;               /* kTcCounters arrival counters, zero between launches */
-  float4* gemv_part = nullptr;         /* GEMV partials of strips shared by CTAs: n_sm x kGemvPartPerSm */
-  int* gemv_cnt = nullptr;             /* kGemvCounters arrival counters, zero between launches */
   int tp_rank = 0, tp_world = 1;
   /* hint: the weights the next GEMV on the stream will read (set just before it by the
      forward pass); the GEMV launched after the hint prefetches them into L2 from its tail.
@@ -125,12 +123,9 @@ int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int e
 /* y = W . rmsnorm(x32) with the fused epilogue `epi`.  Small batches (M <= 8 rows whose fp16
    copy fits kNormSmemBytes) normalise inside the GEMV, each CTA into its own shared memory;
    otherwise rmsnorm_kernel writes x16 [M][K] first.  Both give the same bits. */
-constexpr int kNormSmemBytes = 16384;
-/* GEMV (M <= kGemvMaxRows): dynamic shared memory per CTA at most, arrival counters (one per
-   CTA), cross-CTA partial slots per SM ({first, last strip} x up to 4 n-tiles x 32 lanes) */
+constexpr int kNormSmemBytes = 65536;
+/* GEMV (M <= kGemvMaxRows): dynamic shared memory per CTA at most */
 constexpr size_t kGemvSmemBytes = 230400;
-constexpr int kGemvCounters = 16384;
-constexpr size_t kGemvPartPerSm = 2 * 4 * 32;
 /* out[s] = rmsnorm(x[row]) (row = s*sel + sel - 1 when sel > 0, else s), 256 threads a row */
 int launch_rmsnorm_sel(Ctx* c, const float* x, int ldx, const float* g, int n_out, int d, float eps, int sel,
                        __half* out, int ldo);
