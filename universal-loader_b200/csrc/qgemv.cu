@@ -9,7 +9,7 @@
  *
  * Design (B200):
  *  - one CTA of 16 warps per SM; the matrix is one stream of 16-row x K-tile tiles in layout
- *    order, split into whole strips per SM and equal contiguous ranges per warp, so every SM
+ *    order, split into whole strips per CTA and equal contiguous ranges per warp, so every SM
  *    streams the same bytes to within one strip and every warp one contiguous range;
  *  - each warp loads its tiles with 128-bit L1-bypassing loads straight into a ring of D
  *    tiles of registers (~74 KB in flight per SM); the first D tiles are requested before
@@ -319,7 +319,7 @@ __device__ __forceinline__ void tile_compute(const WTile<ULB_TYPE_Q4_K>& r, cons
 struct Split {
   uint32_t S;     /* strips in the matrix */
   uint32_t G;     /* CTAs (<= S) */
-  uint32_t Wn;    /* working warps per CTA (<= 16, <= the tiles of a CTA) */
+  uint32_t Wn;    /* working warps per CTA (<= W, <= the tiles of a CTA) */
   uint32_t tiles; /* tiles per strip */
 };
 /* first tile of CTA c (c = G gives the end of the matrix) */
@@ -358,57 +358,40 @@ struct GemvStep {
   uint32_t pf_bytes = 0;
 };
 
-/* shared-memory layout of a GEMV CTA: warp partials | activations (fp16 [M][K]) | fp32 rows
-   being normalised ([M][K]) */
+/* shared-memory layout of a GEMV CTA: warp partials | normalised activations (fp16 [M][K]) */
 template <int QT, int NT> __device__ __forceinline__ __half* smem_x(uint8_t* smem) {
   return reinterpret_cast<__half*>(smem + warp_part_bytes<QT, NT>());
 }
-__device__ __forceinline__ size_t align16(size_t b) { return (b + 15) / 16 * 16; }
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
-}
-
-/* copy rows [0, M) of `bytes_per_row` from global (row stride ld_bytes) into shared memory
-   (packed), through L2 (cp.async.cg: coherent with writes of other CTAs before a barrier) */
-__device__ __forceinline__ void stage_rows(void* dst, const void* src, size_t ld_bytes, int M, int bytes_per_row) {
-  const int per = bytes_per_row / 16, tot = per * M;
-  for (int i = threadIdx.x; i < tot; i += blockDim.x) {
-    const int m = i / per, k = i - m * per;
-    cp_async16(reinterpret_cast<uint8_t*>(dst) + (size_t)m * bytes_per_row + k * 16,
-               reinterpret_cast<const uint8_t*>(src) + (size_t)m * ld_bytes + k * 16);
-  }
-  cp_async_wait_all();
-  __syncthreads();
-}
 
 /*
- * xs[m] = fp16((x[m] * r_m) * g), r_m = 1 / sqrt(sum(x[m]^2) / d + eps) for rows m < M held in
- * shared memory (fp32 [M][d]), by all warps of the CTA at once, with exactly the arithmetic of
- * rms_row_256 (rmsnorm_kernel): row m's sum is eight virtual 256-thread blocks' per-thread fmaf
- * chains over float4 j = i*256 + vt, a warp xor tree, and the eight virtual warps in order.
- * Real warp w takes virtual warps w, w + NW, ... of the M * 8.
+ * xs[m] = fp16((x[m] * r_m) * g), r_m = 1 / sqrt(sum(x[m]^2) / d + eps) for rows m < M of x
+ * (fp32, row stride ldx, read through L2), by all warps of the CTA at once, with exactly the
+ * arithmetic of rms_row_256 (rmsnorm_kernel): row m's sum is eight virtual 256-thread blocks'
+ * per-thread fmaf chains over float4 j = i*256 + vt, a warp xor tree, and the eight virtual
+ * warps in order.  Real warp w takes virtual warps w, w + NW, ... of the M * 8.
  */
 template <int NW>
-__device__ __forceinline__ void norm_rows(const float* stg, const float* __restrict__ gw, int d, float eps, int M,
-                                          __half* xs, float* red /* [8 * 8 + 8] */) {
+__device__ __forceinline__ void norm_rows(const float* __restrict__ x, int ldx, const float* __restrict__ gw, int d,
+                                          float eps, int M, __half* xs, float* red /* [8 * 8 + 8] */) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n4 = d >> 2;
   for (int vwi = warp; vwi < M * 8; vwi += NW) {
     const int m = vwi >> 3, vt = (vwi & 7) * 32 + lane;
-    const float4* xv = reinterpret_cast<const float4*>(stg + (size_t)m * d);
+    const float4* xv = reinterpret_cast<const float4*>(x + (size_t)m * ldx);
+    float4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int j = i * 256 + vt;
+      if (j < n4) v[i] = __ldcg(xv + j);
+    }
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int j = i * 256 + vt;
       if (j < n4) {
-        const float4 v = xv[j];
-        ss = __fmaf_rn(v.x, v.x, ss);
-        ss = __fmaf_rn(v.y, v.y, ss);
-        ss = __fmaf_rn(v.z, v.z, ss);
-        ss = __fmaf_rn(v.w, v.w, ss);
+        ss = __fmaf_rn(v[i].x, v[i].x, ss);
+        ss = __fmaf_rn(v[i].y, v[i].y, ss);
+        ss = __fmaf_rn(v[i].z, v[i].z, ss);
+        ss = __fmaf_rn(v[i].w, v[i].w, ss);
       }
     }
 #pragma unroll
@@ -428,7 +411,7 @@ __device__ __forceinline__ void norm_rows(const float* stg, const float* __restr
   for (int idx = threadIdx.x; idx < M * n4; idx += NW * 32) {
     const int m = idx / n4, j = idx - m * n4;
     const float r = red[64 + m];
-    const float4 v = reinterpret_cast<const float4*>(stg + (size_t)m * d)[j];
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(x + (size_t)m * ldx) + j);
     const float4 gg = __ldg(gv + j);
     __half2* o2 = reinterpret_cast<__half2*>(xs + (size_t)m * d) + 2 * j;
     o2[0] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v.x, r), gg.x)),
@@ -450,9 +433,7 @@ template <int QT, int NT>
 __device__ __forceinline__ XIn prep_norm(const GemvStep& S, uint8_t* smem, float* red) {
   const int K = (int)S.sp.tiles * WTile<QT>::TK;
   __half* xs = smem_x<QT, NT>(smem);
-  float* stg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + align16((size_t)S.M * K * sizeof(__half)));
-  stage_rows(stg, S.nin.x, (size_t)S.nin.ldx * sizeof(float), S.M, K * (int)sizeof(float));
-  norm_rows<GemvCfg<QT, NT>::W>(stg, S.nin.g, K, S.nin.eps, S.M, xs, red);
+  norm_rows<GemvCfg<QT, NT>::W>(S.nin.x, S.nin.ldx, S.nin.g, K, S.nin.eps, S.M, xs, red);
   return XIn{xs, K};
 }
 
@@ -502,7 +483,8 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
   const XIn xin = prep();
   if (n == 0) return;
   const __half* xr[NT];
-  activation_rows<NT>(xin.x, xzero, xin.ldx, M, g, t, xr);
+  /* tokens >= M only feed MMA columns the epilogue drops: in shared memory they may read row 0 */
+  activation_rows<NT>(xin.x, XS ? xin.x : xzero, xin.ldx, M, g, t, xr);
   const uint32_t tiles = sp.tiles;
   const uint32_t first_strip = a / tiles;
   float acc[NT][4];
@@ -603,8 +585,8 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
 }
 
 
-/* one GEMV per launch: activations from global memory (through L1), or normalised in shared
-   memory (XS: the step's nin rows) */
+/* one GEMV per launch: XS, the activation rows normalised from the step's nin rows into
+   shared memory; otherwise read from global memory through L1 */
 template <int QT, int NT, int EPI, bool XS>
 __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
     qgemv_kernel(GemvStep S, const __half* __restrict__ xzero) {
@@ -760,12 +742,8 @@ static void take_hint(Ctx* c, GemvStep* S) {
   S->pf_bytes = c->pf_ptr ? (uint32_t)(std::min<size_t>(c->pf_bytes, kPrefetchMaxBytes) & ~(size_t)15) : 0u;
 }
 
-/* shared memory of a step whose activations are staged (raw: M x K fp16; normalised: plus the
-   fp32 rows) */
-static size_t staged_bytes(int M, int K, bool norm) {
-  const size_t xs = ((size_t)M * K * sizeof(__half) + 15) / 16 * 16;
-  return xs + (norm ? (size_t)M * K * sizeof(float) : 0);
-}
+/* shared memory of the normalised activation rows: M x K fp16 */
+static size_t norm_bytes(int M, int K) { return ((size_t)M * K * sizeof(__half) + 15) / 16 * 16; }
 
 template <int QT, int NT, int EPI, bool XS = false>
 int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a, const NormIn& nin = NormIn()) {
@@ -780,7 +758,7 @@ int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const Epi
   S.nin = nin;
   S.ea = a;
   take_hint(c, &S);
-  const size_t smem = warp_part_bytes<QT, NT>() + (XS ? staged_bytes(M, w->K, true) : 0);
+  const size_t smem = warp_part_bytes<QT, NT>() + (XS ? norm_bytes(M, w->K) : 0);
   ULB_CHECK(smem <= kGemvSmemBytes, ULB_EUNSUPPORTED, "qgemv: %d normalised rows of %d", M, w->K);
   static bool attr_set = false;
   if (!attr_set) {

@@ -11,6 +11,8 @@
 #include <cstdint>
 #include <cstdio>
 #include <map>
+#include <mutex>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -164,9 +166,26 @@ size_t sample_scratch_bytes(int rows, int V);
 size_t accept_scratch_bytes(int B, int k, int V);
 
 /* ------------------------------------------------------------------ PDL launch helper */
+/*
+ * Every kernel of the library asks for one shared-memory carveout: an SM whose L1 / shared
+ * memory split changes between consecutive kernels first drains, which costs about a
+ * microsecond per change; with one split throughout there is none.  72% of the 228 KB is the
+ * 164 KB split: enough for every kernel's shared memory, and ~90 KB of L1 for the GEMV's
+ * activation rows.  Set once per kernel, on its first launch.
+ */
+constexpr int kSharedCarveoutPct = 72;
+inline void prefer_max_shared(const void* kern) {
+  static std::mutex mu;
+  static std::set<const void*> done;
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.insert(kern).second)
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, kSharedCarveoutPct);
+}
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(Ctx* c, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
                             Args&&... args) {
+  prefer_max_shared((const void*)kern);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
