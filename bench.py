@@ -36,8 +36,8 @@ DRAFT = dict(n_layer=22, d_model=2048, n_head=32, n_head_kv=4, d_ff=5632, n_voca
              rope_base=1e4, wtype="q4_0", seed=2, ctx_len=2048, name="tinyllama-1.1b-arch-q4_0-s2")
 PROMPT_LEN, K_SPEC, NEW_TOKENS = 512, 5, 256
 # ncu (dram__bytes_read.sum + dram__bytes_write.sum) / algorithmic bytes of one fused Q4_0 GEMV
-# launch (N=11008, K=4096, M=5: 25.44 MB measured vs 25.62 MB algorithmic)
-QGEMV_TRAFFIC_RATIO = 0.993
+# launch (N=11008, K=4096, M=5: 25.48 MB measured vs 25.62 MB algorithmic)
+QGEMV_TRAFFIC_RATIO = 0.994
 WORKLOAD = ("C2: Llama-2-7B-arch Q4_0 target + TinyLlama-1.1B-arch Q4_0 draft, B=1 per GPU, "
             "prompt 512, k=5, 256 new tokens, T=0")
 
@@ -394,7 +394,7 @@ def run_ours(args):
                      "traffic_note": "bytes per average launch: algorithmic bytes x %.3f, the DRAM read+write / "
                                      "algorithmic ratio of an ncu capture of the Q4_0 11008x4096 M=5 launch "
                                      "(no re-reads)" % QGEMV_TRAFFIC_RATIO,
-                     "kernel": "qgemv_q40_kernel<NT=1> (fused Q4_0 dequant-GEMV, 7B verify shapes, M=6)",
+                     "kernel": "qgemv_kernel<Q4_0, NT=1> (warp-streamed fused Q4_0 dequant-GEMV, 7B verify shapes, M=6)",
                      "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
                      "shapes": rl["shapes"]},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
