@@ -9,7 +9,7 @@
  * blocks, KV read from the cache.
  *
  * Tensor-core flash decoding (B200, mma.sync.m16n8k16 with fp32 accumulate):
- *  - grid = (16-query tile x split of 256 keys, kv head, sequence); 4 warps per CTA, warp w
+ *  - grid = (16-query tile, kv head, split of 256 keys x sequence); 4 warps per CTA, warp w
  *    owns keys [split*256 + 64w, +64): it stages that K / V block in shared memory with
  *    cp.async (XOR-swizzled 16-byte chunks, so ldmatrix reads are conflict-free), computes
  *    S = Q.K^T with Q split into hi + lo fp16 parts (two MMAs, ~22 bits of q kept), masks
@@ -42,7 +42,7 @@ constexpr int QT = 16;              /* queries per CTA: one m16 tile */
 constexpr float kLog2e = 1.44269504088896340736f;
 
 struct AttnParams {
-  int H, Hkv, hd, cap, G, rps, n_mt, max_splits, ldq, n_seq;
+  int H, Hkv, hd, cap, G, rps, n_mt, max_splits, ldq, n_seq, n_groups;
   float scale2; /* softmax scale x log2(e): scores live in the base-2 domain */
 };
 
@@ -100,7 +100,9 @@ __global__ void __launch_bounds__(AW * 32, 1)
   constexpr int PST = HD + 2; /* floats per query of a partial: m, l, o[HD] */
   extern __shared__ __align__(128) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const int mt = blockIdx.x % p.n_mt, split = blockIdx.x / p.n_mt, kvh = blockIdx.y, gi = blockIdx.z;
+  /* grid (tile, kv head, split x sequence group): the launch order runs through every head's
+     split 0 first, so the CTAs with keys start before those past the sequences' ends */
+  const int mt = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z / p.n_groups, gi = blockIdx.z % p.n_groups;
   /* Rows' sequences and positions, and the cache rows before this forward's, were written
      before the previous kernel (the QKV GEMV) started: they are read, and those K / V rows
      requested, before griddepcontrol.wait; the rows this forward appended wait for it. */
@@ -364,6 +366,7 @@ void attn_geometry(const ulb_attn_desc* d, int M, int rps, int max_pos, AttnPara
   p->scale2 = d->scale * kLog2e;
   p->n_seq = d->n_seq;
   *n_groups = M / rps;
+  p->n_groups = *n_groups;
 }
 
 size_t attn_smem(int hd) {
@@ -410,7 +413,9 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
                                   (int)attn_smem(128)));
     attr_set = true;
   }
-  dim3 grid(p.n_mt * p.max_splits, p.Hkv, ng), block(AW * 32);
+  ULB_CHECK((long long)ng * p.max_splits <= 65535, ULB_EUNSUPPORTED, "attention: %d sequences x %d splits", ng,
+            p.max_splits);
+  dim3 grid(p.n_mt, p.Hkv, ng * p.max_splits), block(AW * 32);
   cudaError_t e = d->head_dim == 64
                       ? launch_k(c, attn_mma_kernel<64>, grid, block, attn_smem(64), p, q, k, v, row_seq, row_pos,
                                  out, scratch, counters)
