@@ -307,47 +307,43 @@ __global__ void __launch_bounds__(AW * 32, 1)
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  /* merge of the splits in split order: (max, sum) of every (query, split) staged first */
-  float* msm = part;                   /* [QT][MAXSPLIT] max, then weight */
-  float* lsm = part + QT * MAXSPLIT;   /* [QT][MAXSPLIT] sum               */
-  float* Lq = part + 2 * QT * MAXSPLIT; /* [QT]                             */
-  for (int idx = tid; idx < QT * n_splits; idx += AW * 32) {
-    const int qi = idx / n_splits, c = idx % n_splits;
-    msm[qi * MAXSPLIT + c] = __ldcg(gbase + (size_t)c * QT * PST + (size_t)qi * PST);
-    lsm[qi * MAXSPLIT + c] = __ldcg(gbase + (size_t)c * QT * PST + (size_t)qi * PST + 1);
-  }
-  __syncthreads();
-  for (int qi = tid; qi < QT; qi += AW * 32) {
-    float M = -INFINITY;
-    for (int c = 0; c < n_splits; ++c) M = fmaxf(M, msm[qi * MAXSPLIT + c]);
-    float L = 0.f;
-    for (int c = 0; c < n_splits; ++c) {
-      const float mc = msm[qi * MAXSPLIT + c];
-      const float w = mc == -INFINITY ? 0.f : exp2f(mc - M);
-      msm[qi * MAXSPLIT + c] = w;
-      L = __fmaf_rn(lsm[qi * MAXSPLIT + c], w, L);
-    }
-    Lq[qi] = L;
-  }
-  __syncthreads();
+  /* merge of the splits in split order, eight splits per memory round trip: a thread owns one
+     (query, output pair) and loads the splits' (max, sum, output pair) together; across
+     chunks of eight the running sums are rescaled to the new max */
   for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
     const int qi = it / (HD / 2), d2 = it % (HD / 2);
-    float ox = 0.f, oy = 0.f;
+    float M = -INFINITY, L = 0.f, ox = 0.f, oy = 0.f;
     for (int c0 = 0; c0 < n_splits; c0 += 8) {
+      float mc[8], lc[8];
       float2 oc[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (c0 + u < n_splits)
-          oc[u] = __ldcg(reinterpret_cast<const float2*>(gbase + (size_t)(c0 + u) * QT * PST + (size_t)qi * PST + 2) + d2);
+        if (c0 + u < n_splits) {
+          const float* gp = gbase + (size_t)(c0 + u) * QT * PST + (size_t)qi * PST;
+          mc[u] = __ldcg(gp);
+          lc[u] = __ldcg(gp + 1);
+          oc[u] = __ldcg(reinterpret_cast<const float2*>(gp + 2) + d2);
+        }
+      float Mn = M;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + u < n_splits) Mn = fmaxf(Mn, mc[u]);
+      if (c0 > 0 && Mn != M) { /* rescale what the earlier chunks summed */
+        const float r = M == -INFINITY ? 0.f : exp2f(M - Mn);
+        L *= r;
+        ox *= r;
+        oy *= r;
+      }
+      M = Mn;
 #pragma unroll
       for (int u = 0; u < 8; ++u)
         if (c0 + u < n_splits) {
-          const float w = msm[qi * MAXSPLIT + c0 + u];
+          const float w = mc[u] == -INFINITY ? 0.f : exp2f(mc[u] - M);
+          L = __fmaf_rn(lc[u], w, L);
           ox = __fmaf_rn(oc[u].x, w, ox);
           oy = __fmaf_rn(oc[u].y, w, oy);
         }
     }
-    const float L = Lq[qi];
     const float inv = L > 0.f ? 1.0f / L : 0.f;
     out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
   }
@@ -372,8 +368,7 @@ void attn_geometry(const ulb_attn_desc* d, int M, int rps, int max_pos, AttnPara
 size_t attn_smem(int hd) {
   const size_t kv = (size_t)AW * 2 * KB * hd * sizeof(__half);
   const size_t part = (size_t)AW * QT * (hd + 2) * sizeof(float);
-  const size_t merge = ((size_t)2 * QT * MAXSPLIT + QT) * sizeof(float);
-  return std::max(kv, std::max(part, merge));
+  return std::max(kv, part);
 }
 
 }  // namespace
