@@ -204,6 +204,9 @@ def _attn_case(ctx, H, Hkv, hd, S, rps, positions, seed):
     (8, 8, 64, 3, 5, [[10, 11, 12, 13, 14], [127, 128, 129, 130, 131], [0, 1, 2, 3, 4]]),
     (32, 8, 128, 2, 9, [list(range(300, 309)), list(range(4000, 4009))]),  # Llama-3 GQA k=8
     (8, 8, 64, 1, 64, [list(range(0, 64))]),                       # prefill chunk
+    # three sequences with 2, 4 and 1 live key splits of a 4-split cache: thread-block clusters
+    # whose CTAs past a sequence's end only join the cluster barriers
+    (8, 2, 64, 3, 4, [list(range(300, 304)), list(range(1000, 1004)), list(range(5, 9))]),
 ])
 def test_attention_matches_oracle(ctx, H, Hkv, hd, S, rps, positions):
     got, want = _attn_case(ctx, H, Hkv, hd, S, rps, positions, seed=H + hd + S)

@@ -89,7 +89,28 @@ __device__ __forceinline__ int swz(int j, int c) { return c ^ (j & 7); }
  * splits in split order.  Queries: index qi = r * G + j is row r of the sequence, head
  * kv_head * G + j.
  */
-template <int HD>
+/* all threads of every CTA of the cluster: the cluster's shared-memory writes are visible after */
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+/* a float (pair) of the shared memory of CTA `rank` of the cluster, at this CTA's offset p */
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_cluster(uint32_t a) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 ld_cluster2(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a) : "memory");
+  return v;
+}
+
+template <int HD, bool CL>
 __global__ void __launch_bounds__(AW * 32, 1)
     attn_mma_kernel(AttnParams p, const float* __restrict__ q, const __half* __restrict__ kc,
                     const __half* __restrict__ vc, const int* __restrict__ row_seq, const int* __restrict__ row_pos,
@@ -100,9 +121,13 @@ __global__ void __launch_bounds__(AW * 32, 1)
   constexpr int PST = HD + 2; /* floats per query of a partial: m, l, o[HD] */
   extern __shared__ __align__(128) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  /* grid (tile, kv head, split x sequence group): the launch order runs through every head's
-     split 0 first, so the CTAs with keys start before those past the sequences' ends */
-  const int mt = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z / p.n_groups, gi = blockIdx.z % p.n_groups;
+  /* grid (tile, kv head, split x sequence group).  Without clusters the launch order runs
+     through every head's split 0 first, so the CTAs with keys start before those past the
+     sequences' ends; with clusters (CL) the max_splits CTAs of one (tile, head, group) are one
+     cluster, split = the CTA's rank in it. */
+  const int mt = blockIdx.x, kvh = blockIdx.y;
+  const int split = CL ? blockIdx.z % p.max_splits : blockIdx.z / p.n_groups;
+  const int gi = CL ? blockIdx.z / p.max_splits : blockIdx.z % p.n_groups;
   /* Rows' sequences and positions, and the cache rows before this forward's, were written
      before the previous kernel (the QKV GEMV) started: they are read, and those K / V rows
      requested, before griddepcontrol.wait; the rows this forward appended wait for it. */
@@ -126,8 +151,16 @@ __global__ void __launch_bounds__(AW * 32, 1)
   }
   last_pos = max(0, min(last_pos, p.cap - 1)); /* positions past the cache never index it */
   const int n_splits = last_pos / SPLITK + 1;
-  if (split >= n_splits) return;
-  if ((unsigned)seq >= (unsigned)p.n_seq) return;
+  /* n_splits and seq are the same for every CTA of a cluster */
+  const bool live = split < n_splits && (unsigned)seq < (unsigned)p.n_seq;
+  if (!live) {
+    /* a cluster's CTAs all pass its two barriers (see the end of the kernel) */
+    if (CL) {
+      cluster_sync();
+      cluster_sync();
+    }
+    return;
+  }
 
   const int kb0 = (split * AW + warp) * KB;
   const int nk = min(KB, last_pos + 1 - kb0); /* keys of this warp's block (may be <= 0) */
@@ -270,6 +303,8 @@ __global__ void __launch_bounds__(AW * 32, 1)
   };
   const int ti = (gi * p.n_mt + mt) * p.Hkv + kvh;
   float* gbase = scratch + (size_t)ti * p.max_splits * QT * PST;
+  /* CL: this split's partial stays in this CTA's shared memory, after the warp partials */
+  float* cpart = part + (size_t)AW * QT * PST;
   for (int it = tid; it < QT * (HD / 2); it += AW * 32) {
     const int qi = it / (HD / 2), d2 = it % (HD / 2);
     float M = -INFINITY;
@@ -290,7 +325,7 @@ __global__ void __launch_bounds__(AW * 32, 1)
         out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
       }
     } else {
-      float* gp = gbase + (size_t)split * QT * PST + (size_t)qi * PST;
+      float* gp = (CL ? cpart : gbase + (size_t)split * QT * PST) + (size_t)qi * PST;
       if (d2 == 0) {
         gp[0] = M;
         gp[1] = L;
@@ -298,6 +333,44 @@ __global__ void __launch_bounds__(AW * 32, 1)
       gp[2 + 2 * d2] = ox;
       gp[3 + 2 * d2] = oy;
     }
+  }
+  if (CL) {
+    /* the splits' partials merge through distributed shared memory: once every CTA of the
+       cluster has written its partial, split 0 reads them in split order (the arithmetic of
+       the global merge below), and the second barrier keeps the others' shared memory alive
+       until it has */
+    cluster_sync();
+    if (split == 0 && n_splits > 1) {
+      for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
+        const int qi = it / (HD / 2), d2 = it % (HD / 2);
+        float mc[8], lc[8];
+        float2 oc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (u < n_splits) {
+            const float* gp = cpart + (size_t)qi * PST;
+            mc[u] = ld_cluster(cluster_addr(gp, u));
+            lc[u] = ld_cluster(cluster_addr(gp + 1, u));
+            oc[u] = ld_cluster2(cluster_addr(gp + 2 + 2 * d2, u));
+          }
+        float M = -INFINITY, L = 0.f, ox = 0.f, oy = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (u < n_splits) M = fmaxf(M, mc[u]);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (u < n_splits) {
+            const float w = mc[u] == -INFINITY ? 0.f : exp2f(mc[u] - M);
+            L = __fmaf_rn(lc[u], w, L);
+            ox = __fmaf_rn(oc[u].x, w, ox);
+            oy = __fmaf_rn(oc[u].y, w, oy);
+          }
+        const float inv = L > 0.f ? 1.0f / L : 0.f;
+        out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
+      }
+    }
+    cluster_sync();
+    return;
   }
   if (n_splits == 1) return;
   __threadfence();
@@ -367,11 +440,69 @@ void attn_geometry(const ulb_attn_desc* d, int M, int rps, int max_pos, AttnPara
 
 size_t attn_smem(int hd) {
   const size_t kv = (size_t)AW * 2 * KB * hd * sizeof(__half);
-  const size_t part = (size_t)AW * QT * (hd + 2) * sizeof(float);
+  const size_t part = (size_t)(AW + 1) * QT * (hd + 2) * sizeof(float); /* warp partials + the split's */
   return std::max(kv, part);
 }
 
 }  // namespace
+
+/*
+ * With 2..8 splits (a cache of at most 2048 positions) the splits of one (tile, head, group)
+ * run as one thread-block cluster and merge through distributed shared memory; the cluster
+ * form is used once the device reports it can co-schedule such clusters.  Longer caches merge
+ * through global memory (last CTA of the splits).
+ */
+template <int HD>
+cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, const __half* k, const __half* v,
+                        const int* row_seq, const int* row_pos, __half* out, float* scratch, int* counters) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  static int cl_ok[9] = {0}; /* max_splits -> cluster form schedulable */
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)attn_smem(HD));
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)attn_smem(HD));
+    for (int s = 2; s <= 8 && attr_err == cudaSuccess; ++s) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, 1, s);
+      cfg.blockDim = dim3(AW * 32);
+      cfg.dynamicSmemBytes = attn_smem(HD);
+      cudaLaunchAttribute a[1];
+      a[0].id = cudaLaunchAttributeClusterDimension;
+      a[0].val.clusterDim.x = 1;
+      a[0].val.clusterDim.y = 1;
+      a[0].val.clusterDim.z = s;
+      cfg.attrs = a;
+      cfg.numAttrs = 1;
+      int n = 0;
+      cl_ok[s] = cudaOccupancyMaxActiveClusters(&n, attn_mma_kernel<HD, true>, &cfg) == cudaSuccess && n > 0;
+      cudaGetLastError();
+    }
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  const bool cl = p.max_splits >= 2 && p.max_splits <= 8 && cl_ok[p.max_splits];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.n_mt, p.Hkv, ng * p.max_splits);
+  cfg.blockDim = dim3(AW * 32);
+  cfg.dynamicSmemBytes = attn_smem(HD);
+  cfg.stream = c->stream;
+  cudaLaunchAttribute a[2];
+  a[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a[0].val.programmaticStreamSerializationAllowed = c->pdl ? 1 : 0;
+  a[1].id = cudaLaunchAttributeClusterDimension;
+  a[1].val.clusterDim.x = 1;
+  a[1].val.clusterDim.y = 1;
+  a[1].val.clusterDim.z = cl ? p.max_splits : 1;
+  cfg.attrs = a;
+  cfg.numAttrs = cl ? 2 : 1;
+  auto kern = cl ? attn_mma_kernel<HD, true> : attn_mma_kernel<HD, false>;
+  prefer_max_shared((const void*)kern);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, q, k, v, row_seq, row_pos, out, scratch, counters);
+  if (e == cudaSuccess) ++c->launches;
+  return e;
+}
 
 size_t attention_scratch_floats(const ulb_attn_desc* d, int M, int rps, int max_pos, int* n_counters) {
   AttnParams p;
@@ -401,21 +532,10 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
   const size_t need = attention_scratch_floats(d, M, rps, d->capacity - 1, &need_c);
   ULB_CHECK(p.max_splits == 1 || (scratch_floats >= need && n_counters >= need_c), ULB_EINVAL,
             "attention: scratch %zu floats / %d counters, need %zu / %d", scratch_floats, n_counters, need, need_c);
-  static bool attr_set = false;
-  if (!attr_set) {
-    ULB_CUDA(cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(64)));
-    ULB_CUDA(cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)attn_smem(128)));
-    attr_set = true;
-  }
   ULB_CHECK((long long)ng * p.max_splits <= 65535, ULB_EUNSUPPORTED, "attention: %d sequences x %d splits", ng,
             p.max_splits);
-  dim3 grid(p.n_mt, p.Hkv, ng * p.max_splits), block(AW * 32);
-  cudaError_t e = d->head_dim == 64
-                      ? launch_k(c, attn_mma_kernel<64>, grid, block, attn_smem(64), p, q, k, v, row_seq, row_pos,
-                                 out, scratch, counters)
-                      : launch_k(c, attn_mma_kernel<128>, grid, block, attn_smem(128), p, q, k, v, row_seq, row_pos,
-                                 out, scratch, counters);
+  cudaError_t e = d->head_dim == 64 ? launch_attn<64>(c, p, ng, q, k, v, row_seq, row_pos, out, scratch, counters)
+                                    : launch_attn<128>(c, p, ng, q, k, v, row_seq, row_pos, out, scratch, counters);
   if (e != cudaSuccess) return cuda_error(e, "attention launch", __FILE__, __LINE__);
   return ULB_OK;
 }
