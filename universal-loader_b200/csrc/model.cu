@@ -199,17 +199,20 @@ static int tp_reduce_add(Model* m, int M) {
   return ULB_OK;
 }
 
-/* final RMSNorm (of every row, or of each sequence's last row) and the LM head */
+/* final RMSNorm (of every row, or of each sequence's last row) and the LM head, one kernel for
+   up to 8 rows */
 static int forward_head(Model* m, int M, int rps, int logits_mode, float* logits, int ld) {
   Ctx* c = m->c;
   const ulb_model_desc& d = m->d;
   const int n_out = logits_mode == 1 ? M / rps : M;
-  ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, m->out_norm, n_out, d.d_model, d.rms_eps,
-                             logits_mode == 1 ? rps : 0, m->x16, d.d_model));
+  /* the rows the logits come from: every row, or the last of each sequence's rps (a strided
+     view of the residual stream) */
+  const int sel = logits_mode == 1 ? rps : 1;
   EpiArgs o;
   o.y = logits;
   o.ldy = ld;
-  return launch_qgemv(c, &m->out, m->x16, n_out, d.d_model, EPI_STORE, o);
+  return launch_qgemv_rms(c, &m->out, m->x + (size_t)(sel - 1) * d.d_model, sel * d.d_model, m->out_norm, d.rms_eps,
+                          m->x16, n_out, EPI_STORE, o);
 }
 
 int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos, int logits_mode,

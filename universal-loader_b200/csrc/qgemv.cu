@@ -175,23 +175,25 @@ __device__ __forceinline__ uint4 ldw(const uint8_t* p) {
  *   Q4_K: 4 x 16 B of nibble words + the 16 B meta rows of g and g + 8.
  */
 template <int QT> struct WTile;
+/* load(): pw = the tile + lane * 16 (the lane's nibble words), ps = the tile + MO + g * 16 (its
+   scale / meta row); both advance by TB from tile to tile */
 template <> struct WTile<ULB_TYPE_Q4_0> {
-  static constexpr int TB = kQ40TileBytes, TK = kQ40TileK;
+  static constexpr int TB = kQ40TileBytes, TK = kQ40TileK, MO = 1024;
   uint4 w[2], sc;
-  __device__ __forceinline__ void load(const uint8_t* tp, int lane, int g) {
-    w[0] = ldw(tp + lane * 16);
-    w[1] = ldw(tp + 512 + lane * 16);
-    sc = ldw(tp + 1024 + g * 16);
+  __device__ __forceinline__ void load(const uint8_t* pw, const uint8_t* ps) {
+    w[0] = ldw(pw);
+    w[1] = ldw(pw + 512);
+    sc = ldw(ps);
   }
 };
 template <> struct WTile<ULB_TYPE_Q4_K> {
-  static constexpr int TB = kQ4KTileBytes, TK = kQ4KTileK;
+  static constexpr int TB = kQ4KTileBytes, TK = kQ4KTileK, MO = 2048;
   uint4 w[4], mg, mg8;
-  __device__ __forceinline__ void load(const uint8_t* tp, int lane, int g) {
+  __device__ __forceinline__ void load(const uint8_t* pw, const uint8_t* ps) {
 #pragma unroll
-    for (int p = 0; p < 4; ++p) w[p] = ldw(tp + p * 512 + lane * 16);
-    mg = ldw(tp + 2048 + g * 16);
-    mg8 = ldw(tp + 2048 + (g + 8) * 16);
+    for (int p = 0; p < 4; ++p) w[p] = ldw(pw + p * 512);
+    mg = ldw(ps);
+    mg8 = ldw(ps + 8 * 16);
   }
 };
 
@@ -477,7 +479,7 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
   WTile<QT> ring[D];
 #pragma unroll
   for (int i = 0; i < D; ++i)
-    if (i < n) ring[i].load(src + (size_t)i * TB, lane, g);
+    if (i < n) ring[i].load(src + (size_t)i * TB + lane * 16, src + (size_t)i * TB + WTile<QT>::MO + g * 16);
   if (tid < W) wcnt[tid] = 0;
   if (!sync()) return;
   const XIn xin = prep();
@@ -540,12 +542,15 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
   const __half* xp[NT]; /* activations of the current tile */
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) xp[nt] = xr[nt] + kt * TK;
-  const uint8_t* wp = src + (size_t)D * TB; /* the refill of the tile being computed */
+  /* the lane's addresses in the refill of the tile being computed */
+  const uint8_t* wp = src + (size_t)D * TB + lane * 16;
+  const uint8_t* wps = src + (size_t)D * TB + WTile<QT>::MO + g * 16;
   /* after tile j: refill its ring slot with tile j + D, step the activations, finish the strip */
 #define ULB_GEMV_NEXT(u, j)                                                                  \
   {                                                                                          \
-    if ((j) + D < n) ring[u].load(wp, lane, g);                                              \
+    if ((j) + D < n) ring[u].load(wp, wps);                                                  \
     wp += TB;                                                                                \
+    wps += TB;                                                                               \
     if (++kt == tiles) {                                                                     \
       flush(s);                                                                              \
       _Pragma("unroll") for (int nt = 0; nt < NT; ++nt) {                                    \
@@ -835,7 +840,7 @@ int launch_qgemv_rms(Ctx* c, const Tensor* w, const float* x32, int ldx32, const
   if (M == 0) return ULB_OK;
   const bool fuse = M <= 8 && (size_t)M * w->K * sizeof(__half) <= (size_t)kNormSmemBytes && w->K <= 8192 &&
                     w->K % 8 == 0 && ldx32 % 4 == 0 && ((uintptr_t)x32 & 15) == 0 && ((uintptr_t)g & 15) == 0 &&
-                    (epi == EPI_QKV || epi == EPI_SWIGLU);
+                    (epi == EPI_QKV || epi == EPI_SWIGLU || epi == EPI_STORE);
   if (!fuse) {
     ULB_TRY(launch_rmsnorm_sel(c, x32, ldx32, g, M, w->K, eps, 0, x16, w->K));
     return launch_qgemv(c, w, x16, M, w->K, epi, a);
@@ -850,9 +855,12 @@ int launch_qgemv_rms(Ctx* c, const Tensor* w, const float* x32, int ldx32, const
   if (epi == EPI_QKV)
     rc = q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_QKV, true>(c, w, nullptr, M, w->K, a, nin)
              : launch_q<ULB_TYPE_Q4_K, 1, EPI_QKV, true>(c, w, nullptr, M, w->K, a, nin);
-  else
+  else if (epi == EPI_SWIGLU)
     rc = q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_SWIGLU, true>(c, w, nullptr, M, w->K, a, nin)
              : launch_q<ULB_TYPE_Q4_K, 1, EPI_SWIGLU, true>(c, w, nullptr, M, w->K, a, nin);
+  else
+    rc = q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_STORE, true>(c, w, nullptr, M, w->K, a, nin)
+             : launch_q<ULB_TYPE_Q4_K, 1, EPI_STORE, true>(c, w, nullptr, M, w->K, a, nin);
   c->pf_ptr = nullptr;
   c->pf_bytes = 0;
   return rc;
