@@ -41,8 +41,10 @@ def _run(ctx, fn_name, desc, arrays, M, rps, out_elems):
 
 
 @pytest.mark.parametrize("H,Hkv,hd,S,rps,positions", [
-    (32, 32, 128, 1, 6, [[634, 635, 636, 637, 638, 639]]),            # 7B verify rows, 10 key splits
-    (32, 4, 64, 2, 2, [[700, 701], [130, 131]]),                      # TinyLlama-like GQA, ragged
+    # caches past 2048 positions: more than 8 key splits, which merge through the scratch
+    # (shorter caches merge inside a thread-block cluster and use none)
+    (32, 32, 128, 1, 6, [[2434, 2435, 2436, 2437, 2438, 2439]]),      # 7B verify rows, 10 key splits
+    (32, 4, 64, 2, 2, [[2600, 2601], [130, 131]]),                    # TinyLlama-like GQA, ragged
 ])
 def test_noalloc_attention_matches_allocating_entry_point(ctx, H, Hkv, hd, S, rps, positions):
     import ulb_capi as U
