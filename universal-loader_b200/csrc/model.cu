@@ -234,12 +234,17 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     a.q = m->qb; a.ldq = m->nq; a.kc = kc; a.vc = vc;
     a.nq = m->nq; a.nkv = m->nkv; a.hd = d.head_dim; a.cap = kv->cap; a.n_head_kv = d.n_head_kv; a.n_seq = kv->n_seq;
     a.row_seq = seq; a.row_pos = pos; a.rope = kv->rope;
-    /* each GEMV's tail prefetches the weights of the one after it into L2 */
-    auto hint = [c](const Tensor& t) {
-      c->pf_ptr = t.dev;
-      c->pf_bytes = t.bytes;
+    /* GEMV tails prefetch the weights of the GEMVs to come into L2 (the hint is set just
+       before the launch whose tail issues it) */
+    auto hint = [c](const Tensor* t, const Tensor* t2 = nullptr) {
+      c->pf_ptr = t ? t->dev : nullptr;
+      c->pf_bytes = t ? t->bytes : 0;
+      c->pf2_ptr = t2 ? t2->dev : nullptr;
+      c->pf2_bytes = t2 ? t2->bytes : 0;
     };
-    hint(L.o);
+    /* the QKV GEMV's tail prefetches attn_output and ffn_gate_up, which land in L2 while the
+       attention kernel (which reads only the KV cache) leaves HBM mostly idle */
+    hint(&L.o, &L.gateup);
     ULB_TRY(launch_qgemv_rms(c, &L.qkv, m->x, d.d_model, L.attn_norm, d.rms_eps, m->x16, M, EPI_QKV, a));
     ULB_TRY(launch_attention(c, &ad, m->qb, m->nq, kc, vc, seq, pos, M, rps, m->att, kv->attn_scratch,
                              kv->attn_counters, kv->attn_floats, kv->n_counters));
@@ -250,14 +255,14 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     EpiArgs pr;
     pr.y = m->tp_part; pr.ldy = d.d_model;
     const bool tp = m->tp_world > 1;
-    hint(L.gateup);
+    hint(&L.down);
     ULB_TRY(launch_qgemv(c, &L.o, m->att, M, m->nq, tp ? EPI_STORE : EPI_RESID, tp ? pr : r));
     if (tp) ULB_TRY(tp_reduce_add(m, M));
     EpiArgs s;
     s.h = m->h16; s.ldh = d.d_ff;
-    hint(L.down);
+    hint(l + 1 < d.n_layer ? &m->layers[l + 1].qkv : &m->out);
     ULB_TRY(launch_qgemv_rms(c, &L.gateup, m->x, d.d_model, L.ffn_norm, d.rms_eps, m->x16, M, EPI_SWIGLU, s));
-    hint(l + 1 < d.n_layer ? m->layers[l + 1].qkv : m->out);
+    hint(nullptr);
     ULB_TRY(launch_qgemv(c, &L.down, m->h16, M, d.d_ff, tp ? EPI_STORE : EPI_RESID, tp ? pr : r));
     if (tp) ULB_TRY(tp_reduce_add(m, M));
   }

@@ -356,8 +356,11 @@ struct GemvStep {
   int ldx = 0;
   NormIn nin;
   EpiArgs ea;
-  const uint8_t* pf = nullptr; /* weights of the next GEMV: prefetched into L2 from the tail */
+  /* weights of the GEMVs to come (one or two ranges): prefetched into L2 from the tail */
+  const uint8_t* pf = nullptr;
   uint32_t pf_bytes = 0;
+  const uint8_t* pf2 = nullptr;
+  uint32_t pf2_bytes = 0;
 };
 
 /* shared-memory layout of a GEMV CTA: warp partials | normalised activations (fp16 [M][K]) */
@@ -578,13 +581,19 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
       ULB_GEMV_NEXT(u, j + u)
     }
 #undef ULB_GEMV_NEXT
-  if (S.pf_bytes && lane == 0) {
-    /* this warp's loads are all issued: start the next kernel's weights on their way to L2,
-       an equal share per warp, so HBM stays busy through this kernel's tail and the next one's
-       start */
-    const uint64_t nw = (uint64_t)sp.G * sp.Wn;
-    const uint64_t lo = (uint64_t)S.pf_bytes * u / nw & ~15ull, hi = (uint64_t)S.pf_bytes * (u + 1) / nw & ~15ull;
-    for (uint64_t o = lo; o < hi; o += 32768) prefetch_l2_bulk(S.pf + o, hi - o < 32768 ? (uint32_t)(hi - o) : 32768u);
+  if ((S.pf_bytes | S.pf2_bytes) && lane == 0) {
+    /* this warp's loads are all issued: start the weights of the kernels to come on their way
+       to L2, an equal share of the two ranges (back to back) per warp, so HBM stays busy
+       through this kernel's tail and what follows it */
+    const uint64_t nw = (uint64_t)sp.G * sp.Wn, tot = (uint64_t)S.pf_bytes + S.pf2_bytes;
+    const uint64_t lo = tot * u / nw & ~15ull, hi = tot * (u + 1) / nw & ~15ull;
+    for (uint64_t o = lo; o < hi;) {
+      const bool first = o < S.pf_bytes;
+      const uint64_t end = first && hi > S.pf_bytes ? S.pf_bytes : hi;
+      const uint32_t len = end - o < 32768 ? (uint32_t)(end - o) : 32768u;
+      prefetch_l2_bulk(first ? S.pf + o : S.pf2 + (o - S.pf_bytes), len);
+      o += len;
+    }
   }
   if (kt != 0) flush(s); /* the range ends inside strip s */
 }
@@ -745,6 +754,8 @@ static int make_split(Ctx* c, const Tensor* w, Split* sp) {
 static void take_hint(Ctx* c, GemvStep* S) {
   S->pf = (const uint8_t*)c->pf_ptr;
   S->pf_bytes = c->pf_ptr ? (uint32_t)(std::min<size_t>(c->pf_bytes, kPrefetchMaxBytes) & ~(size_t)15) : 0u;
+  S->pf2 = (const uint8_t*)c->pf2_ptr;
+  S->pf2_bytes = c->pf2_ptr ? (uint32_t)(std::min<size_t>(c->pf2_bytes, kPrefetchMaxBytes) & ~(size_t)15) : 0u;
 }
 
 /* shared memory of the normalised activation rows: M x K fp16 */
@@ -799,8 +810,8 @@ static int launch_qgemv_impl(Ctx* c, const Tensor* w, const __half* x, int M, in
 
 int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
   const int rc = launch_qgemv_impl(c, w, x, M, ldx, epi, a0);
-  c->pf_ptr = nullptr; /* the prefetch hint is for the launch that follows it only */
-  c->pf_bytes = 0;
+  c->pf_ptr = c->pf2_ptr = nullptr; /* the prefetch hint is for the launch that follows it only */
+  c->pf_bytes = c->pf2_bytes = 0;
   return rc;
 }
 
@@ -861,8 +872,8 @@ int launch_qgemv_rms(Ctx* c, const Tensor* w, const float* x32, int ldx32, const
   else
     rc = q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_STORE, true>(c, w, nullptr, M, w->K, a, nin)
              : launch_q<ULB_TYPE_Q4_K, 1, EPI_STORE, true>(c, w, nullptr, M, w->K, a, nin);
-  c->pf_ptr = nullptr;
-  c->pf_bytes = 0;
+  c->pf_ptr = c->pf2_ptr = nullptr;
+  c->pf_bytes = c->pf2_bytes = 0;
   return rc;
 }
 

@@ -90,6 +90,8 @@ struct Ctx {
      Every GEMV launch clears it. */
   const void* pf_ptr = nullptr;
   size_t pf_bytes = 0;
+  const void* pf2_ptr = nullptr; /* a second range, prefetched after the first */
+  size_t pf2_bytes = 0;
 };
 constexpr size_t kPrefetchMaxBytes = (size_t)48 << 20;
 /* fp32 sum over the communicator's ranks, in place, on the context stream */
