@@ -46,6 +46,8 @@ extern "C" {
 #define ULB_TYPE_F16 1
 #define ULB_TYPE_Q4_0 2
 #define ULB_TYPE_Q4_K 12
+#define ULB_TYPE_Q8_0 8  /* token_embd and output.weight only (as llama.cpp's Q4_0 files store them) */
+#define ULB_TYPE_Q6_K 14 /* token_embd and output.weight only */
 
 typedef struct ulb_ctx ulb_ctx;
 typedef struct ulb_tensor ulb_tensor;
@@ -226,6 +228,9 @@ ULB_API int ulb_spec_accept(ulb_ctx* ctx, const float* dev_p_logits, const float
  * A LLaMA-family model resident in HBM.  Replaces Model / LayerWeights / KVCache
  * (src/inference/model.h:37-115, model.cpp:154-254) on the device side.  Tensors are
  * given by their GGUF names (token_embd.weight, blk.N.attn_q.weight, ..., output.weight).
+ * Types: the linear weights Q4_0 / Q4_K; token_embd.weight F32 / F16 / Q4_0 / Q8_0 / Q4_K /
+ * Q6_K (rows dequantised inside the embedding kernel); output.weight Q4_0 / Q4_K / Q8_0 / Q6_K
+ * (Q8_0 / Q6_K kept as GGUF rows for a row GEMV) -- the types llama.cpp's Q4_0 files use.
  */
 typedef struct ulb_model_desc {
   int n_layer, d_model, n_head, n_head_kv, head_dim, d_ff, n_vocab;

@@ -25,6 +25,8 @@
 #define T_F16 1
 #define T_Q4_0 2
 #define T_Q4_K 12
+#define T_Q8_0 8
+#define T_Q6_K 14
 
 void orc_set_threads(int n) {
 #ifdef _OPENMP
@@ -100,6 +102,8 @@ size_t orc_type_nbytes(int type, uint64_t n) {
     case T_F16: return n * 2;
     case T_Q4_0: return n % 32 ? 0 : n / 32 * 18;
     case T_Q4_K: return n % 256 ? 0 : n / 256 * 144;
+    case T_Q8_0: return n % 32 ? 0 : n / 32 * 34;
+    case T_Q6_K: return n % 256 ? 0 : n / 256 * 210;
     default: return 0;
   }
 }
@@ -128,8 +132,42 @@ static inline int q4_k_q(const uint8_t* blk, int i) {
   return hi ? (b >> 4) : (b & 0x0F);
 }
 
+/* Q8_0 weight i (0..31) of a block: int8 after the fp16 scale. */
+static inline int q8_0_q(const uint8_t* blk, int i) { return (int)(int8_t)blk[2 + i]; }
+/* Q6_K weight i (0..255) of a super-block as the integer q-32 (GGUF block_q6_K: ql[128],
+   qh[64], int8 scales[16], fp16 d; half h = i/128, k = (i%128)/32, l = i%32: low nibble in
+   ql[64h + l + 32(k&1)] (high nibble when k >= 2), top bits 2k..2k+1 of qh[32h + l]). */
+static inline int q6_k_q(const uint8_t* blk, int i) {
+  int h = i / 128, r = i % 128, k = r / 32, l = r % 32;
+  int lo = (blk[64 * h + l + 32 * (k & 1)] >> (k >= 2 ? 4 : 0)) & 15;
+  int hi = (blk[128 + 32 * h + l] >> (2 * k)) & 3;
+  return (lo | (hi << 4)) - 32;
+}
+static inline float q6_k_step(const uint8_t* blk, int j /* 0..15 */) {
+  uint16_t dh; memcpy(&dh, blk + 208, 2);
+  return h2f(dh) * (float)(int8_t)blk[192 + j];
+}
+
 int orc_dequant(int type, const void* blocks, uint64_t n, float* out) {
   const uint8_t* p = (const uint8_t*)blocks;
+  if (type == T_Q8_0) {
+    if (n % 32) return -1;
+    for (uint64_t b = 0; b < n / 32; ++b) {
+      const uint8_t* blk = p + b * 34;
+      uint16_t dh; memcpy(&dh, blk, 2);
+      float d = h2f(dh);
+      for (int i = 0; i < 32; ++i) out[b * 32 + i] = d * (float)q8_0_q(blk, i);
+    }
+    return 0;
+  }
+  if (type == T_Q6_K) {
+    if (n % 256) return -1;
+    for (uint64_t b = 0; b < n / 256; ++b) {
+      const uint8_t* blk = p + b * 210;
+      for (int i = 0; i < 256; ++i) out[b * 256 + i] = q6_k_step(blk, i / 16) * (float)q6_k_q(blk, i);
+    }
+    return 0;
+  }
   if (type == T_Q4_0) {
     if (n % 32) return -1;
 #pragma omp parallel for schedule(static)
@@ -263,6 +301,47 @@ int orc_qgemv(int type, const void* w, int N, int K, const uint16_t* x16, int M,
           }
         }
         for (int m = 0; m < mc; ++m) y[(size_t)(m0 + m) * ldy + n] = acc[m];
+      }
+    }
+  } else if (type == T_Q8_0) {
+    /* y = sum_b d_b * (sum_{i<32} q_i * x_i) */
+    if (K % 32) { free(xf); return -1; }
+    size_t row_bytes = (size_t)K / 32 * 34;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+      const uint8_t* row = W + (size_t)n * row_bytes;
+      for (int m = 0; m < M; ++m) {
+        const float* xv = xf + (size_t)m * K;
+        float acc = 0.0f;
+        for (int b = 0; b < K / 32; ++b) {
+          const uint8_t* blk = row + (size_t)b * 34;
+          uint16_t dh; memcpy(&dh, blk, 2);
+          float s = 0.0f;
+          for (int i = 0; i < 32; ++i) s += (float)q8_0_q(blk, i) * xv[b * 32 + i];
+          acc = fmaf(h2f(dh), s, acc);
+        }
+        y[(size_t)m * ldy + n] = acc;
+      }
+    }
+  } else if (type == T_Q6_K) {
+    /* y = sum over 16-weight sub-blocks j of (d * sc_j) * (sum_{i in j} (q_i - 32) * x_i) */
+    if (K % 256) { free(xf); return -1; }
+    size_t row_bytes = (size_t)K / 256 * 210;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+      const uint8_t* row = W + (size_t)n * row_bytes;
+      for (int m = 0; m < M; ++m) {
+        const float* xv = xf + (size_t)m * K;
+        float acc = 0.0f;
+        for (int b = 0; b < K / 256; ++b) {
+          const uint8_t* blk = row + (size_t)b * 210;
+          for (int j = 0; j < 16; ++j) {
+            float s = 0.0f;
+            for (int i = 0; i < 16; ++i) s += (float)q6_k_q(blk, 16 * j + i) * xv[b * 256 + 16 * j + i];
+            acc = fmaf(q6_k_step(blk, j), s, acc);
+          }
+        }
+        y[(size_t)m * ldy + n] = acc;
       }
     }
   } else {
@@ -554,9 +633,11 @@ int orc_forward(orc_model* mdl, orc_kv* kv, int M, int rps, const int32_t* token
   float* qkv = (float*)malloc((size_t)M * (nq + 2 * nkv) * 4);
   float* tmp = (float*)malloc((size_t)M * (2 * F > d ? 2 * F : d) * 4);
   uint16_t* att = (uint16_t*)malloc((size_t)M * nq * 2);
-  const uint16_t* emb = (const uint16_t*)mdl->embd->data;
+  /* embedding rows, dequantised with the block formulas of orc_dequant */
+  const size_t erow = orc_type_nbytes(mdl->embd->type, (uint64_t)d);
   for (int m = 0; m < M; ++m)
-    for (int i = 0; i < d; ++i) x[(size_t)m * d + i] = h2f(emb[(size_t)tokens[m] * d + i]);
+    orc_dequant(mdl->embd->type, (const uint8_t*)mdl->embd->data + (size_t)tokens[m] * erow, (uint64_t)d,
+                x + (size_t)m * d);
   int wt = D->wtype;
   for (int l = 0; l < D->n_layer; ++l) {
     const orc_layer* L = &mdl->layers[l];

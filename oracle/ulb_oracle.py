@@ -13,6 +13,7 @@ from . import build as _build  # noqa: F401  (package-relative when imported as 
 _lib = None
 
 T_F32, T_F16, T_Q4_0, T_Q4_K = 0, 1, 2, 12
+T_Q8_0, T_Q6_K = 8, 14
 
 
 class Desc(C.Structure):

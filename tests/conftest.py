@@ -74,6 +74,22 @@ def mid_q40(model_dir):
     return _synth(model_dir, spec, "mid_q40.gguf")
 
 
+@pytest.fixture(scope="session")
+def llamacpp_q40(model_dir):
+    """The tensor types of llama.cpp's Q4_0 files: Q4_0 token_embd and linears, Q6_K output."""
+    spec = dict(n_layer=2, d_model=512, n_head=8, n_head_kv=8, d_ff=1408, n_vocab=4096, rms_eps=1e-5,
+                rope_base=1e4, wtype="q4_0", embd_type="q4_0", out_type="q6_k", seed=11, name="llamacpp-q40")
+    return _synth(model_dir, spec, "llamacpp_q40.gguf")
+
+
+@pytest.fixture(scope="session")
+def q6k_embd_q80_head(model_dir):
+    """Q6_K token_embd and a Q8_0 output.weight over Q4_K linears (GQA)."""
+    spec = dict(n_layer=2, d_model=512, n_head=8, n_head_kv=2, d_ff=1536, n_vocab=4096, rms_eps=1e-5,
+                rope_base=5e5, wtype="q4_k", embd_type="q6_k", out_type="q8_0", seed=12, name="q6k-embd-q80-head")
+    return _synth(model_dir, spec, "q6k_embd_q80_head.gguf")
+
+
 def has_gpu():
     try:
         import ulb_capi

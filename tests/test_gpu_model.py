@@ -151,6 +151,42 @@ def test_mid_model_matches_oracle(ctx, mid_q40):
         gm.close()
 
 
+@pytest.mark.parametrize("fixture", ["llamacpp_q40", "q6k_embd_q80_head"])
+def test_quantised_embd_and_head_match_oracle(ctx, fixture, request):
+    """Q4_0 / Q6_K token_embd (rows dequantised inside the embedding kernel) and Q6_K / Q8_0
+    output.weight (the GGUF-row GEMV after a separate RMSNorm): one logits row of a 20-row
+    prefill, then a 12-row block (the head in chunks of 8 + 4 rows), against the oracle."""
+    path = request.getfixturevalue(fixture)
+    gm = GpuModel(ctx, path)
+    try:
+        kvg = gm.kv(1, 64)
+        kvo = orc.KV(gm.om, 1, 64)
+        toks = _prompt(20, seed=45, vocab=4096)
+        g = gm.forward(kvg, toks, [0] * 20, range(20), 20, logits_mode=1)
+        o = orc.forward(gm.om, kvo, toks, [0] * 20, list(range(20)), 20, logits_mode=1)
+        assert np.abs(g - o).max() / np.abs(o).max() < FWD_RTOL
+        assert g.argmax() == o.argmax()
+        toks = _prompt(12, seed=46, vocab=4096)
+        g = gm.forward(kvg, toks, [0] * 12, range(20, 32), 12)
+        o = orc.forward(gm.om, kvo, toks, [0] * 12, list(range(20, 32)), 12)
+        assert np.abs(g - o).max() / np.abs(o).max() < FWD_RTOL
+        assert (g.argmax(1) == o.argmax(1)).all()
+        gm.U.lib().ulb_kv_free(kvg)
+    finally:
+        gm.close()
+
+
+def test_llamacpp_layout_spec_stream_matches_oracle(llamacpp_q40):
+    """The speculative loop through the public API on a llama.cpp-layout model (drafting with
+    itself, so every draft is accepted): T=0 stream equal to the oracle's."""
+    prompt = _prompt(40, seed=5, vocab=4096)
+    api = _api(llamacpp_q40, llamacpp_q40, k=4)
+    got = api.generate_tokens(prompt.tolist(), _cfg(48))
+    t = orc.Model(llamacpp_q40)
+    want, _, _, margin, tm = orc.spec_generate(t, t, [prompt], 48, 4, (0.0, 0, 1.0), seed=0, with_margins=True)
+    _match_greedy(got, want[0], tm[0])
+
+
 def _api(target, draft=None, k=4):
     import vulkangguf as vg
     api = vg.InferenceAPI()

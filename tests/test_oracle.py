@@ -126,17 +126,76 @@ def test_oracle_quantizer_matches_gguf():
     assert np.array_equal(orc.quantize_q4_0(x), q)
 
 
+# ---------------------------------------------------------------- Q8_0 / Q6_K (llama.cpp's token_embd / output.weight types)
+def _random_q6k_blocks(n, seed):
+    rng = np.random.default_rng(seed)
+    b = rng.integers(0, 256, (n, 210), dtype=np.uint8)  # any ql / qh / int8 scales
+    d = rng.choice(np.array([0x1C00, 0x2E66, 0x0001, 0x9800, 0x03FF], np.uint16), n)
+    b[:, 208:210] = d.view(np.uint8).reshape(n, 2)
+    return b
+
+
+def test_q8_0_decode_matches_gguf_bit_exact():
+    rng = np.random.default_rng(21)
+    x = (rng.standard_normal((32, 256)) * 0.02).astype(np.float32)
+    q = gguf.quants.quantize(x, gguf.GGMLQuantizationType.Q8_0)
+    out = orc.dequant(orc.T_Q8_0, q, x.size)
+    ref = gguf.quants.dequantize(q, gguf.GGMLQuantizationType.Q8_0).ravel()
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+def test_q6_k_decode_matches_gguf_bit_exact():
+    blocks = _random_q6k_blocks(48, 22)
+    out = orc.dequant(orc.T_Q6_K, blocks, 48 * 256)
+    ref = gguf.quants.dequantize(blocks, gguf.GGMLQuantizationType.Q6_K).ravel()
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+QERR = {"q4_0": 0.13, "q8_0": 0.006, "q6_k": 0.04}  # max |dequant - value| / max |value| (Q4_0: up to d = amax / 8)
+
+
+@pytest.mark.parametrize("embd,out", [("q4_0", "q6_k"), ("q6_k", "q8_0"), ("q8_0", "q6_k")])
+def test_synthetic_embd_and_head_types(tmp_path, embd, out):
+    """The synthetic writer's Q4_0 / Q8_0 / Q6_K token_embd and output.weight (the engine's
+    quantisers) decode identically through the oracle and the gguf package, and stay within
+    the format's quantisation error of the same seeded values written as F32 / F16."""
+    import vulkangguf as vg
+    base = dict(n_layer=1, d_model=256, n_head=4, n_head_kv=4, d_ff=512, n_vocab=512, wtype="q4_0", seed=7)
+    pq, pf = str(tmp_path / "q.gguf"), str(tmp_path / "f.gguf")
+    vg.write_synthetic_gguf(pq, dict(base, embd_type=embd, out_type=out))
+    vg.write_synthetic_gguf(pf, dict(base, embd_type="f32"))
+    mq, mf = orc.Model(pq), orc.Model(pf)
+    gt = {"q4_0": gguf.GGMLQuantizationType.Q4_0, "q8_0": gguf.GGMLQuantizationType.Q8_0,
+          "q6_k": gguf.GGMLQuantizationType.Q6_K}
+    for name, ty in (("token_embd.weight", embd), ("output.weight", out)):
+        t, ne, raw = mq.tensor(name)
+        n = ne[0] * ne[1]
+        mine = orc.dequant(t, raw, n)
+        ref = gguf.quants.dequantize(raw.reshape(ne[1], -1), gt[ty]).ravel()
+        assert np.array_equal(mine.view(np.uint32), ref.view(np.uint32)), name
+        if name == "token_embd.weight":
+            tf, nef, rawf = mf.tensor(name)
+            vals = orc.dequant(tf, rawf, n)
+            assert np.abs(mine - vals).max() / np.abs(vals).max() < QERR[ty], name
+    mq.close()
+    mf.close()
+
+
 # ---------------------------------------------------------------- GEMV structure
-@pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
+@pytest.mark.parametrize("qt", ["q4_0", "q4_k", "q8_0", "q6_k"])
 @pytest.mark.parametrize("M", [1, 5, 8])
 def test_qgemv_matches_float64_dot(qt, M):
     rng = np.random.default_rng(M)
     N, K = 48, 512
-    if qt == "q4_0":
-        t = orc.T_Q4_0
-        w = gguf.quants.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32),
-                                 gguf.GGMLQuantizationType.Q4_0)
-        wf = gguf.quants.dequantize(w, gguf.GGMLQuantizationType.Q4_0).reshape(N, K)
+    if qt in ("q4_0", "q8_0"):
+        gq = gguf.GGMLQuantizationType.Q4_0 if qt == "q4_0" else gguf.GGMLQuantizationType.Q8_0
+        t = orc.T_Q4_0 if qt == "q4_0" else orc.T_Q8_0
+        w = gguf.quants.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32), gq)
+        wf = gguf.quants.dequantize(w, gq).reshape(N, K)
+    elif qt == "q6_k":
+        t = orc.T_Q6_K
+        w = _random_q6k_blocks(N * K // 256, M)
+        wf = gguf.quants.dequantize(w, gguf.GGMLQuantizationType.Q6_K).reshape(N, K)
     else:
         t = orc.T_Q4_K
         w = _random_q4k_blocks(N * K // 256, M)

@@ -27,6 +27,8 @@ size_t gguf_type_nbytes(int type, uint64_t n) {
     case 1: return n * 2;                          /* F16  */
     case 2: return n % 32 ? 0 : n / 32 * 18;       /* Q4_0 */
     case 12: return n % 256 ? 0 : n / 256 * 144;   /* Q4_K */
+    case 8: return n % 32 ? 0 : n / 32 * 34;       /* Q8_0 */
+    case 14: return n % 256 ? 0 : n / 256 * 210;   /* Q6_K */
     default: return 0;
   }
 }
@@ -190,6 +192,60 @@ void quantize_q4_0(const float* x, uint64_t n, uint8_t* out) {
  * d = max scale / 63, dmin = max(-min) / 63 (stored fp16); 6-bit sc_j = round(scale_j / d),
  * m_j = round(-min_j / dmin); q = clamp(round((x + dmin*m_j) / (d*sc_j)), 0, 15).
  */
+/* Q8_0 block (34 B): fp16 d, 32 x int8; d = amax / 127, q = round(x / d). */
+void quantize_q8_0(const float* x, uint64_t n, uint8_t* out) {
+  for (uint64_t b = 0; b < n / 32; ++b) {
+    const float* v = x + b * 32;
+    float amax = 0.f;
+    for (int i = 0; i < 32; ++i) amax = std::max(amax, std::fabs(v[i]));
+    const uint16_t dh = ulb_f2h(amax / 127.f);
+    const float d = ulb_h2f(dh), id = d != 0.f ? 1.f / d : 0.f;
+    uint8_t* blk = out + b * 34;
+    memcpy(blk, &dh, 2);
+    for (int i = 0; i < 32; ++i) {
+      const int q = (int)std::lrint(v[i] * id);
+      blk[2 + i] = (uint8_t)(int8_t)std::min(127, std::max(-127, q));
+    }
+  }
+}
+
+/* Q6_K super-block (210 B): ql[128] low nibbles, qh[64] high bit pairs, int8 scales[16] (one
+ * per 16 weights), fp16 d; weight i = d * scales[i / 16] * (q_i - 32).  Weight i of half
+ * h = i / 128 (r = i % 128, k = r / 32, l = r % 32) keeps its low nibble in
+ * ql[64h + l + 32 (k & 1)] (low nibble for k < 2, high for k >= 2) and its top two bits in
+ * bits 2k, 2k + 1 of qh[32h + l].  Scales: sub-block amax / 31 over d = max / 127. */
+void quantize_q6_k(const float* x, uint64_t n, uint8_t* out) {
+  for (uint64_t b = 0; b < n / 256; ++b) {
+    const float* v = x + b * 256;
+    float sub[16], smax = 0.f;
+    for (int j = 0; j < 16; ++j) {
+      float amax = 0.f;
+      for (int i = 0; i < 16; ++i) amax = std::max(amax, std::fabs(v[16 * j + i]));
+      sub[j] = amax / 31.f;
+      smax = std::max(smax, sub[j]);
+    }
+    uint8_t* blk = out + b * 210;
+    memset(blk, 0, 210);
+    const uint16_t dh = ulb_f2h(smax / 127.f);
+    const float d = ulb_h2f(dh);
+    memcpy(blk + 208, &dh, 2);
+    for (int j = 0; j < 16; ++j) {
+      const int sc = d != 0.f ? std::min(127, (int)std::lrint(sub[j] / d)) : 0;
+      blk[192 + j] = (uint8_t)(int8_t)sc;
+      const float step = d * (float)sc;
+      for (int e = 0; e < 16; ++e) {
+        const int i = 16 * j + e;
+        int q = step != 0.f ? (int)std::lrint(v[i] / step) + 32 : 32;
+        q = std::min(63, std::max(0, q));
+        const int h = i / 128, r = i % 128, k = r / 32, l = r % 32;
+        uint8_t& lo = blk[64 * h + l + 32 * (k & 1)];
+        lo |= (uint8_t)((q & 15) << (k >= 2 ? 4 : 0));
+        blk[128 + 32 * h + l] |= (uint8_t)((q >> 4) << (2 * k));
+      }
+    }
+  }
+}
+
 void quantize_q4_k(const float* x, uint64_t n, uint8_t* out) {
   for (uint64_t b = 0; b < n / 256; ++b) {
     const float* v = x + b * 256;
@@ -308,12 +364,19 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
     return fail("synthetic spec: non-positive dimension");
   if (sp.d_model % sp.n_head || sp.n_head % sp.n_head_kv) return fail("synthetic spec: head split");
   if (sp.wtype != 2 && sp.wtype != 12) return fail("synthetic spec: wtype must be 2 (Q4_0) or 12 (Q4_K)");
+  const int out_type = sp.out_type >= 0 ? sp.out_type : sp.wtype;
+  auto qtype_ok = [](int t) { return t == 2 || t == 8 || t == 12 || t == 14; };
+  if (!qtype_ok(out_type)) return fail("synthetic spec: out_type must be Q4_0, Q8_0, Q4_K or Q6_K");
+  if (sp.embd_type != 0 && sp.embd_type != 1 && !qtype_ok(sp.embd_type))
+    return fail("synthetic spec: embd_type must be F32, F16, Q4_0, Q8_0, Q4_K or Q6_K");
+  if (sp.d_model % 256 && (out_type == 12 || out_type == 14 || sp.embd_type == 12 || sp.embd_type == 14))
+    return fail("synthetic spec: d_model must be a multiple of 256 for K-quant token_embd / output");
   const int blk = sp.wtype == 2 ? 32 : 256;
   const int hd = sp.d_model / sp.n_head;
   const uint64_t nq = (uint64_t)sp.n_head * hd, nkv = (uint64_t)sp.n_head_kv * hd;
   if (sp.d_model % blk || sp.d_ff % blk || nq % blk) return fail("synthetic spec: dims must be multiples of the block size");
   std::vector<PlannedTensor> plan;
-  plan.push_back({"token_embd.weight", 1, 2, {(uint64_t)sp.d_model, (uint64_t)sp.n_vocab}, PlannedTensor::NORMAL});
+  plan.push_back({"token_embd.weight", sp.embd_type, 2, {(uint64_t)sp.d_model, (uint64_t)sp.n_vocab}, PlannedTensor::NORMAL});
   for (int l = 0; l < sp.n_layer; ++l) {
     const std::string p = "blk." + std::to_string(l) + ".";
     const uint64_t d = sp.d_model, f = sp.d_ff;
@@ -328,7 +391,7 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
     plan.push_back({p + "ffn_down.weight", sp.wtype, 2, {f, d}, PlannedTensor::NORMAL});
   }
   plan.push_back({"output_norm.weight", 0, 1, {(uint64_t)sp.d_model, 1}, PlannedTensor::ONES});
-  plan.push_back({"output.weight", sp.wtype, 2, {(uint64_t)sp.d_model, (uint64_t)sp.n_vocab}, PlannedTensor::NORMAL});
+  plan.push_back({"output.weight", out_type, 2, {(uint64_t)sp.d_model, (uint64_t)sp.n_vocab}, PlannedTensor::NORMAL});
   const uint64_t align = 32;
   uint64_t off = 0;
   for (PlannedTensor& t : plan) {
@@ -385,18 +448,33 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
           for (int e = 0; e < 4 && q * 4 + e < n; ++e) o[q * 4 + e] = ulb_f2h((float)(sp.stddev * z[e]));
         }
       });
-    } else {
-      const uint64_t nblk = n / blk;
-      parallel_for(nblk, threads, [&](uint64_t a, uint64_t b) {
-        std::vector<float> v(blk);
+    } else if (t.type == 0) {
+      float* o = reinterpret_cast<float*>(buf.data());
+      parallel_for((n + 3) / 4, threads, [&](uint64_t a, uint64_t b) {
         for (uint64_t q = a; q < b; ++q) {
-          for (int e = 0; e < blk; e += 4) {
+          double z[4];
+          normals4(sp.seed, nh, q, z);
+          for (int e = 0; e < 4 && q * 4 + e < n; ++e) o[q * 4 + e] = (float)(sp.stddev * z[e]);
+        }
+      });
+    } else {
+      /* quantised: block by block, the same N(0, stddev) values whatever the type */
+      const int tb = t.type == 2 || t.type == 8 ? 32 : 256;
+      const size_t bb = gguf_type_nbytes(t.type, (uint64_t)tb);
+      const uint64_t nblk = n / tb;
+      parallel_for(nblk, threads, [&](uint64_t a, uint64_t b) {
+        std::vector<float> v(tb);
+        for (uint64_t q = a; q < b; ++q) {
+          for (int e = 0; e < tb; e += 4) {
             double z[4];
-            normals4(sp.seed, nh, (q * blk + e) / 4, z);
+            normals4(sp.seed, nh, (q * tb + e) / 4, z);
             for (int k = 0; k < 4; ++k) v[e + k] = (float)(sp.stddev * z[k]);
           }
-          if (t.type == 2) quantize_q4_0(v.data(), blk, buf.data() + q * 18);
-          else quantize_q4_k(v.data(), blk, buf.data() + q * 144);
+          uint8_t* o = buf.data() + q * bb;
+          if (t.type == 2) quantize_q4_0(v.data(), tb, o);
+          else if (t.type == 12) quantize_q4_k(v.data(), tb, o);
+          else if (t.type == 8) quantize_q8_0(v.data(), tb, o);
+          else quantize_q6_k(v.data(), tb, o);
         }
       });
     }

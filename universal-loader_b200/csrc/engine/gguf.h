@@ -62,6 +62,8 @@ struct SynthSpec {
   int n_layer = 2, d_model = 512, n_head = 8, n_head_kv = 8, d_ff = 1408, n_vocab = 32000, ctx_len = 4096;
   float rms_eps = 1e-5f, rope_base = 10000.f;
   int wtype = 2; /* Q4_0 = 2, Q4_K = 12 */
+  int embd_type = 1;  /* token_embd: F32 = 0, F16 = 1, or Q4_0 / Q8_0 = 8 / Q4_K / Q6_K = 14 */
+  int out_type = -1;  /* output.weight: Q4_0 / Q8_0 / Q4_K / Q6_K; -1 = wtype */
   uint64_t seed = 0;
   float stddev = 0.02f;
 };
@@ -71,6 +73,8 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& spec, int th
 /* quantisers (exposed for tests) */
 void quantize_q4_0(const float* x, uint64_t n, uint8_t* out);
 void quantize_q4_k(const float* x, uint64_t n, uint8_t* out);
+void quantize_q8_0(const float* x, uint64_t n, uint8_t* out);
+void quantize_q6_k(const float* x, uint64_t n, uint8_t* out);
 /* the N(0,1) sample number i of the stream keyed by (seed, name) */
 double synth_normal(uint64_t seed, const std::string& name, uint64_t i);
 

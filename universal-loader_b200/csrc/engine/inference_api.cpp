@@ -28,7 +28,9 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include <cctype>
 #include <chrono>
+#include <map>
 #include <cstdio>
 #include <functional>
 #include <mutex>
@@ -473,6 +475,20 @@ bool write_synthetic(const std::string& path, py::dict spec, int threads) {
       s.wtype = w.cast<int>();
     }
   }
+  /* tensor types by GGML id or name */
+  auto type_of = [&](const char* k, int& v) {
+    if (!spec.contains(k)) return;
+    py::object o = spec[k];
+    if (!py::isinstance<py::str>(o)) { v = o.cast<int>(); return; }
+    std::string n = o.cast<std::string>();
+    for (char& ch : n) ch = (char)std::tolower((unsigned char)ch);
+    const std::map<std::string, int> ids = {{"f32", 0}, {"f16", 1}, {"q4_0", 2}, {"q8_0", 8}, {"q4_k", 12}, {"q6_k", 14}};
+    auto it = ids.find(n);
+    if (it == ids.end()) throw std::runtime_error(std::string(k) + ": unknown tensor type " + n);
+    v = it->second;
+  };
+  type_of("embd_type", s.embd_type);
+  type_of("out_type", s.out_type);
   if (spec.contains("seed")) s.seed = spec["seed"].cast<uint64_t>();
   if (spec.contains("name")) s.name = spec["name"].cast<std::string>();
   if (threads <= 0) threads = (int)std::max(1u, std::thread::hardware_concurrency());

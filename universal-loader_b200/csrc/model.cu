@@ -78,7 +78,54 @@ struct KV {
 
 namespace {
 
-__global__ void embed_kernel(const void* __restrict__ table, int table_type, int d, int V,
+/* element i of one token_embd row in fp32, by the GGUF block formulas (single roundings in
+   the order of the oracle's orc_dequant):
+     Q4_0 d * (q - 8); Q8_0 d * q; Q4_K (d * sc_j) * q - (dmin * m_j);
+     Q6_K (d * sc_j) * (q - 32), sc_j per 16 weights (ql / qh / scales / d layout of block_q6_K) */
+__device__ __forceinline__ float embd_value(const uint8_t* __restrict__ row, int type, int i) {
+  auto half_at = [](const uint8_t* p) { return __half2float(*reinterpret_cast<const __half*>(p)); };
+  switch (type) {
+    case ULB_TYPE_F16: return __half2float(reinterpret_cast<const __half*>(row)[i]);
+    case ULB_TYPE_F32: return reinterpret_cast<const float*>(row)[i];
+    case ULB_TYPE_Q4_0: {
+      const uint8_t* blk = row + (size_t)(i / 32) * 18;
+      const int j = i % 32;
+      const int q = (j < 16 ? (blk[2 + j] & 15) : (blk[2 + j - 16] >> 4)) - 8;
+      return __fmul_rn(half_at(blk), (float)q);
+    }
+    case ULB_TYPE_Q8_0: {
+      const uint8_t* blk = row + (size_t)(i / 32) * 34;
+      return __fmul_rn(half_at(blk), (float)(int8_t)blk[2 + i % 32]);
+    }
+    case ULB_TYPE_Q4_K: {
+      const uint8_t* blk = row + (size_t)(i / 256) * 144;
+      const int ii = i % 256, j = ii / 32;
+      const uint8_t* sc12 = blk + 4;
+      int sc, mn;
+      if (j < 4) {
+        sc = sc12[j] & 63;
+        mn = sc12[j + 4] & 63;
+      } else {
+        sc = (sc12[j + 4] & 0x0F) | ((sc12[j - 4] >> 6) << 4);
+        mn = (sc12[j + 4] >> 4) | ((sc12[j] >> 6) << 4);
+      }
+      const uint8_t qb = blk[16 + 32 * (ii / 64) + ii % 32];
+      const int q = ((ii / 32) & 1) ? (qb >> 4) : (qb & 15);
+      const float s = __fmul_rn(half_at(blk), (float)sc), m = __fmul_rn(half_at(blk + 2), (float)mn);
+      return __fsub_rn(__fmul_rn(s, (float)q), m);
+    }
+    default: { /* ULB_TYPE_Q6_K */
+      const uint8_t* blk = row + (size_t)(i / 256) * 210;
+      const int ii = i % 256, h = ii / 128, r = ii % 128, k = r / 32, l = r % 32;
+      const int lo = (blk[64 * h + l + 32 * (k & 1)] >> (k >= 2 ? 4 : 0)) & 15;
+      const int hi = (blk[128 + 32 * h + l] >> (2 * k)) & 3;
+      const float step = __fmul_rn(half_at(blk + 208), (float)(int8_t)blk[192 + ii / 16]);
+      return __fmul_rn(step, (float)((lo | (hi << 4)) - 32));
+    }
+  }
+}
+
+__global__ void embed_kernel(const void* __restrict__ table, int table_type, size_t row_bytes, int d, int V,
                              const int* __restrict__ tokens, float* __restrict__ x, int* err) {
   pdl_wait();
   pdl_trigger();
@@ -88,12 +135,8 @@ __global__ void embed_kernel(const void* __restrict__ table, int table_type, int
     if (threadIdx.x == 0) atomicOr(err, 1);
     t = t < 0 ? 0 : V - 1;
   }
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    float v;
-    if (table_type == ULB_TYPE_F16) v = __half2float(reinterpret_cast<const __half*>(table)[(size_t)t * d + i]);
-    else v = reinterpret_cast<const float*>(table)[(size_t)t * d + i];
-    x[(size_t)m * d + i] = v;
-  }
+  const uint8_t* row = reinterpret_cast<const uint8_t*>(table) + (size_t)t * row_bytes;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) x[(size_t)m * d + i] = embd_value(row, table_type, i);
 }
 
 /* out[s] = fp16((x[row] * r) * g), r = 1 / sqrt(mean(x^2) + eps); row = s*sel + sel-1 if sel.
@@ -112,7 +155,18 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, int ldx, const float
 
 int launch_embed_t(Ctx* c, const void* table, int type, int d, int V, const int* tokens, int M, float* x, int* err) {
   if (M == 0) return ULB_OK;
-  cudaError_t e = launch_k(c, embed_kernel, dim3(M), dim3(256), 0, table, type, d, V, tokens, x, err);
+  size_t row_bytes = 0;
+  switch (type) {
+    case ULB_TYPE_F32: row_bytes = (size_t)d * 4; break;
+    case ULB_TYPE_F16: row_bytes = (size_t)d * 2; break;
+    case ULB_TYPE_Q4_0: row_bytes = d % 32 ? 0 : (size_t)d / 32 * 18; break;
+    case ULB_TYPE_Q8_0: row_bytes = d % 32 ? 0 : (size_t)d / 32 * 34; break;
+    case ULB_TYPE_Q4_K: row_bytes = d % 256 ? 0 : (size_t)d / 256 * 144; break;
+    case ULB_TYPE_Q6_K: row_bytes = d % 256 ? 0 : (size_t)d / 256 * 210; break;
+    default: break;
+  }
+  ULB_CHECK(row_bytes, ULB_EUNSUPPORTED, "embedding: table type %d with d=%d", type, d);
+  cudaError_t e = launch_k(c, embed_kernel, dim3(M), dim3(256), 0, table, type, row_bytes, d, V, tokens, x, err);
   if (e != cudaSuccess) return cuda_error(e, "embed launch", __FILE__, __LINE__);
   return ULB_OK;
 }
@@ -352,6 +406,8 @@ size_t gguf_row_bytes(int type, uint64_t ne0) {
     case ULB_TYPE_F16: return ne0 * 2;
     case ULB_TYPE_Q4_0: return ne0 / 32 * 18;
     case ULB_TYPE_Q4_K: return ne0 / 256 * 144;
+    case ULB_TYPE_Q8_0: return ne0 / 32 * 34;
+    case ULB_TYPE_Q6_K: return ne0 / 256 * 210;
     default: return 0;
   }
 }
@@ -471,6 +527,8 @@ int ulb_model_set_weight(ulb_model* mm, const char* name, int type, const uint64
     case ULB_TYPE_F16: want = n * 2; break;
     case ULB_TYPE_Q4_0: want = ne[0] % 32 ? 0 : n / 32 * 18; break;
     case ULB_TYPE_Q4_K: want = ne[0] % 256 ? 0 : n / 256 * 144; break;
+    case ULB_TYPE_Q8_0: want = ne[0] % 32 ? 0 : n / 32 * 34; break;
+    case ULB_TYPE_Q6_K: want = ne[0] % 256 ? 0 : n / 256 * 210; break;
     default: return set_error(ULB_EUNSUPPORTED, "%s: tensor type %d not supported", name, type);
   }
   ULB_CHECK(want && want == nbytes, ULB_EFORMAT, "%s: %zu bytes, GGUF size is %zu", name, nbytes, want);
@@ -516,7 +574,14 @@ int ulb_model_finalize(ulb_model* mm) {
   const RawW* r;
   ULB_TRY(get("token_embd.weight", &r));
   ULB_TRY(expect(r, "token_embd.weight", d.d_model, d.n_vocab));
-  ULB_CHECK(r->type == ULB_TYPE_F16 || r->type == ULB_TYPE_F32, ULB_EUNSUPPORTED, "token_embd must be F16 or F32");
+  {
+    const int t = r->type;
+    const bool blk32 = t == ULB_TYPE_Q4_0 || t == ULB_TYPE_Q8_0, blk256 = t == ULB_TYPE_Q4_K || t == ULB_TYPE_Q6_K;
+    ULB_CHECK(t == ULB_TYPE_F16 || t == ULB_TYPE_F32 || blk32 || blk256, ULB_EUNSUPPORTED,
+              "token_embd must be F16, F32, Q4_0, Q8_0, Q4_K or Q6_K (type %d)", t);
+    ULB_CHECK(!(blk32 && d.d_model % 32) && !(blk256 && d.d_model % 256), ULB_EFORMAT,
+              "token_embd: rows of %d are not whole blocks", d.d_model);
+  }
   m->embd_type = r->type;
   ULB_TRY(upload_plain(c, *r, &m->embd, &m->embd_bytes));
   const int nq = m->nq, nkv = m->nkv;
@@ -570,8 +635,19 @@ int ulb_model_finalize(ulb_model* mm) {
   ULB_TRY(upload_plain(c, *r, (void**)&m->out_norm, &b));
   ULB_TRY(get("output.weight", &r));
   ULB_TRY(expect(r, "output.weight", d.d_model, d.n_vocab));
-  ULB_CHECK(is_q4(r->type), ULB_EUNSUPPORTED, "output.weight must be Q4_0 or Q4_K");
-  ULB_TRY(build_plain(c, *r, &m->out));
+  if (r->type == ULB_TYPE_Q8_0 || r->type == ULB_TYPE_Q6_K) {
+    /* kept as GGUF rows for the row GEMV (as llama.cpp's Q4_0 / Q4_K_M files store the head) */
+    ULB_CHECK(d.d_model % (r->type == ULB_TYPE_Q8_0 ? 32 : 256) == 0, ULB_EFORMAT, "output.weight: partial blocks");
+    m->out.type = r->type;
+    m->out.N = d.n_vocab;
+    m->out.K = d.d_model;
+    m->out.ne[0] = (uint64_t)d.d_model;
+    m->out.ne[1] = (uint64_t)d.n_vocab;
+    ULB_TRY(upload_plain(c, *r, &m->out.dev, &m->out.bytes));
+  } else {
+    ULB_CHECK(is_q4(r->type), ULB_EUNSUPPORTED, "output.weight must be Q4_0, Q4_K, Q8_0 or Q6_K");
+    ULB_TRY(build_plain(c, *r, &m->out));
+  }
   m->weight_bytes += m->out.bytes;
   for (auto& kv : m->raw) dev_free(c, kv.second.dev, kv.second.bytes);
   m->raw.clear();

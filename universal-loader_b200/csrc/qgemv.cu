@@ -621,6 +621,103 @@ __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
       });
 }
 
+/* ------------------------------------------------------------------ GGUF-row GEMV (Q8_0 / Q6_K heads) */
+/*
+ * y[m][n] = W[n] . x16[m] for a matrix kept as GGUF rows (Q8_0: fp16 d + 32 int8 per block;
+ * Q6_K: 256-weight super-blocks, weight = (d * sc_j) * (q - 32), sc_j per 16 weights), used for
+ * the output.weight llama.cpp's Q4_0 / Q4_K_M files store in these types.  One warp per row,
+ * M <= 8 tokens.  Q8_0: lane L takes blocks L, L + 32, ...; Q6_K: in each super-block lane L
+ * takes weights 8L..8L+7 (half of sub-block L / 2: eight ql bytes, eight qh bytes).  Each
+ * lane sums its integer dot products in fp32 and applies the block step with one fmaf; the
+ * lanes' sums meet in a warp xor tree.
+ */
+template <int QT>
+__global__ void __launch_bounds__(256) rowgemv_kernel(const uint8_t* __restrict__ w, int N, int K,
+                                                      const __half* __restrict__ x, int ldx, int M,
+                                                      float* __restrict__ y, int ldy) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (n >= N) return;
+  float acc[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) acc[m] = 0.f;
+  auto xdot8 = [&](const int8_t (&q)[8], int k0, float step) {
+#pragma unroll
+    for (int m = 0; m < 8; ++m)
+      if (m < M) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * ldx + k0));
+        const __half* xh = reinterpret_cast<const __half*>(&raw);
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s = __fmaf_rn((float)q[e], __half2float(xh[e]), s);
+        acc[m] = __fmaf_rn(step, s, acc[m]);
+      }
+  };
+  if (QT == ULB_TYPE_Q8_0) {
+    const uint8_t* row = w + (size_t)n * (K / 32) * 34;
+    for (int b = lane; b < K / 32; b += 32) {
+      const uint8_t* blk = row + (size_t)b * 34;
+      const float d = __half2float(*reinterpret_cast<const __half*>(blk));
+      /* the block's integer dot product in weight order (exact products, fp32 sum) */
+#pragma unroll
+      for (int m = 0; m < 8; ++m)
+        if (m < M) {
+          float s = 0.f;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * ldx + b * 32 + 8 * r));
+            const __half* xh = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s = __fmaf_rn((float)(int8_t)blk[2 + 8 * r + e], __half2float(xh[e]), s);
+          }
+          acc[m] = __fmaf_rn(d, s, acc[m]);
+        }
+    }
+  } else {
+    const uint8_t* row = w + (size_t)n * (K / 256) * 210;
+    const int h = lane / 16, k = (lane % 16) / 4, l0 = (8 * lane) % 32;
+    for (int b = 0; b < K / 256; ++b) {
+      const uint8_t* blk = row + (size_t)b * 210;
+      const uint8_t* ql = blk + 64 * h + l0 + 32 * (k & 1);
+      const uint8_t* qh = blk + 128 + 32 * h + l0;
+      const float step = __fmul_rn(__half2float(*reinterpret_cast<const __half*>(blk + 208)),
+                                   (float)(int8_t)blk[192 + lane / 2]);
+      int8_t q[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        q[e] = (int8_t)((((ql[e] >> (k >= 2 ? 4 : 0)) & 15) | (((qh[e] >> (2 * k)) & 3) << 4)) - 32);
+      xdot8(q, b * 256 + 8 * lane, step);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float v = acc[m];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0 && m < M) y[(size_t)m * ldy + n] = v;
+  }
+}
+
+static bool raw_rows_type(int t) { return t == ULB_TYPE_Q8_0 || t == ULB_TYPE_Q6_K; }
+
+static int launch_rowgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a) {
+  ULB_CHECK(epi == EPI_STORE && a.y, ULB_EUNSUPPORTED, "qgemv: a Q8_0 / Q6_K matrix takes the plain store epilogue only");
+  ULB_CHECK(ldx % 8 == 0 && ((uintptr_t)x & 15) == 0, ULB_EINVAL, "qgemv: activations must be 16-byte aligned rows");
+  const dim3 grid((w->N + 7) / 8), block(256);
+  for (int m0 = 0; m0 < M; m0 += 8) {
+    const int mc = M - m0 < 8 ? M - m0 : 8;
+    cudaError_t e = w->type == ULB_TYPE_Q8_0
+                        ? launch_k(c, rowgemv_kernel<ULB_TYPE_Q8_0>, grid, block, 0, (const uint8_t*)w->dev, w->N, w->K,
+                                   x + (size_t)m0 * ldx, ldx, mc, a.y + (size_t)m0 * a.ldy, a.ldy)
+                        : launch_k(c, rowgemv_kernel<ULB_TYPE_Q6_K>, grid, block, 0, (const uint8_t*)w->dev, w->N, w->K,
+                                   x + (size_t)m0 * ldx, ldx, mc, a.y + (size_t)m0 * a.ldy, a.ldy);
+    if (e != cudaSuccess) return cuda_error(e, "row GEMV launch", __FILE__, __LINE__);
+  }
+  return ULB_OK;
+}
+
 /* ------------------------------------------------------------------ repack / dequant */
 __device__ __forceinline__ uint32_t place_nibbles(const uint8_t (&n)[8]) {
   /* nibble i -> bit position {0,16,4,20,8,24,12,28}[i] */
@@ -816,6 +913,7 @@ int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int e
 }
 
 static int launch_qgemv_impl(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
+  if (w && raw_rows_type(w->type)) return M == 0 ? ULB_OK : launch_rowgemv(c, w, x, M, ldx, epi, a0);
   ULB_CHECK(w && (w->type == ULB_TYPE_Q4_0 || w->type == ULB_TYPE_Q4_K), ULB_EINVAL, "qgemv: weight is not Q4_0/Q4_K");
   ULB_CHECK(M >= 0 && ldx % 8 == 0 && ldx >= w->K, ULB_EINVAL, "qgemv: bad M=%d / ldx=%d (K=%d)", M, ldx, w->K);
   ULB_CHECK(((uintptr_t)x & 15) == 0, ULB_EINVAL, "qgemv: activations must be 16-byte aligned");
@@ -847,9 +945,10 @@ static int launch_qgemv_impl(Ctx* c, const Tensor* w, const __half* x, int M, in
 
 int launch_qgemv_rms(Ctx* c, const Tensor* w, const float* x32, int ldx32, const float* g, float eps, __half* x16,
                      int M, int epi, const EpiArgs& a) {
-  ULB_CHECK(w && (w->type == ULB_TYPE_Q4_0 || w->type == ULB_TYPE_Q4_K), ULB_EINVAL, "qgemv: weight is not Q4_0/Q4_K");
+  ULB_CHECK(w && (w->type == ULB_TYPE_Q4_0 || w->type == ULB_TYPE_Q4_K || raw_rows_type(w->type)), ULB_EINVAL,
+            "qgemv: weight is not Q4_0/Q4_K/Q8_0/Q6_K");
   if (M == 0) return ULB_OK;
-  const bool fuse = M <= 8 && (size_t)M * w->K * sizeof(__half) <= (size_t)kNormSmemBytes && w->K <= 8192 &&
+  const bool fuse = !raw_rows_type(w->type) && M <= 8 && (size_t)M * w->K * sizeof(__half) <= (size_t)kNormSmemBytes && w->K <= 8192 &&
                     w->K % 8 == 0 && ldx32 % 4 == 0 && ((uintptr_t)x32 & 15) == 0 && ((uintptr_t)g & 15) == 0 &&
                     (epi == EPI_QKV || epi == EPI_SWIGLU || epi == EPI_STORE);
   if (!fuse) {
