@@ -12,7 +12,9 @@
  *    the GGUF block table (Q4_0: 18 B / 32, Q4_K: 144 B / 256) instead of the reference's
  *    ggml_type_size (src/core/gguf_types.h:35-58), which is wrong for both.
  *  - Q4_0 / Q4_K block decoding as the GGUF format defines it (the reference's decoders,
- *    src/cpu_backend/dequantize_cpu.cpp:6-74, use invented layouts and are not followed).
+ *    src/cpu_backend/dequantize_cpu.cpp:6-74, use invented layouts and are not followed);
+ *    also Q8_0 (34 B / 32) and Q6_K (210 B / 256), for the token_embd / output.weight types
+ *    of llama.cpp's Q4_0 files (a widening: the reference's type set stops at Q4_K).
  *  - the reference's per-layer op order (src/inference/inference_engine.cpp:602-682:
  *    norm -> Q,K,V -> RoPE -> attention -> o -> +res -> norm -> gate,up -> SiLU*mul ->
  *    down -> +res) with each op given its standard LLaMA meaning: RMSNorm with eps,
