@@ -1,0 +1,116 @@
+"""The GGUF SentencePiece tokenizer of the text surface (csrc/engine/tokenizer.cpp), pinned
+against the sentencepiece library on a BPE model trained here with LLaMA's tokenizer settings
+(identity normaliser, dummy-prefix space, byte fallback) and written into a synthetic GGUF as
+tokenizer.ggml.{tokens, scores, token_type} -- the form llama.cpp's files carry it in.
+
+CPU only: the tokenizer is host code and no model is loaded."""
+import io
+import random
+
+import pytest
+
+spm = pytest.importorskip("sentencepiece")
+
+ALPHABET = "abcdefghijklmnopqrstuvwxyz" + "éüß" + "0123456789"
+
+
+def _corpus(seed=0, n_lines=3000):
+    rng = random.Random(seed)
+    words = ["".join(rng.choice(ALPHABET) for _ in range(rng.randint(1, 9))) for _ in range(400)]
+    return [" ".join(rng.choice(words) for _ in range(rng.randint(3, 14))) for _ in range(n_lines)], words
+
+
+@pytest.fixture(scope="module")
+def trained(tmp_path_factory):
+    lines, words = _corpus()
+    buf = io.BytesIO()
+    spm.SentencePieceTrainer.train(sentence_iterator=iter(lines), model_writer=buf, vocab_size=600,
+                                   model_type="bpe", byte_fallback=True, normalization_rule_name="identity",
+                                   add_dummy_prefix=True, remove_extra_whitespaces=False, split_digits=True,
+                                   minloglevel=2)
+    sp = spm.SentencePieceProcessor(model_proto=buf.getvalue())
+    n = sp.get_piece_size()
+    pieces = [sp.id_to_piece(i) for i in range(n)]
+    scores = [sp.get_score(i) for i in range(n)]
+
+    def ttype(i):
+        if sp.is_unknown(i):
+            return 2
+        if sp.is_control(i):
+            return 3
+        if sp.is_byte(i):
+            return 6
+        if sp.is_unused(i):
+            return 5
+        return 1
+
+    types = [ttype(i) for i in range(n)]
+    import vulkangguf as vg
+    path = str(tmp_path_factory.mktemp("tok") / "vocab.gguf")
+    vg.write_synthetic_gguf(path, dict(n_layer=1, d_model=256, n_head=4, n_head_kv=4, d_ff=512, n_vocab=n,
+                                       wtype="q4_0", seed=3, vocab=pieces, scores=scores, token_types=types))
+    return sp, path, words
+
+
+def _texts(words, seed=1, n=200):
+    rng = random.Random(seed)
+    out = ["", " ", "a", "  leading and  double  spaces ", "trailing ", "€ and 中文 are not in the corpus",
+           "tab\tand\nnewline", "0123456789 9876"]
+    for _ in range(n):
+        k = rng.randint(1, 12)
+        parts = []
+        for _ in range(k):
+            r = rng.random()
+            if r < 0.7:
+                parts.append(rng.choice(words))
+            elif r < 0.85:  # unseen spellings of seen characters
+                parts.append("".join(rng.choice(ALPHABET) for _ in range(rng.randint(1, 12))))
+            else:  # characters outside the vocabulary: byte fallback
+                parts.append(rng.choice(["€", "Ω", "ж", "🙂", "~", "ÿ"]) * rng.randint(1, 3))
+        out.append((" " * rng.randint(1, 2)).join(parts))
+    return out
+
+
+def test_encode_matches_sentencepiece(trained):
+    sp, path, words = trained
+    import vulkangguf as vg
+    for t in _texts(words):
+        want = sp.encode(t) if t else []
+        got = vg.gguf_tokenize(path, t, False)
+        assert got == want, (t, got, want)
+
+
+def test_bos_and_decode_round_trip(trained):
+    sp, path, words = trained
+    import vulkangguf as vg
+    for t in _texts(words, seed=2, n=100):
+        ids = vg.gguf_tokenize(path, t, True)
+        assert ids[0] == 1  # <s>
+        assert vg.gguf_detokenize(path, ids).decode("utf-8") == sp.decode(ids[1:]) == t
+
+
+def test_gguf_without_vocabulary_is_rejected(tmp_path):
+    import vulkangguf as vg
+    p = str(tmp_path / "novocab.gguf")
+    vg.write_synthetic_gguf(p, dict(n_layer=1, d_model=256, n_head=4, n_head_kv=4, d_ff=512, n_vocab=512,
+                                    wtype="q4_0", seed=3))
+    with pytest.raises(RuntimeError, match="vocabulary"):
+        vg.gguf_tokenize(p, "abc")
+
+
+@pytest.mark.gpu
+def test_generate_text_uses_the_gguf_vocabulary(trained):
+    """InferenceAPI.generate(str) on a model whose GGUF carries the vocabulary: the prompt is
+    encoded with it (BOS first) and the continuation decoded with it."""
+    sp, path, words = trained
+    import vulkangguf as vg
+    api = vg.InferenceAPI()
+    assert api.load_model(path)
+    cfg = vg.GenerationConfig()
+    cfg.max_tokens = 12
+    cfg.temperature = 0.0
+    cfg.do_sample = False
+    prompt = " ".join(words[:6])
+    ids = vg.gguf_tokenize(path, prompt, True)
+    toks = api.generate_tokens(ids, cfg)
+    assert api.generate(prompt, cfg) == sp.decode(list(toks))

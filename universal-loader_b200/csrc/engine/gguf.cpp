@@ -109,10 +109,17 @@ bool GGUFFile::open(const std::string& path, std::string* err) {
     if (t == GV_ARR) {
       int et = (int)r.u(4);
       uint64_t cnt = r.u(8);
-      for (uint64_t j = 0; j < cnt && !r.bad; ++j) {
-        if (et == GV_STR) r.s();
-        else if (gv_size(et) > 0) r.u(gv_size(et));
-        else return fail("unsupported nested array in " + key);
+      if (cnt > (uint64_t)(r.end - r.p)) return fail("truncated array " + key);
+      if (et == GV_STR) {
+        std::vector<std::string>& v = strarr_[key];
+        v.reserve(cnt);
+        for (uint64_t j = 0; j < cnt && !r.bad; ++j) v.push_back(r.s());
+      } else if (gv_size(et) > 0) {
+        std::vector<double>& v = numarr_[key];
+        v.reserve(cnt);
+        for (uint64_t j = 0; j < cnt && !r.bad; ++j) v.push_back(scalar(r, et));
+      } else {
+        return fail("unsupported nested array in " + key);
       }
       continue;
     }
@@ -159,6 +166,16 @@ double GGUFFile::num(const std::string& key, double dflt) const {
 std::string GGUFFile::str(const std::string& key, const std::string& dflt) const {
   auto it = str_.find(key);
   return it == str_.end() ? dflt : it->second;
+}
+
+const std::vector<std::string>* GGUFFile::str_array(const std::string& key) const {
+  auto it = strarr_.find(key);
+  return it == strarr_.end() ? nullptr : &it->second;
+}
+
+const std::vector<double>* GGUFFile::num_array(const std::string& key) const {
+  auto it = numarr_.find(key);
+  return it == numarr_.end() ? nullptr : &it->second;
 }
 
 /* ------------------------------------------------------------------ quantisers */
@@ -353,6 +370,21 @@ void kv_u32(std::vector<uint8_t>& b, const std::string& k, uint32_t v) { put_str
 void kv_f32(std::vector<uint8_t>& b, const std::string& k, float v) { put_str(b, k); put<uint32_t>(b, GV_F32); put(b, v); }
 void kv_u64(std::vector<uint8_t>& b, const std::string& k, uint64_t v) { put_str(b, k); put<uint32_t>(b, GV_U64); put(b, v); }
 void kv_str(std::vector<uint8_t>& b, const std::string& k, const std::string& v) { put_str(b, k); put<uint32_t>(b, GV_STR); put_str(b, v); }
+void kv_arr_str(std::vector<uint8_t>& b, const std::string& k, const std::vector<std::string>& v) {
+  put_str(b, k);
+  put<uint32_t>(b, GV_ARR);
+  put<uint32_t>(b, GV_STR);
+  put<uint64_t>(b, v.size());
+  for (const std::string& x : v) put_str(b, x);
+}
+template <class T>
+void kv_arr_num(std::vector<uint8_t>& b, const std::string& k, uint32_t gv, const std::vector<T>& v) {
+  put_str(b, k);
+  put<uint32_t>(b, GV_ARR);
+  put<uint32_t>(b, gv);
+  put<uint64_t>(b, v.size());
+  for (const T& x : v) put(b, x);
+}
 }  // namespace
 
 bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int threads, std::string* err) {
@@ -364,6 +396,8 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
     return fail("synthetic spec: non-positive dimension");
   if (sp.d_model % sp.n_head || sp.n_head % sp.n_head_kv) return fail("synthetic spec: head split");
   if (sp.wtype != 2 && sp.wtype != 12) return fail("synthetic spec: wtype must be 2 (Q4_0) or 12 (Q4_K)");
+  if (!sp.vocab.empty() && (sp.scores.size() != sp.vocab.size() || sp.token_types.size() != sp.vocab.size()))
+    return fail("synthetic spec: vocab, scores and token_types differ in length");
   const int out_type = sp.out_type >= 0 ? sp.out_type : sp.wtype;
   auto qtype_ok = [](int t) { return t == 2 || t == 8 || t == 12 || t == 14; };
   if (!qtype_ok(out_type)) return fail("synthetic spec: out_type must be Q4_0, Q8_0, Q4_K or Q6_K");
@@ -403,7 +437,8 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
   h.insert(h.end(), {'G', 'G', 'U', 'F'});
   put<uint32_t>(h, 3);
   put<uint64_t>(h, plan.size());
-  put<uint64_t>(h, 14);
+  const bool with_vocab = !sp.vocab.empty();
+  put<uint64_t>(h, 14 + (with_vocab ? 7 : 0));
   kv_str(h, "general.architecture", "llama");
   kv_str(h, "general.name", sp.name);
   kv_u32(h, "general.alignment", (uint32_t)align);
@@ -418,6 +453,15 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
   kv_u32(h, "llama.context_length", sp.ctx_len);
   kv_u32(h, "llama.vocab_size", sp.n_vocab);
   kv_u64(h, "ulb.synthetic.seed", sp.seed);
+  if (with_vocab) {
+    kv_str(h, "tokenizer.ggml.model", "llama");
+    kv_arr_str(h, "tokenizer.ggml.tokens", sp.vocab);
+    kv_arr_num<float>(h, "tokenizer.ggml.scores", GV_F32, sp.scores);
+    kv_arr_num<int32_t>(h, "tokenizer.ggml.token_type", GV_I32, sp.token_types);
+    kv_u32(h, "tokenizer.ggml.bos_token_id", 1);
+    kv_u32(h, "tokenizer.ggml.eos_token_id", 2);
+    kv_u32(h, "tokenizer.ggml.unknown_token_id", 0);
+  }
   for (const PlannedTensor& t : plan) {
     put_str(h, t.name);
     put<uint32_t>(h, t.n_dims);

@@ -38,6 +38,9 @@ class GGUFFile {
   bool has(const std::string& key) const { return num_.count(key) || str_.count(key); }
   double num(const std::string& key, double dflt) const;
   std::string str(const std::string& key, const std::string& dflt) const;
+  /* array metadata (tokenizer.ggml.tokens / scores / token_type ...); nullptr if absent */
+  const std::vector<std::string>* str_array(const std::string& key) const;
+  const std::vector<double>* num_array(const std::string& key) const;
 
   uint32_t version = 0;
   uint64_t alignment = 32;
@@ -49,6 +52,8 @@ class GGUFFile {
   size_t map_len_ = 0;
   std::map<std::string, double> num_;
   std::map<std::string, std::string> str_;
+  std::map<std::string, std::vector<std::string>> strarr_;
+  std::map<std::string, std::vector<double>> numarr_;
 };
 
 /* bytes of n elements of a GGML type; 0 if unsupported or not a whole number of blocks */
@@ -66,6 +71,11 @@ struct SynthSpec {
   int out_type = -1;  /* output.weight: Q4_0 / Q8_0 / Q4_K / Q6_K; -1 = wtype */
   uint64_t seed = 0;
   float stddev = 0.02f;
+  /* optional SentencePiece vocabulary, written as tokenizer.ggml.{model, tokens, scores,
+     token_type, bos_token_id, eos_token_id, unknown_token_id} */
+  std::vector<std::string> vocab;
+  std::vector<float> scores;
+  std::vector<int32_t> token_types;
 };
 
 bool write_synthetic_gguf(const std::string& path, const SynthSpec& spec, int threads, std::string* err);

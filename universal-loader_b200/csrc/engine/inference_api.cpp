@@ -39,6 +39,7 @@
 
 #include "gguf.h"
 #include "spec_engine.h"
+#include "tokenizer.h"
 
 namespace py = pybind11;
 
@@ -399,6 +400,13 @@ class InferenceAPI {
     }
     const bool ok = engine_->load(path, draft);
     if (!ok) std::fprintf(stderr, "[InferenceAPI] load failed: %s\n", engine_->error().c_str());
+    if (ok && !draft) {
+      /* the target's GGUF vocabulary, when it has one, serves the text surface */
+      spm_ = ulbe::SpmTokenizer();
+      ulbe::GGUFFile f;
+      std::string e;
+      if (f.open(path, &e)) spm_.load(f, &e);
+    }
     return ok;
   }
 
@@ -422,6 +430,8 @@ class InferenceAPI {
     if (tokenizer_) {
       py::gil_scoped_acquire g;
       for (uint32_t t : tokenizer_(s)) ids.push_back((int32_t)t);
+    } else if (spm_.loaded()) {
+      ids = spm_.encode(s, true);
     } else {
       for (unsigned char c : s) ids.push_back((int32_t)c + 3);
     }
@@ -430,6 +440,7 @@ class InferenceAPI {
   }
 
   std::string decode(const std::vector<int32_t>& ids) const {
+    if (!tokenizer_ && spm_.loaded()) return spm_.decode(ids);
     std::string s;
     for (int32_t t : ids) {
       if (t >= 3 && t < 259) s.push_back((char)(t - 3));
@@ -448,6 +459,7 @@ class InferenceAPI {
   std::string wq_ = "NONE", aq_ = "NONE";
   ulbe::GenStats last_;
   std::function<std::vector<uint32_t>(const std::string&)> tokenizer_;
+  ulbe::SpmTokenizer spm_; /* the loaded target's GGUF vocabulary, if it has one */
   std::function<void(const std::string&, const std::string&)> kernel_compiler_;
 };
 
@@ -489,6 +501,12 @@ bool write_synthetic(const std::string& path, py::dict spec, int threads) {
   };
   type_of("embd_type", s.embd_type);
   type_of("out_type", s.out_type);
+  if (spec.contains("vocab")) {
+    s.vocab = spec["vocab"].cast<std::vector<std::string>>();
+    s.scores = spec.contains("scores") ? spec["scores"].cast<std::vector<float>>() : std::vector<float>(s.vocab.size(), 0.f);
+    s.token_types = spec.contains("token_types") ? spec["token_types"].cast<std::vector<int32_t>>()
+                                                 : std::vector<int32_t>(s.vocab.size(), 1);
+  }
   if (spec.contains("seed")) s.seed = spec["seed"].cast<uint64_t>();
   if (spec.contains("name")) s.name = spec["name"].cast<std::string>();
   if (threads <= 0) threads = (int)std::max(1u, std::thread::hardware_concurrency());
@@ -503,6 +521,16 @@ bool write_synthetic(const std::string& path, py::dict spec, int threads) {
 }
 
 }  // namespace vg
+
+/* the GGUF file's SentencePiece tokenizer, for text <-> ids without loading the model */
+static ulbe::SpmTokenizer gguf_spm(const std::string& path) {
+  ulbe::GGUFFile f;
+  std::string err;
+  if (!f.open(path, &err)) throw std::runtime_error(err);
+  ulbe::SpmTokenizer t;
+  if (!t.load(f, &err)) throw std::runtime_error(err);
+  return t;
+}
 
 PYBIND11_MODULE(vulkangguf, m) {
   using namespace vg;
@@ -616,6 +644,15 @@ PYBIND11_MODULE(vulkangguf, m) {
     if (ulb_tp_unique_id(id) != 0) throw std::runtime_error(ulb_last_error());
     return py::bytes(id, sizeof id);
   }, "A new 128-byte NCCL unique id (create on one rank, share with the others)");
+  m.def(
+      "gguf_tokenize",
+      [](const std::string& path, const std::string& text, bool add_bos) { return gguf_spm(path).encode(text, add_bos); },
+      py::arg("path"), py::arg("text"), py::arg("add_bos") = true,
+      "Token ids of text under the GGUF file's SentencePiece vocabulary (tokenizer.ggml.*)");
+  m.def(
+      "gguf_detokenize",
+      [](const std::string& path, const std::vector<int32_t>& ids) { return py::bytes(gguf_spm(path).decode(ids)); },
+      py::arg("path"), py::arg("ids"), "Text (UTF-8 bytes) of token ids under the GGUF file's vocabulary");
   m.def("write_synthetic_gguf", &write_synthetic, py::arg("path"), py::arg("spec"), py::arg("threads") = 0,
         "Write a synthetic LLaMA GGUF: Q4_0/Q4_K weights N(0, stddev), fp16 embeddings, unit norms; "
         "spec keys embd_type / out_type pick other token_embd (f32, f16, q4_0, q8_0, q4_k, q6_k) and "

@@ -1,0 +1,57 @@
+/*
+ * tokenizer.h — the GGUF "llama" tokenizer (a SentencePiece BPE vocabulary stored as
+ * tokenizer.ggml.tokens / scores / token_type) for the text surface of InferenceAPI.
+ *
+ * The reference's engine tokenizes with a placeholder (src/inference/tokenizer.cpp:13-64:
+ * whitespace-split words looked up as decimal id strings) and never reads the GGUF vocabulary;
+ * its BPETokenizer (src/inference/bpe_tokenizer.cpp:19-243) reads a private text format and is
+ * not wired in.  This class is what a GGUF LLaMA checkpoint needs instead: SentencePiece BPE
+ * encoding as the sentencepiece library performs it for LLaMA's model (identity normaliser,
+ * a dummy-prefix space, spaces as U+2581, byte fallback).
+ *
+ * encode: the text (with "▁" prepended and every ' ' replaced by "▁") is split into UTF-8
+ * characters; the adjacent pair whose concatenation is a NORMAL or USER_DEFINED piece with
+ * the highest score is merged (the leftmost pair on equal scores) until no pair merges; a
+ * final symbol that is not a piece becomes its bytes' <0xXX> pieces (or the unknown id).
+ * decode: pieces concatenated with "▁" as ' ', <0xXX> pieces as raw bytes, control pieces
+ * dropped, the unknown piece as " ⁇ ", and the leading space of the dummy prefix removed.
+ */
+#pragma once
+#include <cstdint>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace ulbe {
+
+class GGUFFile;
+
+class SpmTokenizer {
+ public:
+  /* GGUF token types (as tokenizer.ggml.token_type stores them) */
+  enum { NORMAL = 1, UNKNOWN = 2, CONTROL = 3, USER_DEFINED = 4, UNUSED = 5, BYTE = 6 };
+
+  /* from a GGUF file with tokenizer.ggml.model == "llama"; false (and *err) otherwise */
+  bool load(const GGUFFile& f, std::string* err);
+  /* from explicit pieces, scores and types (equal lengths) */
+  bool load(const std::vector<std::string>& pieces, const std::vector<float>& scores,
+            const std::vector<int32_t>& types, int bos, int eos, int unk, std::string* err);
+
+  std::vector<int32_t> encode(const std::string& text, bool add_bos) const;
+  std::string decode(const std::vector<int32_t>& ids) const;
+
+  bool loaded() const { return !pieces_.empty(); }
+  int bos() const { return bos_; }
+  int eos() const { return eos_; }
+  size_t size() const { return pieces_.size(); }
+
+ private:
+  std::vector<std::string> pieces_;
+  std::vector<float> scores_;
+  std::vector<int32_t> types_;
+  std::unordered_map<std::string, int32_t> mergeable_; /* NORMAL / USER_DEFINED pieces */
+  int32_t byte_id_[256];
+  int bos_ = 1, eos_ = 2, unk_ = 0;
+};
+
+}  // namespace ulbe
