@@ -89,6 +89,18 @@ def test_bos_and_decode_round_trip(trained):
         assert vg.gguf_detokenize(path, ids).decode("utf-8") == sp.decode(ids[1:]) == t
 
 
+def test_decode_of_random_ids_matches_sentencepiece(trained):
+    """Any id sequence (byte runs that are not valid UTF-8, control and unknown ids included)
+    decodes as sentencepiece decodes it."""
+    sp, path, words = trained
+    import vulkangguf as vg
+    rng = random.Random(3)
+    n = sp.get_piece_size()
+    for _ in range(300):
+        ids = [rng.randrange(n) for _ in range(rng.randint(1, 20))]
+        assert vg.gguf_detokenize(path, ids).decode("utf-8") == sp.decode(ids), ids
+
+
 def test_gguf_without_vocabulary_is_rejected(tmp_path):
     import vulkangguf as vg
     p = str(tmp_path / "novocab.gguf")

@@ -21,8 +21,9 @@
  * set_speculation_length (as SpeculativeDecoder::set_speculation_length,
  * speculative_decoder.h:40), set_seed, GenerationConfig.seed, generate_tokens,
  * get_last_stats, and the module function write_synthetic_gguf.
- * Text: the GGUF tokenizer is not on this path; without a registered custom tokenizer,
- * text maps to byte-fallback ids (byte b -> id b + 3) and back.
+ * Text: a registered custom tokenizer first; else the target GGUF's SentencePiece vocabulary
+ * (tokenizer.ggml.*, tokenizer.cpp) when it has one; else byte-fallback ids (byte b -> id
+ * b + 3) and back.
  */
 #include <pybind11/functional.h>
 #include <pybind11/pybind11.h>
@@ -441,12 +442,18 @@ class InferenceAPI {
 
   std::string decode(const std::vector<int32_t>& ids) const {
     if (!tokenizer_ && spm_.loaded()) return spm_.decode(ids);
-    std::string s;
+    /* byte-fallback ids: runs of bytes as UTF-8 (U+FFFD for invalid bytes), others as <id> */
+    std::string s, run;
     for (int32_t t : ids) {
-      if (t >= 3 && t < 259) s.push_back((char)(t - 3));
-      else s += "<" + std::to_string(t) + ">";
+      if (t >= 3 && t < 259) {
+        run.push_back((char)(t - 3));
+        continue;
+      }
+      s += ulbe::bytes_to_utf8(run);
+      run.clear();
+      s += "<" + std::to_string(t) + ">";
     }
-    return s;
+    return s + ulbe::bytes_to_utf8(run);
   }
 
   mutable std::mutex mu_;

@@ -11,6 +11,36 @@ namespace ulbe {
 namespace {
 const char kSpace[] = "\xe2\x96\x81"; /* U+2581, SentencePiece's whitespace mark */
 
+/* the bytes of consecutive <0xXX> pieces as UTF-8: each valid character as is, every byte
+   that does not start one (bad lead, short or overlong sequence, surrogate, > U+10FFFF) as
+   U+FFFD */
+void append_bytes_utf8(const std::string& b, std::string* s) {
+  size_t i = 0;
+  while (i < b.size()) {
+    const unsigned char c = (unsigned char)b[i];
+    size_t n = 0;
+    uint32_t cp = 0, lo = 0;
+    if (c < 0x80) { n = 1; cp = c; }
+    else if ((c & 0xE0) == 0xC0) { n = 2; cp = c & 0x1F; lo = 0x80; }
+    else if ((c & 0xF0) == 0xE0) { n = 3; cp = c & 0x0F; lo = 0x800; }
+    else if ((c & 0xF8) == 0xF0) { n = 4; cp = c & 0x07; lo = 0x10000; }
+    bool ok = n > 0 && i + n <= b.size();
+    for (size_t k = 1; ok && k < n; ++k) {
+      const unsigned char cc = (unsigned char)b[i + k];
+      if ((cc & 0xC0) != 0x80) ok = false;
+      else cp = (cp << 6) | (cc & 0x3F);
+    }
+    if (ok && n > 1 && (cp < lo || cp > 0x10FFFF || (cp >= 0xD800 && cp <= 0xDFFF))) ok = false;
+    if (ok) {
+      s->append(b, i, n);
+      i += n;
+    } else {
+      s->append("\xef\xbf\xbd");
+      i += 1;
+    }
+  }
+}
+
 /* byte length of the UTF-8 character starting with c (1 for a stray continuation byte) */
 size_t utf8_len(unsigned char c) {
   if (c < 0x80) return 1;
@@ -20,6 +50,12 @@ size_t utf8_len(unsigned char c) {
   return 1;
 }
 }  // namespace
+
+std::string bytes_to_utf8(const std::string& b) {
+  std::string s;
+  append_bytes_utf8(b, &s);
+  return s;
+}
 
 bool SpmTokenizer::load(const std::vector<std::string>& pieces, const std::vector<float>& scores,
                         const std::vector<int32_t>& types, int bos, int eos, int unk, std::string* err) {
@@ -131,18 +167,20 @@ std::vector<int32_t> SpmTokenizer::encode(const std::string& text, bool add_bos)
 }
 
 std::string SpmTokenizer::decode(const std::vector<int32_t>& ids) const {
-  std::string s;
+  std::string s, bytes;
   for (int32_t id : ids) {
     if (id < 0 || (size_t)id >= pieces_.size()) continue;
     const int t = types_[id];
     if (t == CONTROL || t == UNUSED) continue;
-    if (t == UNKNOWN) {
-      s += " \xe2\x81\x87 ";
-      continue;
-    }
     if (t == BYTE) {
       unsigned v = 0;
-      if (std::sscanf(pieces_[id].c_str(), "<0x%02X>", &v) == 1) s.push_back((char)v);
+      if (std::sscanf(pieces_[id].c_str(), "<0x%02X>", &v) == 1) bytes.push_back((char)v);
+      continue;
+    }
+    append_bytes_utf8(bytes, &s);
+    bytes.clear();
+    if (t == UNKNOWN) {
+      s += " \xe2\x81\x87 ";
       continue;
     }
     const std::string& p = pieces_[id];
@@ -155,6 +193,7 @@ std::string SpmTokenizer::decode(const std::vector<int32_t>& ids) const {
       }
     }
   }
+  append_bytes_utf8(bytes, &s);
   if (!s.empty() && s[0] == ' ') s.erase(0, 1); /* the dummy prefix */
   return s;
 }

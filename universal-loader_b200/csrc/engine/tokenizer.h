@@ -13,8 +13,9 @@
  * characters; the adjacent pair whose concatenation is a NORMAL or USER_DEFINED piece with
  * the highest score is merged (the leftmost pair on equal scores) until no pair merges; a
  * final symbol that is not a piece becomes its bytes' <0xXX> pieces (or the unknown id).
- * decode: pieces concatenated with "▁" as ' ', <0xXX> pieces as raw bytes, control pieces
- * dropped, the unknown piece as " ⁇ ", and the leading space of the dummy prefix removed.
+ * decode: pieces concatenated with "▁" as ' ', runs of <0xXX> pieces as UTF-8 (U+FFFD for
+ * each byte that starts no valid character), control pieces dropped, the unknown piece as
+ * " ⁇ ", and the leading space of the dummy prefix removed -- always valid UTF-8.
  */
 #pragma once
 #include <cstdint>
@@ -25,6 +26,9 @@
 namespace ulbe {
 
 class GGUFFile;
+
+/* b as valid UTF-8: each valid character kept, every other byte as U+FFFD */
+std::string bytes_to_utf8(const std::string& b);
 
 class SpmTokenizer {
  public:
