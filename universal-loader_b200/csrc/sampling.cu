@@ -53,19 +53,20 @@ __device__ __forceinline__ float unkey(uint32_t k) {
 }
 
 /* Visit every element of a logits row as f(i, x): 128-bit loads when the row is 16-byte
-   aligned and V % 4 == 0 (each thread walks float4s i = tid, tid + BT, ...), else scalar. */
+   aligned and V % 4 == 0 (each thread walks float4s i = tid, tid + BT, ..., eight loads in
+   flight, in that order whatever the unrolling), else scalar. */
 template <int BT, typename F>
 __device__ __forceinline__ void row_for_each(const float* __restrict__ l, int V, F f) {
   if ((((uintptr_t)l) & 15) == 0 && (V & 3) == 0) {
     const float4* l4 = reinterpret_cast<const float4*>(l);
     const int V4 = V >> 2;
     int i = threadIdx.x;
-    for (; i + 3 * BT < V4; i += 4 * BT) { /* four 16-byte loads in flight per thread */
-      float4 a[4];
+    for (; i + 7 * BT < V4; i += 8 * BT) { /* eight 16-byte loads in flight per thread */
+      float4 a[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) a[u] = __ldg(l4 + i + u * BT);
+      for (int u = 0; u < 8; ++u) a[u] = __ldg(l4 + i + u * BT);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         const int b = 4 * (i + u * BT);
         f(b, a[u].x); f(b + 1, a[u].y); f(b + 2, a[u].z); f(b + 3, a[u].w);
       }
@@ -317,12 +318,16 @@ __device__ __forceinline__ float rng_u(uint64_t seed, uint32_t round, uint32_t s
 
 /* ------------------------------------------------------------------ kernels */
 
-/* one CTA per row: draft / first-token sampling. out[row * out_stride] = token */
-__global__ void __launch_bounds__(ST) sample_kernel(const float* __restrict__ logits, int V, int ld, ulb_warp w,
+/* one CTA of BT threads per row: draft / first-token sampling. out[row * out_stride] = token.
+   Greedy rows (an argmax, lowest index on ties, whatever BT) run with 1024 threads so the
+   whole row is requested in about one round trip; sampled rows with ST, the block size of
+   stats_kernel, so both reduce the row's sums in the same order. */
+template <int BT>
+__global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ logits, int V, int ld, ulb_warp w,
                                                     uint64_t seed, const uint32_t* dev_round, uint32_t round,
                                                     uint32_t slot, uint32_t tag, uint32_t seq_base, int32_t* out,
                                                     int out_stride) {
-  __shared__ SmemRed<ST> s;
+  __shared__ SmemRed<BT> s;
   __shared__ RowStats st;
   pdl_wait();
   pdl_trigger();
@@ -473,8 +478,12 @@ int launch_sample_seq(Ctx* c, const float* logits, int rows, int V, int ld, cons
                       const uint32_t* dev_round, uint32_t round, uint32_t slot, uint32_t tag, uint32_t seq_base,
                       int32_t* out, int out_stride) {
   if (rows == 0) return ULB_OK;
-  cudaError_t e = launch_k(c, sample_kernel, dim3(rows), dim3(ST), 0, logits, V, ld, *w, seed, dev_round, round,
-                           slot, tag, seq_base, out, out_stride);
+  constexpr int kGreedyThreads = 1024;
+  cudaError_t e = !(w->temperature > 0.f)
+                      ? launch_k(c, sample_kernel<kGreedyThreads>, dim3(rows), dim3(kGreedyThreads), 0, logits, V, ld,
+                                 *w, seed, dev_round, round, slot, tag, seq_base, out, out_stride)
+                      : launch_k(c, sample_kernel<ST>, dim3(rows), dim3(ST), 0, logits, V, ld, *w, seed, dev_round,
+                                 round, slot, tag, seq_base, out, out_stride);
   if (e != cudaSuccess) return cuda_error(e, "sample launch", __FILE__, __LINE__);
   return ULB_OK;
 }
