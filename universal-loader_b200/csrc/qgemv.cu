@@ -23,7 +23,12 @@
  *    memory by the last warp to finish its part, which runs the epilogue; the split depends
  *    on (N, K, SM count) only, so a row's arithmetic never depends on M;
  *  - the fused epilogues write RoPE'd Q / K / V (K and V straight into the fp16 KV cache),
- *    SiLU(gate)*up in fp16, or the fp32 residual add.
+ *    SiLU(gate)*up in fp16, or the fp32 residual add;
+ *  - a GEMV's tail prefetches the weights of GEMVs to come into L2 (up to two ranges the
+ *    forward pass names), e.g. the QKV GEMV's tail brings attn_output and ffn_gate_up in while
+ *    the attention kernel leaves HBM mostly idle;
+ *  - Q8_0 / Q6_K matrices (LM heads of llama.cpp files) stay in GGUF rows and run through
+ *    rowgemv_kernel, one warp per output row.
  * The tensor pipe is idle in this regime (<= 3.6 flop/B at M = 1); mma.sync is used as the
  * cheapest-to-issue dot product engine.
  */

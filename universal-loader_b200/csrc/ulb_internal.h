@@ -85,9 +85,9 @@ struct Ctx {
   size_t tc_ws_floats = 0;
   int* tc_cnt = nullptr;               /* kTcCounters arrival counters, zero between launches */
   int tp_rank = 0, tp_world = 1;
-  /* hint: the weights the next GEMV on the stream will read (set just before it by the
-     forward pass); the GEMV launched after the hint prefetches them into L2 from its tail.
-     Every GEMV launch clears it. */
+  /* hint: up to two byte ranges (weights of GEMVs to come) that the next GEMV launched on the
+     stream prefetches into L2 from its tail; set just before that launch by the forward
+     pass, cleared by every GEMV launch. */
   const void* pf_ptr = nullptr;
   size_t pf_bytes = 0;
   const void* pf2_ptr = nullptr; /* a second range, prefetched after the first */
