@@ -76,7 +76,7 @@ def test_encode_matches_sentencepiece(trained):
     import vulkangguf as vg
     for t in _texts(words):
         want = sp.encode(t) if t else []
-        got = vg.gguf_tokenize(path, t, False)
+        got = vg.gguf_tokenize(path, t, add_bos=False)
         assert got == want, (t, got, want)
 
 
@@ -84,7 +84,7 @@ def test_bos_and_decode_round_trip(trained):
     sp, path, words = trained
     import vulkangguf as vg
     for t in _texts(words, seed=2, n=100):
-        ids = vg.gguf_tokenize(path, t, True)
+        ids = vg.gguf_tokenize(path, t)  # the file has no add_bos_token key: BOS by default
         assert ids[0] == 1  # <s>
         assert vg.gguf_detokenize(path, ids).decode("utf-8") == sp.decode(ids[1:]) == t
 
@@ -99,6 +99,30 @@ def test_decode_of_random_ids_matches_sentencepiece(trained):
     for _ in range(300):
         ids = [rng.randrange(n) for _ in range(rng.randint(1, 20))]
         assert vg.gguf_detokenize(path, ids).decode("utf-8") == sp.decode(ids), ids
+
+
+def test_file_flags_no_space_prefix_and_no_bos(tmp_path):
+    """A file with tokenizer.ggml.add_space_prefix = false encodes without the dummy prefix
+    (as sentencepiece with add_dummy_prefix=False) and keeps a leading space on decode; with
+    add_bos_token = false, add_bos=None prepends no BOS."""
+    lines, words = _corpus(seed=5, n_lines=2000)
+    buf = io.BytesIO()
+    spm.SentencePieceTrainer.train(sentence_iterator=iter(lines), model_writer=buf, vocab_size=500,
+                                   model_type="bpe", byte_fallback=True, normalization_rule_name="identity",
+                                   add_dummy_prefix=False, remove_extra_whitespaces=False, minloglevel=2)
+    sp = spm.SentencePieceProcessor(model_proto=buf.getvalue())
+    n = sp.get_piece_size()
+    types = [2 if sp.is_unknown(i) else 3 if sp.is_control(i) else 6 if sp.is_byte(i) else 1 for i in range(n)]
+    import vulkangguf as vg
+    path = str(tmp_path / "noprefix.gguf")
+    vg.write_synthetic_gguf(path, dict(n_layer=1, d_model=256, n_head=4, n_head_kv=4, d_ff=512, n_vocab=n,
+                                       wtype="q4_0", seed=3, vocab=[sp.id_to_piece(i) for i in range(n)],
+                                       scores=[sp.get_score(i) for i in range(n)], token_types=types,
+                                       add_bos=False, add_space_prefix=False))
+    for t in _texts(words, seed=6, n=100) + [" leading space", "  two"]:
+        ids = vg.gguf_tokenize(path, t)
+        assert ids == (sp.encode(t) if t else []), t
+        assert vg.gguf_detokenize(path, ids).decode("utf-8") == sp.decode(ids) == t
 
 
 def test_gguf_without_vocabulary_is_rejected(tmp_path):

@@ -370,6 +370,11 @@ void kv_u32(std::vector<uint8_t>& b, const std::string& k, uint32_t v) { put_str
 void kv_f32(std::vector<uint8_t>& b, const std::string& k, float v) { put_str(b, k); put<uint32_t>(b, GV_F32); put(b, v); }
 void kv_u64(std::vector<uint8_t>& b, const std::string& k, uint64_t v) { put_str(b, k); put<uint32_t>(b, GV_U64); put(b, v); }
 void kv_str(std::vector<uint8_t>& b, const std::string& k, const std::string& v) { put_str(b, k); put<uint32_t>(b, GV_STR); put_str(b, v); }
+void kv_bool(std::vector<uint8_t>& b, const std::string& k, bool v) {
+  put_str(b, k);
+  put<uint32_t>(b, GV_BOOL);
+  put<uint8_t>(b, v ? 1 : 0);
+}
 void kv_arr_str(std::vector<uint8_t>& b, const std::string& k, const std::vector<std::string>& v) {
   put_str(b, k);
   put<uint32_t>(b, GV_ARR);
@@ -438,7 +443,8 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
   put<uint32_t>(h, 3);
   put<uint64_t>(h, plan.size());
   const bool with_vocab = !sp.vocab.empty();
-  put<uint64_t>(h, 14 + (with_vocab ? 7 : 0));
+  const int n_flags = with_vocab ? (sp.add_bos >= 0) + (sp.add_space_prefix >= 0) : 0;
+  put<uint64_t>(h, 14 + (with_vocab ? 7 : 0) + n_flags);
   kv_str(h, "general.architecture", "llama");
   kv_str(h, "general.name", sp.name);
   kv_u32(h, "general.alignment", (uint32_t)align);
@@ -461,6 +467,8 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
     kv_u32(h, "tokenizer.ggml.bos_token_id", 1);
     kv_u32(h, "tokenizer.ggml.eos_token_id", 2);
     kv_u32(h, "tokenizer.ggml.unknown_token_id", 0);
+    if (sp.add_bos >= 0) kv_bool(h, "tokenizer.ggml.add_bos_token", sp.add_bos != 0);
+    if (sp.add_space_prefix >= 0) kv_bool(h, "tokenizer.ggml.add_space_prefix", sp.add_space_prefix != 0);
   }
   for (const PlannedTensor& t : plan) {
     put_str(h, t.name);

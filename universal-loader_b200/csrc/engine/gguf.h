@@ -76,6 +76,7 @@ struct SynthSpec {
   std::vector<std::string> vocab;
   std::vector<float> scores;
   std::vector<int32_t> token_types;
+  int add_bos = -1, add_space_prefix = -1; /* tokenizer.ggml.add_bos_token / add_space_prefix; -1: not written */
 };
 
 bool write_synthetic_gguf(const std::string& path, const SynthSpec& spec, int threads, std::string* err);

@@ -432,7 +432,7 @@ class InferenceAPI {
       py::gil_scoped_acquire g;
       for (uint32_t t : tokenizer_(s)) ids.push_back((int32_t)t);
     } else if (spm_.loaded()) {
-      ids = spm_.encode(s, true);
+      ids = spm_.encode(s, spm_.add_bos());
     } else {
       for (unsigned char c : s) ids.push_back((int32_t)c + 3);
     }
@@ -513,6 +513,8 @@ bool write_synthetic(const std::string& path, py::dict spec, int threads) {
     s.scores = spec.contains("scores") ? spec["scores"].cast<std::vector<float>>() : std::vector<float>(s.vocab.size(), 0.f);
     s.token_types = spec.contains("token_types") ? spec["token_types"].cast<std::vector<int32_t>>()
                                                  : std::vector<int32_t>(s.vocab.size(), 1);
+    if (spec.contains("add_bos")) s.add_bos = spec["add_bos"].cast<bool>() ? 1 : 0;
+    if (spec.contains("add_space_prefix")) s.add_space_prefix = spec["add_space_prefix"].cast<bool>() ? 1 : 0;
   }
   if (spec.contains("seed")) s.seed = spec["seed"].cast<uint64_t>();
   if (spec.contains("name")) s.name = spec["name"].cast<std::string>();
@@ -653,9 +655,13 @@ PYBIND11_MODULE(vulkangguf, m) {
   }, "A new 128-byte NCCL unique id (create on one rank, share with the others)");
   m.def(
       "gguf_tokenize",
-      [](const std::string& path, const std::string& text, bool add_bos) { return gguf_spm(path).encode(text, add_bos); },
-      py::arg("path"), py::arg("text"), py::arg("add_bos") = true,
-      "Token ids of text under the GGUF file's SentencePiece vocabulary (tokenizer.ggml.*)");
+      [](const std::string& path, const std::string& text, py::object add_bos) {
+        const ulbe::SpmTokenizer t = gguf_spm(path);
+        return t.encode(text, add_bos.is_none() ? t.add_bos() : add_bos.cast<bool>());
+      },
+      py::arg("path"), py::arg("text"), py::arg("add_bos") = py::none(),
+      "Token ids of text under the GGUF file's SentencePiece vocabulary (tokenizer.ggml.*); "
+      "add_bos=None follows the file's tokenizer.ggml.add_bos_token");
   m.def(
       "gguf_detokenize",
       [](const std::string& path, const std::vector<int32_t>& ids) { return py::bytes(gguf_spm(path).decode(ids)); },

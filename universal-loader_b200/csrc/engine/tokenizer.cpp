@@ -99,15 +99,18 @@ bool SpmTokenizer::load(const GGUFFile& f, std::string* err) {
     for (size_t i = 0; i < sc->size(); ++i) scores[i] = (float)(*sc)[i];
   if (ty && ty->size() == tok->size())
     for (size_t i = 0; i < ty->size(); ++i) types[i] = (int32_t)(*ty)[i];
-  return load(*tok, scores, types, (int)f.num("tokenizer.ggml.bos_token_id", 1),
-              (int)f.num("tokenizer.ggml.eos_token_id", 2), (int)f.num("tokenizer.ggml.unknown_token_id", 0), err);
+  if (!load(*tok, scores, types, (int)f.num("tokenizer.ggml.bos_token_id", 1),
+            (int)f.num("tokenizer.ggml.eos_token_id", 2), (int)f.num("tokenizer.ggml.unknown_token_id", 0), err))
+    return false;
+  set_flags(f.num("tokenizer.ggml.add_bos_token", 1) != 0, f.num("tokenizer.ggml.add_space_prefix", 1) != 0);
+  return true;
 }
 
 std::vector<int32_t> SpmTokenizer::encode(const std::string& text, bool add_bos) const {
   std::vector<int32_t> out;
   if (add_bos && bos_ >= 0) out.push_back(bos_);
   if (text.empty()) return out;
-  std::string norm = kSpace;
+  std::string norm = add_space_prefix_ ? kSpace : "";
   for (char ch : text) {
     if (ch == ' ') norm += kSpace;
     else norm.push_back(ch);
@@ -194,7 +197,7 @@ std::string SpmTokenizer::decode(const std::vector<int32_t>& ids) const {
     }
   }
   append_bytes_utf8(bytes, &s);
-  if (!s.empty() && s[0] == ' ') s.erase(0, 1); /* the dummy prefix */
+  if (add_space_prefix_ && !s.empty() && s[0] == ' ') s.erase(0, 1); /* the dummy prefix */
   return s;
 }
 

@@ -9,7 +9,8 @@
  * encoding as the sentencepiece library performs it for LLaMA's model (identity normaliser,
  * a dummy-prefix space, spaces as U+2581, byte fallback).
  *
- * encode: the text (with "▁" prepended and every ' ' replaced by "▁") is split into UTF-8
+ * encode: the text (with "▁" prepended unless the file's tokenizer.ggml.add_space_prefix is
+ * false, and every ' ' replaced by "▁") is split into UTF-8
  * characters; the adjacent pair whose concatenation is a NORMAL or USER_DEFINED piece with
  * the highest score is merged (the leftmost pair on equal scores) until no pair merges; a
  * final symbol that is not a piece becomes its bytes' <0xXX> pieces (or the unknown id).
@@ -40,6 +41,14 @@ class SpmTokenizer {
   /* from explicit pieces, scores and types (equal lengths) */
   bool load(const std::vector<std::string>& pieces, const std::vector<float>& scores,
             const std::vector<int32_t>& types, int bos, int eos, int unk, std::string* err);
+  /* tokenizer.ggml.add_bos_token / add_space_prefix (both true unless the file says false):
+     whether text calls prepend BOS, and whether encode prepends the dummy-prefix space (and
+     decode removes it) */
+  void set_flags(bool add_bos, bool add_space_prefix) {
+    add_bos_ = add_bos;
+    add_space_prefix_ = add_space_prefix;
+  }
+  bool add_bos() const { return add_bos_; }
 
   std::vector<int32_t> encode(const std::string& text, bool add_bos) const;
   std::string decode(const std::vector<int32_t>& ids) const;
@@ -56,6 +65,7 @@ class SpmTokenizer {
   std::unordered_map<std::string, int32_t> mergeable_; /* NORMAL / USER_DEFINED pieces */
   int32_t byte_id_[256];
   int bos_ = 1, eos_ = 2, unk_ = 0;
+  bool add_bos_ = true, add_space_prefix_ = true;
 };
 
 }  // namespace ulbe
