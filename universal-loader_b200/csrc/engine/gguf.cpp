@@ -444,7 +444,8 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
   put<uint64_t>(h, plan.size());
   const bool with_vocab = !sp.vocab.empty();
   const int n_flags = with_vocab ? (sp.add_bos >= 0) + (sp.add_space_prefix >= 0) : 0;
-  put<uint64_t>(h, 14 + (with_vocab ? 7 : 0) + n_flags);
+  const int n_merges = with_vocab && !sp.merges.empty() ? 1 : 0;
+  put<uint64_t>(h, 14 + (with_vocab ? 7 : 0) + n_flags + n_merges);
   kv_str(h, "general.architecture", "llama");
   kv_str(h, "general.name", sp.name);
   kv_u32(h, "general.alignment", (uint32_t)align);
@@ -460,7 +461,8 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
   kv_u32(h, "llama.vocab_size", sp.n_vocab);
   kv_u64(h, "ulb.synthetic.seed", sp.seed);
   if (with_vocab) {
-    kv_str(h, "tokenizer.ggml.model", "llama");
+    kv_str(h, "tokenizer.ggml.model", n_merges ? "gpt2" : "llama");
+    if (n_merges) kv_arr_str(h, "tokenizer.ggml.merges", sp.merges);
     kv_arr_str(h, "tokenizer.ggml.tokens", sp.vocab);
     kv_arr_num<float>(h, "tokenizer.ggml.scores", GV_F32, sp.scores);
     kv_arr_num<int32_t>(h, "tokenizer.ggml.token_type", GV_I32, sp.token_types);

@@ -76,6 +76,7 @@ struct SynthSpec {
   std::vector<std::string> vocab;
   std::vector<float> scores;
   std::vector<int32_t> token_types;
+  std::vector<std::string> merges; /* non-empty: a byte-level BPE ("gpt2") vocabulary */
   int add_bos = -1, add_space_prefix = -1; /* tokenizer.ggml.add_bos_token / add_space_prefix; -1: not written */
 };
 

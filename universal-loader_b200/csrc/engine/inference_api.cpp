@@ -403,7 +403,7 @@ class InferenceAPI {
     if (!ok) std::fprintf(stderr, "[InferenceAPI] load failed: %s\n", engine_->error().c_str());
     if (ok && !draft) {
       /* the target's GGUF vocabulary, when it has one, serves the text surface */
-      spm_ = ulbe::SpmTokenizer();
+      spm_ = ulbe::GgufTokenizer();
       ulbe::GGUFFile f;
       std::string e;
       if (f.open(path, &e)) spm_.load(f, &e);
@@ -466,7 +466,7 @@ class InferenceAPI {
   std::string wq_ = "NONE", aq_ = "NONE";
   ulbe::GenStats last_;
   std::function<std::vector<uint32_t>(const std::string&)> tokenizer_;
-  ulbe::SpmTokenizer spm_; /* the loaded target's GGUF vocabulary, if it has one */
+  ulbe::GgufTokenizer spm_; /* the loaded target's GGUF vocabulary, if it has one */
   std::function<void(const std::string&, const std::string&)> kernel_compiler_;
 };
 
@@ -513,6 +513,7 @@ bool write_synthetic(const std::string& path, py::dict spec, int threads) {
     s.scores = spec.contains("scores") ? spec["scores"].cast<std::vector<float>>() : std::vector<float>(s.vocab.size(), 0.f);
     s.token_types = spec.contains("token_types") ? spec["token_types"].cast<std::vector<int32_t>>()
                                                  : std::vector<int32_t>(s.vocab.size(), 1);
+    if (spec.contains("merges")) s.merges = spec["merges"].cast<std::vector<std::string>>();
     if (spec.contains("add_bos")) s.add_bos = spec["add_bos"].cast<bool>() ? 1 : 0;
     if (spec.contains("add_space_prefix")) s.add_space_prefix = spec["add_space_prefix"].cast<bool>() ? 1 : 0;
   }
@@ -532,11 +533,11 @@ bool write_synthetic(const std::string& path, py::dict spec, int threads) {
 }  // namespace vg
 
 /* the GGUF file's SentencePiece tokenizer, for text <-> ids without loading the model */
-static ulbe::SpmTokenizer gguf_spm(const std::string& path) {
+static ulbe::GgufTokenizer gguf_spm(const std::string& path) {
   ulbe::GGUFFile f;
   std::string err;
   if (!f.open(path, &err)) throw std::runtime_error(err);
-  ulbe::SpmTokenizer t;
+  ulbe::GgufTokenizer t;
   if (!t.load(f, &err)) throw std::runtime_error(err);
   return t;
 }
@@ -656,7 +657,7 @@ PYBIND11_MODULE(vulkangguf, m) {
   m.def(
       "gguf_tokenize",
       [](const std::string& path, const std::string& text, py::object add_bos) {
-        const ulbe::SpmTokenizer t = gguf_spm(path);
+        const ulbe::GgufTokenizer t = gguf_spm(path);
         return t.encode(text, add_bos.is_none() ? t.add_bos() : add_bos.cast<bool>());
       },
       py::arg("path"), py::arg("text"), py::arg("add_bos") = py::none(),

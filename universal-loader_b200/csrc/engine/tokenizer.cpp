@@ -202,3 +202,217 @@ std::string SpmTokenizer::decode(const std::vector<int32_t>& ids) const {
 }
 
 }  // namespace ulbe
+
+/* ------------------------------------------------------------------ byte-level BPE ("gpt2") */
+namespace ulbe {
+namespace {
+#include "unicode_ranges.h"
+
+template <size_t N>
+bool in_ranges(const uint32_t (&r)[N][2], uint32_t cp) {
+  size_t lo = 0, hi = N;
+  while (lo < hi) {
+    const size_t mid = (lo + hi) / 2;
+    if (cp < r[mid][0]) hi = mid;
+    else if (cp > r[mid][1]) lo = mid + 1;
+    else return true;
+  }
+  return false;
+}
+bool is_letter(uint32_t c) { return in_ranges(kLetterRanges, c); }
+bool is_number(uint32_t c) { return in_ranges(kNumberRanges, c); }
+/* Unicode White_Space */
+bool is_space(uint32_t c) {
+  return (c >= 0x09 && c <= 0x0D) || c == 0x20 || c == 0x85 || c == 0xA0 || c == 0x1680 ||
+         (c >= 0x2000 && c <= 0x200A) || c == 0x2028 || c == 0x2029 || c == 0x202F || c == 0x205F || c == 0x3000;
+}
+bool is_nl(uint32_t c) { return c == '\r' || c == '\n'; }
+bool is_other(uint32_t c) { return !is_space(c) && !is_letter(c) && !is_number(c); }
+
+std::string utf8_of(uint32_t cp) {
+  std::string s;
+  if (cp < 0x80) s.push_back((char)cp);
+  else if (cp < 0x800) { s.push_back((char)(0xC0 | (cp >> 6))); s.push_back((char)(0x80 | (cp & 0x3F))); }
+  else if (cp < 0x10000) {
+    s.push_back((char)(0xE0 | (cp >> 12)));
+    s.push_back((char)(0x80 | ((cp >> 6) & 0x3F)));
+    s.push_back((char)(0x80 | (cp & 0x3F)));
+  } else {
+    s.push_back((char)(0xF0 | (cp >> 18)));
+    s.push_back((char)(0x80 | ((cp >> 12) & 0x3F)));
+    s.push_back((char)(0x80 | ((cp >> 6) & 0x3F)));
+    s.push_back((char)(0x80 | (cp & 0x3F)));
+  }
+  return s;
+}
+
+/* code points of s with their byte offsets (offs has one extra entry, s.size()); a byte that
+   starts no valid character counts as one character of its own (category: other) */
+void code_points(const std::string& s, std::vector<uint32_t>* cps, std::vector<size_t>* offs) {
+  for (size_t i = 0; i < s.size();) {
+    const unsigned char c = (unsigned char)s[i];
+    size_t n = utf8_len(c);
+    uint32_t cp = n == 1 ? c : n == 2 ? (c & 0x1F) : n == 3 ? (c & 0x0F) : (c & 0x07);
+    bool ok = i + n <= s.size() && !(n == 1 && c >= 0x80);
+    for (size_t k = 1; ok && k < n; ++k) {
+      const unsigned char cc = (unsigned char)s[i + k];
+      if ((cc & 0xC0) != 0x80) ok = false;
+      else cp = (cp << 6) | (cc & 0x3F);
+    }
+    if (!ok) { n = 1; cp = 0xFFFD; }
+    cps->push_back(cp);
+    offs->push_back(i);
+    i += n;
+  }
+  offs->push_back(s.size());
+}
+
+/* end (exclusive, in code points) of the piece Llama-3's split pattern matches at i */
+size_t split_piece(const std::vector<uint32_t>& c, size_t i) {
+  const size_t n = c.size();
+  auto lower = [](uint32_t x) { return x >= 'A' && x <= 'Z' ? x + 32 : x; };
+  /* (?i:'s|'t|'re|'ve|'m|'ll|'d) */
+  if (c[i] == '\'' && i + 1 < n) {
+    const uint32_t a = lower(c[i + 1]), b = i + 2 < n ? lower(c[i + 2]) : 0;
+    if (a == 's' || a == 't' || a == 'm' || a == 'd') return i + 2;
+    if ((a == 'r' && b == 'e') || (a == 'v' && b == 'e') || (a == 'l' && b == 'l')) return i + 3;
+  }
+  /* [^\r\n\p{L}\p{N}]?\p{L}+ */
+  {
+    size_t j = i;
+    if (!is_nl(c[i]) && !is_letter(c[i]) && !is_number(c[i]) && i + 1 < n && is_letter(c[i + 1])) j = i + 1;
+    if (is_letter(c[j])) {
+      while (j < n && is_letter(c[j])) ++j;
+      return j;
+    }
+  }
+  /* \p{N}{1,3} */
+  if (is_number(c[i])) {
+    size_t j = i;
+    while (j < n && j < i + 3 && is_number(c[j])) ++j;
+    return j;
+  }
+  /*  ?[^\s\p{L}\p{N}]+[\r\n]* */
+  {
+    size_t j = i;
+    if (c[i] == ' ' && i + 1 < n && is_other(c[i + 1])) j = i + 1;
+    if (is_other(c[j])) {
+      while (j < n && is_other(c[j])) ++j;
+      while (j < n && is_nl(c[j])) ++j;
+      return j;
+    }
+  }
+  /* whitespace: \s*[\r\n]+ | \s+(?!\S) | \s+ */
+  size_t j = i;
+  while (j < n && is_space(c[j])) ++j;
+  size_t last_nl = n;
+  for (size_t k = i; k < j; ++k)
+    if (is_nl(c[k])) last_nl = k;
+  if (last_nl < n) return last_nl + 1;
+  if (j == n) return j;
+  if (j - i >= 2) return j - 1;
+  return j > i ? j : i + 1;
+}
+}  // namespace
+
+bool ByteBpeTokenizer::load(const GGUFFile& f, std::string* err) {
+  const std::vector<std::string>* tok = f.str_array("tokenizer.ggml.tokens");
+  const std::vector<std::string>* merges = f.str_array("tokenizer.ggml.merges");
+  if (f.str("tokenizer.ggml.model", "") != "gpt2" || !tok || !merges) {
+    if (err) *err = "tokenizer: no byte-level BPE (tokenizer.ggml.model = gpt2) vocabulary";
+    return false;
+  }
+  tokens_ = *tok;
+  types_.assign(tokens_.size(), SpmTokenizer::NORMAL);
+  if (const std::vector<double>* ty = f.num_array("tokenizer.ggml.token_type"))
+    if (ty->size() == tokens_.size())
+      for (size_t i = 0; i < ty->size(); ++i) types_[i] = (int32_t)(*ty)[i];
+  id_.clear();
+  for (size_t i = 0; i < tokens_.size(); ++i) id_.emplace(tokens_[i], (int32_t)i);
+  rank_.clear();
+  for (size_t i = 0; i < merges->size(); ++i) rank_.emplace((*merges)[i], (int32_t)i);
+  /* GPT-2's byte <-> printable character table: bytes that are printable Latin-1 map to
+     themselves, the others to U+0100 + n in byte order */
+  int n = 0;
+  char_byte_.clear();
+  for (int b = 0; b < 256; ++b) {
+    const bool keep = (b >= '!' && b <= '~') || (b >= 0xA1 && b <= 0xAC) || (b >= 0xAE && b <= 0xFF);
+    const uint32_t cp = keep ? (uint32_t)b : 256u + (uint32_t)n++;
+    byte_char_[b] = utf8_of(cp);
+    char_byte_[cp] = (uint8_t)b;
+  }
+  bos_ = (int)f.num("tokenizer.ggml.bos_token_id", -1);
+  add_bos_ = f.num("tokenizer.ggml.add_bos_token", 1) != 0;
+  return true;
+}
+
+std::vector<int32_t> ByteBpeTokenizer::encode(const std::string& text, bool add_bos) const {
+  std::vector<int32_t> out;
+  if (add_bos && bos_ >= 0) out.push_back(bos_);
+  std::vector<uint32_t> cps;
+  std::vector<size_t> offs;
+  code_points(text, &cps, &offs);
+  for (size_t i = 0; i < cps.size();) {
+    const size_t e = split_piece(cps, i);
+    std::vector<std::string> sym;
+    std::string word;
+    for (size_t b = offs[i]; b < offs[e]; ++b) {
+      sym.push_back(byte_char_[(unsigned char)text[b]]);
+      word += sym.back();
+    }
+    i = e;
+    auto whole = id_.find(word);
+    if (whole != id_.end()) { /* a piece that is a token is not split (ignore_merges) */
+      out.push_back(whole->second);
+      continue;
+    }
+    while (sym.size() > 1) {
+      int best = -1;
+      int32_t best_rank = 0;
+      for (size_t k = 0; k + 1 < sym.size(); ++k) {
+        auto it = rank_.find(sym[k] + " " + sym[k + 1]);
+        if (it != rank_.end() && (best < 0 || it->second < best_rank)) {
+          best = (int)k;
+          best_rank = it->second;
+        }
+      }
+      if (best < 0) break;
+      sym[best] += sym[best + 1];
+      sym.erase(sym.begin() + best + 1);
+    }
+    for (const std::string& s : sym) {
+      auto it = id_.find(s);
+      if (it != id_.end()) out.push_back(it->second);
+    }
+  }
+  return out;
+}
+
+std::string ByteBpeTokenizer::decode(const std::vector<int32_t>& ids) const {
+  std::string bytes;
+  for (int32_t id : ids) {
+    if (id < 0 || (size_t)id >= tokens_.size()) continue;
+    const int t = types_[id];
+    if (t == SpmTokenizer::CONTROL || t == SpmTokenizer::UNUSED) continue;
+    const std::string& p = tokens_[id];
+    std::vector<uint32_t> cps;
+    std::vector<size_t> offs;
+    code_points(p, &cps, &offs);
+    for (size_t k = 0; k < cps.size(); ++k) {
+      auto it = char_byte_.find(cps[k]);
+      if (it != char_byte_.end() && t != SpmTokenizer::USER_DEFINED) bytes.push_back((char)it->second);
+      else bytes.append(p, offs[k], offs[k + 1] - offs[k]); /* added tokens keep their text */
+    }
+  }
+  return bytes_to_utf8(bytes);
+}
+
+bool GgufTokenizer::load(const GGUFFile& f, std::string* err) {
+  spm_ = SpmTokenizer();
+  bpe_ = ByteBpeTokenizer();
+  const std::string model = f.str("tokenizer.ggml.model", "");
+  if (model == "gpt2") return bpe_.load(f, err);
+  return spm_.load(f, err);
+}
+
+}  // namespace ulbe

@@ -68,4 +68,55 @@ class SpmTokenizer {
   bool add_bos_ = true, add_space_prefix_ = true;
 };
 
+/*
+ * The GGUF "gpt2" tokenizer of Llama-3 files: byte-level BPE over tokenizer.ggml.tokens and
+ * tokenizer.ggml.merges ("a b", rank = position), as the HF tokenizers library runs
+ * Llama-3's tokenizer.json.
+ * encode: the text is split by Llama-3's pattern
+ *   (?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}{1,3}| ?[^\s\p{L}\p{N}]+[\r\n]*|
+ *   \s*[\r\n]+|\s+(?!\S)|\s+
+ * (written out as a scanner; \p{L} / \p{N} from unicode_ranges.h, \s = White_Space); each
+ * piece's UTF-8 bytes become GPT-2's printable byte characters; a piece that is itself a token
+ * is emitted whole (ignore_merges), else the adjacent pair of lowest merge rank is merged (the
+ * leftmost on equal ranks) until none merges.
+ * decode: tokens concatenated, byte characters mapped back to bytes, the bytes as UTF-8
+ * (U+FFFD for each byte that starts no valid character); control tokens dropped.
+ */
+class ByteBpeTokenizer {
+ public:
+  bool load(const GGUFFile& f, std::string* err);
+  std::vector<int32_t> encode(const std::string& text, bool add_bos) const;
+  std::string decode(const std::vector<int32_t>& ids) const;
+  bool loaded() const { return !tokens_.empty(); }
+  bool add_bos() const { return add_bos_; }
+
+ private:
+  std::vector<std::string> tokens_;
+  std::vector<int32_t> types_;
+  std::unordered_map<std::string, int32_t> id_;
+  std::unordered_map<std::string, int32_t> rank_; /* "a b" -> merge rank */
+  std::string byte_char_[256];                     /* byte -> its printable character (UTF-8) */
+  std::unordered_map<uint32_t, uint8_t> char_byte_; /* code point -> byte */
+  int bos_ = -1;
+  bool add_bos_ = true;
+};
+
+/* the text tokenizer of a GGUF file: SentencePiece ("llama") or byte-level BPE ("gpt2") */
+class GgufTokenizer {
+ public:
+  bool load(const GGUFFile& f, std::string* err);
+  std::vector<int32_t> encode(const std::string& text, bool add_bos) const {
+    return spm_.loaded() ? spm_.encode(text, add_bos) : bpe_.encode(text, add_bos);
+  }
+  std::string decode(const std::vector<int32_t>& ids) const {
+    return spm_.loaded() ? spm_.decode(ids) : bpe_.decode(ids);
+  }
+  bool loaded() const { return spm_.loaded() || bpe_.loaded(); }
+  bool add_bos() const { return spm_.loaded() ? spm_.add_bos() : bpe_.add_bos(); }
+
+ private:
+  SpmTokenizer spm_;
+  ByteBpeTokenizer bpe_;
+};
+
 }  // namespace ulbe
