@@ -12,6 +12,8 @@ tk = pytest.importorskip("tokenizers")
 LLAMA3_SPLIT = (r"(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}{1,3}|"
                 r" ?[^\s\p{L}\p{N}]+[\r\n]*|\s*[\r\n]+|\s+(?!\S)|\s+")
 
+SPECIALS = ["<|begin_of_text|>", "<|eot_id|>", "<|eot|>", "<|start_header_id|>"]
+
 WORDS = ["hello", "world", "it's", "we'll", "THEY'RE", "naïve", "über", "Straße", "東京", "мир", "123",
          "45678", "3.14", "!!", "...", "x1y2", "café", "don't", "I'M", "e-mail", "(a)", "#tag", "½", "٣٤"]
 
@@ -33,17 +35,22 @@ def trained(tmp_path_factory):
     trainer = tk.trainers.BpeTrainer(vocab_size=700, initial_alphabet=pre_tokenizers.ByteLevel.alphabet(),
                                      show_progress=False)
     tok.train_from_iterator(_lines(0, 3000), trainer)
-    model = json.loads(tok.to_str())["model"]
-    vocab = model["vocab"]
+    tok.add_special_tokens(SPECIALS)
+    j = json.loads(tok.to_str())
+    model = j["model"]
+    vocab = dict(model["vocab"])
+    for a in j["added_tokens"]:
+        vocab[a["content"]] = a["id"]
     pieces = [None] * len(vocab)
     for p, i in vocab.items():
         pieces[i] = p
+    types = [3 if p in SPECIALS else 1 for p in pieces]
     merges = [m if isinstance(m, str) else " ".join(m) for m in model["merges"]]
     import vulkangguf as vg
     path = str(tmp_path_factory.mktemp("bpe") / "bpe.gguf")
     vg.write_synthetic_gguf(path, dict(n_layer=1, d_model=256, n_head=4, n_head_kv=4, d_ff=512,
                                        n_vocab=len(pieces), wtype="q4_0", seed=3, vocab=pieces,
-                                       scores=[0.0] * len(pieces), token_types=[1] * len(pieces), merges=merges,
+                                       scores=[0.0] * len(pieces), token_types=types, merges=merges,
                                        add_bos=False))
     return tok, path
 
@@ -65,6 +72,22 @@ def test_encode_matches_hf_tokenizers(trained):
         want = tok.encode(t).ids
         got = vg.gguf_tokenize(path, t)
         assert got == want, (t, got, want)
+
+
+def test_special_tokens_in_text_split_out(trained):
+    """Control tokens written in the text become their ids (the longest one at each position),
+    the text around them is encoded as usual, and decode drops them (as HF's
+    skip_special_tokens)."""
+    tok, path = trained
+    import vulkangguf as vg
+    rng = random.Random(4)
+    for _ in range(60):
+        parts = [rng.choice(WORDS + SPECIALS + [" ", "\n", "<|", "|>", "<|eot"]) for _ in range(rng.randint(1, 10))]
+        t = "".join(parts)
+        want = tok.encode(t).ids
+        ids = vg.gguf_tokenize(path, t)
+        assert ids == want, (t, ids, want)
+        assert vg.gguf_detokenize(path, ids).decode("utf-8") == tok.decode(ids)
 
 
 def test_decode_round_trip(trained):

@@ -1,6 +1,7 @@
 /* tokenizer.cpp — SentencePiece BPE over a GGUF vocabulary (see tokenizer.h). */
 #include "tokenizer.h"
 
+#include <algorithm>
 #include <cstdio>
 #include <queue>
 
@@ -341,6 +342,12 @@ bool ByteBpeTokenizer::load(const GGUFFile& f, std::string* err) {
     byte_char_[b] = utf8_of(cp);
     char_byte_[cp] = (uint8_t)b;
   }
+  for (auto& v : special_) v.clear();
+  for (size_t i = 0; i < tokens_.size(); ++i)
+    if ((types_[i] == SpmTokenizer::CONTROL || types_[i] == SpmTokenizer::USER_DEFINED) && !tokens_[i].empty())
+      special_[(unsigned char)tokens_[i][0]].push_back((int32_t)i);
+  for (auto& v : special_)
+    std::stable_sort(v.begin(), v.end(), [&](int32_t a, int32_t b) { return tokens_[a].size() > tokens_[b].size(); });
   bos_ = (int)f.num("tokenizer.ggml.bos_token_id", -1);
   add_bos_ = f.num("tokenizer.ggml.add_bos_token", 1) != 0;
   return true;
@@ -349,6 +356,30 @@ bool ByteBpeTokenizer::load(const GGUFFile& f, std::string* err) {
 std::vector<int32_t> ByteBpeTokenizer::encode(const std::string& text, bool add_bos) const {
   std::vector<int32_t> out;
   if (add_bos && bos_ >= 0) out.push_back(bos_);
+  /* special tokens written in the text, longest first at each position */
+  size_t seg = 0;
+  for (size_t i = 0; i < text.size();) {
+    int32_t hit = -1;
+    for (int32_t id : special_[(unsigned char)text[i]])
+      if (text.compare(i, tokens_[id].size(), tokens_[id]) == 0) {
+        hit = id;
+        break;
+      }
+    if (hit < 0) {
+      ++i;
+      continue;
+    }
+    encode_segment(text.substr(seg, i - seg), &out);
+    out.push_back(hit);
+    i += tokens_[hit].size();
+    seg = i;
+  }
+  encode_segment(text.substr(seg), &out);
+  return out;
+}
+
+void ByteBpeTokenizer::encode_segment(const std::string& text, std::vector<int32_t>* outp) const {
+  std::vector<int32_t>& out = *outp;
   std::vector<uint32_t> cps;
   std::vector<size_t> offs;
   code_points(text, &cps, &offs);
@@ -385,7 +416,6 @@ std::vector<int32_t> ByteBpeTokenizer::encode(const std::string& text, bool add_
       if (it != id_.end()) out.push_back(it->second);
     }
   }
-  return out;
 }
 
 std::string ByteBpeTokenizer::decode(const std::vector<int32_t>& ids) const {

@@ -78,7 +78,9 @@ class SpmTokenizer {
  * (written out as a scanner; \p{L} / \p{N} from unicode_ranges.h, \s = White_Space); each
  * piece's UTF-8 bytes become GPT-2's printable byte characters; a piece that is itself a token
  * is emitted whole (ignore_merges), else the adjacent pair of lowest merge rank is merged (the
- * leftmost on equal ranks) until none merges.
+ * leftmost on equal ranks) until none merges.  Control and user-defined tokens written in the
+ * text (<|eot_id|>, ...) are split out first, longest match at each position, and the text
+ * between them is encoded as above.
  * decode: tokens concatenated, byte characters mapped back to bytes, the bytes as UTF-8
  * (U+FFFD for each byte that starts no valid character); control tokens dropped.
  */
@@ -91,10 +93,13 @@ class ByteBpeTokenizer {
   bool add_bos() const { return add_bos_; }
 
  private:
+  void encode_segment(const std::string& text, std::vector<int32_t>* out) const;
   std::vector<std::string> tokens_;
   std::vector<int32_t> types_;
   std::unordered_map<std::string, int32_t> id_;
   std::unordered_map<std::string, int32_t> rank_; /* "a b" -> merge rank */
+  std::vector<int32_t> special_[256];             /* control / user-defined tokens by first byte,
+                                                     longest first: split out of text as is */
   std::string byte_char_[256];                     /* byte -> its printable character (UTF-8) */
   std::unordered_map<uint32_t, uint8_t> char_byte_; /* code point -> byte */
   int bos_ = -1;
