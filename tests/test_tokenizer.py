@@ -150,3 +150,18 @@ def test_generate_text_uses_the_gguf_vocabulary(trained):
     ids = vg.gguf_tokenize(path, prompt, True)
     toks = api.generate_tokens(ids, cfg)
     assert api.generate(prompt, cfg) == sp.decode(list(toks))
+
+
+def test_truncated_vocabulary_arrays_rejected(trained, tmp_path):
+    """A GGUF cut inside its tokenizer arrays is rejected with an error, never read past its end."""
+    sp, path, words = trained
+    import vulkangguf as vg
+    data = open(path, "rb").read()
+    cut = data.find(b"tokenizer.ggml.scores")
+    assert cut > 0
+    bad = str(tmp_path / "cut.gguf")
+    for n in (cut - 100, cut + 30):
+        with open(bad, "wb") as f:
+            f.write(data[:n])
+        with pytest.raises(RuntimeError):
+            vg.gguf_tokenize(bad, "abc")
