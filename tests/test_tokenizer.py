@@ -165,3 +165,40 @@ def test_truncated_vocabulary_arrays_rejected(trained, tmp_path):
             f.write(data[:n])
         with pytest.raises(RuntimeError):
             vg.gguf_tokenize(bad, "abc")
+
+
+def test_user_defined_pieces_match_first_and_never_merge(tmp_path):
+    """User-defined pieces (the added symbols of fine-tuned vocabularies) are matched first,
+    longest at each position, and never merged with their neighbours, as sentencepiece does."""
+    rng = random.Random(0)
+    alpha = "abcdefghijklmnopqrstuvwxyz"
+    words = ["".join(rng.choice(alpha) for _ in range(rng.randint(1, 8))) for _ in range(300)]
+    lines = [" ".join(rng.choice(words) for _ in range(10)) for _ in range(2000)]
+    user = ["<tool>", "ab", "xyz"]
+    buf = io.BytesIO()
+    spm.SentencePieceTrainer.train(sentence_iterator=iter(lines), model_writer=buf, vocab_size=500, model_type="bpe",
+                                   byte_fallback=True, normalization_rule_name="identity", add_dummy_prefix=True,
+                                   remove_extra_whitespaces=False, user_defined_symbols=user, minloglevel=2)
+    sp = spm.SentencePieceProcessor(model_proto=buf.getvalue())
+    n = sp.get_piece_size()
+
+    def ttype(i):
+        if sp.is_unknown(i):
+            return 2
+        if sp.is_control(i):
+            return 3
+        if sp.is_byte(i):
+            return 6
+        return 4 if sp.id_to_piece(i) in user else 1
+
+    import vulkangguf as vg
+    path = str(tmp_path / "user.gguf")
+    vg.write_synthetic_gguf(path, dict(n_layer=1, d_model=256, n_head=4, n_head_kv=4, d_ff=512, n_vocab=n,
+                                       wtype="q4_0", seed=3, vocab=[sp.id_to_piece(i) for i in range(n)],
+                                       scores=[sp.get_score(i) for i in range(n)],
+                                       token_types=[ttype(i) for i in range(n)]))
+    for _ in range(300):
+        t = " ".join(rng.choice(words + ["<tool>", "ab", "xyzab", "aab", "<tool>x"]) for _ in range(rng.randint(1, 8)))
+        if rng.random() < 0.3:
+            t = t.replace(" ", "")
+        assert vg.gguf_tokenize(path, t, add_bos=False) == sp.encode(t), t

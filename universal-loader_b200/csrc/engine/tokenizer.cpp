@@ -71,17 +71,21 @@ bool SpmTokenizer::load(const std::vector<std::string>& pieces, const std::vecto
   eos_ = eos;
   unk_ = unk;
   mergeable_.clear();
+  for (auto& v : user_) v.clear();
   for (int i = 0; i < 256; ++i) byte_id_[i] = -1;
   for (size_t i = 0; i < pieces_.size(); ++i) {
     const int t = types_[i];
     if (t == NORMAL || t == USER_DEFINED) {
       mergeable_.emplace(pieces_[i], (int32_t)i); /* the first id of a duplicated piece wins */
+      if (t == USER_DEFINED && !pieces_[i].empty()) user_[(unsigned char)pieces_[i][0]].push_back((int32_t)i);
     } else if (t == BYTE) {
       unsigned v = 0;
       if (pieces_[i].size() == 6 && std::sscanf(pieces_[i].c_str(), "<0x%02X>", &v) == 1 && v < 256)
         byte_id_[v] = (int32_t)i;
     }
   }
+  for (auto& v : user_)
+    std::stable_sort(v.begin(), v.end(), [&](int32_t a, int32_t b) { return pieces_[a].size() > pieces_[b].size(); });
   return true;
 }
 
@@ -120,12 +124,22 @@ std::vector<int32_t> SpmTokenizer::encode(const std::string& text, bool add_bos)
   struct Sym {
     size_t off, len;
     int prev, next;
+    bool frozen; /* a user-defined piece: never merged */
   };
   std::vector<Sym> sym;
   for (size_t o = 0; o < norm.size();) {
-    size_t l = utf8_len((unsigned char)norm[o]);
-    if (o + l > norm.size()) l = norm.size() - o;
-    sym.push_back({o, l, (int)sym.size() - 1, (int)sym.size() + 1});
+    size_t l = 0;
+    for (int32_t id : user_[(unsigned char)norm[o]])
+      if (norm.compare(o, pieces_[id].size(), pieces_[id]) == 0) {
+        l = pieces_[id].size();
+        break;
+      }
+    const bool frozen = l > 0;
+    if (!frozen) {
+      l = utf8_len((unsigned char)norm[o]);
+      if (o + l > norm.size()) l = norm.size() - o;
+    }
+    sym.push_back({o, l, (int)sym.size() - 1, (int)sym.size() + 1, frozen});
     o += l;
   }
   sym.back().next = -1;
@@ -140,7 +154,7 @@ std::vector<int32_t> SpmTokenizer::encode(const std::string& text, bool add_bos)
   };
   std::priority_queue<Cand, std::vector<Cand>, decltype(worse)> q(worse);
   auto propose = [&](int l, int r) {
-    if (l < 0 || r < 0) return;
+    if (l < 0 || r < 0 || sym[l].frozen || sym[r].frozen) return;
     const std::string s = norm.substr(sym[l].off, sym[l].len + sym[r].len);
     auto it = mergeable_.find(s);
     if (it != mergeable_.end()) q.push({scores_[it->second], l, r, s.size()});

@@ -10,7 +10,8 @@
  * a dummy-prefix space, spaces as U+2581, byte fallback).
  *
  * encode: the text (with "▁" prepended unless the file's tokenizer.ggml.add_space_prefix is
- * false, and every ' ' replaced by "▁") is split into UTF-8
+ * false, and every ' ' replaced by "▁") is split into user-defined pieces (longest match at
+ * each position; these never merge further) and otherwise UTF-8
  * characters; the adjacent pair whose concatenation is a NORMAL or USER_DEFINED piece with
  * the highest score is merged (the leftmost pair on equal scores) until no pair merges; a
  * final symbol that is not a piece becomes its bytes' <0xXX> pieces (or the unknown id).
@@ -63,6 +64,7 @@ class SpmTokenizer {
   std::vector<float> scores_;
   std::vector<int32_t> types_;
   std::unordered_map<std::string, int32_t> mergeable_; /* NORMAL / USER_DEFINED pieces */
+  std::vector<int32_t> user_[256]; /* USER_DEFINED pieces by first byte, longest first */
   int32_t byte_id_[256];
   int bos_ = 1, eos_ = 2, unk_ = 0;
   bool add_bos_ = true, add_space_prefix_ = true;
