@@ -96,3 +96,30 @@ def test_decode_round_trip(trained):
     for t in _texts(2, 80):
         ids = vg.gguf_tokenize(path, t)
         assert vg.gguf_detokenize(path, ids).decode("utf-8") == tok.decode(ids) == t
+
+
+def test_gpt2_pre_tokenizer_files(tmp_path):
+    """tokenizer.ggml.pre = gpt2: GPT-2's own split pattern, merges always applied (no
+    ignore_merges), as HF ByteLevel(use_regex=True) with a plain BPE model."""
+    from tokenizers import Tokenizer, decoders, models, pre_tokenizers, trainers
+    tok = Tokenizer(models.BPE())
+    tok.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False, use_regex=True)
+    tok.decoder = decoders.ByteLevel()
+    tok.train_from_iterator(_lines(7, 3000), trainers.BpeTrainer(
+        vocab_size=700, initial_alphabet=pre_tokenizers.ByteLevel.alphabet(), show_progress=False))
+    model = json.loads(tok.to_str())["model"]
+    pieces = [None] * len(model["vocab"])
+    for p, i in model["vocab"].items():
+        pieces[i] = p
+    merges = [m if isinstance(m, str) else " ".join(m) for m in model["merges"]]
+    import vulkangguf as vg
+    path = str(tmp_path / "gpt2.gguf")
+    vg.write_synthetic_gguf(path, dict(n_layer=1, d_model=256, n_head=4, n_head_kv=4, d_ff=512,
+                                       n_vocab=len(pieces), wtype="q4_0", seed=3, vocab=pieces,
+                                       scores=[0.0] * len(pieces), token_types=[1] * len(pieces), merges=merges,
+                                       tokenizer_pre="gpt2", add_bos=False))
+    for t in _texts(8, 120):
+        want = tok.encode(t).ids
+        got = vg.gguf_tokenize(path, t)
+        assert got == want, (t, got, want)
+        assert vg.gguf_detokenize(path, got).decode("utf-8") == t

@@ -445,7 +445,8 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
   const bool with_vocab = !sp.vocab.empty();
   const int n_flags = with_vocab ? (sp.add_bos >= 0) + (sp.add_space_prefix >= 0) : 0;
   const int n_merges = with_vocab && !sp.merges.empty() ? 1 : 0;
-  put<uint64_t>(h, 14 + (with_vocab ? 7 : 0) + n_flags + n_merges);
+  const int n_pre = with_vocab && !sp.tok_pre.empty() ? 1 : 0;
+  put<uint64_t>(h, 14 + (with_vocab ? 7 : 0) + n_flags + n_merges + n_pre);
   kv_str(h, "general.architecture", "llama");
   kv_str(h, "general.name", sp.name);
   kv_u32(h, "general.alignment", (uint32_t)align);
@@ -463,6 +464,7 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
   if (with_vocab) {
     kv_str(h, "tokenizer.ggml.model", n_merges ? "gpt2" : "llama");
     if (n_merges) kv_arr_str(h, "tokenizer.ggml.merges", sp.merges);
+    if (n_pre) kv_str(h, "tokenizer.ggml.pre", sp.tok_pre);
     kv_arr_str(h, "tokenizer.ggml.tokens", sp.vocab);
     kv_arr_num<float>(h, "tokenizer.ggml.scores", GV_F32, sp.scores);
     kv_arr_num<int32_t>(h, "tokenizer.ggml.token_type", GV_I32, sp.token_types);

@@ -77,6 +77,7 @@ struct SynthSpec {
   std::vector<float> scores;
   std::vector<int32_t> token_types;
   std::vector<std::string> merges; /* non-empty: a byte-level BPE ("gpt2") vocabulary */
+  std::string tok_pre;             /* tokenizer.ggml.pre, written when non-empty */
   int add_bos = -1, add_space_prefix = -1; /* tokenizer.ggml.add_bos_token / add_space_prefix; -1: not written */
 };
 

@@ -514,6 +514,7 @@ bool write_synthetic(const std::string& path, py::dict spec, int threads) {
     s.token_types = spec.contains("token_types") ? spec["token_types"].cast<std::vector<int32_t>>()
                                                  : std::vector<int32_t>(s.vocab.size(), 1);
     if (spec.contains("merges")) s.merges = spec["merges"].cast<std::vector<std::string>>();
+    if (spec.contains("tokenizer_pre")) s.tok_pre = spec["tokenizer_pre"].cast<std::string>();
     if (spec.contains("add_bos")) s.add_bos = spec["add_bos"].cast<bool>() ? 1 : 0;
     if (spec.contains("add_space_prefix")) s.add_space_prefix = spec["add_space_prefix"].cast<bool>() ? 1 : 0;
   }

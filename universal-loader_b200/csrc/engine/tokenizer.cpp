@@ -328,6 +328,30 @@ size_t split_piece(const std::vector<uint32_t>& c, size_t i) {
   if (j - i >= 2) return j - 1;
   return j > i ? j : i + 1;
 }
+/* end of the piece GPT-2's split pattern matches at i:
+   's|'t|'re|'ve|'m|'ll|'d| ?\p{L}+| ?\p{N}+| ?[^\s\p{L}\p{N}]+|\s+(?!\S)|\s+ */
+size_t split_piece_gpt2(const std::vector<uint32_t>& c, size_t i) {
+  const size_t n = c.size();
+  if (c[i] == '\'' && i + 1 < n) {
+    const uint32_t a = c[i + 1], b = i + 2 < n ? c[i + 2] : 0;
+    if (a == 's' || a == 't' || a == 'm' || a == 'd') return i + 2;
+    if ((a == 'r' && b == 'e') || (a == 'v' && b == 'e') || (a == 'l' && b == 'l')) return i + 3;
+  }
+  bool (*cls[3])(uint32_t) = {is_letter, is_number, is_other};
+  for (auto f : cls) {
+    size_t j = i;
+    if (c[i] == ' ' && i + 1 < n && f(c[i + 1])) j = i + 1;
+    if (f(c[j])) {
+      while (j < n && f(c[j])) ++j;
+      return j;
+    }
+  }
+  size_t j = i;
+  while (j < n && is_space(c[j])) ++j;
+  if (j == n) return j;
+  if (j - i >= 2) return j - 1;
+  return j > i ? j : i + 1;
+}
 }  // namespace
 
 bool ByteBpeTokenizer::load(const GGUFFile& f, std::string* err) {
@@ -364,6 +388,7 @@ bool ByteBpeTokenizer::load(const GGUFFile& f, std::string* err) {
     std::stable_sort(v.begin(), v.end(), [&](int32_t a, int32_t b) { return tokens_[a].size() > tokens_[b].size(); });
   bos_ = (int)f.num("tokenizer.ggml.bos_token_id", -1);
   add_bos_ = f.num("tokenizer.ggml.add_bos_token", 1) != 0;
+  gpt2_split_ = f.str("tokenizer.ggml.pre", "") == "gpt2";
   return true;
 }
 
@@ -398,7 +423,7 @@ void ByteBpeTokenizer::encode_segment(const std::string& text, std::vector<int32
   std::vector<size_t> offs;
   code_points(text, &cps, &offs);
   for (size_t i = 0; i < cps.size();) {
-    const size_t e = split_piece(cps, i);
+    const size_t e = gpt2_split_ ? split_piece_gpt2(cps, i) : split_piece(cps, i);
     std::vector<std::string> sym;
     std::string word;
     for (size_t b = offs[i]; b < offs[e]; ++b) {
@@ -406,7 +431,7 @@ void ByteBpeTokenizer::encode_segment(const std::string& text, std::vector<int32
       word += sym.back();
     }
     i = e;
-    auto whole = id_.find(word);
+    auto whole = gpt2_split_ ? id_.end() : id_.find(word);
     if (whole != id_.end()) { /* a piece that is a token is not split (ignore_merges) */
       out.push_back(whole->second);
       continue;

@@ -80,7 +80,9 @@ class SpmTokenizer {
  * (written out as a scanner; \p{L} / \p{N} from unicode_ranges.h, \s = White_Space); each
  * piece's UTF-8 bytes become GPT-2's printable byte characters; a piece that is itself a token
  * is emitted whole (ignore_merges), else the adjacent pair of lowest merge rank is merged (the
- * leftmost on equal ranks) until none merges.  Control and user-defined tokens written in the
+ * leftmost on equal ranks) until none merges.  Files whose tokenizer.ggml.pre is "gpt2"
+ * split with GPT-2's own pattern ('s|'t|'re|'ve|'m|'ll|'d| ?\p{L}+| ?\p{N}+|
+ * ?[^\s\p{L}\p{N}]+|\s+(?!\S)|\s+) and always apply the merges.  Control and user-defined tokens written in the
  * text (<|eot_id|>, ...) are split out first, longest match at each position, and the text
  * between them is encoded as above.
  * decode: tokens concatenated, byte characters mapped back to bytes, the bytes as UTF-8
@@ -106,6 +108,7 @@ class ByteBpeTokenizer {
   std::unordered_map<uint32_t, uint8_t> char_byte_; /* code point -> byte */
   int bos_ = -1;
   bool add_bos_ = true;
+  bool gpt2_split_ = false; /* tokenizer.ggml.pre = gpt2: GPT-2's pattern, merges always applied */
 };
 
 /* the text tokenizer of a GGUF file: SentencePiece ("llama") or byte-level BPE ("gpt2") */
