@@ -671,7 +671,8 @@ PYBIND11_MODULE(vulkangguf, m) {
   m.def("write_synthetic_gguf", &write_synthetic, py::arg("path"), py::arg("spec"), py::arg("threads") = 0,
         "Write a synthetic LLaMA GGUF: Q4_0/Q4_K weights N(0, stddev), fp16 embeddings, unit norms; "
         "spec keys embd_type / out_type pick other token_embd (f32, f16, q4_0, q8_0, q4_k, q6_k) and "
-        "output.weight (q4_0, q8_0, q4_k, q6_k) types");
+        "output.weight (q4_0, q8_0, q4_k, q6_k) types; vocab / scores / token_types (+ merges, "
+        "tokenizer_pre for byte-level BPE; add_bos, add_space_prefix) write a tokenizer.ggml.* vocabulary");
   m.def("synth_normal", &ulbe::synth_normal, "Sample i of the synthetic N(0,1) stream keyed by (seed, name)");
   m.attr("__version__") = "0.1";
 }
