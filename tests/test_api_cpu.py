@@ -42,6 +42,24 @@ def test_null_arguments_are_rejected_with_status():
     assert L.ulb_tensor_free(None) == U.OK
 
 
+@pytest.mark.parametrize("fn", ["ulb_attention", "ulb_attention_noalloc"])
+def test_attention_descriptor_checked_before_any_host_arithmetic(fn):
+    """A zero kv-head count or rows_per_seq must come back as ULB_EINVAL, not as a host
+    division by zero.  The descriptor is checked before the context is used at all, so a
+    stand-in (never dereferenced) context handle is enough to reach the check on the CPU."""
+    import ctypes as C
+    import ulb_capi as U
+    L = U.lib()
+    fake = C.c_void_p(16)
+    for desc, M, rps in ((U.AttnDesc(32, 0, 128, 512, 1, 0.1), 6, 6),
+                         (U.AttnDesc(32, 8, 128, 512, 1, 0.1), 6, 0),
+                         (U.AttnDesc(32, 8, 0, 512, 1, 0.1), 6, 6),
+                         (U.AttnDesc(32, 8, 128, 0, 1, 0.1), 6, 6)):
+        rc = getattr(L, fn)(fake, C.byref(desc), fake, fake, fake, fake, fake, M, rps, fake)
+        assert rc in (U.EINVAL, U.EUNSUPPORTED), rc
+        assert b"attention" in L.ulb_last_error()
+
+
 def test_surface_matches_reference():
     import vulkangguf as vg
     for cls in ("InferenceAPI", "GenerationConfig", "GenerationResult", "GenerationProgress", "ModelMetrics",
@@ -123,6 +141,29 @@ def test_truncated_gguf_rejected(tmp_path, tiny_draft):
     bad.write_bytes(data[: len(data) // 2])
     with pytest.raises(RuntimeError):
         orc.Model(str(bad))
+    import vulkangguf as vg
+    api = vg.InferenceAPI()
+    assert api.load_model(str(bad)) is False
+
+
+@pytest.mark.parametrize("field,value", [
+    ("ne1", 1 << 62),             # element count ne0 * ne1 wraps past 64 bits
+    ("ne1", 1 << 40),             # no wrap, but 316 TB of data past the end of the file
+    ("offset", (1 << 64) - 64),    # data start + offset wraps around
+])
+def test_gguf_with_overflowing_tensor_info_rejected(tmp_path, tiny_draft, field, value):
+    """A crafted tensor info whose sizes or offset overflow 64-bit arithmetic is refused, not
+    read past the end of the mapping."""
+    import struct
+    data = bytearray(open(tiny_draft, "rb").read())
+    name = b"blk.0.attn_q.weight"
+    at = data.index(struct.pack("<Q", len(name)) + name) + 8 + len(name)
+    n_dims = struct.unpack_from("<I", data, at)[0]
+    assert n_dims == 2
+    off = {"ne1": at + 4 + 8, "offset": at + 4 + 8 * n_dims + 4}[field]
+    struct.pack_into("<Q", data, off, value)
+    bad = tmp_path / ("overflow_%s.gguf" % field)
+    bad.write_bytes(bytes(data))
     import vulkangguf as vg
     api = vg.InferenceAPI()
     assert api.load_model(str(bad)) is False

@@ -123,3 +123,19 @@ def test_gpt2_pre_tokenizer_files(tmp_path):
         got = vg.gguf_tokenize(path, t)
         assert got == want, (t, got, want)
         assert vg.gguf_detokenize(path, got).decode("utf-8") == t
+
+
+def test_unpinned_pre_tokenizer_refused(tmp_path):
+    """A byte-level BPE file whose tokenizer.ggml.pre names a split this library does not
+    implement (qwen2, deepseek-llm, starcoder, ...) is refused with an error instead of being
+    tokenized with the Llama-3 pattern."""
+    import vulkangguf as vg
+    pieces = [chr(c) for c in range(33, 127)] + ["ab", "abc"]
+    path = str(tmp_path / "qwen2-pre.gguf")
+    vg.write_synthetic_gguf(path, dict(n_layer=1, d_model=256, n_head=4, n_head_kv=4, d_ff=512,
+                                       n_vocab=len(pieces), wtype="q4_0", seed=3, vocab=pieces,
+                                       scores=[0.0] * len(pieces), token_types=[1] * len(pieces),
+                                       merges=["a b", "ab c"], tokenizer_pre="qwen2", add_bos=False))
+    with pytest.raises(Exception) as e:
+        vg.gguf_tokenize(path, "abc")
+    assert "qwen2" in str(e.value)

@@ -40,16 +40,32 @@ def _run(ctx, fn_name, desc, arrays, M, rps, out_elems):
     return got.astype(np.float32)
 
 
-@pytest.mark.parametrize("H,Hkv,hd,S,rps,positions", [
+def _ragged(rng, S, rps, lo, hi):
+    """S sequences of rps consecutive rows each, the first row at a position in [lo, hi)"""
+    starts = rng.integers(lo, hi, S)
+    return [list(range(int(s0), int(s0) + rps)) for s0 in starts]
+
+
+_R = np.random.default_rng(77)
+
+
+@pytest.mark.parametrize("H,Hkv,hd,S,rps,positions,cap", [
     # caches past 2048 positions: more than 8 key splits, which merge through the scratch
-    # (shorter caches merge inside a thread-block cluster and use none)
-    (32, 32, 128, 1, 6, [[2434, 2435, 2436, 2437, 2438, 2439]]),      # 7B verify rows, 10 key splits
-    (32, 4, 64, 2, 2, [[2600, 2601], [130, 131]]),                    # TinyLlama-like GQA, ragged
+    (32, 32, 128, 1, 6, [[2434, 2435, 2436, 2437, 2438, 2439]], None),  # 7B verify rows, 10 key splits
+    (32, 4, 64, 2, 2, [[2600, 2601], [130, 131]], None),                # TinyLlama-like GQA, ragged
+    # one key split (capacity <= 256): neither the scratch nor the counters are used
+    (32, 8, 128, 5, 3, _ragged(_R, 5, 3, 0, 250), 256),
+    # 2..8 splits merged in a thread-block cluster: 64 sequences of a config-4-like batch, whose
+    # global-merge scratch (4.3 Mi floats) would not fit the static array, are accepted
+    (32, 8, 128, 64, 1, _ragged(_R, 64, 1, 0, 1020), 1024),
+    (32, 4, 64, 9, 2, _ragged(_R, 9, 2, 200, 2040), 2048),
+    # a global merge whose partials (11 x 8 heads x 11 splits x 16 x 130 floats = 2.01 Mi) just fit
+    (32, 8, 128, 11, 1, _ragged(_R, 11, 1, 2400, 2595), 2600),
 ])
-def test_noalloc_attention_matches_allocating_entry_point(ctx, H, Hkv, hd, S, rps, positions):
+def test_noalloc_attention_matches_allocating_entry_point(ctx, H, Hkv, hd, S, rps, positions, cap):
     import ulb_capi as U
     rng = np.random.default_rng(hd + S)
-    cap = max(max(p) for p in positions) + 5
+    cap = cap or max(max(p) for p in positions) + 5
     desc = U.AttnDesc(H, Hkv, hd, cap, S, 1.0 / np.sqrt(hd))
     M = S * rps
     for call in range(2):
@@ -68,3 +84,16 @@ def test_noalloc_attention_rejects_oversized_shapes(ctx):
     rc = U.lib().ulb_attention_noalloc(ctx.h, C.byref(desc), null, null, null, null, null, 64 * 9, 9, null)
     assert rc == U.EINVAL
     assert b"static scratch" in U.lib().ulb_last_error()
+
+
+@pytest.mark.parametrize("fn", ["ulb_attention", "ulb_attention_noalloc"])
+def test_attention_rejects_bad_descriptors_with_einval(ctx, fn):
+    """No head count of zero, rows_per_seq of zero or ragged M reaches the host arithmetic."""
+    import ulb_capi as U
+    null = C.c_void_p(16)
+    for desc, M, rps in ((U.AttnDesc(32, 0, 128, 512, 1, 0.1), 6, 6),
+                         (U.AttnDesc(32, 8, 128, 512, 1, 0.1), 6, 0),
+                         (U.AttnDesc(32, 8, 128, 512, 1, 0.1), 7, 6),
+                         (U.AttnDesc(32, 5, 128, 512, 1, 0.1), 6, 6)):
+        rc = getattr(U.lib(), fn)(ctx.h, C.byref(desc), null, null, null, null, null, M, rps, null)
+        assert rc == U.EINVAL, (fn, rc)

@@ -453,11 +453,10 @@ size_t attn_smem(int hd) {
  * through global memory (last CTA of the splits).
  */
 template <int HD>
-cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, const __half* k, const __half* v,
-                        const int* row_seq, const int* row_pos, __half* out, float* scratch, int* counters) {
+cudaError_t attn_setup(const bool** cl_ok_out) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
-  static int cl_ok[9] = {0}; /* max_splits -> cluster form schedulable */
+  static bool cl_ok[9] = {false}; /* max_splits -> cluster form schedulable */
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)attn_smem(HD));
@@ -481,8 +480,25 @@ cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, con
       cudaGetLastError();
     }
   });
-  if (attr_err != cudaSuccess) return attr_err;
-  const bool cl = p.max_splits >= 2 && p.max_splits <= 8 && cl_ok[p.max_splits];
+  *cl_ok_out = cl_ok;
+  return attr_err;
+}
+
+/* true when a launch with max_splits splits merges them in a thread-block cluster */
+template <int HD>
+cudaError_t attn_cluster_merge(int max_splits, bool* out) {
+  const bool* cl_ok = nullptr;
+  const cudaError_t e = attn_setup<HD>(&cl_ok);
+  *out = e == cudaSuccess && max_splits >= 2 && max_splits <= 8 && cl_ok[max_splits];
+  return e;
+}
+
+template <int HD>
+cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, const __half* k, const __half* v,
+                        const int* row_seq, const int* row_pos, __half* out, float* scratch, int* counters) {
+  bool cl = false;
+  const cudaError_t se = attn_cluster_merge<HD>(p.max_splits, &cl);
+  if (se != cudaSuccess) return se;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_mt, p.Hkv, ng * p.max_splits);
   cfg.blockDim = dim3(AW * 32);
@@ -504,23 +520,45 @@ cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, con
   return e;
 }
 
-size_t attention_scratch_floats(const ulb_attn_desc* d, int M, int rps, int max_pos, int* n_counters) {
+int validate_attn_desc(const ulb_attn_desc* d, int M, int rps) {
+  ULB_CHECK(d, ULB_EINVAL, "attention: NULL descriptor");
+  ULB_CHECK(d->n_head > 0 && d->n_head_kv > 0 && d->n_head % d->n_head_kv == 0, ULB_EINVAL,
+            "attention: n_head %d, n_head_kv %d (both > 0, n_head a multiple of n_head_kv)", d->n_head, d->n_head_kv);
+  ULB_CHECK(d->head_dim == 64 || d->head_dim == 128, ULB_EUNSUPPORTED, "attention: head_dim %d (64 or 128)",
+            d->head_dim);
+  ULB_CHECK(d->capacity > 0 && d->n_seq > 0, ULB_EINVAL, "attention: capacity %d, n_seq %d", d->capacity, d->n_seq);
+  ULB_CHECK(d->capacity <= SPLITK * MAXSPLIT, ULB_EUNSUPPORTED, "attention: capacity %d > %d", d->capacity,
+            SPLITK * MAXSPLIT);
+  ULB_CHECK(rps > 0 && M >= 0 && M % rps == 0, ULB_EINVAL, "attention: M=%d not a multiple of rows_per_seq=%d", M,
+            rps);
+  return ULB_OK;
+}
+
+int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int max_pos, size_t* floats,
+                           int* n_counters) {
+  (void)c;
+  ULB_TRY(validate_attn_desc(d, M, rps));
+  *floats = 0;
+  *n_counters = 0;
+  if (M == 0) return ULB_OK;
   AttnParams p;
   int ng;
   attn_geometry(d, M, rps, max_pos, &p, &ng);
+  if (p.max_splits == 1) return ULB_OK;
+  bool cl = false;
+  const cudaError_t e = d->head_dim == 64 ? attn_cluster_merge<64>(p.max_splits, &cl)
+                                          : attn_cluster_merge<128>(p.max_splits, &cl);
+  if (e != cudaSuccess) return cuda_error(e, "attention setup", __FILE__, __LINE__);
+  if (cl) return ULB_OK;
   *n_counters = ng * p.n_mt * p.Hkv;
-  return (size_t)ng * p.n_mt * p.Hkv * p.max_splits * QT * (size_t)(p.hd + 2);
+  *floats = (size_t)ng * p.n_mt * p.Hkv * p.max_splits * QT * (size_t)(p.hd + 2);
+  return ULB_OK;
 }
 
 int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, const __half* k,
                      const __half* v, const int* row_seq, const int* row_pos, int M, int rps,
                      __half* out, float* scratch, int* counters, size_t scratch_floats, int n_counters) {
-  ULB_CHECK(d->n_head_kv > 0 && d->n_head % d->n_head_kv == 0, ULB_EINVAL, "attention: n_head %% n_head_kv != 0");
-  ULB_CHECK(d->head_dim == 64 || d->head_dim == 128, ULB_EUNSUPPORTED, "attention: head_dim %d (64 or 128)",
-            d->head_dim);
-  ULB_CHECK(d->capacity <= SPLITK * MAXSPLIT, ULB_EUNSUPPORTED, "attention: capacity %d > %d", d->capacity,
-            SPLITK * MAXSPLIT);
-  ULB_CHECK(rps > 0 && M % rps == 0, ULB_EINVAL, "attention: M=%d not a multiple of rows_per_seq=%d", M, rps);
+  ULB_TRY(validate_attn_desc(d, M, rps));
   ULB_CHECK(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 && ldq % 4 == 0,
             ULB_EINVAL, "attention: q / k / v must be 16-byte aligned (ldq a multiple of 4)");
   if (M == 0) return ULB_OK;
@@ -529,8 +567,9 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
   attn_geometry(d, M, rps, d->capacity - 1, &p, &ng);
   p.ldq = ldq;
   int need_c = 0;
-  const size_t need = attention_scratch_floats(d, M, rps, d->capacity - 1, &need_c);
-  ULB_CHECK(p.max_splits == 1 || (scratch_floats >= need && n_counters >= need_c), ULB_EINVAL,
+  size_t need = 0;
+  ULB_TRY(attention_scratch_need(c, d, M, rps, d->capacity - 1, &need, &need_c));
+  ULB_CHECK(need == 0 || (scratch && counters && scratch_floats >= need && n_counters >= need_c), ULB_EINVAL,
             "attention: scratch %zu floats / %d counters, need %zu / %d", scratch_floats, n_counters, need, need_c);
   ULB_CHECK((long long)ng * p.max_splits <= 65535, ULB_EUNSUPPORTED, "attention: %d sequences x %d splits", ng,
             p.max_splits);
@@ -590,12 +629,12 @@ extern "C" int ulb_attention_noalloc(ulb_ctx* ctx, const ulb_attn_desc* d, const
                                      const uint16_t* v, const int32_t* row_seq, const int32_t* row_pos, int M,
                                      int rps, uint16_t* out) {
   ULB_CHECK(ctx && d && q && k && v && row_seq && row_pos && out, ULB_EINVAL, "ulb_attention_noalloc: NULL argument");
-  ULB_CHECK(d->capacity > 0 && d->n_seq > 0, ULB_EINVAL, "ulb_attention_noalloc: capacity / n_seq");
-  ULB_CHECK(rps > 0 && M >= 0 && M % rps == 0, ULB_EINVAL, "ulb_attention_noalloc: M=%d, rows_per_seq=%d", M, rps);
+  ULB_TRY(validate_attn_desc(d, M, rps));
   Ctx* c = &ctx->c;
   ULB_CUDA(cudaSetDevice(c->device));
   int nc = 0;
-  const size_t nf = attention_scratch_floats(d, M, rps, d->capacity - 1, &nc);
+  size_t nf = 0;
+  ULB_TRY(attention_scratch_need(c, d, M, rps, d->capacity - 1, &nf, &nc));
   ULB_CHECK(nf <= kNoAllocScratchFloats && nc <= kNoAllocCounters, ULB_EINVAL,
             "ulb_attention_noalloc: this shape needs %zu scratch floats and %d counters; the static scratch holds "
             "%zu floats and %d counters (use ulb_attention)",
@@ -603,8 +642,9 @@ extern "C" int ulb_attention_noalloc(ulb_ctx* ctx, const ulb_attn_desc* d, const
   float* scratch = nullptr;
   int* counters = nullptr;
   ULB_TRY(noalloc_scratch(c, &scratch, &counters));
-  /* the arrays keep the previous call's contents: the split counters must start at zero */
-  ULB_CUDA(cudaMemsetAsync(counters, 0, (size_t)nc * sizeof(int), c->stream));
+  /* the arrays keep the previous call's contents: the split counters of a global merge must
+     start at zero (the single-split and cluster forms read neither array) */
+  if (nc > 0) ULB_CUDA(cudaMemsetAsync(counters, 0, (size_t)nc * sizeof(int), c->stream));
   return launch_attention(c, d, q, d->n_head * d->head_dim, (const __half*)k, (const __half*)v, row_seq, row_pos, M,
                           rps, (__half*)out, scratch, counters, kNoAllocScratchFloats, kNoAllocCounters);
 }
@@ -613,17 +653,18 @@ extern "C" int ulb_attention(ulb_ctx* ctx, const ulb_attn_desc* d, const float* 
                              const uint16_t* v, const int32_t* row_seq, const int32_t* row_pos, int M,
                              int rps, uint16_t* out) {
   ULB_CHECK(ctx && d && q && k && v && row_seq && row_pos && out, ULB_EINVAL, "ulb_attention: NULL argument");
-  ULB_CHECK(d->capacity > 0 && d->n_seq > 0, ULB_EINVAL, "ulb_attention: capacity / n_seq");
+  ULB_TRY(validate_attn_desc(d, M, rps));
   Ctx* c = &ctx->c;
   ULB_CUDA(cudaSetDevice(c->device));
   int nc = 0;
-  const size_t nf = attention_scratch_floats(d, M, rps, d->capacity - 1, &nc);
+  size_t nf = 0;
+  ULB_TRY(attention_scratch_need(c, d, M, rps, d->capacity - 1, &nf, &nc));
   float* scratch = nullptr;
   int* counters = nullptr;
   ULB_TRY(dev_alloc(c, (void**)&scratch, nf * sizeof(float)));
   int rc = dev_alloc(c, (void**)&counters, (size_t)nc * sizeof(int));
   if (rc == ULB_OK) {
-    cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)nc * sizeof(int), c->stream);
+    cudaError_t e = nc > 0 ? cudaMemsetAsync(counters, 0, (size_t)nc * sizeof(int), c->stream) : cudaSuccess;
     rc = e == cudaSuccess ? launch_attention(c, d, q, d->n_head * d->head_dim, (const __half*)k, (const __half*)v,
                                              row_seq, row_pos, M, rps, (__half*)out, scratch, counters, nf, nc)
                           : cuda_error(e, "memset", __FILE__, __LINE__);

@@ -22,15 +22,22 @@ namespace ulbe {
 enum { GV_U8, GV_I8, GV_U16, GV_I16, GV_U32, GV_I32, GV_F32, GV_BOOL, GV_STR, GV_ARR, GV_U64, GV_I64, GV_F64 };
 
 size_t gguf_type_nbytes(int type, uint64_t n) {
+  /* (units of n, bytes per unit); 0 for an unsupported type, a partial block or a size that
+     does not fit 64 bits */
+  uint64_t unit = 0, per = 0;
   switch (type) {
-    case 0: return n * 4;                          /* F32  */
-    case 1: return n * 2;                          /* F16  */
-    case 2: return n % 32 ? 0 : n / 32 * 18;       /* Q4_0 */
-    case 12: return n % 256 ? 0 : n / 256 * 144;   /* Q4_K */
-    case 8: return n % 32 ? 0 : n / 32 * 34;       /* Q8_0 */
-    case 14: return n % 256 ? 0 : n / 256 * 210;   /* Q6_K */
+    case 0: unit = 1; per = 4; break;      /* F32  */
+    case 1: unit = 1; per = 2; break;      /* F16  */
+    case 2: unit = 32; per = 18; break;    /* Q4_0 */
+    case 12: unit = 256; per = 144; break; /* Q4_K */
+    case 8: unit = 32; per = 34; break;    /* Q8_0 */
+    case 14: unit = 256; per = 210; break; /* Q6_K */
     default: return 0;
   }
+  if (n % unit) return 0;
+  uint64_t bytes = 0;
+  if (__builtin_mul_overflow(n / unit, per, &bytes)) return 0;
+  return (size_t)bytes;
 }
 
 namespace {
@@ -136,17 +143,26 @@ bool GGUFFile::open(const std::string& path, std::string* err) {
     t.n_dims = (int)r.u(4);
     if (r.bad || t.n_dims < 1 || t.n_dims > 4) return fail("bad tensor info");
     uint64_t n = 1;
-    for (int j = 0; j < t.n_dims; ++j) { t.ne[j] = r.u(8); n *= t.ne[j]; }
+    bool wrap = false;
+    for (int j = 0; j < t.n_dims; ++j) {
+      t.ne[j] = r.u(8);
+      wrap |= __builtin_mul_overflow(n, t.ne[j], &n);
+    }
+    if (wrap) return fail("tensor " + t.name + ": element count overflows 64 bits");
     t.type = (int)r.u(4);
     t.offset = r.u(8);
     t.nbytes = gguf_type_nbytes(t.type, n);
-    if (!t.nbytes && n) return fail("tensor " + t.name + ": unsupported type " + std::to_string(t.type));
+    if (!t.nbytes && n)
+      return fail("tensor " + t.name + ": unsupported type " + std::to_string(t.type) +
+                  " (or a size that is not whole blocks / overflows)");
   }
   if (r.bad) return fail("truncated tensor infos");
   const size_t hdr = (size_t)(r.p - (const uint8_t*)map_);
   const size_t data = (hdr + alignment - 1) / alignment * alignment;
   for (GGUFTensor& t : tensors) {
-    if (data + t.offset + t.nbytes > map_len_) return fail("tensor " + t.name + " extends past the end of the file");
+    /* three separate comparisons: no sum of file-supplied values can wrap around */
+    if (data > map_len_ || t.offset > map_len_ - data || t.nbytes > map_len_ - data - t.offset)
+      return fail("tensor " + t.name + " extends past the end of the file");
     t.data = (const uint8_t*)map_ + data + t.offset;
   }
   return true;

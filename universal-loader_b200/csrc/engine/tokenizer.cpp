@@ -388,7 +388,16 @@ bool ByteBpeTokenizer::load(const GGUFFile& f, std::string* err) {
     std::stable_sort(v.begin(), v.end(), [&](int32_t a, int32_t b) { return tokens_[a].size() > tokens_[b].size(); });
   bos_ = (int)f.num("tokenizer.ggml.bos_token_id", -1);
   add_bos_ = f.num("tokenizer.ggml.add_bos_token", 1) != 0;
-  gpt2_split_ = f.str("tokenizer.ggml.pre", "") == "gpt2";
+  /* the pre-tokenizers whose split is implemented (and pinned against HF tokenizers): GPT-2's,
+     and Llama-3's (llama.cpp writes "llama-bpe"; "llama3" and an absent key mean the same);
+     any other name (qwen2, deepseek-llm, starcoder, ...) splits text differently, so such a
+     file is refused instead of being tokenized silently wrong */
+  const std::string pre = f.str("tokenizer.ggml.pre", "");
+  if (pre != "" && pre != "default" && pre != "gpt2" && pre != "llama-bpe" && pre != "llama3") {
+    if (err) *err = "tokenizer: pre-tokenizer '" + pre + "' is not supported (gpt2, llama-bpe / llama3)";
+    return false;
+  }
+  gpt2_split_ = pre == "gpt2";
   return true;
 }
 

@@ -152,7 +152,13 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
                      const __half* v, const int* row_seq, const int* row_pos, int M, int rps,
                      __half* out, float* scratch, int* counters, size_t scratch_floats,
                      int n_counters);
-size_t attention_scratch_floats(const ulb_attn_desc* d, int M, int rps, int max_pos, int* n_counters);
+/* argument checks shared by every attention entry point (no division by a zero head count) */
+int validate_attn_desc(const ulb_attn_desc* d, int M, int rps);
+/* split-merge scratch a launch of this shape needs: zero floats / counters when it has one key
+   split, or when its splits merge in a thread-block cluster (only a global-memory merge, over
+   caches longer than 2048 positions, reads the scratch and counters) */
+int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int max_pos, size_t* floats,
+                           int* n_counters);
 
 int launch_rmsnorm(Ctx* c, const float* x, int ldx, const float* g, int M, int d, float eps,
                    const int* row_select, __half* out, int ldo);
