@@ -22,6 +22,18 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
 
 
+# One line per greedy-stream comparison (matched length, where and why a stream stopped
+# matching), printed at the end of the run so a passing run still shows the evidence.
+PARITY_LOG = []
+
+
+def pytest_terminal_summary(terminalreporter):
+    if PARITY_LOG:
+        terminalreporter.write_sep("-", "greedy stream parity against the oracle")
+        for line in PARITY_LOG:
+            terminalreporter.write_line(line)
+
+
 def _build():
     from oracle import build as obuild
     obuild.build()

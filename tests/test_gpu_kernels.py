@@ -100,10 +100,13 @@ def test_qgemm_op_sweep(ctx, qt, NK, M):
         y_gemv = ctx.qgemm(h, x[M - 1:M], N)[0]
     finally:
         ctx.free_tensor(h)
-    rows = min(M, 8)  # the oracle checks a subset of rows at the large shapes
-    ref = orc.qgemv(t, raw, N, K, x[:rows])
-    assert _rel(y[:rows], ref) < GEMM_RTOL
-    assert _rel(y[:rows], ref) < 1e-4
+    # rows the oracle checks: the first 8, and the first and last row of every 64-token tile
+    # of the tensor-core regimes plus the batch's last row (0, 63, 64, 127, ..., M - 1)
+    rows = sorted({r for r in range(min(M, 8))} | {r for t0 in range(0, M, 64) for r in (t0, t0 + 63) if r < M} |
+                  {M - 1})
+    ref = orc.qgemv(t, raw, N, K, x[rows])
+    assert _rel(y[rows], ref) < GEMM_RTOL
+    assert _rel(y[rows], ref) < 1e-4
     # within a regime every row is computed with the same arithmetic whatever M is
     assert np.array_equal(y_last, y[M - 1])
     # across regimes (tensor-core GEMM vs GEMV) rows agree to fp32 accumulation order: the GEMM
