@@ -1,22 +1,32 @@
 #!/usr/bin/env python
 """Benchmark: accepted tok/s of the speculative draft -> verify -> accept loop.
 
-Workload: Llama-2-7B-architecture Q4_0 target (seed 0) + TinyLlama-1.1B-
-architecture Q4_0 draft (seed 2), weights N(0, 0.02) -> Q4_0, one 512-token uniform random
-prompt, k = 5, 256 committed tokens, T = 0.  Synthetic GGUF files are written once per box.
+Headline workload: Llama-2-7B-architecture Q4_0 target (seed 0) +
+TinyLlama-1.1B-architecture Q4_0 draft (seed 2), weights N(0, 0.02) -> Q4_0, one 512-token
+uniform random prompt, k = 5, 256 committed tokens, T = 0 (and a T = 0.8 figure beside it).
+Synthetic GGUF files are written once per machine.
 
 A step is one generation of 256 tokens from a fresh prefill.  `value` is committed tokens of
 all ranks / the slowest rank's device time of the generation phase (CUDA events on the
 engine's stream; prefill reported separately); `e2e` is the same count over host wall time of
 the public API call (prompt copied in, tokens copied out, prefill included).  With N GPUs each
-rank decodes its own sequence (replicas, no collective: the single-sequence workload does not
-shard), so scaling is weak.
+rank decodes its own C2 sequence (replicas, no collective: one sequence does not shard).
+
+The configurations that do shard are measured in the same run, each in a child process group
+of its own (so one cannot take the headline down with it) and reported as objects of the
+headline line:
+  "c4"  config 4 at every N: 64 Llama-3-8B / 3.2-1B Q4_K sequences sharded round-robin over
+        the GPUs (data parallel, no collective on the data path);
+  "c5"  config 5 at N >= 2: the Llama-2-70B-architecture Q4_0 target tensor-parallel over the
+        GPUs (NCCL all-reduce after attn-out and FFN-down), the 7B draft replicated.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload c2|c4|c5] [--extras auto|none|c4|c5|c4,c5]
 """
 import argparse
 import json
 import os
+import shutil
 import statistics
 import subprocess
 import sys
@@ -29,6 +39,10 @@ for p in (ROOT, PKG):
     if p not in sys.path:
         sys.path.insert(0, p)
 
+# CUDA_VISIBLE_DEVICES as the launcher set it (each rank narrows it to its own GPU later; the
+# child process groups of the c4 / c5 workloads choose their GPU from the original list)
+ORIG_CUDA_VISIBLE = os.environ.get("CUDA_VISIBLE_DEVICES")
+T_START = time.time()
 METRIC = "accepted tok/s (Llama-2-7B-arch Q4_0, k=5) at 1-8 B200; verify HBM GB/s vs peak"
 TARGET = dict(n_layer=32, d_model=4096, n_head=32, n_head_kv=32, d_ff=11008, n_vocab=32000, rms_eps=1e-5,
               rope_base=1e4, wtype="q4_0", seed=0, ctx_len=4096, name="llama2-7b-arch-q4_0-s0")
@@ -79,24 +93,66 @@ C4_WORKLOAD = ("C4: Llama-3-8B-arch Q4_K target + Llama-3.2-1B-arch Q4_K draft, 
                "sequence, T=0.8, top_p=0.9")
 
 
+# all synthetic model files of the bench (C2 + C4 + C5) take ~50 GB
+CACHE_NEED_BYTES = 64 << 30
+
+
+def cache_dir():
+    """Where the synthetic GGUF files live: ULB_BENCH_CACHE, else a machine-wide directory
+    that already holds them, else whichever of /tmp and /dev/shm has room for all of them."""
+    d = os.environ.get("ULB_BENCH_CACHE")
+    if d:
+        return d
+    cands = ["/tmp/ulb_bench_models", "/dev/shm/ulb_bench_models"]
+    for c in cands:
+        if os.path.isdir(c):
+            return c
+    for c in cands:
+        try:
+            if shutil.disk_usage(os.path.dirname(c)).free >= CACHE_NEED_BYTES:
+                return c
+        except OSError:
+            continue
+    return cands[0]
+
+
 def model_paths(target=None, draft=None):
     target, draft = target or TARGET, draft or DRAFT
-    d = os.environ.get("ULB_BENCH_CACHE", "/tmp/ulb_bench_models")
+    d = cache_dir()
     os.makedirs(d, exist_ok=True)
     return os.path.join(d, target["name"] + ".gguf"), os.path.join(d, draft["name"] + ".gguf")
 
 
-def ensure_models(rank, barrier, target=None, draft=None):
+def write_model(path, spec):
+    """Write one synthetic GGUF file (atomically: another process never sees a partial file)."""
     import vulkangguf as vg
+    tmp = "%s.part%d" % (path, os.getpid())
+    t0 = time.time()
+    vg.write_synthetic_gguf(tmp, spec)
+    os.replace(tmp, path)
+    print("[bench] wrote %s in %.1fs" % (path, time.time() - t0), file=sys.stderr)
+
+
+def ensure_models(rank, barrier, target=None, draft=None):
     target, draft = target or TARGET, draft or DRAFT
     tp, dp = model_paths(target, draft)
     if rank == 0:
         for path, spec in ((tp, target), (dp, draft)):
             if not os.path.exists(path):
-                t0 = time.time()
-                vg.write_synthetic_gguf(path, spec)
-                print("[bench] wrote %s in %.1fs" % (path, time.time() - t0), file=sys.stderr)
+                write_model(path, spec)
     barrier()
+    return tp, dp
+
+
+def ensure_models_in_child(target=None, draft=None):
+    """ensure_models for the reference arm: the files are written by a separate process, so
+    the arm's own process loads no library of this package (only the oracle it times)."""
+    target, draft = target or TARGET, draft or DRAFT
+    tp, dp = model_paths(target, draft)
+    if not (os.path.exists(tp) and os.path.exists(dp)):
+        code = ("import sys; sys.path[:0] = [%r, %r]; import bench; bench.ensure_models(0, lambda: None)"
+                % (ROOT, PKG))
+        subprocess.run([sys.executable, "-c", code], check=True)
     return tp, dp
 
 
@@ -166,7 +222,10 @@ def dist_setup():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+        # a child process group (the c4 / c5 workloads) gives up sooner: its parent's time limit
+        # must end it with an error, not with the whole bench's
+        secs = 400 if "--child" in sys.argv else 900
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=secs))
 
         def barrier():
             dist.barrier()
@@ -255,15 +314,76 @@ def qgemv_roofline(device, reps=10):
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle port)
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_port_rounds(tp, dp, rounds, warp=(0.0, 0, 1.0)):
+    """`rounds` speculative rounds of the C2 models on the host cores (the oracle port, OpenMP
+    over every core this process may use: a launcher's OMP_NUM_THREADS does not shrink it)."""
     from oracle import ulb_oracle as orc
     t, d = orc.Model(tp), orc.Model(dp)
     t0 = time.perf_counter()
-    n, stats = orc.bench_rounds(t, d, PROMPT_LEN, K_SPEC, rounds, warp, seed=0)
+    n, stats = orc.bench_rounds(t, d, PROMPT_LEN, K_SPEC, rounds, warp, seed=0, threads=host_cores())
     dt = time.perf_counter() - t0
     t.close()
     d.close()
     return n, dt, stats
+
+
+def reference_kernels(min_s=0.3):
+    """The reference's own CPU kernels (src/cpu_backend/gemm_avx2.cpp:6-25 gemm_avx2_f32 and
+    dequantize_cpu.cpp:6-49 dequantize_q4_0_f32, built from its sources with its flags by
+    oracle/ref_build.py), timed single-threaded as the reference runs them, at the config-3
+    shapes with M = 1.  Their results are not valid (a lane-wise product that reads every
+    eighth row of B; 20-byte Q4_0 blocks): the figures are speeds only."""
+    import ctypes as C
+    import numpy as np
+    path = os.path.join(ROOT, "oracle", "_ref", "libref_cpu.so")
+    if not os.path.exists(path):
+        return {"unavailable": "oracle/_ref/libref_cpu.so not built (oracle/ref_build.py needs the reference tree)"}
+    lib = C.CDLL(path)
+    lib.ref_gemm_avx2_f32.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32]
+    lib.ref_dequantize_q4_0_f32.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]
+    rng = np.random.default_rng(0)
+
+    def timed(fn):
+        fn()
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            reps += 1
+            dt = time.perf_counter() - t0
+            if dt >= min_s:
+                return dt / reps
+
+    out = {}
+    for (N, K) in ((4096, 4096), (11008, 4096), (4096, 11008)):
+        n = N * K
+        blocks = np.zeros((n // 32 + 1, 20), np.uint8)  # one block past the range: the decoder reads it
+        blocks[:, 4:] = rng.integers(0, 256, (n // 32 + 1, 16), dtype=np.uint8)
+        blocks[:, :4] = np.frombuffer(np.float32(0.01).tobytes(), np.uint8)
+        dst = np.empty(n, np.float32)
+        t_dq = timed(lambda: lib.ref_dequantize_q4_0_f32(blocks.ctypes.data, dst.ctypes.data, n))
+        a = rng.standard_normal(K).astype(np.float32)
+        b = rng.standard_normal((K, N)).astype(np.float32)
+        c = np.empty(N, np.float32)
+        t_mm = timed(lambda: lib.ref_gemm_avx2_f32(a.ctypes.data, b.ctypes.data, c.ctypes.data, 1, N, K))
+        q4 = n // 32 * 18
+        out["%dx%d" % (N, K)] = {
+            "dequantize_q4_0_f32_us": t_dq * 1e6, "gemm_avx2_f32_m1_us": t_mm * 1e6,
+            "dequant_plus_gemm_us": (t_dq + t_mm) * 1e6,
+            "q4_gbs_equivalent": q4 / (t_dq + t_mm) / 1e9}
+        del blocks, dst, b
+    return {"kind": "reference", "cores": 1,
+            "sample": "cpu::dequantize_q4_0_f32 then cpu::gemm_avx2_f32 at M=1 (the reference's CPU linear), "
+                      "single-threaded as the reference calls them, g++ -mavx2 -mfma -mf16c -O3 -ffast-math",
+            "validity": "numerically invalid: the GEMM multiplies lane-wise and reads every eighth row of B; the "
+                        "decoder reads 20-byte blocks (fp32 scale); speeds only",
+            "shapes": out}
 
 
 def cpu_baseline(tp, dp, budget_s=20.0):
@@ -273,9 +393,10 @@ def cpu_baseline(tp, dp, budget_s=20.0):
         extra = max(1, int(budget_s / dt) - 1)
         n2, dt2, _ = cpu_port_rounds(tp, dp, extra)
         n, dt, rounds = n + n2, dt + dt2, 1 + extra
-    return {"value": n / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": n / dt, "unit": "tok/s", "cores": host_cores(), "kind": "port",
             "sample": "%d speculative round(s) of the C2 models at context %d (KV caches pre-filled), k=%d, T=0, "
-                      "oracle/oracle.c with OpenMP; %.1f s" % (rounds, PROMPT_LEN, K_SPEC, dt)}
+                      "oracle/oracle.c with OpenMP over %d cores; %.1f s" % (rounds, PROMPT_LEN, K_SPEC, host_cores(), dt),
+            "reference_kernels": reference_kernels()}
 
 
 def run_reference(args):
@@ -283,7 +404,7 @@ def run_reference(args):
     if rank != 0:
         done()
         return 0
-    tp, dp = ensure_models(0, lambda: None)
+    tp, dp = ensure_models_in_child()
     for _ in range(args.warmup):
         cpu_port_rounds(tp, dp, 1)
     toks, tsum = 0, 0.0
@@ -292,20 +413,46 @@ def run_reference(args):
         toks += n
         tsum += dt
     value = toks / tsum
+    cores = host_cores()
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": tsum / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4_0xf16->f32", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": WORKLOAD, "step": "one speculative round at context 512 on the host cores"},
-            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": "one round per step of the C2 workload at context %d (KV pre-filled); the "
-                                       "reference's own CPU path cannot run this loop (its engine computes only "
-                                       "Q/K/V and its AVX2 GEMM/dequant are not valid), so the oracle port "
-                                       "stands in" % PROMPT_LEN},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": "one round per step of the C2 workload at context %d (KV pre-filled), OpenMP "
+                                       "over all %d host cores of the box (rank 0 alone; the host is shared by every "
+                                       "N); the reference's own CPU path cannot run this loop (its engine computes "
+                                       "only Q/K/V and its AVX2 GEMM/dequant are not valid), so the oracle port "
+                                       "stands in; the reference's own kernels are timed under reference_kernels"
+                                       % (PROMPT_LEN, cores),
+                             "reference_kernels": reference_kernels()},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     done()
     return 0
+
+
+def _timed_generations(api, prompt, cfg, steps):
+    """`steps` generations through the public API; returns summed stats"""
+    agg = dict(toks=0, dec_ms=0.0, pre_ms=0.0, launches=0, accepted=0, drafted=0, rounds=0, h2d=0.0, d2h=0.0)
+    outs = []
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        out = api.generate_tokens(prompt, cfg)
+        st = api.get_last_stats()
+        outs.append(out)
+        agg["toks"] += len(out) if out and isinstance(out[0], int) else sum(len(o) for o in out)
+        agg["dec_ms"] += st["decode_ms"]
+        agg["pre_ms"] += st["prefill_ms"]
+        agg["launches"] += st["launches"]
+        agg["accepted"] += st["accepted"]
+        agg["drafted"] += st["drafted"]
+        agg["rounds"] += st["rounds"]
+        agg["h2d"], agg["d2h"] = st["h2d_bytes"], st["d2h_bytes"]
+    agg["wall"] = time.perf_counter() - t0
+    agg["outs"] = outs
+    return agg
 
 
 def run_ours(args):
@@ -321,92 +468,160 @@ def run_ours(args):
         return 1
     api.enable_speculative_decoding(True)
     api.set_speculation_length(K_SPEC)
-    cfg = vg.GenerationConfig()
-    cfg.max_tokens = NEW_TOKENS
-    cfg.temperature = 0.0
-    cfg.do_sample = False
-    cfg.seed = 0
+
+    def cfg_t(temp):
+        cfg = vg.GenerationConfig()
+        cfg.max_tokens = NEW_TOKENS
+        cfg.temperature = temp
+        cfg.do_sample = temp > 0
+        cfg.seed = 0
+        return cfg
+
     prompt = prompt_for(rank)
     for _ in range(args.warmup):
-        api.generate_tokens(prompt, cfg)
+        api.generate_tokens(prompt, cfg_t(0.0))
     barrier()
     clocks = ClockSampler(smi_index)
     clocks.start()
-    t0 = time.perf_counter()
-    toks = 0
-    dec_ms = pre_ms = 0.0
-    launches = 0
-    accepted = drafted = rounds = 0
-    h2d = d2h = 0.0
-    outs = []
-    for _ in range(args.steps):
-        out = api.generate_tokens(prompt, cfg)
-        st = api.get_last_stats()
-        outs.append(out)
-        toks += len(out)
-        dec_ms += st["decode_ms"]
-        pre_ms += st["prefill_ms"]
-        launches += st["launches"]
-        accepted += st["accepted"]
-        drafted += st["drafted"]
-        rounds += st["rounds"]
-        h2d = st["h2d_bytes"]
-        d2h = st["d2h_bytes"]
-    wall = time.perf_counter() - t0
+    g = _timed_generations(api, prompt, cfg_t(0.0), args.steps)
     barrier()
     clk = clocks.stop()
-    assert all(o == outs[0] for o in outs), "greedy generation is not deterministic"
+    assert all(o == g["outs"][0] for o in g["outs"]), "greedy generation is not deterministic"
     prof = api.profile_round()
-    tot_toks = allsum(toks)
-    max_dec = allmax(dec_ms)
-    max_wall = allmax(wall)
-    max_step = allmax((dec_ms + pre_ms) / args.steps)
-    tot_launch = allsum(launches)
+    # config 2 at T = 0.8 (sampled drafts and rejection sampling), a few steps after one warm-up
+    api.generate_tokens(prompt, cfg_t(0.8))
+    t08_steps = max(1, min(args.steps, 5))
+    barrier()
+    g8 = _timed_generations(api, prompt, cfg_t(0.8), t08_steps)
+    prof8 = api.profile_round()
+    tot_toks = allsum(g["toks"])
+    max_dec = allmax(g["dec_ms"])
+    max_wall = allmax(g["wall"])
+    max_step = allmax((g["dec_ms"] + g["pre_ms"]) / args.steps)
+    tot_launch = allsum(g["launches"])
     value = tot_toks / (max_dec / 1e3)
     e2e = tot_toks / max_wall
-    if rank != 0:
-        done()
-        return 0
-    peak, peak_src = load_peaks()
-    ctx_len = PROMPT_LEN + NEW_TOKENS
-    verify_bytes = (q4_0_bytes(linear_weights(TARGET)) + kv_bytes_per_token(TARGET) * ctx_len
-                    + (K_SPEC + 1) * kv_bytes_per_token(TARGET) + (K_SPEC + 1) * TARGET["n_vocab"] * 4)
-    verify_gbs = verify_bytes / (prof["verify_ms"] / 1e3) / 1e9
-    rl = qgemv_roofline(0)
-    line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": max_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "q4_0xf16->f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "parallelism": "replicas (one sequence per GPU, no collective)",
-                   "l2": "inputs larger than L2 (3.7 GB of target weights per verify)",
-                   "timed": "generation phase, CUDA events on the engine stream; prefill reported separately"},
-        "acceptance_rate": accepted / drafted if drafted else 0.0,
-        "rounds_per_step": rounds / args.steps,
-        "prefill_ms": pre_ms / args.steps,
-        "decode_ms": dec_ms / args.steps,
-        "round_profile_ms": prof,
-        "verify": {"bytes": verify_bytes, "ms": prof["verify_ms"], "gbs": verify_gbs,
-                   "frac": verify_gbs / peak, "peak": peak, "peak_source": peak_src,
-                   "frac_of_8tbs": verify_gbs / 8000.0},
-        "roofline": {"bound": "hbm", "achieved": rl["achieved_gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": rl["achieved_gbs"] / peak,
-                     "traffic": rl["bytes_per_layer"] / 4 * QGEMV_TRAFFIC_RATIO,
-                     "traffic_note": "bytes per average launch: algorithmic bytes x %.3f, the DRAM read+write / "
-                                     "algorithmic ratio of an ncu capture of the Q4_0 11008x4096 M=5 launch "
-                                     "(no re-reads)" % QGEMV_TRAFFIC_RATIO,
-                     "kernel": "qgemv_kernel<Q4_0, NT=1> (warp-streamed fused Q4_0 dequant-GEMV, 7B verify shapes, M=6)",
-                     "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
-                     "shapes": rl["shapes"]},
-        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "note": "public API generate_tokens (host prompt in, host tokens out), prefill included"},
-        "gpu_launches": int(tot_launch),
-        "clocks": clk,
-    }
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(tp, dp)
-    print(json.dumps(line), flush=True)
+    value8 = allsum(g8["toks"]) / (allmax(g8["dec_ms"]) / 1e3)
+    e2e8 = allsum(g8["toks"]) / allmax(g8["wall"])
+    line = None
+    if rank == 0:
+        peak, peak_src = load_peaks()
+        ctx_len = PROMPT_LEN + NEW_TOKENS
+        verify_bytes = (q4_0_bytes(linear_weights(TARGET)) + kv_bytes_per_token(TARGET) * ctx_len
+                        + (K_SPEC + 1) * kv_bytes_per_token(TARGET) + (K_SPEC + 1) * TARGET["n_vocab"] * 4)
+        verify_gbs = verify_bytes / (prof["verify_ms"] / 1e3) / 1e9
+        draft_bytes = K_SPEC * (q4_0_bytes(linear_weights(DRAFT)) + kv_bytes_per_token(DRAFT) * ctx_len)
+        draft_gbs = draft_bytes / (prof["draft_ms"] / 1e3) / 1e9
+        rl = qgemv_roofline(0)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_0xf16->f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "parallelism": "replicas (one sequence per GPU, no collective)",
+                       "l2": "inputs larger than L2 (3.7 GB of target weights per verify)",
+                       "timed": "generation phase, CUDA events on the engine stream; prefill reported separately"},
+            "acceptance_rate": g["accepted"] / g["drafted"] if g["drafted"] else 0.0,
+            "rounds_per_step": g["rounds"] / args.steps,
+            "prefill_ms": g["pre_ms"] / args.steps,
+            "decode_ms": g["dec_ms"] / args.steps,
+            "round_profile_ms": prof,
+            "verify": {"bytes": verify_bytes, "ms": prof["verify_ms"], "gbs": verify_gbs,
+                       "frac": verify_gbs / peak, "peak": peak, "peak_source": peak_src,
+                       "frac_of_8tbs": verify_gbs / 8000.0},
+            "draft": {"bytes": draft_bytes, "ms": prof["draft_ms"], "steps": K_SPEC, "gbs": draft_gbs,
+                      "frac": draft_gbs / peak, "note": "k draft steps of one round: TinyLlama weights + KV read"},
+            "t08": {"value": value8, "unit": "tok/s", "e2e": e2e8, "steps": t08_steps,
+                    "acceptance_rate": g8["accepted"] / g8["drafted"] if g8["drafted"] else 0.0,
+                    "rounds_per_step": g8["rounds"] / t08_steps, "round_profile_ms": prof8,
+                    "config": "config 2 at T=0.8 (no top-k / top-p), Philox seed 0"},
+            "value_t08": value8,
+            "roofline": {"bound": "hbm", "achieved": rl["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": rl["achieved_gbs"] / peak,
+                         "traffic": rl["bytes_per_layer"] / 4 * QGEMV_TRAFFIC_RATIO,
+                         "traffic_note": "bytes per average launch: algorithmic bytes x %.3f, the DRAM read+write / "
+                                         "algorithmic ratio of an ncu capture of the Q4_0 11008x4096 M=5 launch "
+                                         "(no re-reads)" % QGEMV_TRAFFIC_RATIO,
+                         "kernel": "qgemv_kernel<Q4_0, NT=1> (warp-streamed fused Q4_0 dequant-GEMV, 7B verify shapes, M=6)",
+                         "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
+                         "shapes": rl["shapes"]},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": g["h2d"], "d2h_bytes_per_step": g["d2h"],
+                    "note": "public API generate_tokens (host prompt in, host tokens out), prefill included"},
+            "gpu_launches": int(tot_launch),
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(tp, dp)
+    # the GPU memory of the C2 models goes back before the sharded workloads run
+    del api
+    import gc
+    gc.collect()
+    barrier()
+    for wl in extras_for(args, world):
+        obj = run_child(wl, args, world, rank, barrier)
+        if line is not None:
+            line[wl] = obj
+    if line is not None:
+        print(json.dumps(line), flush=True)
     done()
     return 0
+
+
+def extras_for(args, world):
+    if args.child or args.extras == "none":
+        return []
+    if args.extras == "auto":
+        return ["c4"] + (["c5"] if world >= 2 else [])
+    return [w for w in args.extras.split(",") if w in ("c4", "c5")]
+
+
+# wall-clock budget of one bench run (the sharded workloads get what the headline leaves)
+BENCH_BUDGET_S = float(os.environ.get("ULB_BENCH_BUDGET_S", "820"))
+CHILD_CAP_S = {"c4": 330.0, "c5": 420.0}
+
+
+def run_child(wl, args, world, rank, barrier):
+    """Run workload `wl` as its own process group (one child per rank, the same rank / world,
+    a port of its own) and return rank 0's JSON line as an object; an error or a timeout in the
+    child is reported, not raised."""
+    left = BENCH_BUDGET_S - (time.time() - T_START) - 20.0
+    timeout = min(CHILD_CAP_S[wl], left)
+    obj = None
+    if timeout < 60:
+        obj = {"skipped": "%.0f s of the bench's %.0f s budget left" % (max(left, 0), BENCH_BUDGET_S)}
+    else:
+        env = dict(os.environ)
+        if ORIG_CUDA_VISIBLE is None:
+            env.pop("CUDA_VISIBLE_DEVICES", None)
+        else:
+            env["CUDA_VISIBLE_DEVICES"] = ORIG_CUDA_VISIBLE
+        if world > 1:
+            env["MASTER_PORT"] = str(int(os.environ.get("MASTER_PORT", "29500")) + (11 if wl == "c4" else 13))
+        if wl == "c5":
+            env.setdefault("NCCL_DEBUG", "INFO")
+            env.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        cmd = [sys.executable, os.path.abspath(__file__), "--workload", wl, "--steps", "1", "--warmup", "1",
+               "--gpus", str(world), "--child"]
+        t0 = time.time()
+        try:
+            r = subprocess.run(cmd, env=env, stdout=subprocess.PIPE, text=True, timeout=timeout)
+            out, rc = r.stdout, r.returncode
+        except subprocess.TimeoutExpired as e:
+            out = e.stdout.decode() if isinstance(e.stdout, bytes) else (e.stdout or "")
+            rc = "killed after %.0f s (time limit)" % timeout
+        parsed = None
+        for ln in out.splitlines():
+            if ln.startswith("{"):
+                try:
+                    parsed = json.loads(ln)
+                    continue
+                except ValueError:
+                    pass
+            print(ln, file=sys.stderr)
+        if rank == 0:
+            obj = parsed if (parsed is not None and rc == 0) else {"error": "child exit %s" % rc, "partial": parsed}
+            obj["child_wall_s"] = time.time() - t0
+    barrier()
+    return obj
 
 
 # BASELINE config 5: Llama-2-70B-arch Q4_0 target (N(0, 0.02), seed 0), tensor-parallel over the GPUs with an
@@ -439,47 +654,36 @@ def run_c5(args):
         if not api.init_tensor_parallel(rank, world, box[0]):
             print("[bench] tensor-parallel init failed", file=sys.stderr)
             return 1
+    t_load = time.time()
     if not api.load_model(tp) or not api.load_draft_model(dp):
         print("[bench] model load failed", file=sys.stderr)
         return 1
+    t_load = time.time() - t_load
     api.enable_speculative_decoding(True)
     api.set_speculation_length(C5_K)
     rng = np.random.default_rng(1)
     prompts = [rng.integers(0, C5_TARGET["n_vocab"], C5_PROMPT).astype(np.int32).tolist() for _ in range(C5_SEQS)]
-    cfg = vg.GenerationConfig()
-    cfg.max_tokens, cfg.temperature, cfg.do_sample, cfg.seed = C5_NEW, 0.0, False, 0
-    for _ in range(args.warmup):
-        api.generate_tokens(prompts, cfg)
+
+    def cfg(n):
+        c = vg.GenerationConfig()
+        c.max_tokens, c.temperature, c.do_sample, c.seed = n, 0.0, False, 0
+        return c
+
+    for _ in range(args.warmup):  # warm-up generations: every kernel shape and the round graph
+        api.generate_tokens(prompts, cfg(8))
     barrier()
     clocks = ClockSampler(smi_index)
     clocks.start()
-    t0 = time.perf_counter()
-    toks = 0
-    dec_ms = pre_ms = 0.0
-    launches = accepted = drafted = rounds = 0
-    h2d = d2h = 0.0
-    outs = []
-    for _ in range(args.steps):
-        out = api.generate_tokens(prompts, cfg)
-        st = api.get_last_stats()
-        outs.append(out)
-        toks += sum(len(o) for o in out)
-        dec_ms += st["decode_ms"]
-        pre_ms += st["prefill_ms"]
-        launches += st["launches"]
-        accepted += st["accepted"]
-        drafted += st["drafted"]
-        rounds += st["rounds"]
-        h2d, d2h = st["h2d_bytes"], st["d2h_bytes"]
-    wall = time.perf_counter() - t0
+    g = _timed_generations(api, prompts, cfg(C5_NEW), args.steps)
     barrier()
     clk = clocks.stop()
     prof = api.profile_round()
-    max_dec = allmax(dec_ms)
-    max_wall = allmax(wall)
-    max_step = allmax((dec_ms + pre_ms) / args.steps)
-    tot_launch = allsum(launches)
+    max_dec = allmax(g["dec_ms"])
+    max_wall = allmax(g["wall"])
+    max_step = allmax((g["dec_ms"] + g["pre_ms"]) / args.steps)
+    tot_launch = allsum(g["launches"])
     verify_ms = allmax(prof["verify_ms"])
+    ar_ms = allmax(prof.get("allreduce_ms", 0.0))
     if rank != 0:
         done()
         return 0
@@ -492,23 +696,30 @@ def run_c5(args):
     lm_head = q4_0_bytes(C5_TARGET["d_model"] * C5_TARGET["n_vocab"])
     verify_bytes = (w_bytes - lm_head) / world + lm_head + C5_SEQS * ctx_len * kv_tok / world
     gbs = verify_bytes / (verify_ms / 1e3) / 1e9
+    rows = C5_SEQS * (C5_K + 1)
+    ar_bytes = rows * C5_TARGET["d_model"] * 4  # one fp32 all-reduce payload (attn_output or ffn_down partials)
     line = {
         "metric": "accepted tok/s (Llama-2-70B-arch Q4_0 tensor-parallel, batch 8, k=6)",
-        "value": toks / (max_dec / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "value": g["toks"] / (max_dec / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": max_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "q4_0xf16->f32", "data": "synthetic",
         "config": {"workload": C5_WORKLOAD, "parallelism": "tp%d (NCCL all-reduce, fp32 partial sums)" % world,
-                   "l2": "inputs larger than L2 (38.6 GB of target weights)",
+                   "l2": "inputs larger than L2 (38.6 GB of target weights)", "warmup_tokens": 8,
                    "timed": "generation phase, CUDA events, max over ranks; prefill separate"},
-        "acceptance_rate": accepted / drafted if drafted else 0.0,
-        "rounds_per_step": rounds / args.steps,
-        "prefill_ms": pre_ms / args.steps, "decode_ms": dec_ms / args.steps,
+        "acceptance_rate": g["accepted"] / g["drafted"] if g["drafted"] else 0.0,
+        "rounds_per_step": g["rounds"] / args.steps,
+        "prefill_ms": g["pre_ms"] / args.steps, "decode_ms": g["dec_ms"] / args.steps,
+        "load_s": t_load,
         "round_profile_ms": prof,
+        "allreduce": {"ms_per_verify": ar_ms, "count_per_verify": prof.get("allreduces", 0),
+                      "bytes_each": ar_bytes, "share_of_verify": ar_ms / verify_ms if verify_ms else None,
+                      "note": "CUDA events on the engine stream around each ncclAllReduce of one profiled round "
+                              "(includes waiting for the slowest rank), max over ranks"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                      "traffic": None, "kernel": "target verify forward of one round per GPU (weights slice + KV)",
                      "peak_source": peak_src},
-        "e2e": {"value": toks / max_wall, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "note": "public API generate_tokens, prefill included"},
+        "e2e": {"value": g["toks"] / max_wall, "unit": "tok/s", "h2d_bytes_per_step": g["h2d"],
+                "d2h_bytes_per_step": g["d2h"], "note": "public API generate_tokens, prefill included"},
         "gpu_launches": int(tot_launch),
         "clocks": clk,
     }
@@ -557,33 +768,21 @@ def run_c4(args):
     barrier()
     clocks = ClockSampler(smi_index)
     clocks.start()
-    t0 = time.perf_counter()
-    toks = 0
-    dec_ms = pre_ms = 0.0
-    launches = accepted = drafted = rounds = 0
-    h2d = d2h = 0.0
-    for _ in range(args.steps):
-        out = api.generate_tokens(prompts, cfg(C4_NEW))
-        st = api.get_last_stats()
-        toks += sum(len(o) for o in out)
-        dec_ms += st["decode_ms"]
-        pre_ms += st["prefill_ms"]
-        launches += st["launches"]
-        accepted += st["accepted"]
-        drafted += st["drafted"]
-        rounds += st["rounds"]
-        h2d, d2h = st["h2d_bytes"], st["d2h_bytes"]
-    wall = time.perf_counter() - t0
+    g = _timed_generations(api, prompts, cfg(C4_NEW), args.steps)
     barrier()
     clk = clocks.stop()
     prof = api.profile_round()
-    tot_toks = allsum(toks)
-    max_dec = allmax(dec_ms)
-    max_wall = allmax(wall)
-    max_step = allmax((dec_ms + pre_ms) / args.steps)
-    tot_launch = allsum(launches)
+    tot_toks = allsum(g["toks"])
+    max_dec = allmax(g["dec_ms"])
+    max_wall = allmax(g["wall"])
+    max_step = allmax((g["dec_ms"] + g["pre_ms"]) / args.steps)
+    tot_launch = allsum(g["launches"])
     verify_ms = allmax(prof["verify_ms"])
+    draft_ms = allmax(prof["draft_ms"])
     rows = len(prompts) * (C4_K + 1)
+    # KV bytes one verify of this rank reads: its sequences' caches at mid-generation
+    ctx_sum = sum(len(p) for p in prompts) + len(prompts) * C4_NEW // 2
+    kv_read = allmax(ctx_sum * kv_bytes_per_token(C4_TARGET))
     if rank != 0:
         done()
         return 0
@@ -599,7 +798,9 @@ def run_c4(args):
     except Exception:
         pass
     tf_peak = float(peaks.get("bf16_tflops_sustained", 1385.6))
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     achieved = flop / (verify_ms / 1e3) / 1e12
+    verify_bytes = n_w * 144 / 256 + kv_read + rows * C4_TARGET["n_vocab"] * 4
     line = {
         "metric": "accepted tok/s (Llama-3-8B-arch Q4_K, 64 sequences, k=8, T=0.8, top_p=0.9), data-parallel",
         "value": tot_toks / (max_dec / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -608,15 +809,20 @@ def run_c4(args):
         "config": {"workload": C4_WORKLOAD, "parallelism": "dp%d (sequences sharded, no collective)" % world,
                    "sequences_per_gpu": len(prompts), "l2": "inputs larger than L2 (4.2 GB of weights, ~18 GB KV)",
                    "warmup_tokens": 8, "timed": "generation phase, CUDA events, max over ranks; prefill separate"},
-        "acceptance_rate": accepted / drafted if drafted else 0.0,
-        "rounds_per_step": rounds / args.steps,
-        "prefill_ms": pre_ms / args.steps, "decode_ms": dec_ms / args.steps,
+        "sequences_per_gpu": len(prompts),
+        "acceptance_rate": g["accepted"] / g["drafted"] if g["drafted"] else 0.0,
+        "rounds_per_step": g["rounds"] / args.steps,
+        "prefill_ms": g["pre_ms"] / args.steps, "decode_ms": g["dec_ms"] / args.steps,
         "round_profile_ms": prof,
+        "verify": {"rows": rows, "ms": verify_ms, "tflops": achieved, "tflops_frac": achieved / tf_peak,
+                   "bytes": verify_bytes, "gbs": verify_bytes / (verify_ms / 1e3) / 1e9,
+                   "hbm_frac": verify_bytes / (verify_ms / 1e3) / 1e9 / hbm_peak, "draft_ms": draft_ms},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak, "unit": "TFLOP/s",
                      "frac": achieved / tf_peak, "traffic": None,
                      "kernel": "verify forward of one round (tcgen05 dequant-GEMM at %d rows + attention)" % rows,
                      "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained" if peaks else "fallback"},
-        "e2e": {"value": tot_toks / max_wall, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+        "e2e": {"value": tot_toks / max_wall, "unit": "tok/s", "h2d_bytes_per_step": g["h2d"],
+                "d2h_bytes_per_step": g["d2h"],
                 "note": "public API generate_tokens on each rank's sequences, prefill included"},
         "gpu_launches": int(tot_launch),
         "clocks": clk,
@@ -750,6 +956,10 @@ def main():
                          "sharded data-parallel over the GPUs; c5: 70B target tensor-parallel over the GPUs + "
                          "replicated 7B draft, batch 8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--extras", default="auto",
+                    help="sharded workloads reported inside the c2 line: auto (c4 at every N, c5 at N >= 2), none, "
+                         "or a list such as c4,c5")
+    ap.add_argument("--child", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -307,6 +307,12 @@ ULB_API int ulb_spec_free(ulb_spec* s);
  * but nothing is committed for them.  Replaces the reference's never-constructed
  * vulkan::Profiler timestamps (src/vulkan_backend/profiler.cpp:174-230). */
 ULB_API int ulb_spec_profile_round(ulb_spec* s, float ms[3]);
+/* ulb_spec_profile_round plus the tensor-parallel exchange of the round: ms[3] the summed
+ * CUDA-event time of the round's NCCL all-reduces (each measured on the context stream from
+ * just before ncclAllReduce to just after, so it includes waiting for the slowest rank; 0
+ * without a communicator), ms[4] how many there were.  Replaces the per-dispatch timestamps
+ * the reference's multi-GPU manager never takes (src/vulkan_backend/multi_gpu_manager.cpp). */
+ULB_API int ulb_spec_profile_round_ex(ulb_spec* s, float ms[5]);
 /* Kernels this loop launched since its last prefill (prefill and every round included). */
 ULB_API int ulb_spec_launch_count(ulb_spec* s, uint64_t* out);
 

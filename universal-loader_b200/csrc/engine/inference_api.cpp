@@ -344,7 +344,7 @@ class InferenceAPI {
   }
 
   py::dict profile_round() {
-    float ms[3] = {0, 0, 0};
+    float ms[5] = {0, 0, 0, 0, 0};
     bool ok;
     {
       std::lock_guard<std::mutex> lk(mu_);
@@ -355,6 +355,8 @@ class InferenceAPI {
     d["draft_ms"] = ms[0];
     d["verify_ms"] = ms[1];
     d["accept_ms"] = ms[2];
+    d["allreduce_ms"] = ms[3];
+    d["allreduces"] = (int)ms[4];
     return d;
   }
 

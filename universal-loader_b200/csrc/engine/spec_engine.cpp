@@ -204,10 +204,10 @@ bool Engine::generate(const std::vector<std::vector<int32_t>>& prompts, const Ge
   return true;
 }
 
-bool Engine::profile_round(float ms[3]) {
+bool Engine::profile_round(float ms[5]) {
   std::lock_guard<std::mutex> lk(mu_);
   if (!spec_) return fail("no generation to profile");
-  if (ulb_spec_profile_round(spec_, ms) != ULB_OK) return fail(ulb_last_error());
+  if (ulb_spec_profile_round_ex(spec_, ms) != ULB_OK) return fail(ulb_last_error());
   return true;
 }
 

@@ -62,8 +62,9 @@ class Engine {
                 std::vector<std::vector<int32_t>>* out, GenStats* st);
   /* logits of the last position after feeding `tokens` to the target from an empty cache */
   bool last_logits(const std::vector<int32_t>& tokens, std::vector<float>* out);
-  /* time one extra round of the last generation's loop by phase: draft, verify, accept (ms) */
-  bool profile_round(float ms[3]);
+  /* time one extra round of the last generation's loop by phase: draft, verify, accept (ms),
+     then the summed time of its tensor-parallel all-reduces (ms) and their count */
+  bool profile_round(float ms[5]);
 
   ulb_ctx* ctx() { return ctx_; }
 

@@ -69,8 +69,14 @@ int check_device_errors(Ctx* c) {
 
 int tp_allreduce_sum(Ctx* c, float* buf, size_t n) {
   ULB_CHECK(c->nccl, ULB_EINVAL, "tensor parallelism: the context has no communicator (ulb_tp_init)");
+  const bool timed = c->ar_timing && c->ar_used + 2 <= c->ar_events.size();
+  if (timed) ULB_CUDA(cudaEventRecord(c->ar_events[c->ar_used], c->stream));
   const ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, (ncclComm_t)c->nccl, c->stream);
   ULB_CHECK(r == ncclSuccess, ULB_ENCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
+  if (timed) {
+    ULB_CUDA(cudaEventRecord(c->ar_events[c->ar_used + 1], c->stream));
+    c->ar_used += 2;
+  }
   return ULB_OK;
 }
 
@@ -146,6 +152,7 @@ int ulb_destroy(ulb_ctx* ctx) {
   cudaSetDevice(ctx->c.device);
   cudaStreamSynchronize(ctx->c.stream);
   if (ctx->c.nccl) ncclCommDestroy((ncclComm_t)ctx->c.nccl);
+  for (cudaEvent_t e : ctx->c.ar_events) cudaEventDestroy(e);
   cudaFree(ctx->c.dev_err);
   cudaFree(ctx->c.zero_row);
   cudaFree(ctx->c.tc_ws);

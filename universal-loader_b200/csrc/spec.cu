@@ -415,6 +415,36 @@ int ulb_spec_profile_round(ulb_spec* h, float ms[3]) {
   return rc;
 }
 
+int ulb_spec_profile_round_ex(ulb_spec* h, float ms[5]) {
+  ULB_CHECK(h && ms, ULB_EINVAL, "ulb_spec_profile_round_ex: NULL argument");
+  Spec* sp = &h->s;
+  Ctx* c = sp->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  /* two events per all-reduce: 2 per layer of the target's verify forward (and of the draft's
+     forwards, which are replicated and do not all-reduce) */
+  if (c->nccl) {
+    const size_t need = (size_t)4 * 512;
+    while (c->ar_events.size() < need) {
+      cudaEvent_t e;
+      ULB_CUDA(cudaEventCreate(&e));
+      c->ar_events.push_back(e);
+    }
+  }
+  c->ar_used = 0;
+  c->ar_timing = c->nccl != nullptr;
+  const int rc = ulb_spec_profile_round(h, ms);
+  c->ar_timing = false;
+  ms[3] = 0.f;
+  ms[4] = (float)(c->ar_used / 2);
+  if (rc != ULB_OK) return rc;
+  for (size_t i = 0; i + 1 < c->ar_used; i += 2) {
+    float t = 0.f;
+    ULB_CUDA(cudaEventElapsedTime(&t, c->ar_events[i], c->ar_events[i + 1]));
+    ms[3] += t;
+  }
+  return ULB_OK;
+}
+
 int ulb_spec_launch_count(ulb_spec* h, uint64_t* out) {
   ULB_CHECK(h && out, ULB_EINVAL, "ulb_spec_launch_count: NULL argument");
   *out = h->s.launches;

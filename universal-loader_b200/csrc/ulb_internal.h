@@ -92,6 +92,11 @@ struct Ctx {
   size_t pf_bytes = 0;
   const void* pf2_ptr = nullptr; /* a second range, prefetched after the first */
   size_t pf2_bytes = 0;
+  /* timing of the tensor-parallel all-reduces (on while a round is profiled): a CUDA event
+     pair is recorded around each ncclAllReduce, events[2i] before and events[2i+1] after */
+  bool ar_timing = false;
+  std::vector<cudaEvent_t> ar_events;
+  size_t ar_used = 0;
 };
 constexpr size_t kPrefetchMaxBytes = (size_t)48 << 20;
 /* fp32 sum over the communicator's ranks, in place, on the context stream */
