@@ -575,8 +575,8 @@ def extras_for(args, world):
 
 
 # wall-clock budget of one bench run (the sharded workloads get what the headline leaves)
-BENCH_BUDGET_S = float(os.environ.get("ULB_BENCH_BUDGET_S", "820"))
-CHILD_CAP_S = {"c4": 330.0, "c5": 420.0}
+BENCH_BUDGET_S = float(os.environ.get("ULB_BENCH_BUDGET_S", "840"))
+CHILD_CAP_S = {"c4": 300.0, "c5": 480.0}
 
 
 def run_child(wl, args, world, rank, barrier):

@@ -301,6 +301,28 @@ ULB_API int ulb_spec_run(ulb_spec* s, int max_rounds, int* out_rounds);
 /* host_tokens int32 [n_seq][max_new], host_counts [n_seq];
  * stats: [0] rounds, [1] drafted tokens, [2] accepted drafts, [3] committed tokens. */
 ULB_API int ulb_spec_read(ulb_spec* s, int32_t* host_tokens, int32_t* host_counts, uint64_t stats[4]);
+/*
+ * Per-round speculation records of sequence `seq` since its last prefill, in round order:
+ * the device form of the reference's SpeculationResult / SpeculativeToken
+ * (src/inference/speculative_decoder.h:11-22), one record per round in which the sequence
+ * was still decoding.  Each record is ULB_SPEC_REC_WORDS(k) int32 words:
+ *   [ULB_SPEC_REC_N_ACCEPTED]  n, drafts accepted (0..k); the round committed n + 1 tokens
+ *   [ULB_SPEC_REC_TOKEN]       the correction (n < k) or bonus (n == k) token
+ *   [ULB_SPEC_REC_POSITION]    sequence position of the first committed token
+ *   [ULB_SPEC_REC_K]           k, the drafts proposed
+ *   [ULB_SPEC_REC_DRAFTS + i]  draft token i, i = 0..k-1 (accepted: i < n; rejected: i >= n)
+ *   [ULB_SPEC_REC_DRAFTS + k + j], j = 0..n: the float bits of the target's probability
+ *       (under the warp) of committed token j (greedy decoding: 1.0)
+ * *out_n = the number of records (up to max_new + 1); at most max_records are copied to
+ * host_records (NULL to ask for the count only).
+ */
+#define ULB_SPEC_REC_N_ACCEPTED 0
+#define ULB_SPEC_REC_TOKEN 1
+#define ULB_SPEC_REC_POSITION 2
+#define ULB_SPEC_REC_K 3
+#define ULB_SPEC_REC_DRAFTS 4
+#define ULB_SPEC_REC_WORDS(k) (ULB_SPEC_REC_DRAFTS + 2 * (k) + 1)
+ULB_API int ulb_spec_read_rounds(ulb_spec* s, int seq, int max_records, int32_t* host_records, int* out_n);
 ULB_API int ulb_spec_free(ulb_spec* s);
 /* Run one round outside any CUDA graph with events between its phases:
  * ms[0] draft steps, ms[1] verify forward, ms[2] accept.  Sequences already done are computed

@@ -63,7 +63,7 @@ def test_attention_descriptor_checked_before_any_host_arithmetic(fn):
 def test_surface_matches_reference():
     import vulkangguf as vg
     for cls in ("InferenceAPI", "GenerationConfig", "GenerationResult", "GenerationProgress", "ModelMetrics",
-                "QuantizationType"):
+                "QuantizationType", "SpeculationResult", "SpeculativeToken"):
         assert hasattr(vg, cls)
     ref_methods = ["load_model", "unload_model", "generate", "generate_default", "generate_streaming",
                    "generate_with_progress", "generate_batch", "enable_gpu", "is_gpu_enabled", "get_model_info",

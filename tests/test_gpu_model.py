@@ -349,3 +349,31 @@ def test_token_logits_api(tiny_target):
     om = orc.Model(tiny_target)
     want = orc.forward(om, orc.KV(om, 1, 70), toks, [0] * 70, list(range(70)), 70, logits_mode=1)[0]
     assert np.abs(got - want).max() / np.abs(want).max() < FWD_RTOL
+
+
+def test_speculation_results_records_every_round(tiny_target, tiny_draft):
+    """get_speculation_results: one SpeculationResult per round, whose committed tokens (accepted
+    drafts then the correction / bonus) concatenate to the generated stream after its first
+    token, with consecutive positions; greedy probabilities are 1, sampled ones in (0, 1]."""
+    prompt = _prompt(128, seed=1)
+    api = _api(tiny_target, tiny_draft, k=4)
+    for cfg in (_cfg(96), _cfg(96, 0.8, 40, 1.0, seed=3)):
+        got = api.generate_tokens(prompt.tolist(), cfg)
+        st = api.get_last_stats()
+        res = api.get_speculation_results(0)
+        assert len(res) == st["rounds"]
+        stream = [t for r in res for t in r.accepted_tokens]
+        assert stream[:len(got) - 1] == got[1:]
+        assert sum(r.num_accepted for r in res) == st["committed"]
+        assert sum(r.num_accepted - 1 for r in res) == st["accepted"]
+        pos = [t.position for r in res for t in r.tokens]
+        assert pos == list(range(len(prompt) + 1, len(prompt) + 1 + len(pos)))
+        for r in res:
+            assert len(r.accepted_tokens) == r.num_accepted and len(r.tokens) == r.num_accepted
+            assert len(r.rejected_tokens) == 4 - (r.num_accepted - 1)
+            assert abs(r.acceptance_rate - (r.num_accepted - 1) / 4) < 1e-6
+            probs = [t.probability for t in r.tokens]
+            if cfg.temperature == 0:
+                assert probs == [1.0] * len(probs)
+            else:
+                assert all(0.0 < p <= 1.0 for p in probs)

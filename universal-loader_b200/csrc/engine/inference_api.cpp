@@ -360,6 +360,15 @@ class InferenceAPI {
     return d;
   }
 
+  /* the last generation's rounds for sequence `seq`, as SpeculationResult records */
+  std::vector<ulbe::SpecRound> get_speculation_results(int seq) {
+    std::lock_guard<std::mutex> lk(mu_);
+    std::vector<ulbe::SpecRound> out;
+    if (!engine_) return out;
+    if (!engine_->speculation_rounds(seq, &out)) throw std::runtime_error(engine_->error());
+    return out;
+  }
+
   std::vector<float> get_token_logits(const std::vector<uint32_t>& tokens) {
     std::lock_guard<std::mutex> lk(mu_);
     std::vector<float> out;
@@ -604,6 +613,8 @@ PYBIND11_MODULE(vulkangguf, m) {
       .def("generate_tokens", &InferenceAPI::generate_tokens, py::arg("prompt_tokens"), py::arg("config"),
            "Generate from token ids; list[int] -> list[int] or list[list[int]] -> list[list[int]]")
       .def("get_last_stats", &InferenceAPI::get_last_stats, "Statistics of the last generation")
+      .def("get_speculation_results", &InferenceAPI::get_speculation_results, py::arg("seq") = 0,
+           "Per-round SpeculationResult records of sequence `seq` of the last generation")
       .def("profile_round", &InferenceAPI::profile_round,
            "Run one more round of the last generation's loop, timed by phase (draft / verify / accept)");
 
@@ -627,6 +638,20 @@ PYBIND11_MODULE(vulkangguf, m) {
       .def_readonly("model_size_bytes", &ModelMetrics::model_size_bytes, "Model size in bytes")
       .def_readonly("architecture", &ModelMetrics::architecture, "Model architecture");
 
+  py::class_<ulbe::SpecToken>(m, "SpeculativeToken")
+      .def(py::init<>())
+      .def_readwrite("token_id", &ulbe::SpecToken::token_id, "Token id")
+      .def_readwrite("probability", &ulbe::SpecToken::probability,
+                     "Target probability of the token under the sampling warp (1.0 when greedy)")
+      .def_readwrite("position", &ulbe::SpecToken::position, "Position in the sequence");
+  py::class_<ulbe::SpecRound>(m, "SpeculationResult")
+      .def(py::init<>())
+      .def_readwrite("accepted_tokens", &ulbe::SpecRound::accepted_tokens,
+                     "Tokens committed this round: accepted drafts, then the correction or bonus token")
+      .def_readwrite("rejected_tokens", &ulbe::SpecRound::rejected_tokens, "Drafts after the first rejection")
+      .def_readwrite("num_accepted", &ulbe::SpecRound::num_accepted, "Tokens committed (accepted drafts + 1)")
+      .def_readwrite("acceptance_rate", &ulbe::SpecRound::acceptance_rate, "Accepted drafts / drafts proposed")
+      .def_readwrite("tokens", &ulbe::SpecRound::tokens, "The committed tokens as SpeculativeToken records");
   py::class_<GenerationResult>(m, "GenerationResult")
       .def_readonly("tokens", &GenerationResult::tokens, "Generated token IDs")
       .def_readonly("text", &GenerationResult::text, "Decoded text")

@@ -211,6 +211,38 @@ bool Engine::profile_round(float ms[5]) {
   return true;
 }
 
+bool Engine::speculation_rounds(int seq, std::vector<SpecRound>* out) {
+  std::lock_guard<std::mutex> lk(mu_);
+  out->clear();
+  if (!spec_) return fail("no generation");
+  if (!spec_has_draft_) return true;
+  int n = 0;
+  if (ulb_spec_read_rounds(spec_, seq, 0, nullptr, &n) != ULB_OK) return fail(ulb_last_error());
+  const int k = spec_desc_.k, words = ULB_SPEC_REC_WORDS(k);
+  std::vector<int32_t> rec((size_t)n * words);
+  if (n && ulb_spec_read_rounds(spec_, seq, n, rec.data(), &n) != ULB_OK) return fail(ulb_last_error());
+  for (int r = 0; r < n; ++r) {
+    const int32_t* w = rec.data() + (size_t)r * words;
+    SpecRound sr;
+    const int na = w[ULB_SPEC_REC_N_ACCEPTED];
+    for (int i = 0; i < k; ++i) (i < na ? sr.accepted_tokens : sr.rejected_tokens).push_back((uint32_t)w[ULB_SPEC_REC_DRAFTS + i]);
+    sr.accepted_tokens.push_back((uint32_t)w[ULB_SPEC_REC_TOKEN]);
+    sr.num_accepted = (uint32_t)(na + 1);
+    sr.acceptance_rate = k > 0 ? (float)na / (float)k : 0.f;
+    for (int j = 0; j <= na; ++j) {
+      SpecToken t;
+      t.token_id = sr.accepted_tokens[j];
+      float pr;
+      std::memcpy(&pr, &w[ULB_SPEC_REC_DRAFTS + k + j], 4);
+      t.probability = pr;
+      t.position = (uint32_t)(w[ULB_SPEC_REC_POSITION] + j);
+      sr.tokens.push_back(t);
+    }
+    out->push_back(std::move(sr));
+  }
+  return true;
+}
+
 bool Engine::last_logits(const std::vector<int32_t>& tokens, std::vector<float>* out) {
   std::lock_guard<std::mutex> lk(mu_);
   if (!target_) return fail("no model loaded");

@@ -35,6 +35,21 @@ struct GenParams {
   bool use_graphs = true;
 };
 
+/* One round of the speculative loop for one sequence, as the reference's SpeculationResult
+   (src/inference/speculative_decoder.h:17-22) with its SpeculativeToken list (:11-15). */
+struct SpecToken {
+  uint32_t token_id = 0;
+  float probability = 0.f; /* the target's probability of the token under the warp (greedy: 1) */
+  uint32_t position = 0;
+};
+struct SpecRound {
+  std::vector<uint32_t> accepted_tokens; /* committed this round: accepted drafts, then the correction / bonus */
+  std::vector<uint32_t> rejected_tokens; /* drafts after the first rejection */
+  uint32_t num_accepted = 0;             /* tokens committed (accepted drafts + 1) */
+  float acceptance_rate = 0.f;           /* accepted drafts / drafts proposed */
+  std::vector<SpecToken> tokens;
+};
+
 struct GenStats {
   uint64_t rounds = 0, drafted = 0, accepted = 0, committed = 0, generated = 0;
   double prefill_ms = 0, decode_ms = 0, total_ms = 0;
@@ -65,6 +80,8 @@ class Engine {
   /* time one extra round of the last generation's loop by phase: draft, verify, accept (ms),
      then the summed time of its tensor-parallel all-reduces (ms) and their count */
   bool profile_round(float ms[5]);
+  /* per-round records of sequence `seq` of the last generation (empty for plain decoding) */
+  bool speculation_rounds(int seq, std::vector<SpecRound>* out);
 
   ulb_ctx* ctx() { return ctx_; }
 

@@ -378,6 +378,9 @@ struct SpecCommit {
   uint32_t* round;   /* [B] per-sequence round counter, incremented here     */
   unsigned long long* stats; /* [4] (unused), drafted, accepted, committed  */
   int32_t* active;   /* [B] rounds in which the sequence was still decoding   */
+  /* per-round records [B][log_rounds][log_stride] (ULB_SPEC_REC_* layout of ulb.h), or NULL */
+  int32_t* log;
+  int log_rounds, log_stride;
 };
 
 /* one CTA per sequence */
@@ -395,10 +398,18 @@ __global__ void __launch_bounds__(DT) decide_kernel(const float* __restrict__ p,
   const uint32_t rnd = dev_round ? dev_round[b] : round;
   const int np = B * (k + 1);
   int n = 0, tok = -1;
+  /* target probability (under the warp) of each committed token, for the round record (which
+     the loop keeps for k <= kMaxLoggedK; ulb_spec_accept may pass a larger k and logs nothing) */
+  constexpr int kMaxLoggedK = 16;
+  float pcommit[kMaxLoggedK + 1];
+  auto note_p = [&](int j, float v) {
+    if (j <= kMaxLoggedK) pcommit[j] = v;
+  };
   for (int i = 0; i < k; ++i) {
     const int x = draft[b * k + i];
     const RowStats sp = rs[b * (k + 1) + i];
     if (greedy) {
+      note_p(n, 1.0f);
       if (x == sp.amax) { ++n; continue; }
       tok = sp.amax;
       break;
@@ -410,6 +421,7 @@ __global__ void __launch_bounds__(DT) decide_kernel(const float* __restrict__ p,
     const double px = in_vocab ? warped_e(pl, x, iT, sp) / sp.Z : 0.0;
     const double qx = in_vocab ? warped_e(ql, x, iT, sq) / sq.Z : 0.0;
     const float u = rng_u(seed, rnd, (uint32_t)b, (uint32_t)i, ULB_RNG_ACCEPT);
+    note_p(n, (float)px);
     if ((double)u * qx < px) { ++n; continue; }
     /* residual norm(max(0, p - q)), as max(0, e_p Z_q - e_q Z_p) = Z_p Z_q max(0, p - q) */
     auto resid = [&](int v) {
@@ -420,15 +432,19 @@ __global__ void __launch_bounds__(DT) decide_kernel(const float* __restrict__ p,
     double R = 0.0;
     tok = block_inv_cdf(V, u2, resid, s, &R);
     if (!(R > 0.0)) tok = block_inv_cdf(V, u2, [&](int v) { return warped_e(pl, v, iT, sp); }, s, nullptr);
+    note_p(n, (float)(warped_e(pl, tok, iT, sp) / sp.Z));
     break;
   }
   if (tok < 0) {
     const RowStats sp = rs[b * (k + 1) + k];
-    if (greedy) tok = sp.amax;
-    else {
+    if (greedy) {
+      tok = sp.amax;
+      note_p(n, 1.0f);
+    } else {
       const float* pl = p + ((size_t)b * (k + 1) + k) * V;
       const float u2 = rng_u(seed, rnd, (uint32_t)b, (uint32_t)k, ULB_RNG_RESID);
       tok = block_inv_cdf(V, u2, [&](int v) { return warped_e(pl, v, iT, sp); }, s, nullptr);
+      note_p(n, (float)(warped_e(pl, tok, iT, sp) / sp.Z));
     }
   }
   if (threadIdx.x != 0) return;
@@ -449,7 +465,17 @@ __global__ void __launch_bounds__(DT) decide_kernel(const float* __restrict__ p,
       atomicAdd(&cm.stats[1], (unsigned long long)k);
       atomicAdd(&cm.stats[2], (unsigned long long)n);
       atomicAdd(&cm.stats[3], (unsigned long long)(n + 1));
-      cm.active[b] += 1;
+      const int a = cm.active[b];
+      if (cm.log && a < cm.log_rounds && k <= kMaxLoggedK) {
+        int32_t* r = cm.log + ((size_t)b * cm.log_rounds + a) * cm.log_stride;
+        r[ULB_SPEC_REC_N_ACCEPTED] = n;
+        r[ULB_SPEC_REC_TOKEN] = tok;
+        r[ULB_SPEC_REC_POSITION] = L;
+        r[ULB_SPEC_REC_K] = k;
+        for (int i = 0; i < k; ++i) r[ULB_SPEC_REC_DRAFTS + i] = draft[b * k + i];
+        for (int i = 0; i <= n; ++i) r[ULB_SPEC_REC_DRAFTS + k + i] = __float_as_int(pcommit[i]);
+      }
+      cm.active[b] = a + 1;
     }
     cm.round[b] = rnd + 1;
   }
@@ -491,10 +517,11 @@ int launch_sample_seq(Ctx* c, const float* logits, int rows, int V, int ld, cons
 int launch_accept_commit(Ctx* c, const float* p, const float* q, const int32_t* draft, int B, int k, int V,
                          const ulb_warp* w, uint64_t seed, const uint32_t* dev_round, void* stats_scratch,
                          int32_t* hist, int hist_len, int32_t* L, int32_t* done, const int32_t* plen, int max_new,
-                         uint32_t* round, unsigned long long* stats, int32_t* active) {
+                         uint32_t* round, unsigned long long* stats, int32_t* active, int32_t* log, int log_rounds) {
   SpecCommit cm;
   cm.hist = hist; cm.hist_len = hist_len; cm.L = L; cm.done = done; cm.prompt_len = plen;
   cm.max_new = max_new; cm.round = round; cm.stats = stats; cm.active = active;
+  cm.log = log; cm.log_rounds = log_rounds; cm.log_stride = ULB_SPEC_REC_WORDS(k);
   return launch_accept_impl(c, p, q, draft, B, k, V, w, seed, dev_round, 0, nullptr, nullptr, stats_scratch, &cm);
 }
 

@@ -36,7 +36,8 @@ int launch_sample_seq(Ctx* c, const float* logits, int rows, int V, int ld, cons
 int launch_accept_commit(Ctx* c, const float* p, const float* q, const int32_t* draft, int B, int k, int V,
                          const ulb_warp* w, uint64_t seed, const uint32_t* dev_round, void* stats_scratch,
                          int32_t* hist, int hist_len, int32_t* L, int32_t* done, const int32_t* plen, int max_new,
-                         uint32_t* round, unsigned long long* stats, int32_t* active_rounds);
+                         uint32_t* round, unsigned long long* stats, int32_t* active_rounds, int32_t* log,
+                         int log_rounds);
 }  // namespace ulb
 
 extern "C" int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* m, int n_seq, int cap, ulb_kv** out);
@@ -113,6 +114,8 @@ struct Spec {
   /* device */
   int32_t *hist = nullptr, *L = nullptr, *done = nullptr, *plen = nullptr, *draft = nullptr;
   int32_t *rtok = nullptr, *rseq = nullptr, *rpos = nullptr, *err = nullptr, *active = nullptr;
+  int32_t* log = nullptr; /* per-round records [S][log_rounds][ULB_SPEC_REC_WORDS(k)] */
+  int log_rounds = 0;
   uint32_t* round = nullptr;
   unsigned long long* stats = nullptr;
   float *plog = nullptr, *qlog = nullptr;
@@ -162,7 +165,11 @@ static int record_round_impl(Spec* sp, void* ev_draft_done, void* ev_verify_done
   if (ev_verify_done) ULB_CUDA(cudaEventRecord((cudaEvent_t)ev_verify_done, c->stream));
   return launch_accept_commit(c, sp->plog, sp->qlog, sp->draft, S, k, V, &sp->d.warp, sp->d.seed, sp->round, sp->rs,
                               sp->hist, sp->hl, sp->L, sp->done, sp->plen, sp->d.max_new, sp->round, sp->stats,
-                              sp->active);
+                              sp->active, sp->log, sp->log_rounds);
+}
+
+static size_t log_bytes(const Spec* sp) {
+  return (size_t)sp->S * sp->log_rounds * ULB_SPEC_REC_WORDS(sp->k) * 4;
 }
 
 static void spec_release(Spec* sp) {
@@ -175,6 +182,7 @@ static void spec_release(Spec* sp) {
   dev_free(c, sp->err, 4); dev_free(c, sp->active, sp->S * 4);
   dev_free(c, sp->round, sp->S * 4); dev_free(c, sp->stats, 4 * 8);
   dev_free(c, sp->plog, sp->plog_bytes); dev_free(c, sp->qlog, sp->qlog_bytes); dev_free(c, sp->rs, sp->rs_bytes);
+  dev_free(c, sp->log, log_bytes(sp));
   if (sp->h_L) cudaFreeHost(sp->h_L);
   if (sp->h_done) cudaFreeHost(sp->h_done);
   ulb_kv_free(sp->kvt);
@@ -247,6 +255,10 @@ int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft, const ulb
   ALLOC(sp->qlog, sp->qlog_bytes);
   sp->rs_bytes = accept_scratch_bytes(S, k, V);
   ALLOC(sp->rs, sp->rs_bytes);
+  /* every round commits at least one token, so max_new rounds (+1 for a profiled round) hold
+     a whole generation */
+  sp->log_rounds = d->max_new + 1;
+  ALLOC(sp->log, log_bytes(sp));
 #undef ALLOC
   if (cudaMallocHost((void**)&sp->h_L, S * 4) != cudaSuccess || cudaMallocHost((void**)&sp->h_done, S * 4) != cudaSuccess)
     return fail(set_error(ULB_ENOMEM, "pinned host allocation failed"));
@@ -387,6 +399,27 @@ int ulb_spec_read(ulb_spec* h, int32_t* tokens, int32_t* counts, uint64_t stats[
     stats[2] = st[2];
     stats[3] = st[3];
   }
+  return ULB_OK;
+}
+
+int ulb_spec_read_rounds(ulb_spec* h, int seq, int max_records, int32_t* out, int* out_n) {
+  ULB_CHECK(h && out_n, ULB_EINVAL, "ulb_spec_read_rounds: NULL argument");
+  Spec* sp = &h->s;
+  ULB_CHECK(sp->prefilled, ULB_EINVAL, "ulb_spec_read_rounds: nothing generated");
+  ULB_CHECK(seq >= 0 && seq < sp->S, ULB_EINVAL, "ulb_spec_read_rounds: sequence %d of %d", seq, sp->S);
+  Ctx* c = sp->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  int32_t act = 0;
+  ULB_CUDA(cudaMemcpyAsync(&act, sp->active + seq, 4, cudaMemcpyDeviceToHost, c->stream));
+  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  const int n = std::min(act, sp->log_rounds);
+  *out_n = n;
+  if (!out || max_records <= 0 || n == 0) return ULB_OK;
+  const size_t words = (size_t)ULB_SPEC_REC_WORDS(sp->k);
+  const size_t take = (size_t)std::min(n, max_records) * words;
+  ULB_CUDA(cudaMemcpyAsync(out, sp->log + (size_t)seq * sp->log_rounds * words, take * 4, cudaMemcpyDeviceToHost,
+                           c->stream));
+  ULB_CUDA(cudaStreamSynchronize(c->stream));
   return ULB_OK;
 }
 

@@ -92,6 +92,7 @@ _SIGS = {
     "ulb_spec_free": (C.c_int, [P]),
     "ulb_spec_profile_round": (C.c_int, [P, C.POINTER(C.c_float)]),
     "ulb_spec_profile_round_ex": (C.c_int, [P, C.POINTER(C.c_float)]),
+    "ulb_spec_read_rounds": (C.c_int, [P, C.c_int, C.c_int, P, C.POINTER(C.c_int)]),
     "ulb_spec_launch_count": (C.c_int, [P, C.POINTER(C.c_uint64)]),
 }
 
