@@ -566,6 +566,24 @@ def run_ours(args):
     return 0
 
 
+def run_pgtest(args):
+    """Process-group plumbing of the child workloads without a GPU (for tests on the CPU):
+    parent ranks spawn one child each, the children form their own gloo group, all-reduce
+    their ranks and rank 0's child prints a JSON line the parent folds into its own."""
+    world, rank, local, barrier, allmax, allsum, done = dist_setup()
+    if args.child:
+        total = allsum(rank)
+        if rank == 0:
+            print(json.dumps({"world": world, "rank_sum": total}), flush=True)
+        done()
+        return 0
+    obj = run_child("pgtest", args, world, rank, barrier)
+    if rank == 0:
+        print(json.dumps({"pgtest": obj}), flush=True)
+    done()
+    return 0
+
+
 def extras_for(args, world):
     if args.child or args.extras == "none":
         return []
@@ -576,7 +594,7 @@ def extras_for(args, world):
 
 # wall-clock budget of one bench run (the sharded workloads get what the headline leaves)
 BENCH_BUDGET_S = float(os.environ.get("ULB_BENCH_BUDGET_S", "840"))
-CHILD_CAP_S = {"c4": 300.0, "c5": 480.0}
+CHILD_CAP_S = {"c4": 300.0, "c5": 480.0, "pgtest": 120.0}
 
 
 def run_child(wl, args, world, rank, barrier):
@@ -589,13 +607,15 @@ def run_child(wl, args, world, rank, barrier):
     if timeout < 60:
         obj = {"skipped": "%.0f s of the bench's %.0f s budget left" % (max(left, 0), BENCH_BUDGET_S)}
     else:
-        env = dict(os.environ)
+        # the children form a process group of their own: without torchrun's agent store (with
+        # TORCHELASTIC_USE_AGENT_STORE set, rank 0 would connect to a store nobody serves)
+        env = {k: v for k, v in os.environ.items() if not k.startswith("TORCHELASTIC")}
         if ORIG_CUDA_VISIBLE is None:
             env.pop("CUDA_VISIBLE_DEVICES", None)
         else:
             env["CUDA_VISIBLE_DEVICES"] = ORIG_CUDA_VISIBLE
         if world > 1:
-            env["MASTER_PORT"] = str(int(os.environ.get("MASTER_PORT", "29500")) + (11 if wl == "c4" else 13))
+            env["MASTER_PORT"] = str(int(os.environ.get("MASTER_PORT", "29500")) + {"c4": 11, "c5": 13}.get(wl, 17))
         if wl == "c5":
             env.setdefault("NCCL_DEBUG", "INFO")
             env.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
@@ -951,7 +971,7 @@ def main():
     ap.add_argument("--mode", default="spec", choices=["spec", "ops"],
                     help="spec: the C2 speculative workload (default); ops: the config-3 kernel sweep")
     ap.add_argument("--only", default="", help="ops mode: run one case, e.g. q4_0:11008x4096:m5 or accept")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"],
+    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5", "pgtest"],
                     help="c2: 7B + TinyLlama, B=1 (default, the headline); c4: Llama-3-8B + 3.2-1B, 64 sequences "
                          "sharded data-parallel over the GPUs; c5: 70B target tensor-parallel over the GPUs + "
                          "replicated 7B draft, batch 8")
@@ -965,6 +985,8 @@ def main():
         return run_reference(args)
     if args.mode == "ops":
         return run_ops(args)
+    if args.workload == "pgtest":
+        return run_pgtest(args)
     if args.workload == "c4":
         return run_c4(args)
     if args.workload == "c5":

@@ -64,3 +64,17 @@ def test_c4_sequences_shard_over_two_gloo_ranks():
         assert o["first"] == [prompts[i][:4] for i in o["idx"][:2]]     # same prompts on every rank
         assert o["sum_tokens"] == sum(len(p) for p in prompts)           # host sum over ranks
         assert o["max_rank"] == 1 and o["n_seq"] == 64                   # host max / sum
+
+
+def test_child_workload_groups_under_torchrun():
+    """bench.py runs the sharded workloads (c4, c5) as child process groups of its own ranks.
+    Under torchrun the children must form their own gloo group (not torchrun's agent store) on
+    a port of their own, and rank 0's child line must come back to the parent: checked with the
+    GPU-free pgtest workload on two ranks."""
+    port = _free_port()
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port), os.path.join(ROOT, "bench.py"),
+                        "--workload", "pgtest", "--gpus", "2"], capture_output=True, text=True, timeout=240)
+    assert r.returncode == 0, r.stderr[-3000:]
+    line = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1])
+    assert line["pgtest"]["world"] == 2 and line["pgtest"]["rank_sum"] == 1.0
