@@ -939,14 +939,20 @@ def run_ops(args):
                           "note": "K/V of one sequence (%.1f MB) fit in L2: a latency figure" % (2 * L * Hkv * hd * 2 / 1e6)}
         for b in bufs + [out]:
             b.free()
-    if not args.only or args.only.startswith("accept"):
-        B, k, V = 64, 8, 32000
+    # rejection sampling: config 3's [64, 9 | 8, 32000] at T = 1 and T = 0, and config 4's vocabulary
+    # (128256) at T = 0.8, top_p = 0.9; draft sampling of 64 rows at config 4's warp
+    for (label, V, warps) in (("accept", 32000, ((1.0, 0, 1.0), (0.0, 0, 1.0))),
+                              ("accept_c4", 128256, ((0.8, 0, 0.9),))):
+        if args.only and not label.startswith(args.only) and not args.only.startswith(label):
+            continue
+        B, k = 64, 8
         pl = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
         ql = (rng.standard_normal((B, k, V)) * 3).astype(np.float32)
         draft = rng.integers(0, V, (B, k)).astype(np.int32)
         bp, bq, bd = ctx.buffer(pl), ctx.buffer(ql), ctx.buffer(draft)
         ot, on = ctx.buffer(nbytes=B * (k + 1) * 4), ctx.buffer(nbytes=B * 4)
-        for warp in ((1.0, 0, 1.0), (0.0, 0, 1.0)):
+        st = ctx.buffer(nbytes=B * 4)
+        for warp in warps:
             w = U.Warp(*warp)
             for _ in range(max(1, args.warmup)):
                 U.check(U.lib().ulb_spec_accept(ctx.h, bp.ptr, bq.ptr, bd.ptr, B, k, V, C.byref(w), 1, 0, ot.ptr, on.ptr))
@@ -956,7 +962,19 @@ def run_ops(args):
             ms = ctx.time_graph(g, max(args.steps, 3)) / 4
             U.lib().ulb_graph_free(g)
             alg = pl.nbytes + ql.nbytes
-            results["accept:T%g" % warp[0]] = {"us": ms * 1e3, "gbs": alg / ms / 1e6, "hbm_frac": alg / ms / 1e6 / peak}
+            name = "%s:T%g%s" % (label, warp[0], ":top_p%g" % warp[2] if warp[2] < 1 else "")
+            results[name] = {"us": ms * 1e3, "gbs": alg / ms / 1e6, "hbm_frac": alg / ms / 1e6 / peak}
+            if warp[0] > 0:  # draft-token sampling of one step: B rows
+                call = lambda: U.check(U.lib().ulb_sample(ctx.h, bq.ptr, B, V, k * V, C.byref(w), 1, 0, 0, 1, st.ptr))
+                call()
+                ctx.sync()
+                g = ctx.capture(lambda: [call() for _ in range(4)])
+                ms = ctx.time_graph(g, max(args.steps, 3)) / 4
+                U.lib().ulb_graph_free(g)
+                results[name.replace("accept", "sample")] = {"us": ms * 1e3, "rows": B,
+                                                             "gbs": B * V * 4 / ms / 1e6}
+        for b in (bp, bq, bd, ot, on, st):
+            b.free()
     ctx.close()
     print(json.dumps({"mode": "ops", "peak_gbs": peak, "peak_source": peak_src, "results": results}), flush=True)
     return 0

@@ -737,9 +737,18 @@ float orc_warp_exp(float x) {
   return p * two_k;
 }
 
+/* top-p masses in 40-bit fixed point, added as integers (order-independent): floor(e * 2^40) */
+static uint64_t orc_mass_fix(float e) { return (uint64_t)((double)e * 1099511627776.0); }
+/* the mass the kept set reaches first: floor(top_p * total), at least 1 */
+static uint64_t orc_topp_target(float top_p, uint64_t total) {
+  uint64_t r = (uint64_t)((double)top_p * (double)total);
+  return r < 1 ? 1 : r;
+}
+
 /*
  * Warp weights.  z = logits * (1/T), 1/T rounded once; top-k keeps z >= k-th largest z; e = orc_warp_exp(z - max)
- * as fp64; top-p keeps v iff (sum of e over z_u > z_v) < top_p * Z; *Zout = sum of kept e.
+ * as fp64; top-p keeps v iff (mass of z_u > z_v) < R, masses in fixed point (E = orc_mass_fix(e), summed as
+ * integers) and R = orc_topp_target(top_p, sum of E over the top-k set); *Zout = sum of kept e (fp64).
  * Greedy (T <= 0): one-hot at the argmax, Z = 1.
  */
 int orc_warp_weights(const float* logits, int V, const orc_warp* w, double* e, double* Zout) {
@@ -769,13 +778,19 @@ int orc_warp_weights(const float* logits, int V, const orc_warp* w, double* e, d
   if (w->top_p > 0.0f && w->top_p < 1.0f) {
     zi_t* s = (zi_t*)malloc((size_t)V * sizeof(zi_t));
     int n = 0;
-    for (int i = 0; i < V; ++i) if (e[i] > 0.0) { s[n].z = z[i]; s[n].i = i; ++n; }
+    uint64_t tot = 0;
+    for (int i = 0; i < V; ++i)
+      if (e[i] > 0.0) {
+        s[n].z = z[i]; s[n].i = i; ++n;
+        tot += orc_mass_fix((float)e[i]);
+      }
     qsort(s, n, sizeof(zi_t), cmp_zi_desc);
-    double P = (double)w->top_p * Z, cum = 0.0;
+    const uint64_t R = orc_topp_target(w->top_p, tot);
+    uint64_t cum = 0;
     float thr_p = s[0].z;
     for (int j = 0; j < n; ++j) {
-      cum += e[s[j].i];
-      if (cum >= P) { thr_p = s[j].z; break; }
+      cum += orc_mass_fix((float)e[s[j].i]);
+      if (cum >= R) { thr_p = s[j].z; break; }
       thr_p = s[j].z;
     }
     free(s);

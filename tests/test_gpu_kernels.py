@@ -249,6 +249,28 @@ def test_sample_top_p_large_vocab(ctx):
     assert got.tolist() == want
 
 
+@pytest.mark.parametrize("kind", ["flat", "ties", "narrow_large_vocab", "one_hot"])
+@pytest.mark.parametrize("warp", [(0.8, 40, 1.0), (0.8, 0, 0.9), (1.0, 1000, 0.5)])
+def test_sample_cut_selection_paths(ctx, kind, warp):
+    """The top-k / top-p cut on rows that stress its selection: all logits equal (one bin holds
+    the whole row: the whole-row fallback), logits on a coarse grid (many exact ties), a narrow
+    128256-wide row (the cut bin overflows the candidate buffer) and a single dominant logit."""
+    rng = np.random.default_rng(21)
+    rows = 4
+    if kind == "flat":
+        logits = np.zeros((rows, 32000), np.float32)
+    elif kind == "ties":
+        logits = (np.round(rng.standard_normal((rows, 32000)) * 4) / 4).astype(np.float32)
+    elif kind == "narrow_large_vocab":
+        logits = (rng.standard_normal((rows, 128256)) * 0.4).astype(np.float32)
+    else:
+        logits = (rng.standard_normal((rows, 32000)) * 0.1).astype(np.float32)
+        logits[:, 17] = 30.0
+    got = _sample_gpu(ctx, logits, warp, seed=31, rnd=2, slot=0, tag=1)
+    want = [orc.sample(logits[r], orc.uniform(31, 2, r, 0, 1), *warp) for r in range(rows)]
+    assert got.tolist() == want
+
+
 def _accept_gpu(ctx, pl, ql, draft, warp, seed, rnd):
     import ulb_capi as U
     B, k = draft.shape

@@ -10,11 +10,20 @@
  *
  * Warp definition (identical in the CPU oracle): z = logit * iT with iT = 1/T rounded once;
  * top-k keeps z >= the k-th largest z; e = ulb_warp_exp(z - max z) (binary32, bit-identical
- * on host and device), summed in fp64; top-p keeps tokens whose strictly-more-probable mass
- * is < top_p * sum(e); p = e / sum over the kept set.  Sampling is an inverse CDF over e in
- * index order.  Keep sets are decided on exact comparisons of z (radix select on the
- * order-preserving integer key of z), so the same logits give the same kept set on host and
- * device.
+ * on host and device); top-p keeps tokens whose strictly-more-probable mass is below
+ * R = floor(top_p * total mass), masses in 40-bit fixed point added as integers
+ * (ulb_mass_fix), so the cut does not depend on the order of the additions; p = e / Z over
+ * the kept set, Z summed in fp64.  Sampling is an inverse CDF over e in index order.  Keep
+ * sets are decided on exact comparisons of z (the order-preserving integer key of z), so the
+ * same logits give the same kept set on host and device.
+ *
+ * Selection of the top-k / top-p cut (B200): one pass over the row histograms it into 1024
+ * bins of max z - z (width 1/32) with integer atomics, which spread over many bins (no
+ * contended fp64 atomics); the bin holding the cut is found by a block scan, a second pass
+ * compacts that bin's elements into shared memory, and a radix select over the compacted
+ * candidates finds the exact key.  Only a bin too large for the candidate buffer (a very flat
+ * row) falls back to a radix select over the whole row.  The row is read from HBM once (the
+ * argmax pass); the later passes find it in L2 (the stats grid keeps few rows in flight).
  *
  * Kernels: row_stats (one CTA per row: max, keep threshold, normaliser, argmax) over all
  * target and draft rows of a round in parallel; sample (stats + inverse CDF for the draft
@@ -85,12 +94,26 @@ struct SmemRed {
   float f[BT / 32];
   int i[BT / 32];
   double d[BT / 32];
-  unsigned int hist_u[256];
-  double hist_d[256];
+  unsigned long long u[BT / 32];
+  unsigned long long hist_w[256]; /* radix-select weights (counts or fixed-point masses) */
   double seg[BT];
   uint32_t prefix;
   int found;
   double above;
+  unsigned long long above_w;
+};
+
+/* top-k / top-p cut selection: histogram of max z - z, and the compacted cut bin */
+constexpr int kSelBins = 1024;     /* bins of max z - z, width 1 / kSelBinScale */
+constexpr float kSelBinScale = 32.f;
+constexpr int kSelCap = 2048;      /* candidates of the cut bin held in shared memory */
+struct SelSmem {
+  unsigned long long bw[kSelBins]; /* weight per bin */
+  uint32_t ck[kSelCap];            /* candidate keys */
+  unsigned long long cw[kSelCap];  /* candidate weights */
+  int n;                           /* candidates found (may exceed kSelCap) */
+  int bin;                         /* the cut bin */
+  unsigned long long before;       /* weight of the bins before it */
 };
 
 template <int BT>
@@ -143,83 +166,149 @@ __device__ int block_argmax(const float* l, int V, SmemRed<BT>& s) {
   return bi == 0x7fffffff ? 0 : bi;
 }
 
-/* key of the k-th largest z (count based radix select, exact) */
+/* deterministic sum of unsigned 64-bit integers over the block */
 template <int BT>
-__device__ uint32_t kth_largest_key(const float* l, int V, float iT, int k, SmemRed<BT>& s) {
-  uint32_t prefix = 0, mask = 0;
-  int need = k; /* rank within the current prefix class (1-based) */
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = threadIdx.x; b < 256; b += BT) s.hist_u[b] = 0;
-    __syncthreads();
-    row_for_each<BT>(l, V, [&](int, float x) {
-      const uint32_t key = fkey(zof(x, iT));
-      if ((key & mask) == prefix) atomicAdd(&s.hist_u[(key >> shift) & 255u], 1u);
-    });
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int cum = 0, b = 255;
-      for (; b > 0; --b) {
-        if (cum + (int)s.hist_u[b] >= need) break;
-        cum += s.hist_u[b];
-      }
-      s.prefix = prefix | ((uint32_t)b << shift);
-      s.found = need - cum;
-    }
-    __syncthreads();
-    prefix = s.prefix;
-    need = s.found;
-    mask |= 255u << shift;
-    __syncthreads();
-  }
-  return prefix;
+__device__ unsigned long long block_sum_u64(unsigned long long v, SmemRed<BT>& s) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) s.u[threadIdx.x >> 5] = v;
+  __syncthreads();
+  unsigned long long r = 0;
+#pragma unroll
+  for (int w = 0; w < BT / 32; ++w) r += s.u[w];
+  return r;
 }
 
 /*
- * key of the smallest z kept by top-p: the first element in descending z order whose
- * inclusive cumulative mass reaches P (mass histograms in fp64).
+ * Radix select over (key, weight) pairs, 8 bits a level: the key t with weight(keys > t) < R
+ * <= weight(keys >= t), for 1 <= R <= the total weight.  visit(f) calls f(key, weight) for
+ * every pair (the whole block calls it; each thread its share).  Weights add as integers.
  */
-template <int BT>
-__device__ uint32_t topp_key(const float* l, int V, float iT, float mx, uint32_t key_lo, double P, SmemRed<BT>& s) {
+template <int BT, class Visit>
+__device__ uint32_t radix_select(Visit visit, unsigned long long R, SmemRed<BT>& s) {
   uint32_t prefix = 0, mask = 0;
-  double above = 0.0;
+  unsigned long long above = 0;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = threadIdx.x; b < 256; b += BT) s.hist_d[b] = 0.0;
+    for (int b = threadIdx.x; b < 256; b += BT) s.hist_w[b] = 0ull;
     __syncthreads();
-    row_for_each<BT>(l, V, [&](int, float x) {
-      const float z = zof(x, iT);
-      const uint32_t key = fkey(z);
-      if (key >= key_lo && (key & mask) == prefix)
-        atomicAdd(&s.hist_d[(key >> shift) & 255u], (double)ulb_warp_exp(__fsub_rn(z, mx)));
+    visit([&](uint32_t key, unsigned long long w) {
+      if ((key & mask) == prefix) atomicAdd(&s.hist_w[(key >> shift) & 255u], w);
     });
     __syncthreads();
     if (threadIdx.x == 0) {
-      int b = 255, last_nonempty = -1;
-      double a = above;
-      for (; b >= 0; --b) {
-        if (s.hist_d[b] > 0.0) {
-          last_nonempty = b;
-          if (a + s.hist_d[b] >= P) break;
-          a += s.hist_d[b];
-        }
-      }
-      if (b < 0) { /* rounding left P just above the total: keep everything down to the last bin */
-        b = last_nonempty < 0 ? 0 : last_nonempty;
-        a = a - s.hist_d[b];
+      unsigned long long a = above;
+      int b = 255;
+      for (; b > 0; --b) {
+        if (a + s.hist_w[b] >= R) break;
+        a += s.hist_w[b];
       }
       s.prefix = prefix | ((uint32_t)b << shift);
-      s.above = a;
+      s.above_w = a;
     }
     __syncthreads();
     prefix = s.prefix;
-    above = s.above;
+    above = s.above_w;
     mask |= 255u << shift;
     __syncthreads();
   }
   return prefix;
 }
 
+/* bin of z: floor((max z - z) * 32), clamped to the last bin (-inf and NaN land there) */
+__device__ __forceinline__ int sel_bin(float mx, float z) {
+  const float d = __fmul_rn(__fsub_rn(mx, z), kSelBinScale);
+  return d < (float)(kSelBins - 1) ? (int)d : kSelBins - 1;
+}
+
+/*
+ * The cut key: with weights w(key) (MASS: ulb_mass_fix of the warp weight; else 1) over the
+ * elements whose key >= key_lo, the key t whose descending cumulative weight first reaches R,
+ * where R = k (count) or ulb_topp_target(top_p, total mass) (MASS).
+ */
+template <int BT, bool MASS>
+__device__ uint32_t select_cut(const float* l, int V, float iT, float mx, uint32_t key_lo, int k, float top_p,
+                               SmemRed<BT>& s, SelSmem& sel) {
+  auto weight = [&](float z) -> unsigned long long {
+    return MASS ? (unsigned long long)ulb_mass_fix(ulb_warp_exp(__fsub_rn(z, mx))) : 1ull;
+  };
+  for (int b = threadIdx.x; b < kSelBins; b += BT) sel.bw[b] = 0ull;
+  if (threadIdx.x == 0) sel.n = 0;
+  __syncthreads();
+  unsigned long long tot = 0;
+  row_for_each<BT>(l, V, [&](int, float x) {
+    const float z = zof(x, iT);
+    if (fkey(z) >= key_lo) {
+      const unsigned long long w = weight(z);
+      tot += w;
+      atomicAdd(&sel.bw[sel_bin(mx, z)], w);
+    }
+  });
+  tot = block_sum_u64(tot, s);
+  const unsigned long long R = MASS ? (unsigned long long)ulb_topp_target(top_p, tot) : (unsigned long long)k;
+  /* the cut bin: block scan of the bins' weights (each thread a contiguous group of bins) */
+  constexpr int PER = kSelBins / BT > 0 ? kSelBins / BT : 1;
+  const int b0 = threadIdx.x * PER;
+  unsigned long long mine = 0;
+  for (int j = 0; j < PER; ++j)
+    if (b0 + j < kSelBins) mine += sel.bw[b0 + j];
+  unsigned long long inc = mine;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) s.u[warp] = inc;
+  if (threadIdx.x == 0) s.found = kSelBins;
+  __syncthreads();
+  unsigned long long cum = inc - mine;
+  for (int w = 0; w < warp; ++w) cum += s.u[w];
+  if (b0 < kSelBins && cum < R && cum + mine >= R) { /* exactly one thread holds the crossing */
+    for (int j = 0; j < PER; ++j) {
+      if (cum + sel.bw[b0 + j] >= R) {
+        sel.bin = b0 + j;
+        sel.before = cum;
+        break;
+      }
+      cum += sel.bw[b0 + j];
+    }
+  }
+  __syncthreads();
+  const int cut = sel.bin;
+  const unsigned long long before = sel.before;
+  /* the cut bin's elements into shared memory */
+  row_for_each<BT>(l, V, [&](int, float x) {
+    const float z = zof(x, iT);
+    const uint32_t key = fkey(z);
+    if (key >= key_lo && sel_bin(mx, z) == cut) {
+      const int slot = atomicAdd(&sel.n, 1);
+      if (slot < kSelCap) {
+        sel.ck[slot] = key;
+        sel.cw[slot] = weight(z);
+      }
+    }
+  });
+  __syncthreads();
+  const int n = sel.n;
+  if (n <= kSelCap) {
+    return radix_select<BT>([&](auto f) {
+      for (int j = threadIdx.x; j < n; j += BT) f(sel.ck[j], sel.cw[j]);
+    }, R - before, s);
+  }
+  /* a very flat row: the cut bin does not fit, select over the whole row */
+  return radix_select<BT>([&](auto f) {
+    row_for_each<BT>(l, V, [&](int, float x) {
+      const float z = zof(x, iT);
+      const uint32_t key = fkey(z);
+      if (key >= key_lo) f(key, weight(z));
+    });
+  }, R, s);
+}
+
 template <int BT>
-__device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowStats& out, SmemRed<BT>& s) {
+__device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowStats& out, SmemRed<BT>& s,
+                                  SelSmem& sel) {
   const int amax = block_argmax(l, V, s);
   if (!(w.temperature > 0.f)) {
     if (threadIdx.x == 0) { out.mx = l[amax]; out.thr = -INFINITY; out.Z = 1.0; out.amax = amax; }
@@ -228,16 +317,8 @@ __device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowS
   const float iT = __fdiv_rn(1.0f, w.temperature); /* inverse temperature */
   const float mx = zof(l[amax], iT); /* scaling by 1/T > 0 is monotone: max z = z of the max logit */
   uint32_t key_lo = 0;
-  if (w.top_k > 0 && w.top_k < V) key_lo = kth_largest_key(l, V, iT, w.top_k, s);
-  if (w.top_p > 0.f && w.top_p < 1.f) {
-    double zs = 0.0;
-    row_for_each<BT>(l, V, [&](int, float x) {
-      const float z = zof(x, iT);
-      if (fkey(z) >= key_lo) zs += (double)ulb_warp_exp(__fsub_rn(z, mx));
-    });
-    const double Z0 = block_sum_d(zs, s);
-    key_lo = topp_key(l, V, iT, mx, key_lo, (double)w.top_p * Z0, s);
-  }
+  if (w.top_k > 0 && w.top_k < V) key_lo = select_cut<BT, false>(l, V, iT, mx, 0u, w.top_k, 0.f, s, sel);
+  if (w.top_p > 0.f && w.top_p < 1.f) key_lo = select_cut<BT, true>(l, V, iT, mx, key_lo, 0, w.top_p, s, sel);
   double zs = 0.0;
   row_for_each<BT>(l, V, [&](int, float x) {
     const float z = zof(x, iT);
@@ -328,12 +409,13 @@ __global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ lo
                                                     uint32_t slot, uint32_t tag, uint32_t seq_base, int32_t* out,
                                                     int out_stride) {
   __shared__ SmemRed<BT> s;
+  __shared__ SelSmem sel;
   __shared__ RowStats st;
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.x;
   const float* l = logits + (size_t)row * ld;
-  compute_row_stats(l, V, w, st, s);
+  compute_row_stats(l, V, w, st, s, sel);
   __syncthreads();
   int tok;
   if (!(w.temperature > 0.f)) {
@@ -353,15 +435,16 @@ __global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ lo
 __global__ void __launch_bounds__(ST) stats_kernel(const float* __restrict__ p, const float* __restrict__ q, int B,
                                                    int k, int V, ulb_warp w, RowStats* __restrict__ out) {
   __shared__ SmemRed<ST> s;
+  __shared__ SelSmem sel;
   __shared__ RowStats st;
   pdl_wait();
   pdl_trigger();
   /* persistent: few rows in flight per SM, so a row read by the max pass is still in L2
-     when the sum pass reads it again */
+     when the later passes read it again */
   const int np = B * (k + 1), rows = np + B * k;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const float* l = row < np ? p + (size_t)row * V : q + (size_t)(row - np) * V;
-    compute_row_stats(l, V, w, st, s);
+    compute_row_stats(l, V, w, st, s, sel);
     __syncthreads();
     if (threadIdx.x == 0) out[row] = st;
     __syncthreads();

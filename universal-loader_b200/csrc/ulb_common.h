@@ -100,6 +100,19 @@ ULB_HD float ulb_warp_exp(float x) {
   return ULB_FMUL(p, two_k.f);
 }
 
+/*
+ * Top-p masses in fixed point: a warp weight e (a binary32 from ulb_warp_exp, at most 1) as
+ * floor(e * 2^40) in 64 bits.  Integer sums do not depend on their order, so the host and the
+ * device find the same top-p cut whatever order they add in; a vocabulary of 2^23 weights of
+ * at most 2^40 each cannot overflow.  (double)e * 2^40 is exact; the conversion truncates.
+ */
+ULB_HD uint64_t ulb_mass_fix(float e) { return (uint64_t)((double)e * 1099511627776.0); }
+/* the mass the kept set must reach: floor(top_p * total), at least 1 (the largest weight is 2^40) */
+ULB_HD uint64_t ulb_topp_target(float top_p, uint64_t total) {
+  const uint64_t r = (uint64_t)((double)top_p * (double)total);
+  return r < 1 ? 1 : r;
+}
+
 /* ---------------------------------------------------------------- binary16 */
 ULB_HD float ulb_h2f(uint16_t h) {
   uint32_t s = (uint32_t)(h >> 15) << 31;
