@@ -37,7 +37,7 @@ namespace ulb {
 
 namespace {
 
-constexpr int ST = 256;  /* threads per row CTA (stats, draft sampling) */
+constexpr int ST = 1024; /* threads per row CTA (stats, draft sampling): a row's passes are latency-bound */
 constexpr int DT = 1024; /* threads per sequence CTA (decide: residual / bonus sampling) */
 
 struct RowStats {
@@ -400,9 +400,9 @@ __device__ __forceinline__ float rng_u(uint64_t seed, uint32_t round, uint32_t s
 /* ------------------------------------------------------------------ kernels */
 
 /* one CTA of BT threads per row: draft / first-token sampling. out[row * out_stride] = token.
-   Greedy rows (an argmax, lowest index on ties, whatever BT) run with 1024 threads so the
-   whole row is requested in about one round trip; sampled rows with ST, the block size of
-   stats_kernel, so both reduce the row's sums in the same order. */
+   Rows run with ST = 1024 threads, the block size of stats_kernel, so a greedy row is
+   requested in about one round trip and a sampled row's sums reduce in the same order as in
+   stats_kernel. */
 template <int BT>
 __global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ logits, int V, int ld, ulb_warp w,
                                                     uint64_t seed, const uint32_t* dev_round, uint32_t round,
@@ -614,8 +614,9 @@ int launch_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* dr
   if (B == 0) return ULB_OK;
   RowStats* rs = (RowStats*)stats_scratch;
   const int rows = B * (k + 1) + B * k;
-  /* rows in flight (one per CTA): as many as keep ~60 MB of rows in L2, between 1 and 3 per SM */
-  const int fit = (int)std::min<long long>(3LL * c->n_sm, std::max<long long>(c->n_sm, 60000000LL / ((long long)V * 4)));
+  /* rows in flight (one per CTA): as many as keep ~100 MB of rows in L2, between 1 and 2 per SM
+     (two 1024-thread CTAs fill an SM) */
+  const int fit = (int)std::min<long long>(2LL * c->n_sm, std::max<long long>(c->n_sm, 100000000LL / ((long long)V * 4)));
   const int grid = std::min(rows, fit);
   cudaError_t e = launch_k(c, stats_kernel, dim3(grid), dim3(ST), 0, p, q, B, k, V, *w, rs);
   if (e != cudaSuccess) return cuda_error(e, "stats launch", __FILE__, __LINE__);
