@@ -291,10 +291,6 @@ typedef struct ulb_spec_desc {
   int use_graphs;   /* 1: capture each round into a CUDA graph              */
 } ulb_spec_desc;
 
-/* The draft model is marked for small batches: from then on its forwards of at most 8 rows
- * run their GEMVs as 8-warp CTAs, two of which share an SM, so each kernel's CTAs are
- * resident (and streaming their weights) while the previous kernel finishes.  Its rows are
- * summed in a different order than in the 16-warp form the target keeps. */
 ULB_API int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft,
                     const ulb_spec_desc* desc, ulb_spec** out);
 /* Copy prompts (host int32 [n_seq][max_prompt], lengths [n_seq]) and prefill both models;

@@ -59,9 +59,6 @@ struct Model {
   __half* h16 = nullptr;
   float* tp_part = nullptr; /* [rows][d] partial attn_output / ffn_down sums (tensor parallel) */
   size_t ws_bytes = 0;
-  /* the GEMVs of this model's forwards of <= 8 rows use the small-batch latency form (the
-     speculative loop marks its draft model: M = 1..2 row steps, latency-bound) */
-  bool lat_form = false;
 };
 
 struct KV {
@@ -273,23 +270,8 @@ static int forward_head(Model* m, int M, int rps, int logits_mode, float* logits
                           m->x16, n_out, EPI_STORE, o);
 }
 
-static int model_forward_impl(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos,
-                              int logits_mode, float* logits, int ld, int* err);
-
 int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos, int logits_mode,
                   float* logits, int ld, int* err) {
-  Ctx* c = m->c;
-  const bool prev = c->gemv_lat;
-  c->gemv_lat = m->lat_form;
-  const int rc = model_forward_impl(m, kv, M, rps, tok, seq, pos, logits_mode, logits, ld, err);
-  c->gemv_lat = prev;
-  return rc;
-}
-
-void model_set_latency_form(Model* m, bool on) { m->lat_form = on; }
-
-static int model_forward_impl(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos,
-                              int logits_mode, float* logits, int ld, int* err) {
   Ctx* c = m->c;
   const ulb_model_desc& d = m->d;
   ULB_CHECK(m->finalized, ULB_EINVAL, "forward: model not finalized");

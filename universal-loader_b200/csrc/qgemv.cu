@@ -217,16 +217,13 @@ __device__ __forceinline__ void block_dot(const uint32_t (&w)[8], const uint4& b
 }
 
 constexpr int kGW = 16; /* warps per CTA (one CTA per SM) */
-/* warps per CTA of the small-batch latency form: half an SM's registers, so the next
-   kernel's CTAs become resident next to a running one and start their weight loads early */
-constexpr int kGWLat = 8;
 
 /* GEMV configuration per weight type and n-tile count:
      W    warps per CTA (one CTA per SM; the split of the weight stream depends on it, so it is
           the same for every NT of a weight type)
      D    weight tiles in flight per warp (the register ring) */
-template <int QT, int NT, int WARPS = kGW> struct GemvCfg {
-  static constexpr int W = WARPS;
+template <int QT, int NT> struct GemvCfg {
+  static constexpr int W = kGW;
   static constexpr int D = QT == ULB_TYPE_Q4_0 ? (NT == 4 ? 2 : 4) : (NT == 4 ? 1 : 2);
 };
 
@@ -351,8 +348,8 @@ struct NormIn {
 };
 
 /* bytes of the per-warp strip partials in shared memory: W warps x {first, last strip} */
-template <int QT, int NT, int W> constexpr size_t warp_part_bytes() {
-  return (size_t)W * 2 * NT * 32 * sizeof(float4);
+template <int QT, int NT> constexpr size_t warp_part_bytes() {
+  return (size_t)GemvCfg<QT, NT>::W * 2 * NT * 32 * sizeof(float4);
 }
 
 /* one GEMV of a launch: y (by its epilogue) = W . activations */
@@ -372,8 +369,8 @@ struct GemvStep {
 };
 
 /* shared-memory layout of a GEMV CTA: warp partials | normalised activations (fp16 [M][K]) */
-template <int QT, int NT, int W> __device__ __forceinline__ __half* smem_x(uint8_t* smem) {
-  return reinterpret_cast<__half*>(smem + warp_part_bytes<QT, NT, W>());
+template <int QT, int NT> __device__ __forceinline__ __half* smem_x(uint8_t* smem) {
+  return reinterpret_cast<__half*>(smem + warp_part_bytes<QT, NT>());
 }
 
 /*
@@ -442,11 +439,11 @@ struct XIn {
 };
 
 /* the normalised activations of a step (its nin rows), in shared memory: fp16 [M][K] */
-template <int QT, int NT, int W>
+template <int QT, int NT>
 __device__ __forceinline__ XIn prep_norm(const GemvStep& S, uint8_t* smem, float* red) {
   const int K = (int)S.sp.tiles * WTile<QT>::TK;
-  __half* xs = smem_x<QT, NT, W>(smem);
-  norm_rows<W>(S.nin.x, S.nin.ldx, S.nin.g, K, S.nin.eps, S.M, xs, red);
+  __half* xs = smem_x<QT, NT>(smem);
+  norm_rows<GemvCfg<QT, NT>::W>(S.nin.x, S.nin.ldx, S.nin.g, K, S.nin.eps, S.M, xs, red);
   return XIn{xs, K};
 }
 
@@ -466,10 +463,10 @@ __device__ __forceinline__ XIn prep_norm(const GemvStep& S, uint8_t* smem, float
  * (shared memory, or global memory written earlier in the same launch); otherwise with
  * read-only loads.
  */
-template <int QT, int NT, int EPI, bool XS, int W, class Sync, class Prep>
+template <int QT, int NT, int EPI, bool XS, class Sync, class Prep>
 __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint32_t* wcnt,
                                           const __half* __restrict__ xzero, Sync sync, Prep prep) {
-  constexpr int TB = WTile<QT>::TB, D = GemvCfg<QT, NT, W>::D;
+  constexpr int TB = WTile<QT>::TB, D = GemvCfg<QT, NT>::D, W = GemvCfg<QT, NT>::W;
   const Split sp = S.sp;
   const int M = S.M, N = S.N;
   const EpiArgs& ea = S.ea;
@@ -609,13 +606,13 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
 
 /* one GEMV per launch: XS, the activation rows normalised from the step's nin rows into
    shared memory; otherwise read from global memory through L1 */
-template <int QT, int NT, int EPI, bool XS, int W>
-__global__ void __launch_bounds__(W * 32, kGW / W)
+template <int QT, int NT, int EPI, bool XS>
+__global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
     qgemv_kernel(GemvStep S, const __half* __restrict__ xzero) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint32_t wcnt[W];
+  __shared__ uint32_t wcnt[GemvCfg<QT, NT>::W];
   __shared__ float red[72];
-  gemv_body<QT, NT, EPI, XS, W>(
+  gemv_body<QT, NT, EPI, XS>(
       S, smem, wcnt, xzero,
       [] {
         pdl_wait();
@@ -623,7 +620,7 @@ __global__ void __launch_bounds__(W * 32, kGW / W)
         return true;
       },
       [&]() -> XIn {
-        if (XS) return prep_norm<QT, NT, W>(S, smem, red);
+        if (XS) return prep_norm<QT, NT>(S, smem, red);
         __syncthreads();
         return XIn{S.x, S.ldx};
       });
@@ -843,7 +840,7 @@ __global__ void dequant_q4k_kernel(const uint8_t* __restrict__ w, int tiles, int
 }
 
 /* the split of a matrix over the SMs (see Split) */
-template <int QT, int NT, int W>
+template <int QT, int NT>
 static int make_split(Ctx* c, const Tensor* w, Split* sp) {
   const long long S = w->n_strips;
   ULB_CHECK(S > 0 && (long long)w->tiles * S * c->n_sm < (1ll << 31), ULB_EUNSUPPORTED, "qgemv: %lld strips of %d tiles",
@@ -851,7 +848,7 @@ static int make_split(Ctx* c, const Tensor* w, Split* sp) {
   sp->S = (uint32_t)S;
   sp->G = (uint32_t)std::min<long long>(c->n_sm, S);
   sp->tiles = (uint32_t)w->tiles;
-  sp->Wn = (uint32_t)std::min<long long>(W, S / sp->G * w->tiles);
+  sp->Wn = (uint32_t)std::min<long long>(GemvCfg<QT, NT>::W, S / sp->G * w->tiles);
   return ULB_OK;
 }
 
@@ -866,12 +863,12 @@ static void take_hint(Ctx* c, GemvStep* S) {
 /* shared memory of the normalised activation rows: M x K fp16 */
 static size_t norm_bytes(int M, int K) { return ((size_t)M * K * sizeof(__half) + 15) / 16 * 16; }
 
-template <int QT, int NT, int EPI, bool XS, int W>
-int launch_q_w(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a, const NormIn& nin) {
+template <int QT, int NT, int EPI, bool XS = false>
+int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a, const NormIn& nin = NormIn()) {
   ULB_CHECK(w->K + 8 <= kZeroRowHalves, ULB_EUNSUPPORTED, "qgemv: K=%d too long", w->K);
   GemvStep S;
   S.w = (const uint8_t*)w->dev;
-  ULB_TRY((make_split<QT, NT, W>(c, w, &S.sp)));
+  ULB_TRY((make_split<QT, NT>(c, w, &S.sp)));
   S.N = w->N;
   S.M = M;
   S.x = x;
@@ -879,29 +876,18 @@ int launch_q_w(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const E
   S.nin = nin;
   S.ea = a;
   take_hint(c, &S);
-  const size_t smem = warp_part_bytes<QT, NT, W>() + (XS ? norm_bytes(M, w->K) : 0);
+  const size_t smem = warp_part_bytes<QT, NT>() + (XS ? norm_bytes(M, w->K) : 0);
   ULB_CHECK(smem <= kGemvSmemBytes, ULB_EUNSUPPORTED, "qgemv: %d normalised rows of %d", M, w->K);
   static bool attr_set = false;
   if (!attr_set) {
-    ULB_CUDA(cudaFuncSetAttribute(qgemv_kernel<QT, NT, EPI, XS, W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    ULB_CUDA(cudaFuncSetAttribute(qgemv_kernel<QT, NT, EPI, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)kGemvSmemBytes));
     attr_set = true;
   }
-  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI, XS, W>, dim3(S.sp.G), dim3(W * 32), smem, S,
+  cudaError_t e = launch_k(c, qgemv_kernel<QT, NT, EPI, XS>, dim3(S.sp.G), dim3(GemvCfg<QT, NT>::W * 32), smem, S,
                            (const __half*)c->zero_row);
   if (e != cudaSuccess) return cuda_error(e, "qgemv launch", __FILE__, __LINE__);
   return ULB_OK;
-}
-
-/* the one-n-tile GEMV of a model in small-batch latency form runs kGWLat warps a CTA (its
-   rows' split differs from the 16-warp form, so a model uses one form for all its M <= 8
-   forwards) */
-template <int QT, int NT, int EPI, bool XS = false>
-int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const EpiArgs& a, const NormIn& nin = NormIn()) {
-  if constexpr (NT == 1) {
-    if (c->gemv_lat) return launch_q_w<QT, NT, EPI, XS, kGWLat>(c, w, x, M, ldx, a, nin);
-  }
-  return launch_q_w<QT, NT, EPI, XS, kGW>(c, w, x, M, ldx, a, nin);
 }
 
 template <int NT, int EPI>

@@ -37,7 +37,8 @@ namespace ulb {
 
 namespace {
 
-constexpr int ST = 1024; /* threads per row CTA (stats, draft sampling): a row's passes are latency-bound */
+constexpr int ST = 256;  /* threads per row CTA of the stats grid (many rows in flight) */
+constexpr int RT = 1024; /* threads per row CTA of draft-token sampling (one row per CTA: latency-bound) */
 constexpr int DT = 1024; /* threads per sequence CTA (decide: residual / bonus sampling) */
 
 struct RowStats {
@@ -400,9 +401,9 @@ __device__ __forceinline__ float rng_u(uint64_t seed, uint32_t round, uint32_t s
 /* ------------------------------------------------------------------ kernels */
 
 /* one CTA of BT threads per row: draft / first-token sampling. out[row * out_stride] = token.
-   Rows run with ST = 1024 threads, the block size of stats_kernel, so a greedy row is
-   requested in about one round trip and a sampled row's sums reduce in the same order as in
-   stats_kernel. */
+   Rows run with RT = 1024 threads, so a row is requested in about one round trip and its
+   passes have four times the threads of a stats row (the normaliser Z of a sampled row is
+   summed in another order than stats_kernel's, which moves it by at most an fp64 ulp). */
 template <int BT>
 __global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ logits, int V, int ld, ulb_warp w,
                                                     uint64_t seed, const uint32_t* dev_round, uint32_t round,
@@ -587,12 +588,8 @@ int launch_sample_seq(Ctx* c, const float* logits, int rows, int V, int ld, cons
                       const uint32_t* dev_round, uint32_t round, uint32_t slot, uint32_t tag, uint32_t seq_base,
                       int32_t* out, int out_stride) {
   if (rows == 0) return ULB_OK;
-  constexpr int kGreedyThreads = 1024;
-  cudaError_t e = !(w->temperature > 0.f)
-                      ? launch_k(c, sample_kernel<kGreedyThreads>, dim3(rows), dim3(kGreedyThreads), 0, logits, V, ld,
-                                 *w, seed, dev_round, round, slot, tag, seq_base, out, out_stride)
-                      : launch_k(c, sample_kernel<ST>, dim3(rows), dim3(ST), 0, logits, V, ld, *w, seed, dev_round,
-                                 round, slot, tag, seq_base, out, out_stride);
+  cudaError_t e = launch_k(c, sample_kernel<RT>, dim3(rows), dim3(RT), 0, logits, V, ld, *w, seed, dev_round, round,
+                           slot, tag, seq_base, out, out_stride);
   if (e != cudaSuccess) return cuda_error(e, "sample launch", __FILE__, __LINE__);
   return ULB_OK;
 }
@@ -614,9 +611,8 @@ int launch_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* dr
   if (B == 0) return ULB_OK;
   RowStats* rs = (RowStats*)stats_scratch;
   const int rows = B * (k + 1) + B * k;
-  /* rows in flight (one per CTA): as many as keep ~100 MB of rows in L2, between 1 and 2 per SM
-     (two 1024-thread CTAs fill an SM) */
-  const int fit = (int)std::min<long long>(2LL * c->n_sm, std::max<long long>(c->n_sm, 100000000LL / ((long long)V * 4)));
+  /* rows in flight (one per CTA): as many as keep ~60 MB of rows in L2, between 1 and 3 per SM */
+  const int fit = (int)std::min<long long>(3LL * c->n_sm, std::max<long long>(c->n_sm, 60000000LL / ((long long)V * 4)));
   const int grid = std::min(rows, fit);
   cudaError_t e = launch_k(c, stats_kernel, dim3(grid), dim3(ST), 0, p, q, B, k, V, *w, rs);
   if (e != cudaSuccess) return cuda_error(e, "stats launch", __FILE__, __LINE__);

@@ -28,7 +28,6 @@ namespace ulb {
 struct Model;
 struct KV;
 int model_prepare(Model* m, KV* kv, int M, int rps);
-void model_set_latency_form(Model* m, bool on);
 int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos, int logits_mode,
                   float* logits, int ld, int* err);
 int launch_sample_seq(Ctx* c, const float* logits, int rows, int V, int ld, const ulb_warp* w, uint64_t seed,
@@ -221,9 +220,6 @@ int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft, const ulb
   sp->ctx = ctx;
   sp->tgt = model_of(target);
   sp->dft = draft && d->k > 0 ? model_of(draft) : nullptr;
-  /* the draft decodes 1-2 rows a step: its GEMVs run in the small-batch latency form (its
-     results need not match any other batch size; the target's arithmetic is untouched) */
-  if (sp->dft) model_set_latency_form(sp->dft, true);
   sp->tgt_h = target;
   sp->dft_h = sp->dft ? draft : nullptr;
   sp->d = *d;

@@ -94,9 +94,6 @@ struct Ctx {
   size_t pf2_bytes = 0;
   /* timing of the tensor-parallel all-reduces (on while a round is profiled): a CUDA event
      pair is recorded around each ncclAllReduce, events[2i] before and events[2i+1] after */
-  /* small-batch latency form of the GEMV (8-warp CTAs, two can share an SM), set by a
-     forward of a model marked for it (the draft model of the speculative loop) */
-  bool gemv_lat = false;
   bool ar_timing = false;
   std::vector<cudaEvent_t> ar_events;
   size_t ar_used = 0;
