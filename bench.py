@@ -433,12 +433,14 @@ def run_reference(args):
     return 0
 
 
-def _timed_generations(api, prompt, cfg, steps):
+def _timed_generations(api, prompt, cfg, steps, before=None):
     """`steps` generations through the public API; returns summed stats"""
     agg = dict(toks=0, dec_ms=0.0, pre_ms=0.0, launches=0, accepted=0, drafted=0, rounds=0, h2d=0.0, d2h=0.0)
     outs = []
     t0 = time.perf_counter()
-    for _ in range(steps):
+    for i in range(steps):
+        if before is not None and i > 0:
+            before()
         out = api.generate_tokens(prompt, cfg)
         st = api.get_last_stats()
         outs.append(out)
@@ -667,13 +669,28 @@ def run_c5(args):
     import vulkangguf as vg
     tp, dp = ensure_models(rank, barrier, C5_TARGET, TARGET)
     api = vg.InferenceAPI()
+    mon = None
     if world > 1:
+        import datetime
         import torch.distributed as dist
+        from ulb_tp import PeerMonitor
         box = [vg.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         if not api.init_tensor_parallel(rank, world, box[0]):
             print("[bench] tensor-parallel init failed", file=sys.stderr)
             return 1
+        # a lost rank is found on the host between generations (PeerMonitor), and a wait for a
+        # collective whose peer is gone mid-generation gives up (set_collective_timeout)
+        store = dist.TCPStore(os.environ.get("MASTER_ADDR", "127.0.0.1"), int(os.environ["MASTER_PORT"]) + 1, world,
+                              rank == 0, timeout=datetime.timedelta(seconds=120))
+        mon = PeerMonitor(store, rank, world, timeout_s=120.0)
+        api.set_collective_timeout(300.0)
+    step = [0]
+
+    def peers_ready():
+        if mon is not None:
+            mon.wait_step(step[0])
+        step[0] += 1
     t_load = time.time()
     if not api.load_model(tp) or not api.load_draft_model(dp):
         print("[bench] model load failed", file=sys.stderr)
@@ -690,11 +707,13 @@ def run_c5(args):
         return c
 
     for _ in range(args.warmup):  # warm-up generations: every kernel shape and the round graph
+        peers_ready()
         api.generate_tokens(prompts, cfg(8))
+    peers_ready()
     barrier()
     clocks = ClockSampler(smi_index)
     clocks.start()
-    g = _timed_generations(api, prompts, cfg(C5_NEW), args.steps)
+    g = _timed_generations(api, prompts, cfg(C5_NEW), args.steps, before=peers_ready)
     barrier()
     clk = clocks.stop()
     prof = api.profile_round()

@@ -69,6 +69,16 @@ ULB_API int ulb_destroy(ulb_ctx* ctx);
 ULB_API void* ulb_stream(ulb_ctx* ctx);
 /* Replaces ComputeDispatcher::wait_for_completion (src/vulkan_backend/compute.cpp:82-121). */
 ULB_API int ulb_stream_sync(ulb_ctx* ctx);
+/*
+ * Bounded device-side wait: enqueue on the context stream a wait until the int32 at dev_flag
+ * (device memory, or memory the device can reach: another stream's or process's flag) is
+ * >= value.  Later work on the stream runs after it.  If the flag does not get there within
+ * timeout_ns (at most 10 s), the wait gives up instead of hanging the device: it raises the
+ * device error flag, which the next ulb_stream_sync reports as ULB_ETIMEOUT, and the context
+ * stays usable.  No counterpart in the reference (its Vulkan fences wait on the host,
+ * src/vulkan_backend/compute.cpp:82-121, with no bound).
+ */
+ULB_API int ulb_wait_flag(ulb_ctx* ctx, const int32_t* dev_flag, int32_t value, uint64_t timeout_ns);
 /* Device bytes currently held by the context (weights, caches, workspaces). */
 ULB_API int ulb_mem_used(ulb_ctx* ctx, size_t* out_bytes);
 
@@ -92,6 +102,14 @@ ULB_API int ulb_event_destroy(void* event);
  * (any host channel), then every rank calls ulb_tp_init on its own context. */
 ULB_API int ulb_tp_unique_id(void* out_id128);
 ULB_API int ulb_tp_init(ulb_ctx* ctx, int rank, int world, const void* id128);
+/* Bound (ms; 0 = unbounded, the default) on every host wait of this context for work that
+ * holds tensor-parallel collectives (the speculative loop, ulb_model_forward,
+ * ulb_stream_sync).  Past it -- a peer rank died or stopped answering -- the communicator is
+ * aborted (ncclCommAbort, so the collective's kernel stops waiting), the call returns
+ * ULB_ETIMEOUT, and every later tensor-parallel call fails with ULB_ENCCL.  An asynchronous
+ * communicator error is handled the same way (ULB_ENCCL).  No counterpart in the reference,
+ * whose multi-GPU manager has no data path (src/vulkan_backend/multi_gpu_manager.cpp). */
+ULB_API int ulb_tp_set_timeout(ulb_ctx* ctx, int timeout_ms);
 
 /* CUDA-graph capture of a fixed sequence of per-op calls on the context's stream, replayed
  * with one launch (replaces re-recording the reference's command buffers per dispatch,

@@ -129,6 +129,16 @@ class InferenceAPI {
     if (!ok) std::fprintf(stderr, "[InferenceAPI] init_tensor_parallel: %s\n", engine_->error().c_str());
     return ok;
   }
+  /* bound (seconds) on every wait for tensor-parallel work: past it the communicator is
+     aborted and the generation raises instead of blocking on a peer that is gone */
+  bool set_collective_timeout(double seconds) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!engine_) return false;
+    const bool ok = engine_->set_tp_timeout((int)(seconds * 1000.0));
+    if (!ok) std::fprintf(stderr, "[InferenceAPI] set_collective_timeout: %s\n", engine_->error().c_str());
+    return ok;
+  }
+
 
   bool load_model(const std::string& path) { return load(path, false); }
   bool load_draft_model(const std::string& path) { return load(path, true); }
@@ -605,6 +615,8 @@ PYBIND11_MODULE(vulkangguf, m) {
            "Register custom shader compiler function")
       /* additions for the speculative path */
       .def("load_draft_model", &InferenceAPI::load_draft_model, "Load the GGUF draft model for speculative decoding")
+      .def("set_collective_timeout", &InferenceAPI::set_collective_timeout, py::arg("seconds"),
+           "Bound on waits for tensor-parallel work; past it the communicator is aborted and the call raises")
       .def("init_tensor_parallel", &InferenceAPI::init_tensor_parallel, py::arg("rank"), py::arg("world"),
            py::arg("nccl_id"), "Join a tensor-parallel NCCL communicator before load_model (one GPU per process)")
       .def("unload_draft_model", &InferenceAPI::unload_draft_model, "Unload the draft model")

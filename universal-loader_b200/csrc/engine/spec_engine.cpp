@@ -55,6 +55,13 @@ bool Engine::init_tp(int rank, int world, const void* nccl_id128) {
   return true;
 }
 
+bool Engine::set_tp_timeout(int ms) {
+  std::lock_guard<std::mutex> lk(mu_);
+  if (!ctx_) return fail("no CUDA device: " + err_);
+  if (ulb_tp_set_timeout(ctx_, ms) != ULB_OK) return fail(ulb_last_error());
+  return true;
+}
+
 bool Engine::load(const std::string& path, bool draft) {
   std::lock_guard<std::mutex> lk(mu_);
   if (!ctx_) return fail("no CUDA device: " + err_);

@@ -68,6 +68,8 @@ class Engine {
   /* join a tensor-parallel communicator: later target loads keep this rank's slice (the
      draft stays replicated) */
   bool init_tp(int rank, int world, const void* nccl_id128);
+  /* bound on host waits for tensor-parallel work (ulb_tp_set_timeout); 0 = unbounded */
+  bool set_tp_timeout(int ms);
   void unload(bool draft);
   bool has_model(bool draft) const { return draft ? draft_ != nullptr : target_ != nullptr; }
   const ModelInfo& info(bool draft) const { return draft ? dinfo_ : tinfo_; }

@@ -746,8 +746,8 @@ int ulb_model_forward(ulb_ctx* ctx, ulb_model* mm, ulb_kv* kvh, int M, int rps, 
   int herr = 0;
   if (rc == ULB_OK) {
     cudaError_t e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) rc = cuda_error(e, "forward", __FILE__, __LINE__);
+    else rc = sync_stream(c);
   }
   dev_free(c, err, sizeof(int));
   if (rc == ULB_OK && herr) rc = set_error(ULB_EINVAL, "ulb_model_forward: token id out of range");

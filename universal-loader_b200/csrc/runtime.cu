@@ -16,10 +16,14 @@
 #include <nccl.h>
 
 #include "ulb_internal.h"
+#include "watchdog.h"
 
 namespace ulb {
 
 static thread_local std::string g_last_error;
+/* longest wait ulb_wait_flag accepts: a bounded wait must stay short enough that a missing
+   writer costs seconds, not a hung device */
+constexpr uint64_t kMaxFlagWaitNs = 10ull * 1000 * 1000 * 1000;
 
 int set_error(int code, const char* fmt, ...) {
   char buf[512];
@@ -55,10 +59,66 @@ void dev_free(Ctx* c, void* p, size_t bytes) {
   c->bytes_live -= bytes;
 }
 
+/* one lane polls the flag with acquire loads until it reaches `value` or the timeout passes;
+   on the timeout it raises bit 4 of the device error word and returns (nothing is left in
+   flight: the wait is a plain load loop) */
+__global__ void wait_flag_kernel(const int* flag, int value, unsigned long long timeout_ns, int* err) {
+  pdl_wait();
+  if (threadIdx.x != 0) return;
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v >= value) return;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > timeout_ns) {
+      atomicOr(err, 16);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
+int sync_stream(Ctx* c) {
+  if (!c->nccl || c->tp_timeout_ms <= 0) {
+    ULB_CUDA(cudaStreamSynchronize(c->stream));
+    return ULB_OK;
+  }
+  ncclComm_t comm = (ncclComm_t)c->nccl;
+  cudaError_t qerr = cudaSuccess;
+  const int rc = bounded_wait(
+      [&] {
+        const cudaError_t e = cudaStreamQuery(c->stream);
+        if (e == cudaSuccess) return Poll::kDone;
+        if (e == cudaErrorNotReady) return Poll::kPending;
+        qerr = e;
+        return Poll::kError;
+      },
+      [&] {
+        ncclResult_t a = ncclSuccess;
+        return ncclCommGetAsyncError(comm, &a) == ncclSuccess && a != ncclSuccess && a != ncclInProgress;
+      },
+      [&] {
+        /* the collective's kernel stops waiting for the missing peer; the communicator is gone */
+        ncclCommAbort(comm);
+        c->nccl = nullptr;
+        c->tp_aborted = true;
+      },
+      c->tp_timeout_ms / 1000.0);
+  if (rc == ULB_ECUDA) return cuda_error(qerr, "stream", __FILE__, __LINE__);
+  if (rc == ULB_ETIMEOUT)
+    return set_error(ULB_ETIMEOUT, "tensor parallel: the stream did not finish within %d ms (a peer rank is not "
+                     "answering); the communicator was aborted", c->tp_timeout_ms);
+  if (rc == ULB_ENCCL)
+    return set_error(ULB_ENCCL, "tensor parallel: the communicator reported an asynchronous error; it was aborted");
+  return ULB_OK;
+}
+
 int check_device_errors(Ctx* c) {
   int h = 0;
   ULB_CUDA(cudaMemcpyAsync(&h, c->dev_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
-  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  ULB_TRY(sync_stream(c));
   if (h) {
     ULB_CUDA(cudaMemsetAsync(c->dev_err, 0, sizeof(int), c->stream));
 
@@ -68,6 +128,7 @@ int check_device_errors(Ctx* c) {
 }
 
 int tp_allreduce_sum(Ctx* c, float* buf, size_t n) {
+  ULB_CHECK(!c->tp_aborted, ULB_ENCCL, "tensor parallelism: the communicator was aborted after a peer stopped answering");
   ULB_CHECK(c->nccl, ULB_EINVAL, "tensor parallelism: the context has no communicator (ulb_tp_init)");
   const bool timed = c->ar_timing && c->ar_used + 2 <= c->ar_events.size();
   if (timed) ULB_CUDA(cudaEventRecord(c->ar_events[c->ar_used], c->stream));
@@ -144,6 +205,24 @@ int ulb_tp_init(ulb_ctx* ctx, int rank, int world, const void* id128) {
   ctx->c.nccl = comm;
   ctx->c.tp_rank = rank;
   ctx->c.tp_world = world;
+  return ULB_OK;
+}
+
+int ulb_wait_flag(ulb_ctx* ctx, const int32_t* flag, int32_t value, uint64_t timeout_ns) {
+  ULB_CHECK(ctx && flag, ULB_EINVAL, "ulb_wait_flag: NULL argument");
+  ULB_CHECK(timeout_ns > 0 && timeout_ns <= kMaxFlagWaitNs, ULB_EINVAL, "ulb_wait_flag: timeout %llu ns outside (0, %llu]",
+            (unsigned long long)timeout_ns, (unsigned long long)kMaxFlagWaitNs);
+  Ctx* c = &ctx->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  cudaError_t e = launch_k(c, wait_flag_kernel, dim3(1), dim3(32), 0, (const int*)flag, (int)value,
+                           (unsigned long long)timeout_ns, c->dev_err);
+  if (e != cudaSuccess) return cuda_error(e, "wait_flag launch", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
+int ulb_tp_set_timeout(ulb_ctx* ctx, int timeout_ms) {
+  ULB_CHECK(ctx && timeout_ms >= 0, ULB_EINVAL, "ulb_tp_set_timeout: bad argument");
+  ctx->c.tp_timeout_ms = timeout_ms;
   return ULB_OK;
 }
 

@@ -320,7 +320,7 @@ int ulb_spec_prefill(ulb_spec* h, const int32_t* prompts, const int32_t* lens) {
   }
   ULB_CUDA(cudaMemcpyAsync(sp->L, L.data(), S * 4, cudaMemcpyHostToDevice, c->stream));
   ULB_CUDA(cudaMemcpyAsync(sp->done, done.data(), S * 4, cudaMemcpyHostToDevice, c->stream));
-  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  ULB_TRY(sync_stream(c));
   sp->launches = c->launches - launches0;
   sp->prefilled = true;
   return ULB_OK;
@@ -348,7 +348,7 @@ int ulb_spec_run(ulb_spec* h, int max_rounds, int* out_rounds) {
   while (max_rounds <= 0 || ran < max_rounds) {
     ULB_CUDA(cudaMemcpyAsync(sp->h_L, sp->L, S * 4, cudaMemcpyDeviceToHost, c->stream));
     ULB_CUDA(cudaMemcpyAsync(sp->h_done, sp->done, S * 4, cudaMemcpyDeviceToHost, c->stream));
-    ULB_CUDA(cudaStreamSynchronize(c->stream));
+    ULB_TRY(sync_stream(c));
     int rem_max = 0;
     for (int s = 0; s < S; ++s)
       if (!sp->h_done[s]) rem_max = std::max(rem_max, sp->d.max_new - (sp->h_L[s] - sp->h_plen[s]));
@@ -384,7 +384,7 @@ int ulb_spec_read(ulb_spec* h, int32_t* tokens, int32_t* counts, uint64_t stats[
   ULB_CUDA(cudaMemcpyAsync(L.data(), sp->L, S * 4, cudaMemcpyDeviceToHost, c->stream));
   ULB_CUDA(cudaMemcpyAsync(act.data(), sp->active, S * 4, cudaMemcpyDeviceToHost, c->stream));
   ULB_CUDA(cudaMemcpyAsync(st, sp->stats, sizeof st, cudaMemcpyDeviceToHost, c->stream));
-  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  ULB_TRY(sync_stream(c));
   for (int s = 0; s < S; ++s) {
     const int P = sp->h_plen[s];
     const int cnt = std::min(L[s] - P, N);
@@ -411,7 +411,7 @@ int ulb_spec_read_rounds(ulb_spec* h, int seq, int max_records, int32_t* out, in
   ULB_CUDA(cudaSetDevice(c->device));
   int32_t act = 0;
   ULB_CUDA(cudaMemcpyAsync(&act, sp->active + seq, 4, cudaMemcpyDeviceToHost, c->stream));
-  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  ULB_TRY(sync_stream(c));
   const int n = std::min(act, sp->log_rounds);
   *out_n = n;
   if (!out || max_records <= 0 || n == 0) return ULB_OK;
@@ -419,7 +419,7 @@ int ulb_spec_read_rounds(ulb_spec* h, int seq, int max_records, int32_t* out, in
   const size_t take = (size_t)std::min(n, max_records) * words;
   ULB_CUDA(cudaMemcpyAsync(out, sp->log + (size_t)seq * sp->log_rounds * words, take * 4, cudaMemcpyDeviceToHost,
                            c->stream));
-  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  ULB_TRY(sync_stream(c));
   return ULB_OK;
 }
 
@@ -438,7 +438,13 @@ int ulb_spec_profile_round(ulb_spec* h, float ms[3]) {
   if (rc == ULB_OK) {
     sp->launches += sp->per_round;
     e = cudaEventRecord(ev[3], c->stream);
-    if (e == cudaSuccess) e = cudaEventSynchronize(ev[3]);
+    if (e == cudaSuccess) {
+      const int src = sync_stream(c); /* bounded when the round holds tensor-parallel collectives */
+      if (src != ULB_OK) {
+        for (auto& x : ev) cudaEventDestroy(x);
+        return src;
+      }
+    }
     if (e == cudaSuccess) e = cudaEventElapsedTime(&ms[0], ev[0], ev[1]);
     if (e == cudaSuccess) e = cudaEventElapsedTime(&ms[1], ev[1], ev[2]);
     if (e == cudaSuccess) e = cudaEventElapsedTime(&ms[2], ev[2], ev[3]);

@@ -94,6 +94,10 @@ struct Ctx {
   size_t pf2_bytes = 0;
   /* timing of the tensor-parallel all-reduces (on while a round is profiled): a CUDA event
      pair is recorded around each ncclAllReduce, events[2i] before and events[2i+1] after */
+  /* host-side bound on waits for a stream holding tensor-parallel collectives (ms, 0 = none):
+     past it the communicator is aborted and the call returns ULB_ETIMEOUT */
+  int tp_timeout_ms = 0;
+  bool tp_aborted = false;
   bool ar_timing = false;
   std::vector<cudaEvent_t> ar_events;
   size_t ar_used = 0;
@@ -105,6 +109,10 @@ constexpr int kZeroRowHalves = 65536 + 64;
 
 /* read and clear the device error word (synchronises the stream) */
 int check_device_errors(Ctx* c);
+/* wait for the context stream: cudaStreamSynchronize, or, on a context with a communicator
+   and a tensor-parallel timeout, the bounded wait of watchdog.h (aborting the communicator
+   when a peer never answers) */
+int sync_stream(Ctx* c);
 
 /* tracked device allocation */
 int dev_alloc(Ctx* c, void** p, size_t bytes);

@@ -61,6 +61,8 @@ _SIGS = {
     "ulb_event_destroy": (C.c_int, [P]),
     "ulb_tp_unique_id": (C.c_int, [P]),
     "ulb_tp_init": (C.c_int, [P, C.c_int, C.c_int, P]),
+    "ulb_tp_set_timeout": (C.c_int, [P, C.c_int]),
+    "ulb_wait_flag": (C.c_int, [P, P, C.c_int32, C.c_uint64]),
     "ulb_model_set_tp": (C.c_int, [P, C.c_int, C.c_int]),
     "ulb_capture_begin": (C.c_int, [P]),
     "ulb_capture_end": (C.c_int, [P, C.POINTER(P)]),
