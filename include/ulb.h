@@ -181,6 +181,22 @@ ULB_API int ulb_attention(ulb_ctx* ctx, const ulb_attn_desc* desc, const float* 
                   const int32_t* dev_row_pos, int M, int rows_per_seq, uint16_t* dev_out);
 
 /*
+ * ulb_attention over a paged KV cache, the layout the model caches use.  A sequence's
+ * positions map to pages of ULB_KV_PAGE positions through its row of the block table:
+ *   dev_k_pool/dev_v_pool  fp16 [n_pages][n_head_kv][ULB_KV_PAGE][head_dim]
+ *   dev_block_table        int32 [n_seq][max_pages]: page of positions [j*ULB_KV_PAGE, (j+1)*ULB_KV_PAGE)
+ *                          of sequence s at [s*max_pages + j], -1 = unmapped (those keys are
+ *                          treated as absent; nothing is read there)
+ * desc->capacity <= max_pages * ULB_KV_PAGE.  Everything else as ulb_attention.  Replaces the
+ * reference's KVCache::retrieve over one flat host array per layer (src/inference/model.h:49-77).
+ */
+#define ULB_KV_PAGE 256
+ULB_API int ulb_attention_paged(ulb_ctx* ctx, const ulb_attn_desc* desc, const float* dev_q,
+                        const uint16_t* dev_k_pool, const uint16_t* dev_v_pool, const int32_t* dev_block_table,
+                        int max_pages, const int32_t* dev_row_seq, const int32_t* dev_row_pos, int M,
+                        int rows_per_seq, uint16_t* dev_out);
+
+/*
  * ulb_attention without any device allocation.  This entry point has no counterpart in the
  * reference.  It is for callers that must not call cudaMalloc / cudaFree: code that runs
  * between the kernels of a latency-bound decode step (an allocation can synchronise the
@@ -277,8 +293,19 @@ ULB_API int ulb_model_finalize(ulb_model* m);
 ULB_API int ulb_model_free(ulb_model* m);
 ULB_API int ulb_model_weight_bytes(const ulb_model* m, size_t* out_bytes);
 
-/* KV cache: fp16 [n_layer][n_seq][n_head_kv][capacity][head_dim] for K and for V. */
+/* KV cache, paged: per layer a pool of pages fp16 [page][n_head_kv][ULB_KV_PAGE][head_dim] for K
+ * and for V, and a block table [n_seq][max_pages] mapping each sequence's positions to pages
+ * (replaces the reference's KVCache of one host array per layer, src/inference/model.h:49-77,
+ * model.cpp:11-131).  ulb_kv_alloc gives every sequence the pages of its whole capacity
+ * (identity table).  ulb_kv_alloc_paged makes a pool of n_pages pages shared by n_seq
+ * sequences of at most max_pages_per_seq pages each, all unmapped; ulb_kv_map then maps
+ * pages [first, first + n) of sequence seq (page ids, -1 = unmap) -- enqueued on the context
+ * stream, so kernels after it see the new mapping.  Keys on unmapped pages are absent to the
+ * attention and K / V rows for them are not written. */
 ULB_API int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* m, int n_seq, int capacity, ulb_kv** out);
+ULB_API int ulb_kv_alloc_paged(ulb_ctx* ctx, const ulb_model* m, int n_seq, int n_pages, int max_pages_per_seq,
+                               ulb_kv** out);
+ULB_API int ulb_kv_map(ulb_kv* kv, int seq, int first, int n, const int32_t* host_pages);
 ULB_API int ulb_kv_free(ulb_kv* kv);
 
 /*
@@ -307,6 +334,9 @@ typedef struct ulb_spec_desc {
   ulb_warp warp;    /* applied identically to target and draft               */
   uint64_t seed;    /* Philox key                                           */
   int use_graphs;   /* 1: capture each round into a CUDA graph              */
+  int kv_pages;     /* 0: every sequence slot owns pages for its whole capacity;
+                       > 0: a pool of this many pages per model, mapped to the slots
+                       as their sequences grow and returned when they finish     */
 } ulb_spec_desc;
 
 ULB_API int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft,
@@ -316,6 +346,17 @@ ULB_API int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft,
 ULB_API int ulb_spec_prefill(ulb_spec* s, const int32_t* host_prompts, const int32_t* host_prompt_lens);
 /* Run rounds until every sequence has max_new tokens or max_rounds rounds ran. */
 ULB_API int ulb_spec_run(ulb_spec* s, int max_rounds, int* out_rounds);
+/*
+ * Continuous batching: start a new sequence in slot `slot` (0..n_seq-1) once its previous one
+ * is done (ULB_EINVAL while it is still decoding): the prompt (host int32, len <= max_prompt)
+ * is prefilled into both caches -- on pages taken from the pool when kv_pages > 0 -- and its
+ * first token committed; the next ulb_spec_run rounds decode it with the other live slots.
+ * Read the finished sequence's tokens (ulb_spec_read) before admitting a new one.  The slot's
+ * Philox stream restarts at round 0 (sampled decoding of successive occupants of one slot
+ * draws the same uniforms).  Replaces ContinuousBatcher's queue -> padded batch stub
+ * (src/inference/continuous_batcher.cpp:20-122), which never reached a model.
+ */
+ULB_API int ulb_spec_admit(ulb_spec* s, int slot, const int32_t* host_prompt, int len);
 /* host_tokens int32 [n_seq][max_new], host_counts [n_seq];
  * stats: [0] rounds, [1] drafted tokens, [2] accepted drafts, [3] committed tokens. */
 ULB_API int ulb_spec_read(ulb_spec* s, int32_t* host_tokens, int32_t* host_counts, uint64_t stats[4]);

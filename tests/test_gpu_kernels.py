@@ -216,6 +216,50 @@ def test_attention_matches_oracle(ctx, H, Hkv, hd, S, rps, positions):
     assert np.abs(got - want).max() < 2e-3
 
 
+@pytest.mark.parametrize("H,Hkv,hd,S,rps,positions", [
+    (32, 32, 128, 1, 6, [[639, 640, 641, 642, 643, 644]]),                      # 7B verify rows, 3 pages
+    (32, 4, 64, 3, 2, [[700, 701], [30, 31], [1500, 1501]]),                     # draft rows, ragged
+    (32, 8, 128, 2, 9, [list(range(2300, 2309)), list(range(4000, 4009))]),      # > 8 splits: global merge
+])
+def test_paged_attention_matches_oracle(ctx, H, Hkv, hd, S, rps, positions):
+    """ulb_attention_paged: the same keys as a contiguous cache, scattered over a shuffled pool
+    of 256-position pages through the block table (pages past a sequence's last position left
+    unmapped), give the oracle's attention."""
+    import ulb_capi as U
+    rng = np.random.default_rng(hd + S + 100)
+    PAGE = 256
+    cap = max(max(p) for p in positions) + 3
+    maxp = (cap + PAGE - 1) // PAGE
+    M = S * rps
+    q = rng.standard_normal((M, H * hd)).astype(np.float32)
+    k = rng.standard_normal((S, Hkv, maxp * PAGE, hd)).astype(np.float16)
+    v = rng.standard_normal((S, Hkv, maxp * PAGE, hd)).astype(np.float16)
+    row_seq = np.repeat(np.arange(S, dtype=np.int32), rps)
+    row_pos = np.concatenate([np.asarray(p, np.int32) for p in positions])
+    want = orc.attention(H, Hkv, hd, maxp * PAGE, 1.0 / np.sqrt(hd), q, k.view(np.uint16), v.view(np.uint16),
+                         row_seq, row_pos)
+    n_pages = S * maxp + 3
+    perm = rng.permutation(n_pages)
+    table = np.full((S, maxp), -1, np.int32)
+    kp = np.zeros((n_pages, Hkv, PAGE, hd), np.float16)
+    vp = np.zeros((n_pages, Hkv, PAGE, hd), np.float16)
+    for s in range(S):
+        for j in range(max(positions[s]) // PAGE + 1):
+            pg = perm[s * maxp + j]
+            table[s, j] = pg
+            kp[pg] = k[s, :, j * PAGE:(j + 1) * PAGE]
+            vp[pg] = v[s, :, j * PAGE:(j + 1) * PAGE]
+    bufs = [ctx.buffer(a) for a in (q, kp, vp, table, row_seq, row_pos)]
+    out = ctx.buffer(nbytes=M * H * hd * 2)
+    d = U.AttnDesc(H, Hkv, hd, cap, S, 1.0 / np.sqrt(hd))
+    U.check(U.lib().ulb_attention_paged(ctx.h, C.byref(d), bufs[0].ptr, bufs[1].ptr, bufs[2].ptr, bufs[3].ptr, maxp,
+                                        bufs[4].ptr, bufs[5].ptr, M, rps, out.ptr))
+    got = out.download(np.float16, (M, H * hd)).astype(np.float32)
+    for b in bufs + [out]:
+        b.free()
+    assert np.abs(got - want.astype(np.float32)).max() < 2e-3
+
+
 def _sample_gpu(ctx, logits, warp, seed, rnd, slot, tag):
     import ulb_capi as U
     rows, V = logits.shape

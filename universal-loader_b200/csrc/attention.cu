@@ -44,7 +44,10 @@ constexpr float kLog2e = 1.44269504088896340736f;
 struct AttnParams {
   int H, Hkv, hd, cap, G, rps, n_mt, max_splits, ldq, n_seq, n_groups;
   float scale2; /* softmax scale x log2(e): scores live in the base-2 domain */
+  const int* bt; /* block table of a paged cache (one page = one key split), or NULL */
+  int max_pages;
 };
+static_assert(SPLITK == kKvPage, "a key split is one KV cache page");
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -163,14 +166,24 @@ __global__ void __launch_bounds__(AW * 32, 1)
   }
 
   const int kb0 = (split * AW + warp) * KB;
-  const int nk = min(KB, last_pos + 1 - kb0); /* keys of this warp's block (may be <= 0) */
+  /* the cache rows of this split: contiguous [S][Hkv][cap][hd], or page bt[seq][split] of the
+     pool [page][Hkv][kKvPage][hd] (an unmapped page holds no keys: the split is masked out) */
+  size_t kvoff;
+  int page_ok = 1;
+  if (p.bt) {
+    const int page = p.bt[(size_t)seq * p.max_pages + split];
+    page_ok = page >= 0;
+    kvoff = (((size_t)max(page, 0) * p.Hkv + kvh) * kKvPage + warp * KB) * HD;
+  } else {
+    kvoff = (((size_t)seq * p.Hkv + kvh) * p.cap + max(kb0, 0)) * HD;
+  }
+  const int nk = page_ok ? min(KB, last_pos + 1 - kb0) : 0; /* keys of this warp's block (may be <= 0) */
   float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
   float o[DN][4];
 #pragma unroll
   for (int d = 0; d < DN; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
   __half* Ks = reinterpret_cast<__half*>(sm) + (size_t)warp * 2 * KB * HD;
   __half* Vs = Ks + KB * HD;
-  const size_t kvoff = (((size_t)seq * p.Hkv + kvh) * p.cap + max(kb0, 0)) * HD;
   const __half* kg = kc + kvoff;
   const __half* vg = vc + kvoff;
   /* keys [0, n_old) of the block predate this forward, keys [n_old, nk) were just written */
@@ -557,7 +570,8 @@ int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int m
 
 int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, const __half* k,
                      const __half* v, const int* row_seq, const int* row_pos, int M, int rps,
-                     __half* out, float* scratch, int* counters, size_t scratch_floats, int n_counters) {
+                     __half* out, float* scratch, int* counters, size_t scratch_floats, int n_counters,
+                     const int* bt, int max_pages) {
   ULB_TRY(validate_attn_desc(d, M, rps));
   ULB_CHECK(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 && ldq % 4 == 0,
             ULB_EINVAL, "attention: q / k / v must be 16-byte aligned (ldq a multiple of 4)");
@@ -566,6 +580,10 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
   int ng;
   attn_geometry(d, M, rps, d->capacity - 1, &p, &ng);
   p.ldq = ldq;
+  p.bt = bt;
+  p.max_pages = max_pages;
+  ULB_CHECK(!bt || (long long)max_pages * kKvPage >= d->capacity, ULB_EINVAL,
+            "attention: %d pages of %d positions per sequence cannot hold capacity %d", max_pages, kKvPage, d->capacity);
   int need_c = 0;
   size_t need = 0;
   ULB_TRY(attention_scratch_need(c, d, M, rps, d->capacity - 1, &need, &need_c));
@@ -647,6 +665,36 @@ extern "C" int ulb_attention_noalloc(ulb_ctx* ctx, const ulb_attn_desc* d, const
   if (nc > 0) ULB_CUDA(cudaMemsetAsync(counters, 0, (size_t)nc * sizeof(int), c->stream));
   return launch_attention(c, d, q, d->n_head * d->head_dim, (const __half*)k, (const __half*)v, row_seq, row_pos, M,
                           rps, (__half*)out, scratch, counters, kNoAllocScratchFloats, kNoAllocCounters);
+}
+
+extern "C" int ulb_attention_paged(ulb_ctx* ctx, const ulb_attn_desc* d, const float* q, const uint16_t* k_pool,
+                                   const uint16_t* v_pool, const int32_t* block_table, int max_pages,
+                                   const int32_t* row_seq, const int32_t* row_pos, int M, int rps, uint16_t* out) {
+  ULB_CHECK(ctx && d && q && k_pool && v_pool && block_table && row_seq && row_pos && out, ULB_EINVAL,
+            "ulb_attention_paged: NULL argument");
+  ULB_TRY(validate_attn_desc(d, M, rps));
+  ULB_CHECK(max_pages > 0 && (long long)max_pages * kKvPage >= d->capacity, ULB_EINVAL,
+            "ulb_attention_paged: %d pages of %d positions per sequence, capacity %d", max_pages, kKvPage, d->capacity);
+  Ctx* c = &ctx->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  int nc = 0;
+  size_t nf = 0;
+  ULB_TRY(attention_scratch_need(c, d, M, rps, d->capacity - 1, &nf, &nc));
+  float* scratch = nullptr;
+  int* counters = nullptr;
+  ULB_TRY(dev_alloc(c, (void**)&scratch, nf * sizeof(float)));
+  int rc = dev_alloc(c, (void**)&counters, (size_t)nc * sizeof(int));
+  if (rc == ULB_OK) {
+    cudaError_t e = nc > 0 ? cudaMemsetAsync(counters, 0, (size_t)nc * sizeof(int), c->stream) : cudaSuccess;
+    rc = e == cudaSuccess ? launch_attention(c, d, q, d->n_head * d->head_dim, (const __half*)k_pool,
+                                             (const __half*)v_pool, row_seq, row_pos, M, rps, (__half*)out, scratch,
+                                             counters, nf, nc, block_table, max_pages)
+                          : cuda_error(e, "memset", __FILE__, __LINE__);
+  }
+  if (rc == ULB_OK) rc = check_device_errors(c);
+  dev_free(c, counters, (size_t)nc * sizeof(int));
+  dev_free(c, scratch, nf * sizeof(float));
+  return rc;
 }
 
 extern "C" int ulb_attention(ulb_ctx* ctx, const ulb_attn_desc* d, const float* q, const uint16_t* k,

@@ -349,6 +349,7 @@ class InferenceAPI {
     d["h2d_bytes"] = last_.h2d_bytes;
     d["d2h_bytes"] = last_.d2h_bytes;
     d["launches"] = last_.launches;
+    d["admitted"] = last_.admitted;
     d["speculative"] = last_spec_;
     return d;
   }
@@ -443,6 +444,7 @@ class InferenceAPI {
     p.seed = cfg.seed ? cfg.seed : config_.seed;
     const bool spec = spec_enabled_ && engine_->has_model(true) && spec_k_ > 0;
     p.k = spec ? spec_k_ : 0;
+    p.max_batch = (int)max_batch_;
     last_spec_ = spec;
     return engine_->generate(in, p, out, &last_);
   }

@@ -138,8 +138,10 @@ bool Engine::generate(const std::vector<std::vector<int32_t>>& prompts, const Ge
     max_prompt = std::max(max_prompt, (int)pr.size());
   }
   const bool use_draft = draft_ != nullptr && p.k > 0;
+  const int n_prompts = (int)prompts.size();
+  const bool continuous = p.max_batch > 0 && n_prompts > p.max_batch;
   ulb_spec_desc sd{};
-  sd.n_seq = (int)prompts.size();
+  sd.n_seq = continuous ? p.max_batch : n_prompts;
   sd.k = use_draft ? p.k : 0;
   sd.max_prompt = max_prompt;
   sd.max_new = (int)p.max_new;
@@ -148,6 +150,13 @@ bool Engine::generate(const std::vector<std::vector<int32_t>>& prompts, const Ge
   sd.warp.top_p = p.top_p;
   sd.seed = p.seed;
   sd.use_graphs = p.use_graphs ? 1 : 0;
+  sd.kv_pages = p.kv_pages;
+  if (continuous && sd.kv_pages == 0) {
+    /* the slots share one pool (as much as every slot's capacity): pages follow the live
+       sequences and a finished sequence's pages serve the next prompt */
+    const int cap = max_prompt + (int)p.max_new + 2 * sd.k + 2;
+    sd.kv_pages = sd.n_seq * ((cap + ULB_KV_PAGE - 1) / ULB_KV_PAGE);
+  }
   const bool same = spec_ && spec_has_draft_ == use_draft && !memcmp(&sd, &spec_desc_, sizeof sd);
   if (!same) {
     drop_spec();
@@ -171,12 +180,55 @@ bool Engine::generate(const std::vector<std::vector<int32_t>>& prompts, const Ge
   int rc = ulb_spec_prefill(spec_, flat.data(), lens.data());
   ulb_event_record(ctx_, e1);
   int rounds = 0;
-  if (rc == ULB_OK) rc = ulb_spec_run(spec_, 0, &rounds);
-  ulb_event_record(ctx_, e2);
   std::vector<int32_t> toks((size_t)sd.n_seq * sd.max_new), counts(sd.n_seq);
-  uint64_t stats[4] = {0, 0, 0, 0}, launches = 0;
+  uint64_t stats[4] = {0, 0, 0, 0}, launches = 0, admitted = 0;
+  /* slot -> prompt it decodes (-1: idle); prompts beyond the slots wait for a finished one */
+  std::vector<int> slot_of(sd.n_seq);
+  for (int s = 0; s < sd.n_seq; ++s) slot_of[s] = s;
+  int next = sd.n_seq;
+  std::vector<std::vector<int32_t>> done_out(n_prompts);
+  uint64_t run_rounds = 0;
+  const int R = sd.k + 1;
+  while (rc == ULB_OK) {
+    if (!continuous) {
+      rc = ulb_spec_run(spec_, 0, &rounds);
+      break;
+    }
+    /* run until the first live slot can have finished, then hand its slot to the next prompt */
+    rc = ulb_spec_read(spec_, toks.data(), counts.data(), stats);
+    if (rc != ULB_OK) break;
+    int min_rem = -1;
+    bool any = false;
+    for (int s = 0; s < sd.n_seq && rc == ULB_OK; ++s) {
+      if (slot_of[s] < 0) continue;
+      if (counts[s] >= sd.max_new) {
+        done_out[slot_of[s]].assign(toks.begin() + (size_t)s * sd.max_new, toks.begin() + (size_t)(s + 1) * sd.max_new);
+        slot_of[s] = -1;
+        if (next < n_prompts) {
+          rc = ulb_spec_admit(spec_, s, prompts[next].data(), (int)prompts[next].size());
+          slot_of[s] = next++;
+          ++admitted;
+        }
+      }
+      if (slot_of[s] >= 0) {
+        any = true;
+        const int rem = sd.max_new - (slot_of[s] >= 0 && counts[s] < sd.max_new ? counts[s] : 1);
+        if (min_rem < 0 || rem < min_rem) min_rem = rem;
+      }
+    }
+    if (rc != ULB_OK || !any) break;
+    int ran = 0;
+    rc = ulb_spec_run(spec_, std::max(1, (min_rem + R - 1) / R), &ran);
+    run_rounds += (uint64_t)ran;
+  }
+  ulb_event_record(ctx_, e2);
   if (rc == ULB_OK) rc = ulb_spec_read(spec_, toks.data(), counts.data(), stats);
   if (rc == ULB_OK) rc = ulb_spec_launch_count(spec_, &launches);
+  if (rc == ULB_OK && continuous) {
+    /* stats[0] is the most rounds any slot was live since its start: count every run instead */
+    stats[0] = run_rounds;
+    rounds = (int)run_rounds;
+  }
   float pms = 0, dms = 0;
   if (rc == ULB_OK) {
     ulb_event_elapsed_ms(e0, e1, &pms);
@@ -191,9 +243,16 @@ bool Engine::generate(const std::vector<std::vector<int32_t>>& prompts, const Ge
     return fail(msg);
   }
   uint64_t gen = 0;
-  for (int s = 0; s < sd.n_seq; ++s) {
-    (*out)[s].assign(toks.begin() + (size_t)s * sd.max_new, toks.begin() + (size_t)s * sd.max_new + counts[s]);
-    gen += (uint64_t)counts[s];
+  if (continuous) {
+    for (int i = 0; i < n_prompts; ++i) {
+      (*out)[i] = std::move(done_out[i]);
+      gen += (*out)[i].size();
+    }
+  } else {
+    for (int s = 0; s < sd.n_seq; ++s) {
+      (*out)[s].assign(toks.begin() + (size_t)s * sd.max_new, toks.begin() + (size_t)s * sd.max_new + counts[s]);
+      gen += (uint64_t)counts[s];
+    }
   }
   if (st) {
     st->rounds = stats[0];
@@ -207,6 +266,7 @@ bool Engine::generate(const std::vector<std::vector<int32_t>>& prompts, const Ge
     st->h2d_bytes = (double)(flat.size() + lens.size()) * 4.0;
     st->d2h_bytes = (double)(toks.size() + counts.size()) * 4.0;
     st->launches = launches;
+    st->admitted = admitted;
   }
   return true;
 }

@@ -33,6 +33,11 @@ struct GenParams {
   uint64_t seed = 0;
   int k = 0;              /* speculation length; 0 = plain decoding */
   bool use_graphs = true;
+  /* continuous batching: at most this many sequences decode at once (0 = all of them); with
+     more prompts than that, a finished sequence's slot is given to the next prompt */
+  int max_batch = 0;
+  /* KV cache pages per model (0: every slot owns its whole capacity; otherwise on demand) */
+  int kv_pages = 0;
 };
 
 /* One round of the speculative loop for one sequence, as the reference's SpeculationResult
@@ -55,6 +60,7 @@ struct GenStats {
   double prefill_ms = 0, decode_ms = 0, total_ms = 0;
   double h2d_bytes = 0, d2h_bytes = 0;
   uint64_t launches = 0; /* kernels launched by the library for this generation */
+  uint64_t admitted = 0; /* sequences started in a freed slot (continuous batching) */
 };
 
 class Engine {

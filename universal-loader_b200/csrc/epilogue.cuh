@@ -39,6 +39,23 @@ __device__ __forceinline__ void epilogue_token(const EpiArgs& e, int strip, int 
     const int pos = e.row_pos[tok];
     const int seq = e.row_seq[tok];
     if ((unsigned)pos >= (unsigned)e.cap || (unsigned)seq >= (unsigned)e.n_seq) return; /* never write outside the cache */
+    /* the cache row of (seq, kv head, pos): contiguous [S][Hkv][cap][hd], or page pool
+       [page][Hkv][kKvPage][hd] through the block table (an unmapped page is never written) */
+    size_t sbase, pstride;
+    int prow;
+    bool kv_ok = true;
+    if (e.bt) {
+      const int page = e.bt[(size_t)seq * e.max_pages + pos / kKvPage];
+      kv_ok = page >= 0;
+      sbase = (size_t)(kv_ok ? page : 0) * e.n_head_kv;
+      pstride = kKvPage;
+      prow = pos % kKvPage;
+    } else {
+      sbase = (size_t)seq * e.n_head_kv;
+      pstride = (size_t)e.cap;
+      prow = pos;
+    }
+    auto row_at = [&](int kvh) { return ((sbase + kvh) * pstride + prow) * e.hd; };
     if (f0 < e.nq + e.nkv) {
       /* RoPE-permuted strip: row g = feature f0 + 2g, row g + 8 = feature f0 + 2g + 1 */
       const int f = f0 + 2 * g;
@@ -50,19 +67,19 @@ __device__ __forceinline__ void epilogue_token(const EpiArgs& e, int strip, int 
         float* q = e.q + (size_t)tok * e.ldq + f;
         q[0] = y0;
         q[1] = y1;
-      } else {
+      } else if (kv_ok) {
         const int fk = f - e.nq, kvh = fk / e.hd, d = fk % e.hd;
-        __half2* kp = reinterpret_cast<__half2*>(e.kc + (((size_t)seq * e.n_head_kv + kvh) * e.cap + pos) * e.hd + d);
+        __half2* kp = reinterpret_cast<__half2*>(e.kc + row_at(kvh) + d);
         *kp = __halves2half2(__float2half_rn(y0), __float2half_rn(y1));
       }
-    } else {
+    } else if (kv_ok) {
       /* V strip, identity rows */
       const float vals[2] = {vg, vg8};
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int fv = f0 + g + 8 * i - e.nq - e.nkv;
         const int kvh = fv / e.hd, d = fv % e.hd;
-        e.vc[(((size_t)seq * e.n_head_kv + kvh) * e.cap + pos) * e.hd + d] = __float2half_rn(vals[i]);
+        e.vc[row_at(kvh) + d] = __float2half_rn(vals[i]);
       }
     }
   }

@@ -64,6 +64,11 @@ struct Model {
 struct KV {
   Model* m = nullptr;
   int n_seq = 0, cap = 0;
+  /* paged: per layer a pool of n_pages pages [page][n_head_kv][kKvPage][head_dim] for K and
+     for V; sequence s's position p lives in page bt[s * max_pages + p / kKvPage] */
+  int n_pages = 0, max_pages = 0;
+  int* bt = nullptr;
+  std::vector<int> h_bt;
   __half* k = nullptr;
   __half* v = nullptr;
   size_t layer_elems = 0;
@@ -289,6 +294,7 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     a.q = m->qb; a.ldq = m->nq; a.kc = kc; a.vc = vc;
     a.nq = m->nq; a.nkv = m->nkv; a.hd = d.head_dim; a.cap = kv->cap; a.n_head_kv = d.n_head_kv; a.n_seq = kv->n_seq;
     a.row_seq = seq; a.row_pos = pos; a.rope = kv->rope;
+    a.bt = kv->bt; a.max_pages = kv->max_pages;
     /* GEMV tails prefetch the weights of the GEMVs to come into L2 (the hint is set just
        before the launch whose tail issues it) */
     auto hint = [c](const Tensor* t, const Tensor* t2 = nullptr) {
@@ -302,7 +308,7 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     hint(&L.o, &L.gateup);
     ULB_TRY(launch_qgemv_rms(c, &L.qkv, m->x, d.d_model, L.attn_norm, d.rms_eps, m->x16, M, EPI_QKV, a));
     ULB_TRY(launch_attention(c, &ad, m->qb, m->nq, kc, vc, seq, pos, M, rps, m->att, kv->attn_scratch,
-                             kv->attn_counters, kv->attn_floats, kv->n_counters));
+                             kv->attn_counters, kv->attn_floats, kv->n_counters, kv->bt, kv->max_pages));
     EpiArgs r;
     r.y = m->x; r.ldy = d.d_model;
     /* tensor parallel: this rank's heads / features give a partial sum of attn_output and
@@ -684,9 +690,10 @@ int ulb_model_weight_bytes(const ulb_model* mm, size_t* out) {
   return ULB_OK;
 }
 
-int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* mm, int n_seq, int cap, ulb_kv** out) {
-  ULB_CHECK(ctx && mm && out, ULB_EINVAL, "ulb_kv_alloc: NULL argument");
-  ULB_CHECK(n_seq > 0 && cap > 0, ULB_EINVAL, "ulb_kv_alloc: n_seq %d cap %d", n_seq, cap);
+/* a paged cache of n_pages pages for n_seq sequences of at most max_pages pages each, with
+   the block table given (host, n_seq * max_pages entries, -1 = unmapped) or identity */
+static int kv_create(ulb_ctx* ctx, const ulb_model* mm, int n_seq, int cap, int n_pages, int max_pages,
+                     const int* table, ulb_kv** out) {
   Ctx* c = &ctx->c;
   ULB_CUDA(cudaSetDevice(c->device));
   std::unique_ptr<ulb_kv> kvh(new ulb_kv());
@@ -695,12 +702,26 @@ int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* mm, int n_seq, int cap, ulb_kv**
   const ulb_model_desc& d = mm->m.d;
   kv->n_seq = n_seq;
   kv->cap = cap;
-  kv->layer_elems = (size_t)n_seq * d.n_head_kv * cap * d.head_dim;
+  kv->n_pages = n_pages;
+  kv->max_pages = max_pages;
+  kv->h_bt.assign(table, table + (size_t)n_seq * max_pages);
+  kv->layer_elems = (size_t)n_pages * d.n_head_kv * kKvPage * d.head_dim;
   kv->bytes = kv->layer_elems * d.n_layer * 2;
-  ULB_TRY(dev_alloc(c, (void**)&kv->k, kv->bytes));
-  ULB_TRY(dev_alloc(c, (void**)&kv->v, kv->bytes));
-  ULB_CUDA(cudaMemsetAsync(kv->k, 0, kv->bytes, c->stream));
-  ULB_CUDA(cudaMemsetAsync(kv->v, 0, kv->bytes, c->stream));
+  auto fail = [&](int rc) {
+    dev_free(c, kv->k, kv->bytes);
+    dev_free(c, kv->v, kv->bytes);
+    dev_free(c, kv->bt, kv->h_bt.size() * 4);
+    dev_free(c, kv->rope, kv->rope_bytes);
+    return rc;
+  };
+  int rc;
+  if ((rc = dev_alloc(c, (void**)&kv->k, kv->bytes)) || (rc = dev_alloc(c, (void**)&kv->v, kv->bytes)) ||
+      (rc = dev_alloc(c, (void**)&kv->bt, kv->h_bt.size() * 4)))
+    return fail(rc);
+  if (cudaMemsetAsync(kv->k, 0, kv->bytes, c->stream) != cudaSuccess ||
+      cudaMemsetAsync(kv->v, 0, kv->bytes, c->stream) != cudaSuccess ||
+      cudaMemcpyAsync(kv->bt, kv->h_bt.data(), kv->h_bt.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+    return fail(cuda_error(cudaGetLastError(), "kv init", __FILE__, __LINE__));
   /* RoPE table: theta = pos * base^(-2i/hd) in fp64, cos/sin rounded to fp32 */
   const int half = d.head_dim / 2;
   std::vector<float2> tab((size_t)cap * half);
@@ -710,10 +731,50 @@ int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* mm, int n_seq, int cap, ulb_kv**
       tab[(size_t)p * half + i] = make_float2((float)std::cos(th), (float)std::sin(th));
     }
   kv->rope_bytes = tab.size() * sizeof(float2);
-  ULB_TRY(dev_alloc(c, (void**)&kv->rope, kv->rope_bytes));
-  ULB_CUDA(cudaMemcpyAsync(kv->rope, tab.data(), kv->rope_bytes, cudaMemcpyHostToDevice, c->stream));
-  ULB_CUDA(cudaStreamSynchronize(c->stream));
+  if ((rc = dev_alloc(c, (void**)&kv->rope, kv->rope_bytes))) return fail(rc);
+  if (cudaMemcpyAsync(kv->rope, tab.data(), kv->rope_bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+      cudaStreamSynchronize(c->stream) != cudaSuccess)
+    return fail(cuda_error(cudaGetLastError(), "kv init", __FILE__, __LINE__));
   *out = kvh.release();
+  return ULB_OK;
+}
+
+int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* mm, int n_seq, int cap, ulb_kv** out) {
+  ULB_CHECK(ctx && mm && out, ULB_EINVAL, "ulb_kv_alloc: NULL argument");
+  ULB_CHECK(n_seq > 0 && cap > 0, ULB_EINVAL, "ulb_kv_alloc: n_seq %d cap %d", n_seq, cap);
+  /* every sequence owns the pages of its whole capacity: identity block table */
+  const int pps = (cap + kKvPage - 1) / kKvPage;
+  ULB_CHECK((long long)n_seq * pps < (1ll << 31), ULB_EINVAL, "ulb_kv_alloc: too many pages");
+  std::vector<int> table((size_t)n_seq * pps);
+  for (size_t i = 0; i < table.size(); ++i) table[i] = (int)i;
+  return kv_create(ctx, mm, n_seq, cap, n_seq * pps, pps, table.data(), out);
+}
+
+int ulb_kv_alloc_paged(ulb_ctx* ctx, const ulb_model* mm, int n_seq, int n_pages, int max_pages_per_seq,
+                       ulb_kv** out) {
+  ULB_CHECK(ctx && mm && out, ULB_EINVAL, "ulb_kv_alloc_paged: NULL argument");
+  ULB_CHECK(n_seq > 0 && n_pages > 0 && max_pages_per_seq > 0, ULB_EINVAL,
+            "ulb_kv_alloc_paged: n_seq %d n_pages %d max_pages %d", n_seq, n_pages, max_pages_per_seq);
+  ULB_CHECK((long long)max_pages_per_seq * kKvPage <= 8192, ULB_EUNSUPPORTED,
+            "ulb_kv_alloc_paged: %d pages of %d positions exceed the attention's 8192", max_pages_per_seq, kKvPage);
+  std::vector<int> table((size_t)n_seq * max_pages_per_seq, -1);
+  return kv_create(ctx, mm, n_seq, max_pages_per_seq * kKvPage, n_pages, max_pages_per_seq, table.data(), out);
+}
+
+int ulb_kv_map(ulb_kv* kvh, int seq, int first, int n, const int32_t* pages) {
+  ULB_CHECK(kvh && (n == 0 || pages), ULB_EINVAL, "ulb_kv_map: NULL argument");
+  KV* kv = &kvh->kv;
+  ULB_CHECK(seq >= 0 && seq < kv->n_seq && first >= 0 && n >= 0 && first + n <= kv->max_pages, ULB_EINVAL,
+            "ulb_kv_map: sequence %d pages [%d, %d) of %d", seq, first, first + n, kv->max_pages);
+  for (int i = 0; i < n; ++i)
+    ULB_CHECK(pages[i] >= -1 && pages[i] < kv->n_pages, ULB_EINVAL, "ulb_kv_map: page %d of %d", pages[i], kv->n_pages);
+  if (n == 0) return ULB_OK;
+  int* row = kv->h_bt.data() + (size_t)seq * kv->max_pages + first;
+  memcpy(row, pages, (size_t)n * 4);
+  Ctx* c = kv->m->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  ULB_CUDA(cudaMemcpyAsync(kv->bt + (size_t)seq * kv->max_pages + first, row, (size_t)n * 4, cudaMemcpyHostToDevice,
+                           c->stream));
   return ULB_OK;
 }
 
@@ -724,6 +785,7 @@ int ulb_kv_free(ulb_kv* kvh) {
   cudaSetDevice(c->device);
   dev_free(c, kv->k, kv->bytes);
   dev_free(c, kv->v, kv->bytes);
+  dev_free(c, kv->bt, kv->h_bt.size() * 4);
   dev_free(c, kv->rope, kv->rope_bytes);
   dev_free(c, kv->attn_scratch, kv->attn_floats * 4);
   dev_free(c, kv->attn_counters, (size_t)kv->n_counters * 4);

@@ -22,6 +22,7 @@
 #include <cstring>
 #include <memory>
 
+#include "paging.h"
 #include "ulb_internal.h"
 
 namespace ulb {
@@ -41,6 +42,8 @@ int launch_accept_commit(Ctx* c, const float* p, const float* q, const int32_t* 
 }  // namespace ulb
 
 extern "C" int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* m, int n_seq, int cap, ulb_kv** out);
+extern "C" int ulb_kv_alloc_paged(ulb_ctx* ctx, const ulb_model* m, int n_seq, int n_pages, int max_pages, ulb_kv** out);
+extern "C" int ulb_kv_map(ulb_kv* kv, int seq, int first, int n, const int32_t* pages);
 extern "C" int ulb_kv_free(ulb_kv* kv);
 
 namespace ulb {
@@ -127,6 +130,8 @@ struct Spec {
   std::vector<int> h_plen;
   cudaGraphExec_t exec = nullptr;
   bool prefilled = false;
+  /* pages of both caches on demand (desc.kv_pages > 0), else every slot owns its capacity */
+  std::unique_ptr<PagePool> pool;
   /* launch accounting */
   uint64_t per_round = 0;   /* kernels in one round (counted while recording it) */
   uint64_t launches = 0;    /* since the last prefill */
@@ -190,6 +195,47 @@ static void spec_release(Spec* sp) {
   cudaStreamSynchronize(c->stream);
 }
 
+/* map pages so slot s covers positions [0, positions) in both caches (paged loop only) */
+static int map_slot(Spec* sp, int s, int positions) {
+  if (!sp->pool) return ULB_OK;
+  int first = 0;
+  std::vector<int> added;
+  if (!sp->pool->ensure(s, std::min(positions, sp->cap), &first, &added))
+    return set_error(ULB_ENOMEM, "KV page pool exhausted: slot %d needs %d positions, %d pages free", s, positions,
+                     sp->pool->free_pages());
+  if (added.empty()) return ULB_OK;
+  ULB_TRY(ulb_kv_map(sp->kvt, s, first, (int)added.size(), added.data()));
+  if (sp->kvd) ULB_TRY(ulb_kv_map(sp->kvd, s, first, (int)added.size(), added.data()));
+  return ULB_OK;
+}
+
+/* return slot s's pages to the pool (its cache rows become unmapped) */
+static int unmap_slot(Spec* sp, int s) {
+  if (!sp->pool || sp->pool->mapped(s) == 0) return ULB_OK;
+  const int n = sp->pool->release(s);
+  std::vector<int> none((size_t)n, -1);
+  ULB_TRY(ulb_kv_map(sp->kvt, s, 0, n, none.data()));
+  if (sp->kvd) ULB_TRY(ulb_kv_map(sp->kvd, s, 0, n, none.data()));
+  return ULB_OK;
+}
+
+/* prompt rows of slot s (already in hist) through both models in chunks, then the slot's first
+   token from the target's last-position logits */
+static int prefill_slot(Spec* sp, int s, int n_total) {
+  Ctx* c = sp->c;
+  const int V = sp->V;
+  for (int c0 = 0; c0 < n_total; c0 += kPrefillChunk) {
+    const int n = std::min(kPrefillChunk, n_total - c0);
+    cudaError_t e = launch_k(c, stage_prefill_kernel, dim3((n + 127) / 128), dim3(128), 0, s, c0, n,
+                             (const int*)sp->hist, sp->hl, sp->rtok, sp->rseq, sp->rpos);
+    if (e != cudaSuccess) return cuda_error(e, "stage_prefill", __FILE__, __LINE__);
+    ULB_TRY(model_forward(sp->tgt, sp->kvt_i, n, n, sp->rtok, sp->rseq, sp->rpos, 1, sp->plog, V, sp->err));
+    if (sp->dft) ULB_TRY(model_forward(sp->dft, sp->kvd_i, n, n, sp->rtok, sp->rseq, sp->rpos, 1, sp->qlog, V, sp->err));
+  }
+  return launch_sample_seq(c, sp->plog, 1, V, V, &sp->d.warp, sp->d.seed, nullptr, 0, 0, ULB_RNG_FIRST, (uint32_t)s,
+                           sp->hist + (size_t)s * sp->hl + n_total, 1);
+}
+
 }  // namespace ulb
 
 struct ulb_spec {
@@ -236,12 +282,19 @@ int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft, const ulb
     spec_release(sp);
     return code;
   };
-  if ((rc = ulb_kv_alloc(ctx, target, S, sp->cap, &sp->kvt))) return fail(rc);
-  sp->kvt_i = kv_of(sp->kvt);
-  if (sp->dft) {
-    if ((rc = ulb_kv_alloc(ctx, draft, S, sp->cap, &sp->kvd))) return fail(rc);
-    sp->kvd_i = kv_of(sp->kvd);
+  if (d->kv_pages > 0) {
+    /* one pool of kv_pages pages per model, mapped to slots as they grow */
+    const int pps = (sp->cap + kKvPage - 1) / kKvPage;
+    ULB_CHECK(pps * kKvPage <= 8192, ULB_EUNSUPPORTED, "ulb_spec_create: capacity %d > 8192 positions", sp->cap);
+    sp->pool.reset(new PagePool(d->kv_pages, S, pps, kKvPage));
+    if ((rc = ulb_kv_alloc_paged(ctx, target, S, d->kv_pages, pps, &sp->kvt))) return fail(rc);
+    if (sp->dft && (rc = ulb_kv_alloc_paged(ctx, draft, S, d->kv_pages, pps, &sp->kvd))) return fail(rc);
+  } else {
+    if ((rc = ulb_kv_alloc(ctx, target, S, sp->cap, &sp->kvt))) return fail(rc);
+    if (sp->dft && (rc = ulb_kv_alloc(ctx, draft, S, sp->cap, &sp->kvd))) return fail(rc);
   }
+  sp->kvt_i = kv_of(sp->kvt);
+  if (sp->dft) sp->kvd_i = kv_of(sp->kvd);
   sp->rows_cap = (size_t)std::max({S * (k + 1), 2 * S, kPrefillChunk});
 #define ALLOC(ptr, bytes) if ((rc = dev_alloc(c, (void**)&(ptr), (bytes)))) return fail(rc)
   ALLOC(sp->hist, (size_t)S * sp->hl * 4);
@@ -300,18 +353,10 @@ int ulb_spec_prefill(ulb_spec* h, const int32_t* prompts, const int32_t* lens) {
   ULB_CUDA(cudaMemsetAsync(sp->err, 0, 4, c->stream));
   const uint64_t launches0 = c->launches;
   for (int s = 0; s < S; ++s) {
-    const int n_total = lens[s];
-    for (int c0 = 0; c0 < n_total; c0 += kPrefillChunk) {
-      const int n = std::min(kPrefillChunk, n_total - c0);
-      cudaError_t e = launch_k(c, stage_prefill_kernel, dim3((n + 127) / 128), dim3(128), 0, s, c0, n,
-                               (const int*)sp->hist, sp->hl, sp->rtok, sp->rseq, sp->rpos);
-      if (e != cudaSuccess) return cuda_error(e, "stage_prefill", __FILE__, __LINE__);
-      ULB_TRY(model_forward(sp->tgt, sp->kvt_i, n, n, sp->rtok, sp->rseq, sp->rpos, 1, sp->plog, V, sp->err));
-      if (sp->dft)
-        ULB_TRY(model_forward(sp->dft, sp->kvd_i, n, n, sp->rtok, sp->rseq, sp->rpos, 1, sp->qlog, V, sp->err));
-    }
-    ULB_TRY(launch_sample_seq(c, sp->plog, 1, V, V, &sp->d.warp, sp->d.seed, nullptr, 0, 0, ULB_RNG_FIRST,
-                              (uint32_t)s, sp->hist + (size_t)s * sp->hl + n_total, 1));
+    /* pages for the prompt and the first round (it writes positions up to lens + k) */
+    ULB_TRY(unmap_slot(sp, s));
+    ULB_TRY(map_slot(sp, s, lens[s] + sp->k + 1));
+    ULB_TRY(prefill_slot(sp, s, lens[s]));
   }
   std::vector<int32_t> L(S), done(S);
   for (int s = 0; s < S; ++s) {
@@ -356,6 +401,21 @@ int ulb_spec_run(ulb_spec* h, int max_rounds, int* out_rounds) {
     /* every sequence commits at most k+1 tokens a round: this many rounds are all needed */
     int r = std::max(1, (rem_max + R - 1) / R);
     if (max_rounds > 0) r = std::min(r, max_rounds - ran);
+    if (sp->pool) {
+      /* finished slots give their pages back; live ones get pages for the positions the next
+         r rounds can write (each commits at most k + 1 and writes up to L + k), or for one
+         round when the pool is short */
+      for (int s = 0; s < S; ++s)
+        if (sp->h_done[s]) ULB_TRY(unmap_slot(sp, s));
+      for (int attempt = 0;; ++attempt) {
+        int rc = ULB_OK;
+        for (int s = 0; s < S && rc == ULB_OK; ++s)
+          if (!sp->h_done[s]) rc = map_slot(sp, s, sp->h_L[s] + r * R + sp->k + 1);
+        if (rc == ULB_OK) break;
+        if (r == 1 || attempt > 0) return rc;
+        r = 1;
+      }
+    }
     for (int i = 0; i < r; ++i) {
       if (sp->exec) ULB_CUDA(cudaGraphLaunch(sp->exec, c->stream));
       else ULB_TRY(record_round(sp));
@@ -399,6 +459,41 @@ int ulb_spec_read(ulb_spec* h, int32_t* tokens, int32_t* counts, uint64_t stats[
     stats[2] = st[2];
     stats[3] = st[3];
   }
+  return ULB_OK;
+}
+
+int ulb_spec_admit(ulb_spec* h, int slot, const int32_t* prompt, int len) {
+  ULB_CHECK(h && prompt, ULB_EINVAL, "ulb_spec_admit: NULL argument");
+  Spec* sp = &h->s;
+  ULB_CHECK(sp->prefilled, ULB_EINVAL, "ulb_spec_admit: call ulb_spec_prefill first");
+  ULB_CHECK(slot >= 0 && slot < sp->S, ULB_EINVAL, "ulb_spec_admit: slot %d of %d", slot, sp->S);
+  ULB_CHECK(len >= 1 && len <= sp->d.max_prompt, ULB_EINVAL, "ulb_spec_admit: prompt length %d outside [1, %d]", len,
+            sp->d.max_prompt);
+  for (int i = 0; i < len; ++i)
+    ULB_CHECK(prompt[i] >= 0 && prompt[i] < sp->V, ULB_EINVAL, "ulb_spec_admit: token %d = %d outside the vocabulary",
+              i, prompt[i]);
+  Ctx* c = sp->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  int32_t done = 0;
+  ULB_CUDA(cudaMemcpyAsync(&done, sp->done + slot, 4, cudaMemcpyDeviceToHost, c->stream));
+  ULB_TRY(sync_stream(c));
+  ULB_CHECK(done, ULB_EINVAL, "ulb_spec_admit: slot %d is still decoding", slot);
+  /* the slot starts over: its pages, prompt, lengths and counters */
+  ULB_TRY(unmap_slot(sp, slot));
+  ULB_TRY(map_slot(sp, slot, len + sp->k + 1));
+  const int32_t zero = 0;
+  ULB_CUDA(cudaMemcpyAsync(sp->hist + (size_t)slot * sp->hl, prompt, (size_t)len * 4, cudaMemcpyHostToDevice, c->stream));
+  ULB_CUDA(cudaMemcpyAsync(sp->plen + slot, &len, 4, cudaMemcpyHostToDevice, c->stream));
+  ULB_CUDA(cudaMemcpyAsync(sp->round + slot, &zero, 4, cudaMemcpyHostToDevice, c->stream));
+  ULB_CUDA(cudaMemcpyAsync(sp->active + slot, &zero, 4, cudaMemcpyHostToDevice, c->stream));
+  sp->h_plen[slot] = len;
+  const uint64_t launches0 = c->launches;
+  ULB_TRY(prefill_slot(sp, slot, len));
+  const int32_t L = len + 1, dn = 1 >= sp->d.max_new;
+  ULB_CUDA(cudaMemcpyAsync(sp->L + slot, &L, 4, cudaMemcpyHostToDevice, c->stream));
+  ULB_CUDA(cudaMemcpyAsync(sp->done + slot, &dn, 4, cudaMemcpyHostToDevice, c->stream));
+  ULB_TRY(sync_stream(c));
+  sp->launches += c->launches - launches0;
   return ULB_OK;
 }
 

@@ -125,6 +125,13 @@ int repack_q4(Ctx* c, int type, const void* dev_raw, int raw_rows, int K, const 
 /* ------------------------------------------------------------------ kernels (launchers) */
 enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
 
+/* KV cache pages: positions of a sequence are mapped to pages of kKvPage positions through a
+   block table (bt[seq * max_pages + pos / kKvPage] = page, -1 = unmapped).  A page holds
+   every kv head: [page][n_head_kv][kKvPage][head_dim] fp16, one pool per layer for K and for
+   V.  One page is one attention key split, so a split never crosses pages. */
+constexpr int kKvPage = 256;
+static_assert(kKvPage == ULB_KV_PAGE, "the page size of the C ABI");
+
 struct EpiArgs {
   float* y = nullptr;   int ldy = 0;   /* STORE: y[m*ldy+n] = v; RESID: y[m*ldy+n] += v     */
   __half* h = nullptr;  int ldh = 0;   /* SWIGLU: h[m*ldh + f] = fp16(silu(gate_f) * up_f)  */
@@ -134,6 +141,8 @@ struct EpiArgs {
   int nq = 0, nkv = 0, hd = 0, cap = 0, n_head_kv = 0, n_seq = 0;
   const int* row_seq = nullptr; const int* row_pos = nullptr;
   const float2* rope = nullptr; /* [pos][hd/2] (cos, sin) */
+  /* paged cache (kc / vc are the layer's page pools): NULL = contiguous [S][Hkv][cap][hd] */
+  const int* bt = nullptr; int max_pages = 0;
 };
 
 int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a);
@@ -161,10 +170,12 @@ int launch_qgemm_tc(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, in
 
 int launch_dequant(Ctx* c, const Tensor* w, float* out);
 
+/* bt: block table of a paged cache (k / v are then page pools [page][Hkv][kKvPage][hd]), or
+   NULL for a contiguous cache [n_seq][Hkv][capacity][hd] */
 int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, const __half* k,
                      const __half* v, const int* row_seq, const int* row_pos, int M, int rps,
                      __half* out, float* scratch, int* counters, size_t scratch_floats,
-                     int n_counters);
+                     int n_counters, const int* bt = nullptr, int max_pages = 0);
 /* argument checks shared by every attention entry point (no division by a zero head count) */
 int validate_attn_desc(const ulb_attn_desc* d, int M, int rps);
 /* split-merge scratch a launch of this shape needs: zero floats / counters when it has one key

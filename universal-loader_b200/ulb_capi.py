@@ -40,7 +40,7 @@ class ModelDesc(C.Structure):
 class SpecDesc(C.Structure):
     _fields_ = [("n_seq", C.c_int), ("k", C.c_int), ("max_prompt", C.c_int),
                 ("max_new", C.c_int), ("warp", Warp), ("seed", C.c_uint64),
-                ("use_graphs", C.c_int)]
+                ("use_graphs", C.c_int), ("kv_pages", C.c_int)]
 
 
 _SIGS = {
@@ -75,6 +75,7 @@ _SIGS = {
     "ulb_qgemm": (C.c_int, [P, P, P, C.c_int, P, C.c_int]),
     "ulb_attention": (C.c_int, [P, C.POINTER(AttnDesc), P, P, P, P, P, C.c_int, C.c_int, P]),
     "ulb_attention_noalloc": (C.c_int, [P, C.POINTER(AttnDesc), P, P, P, P, P, C.c_int, C.c_int, P]),
+    "ulb_attention_paged": (C.c_int, [P, C.POINTER(AttnDesc), P, P, P, P, C.c_int, P, P, C.c_int, C.c_int, P]),
     "ulb_sample": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, C.POINTER(Warp), C.c_uint64,
                              C.c_uint32, C.c_uint32, C.c_uint32, P]),
     "ulb_spec_accept": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.POINTER(Warp),
@@ -85,6 +86,8 @@ _SIGS = {
     "ulb_model_free": (C.c_int, [P]),
     "ulb_model_weight_bytes": (C.c_int, [P, C.POINTER(C.c_size_t)]),
     "ulb_kv_alloc": (C.c_int, [P, P, C.c_int, C.c_int, C.POINTER(P)]),
+    "ulb_kv_alloc_paged": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, C.POINTER(P)]),
+    "ulb_kv_map": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P]),
     "ulb_kv_free": (C.c_int, [P]),
     "ulb_model_forward": (C.c_int, [P, P, P, C.c_int, C.c_int, P, P, P, C.c_int, P, C.c_int]),
     "ulb_spec_create": (C.c_int, [P, P, P, C.POINTER(SpecDesc), C.POINTER(P)]),
@@ -95,6 +98,7 @@ _SIGS = {
     "ulb_spec_profile_round": (C.c_int, [P, C.POINTER(C.c_float)]),
     "ulb_spec_profile_round_ex": (C.c_int, [P, C.POINTER(C.c_float)]),
     "ulb_spec_read_rounds": (C.c_int, [P, C.c_int, C.c_int, P, C.POINTER(C.c_int)]),
+    "ulb_spec_admit": (C.c_int, [P, C.c_int, P, C.c_int]),
     "ulb_spec_launch_count": (C.c_int, [P, C.POINTER(C.c_uint64)]),
 }
 
