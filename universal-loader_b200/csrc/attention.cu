@@ -44,7 +44,8 @@ constexpr float kLog2e = 1.44269504088896340736f;
 struct AttnParams {
   int H, Hkv, hd, cap, G, rps, n_mt, max_splits, ldq, n_seq, n_groups;
   float scale2; /* softmax scale x log2(e): scores live in the base-2 domain */
-  const int* bt; /* block table of a paged cache (one page = one key split), or NULL */
+  /* paged cache (max_pages > 0; one page = one key split): block table bt, NULL = identity */
+  const int* bt;
   int max_pages;
 };
 static_assert(SPLITK == kKvPage, "a key split is one KV cache page");
@@ -170,8 +171,9 @@ __global__ void __launch_bounds__(AW * 32, 1)
      pool [page][Hkv][kKvPage][hd] (an unmapped page holds no keys: the split is masked out) */
   size_t kvoff;
   int page_ok = 1;
-  if (p.bt) {
-    const int page = p.bt[(size_t)seq * p.max_pages + split];
+  if (p.max_pages > 0) {
+    const int slot = seq * p.max_pages + split;
+    const int page = p.bt ? p.bt[slot] : slot;
     page_ok = page >= 0;
     kvoff = (((size_t)max(page, 0) * p.Hkv + kvh) * kKvPage + warp * KB) * HD;
   } else {
@@ -582,7 +584,7 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
   p.ldq = ldq;
   p.bt = bt;
   p.max_pages = max_pages;
-  ULB_CHECK(!bt || (long long)max_pages * kKvPage >= d->capacity, ULB_EINVAL,
+  ULB_CHECK(max_pages == 0 || (long long)max_pages * kKvPage >= d->capacity, ULB_EINVAL,
             "attention: %d pages of %d positions per sequence cannot hold capacity %d", max_pages, kKvPage, d->capacity);
   int need_c = 0;
   size_t need = 0;

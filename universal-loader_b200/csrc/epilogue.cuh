@@ -44,8 +44,9 @@ __device__ __forceinline__ void epilogue_token(const EpiArgs& e, int strip, int 
     size_t sbase, pstride;
     int prow;
     bool kv_ok = true;
-    if (e.bt) {
-      const int page = e.bt[(size_t)seq * e.max_pages + pos / kKvPage];
+    if (e.max_pages > 0) {
+      const int slot = seq * e.max_pages + pos / kKvPage;
+      const int page = e.bt ? e.bt[slot] : slot;
       kv_ok = page >= 0;
       sbase = (size_t)(kv_ok ? page : 0) * e.n_head_kv;
       pstride = kKvPage;

@@ -69,6 +69,7 @@ struct KV {
   int n_pages = 0, max_pages = 0;
   int* bt = nullptr;
   std::vector<int> h_bt;
+  bool identity = false; /* bt is the identity table: kernels compute pages instead of loading them */
   __half* k = nullptr;
   __half* v = nullptr;
   size_t layer_elems = 0;
@@ -294,7 +295,7 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     a.q = m->qb; a.ldq = m->nq; a.kc = kc; a.vc = vc;
     a.nq = m->nq; a.nkv = m->nkv; a.hd = d.head_dim; a.cap = kv->cap; a.n_head_kv = d.n_head_kv; a.n_seq = kv->n_seq;
     a.row_seq = seq; a.row_pos = pos; a.rope = kv->rope;
-    a.bt = kv->bt; a.max_pages = kv->max_pages;
+    a.bt = kv->identity ? nullptr : kv->bt; a.max_pages = kv->max_pages;
     /* GEMV tails prefetch the weights of the GEMVs to come into L2 (the hint is set just
        before the launch whose tail issues it) */
     auto hint = [c](const Tensor* t, const Tensor* t2 = nullptr) {
@@ -308,7 +309,8 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     hint(&L.o, &L.gateup);
     ULB_TRY(launch_qgemv_rms(c, &L.qkv, m->x, d.d_model, L.attn_norm, d.rms_eps, m->x16, M, EPI_QKV, a));
     ULB_TRY(launch_attention(c, &ad, m->qb, m->nq, kc, vc, seq, pos, M, rps, m->att, kv->attn_scratch,
-                             kv->attn_counters, kv->attn_floats, kv->n_counters, kv->bt, kv->max_pages));
+                             kv->attn_counters, kv->attn_floats, kv->n_counters, kv->identity ? nullptr : kv->bt,
+                             kv->max_pages));
     EpiArgs r;
     r.y = m->x; r.ldy = d.d_model;
     /* tensor parallel: this rank's heads / features give a partial sum of attn_output and
@@ -747,7 +749,9 @@ int ulb_kv_alloc(ulb_ctx* ctx, const ulb_model* mm, int n_seq, int cap, ulb_kv**
   ULB_CHECK((long long)n_seq * pps < (1ll << 31), ULB_EINVAL, "ulb_kv_alloc: too many pages");
   std::vector<int> table((size_t)n_seq * pps);
   for (size_t i = 0; i < table.size(); ++i) table[i] = (int)i;
-  return kv_create(ctx, mm, n_seq, cap, n_seq * pps, pps, table.data(), out);
+  ULB_TRY(kv_create(ctx, mm, n_seq, cap, n_seq * pps, pps, table.data(), out));
+  (*out)->kv.identity = true;
+  return ULB_OK;
 }
 
 int ulb_kv_alloc_paged(ulb_ctx* ctx, const ulb_model* mm, int n_seq, int n_pages, int max_pages_per_seq,
@@ -771,6 +775,7 @@ int ulb_kv_map(ulb_kv* kvh, int seq, int first, int n, const int32_t* pages) {
   if (n == 0) return ULB_OK;
   int* row = kv->h_bt.data() + (size_t)seq * kv->max_pages + first;
   memcpy(row, pages, (size_t)n * 4);
+  kv->identity = false; /* from now on the kernels read the table */
   Ctx* c = kv->m->c;
   ULB_CUDA(cudaSetDevice(c->device));
   ULB_CUDA(cudaMemcpyAsync(kv->bt + (size_t)seq * kv->max_pages + first, row, (size_t)n * 4, cudaMemcpyHostToDevice,

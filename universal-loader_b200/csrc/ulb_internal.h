@@ -141,7 +141,9 @@ struct EpiArgs {
   int nq = 0, nkv = 0, hd = 0, cap = 0, n_head_kv = 0, n_seq = 0;
   const int* row_seq = nullptr; const int* row_pos = nullptr;
   const float2* rope = nullptr; /* [pos][hd/2] (cos, sin) */
-  /* paged cache (kc / vc are the layer's page pools): NULL = contiguous [S][Hkv][cap][hd] */
+  /* paged cache (max_pages > 0: kc / vc are the layer's page pools, sequence s's position p in
+     page bt[s * max_pages + p / kKvPage], or in page s * max_pages + p / kKvPage when bt is
+     NULL, the identity table); max_pages == 0: contiguous [S][Hkv][cap][hd] */
   const int* bt = nullptr; int max_pages = 0;
 };
 
@@ -170,8 +172,9 @@ int launch_qgemm_tc(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, in
 
 int launch_dequant(Ctx* c, const Tensor* w, float* out);
 
-/* bt: block table of a paged cache (k / v are then page pools [page][Hkv][kKvPage][hd]), or
-   NULL for a contiguous cache [n_seq][Hkv][capacity][hd] */
+/* max_pages > 0: a paged cache (k / v are page pools [page][Hkv][kKvPage][hd]) with block
+   table bt (NULL: the identity table, page = seq * max_pages + position / kKvPage);
+   max_pages == 0: a contiguous cache [n_seq][Hkv][capacity][hd] */
 int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, const __half* k,
                      const __half* v, const int* row_seq, const int* row_pos, int M, int rps,
                      __half* out, float* scratch, int* counters, size_t scratch_floats,
