@@ -303,6 +303,20 @@ int orc_qgemv(int type, const void* w, int N, int K, const uint16_t* x16, int M,
         for (int m = 0; m < mc; ++m) y[(size_t)(m0 + m) * ldy + n] = acc[m];
       }
     }
+  } else if (type == T_F16 || type == T_F32) {
+    /* plain rows (a tied F16 / F32 head): y = sum_i w_i * x_i in index order */
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+      for (int m = 0; m < M; ++m) {
+        const float* xv = xf + (size_t)m * K;
+        float acc = 0.0f;
+        for (int i = 0; i < K; ++i) {
+          const float wv = type == T_F16 ? h2f(((const uint16_t*)W)[(size_t)n * K + i]) : ((const float*)W)[(size_t)n * K + i];
+          acc = fmaf(wv, xv[i], acc);
+        }
+        y[(size_t)m * ldy + n] = acc;
+      }
+    }
   } else if (type == T_Q8_0) {
     /* y = sum_b d_b * (sum_{i<32} q_i * x_i) */
     if (K % 32) { free(xf); return -1; }
@@ -556,6 +570,7 @@ orc_model* orc_model_load(const char* path, char* err, int errlen) {
     m->embd = find_t(m, "token_embd.weight");
     m->out_norm = find_t(m, "output_norm.weight");
     m->out = find_t(m, "output.weight");
+    if (!m->out) m->out = m->embd; /* tied embeddings: the LM head is token_embd */
     if (!m->embd || !m->out_norm || !m->out) FAIL("missing token_embd/output_norm/output");
     d->wtype = m->layers[0].q->type;
   }

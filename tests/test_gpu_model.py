@@ -396,3 +396,64 @@ def test_continuous_batching_matches_each_sequence_alone(tiny_target, tiny_draft
     plain = _api(tiny_target)
     plain.set_max_batch_size(3)
     assert plain.generate_tokens([p.tolist() for p in prompts], _cfg(40)) == alone
+
+
+@pytest.mark.parametrize("embd_type", ["f16", "f32", "q8_0", "q4_0", "q6_k"])
+def test_tied_embeddings_head_matches_oracle(ctx, model_dir, embd_type):
+    """A file without output.weight: the LM head is token_embd (the row GEMV over F16 / F32 /
+    Q8_0 / Q6_K rows sharing the embedding's device copy, or the packed Q4 GEMV), against the
+    oracle, which uses token_embd as the head the same way."""
+    import os
+    import vulkangguf as vg
+    path = os.path.join(str(model_dir), "tied_%s.gguf" % embd_type)
+    if not os.path.exists(path):
+        vg.write_synthetic_gguf(path, dict(n_layer=2, d_model=512, n_head=8, n_head_kv=4, d_ff=1536, n_vocab=4096,
+                                           rms_eps=1e-5, rope_base=1e4, wtype="q4_0", embd_type=embd_type, tied=True,
+                                           seed=13, name="tied"))
+    import gguf
+    assert "output.weight" not in [t.name for t in gguf.GGUFReader(path).tensors]
+    om = orc.Model(path)
+    gm = GpuModelTied(ctx, path)
+    try:
+        kvg = gm.kv(1, 64)
+        kvo = orc.KV(om, 1, 64)
+        toks = _prompt(20, seed=47, vocab=4096)
+        g = gm.forward(kvg, toks, [0] * 20, range(20), 20, logits_mode=1)
+        o = orc.forward(om, kvo, toks, [0] * 20, list(range(20)), 20, logits_mode=1)
+        assert np.abs(g - o).max() / np.abs(o).max() < FWD_RTOL
+        assert g.argmax() == o.argmax()
+        toks = _prompt(5, seed=48, vocab=4096)
+        g = gm.forward(kvg, toks, [0] * 5, range(20, 25), 5)
+        o = orc.forward(om, kvo, toks, [0] * 5, list(range(20, 25)), 5)
+        assert np.abs(g - o).max() / np.abs(o).max() < FWD_RTOL
+        assert (g.argmax(1) == o.argmax(1)).all()
+        gm.U.lib().ulb_kv_free(kvg)
+    finally:
+        gm.close()
+
+
+class GpuModelTied(GpuModel):
+    """GpuModel for files without output.weight (every tensor the file has is set)."""
+
+    def __init__(self, ctx, path):
+        import ulb_capi as U
+        self.U, self.ctx = U, ctx
+        om = orc.Model(path)
+        d = om.desc
+        self.desc = d
+        md = U.ModelDesc(d.n_layer, d.d_model, d.n_head, d.n_head_kv, d.head_dim, d.d_ff, d.n_vocab,
+                         d.rms_eps, d.rope_base, 64)
+        h = C.c_void_p()
+        U.check(U.lib().ulb_model_create(ctx.h, C.byref(md), C.byref(h)))
+        self.h = h
+        names = ["token_embd.weight", "output_norm.weight"]
+        for l in range(d.n_layer):
+            names += ["blk.%d.%s.weight" % (l, s) for s in
+                      ("attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm", "ffn_gate",
+                       "ffn_up", "ffn_down")]
+        for nm in names:
+            t, ne, raw = om.tensor(nm)
+            ne4 = (C.c_uint64 * 4)(*ne)
+            U.check(U.lib().ulb_model_set_weight(h, nm.encode(), t, ne4, raw.ctypes.data_as(C.c_void_p), raw.nbytes))
+        U.check(U.lib().ulb_model_finalize(h))
+        self.om = om

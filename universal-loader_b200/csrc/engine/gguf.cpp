@@ -446,7 +446,8 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
     plan.push_back({p + "ffn_down.weight", sp.wtype, 2, {f, d}, PlannedTensor::NORMAL});
   }
   plan.push_back({"output_norm.weight", 0, 1, {(uint64_t)sp.d_model, 1}, PlannedTensor::ONES});
-  plan.push_back({"output.weight", out_type, 2, {(uint64_t)sp.d_model, (uint64_t)sp.n_vocab}, PlannedTensor::NORMAL});
+  if (!sp.tied)
+    plan.push_back({"output.weight", out_type, 2, {(uint64_t)sp.d_model, (uint64_t)sp.n_vocab}, PlannedTensor::NORMAL});
   const uint64_t align = 32;
   uint64_t off = 0;
   for (PlannedTensor& t : plan) {

@@ -530,6 +530,7 @@ bool write_synthetic(const std::string& path, py::dict spec, int threads) {
     v = it->second;
   };
   type_of("embd_type", s.embd_type);
+  if (spec.contains("tied")) s.tied = spec["tied"].cast<bool>();
   type_of("out_type", s.out_type);
   if (spec.contains("vocab")) {
     s.vocab = spec["vocab"].cast<std::vector<std::string>>();
@@ -711,6 +712,7 @@ PYBIND11_MODULE(vulkangguf, m) {
       py::arg("path"), py::arg("ids"), "Text (UTF-8 bytes) of token ids under the GGUF file's vocabulary");
   m.def("write_synthetic_gguf", &write_synthetic, py::arg("path"), py::arg("spec"), py::arg("threads") = 0,
         "Write a synthetic LLaMA GGUF: Q4_0/Q4_K weights N(0, stddev), fp16 embeddings, unit norms; "
+        "spec key tied=True writes no output.weight (the head is token_embd); "
         "spec keys embd_type / out_type pick other token_embd (f32, f16, q4_0, q8_0, q4_k, q6_k) and "
         "output.weight (q4_0, q8_0, q4_k, q6_k) types; vocab / scores / token_types (+ merges, "
         "tokenizer_pre for byte-level BPE; add_bos, add_space_prefix) write a tokenizer.ggml.* vocabulary");

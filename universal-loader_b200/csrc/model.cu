@@ -49,6 +49,7 @@ struct Model {
   std::vector<Layer> layers;
   float* out_norm = nullptr;
   Tensor out;
+  bool out_shared = false; /* out.dev is the token_embd buffer (tied F16 / F32 / Q8_0 / Q6_K rows) */
   size_t weight_bytes = 0;
   /* workspace */
   int ws_rows = 0;
@@ -642,19 +643,30 @@ int ulb_model_finalize(ulb_model* mm) {
   ULB_CHECK(r->type == ULB_TYPE_F32 && r->ne[0] == (uint64_t)d.d_model, ULB_EFORMAT, "output_norm");
   size_t b;
   ULB_TRY(upload_plain(c, *r, (void**)&m->out_norm, &b));
-  ULB_TRY(get("output.weight", &r));
+  /* tied embeddings (no output.weight, as small LLaMA-family models store them): the LM head
+     is token_embd itself */
+  const bool tied = m->raw.find("output.weight") == m->raw.end();
+  ULB_TRY(get(tied ? "token_embd.weight" : "output.weight", &r));
   ULB_TRY(expect(r, "output.weight", d.d_model, d.n_vocab));
-  if (r->type == ULB_TYPE_Q8_0 || r->type == ULB_TYPE_Q6_K) {
-    /* kept as GGUF rows for the row GEMV (as llama.cpp's Q4_0 / Q4_K_M files store the head) */
-    ULB_CHECK(d.d_model % (r->type == ULB_TYPE_Q8_0 ? 32 : 256) == 0, ULB_EFORMAT, "output.weight: partial blocks");
+  if (r->type == ULB_TYPE_Q8_0 || r->type == ULB_TYPE_Q6_K || r->type == ULB_TYPE_F16 || r->type == ULB_TYPE_F32) {
+    /* kept as GGUF rows for the row GEMV (as llama.cpp's Q4_0 / Q4_K_M files store the head,
+       or a tied F16 / F32 embedding) */
+    ULB_CHECK(r->type == ULB_TYPE_F16 || r->type == ULB_TYPE_F32 || d.d_model % (r->type == ULB_TYPE_Q8_0 ? 32 : 256) == 0,
+              ULB_EFORMAT, "output.weight: partial blocks");
     m->out.type = r->type;
     m->out.N = d.n_vocab;
     m->out.K = d.d_model;
     m->out.ne[0] = (uint64_t)d.d_model;
     m->out.ne[1] = (uint64_t)d.n_vocab;
-    ULB_TRY(upload_plain(c, *r, &m->out.dev, &m->out.bytes));
+    if (tied) {
+      m->out.dev = m->embd; /* the embedding rows are the head's rows: one device copy */
+      m->out.bytes = 0;
+      m->out_shared = true;
+    } else {
+      ULB_TRY(upload_plain(c, *r, &m->out.dev, &m->out.bytes));
+    }
   } else {
-    ULB_CHECK(is_q4(r->type), ULB_EUNSUPPORTED, "output.weight must be Q4_0, Q4_K, Q8_0 or Q6_K");
+    ULB_CHECK(is_q4(r->type), ULB_EUNSUPPORTED, "output.weight must be Q4_0, Q4_K, Q8_0, Q6_K, F16 or F32");
     ULB_TRY(build_plain(c, *r, &m->out));
   }
   m->weight_bytes += m->out.bytes;
@@ -678,7 +690,7 @@ int ulb_model_free(ulb_model* mm) {
     free_tensor(c, L.qkv); free_tensor(c, L.o); free_tensor(c, L.gateup); free_tensor(c, L.down);
   }
   dev_free(c, m->out_norm, (size_t)m->d.d_model * 4);
-  free_tensor(c, m->out);
+  if (!m->out_shared) free_tensor(c, m->out);
   dev_free(c, m->x, 0); dev_free(c, m->x16, 0); dev_free(c, m->qb, 0); dev_free(c, m->att, 0); dev_free(c, m->h16, 0);
   c->bytes_live -= m->ws_bytes;
   cudaStreamSynchronize(c->stream);

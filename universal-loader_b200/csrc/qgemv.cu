@@ -660,7 +660,30 @@ __global__ void __launch_bounds__(256) rowgemv_kernel(const uint8_t* __restrict_
         acc[m] = __fmaf_rn(step, s, acc[m]);
       }
   };
-  if (QT == ULB_TYPE_Q8_0) {
+  if (QT == ULB_TYPE_F16 || QT == ULB_TYPE_F32) {
+    /* plain rows: lane L takes weights 8L..8L+7 of every 256, products summed in that order */
+    for (int k0 = 8 * lane; k0 < K; k0 += 256) {
+      float wv[8];
+      if (QT == ULB_TYPE_F16) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(w) + (size_t)n * K + k0));
+        const __half* wh = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wv[e] = __half2float(wh[e]);
+      } else {
+        const float4* p4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(w) + (size_t)n * K + k0);
+        const float4 a = __ldg(p4), b = __ldg(p4 + 1);
+        wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w; wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+      }
+#pragma unroll
+      for (int m = 0; m < 8; ++m)
+        if (m < M) {
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * ldx + k0));
+          const __half* xh = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[m] = __fmaf_rn(wv[e], __half2float(xh[e]), acc[m]);
+        }
+    }
+  } else if (QT == ULB_TYPE_Q8_0) {
     const uint8_t* row = w + (size_t)n * (K / 32) * 34;
     for (int b = lane; b < K / 32; b += 32) {
       const uint8_t* blk = row + (size_t)b * 34;
@@ -705,19 +728,23 @@ __global__ void __launch_bounds__(256) rowgemv_kernel(const uint8_t* __restrict_
   }
 }
 
-static bool raw_rows_type(int t) { return t == ULB_TYPE_Q8_0 || t == ULB_TYPE_Q6_K; }
+static bool raw_rows_type(int t) {
+  return t == ULB_TYPE_Q8_0 || t == ULB_TYPE_Q6_K || t == ULB_TYPE_F16 || t == ULB_TYPE_F32;
+}
 
 static int launch_rowgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a) {
   ULB_CHECK(epi == EPI_STORE && a.y, ULB_EUNSUPPORTED, "qgemv: a Q8_0 / Q6_K matrix takes the plain store epilogue only");
   ULB_CHECK(ldx % 8 == 0 && ((uintptr_t)x & 15) == 0, ULB_EINVAL, "qgemv: activations must be 16-byte aligned rows");
+  ULB_CHECK(w->K % 8 == 0, ULB_EUNSUPPORTED, "row GEMV: K=%d not a multiple of 8", w->K);
   const dim3 grid((w->N + 7) / 8), block(256);
+  auto kern = w->type == ULB_TYPE_Q8_0   ? rowgemv_kernel<ULB_TYPE_Q8_0>
+              : w->type == ULB_TYPE_Q6_K ? rowgemv_kernel<ULB_TYPE_Q6_K>
+              : w->type == ULB_TYPE_F16  ? rowgemv_kernel<ULB_TYPE_F16>
+                                         : rowgemv_kernel<ULB_TYPE_F32>;
   for (int m0 = 0; m0 < M; m0 += 8) {
     const int mc = M - m0 < 8 ? M - m0 : 8;
-    cudaError_t e = w->type == ULB_TYPE_Q8_0
-                        ? launch_k(c, rowgemv_kernel<ULB_TYPE_Q8_0>, grid, block, 0, (const uint8_t*)w->dev, w->N, w->K,
-                                   x + (size_t)m0 * ldx, ldx, mc, a.y + (size_t)m0 * a.ldy, a.ldy)
-                        : launch_k(c, rowgemv_kernel<ULB_TYPE_Q6_K>, grid, block, 0, (const uint8_t*)w->dev, w->N, w->K,
-                                   x + (size_t)m0 * ldx, ldx, mc, a.y + (size_t)m0 * a.ldy, a.ldy);
+    cudaError_t e = launch_k(c, kern, grid, block, 0, (const uint8_t*)w->dev, w->N, w->K, x + (size_t)m0 * ldx, ldx, mc,
+                             a.y + (size_t)m0 * a.ldy, a.ldy);
     if (e != cudaSuccess) return cuda_error(e, "row GEMV launch", __FILE__, __LINE__);
   }
   return ULB_OK;
@@ -951,7 +978,7 @@ static int launch_qgemv_impl(Ctx* c, const Tensor* w, const __half* x, int M, in
 int launch_qgemv_rms(Ctx* c, const Tensor* w, const float* x32, int ldx32, const float* g, float eps, __half* x16,
                      int M, int epi, const EpiArgs& a) {
   ULB_CHECK(w && (w->type == ULB_TYPE_Q4_0 || w->type == ULB_TYPE_Q4_K || raw_rows_type(w->type)), ULB_EINVAL,
-            "qgemv: weight is not Q4_0/Q4_K/Q8_0/Q6_K");
+            "qgemv: weight is not Q4_0/Q4_K/Q8_0/Q6_K/F16/F32");
   if (M == 0) return ULB_OK;
   const bool fuse = !raw_rows_type(w->type) && M <= 8 && (size_t)M * w->K * sizeof(__half) <= (size_t)kNormSmemBytes && w->K <= 8192 &&
                     w->K % 8 == 0 && ldx32 % 4 == 0 && ((uintptr_t)x32 & 15) == 0 && ((uintptr_t)g & 15) == 0 &&
