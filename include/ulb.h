@@ -181,6 +181,23 @@ ULB_API int ulb_attention(ulb_ctx* ctx, const ulb_attn_desc* desc, const float* 
                   const int32_t* dev_row_pos, int M, int rows_per_seq, uint16_t* dev_out);
 
 /*
+ * Kernel form of every attention launch on this context (ulb_attention*, ulb_model_forward,
+ * the speculative loop):
+ *   ULB_ATTN_AUTO    (default) chosen per launch from the shape
+ *   ULB_ATTN_SPLIT   one CTA per (query tile, kv head, sequence, 256-key split): every split in
+ *                    flight at once, the short-latency form for a few sequences
+ *   ULB_ATTN_STREAM  one CTA per (query tile, kv head, sequence) walking its splits in order
+ *                    with the K / V loads of the next split in flight: the throughput form for
+ *                    many sequences and long caches
+ * Both forms give every row the same bits; the setting only moves time.  No counterpart in
+ * the reference (its flash_attention dispatch has one form, inference_engine.cpp:628-630).
+ */
+#define ULB_ATTN_AUTO 0
+#define ULB_ATTN_SPLIT 1
+#define ULB_ATTN_STREAM 2
+ULB_API int ulb_attention_set_form(ulb_ctx* ctx, int form);
+
+/*
  * ulb_attention over a paged KV cache, the layout the model caches use.  A sequence's
  * positions map to pages of ULB_KV_PAGE positions through its row of the block table:
  *   dev_k_pool/dev_v_pool  fp16 [n_pages][n_head_kv][ULB_KV_PAGE][head_dim]

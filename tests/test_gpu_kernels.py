@@ -216,6 +216,81 @@ def test_attention_matches_oracle(ctx, H, Hkv, hd, S, rps, positions):
     assert np.abs(got - want).max() < 2e-3
 
 
+def _attn_form(ctx, form, H, Hkv, hd, S, rps, positions, cap, arrays, paged=None):
+    """attention output (fp16 bits) with the kernel form forced to `form`"""
+    import ulb_capi as U
+    M = S * rps
+    bufs = [ctx.buffer(a) for a in arrays]
+    out = ctx.buffer(nbytes=M * H * hd * 2)
+    d = U.AttnDesc(H, Hkv, hd, cap, S, 1.0 / np.sqrt(hd))
+    U.check(U.lib().ulb_attention_set_form(ctx.h, form))
+    try:
+        if paged is None:
+            U.check(U.lib().ulb_attention(ctx.h, C.byref(d), bufs[0].ptr, bufs[1].ptr, bufs[2].ptr, bufs[3].ptr,
+                                          bufs[4].ptr, M, rps, out.ptr))
+        else:
+            tb = ctx.buffer(paged[0])
+            U.check(U.lib().ulb_attention_paged(ctx.h, C.byref(d), bufs[0].ptr, bufs[1].ptr, bufs[2].ptr, tb.ptr,
+                                                paged[1], bufs[3].ptr, bufs[4].ptr, M, rps, out.ptr))
+            tb.free()
+    finally:
+        U.check(U.lib().ulb_attention_set_form(ctx.h, 0))
+    got = out.download(np.uint16, (M, H * hd))
+    for b in bufs + [out]:
+        b.free()
+    return got
+
+
+_RF = np.random.default_rng(5)
+
+
+@pytest.mark.parametrize("H,Hkv,hd,S,rps,positions", [
+    (32, 32, 128, 1, 6, [list(range(2434, 2440))]),                                    # 7B verify, 10 splits
+    (32, 8, 128, 24, 9, [list(range(int(a), int(a) + 9)) for a in _RF.integers(100, 3000, 24)]),  # config-4 verify
+    (32, 8, 64, 40, 1, [[int(a)] for a in _RF.integers(0, 2900, 40)]),                  # config-4 draft rows
+    (64, 8, 128, 8, 7, [list(range(int(a), int(a) + 7)) for a in _RF.integers(1900, 2300, 8)]),  # config-5 verify
+    (32, 4, 64, 3, 2, [[700, 701], [30, 31], [1500, 1501]]),                             # 1..6 splits, ragged
+])
+def test_attention_forms_give_the_same_bits(ctx, H, Hkv, hd, S, rps, positions):
+    """The per-split and the streaming attention kernels compute every row with the same
+    arithmetic: forcing either form gives bit-identical outputs (so the form chosen for a
+    batch never changes a sequence's result), contiguous and paged caches alike; the streaming
+    form also matches the oracle."""
+    rng = np.random.default_rng(hd * S + rps)
+    cap = max(max(p) for p in positions) + 3
+    M = S * rps
+    q = rng.standard_normal((M, H * hd)).astype(np.float32)
+    k = rng.standard_normal((S, Hkv, cap, hd)).astype(np.float16)
+    v = rng.standard_normal((S, Hkv, cap, hd)).astype(np.float16)
+    row_seq = np.repeat(np.arange(S, dtype=np.int32), rps)
+    row_pos = np.concatenate([np.asarray(p, np.int32) for p in positions])
+    arrays = (q, k, v, row_seq, row_pos)
+    a = _attn_form(ctx, 1, H, Hkv, hd, S, rps, positions, cap, arrays)
+    b = _attn_form(ctx, 2, H, Hkv, hd, S, rps, positions, cap, arrays)
+    assert np.array_equal(a, b), "forms differ at %d of %d outputs" % (int((a != b).sum()), a.size)
+    # the same keys over a shuffled pool of 256-position pages
+    PAGE = 256
+    maxp = (cap + PAGE - 1) // PAGE
+    n_pages = S * maxp
+    perm = rng.permutation(n_pages)
+    table = perm.reshape(S, maxp).astype(np.int32)
+    kp = np.zeros((n_pages, Hkv, PAGE, hd), np.float16)
+    vp = np.zeros((n_pages, Hkv, PAGE, hd), np.float16)
+    for s_ in range(S):
+        for j in range(maxp):
+            n = min(PAGE, cap - j * PAGE)
+            kp[table[s_, j], :, :n] = k[s_, :, j * PAGE:j * PAGE + n]
+            vp[table[s_, j], :, :n] = v[s_, :, j * PAGE:j * PAGE + n]
+    pa = _attn_form(ctx, 1, H, Hkv, hd, S, rps, positions, cap, (q, kp, vp, row_seq, row_pos), (table, maxp))
+    pb = _attn_form(ctx, 2, H, Hkv, hd, S, rps, positions, cap, (q, kp, vp, row_seq, row_pos), (table, maxp))
+    assert np.array_equal(pa, pb)
+    assert np.array_equal(pa, a), "paged and contiguous caches differ"
+    if M * cap <= 200000:
+        want = orc.attention(H, Hkv, hd, cap, 1.0 / np.sqrt(hd), q, k.view(np.uint16), v.view(np.uint16),
+                             row_seq, row_pos)
+        assert np.abs(b.view(np.float16).astype(np.float32) - want.astype(np.float32)).max() < 2e-3
+
+
 @pytest.mark.parametrize("H,Hkv,hd,S,rps,positions", [
     (32, 32, 128, 1, 6, [[639, 640, 641, 642, 643, 644]]),                      # 7B verify rows, 3 pages
     (32, 4, 64, 3, 2, [[700, 701], [30, 31], [1500, 1501]]),                     # draft rows, ragged

@@ -62,26 +62,36 @@ _R = np.random.default_rng(77)
     # a global merge whose partials (11 x 8 heads x 11 splits x 16 x 130 floats = 2.01 Mi) just fit
     (32, 8, 128, 11, 1, _ragged(_R, 11, 1, 2400, 2595), 2600),
 ])
-def test_noalloc_attention_matches_allocating_entry_point(ctx, H, Hkv, hd, S, rps, positions, cap):
+@pytest.mark.parametrize("form", [0, 1])  # the form the library picks; the per-split form (which uses the scratch)
+def test_noalloc_attention_matches_allocating_entry_point(ctx, H, Hkv, hd, S, rps, positions, cap, form):
     import ulb_capi as U
     rng = np.random.default_rng(hd + S)
     cap = cap or max(max(p) for p in positions) + 5
     desc = U.AttnDesc(H, Hkv, hd, cap, S, 1.0 / np.sqrt(hd))
     M = S * rps
-    for call in range(2):
-        arrays = _inputs(rng, H, Hkv, hd, S, rps, positions, cap)
-        want = _run(ctx, "ulb_attention", desc, arrays, M, rps, M * H * hd)
-        got = _run(ctx, "ulb_attention_noalloc", desc, arrays, M, rps, M * H * hd)
-        assert np.isfinite(got).all()
-        assert np.abs(got - want).max() <= ATTN_ATOL, (call, float(np.abs(got - want).max()))
+    U.check(U.lib().ulb_attention_set_form(ctx.h, form))
+    try:
+        for call in range(2):
+            arrays = _inputs(rng, H, Hkv, hd, S, rps, positions, cap)
+            want = _run(ctx, "ulb_attention", desc, arrays, M, rps, M * H * hd)
+            got = _run(ctx, "ulb_attention_noalloc", desc, arrays, M, rps, M * H * hd)
+            assert np.isfinite(got).all()
+            assert np.abs(got - want).max() <= ATTN_ATOL, (call, float(np.abs(got - want).max()))
+    finally:
+        U.check(U.lib().ulb_attention_set_form(ctx.h, 0))
 
 
 def test_noalloc_attention_rejects_oversized_shapes(ctx):
     import ulb_capi as U
-    # 64 sequences x 32 kv heads x 64 splits of partials exceed the static scratch
+    # in the per-split form, 64 sequences x 32 kv heads x 16 splits of partials exceed the static
+    # scratch; the call is rejected before anything is launched (the pointers are never read)
     desc = U.AttnDesc(32, 32, 128, 4096, 64, 1.0 / np.sqrt(128))
     null = C.c_void_p(16)
-    rc = U.lib().ulb_attention_noalloc(ctx.h, C.byref(desc), null, null, null, null, null, 64 * 9, 9, null)
+    U.check(U.lib().ulb_attention_set_form(ctx.h, 1))
+    try:
+        rc = U.lib().ulb_attention_noalloc(ctx.h, C.byref(desc), null, null, null, null, null, 64 * 9, 9, null)
+    finally:
+        U.check(U.lib().ulb_attention_set_form(ctx.h, 0))
     assert rc == U.EINVAL
     assert b"static scratch" in U.lib().ulb_last_error()
 

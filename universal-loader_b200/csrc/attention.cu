@@ -114,12 +114,191 @@ __device__ __forceinline__ float2 ld_cluster2(uint32_t a) {
   return v;
 }
 
+/*
+ * The per-block arithmetic shared by both attention kernels (so a row gets the same bits from
+ * either): staging of one 64-key block, Q as hi + lo fp16 fragments, the block's scores,
+ * causal mask and softmax, P.V, the warp partial, the in-CTA merge of the 4 warp blocks of a
+ * split and the merge of split partials in split order.
+ */
+/* rows [j0, j1) of a 64-key block into the swizzled buffer; rows >= nk are zero-filled */
+template <int HD>
+__device__ __forceinline__ void stage_rows(__half* dst, const __half* src, int nk, int j0, int j1, int lane) {
+  constexpr int NCH = HD / 8;
+  for (int i = lane; i < KB * NCH; i += 32) {
+    const int j = i / NCH, c = i % NCH;
+    if (j < j0 || j >= j1) continue;
+    const bool ok = j < nk;
+    const size_t off = ok ? (size_t)j * HD + c * 8 : 0;
+    cp_async16z(dst + j * HD + swz(j, c) * 8, src + off, ok);
+  }
+}
+
+/* Q as A fragments of rows qpa (g) / qpb (g + 8), split hi + lo into two fp16 parts so the
+   scores keep ~22 bits of q */
+template <int HD>
+__device__ __forceinline__ void q_frags(const float* qpa, const float* qpb, bool va, bool vb, int t,
+                                        uint32_t (&qh)[HD / 16][4], uint32_t (&ql)[HD / 16][4]) {
+#pragma unroll
+  for (int ks = 0; ks < HD / 16; ++ks) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const bool v = (r & 1) ? vb : va;
+      const float* src = ((r & 1) ? qpb : qpa) + ks * 16 + 2 * t + (r >> 1) * 8;
+      const float2 f = v ? *reinterpret_cast<const float2*>(src) : make_float2(0.f, 0.f);
+      const __half2 h = __floats2half2_rn(f.x, f.y);
+      const float2 hf = __half22float2(h);
+      qh[ks][r] = *reinterpret_cast<const uint32_t*>(&h);
+      ql[ks][r] = pack_h2(f.x - hf.x, f.y - hf.y);
+    }
+  }
+}
+
+/* scores of the tile against the 64 keys from kb0 in Ks, causal mask (key <= the query's
+   position), the block softmax: s becomes exp2(s - m) (unnormalised P), l its row sums */
+template <int HD>
+__device__ __forceinline__ void score_block(const __half* Ks, const uint32_t (&qh)[HD / 16][4],
+                                            const uint32_t (&ql)[HD / 16][4], int kb0, int pa, int pb, float scale2,
+                                            int lane, float (&s)[8][4], float& mA, float& mB, float& lA, float& lB) {
+  constexpr int KS = HD / 16;
+  const int t = lane & 3;
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb) {
+    s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+    const int key = nb * 8 + (lane & 7);
+#pragma unroll
+    for (int kp = 0; kp < KS / 2; ++kp) {
+      uint32_t b0, b1, b2, b3;
+      ldsm4(saddr(Ks + key * HD + swz(key, kp * 4 + (lane >> 3)) * 8), b0, b1, b2, b3);
+      mma_acc(s[nb], qh[2 * kp], b0, b1);
+      mma_acc(s[nb], ql[2 * kp], b0, b1);
+      mma_acc(s[nb], qh[2 * kp + 1], b2, b3);
+      mma_acc(s[nb], ql[2 * kp + 1], b2, b3);
+    }
+  }
+  float mxA = -INFINITY, mxB = -INFINITY;
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int key = kb0 + nb * 8 + 2 * t + e;
+      s[nb][e] = key <= pa ? s[nb][e] * scale2 : -INFINITY;
+      s[nb][2 + e] = key <= pb ? s[nb][2 + e] * scale2 : -INFINITY;
+      mxA = fmaxf(mxA, s[nb][e]);
+      mxB = fmaxf(mxB, s[nb][2 + e]);
+    }
+  mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
+  mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
+  mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
+  mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+  float sA = 0.f, sB = 0.f;
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      s[nb][e] = mxA == -INFINITY ? 0.f : exp2f(s[nb][e] - mxA);
+      s[nb][2 + e] = mxB == -INFINITY ? 0.f : exp2f(s[nb][2 + e] - mxB);
+      sA += s[nb][e];
+      sB += s[nb][2 + e];
+    }
+  sA += __shfl_xor_sync(0xffffffffu, sA, 1);
+  sA += __shfl_xor_sync(0xffffffffu, sA, 2);
+  sB += __shfl_xor_sync(0xffffffffu, sB, 1);
+  sB += __shfl_xor_sync(0xffffffffu, sB, 2);
+  lA = sA;
+  lB = sB;
+  mA = mxA;
+  mB = mxB;
+}
+
+/* O = P.V: P (fp16) as A fragments straight from the score registers */
+template <int HD>
+__device__ __forceinline__ void pv_block(const __half* Vs, const float (&s)[8][4], int lane, float (&o)[HD / 8][4]) {
+  constexpr int DN = HD / 8;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const uint32_t pf[4] = {pack_h2(s[2 * kk][0], s[2 * kk][1]), pack_h2(s[2 * kk][2], s[2 * kk][3]),
+                            pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]),
+                            pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3])};
+    const int key = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+    for (int dp = 0; dp < DN / 2; ++dp) {
+      uint32_t b0, b1, b2, b3;
+      ldsm4t(saddr(Vs + key * HD + swz(key, dp * 2 + (lane >> 4)) * 8), b0, b1, b2, b3);
+      mma_acc(o[2 * dp], pf, b0, b1);
+      mma_acc(o[2 * dp + 1], pf, b2, b3);
+    }
+  }
+}
+
+/* a warp block's (max, sum, output) of its 16 queries: pw[q * (HD + 2) + {0: m, 1: l, 2..: o}] */
+template <int HD>
+__device__ __forceinline__ void write_warp_partial(float* pw, int lane, float mA, float mB, float lA, float lB,
+                                                   const float (&o)[HD / 8][4]) {
+  constexpr int PST = HD + 2;
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int d = 0; d < HD / 8; ++d) {
+    pw[g * PST + 2 + d * 8 + 2 * t] = o[d][0];
+    pw[g * PST + 3 + d * 8 + 2 * t] = o[d][1];
+    pw[(g + 8) * PST + 2 + d * 8 + 2 * t] = o[d][2];
+    pw[(g + 8) * PST + 3 + d * 8 + 2 * t] = o[d][3];
+  }
+  if (t == 0) {
+    pw[g * PST] = mA;
+    pw[g * PST + 1] = lA;
+    pw[(g + 8) * PST] = mB;
+    pw[(g + 8) * PST + 1] = lB;
+  }
+}
+
+/* the split's (max, sum, output pair d2) of query qi from the 4 warp partials, warp order;
+   warp w's partial starts at part + w * wstride */
+template <int HD>
+__device__ __forceinline__ void cta_merge_item(const float* part, size_t wstride, int qi, int d2, float& M, float& L,
+                                               float& ox, float& oy) {
+  constexpr int PST = HD + 2;
+  M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < AW; ++w) M = fmaxf(M, part[w * wstride + (size_t)qi * PST]);
+  L = 0.f;
+  ox = 0.f;
+  oy = 0.f;
+#pragma unroll
+  for (int w = 0; w < AW; ++w) {
+    const float* pw = part + w * wstride + (size_t)qi * PST;
+    const float e = pw[0] == -INFINITY ? 0.f : exp2f(pw[0] - M);
+    L = __fmaf_rn(pw[1], e, L);
+    ox = __fmaf_rn(pw[2 + 2 * d2], e, ox);
+    oy = __fmaf_rn(pw[3 + 2 * d2], e, oy);
+  }
+}
+
+/* the next split's partial (m, l, (oxs, oys)) into the running merge (M, L, ox, oy) of the
+   splits before it, in split order; split 0's partial is taken as it is.  Every form of the
+   kernel merges splits with exactly this arithmetic. */
+__device__ __forceinline__ void merge_next(bool first, float m, float l, float oxs, float oys, float& M, float& L,
+                                           float& ox, float& oy) {
+  if (first) {
+    M = m;
+    L = l;
+    ox = oxs;
+    oy = oys;
+    return;
+  }
+  const float Mn = fmaxf(M, m);
+  const float a = M == -INFINITY ? 0.f : exp2f(M - Mn);
+  const float b = m == -INFINITY ? 0.f : exp2f(m - Mn);
+  L = __fmaf_rn(l, b, L * a);
+  ox = __fmaf_rn(oxs, b, ox * a);
+  oy = __fmaf_rn(oys, b, oy * a);
+  M = Mn;
+}
+
 template <int HD, bool CL>
 __global__ void __launch_bounds__(AW * 32, 1)
     attn_mma_kernel(AttnParams p, const float* __restrict__ q, const __half* __restrict__ kc,
                     const __half* __restrict__ vc, const int* __restrict__ row_seq, const int* __restrict__ row_pos,
                     __half* __restrict__ out, float* scratch, int* counters) {
-  constexpr int NCH = HD / 8; /* 16-byte chunks per K / V row */
   constexpr int KS = HD / 16; /* k-steps of Q.K^T */
   constexpr int DN = HD / 8;  /* n-tiles of the output */
   constexpr int PST = HD + 2; /* floats per query of a partial: m, l, o[HD] */
@@ -190,127 +369,34 @@ __global__ void __launch_bounds__(AW * 32, 1)
   const __half* vg = vc + kvoff;
   /* keys [0, n_old) of the block predate this forward, keys [n_old, nk) were just written */
   const int n_old = max(0, min(nk, first_new - kb0));
-  auto stage = [&](int j0, int j1) {
-    for (int i = lane; i < KB * NCH; i += 32) {
-      const int j = i / NCH, c = i % NCH;
-      if (j < j0 || j >= j1) continue;
-      const bool ok = j < nk;
-      const size_t off = ok ? (size_t)j * HD + c * 8 : 0;
-      cp_async16z(Ks + j * HD + swz(j, c) * 8, kg + off, ok);
-      cp_async16z(Vs + j * HD + swz(j, c) * 8, vg + off, ok);
-    }
-  };
-  if (nk > 0) stage(0, n_old);
+  if (nk > 0) {
+    stage_rows<HD>(Ks, kg, nk, 0, n_old, lane);
+    stage_rows<HD>(Vs, vg, nk, 0, n_old, lane);
+  }
   pdl_wait();
   pdl_trigger();
-  if (nk > 0) {
-    stage(n_old, KB); /* the new keys, and zero fill past the last key */
+  if (nk > 0) { /* the new keys, and zero fill past the last key */
+    stage_rows<HD>(Ks, kg, nk, n_old, KB, lane);
+    stage_rows<HD>(Vs, vg, nk, n_old, KB, lane);
     cp_commit();
   }
   const float* qpa = q + (size_t)(m0 + (va ? qa : q0) / p.G) * p.ldq + (kvh * p.G + (va ? qa : q0) % p.G) * HD;
   const float* qpb = q + (size_t)(m0 + (vb ? qb : q0) / p.G) * p.ldq + (kvh * p.G + (vb ? qb : q0) % p.G) * HD;
-  /* Q as A fragments, split hi + lo into two fp16 parts so the scores keep ~22 bits of q */
   uint32_t qh[KS][4], ql[KS][4];
-#pragma unroll
-  for (int ks = 0; ks < KS; ++ks) {
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const bool v = (r & 1) ? vb : va;
-      const float* src = ((r & 1) ? qpb : qpa) + ks * 16 + 2 * t + (r >> 1) * 8;
-      const float2 f = v ? *reinterpret_cast<const float2*>(src) : make_float2(0.f, 0.f);
-      const __half2 h = __floats2half2_rn(f.x, f.y);
-      const float2 hf = __half22float2(h);
-      qh[ks][r] = *reinterpret_cast<const uint32_t*>(&h);
-      ql[ks][r] = pack_h2(f.x - hf.x, f.y - hf.y);
-    }
-  }
+  q_frags<HD>(qpa, qpb, va, vb, t, qh, ql);
 
   if (nk > 0) {
     cp_wait_all();
     __syncwarp();
-    /* S = Q.K^T for 8 n-tiles of 8 keys */
     float s[8][4];
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
-      const int key = nb * 8 + (lane & 7);
-#pragma unroll
-      for (int kp = 0; kp < KS / 2; ++kp) {
-        uint32_t b0, b1, b2, b3;
-        ldsm4(saddr(Ks + key * HD + swz(key, kp * 4 + (lane >> 3)) * 8), b0, b1, b2, b3);
-        mma_acc(s[nb], qh[2 * kp], b0, b1);
-        mma_acc(s[nb], ql[2 * kp], b0, b1);
-        mma_acc(s[nb], qh[2 * kp + 1], b2, b3);
-        mma_acc(s[nb], ql[2 * kp + 1], b2, b3);
-      }
-    }
-    /* causal mask (key <= the query's position) and the block's softmax */
-    float mxA = -INFINITY, mxB = -INFINITY;
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int key = kb0 + nb * 8 + 2 * t + e;
-        s[nb][e] = key <= pa ? s[nb][e] * p.scale2 : -INFINITY;
-        s[nb][2 + e] = key <= pb ? s[nb][2 + e] * p.scale2 : -INFINITY;
-        mxA = fmaxf(mxA, s[nb][e]);
-        mxB = fmaxf(mxB, s[nb][2 + e]);
-      }
-    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
-    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
-    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
-    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        s[nb][e] = mxA == -INFINITY ? 0.f : exp2f(s[nb][e] - mxA);
-        s[nb][2 + e] = mxB == -INFINITY ? 0.f : exp2f(s[nb][2 + e] - mxB);
-        lA += s[nb][e];
-        lB += s[nb][2 + e];
-      }
-    lA += __shfl_xor_sync(0xffffffffu, lA, 1);
-    lA += __shfl_xor_sync(0xffffffffu, lA, 2);
-    lB += __shfl_xor_sync(0xffffffffu, lB, 1);
-    lB += __shfl_xor_sync(0xffffffffu, lB, 2);
-    mA = mxA;
-    mB = mxB;
-    /* O = P.V: P (fp16) as A fragments straight from the score registers */
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t pf[4] = {pack_h2(s[2 * kk][0], s[2 * kk][1]), pack_h2(s[2 * kk][2], s[2 * kk][3]),
-                              pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]),
-                              pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3])};
-      const int key = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
-#pragma unroll
-      for (int dp = 0; dp < DN / 2; ++dp) {
-        uint32_t b0, b1, b2, b3;
-        ldsm4t(saddr(Vs + key * HD + swz(key, dp * 2 + (lane >> 4)) * 8), b0, b1, b2, b3);
-        mma_acc(o[2 * dp], pf, b0, b1);
-        mma_acc(o[2 * dp + 1], pf, b2, b3);
-      }
-    }
+    score_block<HD>(Ks, qh, ql, kb0, pa, pb, p.scale2, lane, s, mA, mB, lA, lB);
+    pv_block<HD>(Vs, s, lane, o);
   }
 
   /* merge the 4 warp blocks (shared memory, warp order) */
   float* part = reinterpret_cast<float*>(sm); /* [AW][QT][PST], over the K / V staging */
   __syncthreads();
-  {
-    float* pw = part + (size_t)warp * QT * PST;
-#pragma unroll
-    for (int d = 0; d < DN; ++d) {
-      pw[g * PST + 2 + d * 8 + 2 * t] = o[d][0];
-      pw[g * PST + 3 + d * 8 + 2 * t] = o[d][1];
-      pw[(g + 8) * PST + 2 + d * 8 + 2 * t] = o[d][2];
-      pw[(g + 8) * PST + 3 + d * 8 + 2 * t] = o[d][3];
-    }
-    if (t == 0) {
-      pw[g * PST] = mA;
-      pw[g * PST + 1] = lA;
-      pw[(g + 8) * PST] = mB;
-      pw[(g + 8) * PST + 1] = lB;
-    }
-  }
+  write_warp_partial<HD>(part + (size_t)warp * QT * PST, lane, mA, mB, lA, lB, o);
   __syncthreads();
   auto out_ptr = [&](int qi) {
     const int qq = q0 + qi;
@@ -322,18 +408,8 @@ __global__ void __launch_bounds__(AW * 32, 1)
   float* cpart = part + (size_t)AW * QT * PST;
   for (int it = tid; it < QT * (HD / 2); it += AW * 32) {
     const int qi = it / (HD / 2), d2 = it % (HD / 2);
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < AW; ++w) M = fmaxf(M, part[(w * QT + qi) * PST]);
-    float L = 0.f, ox = 0.f, oy = 0.f;
-#pragma unroll
-    for (int w = 0; w < AW; ++w) {
-      const float* pw = part + (size_t)(w * QT + qi) * PST;
-      const float e = pw[0] == -INFINITY ? 0.f : exp2f(pw[0] - M);
-      L = __fmaf_rn(pw[1], e, L);
-      ox = __fmaf_rn(pw[2 + 2 * d2], e, ox);
-      oy = __fmaf_rn(pw[3 + 2 * d2], e, oy);
-    }
+    float M, L, ox, oy;
+    cta_merge_item<HD>(part, (size_t)QT * PST, qi, d2, M, L, ox, oy);
     if (n_splits == 1) {
       if (qi < nq) {
         const float inv = L > 0.f ? 1.0f / L : 0.f;
@@ -371,15 +447,7 @@ __global__ void __launch_bounds__(AW * 32, 1)
         float M = -INFINITY, L = 0.f, ox = 0.f, oy = 0.f;
 #pragma unroll
         for (int u = 0; u < 8; ++u)
-          if (u < n_splits) M = fmaxf(M, mc[u]);
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (u < n_splits) {
-            const float w = mc[u] == -INFINITY ? 0.f : exp2f(mc[u] - M);
-            L = __fmaf_rn(lc[u], w, L);
-            ox = __fmaf_rn(oc[u].x, w, ox);
-            oy = __fmaf_rn(oc[u].y, w, oy);
-          }
+          if (u < n_splits) merge_next(u == 0, mc[u], lc[u], oc[u].x, oc[u].y, M, L, ox, oy);
         const float inv = L > 0.f ? 1.0f / L : 0.f;
         out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
       }
@@ -395,9 +463,8 @@ __global__ void __launch_bounds__(AW * 32, 1)
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  /* merge of the splits in split order, eight splits per memory round trip: a thread owns one
-     (query, output pair) and loads the splits' (max, sum, output pair) together; across
-     chunks of eight the running sums are rescaled to the new max */
+  /* merge of the splits in split order, eight splits' loads per memory round trip: a thread
+     owns one (query, output pair) and loads the splits' (max, sum, output pair) together */
   for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
     const int qi = it / (HD / 2), d2 = it % (HD / 2);
     float M = -INFINITY, L = 0.f, ox = 0.f, oy = 0.f;
@@ -412,30 +479,163 @@ __global__ void __launch_bounds__(AW * 32, 1)
           lc[u] = __ldcg(gp + 1);
           oc[u] = __ldcg(reinterpret_cast<const float2*>(gp + 2) + d2);
         }
-      float Mn = M;
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (c0 + u < n_splits) Mn = fmaxf(Mn, mc[u]);
-      if (c0 > 0 && Mn != M) { /* rescale what the earlier chunks summed */
-        const float r = M == -INFINITY ? 0.f : exp2f(M - Mn);
-        L *= r;
-        ox *= r;
-        oy *= r;
-      }
-      M = Mn;
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (c0 + u < n_splits) {
-          const float w = mc[u] == -INFINITY ? 0.f : exp2f(mc[u] - M);
-          L = __fmaf_rn(lc[u], w, L);
-          ox = __fmaf_rn(oc[u].x, w, ox);
-          oy = __fmaf_rn(oc[u].y, w, oy);
-        }
+        if (c0 + u < n_splits) merge_next(c0 + u == 0, mc[u], lc[u], oc[u].x, oc[u].y, M, L, ox, oy);
     }
     const float inv = L > 0.f ? 1.0f / L : 0.f;
     out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
   }
   if (tid == 0) counters[ti] = 0; /* ready for the next launch / graph replay */
+}
+
+/*
+ * Streaming form for large batches (many sequences x heads, long caches): one CTA per
+ * (16-query tile, kv head, sequence) walks all of the tile's key splits in order, so a CTA
+ * never exits between splits and the split partials never leave the SM.  Per split, warp w
+ * scores its 64-key block exactly as attn_mma_kernel does (same staging, same block
+ * arithmetic, same in-CTA merge), and each thread folds the split's partial of its (query,
+ * output pair) items into a running merge in registers with merge_next, the arithmetic of
+ * the other forms' split merges: a row gets the same bits from either kernel.
+ * Each warp's K and V blocks are a pipeline: the next split's keys are requested as soon as
+ * this split's scores are computed, its values as soon as P.V is done, and the blocks of the
+ * split after that are prefetched into L2 (cp.async.bulk.prefetch), so HBM keeps streaming
+ * while the SM computes.  Shared memory: K [4][64][HD] | V [4][64][HD] | warp partials
+ * [4][16][HD + 2].  No scratch, no counters.
+ */
+template <int HD>
+__global__ void __launch_bounds__(AW * 32, 1)
+    attn_stream_kernel(AttnParams p, const float* __restrict__ q, const __half* __restrict__ kc,
+                       const __half* __restrict__ vc, const int* __restrict__ row_seq,
+                       const int* __restrict__ row_pos, __half* __restrict__ out) {
+  constexpr int KS = HD / 16, DN = HD / 8, PST = HD + 2;
+  constexpr int ITEMS = QT * (HD / 2) / (AW * 32); /* (query, output pair) items per thread */
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int mt = blockIdx.x, kvh = blockIdx.y, gi = blockIdx.z;
+  const int Q = p.G * p.rps, q0 = mt * QT, nq = min(QT, Q - q0);
+  const int m0 = gi * p.rps;
+  const int qa = q0 + g, qb = q0 + g + 8;
+  const bool va = g < nq, vb = g + 8 < nq;
+  int last_pos = lane < nq ? row_pos[m0 + (q0 + lane) / p.G] : 0;
+  const int seq = row_seq[m0];
+  const int pa = va ? row_pos[m0 + qa / p.G] : -1, pb = vb ? row_pos[m0 + qb / p.G] : -1;
+  int first_new = lane < p.rps ? row_pos[m0 + lane] : INT_MAX;
+  for (int r = lane + 32; r < p.rps; r += 32) first_new = min(first_new, row_pos[m0 + r]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    last_pos = max(last_pos, __shfl_xor_sync(0xffffffffu, last_pos, o));
+    first_new = min(first_new, __shfl_xor_sync(0xffffffffu, first_new, o));
+  }
+  last_pos = max(0, min(last_pos, p.cap - 1));
+  const int n_splits = last_pos / SPLITK + 1;
+  if ((unsigned)seq >= (unsigned)p.n_seq) return;
+
+  __half* const Ks = reinterpret_cast<__half*>(sm) + (size_t)warp * KB * HD;
+  __half* const Vs = reinterpret_cast<__half*>(sm) + (size_t)(AW + warp) * KB * HD;
+  float* const part = reinterpret_cast<float*>(sm + (size_t)2 * AW * KB * HD * sizeof(__half));
+  /* this warp's block of split s: its first key, cache offset and key count (<= 0: none) */
+  auto block_of = [&](int s, int& kb0, size_t& kvoff, int& nk) {
+    kb0 = (s * AW + warp) * KB;
+    int page_ok = 1;
+    if (p.max_pages > 0) {
+      const int slot = seq * p.max_pages + s;
+      const int page = p.bt ? p.bt[slot] : slot;
+      page_ok = page >= 0;
+      kvoff = (((size_t)max(page, 0) * p.Hkv + kvh) * kKvPage + warp * KB) * HD;
+    } else {
+      kvoff = (((size_t)seq * p.Hkv + kvh) * p.cap + max(kb0, 0)) * HD;
+    }
+    nk = page_ok ? min(KB, last_pos + 1 - kb0) : 0;
+  };
+  /* the K / V rows of this warp's block of split s on their way to L2 */
+  auto prefetch = [&](int s) {
+    if (s >= n_splits || lane != 0) return;
+    int kb, n;
+    size_t off;
+    block_of(s, kb, off, n);
+    if (n <= 0) return;
+    const uint32_t bytes = (uint32_t)n * HD * sizeof(__half);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kc + off), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vc + off), "r"(bytes) : "memory");
+  };
+  int kb0, nk;
+  size_t kvoff;
+  block_of(0, kb0, kvoff, nk);
+  {
+    /* split 0: the rows that predate this forward before griddepcontrol.wait, the rest after */
+    const int n_old = max(0, min(nk, first_new - kb0));
+    if (nk > 0) {
+      stage_rows<HD>(Ks, kc + kvoff, nk, 0, n_old, lane);
+      stage_rows<HD>(Vs, vc + kvoff, nk, 0, n_old, lane);
+    }
+    prefetch(1); /* a hint into L2, the point of coherence: rows still to be written may go too */
+    pdl_wait();
+    pdl_trigger();
+    if (nk > 0) {
+      stage_rows<HD>(Ks, kc + kvoff, nk, n_old, KB, lane);
+      stage_rows<HD>(Vs, vc + kvoff, nk, n_old, KB, lane);
+    }
+    cp_commit();
+  }
+  const float* qpa = q + (size_t)(m0 + (va ? qa : q0) / p.G) * p.ldq + (kvh * p.G + (va ? qa : q0) % p.G) * HD;
+  const float* qpb = q + (size_t)(m0 + (vb ? qb : q0) / p.G) * p.ldq + (kvh * p.G + (vb ? qb : q0) % p.G) * HD;
+  uint32_t qh[KS][4], ql[KS][4];
+  q_frags<HD>(qpa, qpb, va, vb, t, qh, ql);
+
+  /* the running merge of the splits' partials: thread items it = tid + 128 j */
+  float RM[ITEMS], RL[ITEMS], RX[ITEMS], RY[ITEMS];
+  for (int s = 0; s < n_splits; ++s) {
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+    float o[DN][4];
+#pragma unroll
+    for (int d = 0; d < DN; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
+    float sc[8][4];
+    /* keys of split s (groups pending: K_s, V_s; split 0: one group) */
+    if (s == 0) asm volatile("cp.async.wait_group 0;" ::: "memory");
+    else asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncwarp();
+    if (nk > 0) score_block<HD>(Ks, qh, ql, kb0, pa, pb, p.scale2, lane, sc, mA, mB, lA, lB);
+    __syncwarp();
+    /* this warp's block of the next split: keys now, values once this split's are consumed */
+    int kb1 = 0, nk1 = 0;
+    size_t kvoff1 = 0;
+    if (s + 1 < n_splits) {
+      block_of(s + 1, kb1, kvoff1, nk1);
+      if (nk1 > 0) stage_rows<HD>(Ks, kc + kvoff1, nk1, 0, KB, lane);
+    }
+    cp_commit();
+    prefetch(s + 2);
+    asm volatile("cp.async.wait_group 1;" ::: "memory"); /* V_s */
+    __syncwarp();
+    if (nk > 0) pv_block<HD>(Vs, sc, lane, o);
+    __syncwarp();
+    if (s + 1 < n_splits && nk1 > 0) stage_rows<HD>(Vs, vc + kvoff1, nk1, 0, KB, lane);
+    cp_commit();
+    write_warp_partial<HD>(part + (size_t)warp * QT * PST, lane, mA, mB, lA, lB, o);
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+      const int it = tid + j * AW * 32, qi = it / (HD / 2), d2 = it % (HD / 2);
+      float M, L, ox, oy;
+      cta_merge_item<HD>(part, (size_t)QT * PST, qi, d2, M, L, ox, oy);
+      merge_next(s == 0, M, L, ox, oy, RM[j], RL[j], RX[j], RY[j]);
+    }
+    __syncthreads();
+    kb0 = kb1;
+    nk = nk1;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < ITEMS; ++j) {
+    const int it = tid + j * AW * 32, qi = it / (HD / 2), d2 = it % (HD / 2);
+    if (qi < nq) {
+      const float inv = RL[j] > 0.f ? 1.0f / RL[j] : 0.f;
+      const int qq = q0 + qi;
+      reinterpret_cast<__half2*>(out + (size_t)(m0 + qq / p.G) * p.H * HD + (kvh * p.G + qq % p.G) * HD)[d2] =
+          __floats2half2_rn(RX[j] * inv, RY[j] * inv);
+    }
+  }
 }
 
 void attn_geometry(const ulb_attn_desc* d, int M, int rps, int max_pos, AttnParams* p, int* n_groups) {
@@ -457,6 +657,28 @@ size_t attn_smem(int hd) {
   const size_t kv = (size_t)AW * 2 * KB * hd * sizeof(__half);
   const size_t part = (size_t)(AW + 1) * QT * (hd + 2) * sizeof(float); /* warp partials + the split's */
   return std::max(kv, part);
+}
+/* streaming form: K / V blocks of the 4 warps + their partials */
+size_t attn_stream_smem(int hd) {
+  return (size_t)AW * 2 * KB * hd * sizeof(__half) + (size_t)AW * QT * (hd + 2) * sizeof(float);
+}
+
+/* Which form runs a launch: one CTA per key split (short latency for a few sequences: every
+   split of every head in flight at once) or one CTA walking all splits of its (tile, head,
+   sequence) (throughput for many sequences: no CTA turnover or merge traffic per split).
+   Estimated from the waves each needs: a per-split CTA costs ~12 us of latency at one CTA
+   per SM; a streaming CTA ~6 us plus ~2.5 us per split, two CTAs per SM at head_dim 64.
+   Both forms give a row the same bits, so the choice never changes a result. */
+bool attn_use_stream(const Ctx* c, const AttnParams& p, int ng) {
+  if (c && c->attn_form == ULB_ATTN_SPLIT) return false;
+  if (c && c->attn_form == ULB_ATTN_STREAM) return true;
+  const int n_sm = c ? c->n_sm : 0;
+  if (p.max_splits < 2) return false;
+  const long long base = (long long)p.n_mt * p.Hkv * ng, sm = n_sm > 0 ? n_sm : 148;
+  const long long occ = p.hd == 64 ? 2 : 1;
+  const double t_split = (double)((base * p.max_splits + sm - 1) / sm) * 12.0;
+  const double t_stream = (double)((base + sm * occ - 1) / (sm * occ)) * (6.0 + 2.5 * p.max_splits);
+  return t_stream < 0.8 * t_split; /* a close call stays with the short-latency form */
 }
 
 }  // namespace
@@ -511,6 +733,17 @@ cudaError_t attn_cluster_merge(int max_splits, bool* out) {
 template <int HD>
 cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, const __half* k, const __half* v,
                         const int* row_seq, const int* row_pos, __half* out, float* scratch, int* counters) {
+  if (attn_use_stream(c, p, ng)) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+      attr_err = cudaFuncSetAttribute(attn_stream_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)attn_stream_smem(HD));
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    return launch_k(c, attn_stream_kernel<HD>, dim3(p.n_mt, p.Hkv, ng), dim3(AW * 32), attn_stream_smem(HD), p, q, k,
+                    v, row_seq, row_pos, out);
+  }
   bool cl = false;
   const cudaError_t se = attn_cluster_merge<HD>(p.max_splits, &cl);
   if (se != cudaSuccess) return se;
@@ -551,7 +784,6 @@ int validate_attn_desc(const ulb_attn_desc* d, int M, int rps) {
 
 int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int max_pos, size_t* floats,
                            int* n_counters) {
-  (void)c;
   ULB_TRY(validate_attn_desc(d, M, rps));
   *floats = 0;
   *n_counters = 0;
@@ -559,7 +791,7 @@ int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int m
   AttnParams p;
   int ng;
   attn_geometry(d, M, rps, max_pos, &p, &ng);
-  if (p.max_splits == 1) return ULB_OK;
+  if (attn_use_stream(c, p, ng) || p.max_splits == 1) return ULB_OK;
   bool cl = false;
   const cudaError_t e = d->head_dim == 64 ? attn_cluster_merge<64>(p.max_splits, &cl)
                                           : attn_cluster_merge<128>(p.max_splits, &cl);
@@ -667,6 +899,14 @@ extern "C" int ulb_attention_noalloc(ulb_ctx* ctx, const ulb_attn_desc* d, const
   if (nc > 0) ULB_CUDA(cudaMemsetAsync(counters, 0, (size_t)nc * sizeof(int), c->stream));
   return launch_attention(c, d, q, d->n_head * d->head_dim, (const __half*)k, (const __half*)v, row_seq, row_pos, M,
                           rps, (__half*)out, scratch, counters, kNoAllocScratchFloats, kNoAllocCounters);
+}
+
+extern "C" int ulb_attention_set_form(ulb_ctx* ctx, int form) {
+  ULB_CHECK(ctx, ULB_EINVAL, "ulb_attention_set_form: NULL context");
+  ULB_CHECK(form == ULB_ATTN_AUTO || form == ULB_ATTN_SPLIT || form == ULB_ATTN_STREAM, ULB_EINVAL,
+            "ulb_attention_set_form: form %d (0 auto, 1 split, 2 stream)", form);
+  ctx->c.attn_form = form;
+  return ULB_OK;
 }
 
 extern "C" int ulb_attention_paged(ulb_ctx* ctx, const ulb_attn_desc* d, const float* q, const uint16_t* k_pool,

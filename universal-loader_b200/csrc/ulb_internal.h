@@ -85,6 +85,7 @@ struct Ctx {
   size_t tc_ws_floats = 0;
   int* tc_cnt = nullptr;               /* kTcCounters arrival counters, zero between launches */
   int tp_rank = 0, tp_world = 1;
+  int attn_form = 0; /* ULB_ATTN_AUTO / SPLIT / STREAM */
   /* hint: up to two byte ranges (weights of GEMVs to come) that the next GEMV launched on the
      stream prefetches into L2 from its tail; set just before that launch by the forward
      pass, cleared by every GEMV launch. */

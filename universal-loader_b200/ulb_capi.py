@@ -75,6 +75,7 @@ _SIGS = {
     "ulb_qgemm": (C.c_int, [P, P, P, C.c_int, P, C.c_int]),
     "ulb_attention": (C.c_int, [P, C.POINTER(AttnDesc), P, P, P, P, P, C.c_int, C.c_int, P]),
     "ulb_attention_noalloc": (C.c_int, [P, C.POINTER(AttnDesc), P, P, P, P, P, C.c_int, C.c_int, P]),
+    "ulb_attention_set_form": (C.c_int, [P, C.c_int]),
     "ulb_attention_paged": (C.c_int, [P, C.POINTER(AttnDesc), P, P, P, P, C.c_int, P, P, C.c_int, C.c_int, P]),
     "ulb_sample": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, C.POINTER(Warp), C.c_uint64,
                              C.c_uint32, C.c_uint32, C.c_uint32, P]),
