@@ -899,6 +899,102 @@ int orc_spec_accept(const float* pl, const float* ql, const int32_t* draft, int 
   return 0;
 }
 
+/*
+ * Tree speculation (the reference's TreeSpeculation(vocab, beam_width, max_depth),
+ * src/inference/speculative_decoder.h:62-87, a stub there): a full tree of width w and depth D
+ * whose nodes are numbered breadth first, depth 1 first: node i of depth d has rank
+ * i - first(d) in its level (first(d) = w + w^2 + ... + w^(d-1)), and the children of the
+ * root are nodes 0..w-1, those of node i (depth d < D) first(d+1) + rank * w + c.
+ * p rows [B][1 + N][V]: row 0 the root (the last committed token), row 1 + i node i;
+ * q rows [B][1 + first(D)][V]: row 0 the root, row 1 + i internal node i (depth < D).
+ * tokens [B][N]: the drafted token of each node.
+ * Walk from the root.  T = 0: move to the first child whose token is the target's argmax,
+ * else commit that argmax and stop.  T > 0: multi-candidate speculative sampling (SpecInfer,
+ * Miao et al. 2024): the children are w independent draws from q_u; child c_j is accepted
+ * with probability min(1, P_j(x) / q(x)), where P_1 = p_u and, after each rejection,
+ * P_(j+1) = norm(max(0, P_j - q_u)); when all w are rejected the correction is drawn from
+ * P_(w+1).  In weights: R_1 = max(0, e_p Z_q - e_q Z_p), R_(j+1) = max(0, R_j Z_q - e_q W_j),
+ * W_j = sum of R_j, P_(j+1) = R_j / W_j.  A leaf reached (depth D) draws its bonus from p.
+ * Uniforms: child c's test (slot c, tag 2); the draw at p row r (slot r, tag 3).  With w = 1
+ * this is orc_spec_accept.  Outputs: path[B][D] (nodes accepted, -1 after), n[B], tok[B].
+ */
+static int tree_first(int w, int d) { int f = 0, p = 1; for (int j = 1; j < d; ++j) { p *= w; f += p; } return f; }
+
+int orc_tree_accept(const float* pl, const float* ql, const int32_t* tokens, int B, int width, int depth, int V,
+                    const orc_warp* w, uint64_t seed, uint32_t round, int32_t* out_path, int32_t* out_n,
+                    int32_t* out_tok) {
+  const int N = tree_first(width, depth + 1), NI = tree_first(width, depth);
+  const int greedy = !(w->temperature > 0.0f);
+  double* p = (double*)malloc((size_t)V * 8);
+  double* q = (double*)malloc((size_t)V * 8);
+  double* r = (double*)malloc((size_t)V * 8);
+  for (int b = 0; b < B; ++b) {
+    int n = 0, tok = -1, u = -1, d = 0; /* u = -1: the root */
+    for (int j = 0; j < depth; ++j) out_path[b * depth + j] = -1;
+    while (tok < 0) {
+      const int prow = u + 1;
+      const float* pu = pl + ((size_t)b * (1 + N) + prow) * V;
+      if (d == depth) { /* a leaf: the bonus token from p */
+        if (greedy) tok = argmax_f(pu, V);
+        else {
+          double Zp;
+          orc_warp_weights(pu, V, w, p, &Zp);
+          tok = inv_cdf(p, V, orc_uniform(seed, round, (uint32_t)b, (uint32_t)prow, 3));
+        }
+        break;
+      }
+      const int c0 = u < 0 ? 0 : tree_first(width, d + 1) + (u - tree_first(width, d)) * width;
+      if (greedy) {
+        const int a = argmax_f(pu, V);
+        int next = -1;
+        for (int c = 0; c < width; ++c)
+          if (tokens[b * N + c0 + c] == a) { next = c0 + c; break; }
+        if (next < 0) { tok = a; break; }
+        out_path[b * depth + n++] = next;
+        u = next;
+        ++d;
+        continue;
+      }
+      const float* qu = ql + ((size_t)b * (1 + NI) + prow) * V;
+      double Zp, Zq, W = 0.0;
+      orc_warp_weights(pu, V, w, p, &Zp);
+      orc_warp_weights(qu, V, w, q, &Zq);
+      int next = -1, level = 0; /* level j: P_(j+1) = r / W after j rejections */
+      for (int c = 0; c < width && next < 0; ++c) {
+        const int x = tokens[b * N + c0 + c];
+        const int ok = (unsigned)x < (unsigned)V;
+        const double qx = ok ? q[x] / Zq : 0.0;
+        double px;
+        if (level == 0) px = ok ? p[x] / Zp : 0.0;
+        else px = ok && W > 0.0 ? r[x] / W : 0.0;
+        const float ua = orc_uniform(seed, round, (uint32_t)b, (uint32_t)(c0 + c), 2);
+        if ((double)ua * qx < px) { next = c0 + c; break; }
+        if (level > 0 && !(W > 0.0)) continue; /* nothing left to remove */
+        double tot = 0.0;
+        for (int v = 0; v < V; ++v) {
+          const double t = level == 0 ? p[v] * Zq - q[v] * Zp : r[v] * Zq - q[v] * W;
+          r[v] = t > 0.0 ? t : 0.0;
+          tot += r[v];
+        }
+        W = tot;
+        ++level;
+      }
+      if (next >= 0) {
+        out_path[b * depth + n++] = next;
+        u = next;
+        ++d;
+        continue;
+      }
+      const float u2 = orc_uniform(seed, round, (uint32_t)b, (uint32_t)prow, 3);
+      tok = W > 0.0 ? inv_cdf(r, V, u2) : inv_cdf(p, V, u2);
+    }
+    out_n[b] = n;
+    out_tok[b] = tok;
+  }
+  free(p); free(q); free(r);
+  return 0;
+}
+
 static double top2_margin(const float* l, int V) {
   float a = -INFINITY, b = -INFINITY;
   for (int i = 0; i < V; ++i) {

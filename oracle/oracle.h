@@ -95,6 +95,11 @@ int orc_warp_weights(const float* logits, int V, const orc_warp* w, double* e, d
 /* warped probabilities e / Z; returns 0 */
 int orc_warp_probs(const float* logits, int V, const orc_warp* w, double* probs);
 int orc_sample(const float* logits, int V, const orc_warp* w, float u);
+/* tree speculation acceptance (see oracle.c): p rows [B][1+N][V], q rows [B][1+NI][V],
+   tokens [B][N] in breadth-first node order; path [B][depth], n [B], tok [B] */
+int orc_tree_accept(const float* p_logits, const float* q_logits, const int32_t* tokens, int B, int width,
+                    int depth, int V, const orc_warp* w, uint64_t seed, uint32_t round, int32_t* out_path,
+                    int32_t* out_n, int32_t* out_tok);
 int orc_spec_accept(const float* p_logits, const float* q_logits, const int32_t* draft, int B,
                     int k, int V, const orc_warp* w, uint64_t seed, uint32_t round,
                     int32_t* out_tokens, int32_t* out_n);

@@ -62,6 +62,8 @@ def lib():
         L.orc_sample.argtypes = [P, C.c_int, C.POINTER(Warp), C.c_float]
         L.orc_spec_accept.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.POINTER(Warp),
                                       C.c_uint64, C.c_uint32, P, P]
+        L.orc_tree_accept.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(Warp),
+                                      C.c_uint64, C.c_uint32, P, P, P]
         L.orc_spec_generate.argtypes = [P, P, C.c_int, P, P, C.c_int, C.c_int, C.c_int,
                                         C.POINTER(Warp), C.c_uint64, P, P, P,
                                         C.POINTER(C.c_double), P]
@@ -170,6 +172,42 @@ def spec_accept(p_logits, q_logits, draft, warp, seed, rnd):
     lib().orc_spec_accept(_p(p_logits), _p(q_logits), _p(draft), B, k, V, C.byref(w), seed, rnd,
                           _p(out), _p(n))
     return out, n
+
+
+def tree_nodes(width, depth):
+    """nodes of a full tree of this width and depth (breadth first, the root not counted)"""
+    return sum(width ** d for d in range(1, depth + 1))
+
+
+def tree_children(width, depth, node):
+    """breadth-first indices of the children of `node` (-1: the root)"""
+    if node < 0:
+        return list(range(width))
+    d, first = 1, 0
+    while node >= first + width ** d:
+        first += width ** d
+        d += 1
+    if d >= depth:
+        return []
+    nxt = first + width ** d
+    return [nxt + (node - first) * width + c for c in range(width)]
+
+
+def tree_accept(p_logits, q_logits, tokens, width, depth, warp, seed, rnd):
+    """orc_tree_accept: p [B][1 + N][V], q [B][1 + internal][V], tokens [B][N] -> path [B][depth]
+    (accepted nodes, -1 after), n [B], tok [B]"""
+    p_logits = np.ascontiguousarray(p_logits, np.float32)
+    q_logits = np.ascontiguousarray(q_logits, np.float32)
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    B = tokens.shape[0]
+    V = p_logits.shape[-1]
+    path = np.full((B, depth), -1, np.int32)
+    n = np.empty(B, np.int32)
+    tok = np.empty(B, np.int32)
+    w = Warp(*warp)
+    lib().orc_tree_accept(_p(p_logits), _p(q_logits), _p(tokens), B, width, depth, V, C.byref(w), seed, rnd,
+                          _p(path), _p(n), _p(tok))
+    return path, n, tok
 
 
 class Model:

@@ -1,7 +1,8 @@
 """GPU parity of the sm_100a kernels against the CPU oracle, through the C ABI.
 
 Bars: dequantised weights bit-exact; GEMM relative error <= 1e-2 of the fp32-accumulate
-oracle (observed ~1e-6: both apply each block's scale to an exact integer dot product);
+oracle (observed ~1e-6 in the GEMV regime, where both apply each block's scale to an exact
+integer dot product; ~2e-4 in the tensor-core regimes, which round each weight once to fp16);
 attention within 2e-3 absolute on fp16 outputs; identical accept/reject decisions and
 sampled tokens when both sides get the same logits and Philox uniforms."""
 import ctypes as C
@@ -15,6 +16,9 @@ from oracle import ulb_oracle as orc
 pytestmark = pytest.mark.gpu
 
 GEMM_RTOL = 1e-2  # GEMM outputs within 1e-2 relative error (fp32 accumulate)
+# the tensor-core regimes (M > 32 rows) round each dequantised weight once to fp16 (<= 2^-12
+# relative per weight; ~2e-4 of the largest output on these shapes); the GEMV keeps them exact
+TC_RTOL = 1e-3
 
 
 def _q40(rng, N, K):
@@ -78,7 +82,7 @@ def test_qgemm_matches_oracle_small(ctx, qt, M):
     finally:
         ctx.free_tensor(h)
     ref = orc.qgemv(t, raw, N, K, x)
-    assert _rel(y, ref) < 1e-5, _rel(y, ref)
+    assert _rel(y, ref) < (1e-5 if M <= 32 else TC_RTOL), _rel(y, ref)
 
 
 @pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
@@ -106,13 +110,13 @@ def test_qgemm_op_sweep(ctx, qt, NK, M):
                   {M - 1})
     ref = orc.qgemv(t, raw, N, K, x[rows])
     assert _rel(y[rows], ref) < GEMM_RTOL
-    assert _rel(y[rows], ref) < 1e-4
+    assert _rel(y[rows], ref) < (1e-4 if M <= 32 else TC_RTOL)
     # within a regime every row is computed with the same arithmetic whatever M is
     assert np.array_equal(y_last, y[M - 1])
-    # across regimes (tensor-core GEMM vs GEMV) rows agree to fp32 accumulation order: the GEMM
-    # chains K/16 fp32 tensor-core accumulations over the whole row (a Q4_K weight d*sc*q - dmin*m
-    # is also rounded once to fp32 there); the GEMV sums scaled 32-weight blocks
-    assert _rel(y[M - 1], y_gemv) < 1e-4
+    # across regimes (tensor-core GEMM vs GEMV) rows agree to the GEMM's fp16 weights and fp32
+    # accumulation order: the GEMM chains K/16 fp32 tensor-core accumulations over the whole row
+    # of fp16-rounded weights; the GEMV sums scaled 32-weight blocks of exact weights
+    assert _rel(y[M - 1], y_gemv) < (1e-4 if M <= 32 else TC_RTOL)
 
 
 @pytest.mark.parametrize("qt", ["q4_0", "q4_k"])
@@ -134,7 +138,7 @@ def test_qgemm_split_regime_in_several_launches(ctx, qt):
         ctx.free_tensor(h)
     pick = [0, 63, 64, 191, 192, 249]  # rows on both sides of the launch boundaries
     ref = orc.qgemv(t, raw, N, K, x[pick])
-    assert _rel(y[pick], ref) < 1e-4
+    assert _rel(y[pick], ref) < TC_RTOL
     assert np.array_equal(y[M - 33:], y33)
     assert np.array_equal(y, y_again)
 

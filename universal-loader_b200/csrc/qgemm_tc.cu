@@ -11,13 +11,15 @@
  * One CTA computes a 128-weight-row x NT-token tile of y = W x^T over the whole of K, fed by
  * TMA (each copy to this CTA only): one 3-D tensor-map load per packed K-tile brings the 8 strips'
  * raw Q4 bytes, one 2-D load per 64-k stage brings the activation tile already in the
- * 128-byte-swizzled K-major layout; 8 warps dequantise each stage into fp16 hi and lo parts
- * (hi = fp16(w), lo = fp16(w - hi): a Q4_0 weight d (q - 8) has <= 15 significant bits, so
- * hi + lo == w exactly) in the same layout; one lane issues tcgen05.mma (M = 128, N = NT,
- * K = 16, fp16 x fp16 -> fp32 in TMEM) twice per k-step (hi, lo) and commits each stage to
- * the mbarriers that free its slots; the 8 warps then read TMEM and run the epilogue.
- * From kTcWideRows rows on, parallelism comes from the token tile (64 ... 256 tokens, the
- * largest that still gives a CTA per SM) and K is never split; below that (33 ... 255 rows)
+ * 128-byte-swizzled K-major layout; 8 warps dequantise each stage into fp16 weights in the
+ * same layout, each weight rounded once to fp16 (a Q4_0 weight d (q - 8) is the correctly
+ * rounded product of two exact fp16 values; a Q4_K weight d sc q - dmin m is formed in fp32
+ * first), so a weight carries at most 2^-12 relative error here, where the GEMV regime keeps
+ * weights exact; one lane issues tcgen05.mma (M = 128, N = NT, K = 16, fp16 x fp16 -> fp32 in
+ * TMEM) once per k-step and commits each stage to the mbarriers that free its slots; the 8
+ * warps then read TMEM and run the epilogue.
+ * From kTcWideRows rows on, parallelism comes from the token tile (64 ... 256 tokens, the one
+ * with the shortest estimated makespan over the SMs) and K is never split; below that (33 ... 255 rows)
  * the tile is 64 tokens and K is split S ways, S fixed per matrix (tc_splits), with the
  * partials added in split order.  Either way a row's summation order does not depend on M.
  * Every mbarrier wait has a deadline (2 s): past it the CTA raises bit 3 of the device error
@@ -156,13 +158,13 @@ __device__ __forceinline__ void q4k_scale_min(const uint8_t* s12, int j, int& sc
 template <int QT, int NT>
 struct TcCfg {
   static constexpr int TB = QT == ULB_TYPE_Q4_0 ? kQ40TileBytes : kQ4KTileBytes;
-  static constexpr int A_BYTES = 2 * BM * KS * 2;        /* 32 KB: dequantised hi + lo parts     */
+  static constexpr int A_BYTES = BM * KS * 2;            /* 16 KB: dequantised fp16 weights      */
   static constexpr int B_BYTES = NT * KS * 2;            /* activation tile (TMA, 128 B swizzle) */
   static constexpr int RAW_BYTES = 8 * TB;               /* one packed K-tile of the 8 strips    */
   /* ring depths: A slots cover dequantise + MMA, activation slots an L2 round trip, and the
      raw-weight ring (K-tiles of 2 or 4 stages) the several-microsecond latency of weight
      tiles streamed by every SM at once */
-  static constexpr int SA = NT <= 128 ? 3 : 2;
+  static constexpr int SA = NT <= 128 ? 6 : 4;
   static constexpr int SB = NT == 64 ? 8 : 3;
   static constexpr int RT = QT == ULB_TYPE_Q4_0 ? (NT == 192 ? 8 : 6) : (NT == 192 ? 4 : 3);
   static constexpr int SMEM = SA * A_BYTES + SB * B_BYTES + RT * RAW_BYTES + 1024; /* + alignment slack */
@@ -203,7 +205,7 @@ constexpr int kTmaBox = 144; /* u64 words per weight box: a Q4_0 tile, half a Q4
  *          128-byte swizzle writes the K-major layout the MMA reads; rows past M are zero)
  *   1      raw weights: one TMA load per packed K-tile (two for Q4_K) of all 8 strips into
  *          the raw ring; weights do not depend on earlier kernels, so it never waits for them
- *   2 - 9  dequantise raw -> A ring (hi, lo; two threads per weight row), then the epilogue
+ *   2 - 9  dequantise raw -> A ring (fp16; two threads per weight row), then the epilogue
  *          from TMEM (two warps per TMEM lane quarter, each half of the token columns)
  *   10     TMEM owner; lane 0 issues tcgen05.mma and commits to the A / B free barriers
  */
@@ -298,7 +300,6 @@ __global__ void __launch_bounds__(TCW * 32, 1)
       if (i >= SA && !mb_wait(&free_a[ai], (uint32_t)((i / SA) - 1) & 1u, deadline)) { ok = false; break; }
       const uint8_t* slot = raw_ring + rs * C::RAW_BYTES;
       uint8_t* ahi = a_ring + ai * C::A_BYTES;
-      uint8_t* alo = ahi + C::A_BYTES / 2;
       float s = 0.f, mm = 0.f;
       __half2 d2;
       if (QT == ULB_TYPE_Q4_0) {
@@ -320,16 +321,12 @@ __global__ void __launch_bounds__(TCW * 32, 1)
         const int c = bb * 4 + t4;
         const uint32_t word =
             *reinterpret_cast<const uint32_t*>(tile_byte(slot, part * 512 + (g * 4 + t4) * 16 + (bb * 2 + hr) * 4));
-        uint32_t hi[4], lo[4];
+        uint32_t hi[4];
         if (QT == ULB_TYPE_Q4_0) {
           uint32_t q[4];
           nib4<8>(word, q);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __half2 h = __hmul2(u2h(q[e]), d2);               /* fp16(d (q - 8)) */
-            hi[e] = h2u(h);
-            lo[e] = h2u(__hfma2(u2h(q[e]), d2, __hneg2(h)));        /* exact remainder */
-          }
+          for (int e = 0; e < 4; ++e) hi[e] = h2u(__hmul2(u2h(q[e]), d2)); /* fp16(d (q - 8)), one rounding */
         } else {
           uint32_t q[4];
           nib4<0>(word, q);
@@ -337,15 +334,11 @@ __global__ void __launch_bounds__(TCW * 32, 1)
           for (int e = 0; e < 4; ++e) {
             const float2 qf = __half22float2(u2h(q[e]));
             const float w0 = __fmaf_rn(s, qf.x, -mm), w1 = __fmaf_rn(s, qf.y, -mm);
-            const __half2 h = __floats2half2_rn(w0, w1);
-            const float2 hf = __half22float2(h);
-            hi[e] = h2u(h);
-            lo[e] = h2u(__floats2half2_rn(w0 - hf.x, w1 - hf.y));
+            hi[e] = h2u(__floats2half2_rn(w0, w1));
           }
         }
         const uint32_t off = sw128_off(r, c);
         *reinterpret_cast<uint4*>(ahi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(alo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
       fence_async_smem();
       __syncwarp();
@@ -367,13 +360,10 @@ __global__ void __launch_bounds__(TCW * 32, 1)
             !mb_wait(&full_b[bi], (uint32_t)(i / SB) & 1u, deadline)) { ok = false; break; }
         tc_fence_after();
         uint8_t* ah = a_ring + ai * C::A_BYTES;
-        const uint64_t dh = sw128_desc(sa(ah)), dl = sw128_desc(sa(ah + C::A_BYTES / 2)),
-                       db = sw128_desc(sa(b_ring + bi * C::B_BYTES));
+        const uint64_t dh = sw128_desc(sa(ah)), db = sw128_desc(sa(b_ring + bi * C::B_BYTES));
 #pragma unroll
-        for (int kk = 0; kk < KS / 16; ++kk) { /* 32 bytes of K per step: +2 in the address field */
+        for (int kk = 0; kk < KS / 16; ++kk) /* 32 bytes of K per step: +2 in the address field */
           umma(tmem, dh + 2 * kk, db + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-          umma(tmem, dl + 2 * kk, db + 2 * kk, idesc, 1u);
-        }
         umma_commit(&free_a[ai]);
         umma_commit(&free_b[bi]);
       }
@@ -457,14 +447,25 @@ __global__ void __launch_bounds__(TCW * 32, 1)
   }
 }
 
-/* token tile: the largest of 256 / 192 / 128 / 64 that still gives one CTA per SM; tiles
-   of the weights x tiles of the tokens is the whole grid (K is never split) */
+/* token tile of the wide regime: tiles of the weights x tiles of the tokens is the whole grid
+   (K is never split, and the tile width does not change a row's summation order), so pick the
+   width with the shortest estimated makespan: waves of CTAs x per-CTA time, a CTA's time per
+   64-k stage being the larger of its dequantisation (~fixed) and its MMAs (~NT) */
 inline int tc_ntile(const Ctx* c, const Tensor* w, int M) {
-  const int n_wt = (w->n_strips + 7) / 8;
+  const long long n_wt = (w->n_strips + 7) / 8, sm = c->n_sm > 0 ? c->n_sm : 148;
   const int cand[4] = {256, 192, 128, 64};
-  for (int i = 0; i < 4; ++i)
-    if ((long long)n_wt * ((M + cand[i] - 1) / cand[i]) >= c->n_sm) return cand[i];
-  return 64;
+  int best_nt = 64;
+  double best = -1.0;
+  for (int i = 0; i < 4; ++i) {
+    const long long ctas = n_wt * ((M + cand[i] - 1) / cand[i]);
+    const double waves = (double)((ctas + sm - 1) / sm);
+    const double cost = waves * std::max(320.0, 2.9 * cand[i]) + 0.02 * cand[i];
+    if (best < 0 || cost < best) {
+      best = cost;
+      best_nt = cand[i];
+    }
+  }
+  return best_nt;
 }
 
 /*
