@@ -354,10 +354,46 @@ typedef struct ulb_spec_desc {
   int kv_pages;     /* 0: every sequence slot owns pages for its whole capacity;
                        > 0: a pool of this many pages per model, mapped to the slots
                        as their sequences grow and returned when they finish     */
+  int tree_width;   /* 0 or 1: a chain of k drafts per round; >= 2: tree speculation, a
+                       full tree of this width and depth k (the reference's
+                       TreeSpeculation(vocab, beam_width, max_depth),
+                       src/inference/speculative_decoder.h:62-87, a stub there): k draft
+                       steps over the tree's levels, one verify over all its nodes with
+                       tree attention, multi-candidate acceptance (ulb_spec_tree_accept);
+                       at most 63 nodes (width^1 + ... + width^k) and width <= 8 */
 } ulb_spec_desc;
 
 ULB_API int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft,
                     const ulb_spec_desc* desc, ulb_spec** out);
+
+/*
+ * Acceptance of speculation trees (one per sequence), the decision of a tree round.  A tree
+ * of width w and depth D has N = w + w^2 + ... + w^D nodes numbered breadth first from depth 1
+ * (node i of depth d has rank r = i - first(d), first(d) = w + ... + w^(d-1); the root's
+ * children are nodes 0..w-1, node i's are first(d+1) + r*w + c).  The root is the last
+ * committed token.
+ *   dev_p       fp32 target logits [B][1 + N][V]: row 0 the root, row 1 + i node i
+ *   dev_q       fp32 draft logits [B][1 + NI][V] of the root and the NI = first(D) internal
+ *               nodes (the distributions the children were drawn from)
+ *   dev_tokens  int32 [B][N] the drafted token of each node
+ * From the root, the children of the current node are tested in order: T = 0, the first whose
+ * token is the target's argmax is accepted; T > 0, multi-candidate speculative sampling
+ * (SpecInfer, Miao et al. 2024, for children drawn independently from q): child c_j is
+ * accepted with probability min(1, P_j(x) / q(x)), P_1 = p and P_(j+1) = norm(max(0, P_j - q))
+ * after each rejection; the first accepted child becomes the current node.  When all children
+ * are rejected the correction is drawn from the last residual (T = 0: the argmax); a leaf
+ * reached adds a bonus token from its p.  Uniforms: Philox (seed, round, sequence b, slot,
+ * tag) with the child's node index as slot for its test (ULB_RNG_ACCEPT) and the node's p row
+ * as slot for a correction / bonus draw (ULB_RNG_RESID).  A tree of width 1 is the chain of
+ * ulb_spec_accept.
+ *   dev_path    int32 [B][D]: the accepted nodes, -1 after;  dev_n int32 [B]: their number;
+ *   dev_tok     int32 [B]: the correction / bonus token.
+ * Replaces TreeSpeculation::generate_tree_speculation / verify_tree
+ * (src/inference/speculative_decoder.cpp:118-176, which returns its placeholder tree).
+ */
+ULB_API int ulb_spec_tree_accept(ulb_ctx* ctx, const float* dev_p, const float* dev_q, const int32_t* dev_tokens,
+                         int B, int width, int depth, int V, const ulb_warp* warp, uint64_t seed,
+                         uint32_t round, int32_t* dev_path, int32_t* dev_n, int32_t* dev_tok);
 /* Copy prompts (host int32 [n_seq][max_prompt], lengths [n_seq]) and prefill both models;
  * commits the first generated token of every sequence. */
 ULB_API int ulb_spec_prefill(ulb_spec* s, const int32_t* host_prompts, const int32_t* host_prompt_lens);

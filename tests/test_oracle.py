@@ -317,3 +317,104 @@ def test_spec_sampling_is_lossless_chi2():
     chi2 = ((counts - exp) ** 2 / exp).sum()
     assert chi2 < 25.0, (chi2, counts, exp)  # 5 dof, p ~ 1e-4
     assert not np.allclose(p, q)
+
+
+# ---------------------------------------------------------------- speculation trees (oracle)
+def _tree_inputs(rng, B, w, D, V, warp, seed=4, rnd=2, agree=0.5):
+    """p / q logits of every tree row and children drawn as the GPU loop draws them: the w
+    most likely tokens (T = 0) or w independent draws from the warped q (slot = child node)."""
+    N, NI = orc.tree_nodes(w, D), orc.tree_nodes(w, D - 1)
+    pl = (rng.standard_normal((B, 1 + N, V)) * 2).astype(np.float32)
+    ql = (rng.standard_normal((B, 1 + NI, V)) * 2).astype(np.float32)
+    nb = int(B * agree)
+    ql[:nb] = pl[:nb, :1 + NI] + 0.3 * ql[:nb]  # drafts that often agree with the target
+    tok = np.zeros((B, N), np.int32)
+    for b in range(B):
+        for u in [-1] + list(range(NI)):
+            ch = orc.tree_children(w, D, u)
+            lq = ql[b, u + 1]
+            if warp[0] <= 0:
+                order = np.argsort(-lq, kind="stable")  # most likely first, lowest index on ties
+                for c, t in zip(ch, order[:w]):
+                    tok[b, c] = t
+            else:
+                for c in ch:
+                    tok[b, c] = orc.sample(lq, orc.uniform(seed, rnd, b, c, 1), *warp)
+    return pl, ql, tok
+
+
+def test_tree_geometry():
+    assert orc.tree_nodes(2, 3) == 14 and orc.tree_nodes(3, 2) == 12 and orc.tree_nodes(1, 5) == 5
+    assert orc.tree_children(2, 3, -1) == [0, 1]
+    assert orc.tree_children(2, 3, 1) == [4, 5]
+    assert orc.tree_children(2, 3, 5) == [12, 13]
+    assert orc.tree_children(2, 3, 6) == []  # depth-3 leaves
+
+
+@pytest.mark.parametrize("warp", [(0.0, 0, 1.0), (1.0, 0, 1.0), (0.8, 40, 1.0)])
+def test_tree_of_width_one_is_the_chain(warp):
+    """A tree of width 1 is a chain of k drafts: the same decisions and tokens as orc_spec_accept
+    given the same logits and uniforms."""
+    rng = np.random.default_rng(21)
+    B, D, V = 24, 4, 500
+    pl, ql, tok = _tree_inputs(rng, B, 1, D, V, warp)
+    path, n, t = orc.tree_accept(pl, ql, tok, 1, D, warp, 4, 2)
+    out, n2 = orc.spec_accept(pl, ql, tok, warp, 4, 2)
+    assert n.tolist() == n2.tolist()
+    for b in range(B):
+        assert path[b, :n[b]].tolist() == list(range(n[b]))
+        assert t[b] == out[b, n[b]]
+    assert n.max() > 0 and n.min() < D
+
+
+def test_tree_greedy_walk_known_answers():
+    """T = 0: the walk follows the child equal to the target's argmax; p == q accepts every level
+    through the first children and ends with the bonus argmax of the leaf."""
+    rng = np.random.default_rng(5)
+    B, w, D, V = 6, 3, 3, 80
+    pl, ql, tok = _tree_inputs(rng, B, w, D, V, (0.0, 0, 1.0), agree=0.0)
+    NI = orc.tree_nodes(w, D - 1)
+    ql = pl[:, :1 + NI].copy()
+    # children: top-3 of q == p; every level's argmax is its first child
+    for b in range(B):
+        for u in [-1] + list(range(NI)):
+            order = np.argsort(-ql[b, u + 1], kind="stable")
+            for c, x in zip(orc.tree_children(w, D, u), order[:w]):
+                tok[b, c] = x
+    path, n, t = orc.tree_accept(pl, ql, tok, w, D, (0.0, 0, 1.0), 1, 0)
+    assert n.tolist() == [D] * B
+    for b in range(B):
+        assert path[b].tolist() == [0, w, w + w * w]  # the first child at every level
+        assert t[b] == int(np.argmax(pl[b, 1 + path[b, -1]]))
+    # the second child holds the argmax at the root: the walk goes there and stops below it
+    tok[:, 1] = tok[:, 0]
+    tok[:, 0] = (tok[:, 1] + 1) % V
+    for b in range(B):
+        tok[b, w + w:w + 2 * w] = (np.argmax(pl[b, 2]) + 1 + np.arange(w)) % V  # no child of node 1 matches
+    path, n, t = orc.tree_accept(pl, ql, tok, w, D, (0.0, 0, 1.0), 1, 0)
+    assert n.tolist() == [1] * B and path[:, 0].tolist() == [1] * B
+    for b in range(B):
+        assert t[b] == int(np.argmax(pl[b, 2]))
+
+
+def test_tree_sampling_is_lossless_chi2():
+    """Multi-candidate speculative sampling keeps the target distribution: with w = 3 children
+    drawn independently from q at the root, the first committed token is distributed as p."""
+    V, w = 6, 3
+    rng = np.random.default_rng(8)
+    p_log = (rng.standard_normal(V) * 1.5).astype(np.float32)
+    q_log = (rng.standard_normal(V) * 1.5).astype(np.float32)
+    p = orc.warp_probs(p_log, 1.0)
+    B = 6000
+    pl = np.broadcast_to(p_log, (B, 1 + w, V)).copy()
+    ql = np.broadcast_to(q_log, (B, 1, V)).copy()
+    tok = np.array([[orc.sample(q_log, orc.uniform(13, 0, b, c, 1), 1.0) for c in range(w)] for b in range(B)],
+                   np.int32)
+    path, n, t = orc.tree_accept(pl, ql, tok, w, 1, (1.0, 0, 1.0), 13, 0)
+    first = np.where(n > 0, tok[np.arange(B), np.maximum(path[:, 0], 0)], t)
+    counts = np.bincount(first, minlength=V)
+    chi2 = ((counts - p * B) ** 2 / (p * B)).sum()
+    assert chi2 < 25.0, (chi2, counts, p * B)  # 5 dof, p ~ 1e-4
+    # and more candidates are accepted than with one child
+    path1, n1, _ = orc.tree_accept(pl[:, :2], ql, tok[:, :1], 1, 1, (1.0, 0, 1.0), 13, 0)
+    assert n.sum() > n1.sum()

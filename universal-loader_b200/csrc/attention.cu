@@ -47,6 +47,11 @@ struct AttnParams {
   /* paged cache (max_pages > 0; one page = one key split): block table bt, NULL = identity */
   const int* bt;
   int max_pages;
+  /* tree rows (speculation trees): row m sees the keys before tpref[m] and the keys
+     tpref[m] + j for each set bit j of tmask[m] (its ancestors and itself); NULL = causal by
+     position (key <= row_pos[m]) */
+  const int* tpref;
+  const unsigned long long* tmask;
 };
 static_assert(SPLITK == kKvPage, "a key split is one KV cache page");
 
@@ -155,10 +160,22 @@ __device__ __forceinline__ void q_frags(const float* qpa, const float* qpb, bool
 
 /* scores of the tile against the 64 keys from kb0 in Ks, causal mask (key <= the query's
    position), the block softmax: s becomes exp2(s - m) (unnormalised P), l its row sums */
-template <int HD>
+/* the visibility of `key` to a row: causal (key <= pos), or for a tree row the keys before
+   its prefix end and the set bits of its mask after it */
+template <bool TREE>
+__device__ __forceinline__ bool key_visible(int key, int pos, int pref, unsigned long long mask) {
+  if (!TREE) return key <= pos;
+  if (key < pref) return true;
+  const unsigned j = (unsigned)(key - pref);
+  return j < 64u && ((mask >> j) & 1ull) != 0ull;
+}
+
+template <int HD, bool TREE = false>
 __device__ __forceinline__ void score_block(const __half* Ks, const uint32_t (&qh)[HD / 16][4],
                                             const uint32_t (&ql)[HD / 16][4], int kb0, int pa, int pb, float scale2,
-                                            int lane, float (&s)[8][4], float& mA, float& mB, float& lA, float& lB) {
+                                            int lane, float (&s)[8][4], float& mA, float& mB, float& lA, float& lB,
+                                            int prA = 0, int prB = 0, unsigned long long mkA = 0ull,
+                                            unsigned long long mkB = 0ull) {
   constexpr int KS = HD / 16;
   const int t = lane & 3;
 #pragma unroll
@@ -181,8 +198,8 @@ __device__ __forceinline__ void score_block(const __half* Ks, const uint32_t (&q
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int key = kb0 + nb * 8 + 2 * t + e;
-      s[nb][e] = key <= pa ? s[nb][e] * scale2 : -INFINITY;
-      s[nb][2 + e] = key <= pb ? s[nb][2 + e] * scale2 : -INFINITY;
+      s[nb][e] = key_visible<TREE>(key, pa, prA, mkA) ? s[nb][e] * scale2 : -INFINITY;
+      s[nb][2 + e] = key_visible<TREE>(key, pb, prB, mkB) ? s[nb][2 + e] * scale2 : -INFINITY;
       mxA = fmaxf(mxA, s[nb][e]);
       mxB = fmaxf(mxB, s[nb][2 + e]);
     }
@@ -294,7 +311,7 @@ __device__ __forceinline__ void merge_next(bool first, float m, float l, float o
   M = Mn;
 }
 
-template <int HD, bool CL>
+template <int HD, bool CL, bool TREE>
 __global__ void __launch_bounds__(AW * 32, 1)
     attn_mma_kernel(AttnParams p, const float* __restrict__ q, const __half* __restrict__ kc,
                     const __half* __restrict__ vc, const int* __restrict__ row_seq, const int* __restrict__ row_pos,
@@ -324,6 +341,12 @@ __global__ void __launch_bounds__(AW * 32, 1)
   int last_pos = lane < nq ? row_pos[m0 + (q0 + lane) / p.G] : 0;
   const int seq = row_seq[m0];
   const int pa = va ? row_pos[m0 + qa / p.G] : -1, pb = vb ? row_pos[m0 + qb / p.G] : -1;
+  int prA = 0, prB = 0;
+  unsigned long long mkA = 0ull, mkB = 0ull;
+  if (TREE) {
+    if (va) { prA = p.tpref[m0 + qa / p.G]; mkA = p.tmask[m0 + qa / p.G]; }
+    if (vb) { prB = p.tpref[m0 + qb / p.G]; mkB = p.tmask[m0 + qb / p.G]; }
+  }
   /* and the first position this forward wrote for the sequence (rows m0 .. m0 + rps - 1) */
   int first_new = lane < p.rps ? row_pos[m0 + lane] : INT_MAX;
   for (int r = lane + 32; r < p.rps; r += 32) first_new = min(first_new, row_pos[m0 + r]);
@@ -389,7 +412,7 @@ __global__ void __launch_bounds__(AW * 32, 1)
     cp_wait_all();
     __syncwarp();
     float s[8][4];
-    score_block<HD>(Ks, qh, ql, kb0, pa, pb, p.scale2, lane, s, mA, mB, lA, lB);
+    score_block<HD, TREE>(Ks, qh, ql, kb0, pa, pb, p.scale2, lane, s, mA, mB, lA, lB, prA, prB, mkA, mkB);
     pv_block<HD>(Vs, s, lane, o);
   }
 
@@ -669,7 +692,8 @@ size_t attn_stream_smem(int hd) {
    Estimated from the waves each needs: a per-split CTA costs ~12 us of latency at one CTA
    per SM; a streaming CTA ~6 us plus ~2.5 us per split, two CTAs per SM at head_dim 64.
    Both forms give a row the same bits, so the choice never changes a result. */
-bool attn_use_stream(const Ctx* c, const AttnParams& p, int ng) {
+bool attn_use_stream(const Ctx* c, const AttnParams& p, int ng, bool tree) {
+  if (tree) return false; /* tree masks: the per-split form only */
   if (c && c->attn_form == ULB_ATTN_SPLIT) return false;
   if (c && c->attn_form == ULB_ATTN_STREAM) return true;
   const int n_sm = c ? c->n_sm : 0;
@@ -695,10 +719,16 @@ cudaError_t attn_setup(const bool** cl_ok_out) {
   static cudaError_t attr_err = cudaSuccess;
   static bool cl_ok[9] = {false}; /* max_splits -> cluster form schedulable */
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)attn_smem(HD));
     if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)attn_smem(HD));
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)attn_smem(HD));
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)attn_smem(HD));
     for (int s = 2; s <= 8 && attr_err == cudaSuccess; ++s) {
       cudaLaunchConfig_t cfg = {};
@@ -713,7 +743,7 @@ cudaError_t attn_setup(const bool** cl_ok_out) {
       cfg.attrs = a;
       cfg.numAttrs = 1;
       int n = 0;
-      cl_ok[s] = cudaOccupancyMaxActiveClusters(&n, attn_mma_kernel<HD, true>, &cfg) == cudaSuccess && n > 0;
+      cl_ok[s] = cudaOccupancyMaxActiveClusters(&n, attn_mma_kernel<HD, true, false>, &cfg) == cudaSuccess && n > 0;
       cudaGetLastError();
     }
   });
@@ -733,7 +763,7 @@ cudaError_t attn_cluster_merge(int max_splits, bool* out) {
 template <int HD>
 cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, const __half* k, const __half* v,
                         const int* row_seq, const int* row_pos, __half* out, float* scratch, int* counters) {
-  if (attn_use_stream(c, p, ng)) {
+  if (attn_use_stream(c, p, ng, p.tmask != nullptr)) {
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [] {
@@ -761,7 +791,8 @@ cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, con
   a[1].val.clusterDim.z = cl ? p.max_splits : 1;
   cfg.attrs = a;
   cfg.numAttrs = cl ? 2 : 1;
-  auto kern = cl ? attn_mma_kernel<HD, true> : attn_mma_kernel<HD, false>;
+  auto kern = p.tmask ? (cl ? attn_mma_kernel<HD, true, true> : attn_mma_kernel<HD, false, true>)
+                      : (cl ? attn_mma_kernel<HD, true, false> : attn_mma_kernel<HD, false, false>);
   prefer_max_shared((const void*)kern);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, q, k, v, row_seq, row_pos, out, scratch, counters);
   if (e == cudaSuccess) ++c->launches;
@@ -783,15 +814,15 @@ int validate_attn_desc(const ulb_attn_desc* d, int M, int rps) {
 }
 
 int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int max_pos, size_t* floats,
-                           int* n_counters) {
+                           int* n_counters, bool tree) {
   ULB_TRY(validate_attn_desc(d, M, rps));
   *floats = 0;
   *n_counters = 0;
   if (M == 0) return ULB_OK;
-  AttnParams p;
+  AttnParams p{};
   int ng;
   attn_geometry(d, M, rps, max_pos, &p, &ng);
-  if (attn_use_stream(c, p, ng) || p.max_splits == 1) return ULB_OK;
+  if (attn_use_stream(c, p, ng, tree) || p.max_splits == 1) return ULB_OK;
   bool cl = false;
   const cudaError_t e = d->head_dim == 64 ? attn_cluster_merge<64>(p.max_splits, &cl)
                                           : attn_cluster_merge<128>(p.max_splits, &cl);
@@ -805,22 +836,25 @@ int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int m
 int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, const __half* k,
                      const __half* v, const int* row_seq, const int* row_pos, int M, int rps,
                      __half* out, float* scratch, int* counters, size_t scratch_floats, int n_counters,
-                     const int* bt, int max_pages) {
+                     const int* bt, int max_pages, const int* tree_pref, const unsigned long long* tree_mask) {
   ULB_TRY(validate_attn_desc(d, M, rps));
   ULB_CHECK(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 && ldq % 4 == 0,
             ULB_EINVAL, "attention: q / k / v must be 16-byte aligned (ldq a multiple of 4)");
   if (M == 0) return ULB_OK;
-  AttnParams p;
+  AttnParams p{};
   int ng;
   attn_geometry(d, M, rps, d->capacity - 1, &p, &ng);
   p.ldq = ldq;
   p.bt = bt;
   p.max_pages = max_pages;
+  p.tpref = tree_pref;
+  p.tmask = tree_mask;
+  ULB_CHECK(!tree_mask == !tree_pref, ULB_EINVAL, "attention: tree rows need both prefix ends and masks");
   ULB_CHECK(max_pages == 0 || (long long)max_pages * kKvPage >= d->capacity, ULB_EINVAL,
             "attention: %d pages of %d positions per sequence cannot hold capacity %d", max_pages, kKvPage, d->capacity);
   int need_c = 0;
   size_t need = 0;
-  ULB_TRY(attention_scratch_need(c, d, M, rps, d->capacity - 1, &need, &need_c));
+  ULB_TRY(attention_scratch_need(c, d, M, rps, d->capacity - 1, &need, &need_c, tree_mask != nullptr));
   ULB_CHECK(need == 0 || (scratch && counters && scratch_floats >= need && n_counters >= need_c), ULB_EINVAL,
             "attention: scratch %zu floats / %d counters, need %zu / %d", scratch_floats, n_counters, need, need_c);
   ULB_CHECK((long long)ng * p.max_splits <= 65535, ULB_EUNSUPPORTED, "attention: %d sequences x %d splits", ng,

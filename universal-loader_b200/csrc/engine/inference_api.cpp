@@ -19,7 +19,8 @@
  *    returns 0, inference_engine.cpp:793-799).
  * Additions (the reference cannot name a draft model): load_draft_model, unload_draft_model,
  * set_speculation_length (as SpeculativeDecoder::set_speculation_length,
- * speculative_decoder.h:40), set_seed, GenerationConfig.seed, generate_tokens,
+ * speculative_decoder.h:40), enable_tree_speculation (TreeSpeculation's beam_width /
+ * max_depth, speculative_decoder.h:62-87), set_seed, GenerationConfig.seed, generate_tokens,
  * get_last_stats, and the module function write_synthetic_gguf.
  * Text: a registered custom tokenizer first; else the target GGUF's SentencePiece vocabulary
  * (tokenizer.ggml.*, tokenizer.cpp) when it has one; else byte-fallback ids (byte b -> id
@@ -305,6 +306,14 @@ class InferenceAPI {
   }
   void enable_multi_gpu(bool e) { std::lock_guard<std::mutex> lk(mu_); multi_gpu_ = e; }
   void set_speculation_length(uint32_t k) { std::lock_guard<std::mutex> lk(mu_); spec_k_ = (int)k; }
+  /* TreeSpeculation(vocab, beam_width, max_depth) (speculative_decoder.h:62-87): each round
+     drafts a full tree of beam_width children per node and max_depth levels and verifies it
+     in one target pass; beam_width <= 1 goes back to a chain of set_speculation_length drafts */
+  void enable_tree_speculation(uint32_t beam_width, uint32_t max_depth) {
+    std::lock_guard<std::mutex> lk(mu_);
+    tree_width_ = beam_width >= 2 ? (int)beam_width : 0;
+    if (tree_width_) spec_k_ = (int)max_depth;
+  }
   void set_seed(uint64_t s) { std::lock_guard<std::mutex> lk(mu_); config_.seed = s; }
 
   float get_acceptance_rate() const {
@@ -444,6 +453,7 @@ class InferenceAPI {
     p.seed = cfg.seed ? cfg.seed : config_.seed;
     const bool spec = spec_enabled_ && engine_->has_model(true) && spec_k_ > 0;
     p.k = spec ? spec_k_ : 0;
+    p.tree_width = spec ? tree_width_ : 0;
     p.max_batch = (int)max_batch_;
     last_spec_ = spec;
     return engine_->generate(in, p, out, &last_);
@@ -484,6 +494,7 @@ class InferenceAPI {
   GenerationConfig config_{};
   bool spec_enabled_ = false, multi_gpu_ = false, profiling_ = false, quant_enabled_ = false, last_spec_ = false;
   int spec_k_ = 5;
+  int tree_width_ = 0;
   uint32_t max_batch_ = 64, threads_ = 8;
   size_t cache_mb_ = 1024;
   std::string wq_ = "NONE", aq_ = "NONE";
@@ -624,6 +635,9 @@ PYBIND11_MODULE(vulkangguf, m) {
            py::arg("nccl_id"), "Join a tensor-parallel NCCL communicator before load_model (one GPU per process)")
       .def("unload_draft_model", &InferenceAPI::unload_draft_model, "Unload the draft model")
       .def("set_speculation_length", &InferenceAPI::set_speculation_length, "Draft tokens per round (k)")
+      .def("enable_tree_speculation", &InferenceAPI::enable_tree_speculation, py::arg("beam_width"),
+           py::arg("max_depth"),
+           "Tree speculation: beam_width candidates per node, max_depth levels per round (beam_width < 2: chain)")
       .def("set_seed", &InferenceAPI::set_seed, "Seed of the Philox sampler")
       .def("generate_tokens", &InferenceAPI::generate_tokens, py::arg("prompt_tokens"), py::arg("config"),
            "Generate from token ids; list[int] -> list[int] or list[list[int]] -> list[list[int]]")

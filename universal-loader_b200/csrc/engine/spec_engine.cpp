@@ -151,10 +151,13 @@ bool Engine::generate(const std::vector<std::vector<int32_t>>& prompts, const Ge
   sd.seed = p.seed;
   sd.use_graphs = p.use_graphs ? 1 : 0;
   sd.kv_pages = p.kv_pages;
+  sd.tree_width = use_draft && p.tree_width >= 2 ? p.tree_width : 0;
   if (continuous && sd.kv_pages == 0) {
     /* the slots share one pool (as much as every slot's capacity): pages follow the live
        sequences and a finished sequence's pages serve the next prompt */
-    const int cap = max_prompt + (int)p.max_new + 2 * sd.k + 2;
+    int nodes = 0;
+    for (int d = 1, pw = 1; sd.tree_width >= 2 && d <= sd.k; ++d) nodes += (pw *= sd.tree_width);
+    const int cap = max_prompt + (int)p.max_new + 2 * sd.k + 2 + nodes;
     sd.kv_pages = sd.n_seq * ((cap + ULB_KV_PAGE - 1) / ULB_KV_PAGE);
   }
   const bool same = spec_ && spec_has_draft_ == use_draft && !memcmp(&sd, &spec_desc_, sizeof sd);

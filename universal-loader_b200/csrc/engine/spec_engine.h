@@ -38,6 +38,8 @@ struct GenParams {
   int max_batch = 0;
   /* KV cache pages per model (0: every slot owns its whole capacity; otherwise on demand) */
   int kv_pages = 0;
+  /* tree speculation: children per node (>= 2; 0 = a chain of k drafts); k is the depth */
+  int tree_width = 0;
 };
 
 /* One round of the speculative loop for one sequence, as the reference's SpeculationResult

@@ -61,7 +61,8 @@ __device__ __forceinline__ void epilogue_token(const EpiArgs& e, int strip, int 
       /* RoPE-permuted strip: row g = feature f0 + 2g, row g + 8 = feature f0 + 2g + 1 */
       const int f = f0 + 2 * g;
       const int pair = (f % e.hd) >> 1;
-      const float2 cs = e.rope[(size_t)pos * (e.hd >> 1) + pair];
+      const int rpos = e.row_rope ? e.row_rope[tok] : pos;
+      const float2 cs = e.rope[(size_t)rpos * (e.hd >> 1) + pair];
       const float y0 = __fmaf_rn(vg, cs.x, -__fmul_rn(vg8, cs.y));
       const float y1 = __fmaf_rn(vg, cs.y, __fmul_rn(vg8, cs.x));
       if (f < e.nq) {

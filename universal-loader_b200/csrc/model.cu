@@ -213,12 +213,12 @@ static int ensure_ws(Model* m, int rows) {
   return ULB_OK;
 }
 
-static int ensure_attn(KV* kv, int M, int rps) {
+static int ensure_attn(KV* kv, int M, int rps, bool tree) {
   const ulb_model_desc& d = kv->m->d;
   ulb_attn_desc ad{d.n_head, d.n_head_kv, d.head_dim, kv->cap, kv->n_seq, 1.0f / std::sqrt((float)d.head_dim)};
   int nc = 0;
   size_t nf = 0;
-  ULB_TRY(attention_scratch_need(kv->m->c, &ad, M, rps, kv->cap - 1, &nf, &nc));
+  ULB_TRY(attention_scratch_need(kv->m->c, &ad, M, rps, kv->cap - 1, &nf, &nc, tree));
   if (nf <= kv->attn_floats && nc <= kv->n_counters) return ULB_OK;
   /* grow to the largest shape seen so far: every prepared shape must keep fitting */
   const size_t f2 = nf > kv->attn_floats ? nf : kv->attn_floats;
@@ -237,9 +237,9 @@ static int ensure_attn(KV* kv, int M, int rps) {
 
 /* Make workspaces large enough for a forward of M rows (rps per sequence).  Must be called
  * before a forward is captured into a CUDA graph. */
-int model_prepare(Model* m, KV* kv, int M, int rps) {
+int model_prepare(Model* m, KV* kv, int M, int rps, bool tree) {
   ULB_TRY(ensure_ws(m, M));
-  ULB_TRY(ensure_attn(kv, M, rps));
+  ULB_TRY(ensure_attn(kv, M, rps, tree));
   return ULB_OK;
 }
 
@@ -277,8 +277,61 @@ static int forward_head(Model* m, int M, int rps, int logits_mode, float* logits
                           m->x16, n_out, EPI_STORE, o);
 }
 
+/* After a tree round: sequence s accepted n = comp[s][1] nodes; node comp[s][2 + j] sits in
+   cache slot L + node (L = comp[s][0]) and moves to its sequence position L + j, in every layer,
+   K and V.  Grid (layers, sequences); each thread copies the same 16-byte chunks of every row
+   it moves, in path order, so a row moved into a later node's old slot was read first (the
+   destinations L + j never exceed a later node's source). */
+__global__ void kv_tree_compact_kernel(__half* __restrict__ kc, __half* __restrict__ vc, size_t layer_elems, int Hkv,
+                                       int hd, int cap, const int* __restrict__ bt, int max_pages,
+                                       const int32_t* __restrict__ comp, int D) {
+  pdl_wait();
+  pdl_trigger();
+  const int l = blockIdx.x, s = blockIdx.y;
+  const int32_t* cp = comp + (size_t)s * (2 + D);
+  const int L = cp[0], n = cp[1];
+  __half* kl = kc + (size_t)l * layer_elems;
+  __half* vl = vc + (size_t)l * layer_elems;
+  /* the head-0 row of position pos, heads `hs` elements apart; false for an unmapped page */
+  auto row_of = [&](int pos, size_t* base, size_t* hs) -> bool {
+    if (max_pages > 0) {
+      const int slot = s * max_pages + pos / kKvPage;
+      const int page = bt ? bt[slot] : slot;
+      if (page < 0) return false;
+      *base = ((size_t)page * Hkv * kKvPage + pos % kKvPage) * hd;
+      *hs = (size_t)kKvPage * hd;
+    } else {
+      *base = ((size_t)s * Hkv * cap + pos) * hd;
+      *hs = (size_t)cap * hd;
+    }
+    return true;
+  };
+  const int cpr = hd / 8; /* 16-byte chunks per head row */
+  for (int j = 0; j < n; ++j) {
+    const int src = L + cp[2 + j], dst = L + j;
+    size_t sb, db, hs;
+    if (src == dst || src >= cap || dst < 0 || !row_of(src, &sb, &hs) || !row_of(dst, &db, &hs)) continue;
+    for (int e = threadIdx.x; e < Hkv * cpr; e += blockDim.x) {
+      const int h = e / cpr, c = e % cpr;
+      const size_t a = sb + h * hs + c * 8, b = db + h * hs + c * 8;
+      *reinterpret_cast<uint4*>(kl + b) = *reinterpret_cast<const uint4*>(kl + a);
+      *reinterpret_cast<uint4*>(vl + b) = *reinterpret_cast<const uint4*>(vl + a);
+    }
+  }
+}
+
+int kv_tree_compact(KV* kv, const int32_t* comp, int S, int D) {
+  Model* m = kv->m;
+  const ulb_model_desc& d = m->d;
+  cudaError_t e = launch_k(m->c, kv_tree_compact_kernel, dim3(d.n_layer, S), dim3(256), 0, kv->k, kv->v,
+                           kv->layer_elems, d.n_head_kv, d.head_dim, kv->cap, (const int*)(kv->identity ? nullptr : kv->bt),
+                           kv->max_pages, comp, D);
+  if (e != cudaSuccess) return cuda_error(e, "tree cache compaction", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
 int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos, int logits_mode,
-                  float* logits, int ld, int* err) {
+                  float* logits, int ld, int* err, const TreeRows* tree) {
   Ctx* c = m->c;
   const ulb_model_desc& d = m->d;
   ULB_CHECK(m->finalized, ULB_EINVAL, "forward: model not finalized");
@@ -297,6 +350,7 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     a.nq = m->nq; a.nkv = m->nkv; a.hd = d.head_dim; a.cap = kv->cap; a.n_head_kv = d.n_head_kv; a.n_seq = kv->n_seq;
     a.row_seq = seq; a.row_pos = pos; a.rope = kv->rope;
     a.bt = kv->identity ? nullptr : kv->bt; a.max_pages = kv->max_pages;
+    a.row_rope = tree ? tree->rope : nullptr;
     /* GEMV tails prefetch the weights of the GEMVs to come into L2 (the hint is set just
        before the launch whose tail issues it) */
     auto hint = [c](const Tensor* t, const Tensor* t2 = nullptr) {
@@ -311,7 +365,7 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     ULB_TRY(launch_qgemv_rms(c, &L.qkv, m->x, d.d_model, L.attn_norm, d.rms_eps, m->x16, M, EPI_QKV, a));
     ULB_TRY(launch_attention(c, &ad, m->qb, m->nq, kc, vc, seq, pos, M, rps, m->att, kv->attn_scratch,
                              kv->attn_counters, kv->attn_floats, kv->n_counters, kv->identity ? nullptr : kv->bt,
-                             kv->max_pages));
+                             kv->max_pages, tree ? tree->pref : nullptr, tree ? tree->mask : nullptr));
     EpiArgs r;
     r.y = m->x; r.ldy = d.d_model;
     /* tensor parallel: this rank's heads / features give a partial sum of attn_output and

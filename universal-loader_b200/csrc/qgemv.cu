@@ -962,6 +962,7 @@ static int launch_qgemv_impl(Ctx* c, const Tensor* w, const __half* x, int M, in
     if (a.q) a.q += (size_t)m0 * a.ldq;
     if (a.row_seq) a.row_seq += m0;
     if (a.row_pos) a.row_pos += m0;
+    if (a.row_rope) a.row_rope += m0;
     int rc;
     switch (epi) {
       case EPI_STORE: rc = launch_epi<EPI_STORE>(c, w, xc, mc, ldx, a); break;

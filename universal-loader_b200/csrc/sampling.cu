@@ -432,9 +432,9 @@ __global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ lo
   if (threadIdx.x == 0) out[(size_t)row * out_stride] = tok;
 }
 
-/* stats for p rows [B][k+1] followed by q rows [B][k] */
-__global__ void __launch_bounds__(ST) stats_kernel(const float* __restrict__ p, const float* __restrict__ q, int B,
-                                                   int k, int V, ulb_warp w, RowStats* __restrict__ out) {
+/* stats for np p rows followed by nq q rows */
+__global__ void __launch_bounds__(ST) stats_kernel(const float* __restrict__ p, const float* __restrict__ q, int np,
+                                                   int nq, int V, ulb_warp w, RowStats* __restrict__ out) {
   __shared__ SmemRed<ST> s;
   __shared__ SelSmem sel;
   __shared__ RowStats st;
@@ -442,7 +442,7 @@ __global__ void __launch_bounds__(ST) stats_kernel(const float* __restrict__ p, 
   pdl_trigger();
   /* persistent: few rows in flight per SM, so a row read by the max pass is still in L2
      when the later passes read it again */
-  const int np = B * (k + 1), rows = np + B * k;
+  const int rows = np + nq;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const float* l = row < np ? p + (size_t)row * V : q + (size_t)(row - np) * V;
     compute_row_stats(l, V, w, st, s, sel);
@@ -565,6 +565,253 @@ __global__ void __launch_bounds__(DT) decide_kernel(const float* __restrict__ p,
   }
 }
 
+/* ------------------------------------------------------------------ speculation trees */
+/* argmax over the row, lowest index on ties, skipping the n indices in excl */
+template <int BT>
+__device__ int block_argmax_excl(const float* l, int V, const int* excl, int n, SmemRed<BT>& s) {
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += BT) {
+    bool skip = false;
+    for (int j = 0; j < n; ++j) skip |= excl[j] == i;
+    const float x = l[i];
+    if (!skip && (x > bv || (x == bv && i < bi))) { bv = x; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) { s.f[threadIdx.x >> 5] = bv; s.i[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  bv = s.f[0]; bi = s.i[0];
+  for (int w = 1; w < BT / 32; ++w)
+    if (s.f[w] > bv || (s.f[w] == bv && s.i[w] < bi)) { bv = s.f[w]; bi = s.i[w]; }
+  __syncthreads();
+  return bi == 0x7fffffff ? 0 : bi;
+}
+
+/*
+ * The children of the tree nodes of one level from the draft's logits of their parents: one
+ * CTA per parent row (row m of the level: sequence m / w^d, parent rank m % w^d; level 0 is
+ * the root).  Greedy: the w most probable tokens in order (lowest index on ties); sampled: w
+ * independent draws from the warped q, child c with the uniform (round, sequence, slot c,
+ * draft tag).  tokens [S][N] get the children's tokens.
+ */
+__global__ void __launch_bounds__(RT) tree_children_kernel(const float* __restrict__ logits, int V, int w, int d,
+                                                           ulb_warp wp, uint64_t seed,
+                                                           const uint32_t* __restrict__ dev_round, int N,
+                                                           int32_t* tokens) {
+  __shared__ SmemRed<RT> s;
+  __shared__ SelSmem sel;
+  __shared__ RowStats st;
+  __shared__ int picked[kTreeMaxWidth];
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x;
+  int per = 1;
+  for (int j = 0; j < d; ++j) per *= w;
+  const int seq = m / per, r = m % per;
+  const int c0 = d == 0 ? 0 : tree_first(w, d + 1) + r * w;
+  const float* l = logits + (size_t)m * V;
+  if (!(wp.temperature > 0.f)) {
+    for (int c = 0; c < w; ++c) {
+      const int t = block_argmax_excl<RT>(l, V, picked, c, s);
+      if (threadIdx.x == 0) picked[c] = t;
+      __syncthreads();
+    }
+  } else {
+    compute_row_stats(l, V, wp, st, s, sel);
+    __syncthreads();
+    const float iT = __fdiv_rn(1.0f, wp.temperature);
+    const RowStats stc = st;
+    const uint32_t rnd = dev_round ? dev_round[seq] : 0u;
+    for (int c = 0; c < w; ++c) {
+      const float u = rng_u(seed, rnd, (uint32_t)seq, (uint32_t)(c0 + c), ULB_RNG_DRAFT);
+      const int t = block_inv_cdf(V, u, [&](int i) { return warped_e(l, i, iT, stc); }, s, nullptr);
+      if (threadIdx.x == 0) picked[c] = t;
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x < w) tokens[(size_t)seq * N + c0 + threadIdx.x] = picked[threadIdx.x];
+}
+
+struct TreeShape {
+  int w, D, N, NI;
+  /* q rows: level-major (the loop: level 0 = the S roots, then level d's S * w^d rows) or
+     sequence-major [S][1 + NI] (ulb_spec_tree_accept) */
+  bool q_level_major;
+  int S;
+};
+/* q row of (sequence b, node u; u < 0 = the root) */
+__device__ __forceinline__ int tree_qrow(const TreeShape& t, int b, int u) {
+  if (!t.q_level_major) return b * (1 + t.NI) + 1 + u;
+  if (u < 0) return b;
+  const int d = tree_depth(t.w, u);
+  int per = 1;
+  for (int j = 0; j < d; ++j) per *= t.w;
+  return t.S * (1 + tree_first(t.w, d)) + b * per + (u - tree_first(t.w, d));
+}
+
+/* outputs of a tree round: the accepted nodes [B][D] (-1 after), their count, the correction /
+   bonus token, and for the cache compaction [B][2 + D]: the length before the round, n, path */
+struct TreeOut {
+  int32_t* path;
+  int32_t* n;
+  int32_t* tok;
+  int32_t* comp;
+};
+
+/*
+ * The walk of one sequence's tree, one CTA per sequence (multi-candidate speculative sampling;
+ * the arithmetic of orc_tree_accept): the root's children are tested in order against p_root
+ * (and the residuals left by each rejection), the first accepted one becomes the next node,
+ * and so on; the correction comes from the last residual, the bonus of a leaf from its p.
+ * With a commit struct the committed tokens go to the history as in decide_kernel.
+ */
+__global__ void __launch_bounds__(DT) tree_decide_kernel(const float* __restrict__ p, const float* __restrict__ q,
+                                                         const int32_t* __restrict__ tokens,
+                                                         const RowStats* __restrict__ rs, TreeShape t, int V,
+                                                         ulb_warp wp, uint64_t seed, const uint32_t* dev_round,
+                                                         uint32_t round, TreeOut out, SpecCommit cm) {
+  __shared__ SmemRed<DT> s;
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x;
+  const bool greedy = !(wp.temperature > 0.f);
+  const float iT = greedy ? 1.f : __fdiv_rn(1.0f, wp.temperature);
+  const uint32_t rnd = dev_round ? dev_round[b] : round;
+  const int np = t.S * (1 + t.N);
+  int n = 0, tok = -1, u = -1, d = 0;
+  int path[8]; /* depth <= 5 for width >= 2 (at most 63 nodes) */
+  float pcommit[17];
+  while (tok < 0) {
+    const int prow = b * (1 + t.N) + u + 1;
+    const RowStats sp = rs[prow];
+    const float* pl = p + (size_t)prow * V;
+    if (d == t.D) { /* a leaf: the bonus from p */
+      if (greedy) {
+        tok = sp.amax;
+        pcommit[n] = 1.0f;
+      } else {
+        const float u2 = rng_u(seed, rnd, (uint32_t)b, (uint32_t)(u + 1), ULB_RNG_RESID);
+        tok = block_inv_cdf(V, u2, [&](int v) { return warped_e(pl, v, iT, sp); }, s, nullptr);
+        pcommit[n] = (float)(warped_e(pl, tok, iT, sp) / sp.Z);
+      }
+      break;
+    }
+    const int c0 = u < 0 ? 0 : tree_first(t.w, d + 1) + (u - tree_first(t.w, d)) * t.w;
+    if (greedy) {
+      int next = -1;
+      for (int c = 0; c < t.w && next < 0; ++c)
+        if (tokens[(size_t)b * t.N + c0 + c] == sp.amax) next = c0 + c;
+      pcommit[n] = 1.0f;
+      if (next < 0) { tok = sp.amax; break; }
+      path[n++] = next;
+      u = next;
+      ++d;
+      continue;
+    }
+    const int qrow = tree_qrow(t, b, u);
+    const RowStats sq = rs[np + qrow];
+    const float* ql = q + (size_t)qrow * V;
+    /* R_1 = max(0, e_p Z_q - e_q Z_p), R_(j+1) = max(0, R_j Z_q - e_q W_j), W_j = sum of R_j */
+    double W[kTreeMaxWidth + 1];
+    int level = 0;
+    auto resid = [&](int v) -> double {
+      const double eq = warped_e(ql, v, iT, sq);
+      double r = warped_e(pl, v, iT, sp) * sq.Z - eq * sp.Z;
+      r = r > 0.0 ? r : 0.0;
+      for (int j = 1; j < level; ++j) {
+        r = r * sq.Z - eq * W[j];
+        r = r > 0.0 ? r : 0.0;
+      }
+      return r;
+    };
+    int next = -1;
+    bool dead = false; /* a residual summed to zero: nothing left to accept from */
+    for (int c = 0; c < t.w; ++c) {
+      const int x = tokens[(size_t)b * t.N + c0 + c];
+      const bool ok = (unsigned)x < (unsigned)V;
+      const double qx = ok ? warped_e(ql, x, iT, sq) / sq.Z : 0.0;
+      double px;
+      if (level == 0) px = ok ? warped_e(pl, x, iT, sp) / sp.Z : 0.0;
+      else px = ok && !dead ? resid(x) / W[level] : 0.0;
+      const float ua = rng_u(seed, rnd, (uint32_t)b, (uint32_t)(c0 + c), ULB_RNG_ACCEPT);
+      if ((double)ua * qx < px) {
+        next = c0 + c;
+        pcommit[n] = (float)(warped_e(pl, x, iT, sp) / sp.Z);
+        break;
+      }
+      if (dead) continue;
+      ++level;
+      double part = 0.0;
+      for (int v = threadIdx.x; v < V; v += DT) part += resid(v);
+      W[level] = block_sum_d<DT>(part, s);
+      dead = !(W[level] > 0.0);
+    }
+    if (next >= 0) {
+      path[n++] = next;
+      u = next;
+      ++d;
+      continue;
+    }
+    const float u2 = rng_u(seed, rnd, (uint32_t)b, (uint32_t)(u + 1), ULB_RNG_RESID);
+    if (!dead && level > 0) tok = block_inv_cdf(V, u2, resid, s, nullptr);
+    else tok = block_inv_cdf(V, u2, [&](int v) { return warped_e(pl, v, iT, sp); }, s, nullptr);
+    pcommit[n] = (float)(warped_e(pl, tok, iT, sp) / sp.Z);
+  }
+  if (threadIdx.x != 0) return;
+  if (out.path) {
+    for (int j = 0; j < t.D; ++j) out.path[b * t.D + j] = j < n ? path[j] : -1;
+    out.n[b] = n;
+    out.tok[b] = tok;
+  }
+  if (cm.hist) {
+    const int L = cm.L[b];
+    if (out.comp) {
+      int32_t* cp = out.comp + (size_t)b * (2 + t.D);
+      cp[0] = L;
+      cp[1] = cm.done[b] ? 0 : n;
+      for (int j = 0; j < t.D; ++j) cp[2 + j] = j < n ? path[j] : -1;
+    }
+    if (!cm.done[b]) {
+      int32_t* h = cm.hist + (size_t)b * cm.hist_len;
+      for (int i = 0; i < n; ++i) h[L + i] = tokens[(size_t)b * t.N + path[i]];
+      h[L + n] = tok;
+      cm.L[b] = L + n + 1;
+      if (L + n + 1 - cm.prompt_len[b] >= cm.max_new) cm.done[b] = 1;
+      atomicAdd(&cm.stats[1], (unsigned long long)t.D);
+      atomicAdd(&cm.stats[2], (unsigned long long)n);
+      atomicAdd(&cm.stats[3], (unsigned long long)(n + 1));
+      const int a = cm.active[b];
+      if (cm.log && a < cm.log_rounds && t.D <= 16) {
+        int32_t* r = cm.log + ((size_t)b * cm.log_rounds + a) * cm.log_stride;
+        r[ULB_SPEC_REC_N_ACCEPTED] = n;
+        r[ULB_SPEC_REC_TOKEN] = tok;
+        r[ULB_SPEC_REC_POSITION] = L;
+        r[ULB_SPEC_REC_K] = t.D;
+        /* the drafts of the round's record: the accepted path, then the first candidate of the
+           node where the walk stopped and of its first descendants */
+        int v = n > 0 ? path[n - 1] : -1;
+        for (int i = 0; i < t.D; ++i) {
+          if (i < n) {
+            r[ULB_SPEC_REC_DRAFTS + i] = tokens[(size_t)b * t.N + path[i]];
+          } else {
+            v = v < 0 ? 0 : tree_first(t.w, i + 1) + (v - tree_first(t.w, i)) * t.w;
+            r[ULB_SPEC_REC_DRAFTS + i] = tokens[(size_t)b * t.N + v];
+          }
+        }
+        for (int i = 0; i <= n; ++i) r[ULB_SPEC_REC_DRAFTS + t.D + i] = __float_as_int(pcommit[i]);
+      }
+      cm.active[b] = a + 1;
+    }
+    cm.round[b] = rnd + 1;
+  }
+}
+
 }  // namespace
 
 int launch_sample_seq(Ctx* c, const float* logits, int rows, int V, int ld, const ulb_warp* w, uint64_t seed,
@@ -614,7 +861,7 @@ int launch_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* dr
   /* rows in flight (one per CTA): as many as keep ~60 MB of rows in L2, between 1 and 3 per SM */
   const int fit = (int)std::min<long long>(3LL * c->n_sm, std::max<long long>(c->n_sm, 60000000LL / ((long long)V * 4)));
   const int grid = std::min(rows, fit);
-  cudaError_t e = launch_k(c, stats_kernel, dim3(grid), dim3(ST), 0, p, q, B, k, V, *w, rs);
+  cudaError_t e = launch_k(c, stats_kernel, dim3(grid), dim3(ST), 0, p, q, B * (k + 1), B * k, V, *w, rs);
   if (e != cudaSuccess) return cuda_error(e, "stats launch", __FILE__, __LINE__);
   SpecCommit cm = {};
   if (commit) cm = *(const SpecCommit*)commit;
@@ -630,9 +877,82 @@ int launch_spec_accept(Ctx* c, const float* p, const float* q, const int32_t* dr
   return launch_accept_impl(c, p, q, draft, B, k, V, w, seed, dev_round, round, out_tokens, out_n, scratch, nullptr);
 }
 
+size_t tree_accept_scratch_bytes(int B, int w, int D) {
+  return sizeof(RowStats) * (size_t)B * (2 + tree_first(w, D + 1) + tree_first(w, D));
+}
+
+int launch_tree_children(Ctx* c, const float* logits, int rows, int V, int w, int d, const ulb_warp* wp,
+                         uint64_t seed, const uint32_t* dev_round, int N, int32_t* tokens) {
+  if (rows == 0) return ULB_OK;
+  cudaError_t e = launch_k(c, tree_children_kernel, dim3(rows), dim3(RT), 0, logits, V, w, d, *wp, seed, dev_round, N,
+                           tokens);
+  if (e != cudaSuccess) return cuda_error(e, "tree children launch", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
+/* stats of every p and q row of the trees, then the walk of each sequence's tree */
+static int launch_tree_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* tokens, int B, int w, int D,
+                                   int V, const ulb_warp* wp, uint64_t seed, const uint32_t* dev_round, uint32_t round,
+                                   bool q_level_major, void* stats_scratch, const TreeOut& out, const SpecCommit& cm) {
+  if (B == 0) return ULB_OK;
+  TreeShape t;
+  t.w = w;
+  t.D = D;
+  t.N = tree_first(w, D + 1);
+  t.NI = tree_first(w, D);
+  t.q_level_major = q_level_major;
+  t.S = B;
+  RowStats* rs = (RowStats*)stats_scratch;
+  const int np = B * (1 + t.N), nq = B * (1 + t.NI);
+  const int fit = (int)std::min<long long>(3LL * c->n_sm, std::max<long long>(c->n_sm, 60000000LL / ((long long)V * 4)));
+  const int grid = std::min(np + nq, fit);
+  cudaError_t e = launch_k(c, stats_kernel, dim3(grid), dim3(ST), 0, p, q, np, nq, V, *wp, rs);
+  if (e != cudaSuccess) return cuda_error(e, "stats launch", __FILE__, __LINE__);
+  e = launch_k(c, tree_decide_kernel, dim3(B), dim3(DT), 0, p, q, tokens, (const RowStats*)rs, t, V, *wp, seed,
+               dev_round, round, out, cm);
+  if (e != cudaSuccess) return cuda_error(e, "tree decide launch", __FILE__, __LINE__);
+  return ULB_OK;
+}
+
+int launch_tree_accept_commit(Ctx* c, const float* p, const float* q, const int32_t* tokens, int B, int w, int D,
+                              int V, const ulb_warp* wp, uint64_t seed, const uint32_t* dev_round, void* stats_scratch,
+                              int32_t* comp, int32_t* hist, int hist_len, int32_t* L, int32_t* done,
+                              const int32_t* plen, int max_new, uint32_t* round, unsigned long long* stats,
+                              int32_t* active, int32_t* log, int log_rounds) {
+  SpecCommit cm;
+  cm.hist = hist; cm.hist_len = hist_len; cm.L = L; cm.done = done; cm.prompt_len = plen;
+  cm.max_new = max_new; cm.round = round; cm.stats = stats; cm.active = active;
+  cm.log = log; cm.log_rounds = log_rounds; cm.log_stride = ULB_SPEC_REC_WORDS(D);
+  TreeOut out = {nullptr, nullptr, nullptr, comp};
+  return launch_tree_accept_impl(c, p, q, tokens, B, w, D, V, wp, seed, dev_round, 0, true, stats_scratch, out, cm);
+}
+
 }  // namespace ulb
 
 using namespace ulb;
+
+extern "C" int ulb_spec_tree_accept(ulb_ctx* ctx, const float* p, const float* q, const int32_t* tokens, int B,
+                                    int width, int depth, int V, const ulb_warp* w, uint64_t seed, uint32_t round,
+                                    int32_t* out_path, int32_t* out_n, int32_t* out_tok) {
+  ULB_CHECK(ctx && p && q && tokens && w && out_path && out_n && out_tok, ULB_EINVAL,
+            "ulb_spec_tree_accept: NULL argument");
+  ULB_CHECK(B >= 0 && V > 0 && width >= 1 && width <= kTreeMaxWidth && depth >= 1, ULB_EINVAL,
+            "ulb_spec_tree_accept: B %d, width %d, depth %d, V %d", B, width, depth, V);
+  ULB_CHECK(tree_first(width, depth + 1) <= kTreeMaxNodes && depth <= 8, ULB_EUNSUPPORTED,
+            "ulb_spec_tree_accept: a tree of width %d and depth %d has more than %d nodes", width, depth,
+            kTreeMaxNodes);
+  Ctx* c = &ctx->c;
+  ULB_CUDA(cudaSetDevice(c->device));
+  void* scratch = nullptr;
+  const size_t bytes = tree_accept_scratch_bytes(B, width, depth);
+  ULB_TRY(dev_alloc(c, &scratch, bytes));
+  TreeOut out = {out_path, out_n, out_tok, nullptr};
+  int rc = launch_tree_accept_impl(c, p, q, tokens, B, width, depth, V, w, seed, nullptr, round, false, scratch, out,
+                                   SpecCommit{});
+  if (rc == ULB_OK) rc = check_device_errors(c);
+  dev_free(c, scratch, bytes);
+  return rc;
+}
 
 extern "C" int ulb_sample(ulb_ctx* ctx, const float* logits, int rows, int V, int ld, const ulb_warp* w,
                           uint64_t seed, uint32_t round, uint32_t slot, uint32_t tag, int32_t* out) {

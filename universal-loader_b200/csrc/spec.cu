@@ -26,14 +26,17 @@
 #include "ulb_internal.h"
 
 namespace ulb {
-struct Model;
-struct KV;
-int model_prepare(Model* m, KV* kv, int M, int rps);
-int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos, int logits_mode,
-                  float* logits, int ld, int* err);
 int launch_sample_seq(Ctx* c, const float* logits, int rows, int V, int ld, const ulb_warp* w, uint64_t seed,
                       const uint32_t* dev_round, uint32_t round, uint32_t slot, uint32_t tag, uint32_t seq_base,
                       int32_t* out, int out_stride);
+size_t tree_accept_scratch_bytes(int B, int w, int D);
+int launch_tree_children(Ctx* c, const float* logits, int rows, int V, int w, int d, const ulb_warp* wp,
+                         uint64_t seed, const uint32_t* dev_round, int N, int32_t* tokens);
+int launch_tree_accept_commit(Ctx* c, const float* p, const float* q, const int32_t* tokens, int B, int w, int D,
+                              int V, const ulb_warp* wp, uint64_t seed, const uint32_t* dev_round, void* stats_scratch,
+                              int32_t* comp, int32_t* hist, int hist_len, int32_t* L, int32_t* done,
+                              const int32_t* plen, int max_new, uint32_t* round, unsigned long long* stats,
+                              int32_t* active, int32_t* log, int log_rounds);
 int launch_accept_commit(Ctx* c, const float* p, const float* q, const int32_t* draft, int B, int k, int V,
                          const ulb_warp* w, uint64_t seed, const uint32_t* dev_round, void* stats_scratch,
                          int32_t* hist, int hist_len, int32_t* L, int32_t* done, const int32_t* plen, int max_new,
@@ -95,6 +98,64 @@ __global__ void stage_prefill_kernel(int s, int c0, int n, const int* __restrict
   rpos[i] = c0 + i;
 }
 
+/* Tree rounds (width w, depth D = k).  Draft step 0 is the chain's (rows L - 2, L - 1, plain
+   causal rows); step d >= 1 feeds the w^d nodes of depth d: node i in cache slot L + i,
+   rotated as position L - 1 + d, seeing the committed keys (< L) and its ancestors. */
+__global__ void stage_tree_draft_kernel(int S, int d, int w, int N, const int* __restrict__ hist, int hl,
+                                        const int* __restrict__ L, const int* __restrict__ ttok, int* rtok, int* rseq,
+                                        int* rpos, int* rrope, int* rpref, unsigned long long* rmask) {
+  pdl_wait();
+  pdl_trigger();
+  int per = 1;
+  for (int j = 0; j < d; ++j) per *= w;
+  const int rps = d == 0 ? 2 : per;
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= S * rps) return;
+  const int s = m / rps, e = m % rps;
+  if (d == 0) {
+    const int pos = L[s] - 2 + e;
+    rtok[m] = hist[(size_t)s * hl + pos];
+    rpos[m] = pos;
+    rrope[m] = pos;
+    rpref[m] = pos + 1;
+    rmask[m] = 0ull;
+  } else {
+    const int node = tree_first(w, d) + e;
+    rtok[m] = ttok[(size_t)s * N + node];
+    rpos[m] = L[s] + node;
+    rrope[m] = L[s] - 1 + d;
+    rpref[m] = L[s];
+    rmask[m] = tree_ancestors(w, node);
+  }
+  rseq[m] = s;
+}
+
+/* the verify rows of a tree round: the root (the last committed token) and every node */
+__global__ void stage_tree_verify_kernel(int S, int w, int N, const int* __restrict__ hist, int hl,
+                                         const int* __restrict__ L, const int* __restrict__ ttok, int* rtok, int* rseq,
+                                         int* rpos, int* rrope, int* rpref, unsigned long long* rmask) {
+  pdl_wait();
+  pdl_trigger();
+  const int R = N + 1;
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= S * R) return;
+  const int s = m / R, e = m % R;
+  if (e == 0) {
+    rtok[m] = hist[(size_t)s * hl + L[s] - 1];
+    rpos[m] = L[s] - 1;
+    rrope[m] = L[s] - 1;
+    rmask[m] = 0ull;
+  } else {
+    const int node = e - 1;
+    rtok[m] = ttok[(size_t)s * N + node];
+    rpos[m] = L[s] + node;
+    rrope[m] = L[s] - 1 + tree_depth(w, node);
+    rmask[m] = tree_ancestors(w, node);
+  }
+  rpref[m] = L[s];
+  rseq[m] = s;
+}
+
 /* prompt rows per prefill forward: large enough for the tensor-core GEMM (>= 128 rows) */
 constexpr int kPrefillChunk = 256;
 
@@ -132,6 +193,12 @@ struct Spec {
   bool prefilled = false;
   /* pages of both caches on demand (desc.kv_pages > 0), else every slot owns its capacity */
   std::unique_ptr<PagePool> pool;
+  /* tree speculation (tw >= 2): width, nodes, internal nodes, the drafted node tokens
+     [S][tN], the last round's accepted paths for the cache compaction [S][2 + k] and the
+     tree fields of the rows (RoPE position, prefix end, ancestor mask) */
+  int tw = 0, tN = 0, tNI = 0;
+  int32_t *ttok = nullptr, *comp = nullptr, *rrope = nullptr, *rpref = nullptr;
+  unsigned long long* rmask = nullptr;
   /* launch accounting */
   uint64_t per_round = 0;   /* kernels in one round (counted while recording it) */
   uint64_t launches = 0;    /* since the last prefill */
@@ -147,7 +214,45 @@ static int record_round(Spec* sp, void* ev_draft_done = nullptr, void* ev_verify
   return rc;
 }
 
+static int record_tree_round(Spec* sp, void* ev_draft_done, void* ev_verify_done) {
+  Ctx* c = sp->c;
+  const int S = sp->S, w = sp->tw, D = sp->k, V = sp->V, N = sp->tN;
+  TreeRows tr;
+  tr.rope = sp->rrope;
+  tr.pref = sp->rpref;
+  tr.mask = sp->rmask;
+  size_t qbase = 0; /* q rows of the levels so far (level-major) */
+  int per = 1;      /* w^d */
+  for (int d = 0; d < D; ++d) {
+    const int rps = d == 0 ? 2 : per, M = S * rps;
+    cudaError_t e = launch_k(c, stage_tree_draft_kernel, dim3((M + 127) / 128), dim3(128), 0, S, d, w, N,
+                             (const int*)sp->hist, sp->hl, (const int*)sp->L, (const int*)sp->ttok, sp->rtok, sp->rseq,
+                             sp->rpos, sp->rrope, sp->rpref, sp->rmask);
+    if (e != cudaSuccess) return cuda_error(e, "stage_tree_draft", __FILE__, __LINE__);
+    ULB_TRY(model_forward(sp->dft, sp->kvd_i, M, rps, sp->rtok, sp->rseq, sp->rpos, d == 0 ? 1 : 0,
+                          sp->qlog + qbase * V, V, sp->err, &tr));
+    ULB_TRY(launch_tree_children(c, sp->qlog + qbase * V, S * per, V, w, d, &sp->d.warp, sp->d.seed, sp->round, N,
+                                 sp->ttok));
+    qbase += (size_t)S * per;
+    per *= w;
+  }
+  if (ev_draft_done) ULB_CUDA(cudaEventRecord((cudaEvent_t)ev_draft_done, c->stream));
+  const int M = S * (N + 1);
+  cudaError_t e = launch_k(c, stage_tree_verify_kernel, dim3((M + 127) / 128), dim3(128), 0, S, w, N,
+                           (const int*)sp->hist, sp->hl, (const int*)sp->L, (const int*)sp->ttok, sp->rtok, sp->rseq,
+                           sp->rpos, sp->rrope, sp->rpref, sp->rmask);
+  if (e != cudaSuccess) return cuda_error(e, "stage_tree_verify", __FILE__, __LINE__);
+  ULB_TRY(model_forward(sp->tgt, sp->kvt_i, M, N + 1, sp->rtok, sp->rseq, sp->rpos, 0, sp->plog, V, sp->err, &tr));
+  if (ev_verify_done) ULB_CUDA(cudaEventRecord((cudaEvent_t)ev_verify_done, c->stream));
+  ULB_TRY(launch_tree_accept_commit(c, sp->plog, sp->qlog, sp->ttok, S, w, D, V, &sp->d.warp, sp->d.seed, sp->round,
+                                    sp->rs, sp->comp, sp->hist, sp->hl, sp->L, sp->done, sp->plen, sp->d.max_new,
+                                    sp->round, sp->stats, sp->active, sp->log, sp->log_rounds));
+  ULB_TRY(kv_tree_compact(sp->kvt_i, sp->comp, S, D));
+  return kv_tree_compact(sp->kvd_i, sp->comp, S, D);
+}
+
 static int record_round_impl(Spec* sp, void* ev_draft_done, void* ev_verify_done) {
+  if (sp->tw >= 2) return record_tree_round(sp, ev_draft_done, ev_verify_done);
   Ctx* c = sp->c;
   const int S = sp->S, k = sp->k, V = sp->V;
   for (int j = 0; j < k; ++j) {
@@ -188,12 +293,21 @@ static void spec_release(Spec* sp) {
   dev_free(c, sp->round, sp->S * 4); dev_free(c, sp->stats, 4 * 8);
   dev_free(c, sp->plog, sp->plog_bytes); dev_free(c, sp->qlog, sp->qlog_bytes); dev_free(c, sp->rs, sp->rs_bytes);
   dev_free(c, sp->log, log_bytes(sp));
+  dev_free(c, sp->ttok, (size_t)sp->S * sp->tN * 4);
+  dev_free(c, sp->comp, (size_t)sp->S * (2 + sp->k) * 4);
+  dev_free(c, sp->rrope, sp->rows_cap * 4);
+  dev_free(c, sp->rpref, sp->rows_cap * 4);
+  dev_free(c, sp->rmask, sp->rows_cap * 8);
   if (sp->h_L) cudaFreeHost(sp->h_L);
   if (sp->h_done) cudaFreeHost(sp->h_done);
   ulb_kv_free(sp->kvt);
   ulb_kv_free(sp->kvd);
   cudaStreamSynchronize(c->stream);
 }
+
+/* cache positions past the committed length L that one round may write: up to L + k for a
+   chain, up to L + N - 1 for a tree of N nodes (plus the pending row) */
+static int round_span(const Spec* sp) { return (sp->tw >= 2 ? sp->tN : sp->k) + 1; }
 
 /* map pages so slot s covers positions [0, positions) in both caches (paged loop only) */
 static int map_slot(Spec* sp, int s, int positions) {
@@ -275,7 +389,15 @@ int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft, const ulb
   if (sp->dft)
     ULB_CHECK(model_vocab(sp->dft) == sp->V, ULB_EINVAL, "draft vocab %d != target vocab %d", model_vocab(sp->dft), sp->V);
   const int S = sp->S, k = sp->k, V = sp->V;
-  sp->cap = d->max_prompt + d->max_new + 2 * k + 2;
+  if (sp->dft && d->tree_width >= 2) {
+    ULB_CHECK(d->tree_width <= kTreeMaxWidth && k <= 8 && tree_first(d->tree_width, k + 1) <= kTreeMaxNodes,
+              ULB_EUNSUPPORTED, "ulb_spec_create: a tree of width %d and depth %d (at most %d nodes, width <= %d)",
+              d->tree_width, k, kTreeMaxNodes, kTreeMaxWidth);
+    sp->tw = d->tree_width;
+    sp->tN = tree_first(sp->tw, k + 1);
+    sp->tNI = tree_first(sp->tw, k);
+  }
+  sp->cap = d->max_prompt + d->max_new + 2 * k + 2 + sp->tN;
   sp->hl = sp->cap;
   int rc = ULB_OK;
   auto fail = [&](int code) {
@@ -295,18 +417,25 @@ int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft, const ulb
   }
   sp->kvt_i = kv_of(sp->kvt);
   if (sp->dft) sp->kvd_i = kv_of(sp->kvd);
-  sp->rows_cap = (size_t)std::max({S * (k + 1), 2 * S, kPrefillChunk});
+  sp->rows_cap = (size_t)std::max({S * (k + 1), 2 * S, kPrefillChunk, S * (sp->tN + 1)});
 #define ALLOC(ptr, bytes) if ((rc = dev_alloc(c, (void**)&(ptr), (bytes)))) return fail(rc)
   ALLOC(sp->hist, (size_t)S * sp->hl * 4);
   ALLOC(sp->L, S * 4); ALLOC(sp->done, S * 4); ALLOC(sp->plen, S * 4);
   ALLOC(sp->draft, (size_t)S * std::max(k, 1) * 4);
   ALLOC(sp->rtok, sp->rows_cap * 4); ALLOC(sp->rseq, sp->rows_cap * 4); ALLOC(sp->rpos, sp->rows_cap * 4);
   ALLOC(sp->err, 4); ALLOC(sp->active, S * 4); ALLOC(sp->round, S * 4); ALLOC(sp->stats, 4 * 8);
-  sp->plog_bytes = (size_t)S * (k + 1) * V * 4;
-  sp->qlog_bytes = (size_t)S * std::max(k, 1) * V * 4;
+  sp->plog_bytes = (size_t)S * (std::max(k, sp->tN) + 1) * V * 4;
+  sp->qlog_bytes = (size_t)S * std::max({k, 1, sp->tNI + 1}) * V * 4;
   ALLOC(sp->plog, sp->plog_bytes);
   ALLOC(sp->qlog, sp->qlog_bytes);
-  sp->rs_bytes = accept_scratch_bytes(S, k, V);
+  sp->rs_bytes = sp->tw >= 2 ? tree_accept_scratch_bytes(S, sp->tw, k) : accept_scratch_bytes(S, k, V);
+  if (sp->tw >= 2) {
+    ALLOC(sp->ttok, (size_t)S * sp->tN * 4);
+    ALLOC(sp->comp, (size_t)S * (2 + k) * 4);
+    ALLOC(sp->rrope, sp->rows_cap * 4);
+    ALLOC(sp->rpref, sp->rows_cap * 4);
+    ALLOC(sp->rmask, sp->rows_cap * 8);
+  }
   ALLOC(sp->rs, sp->rs_bytes);
   /* every round commits at least one token, so max_new rounds (+1 for a profiled round) hold
      a whole generation */
@@ -323,6 +452,12 @@ int ulb_spec_create(ulb_ctx* ctx, ulb_model* target, ulb_model* draft, const ulb
     if ((rc = model_prepare(sp->dft, sp->kvd_i, kPrefillChunk, kPrefillChunk))) return fail(rc);
     if ((rc = model_prepare(sp->dft, sp->kvd_i, 2 * S, 2))) return fail(rc);
     if ((rc = model_prepare(sp->dft, sp->kvd_i, S, 1))) return fail(rc);
+  }
+  if (sp->tw >= 2) { /* the tree round's forwards */
+    if ((rc = model_prepare(sp->tgt, sp->kvt_i, S * (sp->tN + 1), sp->tN + 1, true))) return fail(rc);
+    if ((rc = model_prepare(sp->dft, sp->kvd_i, 2 * S, 2, true))) return fail(rc);
+    for (int dd = 1, per = sp->tw; dd < k; ++dd, per *= sp->tw)
+      if ((rc = model_prepare(sp->dft, sp->kvd_i, S * per, per, true))) return fail(rc);
   }
   if (cudaStreamSynchronize(c->stream) != cudaSuccess) return fail(cuda_error(cudaGetLastError(), "create", __FILE__, __LINE__));
   *out = h.release();
@@ -355,7 +490,7 @@ int ulb_spec_prefill(ulb_spec* h, const int32_t* prompts, const int32_t* lens) {
   for (int s = 0; s < S; ++s) {
     /* pages for the prompt and the first round (it writes positions up to lens + k) */
     ULB_TRY(unmap_slot(sp, s));
-    ULB_TRY(map_slot(sp, s, lens[s] + sp->k + 1));
+    ULB_TRY(map_slot(sp, s, lens[s] + round_span(sp)));
     ULB_TRY(prefill_slot(sp, s, lens[s]));
   }
   std::vector<int32_t> L(S), done(S);
@@ -410,7 +545,7 @@ int ulb_spec_run(ulb_spec* h, int max_rounds, int* out_rounds) {
       for (int attempt = 0;; ++attempt) {
         int rc = ULB_OK;
         for (int s = 0; s < S && rc == ULB_OK; ++s)
-          if (!sp->h_done[s]) rc = map_slot(sp, s, sp->h_L[s] + r * R + sp->k + 1);
+          if (!sp->h_done[s]) rc = map_slot(sp, s, sp->h_L[s] + r * R + round_span(sp));
         if (rc == ULB_OK) break;
         if (r == 1 || attempt > 0) return rc;
         r = 1;
@@ -480,7 +615,7 @@ int ulb_spec_admit(ulb_spec* h, int slot, const int32_t* prompt, int len) {
   ULB_CHECK(done, ULB_EINVAL, "ulb_spec_admit: slot %d is still decoding", slot);
   /* the slot starts over: its pages, prompt, lengths and counters */
   ULB_TRY(unmap_slot(sp, slot));
-  ULB_TRY(map_slot(sp, slot, len + sp->k + 1));
+  ULB_TRY(map_slot(sp, slot, len + round_span(sp)));
   const int32_t zero = 0;
   ULB_CUDA(cudaMemcpyAsync(sp->hist + (size_t)slot * sp->hl, prompt, (size_t)len * 4, cudaMemcpyHostToDevice, c->stream));
   ULB_CUDA(cudaMemcpyAsync(sp->plen + slot, &len, 4, cudaMemcpyHostToDevice, c->stream));

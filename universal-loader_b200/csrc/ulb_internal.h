@@ -146,9 +146,33 @@ struct EpiArgs {
      page bt[s * max_pages + p / kKvPage], or in page s * max_pages + p / kKvPage when bt is
      NULL, the identity table); max_pages == 0: contiguous [S][Hkv][cap][hd] */
   const int* bt = nullptr; int max_pages = 0;
+  /* RoPE position of each row when it differs from the cache position row_pos (tree rows:
+     a node at depth d sits in cache slot L + node index but rotates as position L - 1 + d);
+     NULL = row_pos */
+  const int* row_rope = nullptr;
 };
 
 int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a);
+
+/* rows of a forward that are nodes of a speculation tree: row m rotates as position rope[m]
+   (its cache slot is its row position), and sees the keys before pref[m] plus pref[m] + j for
+   the set bits j of mask[m] */
+struct TreeRows {
+  const int* rope = nullptr;
+  const int* pref = nullptr;
+  const unsigned long long* mask = nullptr;
+};
+
+/* the model forward of model.cu: workspaces for a shape (before any capture), then one pass
+   over M rows (rps per sequence); tree != NULL for the rows of a speculation tree */
+struct Model;
+struct KV;
+int model_prepare(Model* m, KV* kv, int M, int rps, bool tree = false);
+int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* seq, const int* pos, int logits_mode,
+                  float* logits, int ld, int* err, const TreeRows* tree = nullptr);
+/* move the accepted nodes of the last tree round to their sequence positions (comp [S][2 + D]:
+   length before the round, nodes accepted, their node indices) */
+int kv_tree_compact(KV* kv, const int32_t* comp, int S, int D);
 /* y = W . rmsnorm(x32) with the fused epilogue `epi`.  Small batches (M <= 8 rows whose fp16
    copy fits kNormSmemBytes) normalise inside the GEMV, each CTA into its own shared memory;
    otherwise rmsnorm_kernel writes x16 [M][K] first.  Both give the same bits. */
@@ -179,14 +203,15 @@ int launch_dequant(Ctx* c, const Tensor* w, float* out);
 int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, const __half* k,
                      const __half* v, const int* row_seq, const int* row_pos, int M, int rps,
                      __half* out, float* scratch, int* counters, size_t scratch_floats,
-                     int n_counters, const int* bt = nullptr, int max_pages = 0);
+                     int n_counters, const int* bt = nullptr, int max_pages = 0,
+                     const int* tree_pref = nullptr, const unsigned long long* tree_mask = nullptr);
 /* argument checks shared by every attention entry point (no division by a zero head count) */
 int validate_attn_desc(const ulb_attn_desc* d, int M, int rps);
 /* split-merge scratch a launch of this shape needs: zero floats / counters when it has one key
    split, or when its splits merge in a thread-block cluster (only a global-memory merge, over
    caches longer than 2048 positions, reads the scratch and counters) */
 int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int max_pos, size_t* floats,
-                           int* n_counters);
+                           int* n_counters, bool tree = false);
 
 int launch_rmsnorm(Ctx* c, const float* x, int ldx, const float* g, int M, int d, float eps,
                    const int* row_select, __half* out, int ldo);
@@ -256,6 +281,43 @@ namespace ulb {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 /* Allow the next kernel in the stream to begin launching its CTAs. */
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+/* Speculation trees: full trees of width w and depth D whose nodes are numbered breadth
+   first from depth 1 (the root, the last committed token, is not a node).  tree_first(w, d)
+   = w + w^2 + ... + w^(d-1) is the first node of depth d, so a tree has tree_first(w, D + 1)
+   nodes and tree_first(w, D) internal ones (depth < D).  The children of the root are nodes
+   0..w-1; those of node i of depth d, tree_first(w, d + 1) + (i - tree_first(w, d)) * w + c. */
+__host__ __device__ inline int tree_first(int w, int d) {
+  int f = 0, p = 1;
+  for (int j = 1; j < d; ++j) {
+    p *= w;
+    f += p;
+  }
+  return f;
+}
+__host__ __device__ inline int tree_depth(int w, int i) {
+  int d = 1, f = 0, p = w;
+  while (i >= f + p) {
+    f += p;
+    p *= w;
+    ++d;
+  }
+  return d;
+}
+/* bit j set: node j is node i or one of its ancestors */
+__host__ __device__ inline unsigned long long tree_ancestors(int w, int i) {
+  unsigned long long m = 0ull;
+  int d = tree_depth(w, i);
+  while (true) {
+    m |= 1ull << i;
+    if (d == 1) break;
+    i = tree_first(w, d - 1) + (i - tree_first(w, d)) / w;
+    --d;
+  }
+  return m;
+}
+constexpr int kTreeMaxNodes = 63;
+constexpr int kTreeMaxWidth = 8;
 
 /* barrier of a 256-thread group: the whole block (bar == 0, a 256-thread block) or named
    barrier `bar` of 256 threads inside a larger block */

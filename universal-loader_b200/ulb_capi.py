@@ -40,7 +40,7 @@ class ModelDesc(C.Structure):
 class SpecDesc(C.Structure):
     _fields_ = [("n_seq", C.c_int), ("k", C.c_int), ("max_prompt", C.c_int),
                 ("max_new", C.c_int), ("warp", Warp), ("seed", C.c_uint64),
-                ("use_graphs", C.c_int), ("kv_pages", C.c_int)]
+                ("use_graphs", C.c_int), ("kv_pages", C.c_int), ("tree_width", C.c_int)]
 
 
 _SIGS = {
@@ -81,6 +81,8 @@ _SIGS = {
                              C.c_uint32, C.c_uint32, C.c_uint32, P]),
     "ulb_spec_accept": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.POINTER(Warp),
                                   C.c_uint64, C.c_uint32, P, P]),
+    "ulb_spec_tree_accept": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(Warp),
+                                       C.c_uint64, C.c_uint32, P, P, P]),
     "ulb_model_create": (C.c_int, [P, C.POINTER(ModelDesc), C.POINTER(P)]),
     "ulb_model_set_weight": (C.c_int, [P, C.c_char_p, C.c_int, C.POINTER(C.c_uint64), P, C.c_size_t]),
     "ulb_model_finalize": (C.c_int, [P]),
