@@ -16,6 +16,9 @@ for p in (ROOT, PKG):
 TINY_TARGET = dict(n_layer=8, d_model=512, n_head=8, n_head_kv=8, d_ff=1408, n_vocab=32000,
                    rms_eps=1e-5, rope_base=1e4, wtype="q4_0", seed=0, name="tiny-target")
 TINY_DRAFT = dict(TINY_TARGET, n_layer=2, name="tiny-draft")
+# a draft sharing the target's first 7 of 8 blocks: one that agrees with the target often
+# enough for whole tree paths to be accepted
+TINY_NEAR_DRAFT = dict(TINY_TARGET, n_layer=7, name="tiny-near-draft")
 
 
 def pytest_configure(config):
@@ -69,6 +72,11 @@ def tiny_target(model_dir):
 @pytest.fixture(scope="session")
 def tiny_draft(model_dir):
     return _synth(model_dir, TINY_DRAFT, "tiny_draft.gguf")
+
+
+@pytest.fixture(scope="session")
+def near_draft(model_dir):
+    return _synth(model_dir, TINY_NEAR_DRAFT, "tiny_near_draft.gguf")
 
 
 @pytest.fixture(scope="session")
