@@ -967,12 +967,20 @@ def run_ops(args):
         B, k = 64, 8
         pl = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
         ql = (rng.standard_normal((B, k, V)) * 3).astype(np.float32)
-        draft = rng.integers(0, V, (B, k)).astype(np.int32)
-        bp, bq, bd = ctx.buffer(pl), ctx.buffer(ql), ctx.buffer(draft)
+        bp, bq = ctx.buffer(pl), ctx.buffer(ql)
         ot, on = ctx.buffer(nbytes=B * (k + 1) * 4), ctx.buffer(nbytes=B * 4)
         st = ctx.buffer(nbytes=B * 4)
         for warp in warps:
             w = U.Warp(*warp)
+            # the drafts as the loop makes them: token i of each sequence drawn from q_i under the warp
+            draft = np.zeros((B, k), np.int32)
+            tb = ctx.buffer(nbytes=B * 4)
+            for i in range(k):
+                U.check(U.lib().ulb_sample(ctx.h, C.c_void_p(bq.ptr.value + i * V * 4), B, V, k * V, C.byref(w), 7, 0,
+                                           i, U.RNG_DRAFT, tb.ptr))
+                draft[:, i] = tb.download(np.int32, (B,))
+            tb.free()
+            bd = ctx.buffer(draft)
             for _ in range(max(1, args.warmup)):
                 U.check(U.lib().ulb_spec_accept(ctx.h, bp.ptr, bq.ptr, bd.ptr, B, k, V, C.byref(w), 1, 0, ot.ptr, on.ptr))
             ctx.sync()
@@ -980,9 +988,15 @@ def run_ops(args):
                                                                       1, r, ot.ptr, on.ptr)) for r in range(4)])
             ms = ctx.time_graph(g, max(args.steps, 3)) / 4
             U.lib().ulb_graph_free(g)
-            alg = pl.nbytes + ql.nbytes
+            # the walk reads p_i (and q_i when sampling) for each position it tests, and p_k after a
+            # full accept: the algorithmic bytes of the rows it needs
+            n_acc = on.download(np.int32, (B,))
+            rows = sum(min(int(n) + 1, k) * (1 if warp[0] <= 0 else 2) + (1 if n == k else 0) for n in n_acc)
+            alg = rows * V * 4
             name = "%s:T%g%s" % (label, warp[0], ":top_p%g" % warp[2] if warp[2] < 1 else "")
-            results[name] = {"us": ms * 1e3, "gbs": alg / ms / 1e6, "hbm_frac": alg / ms / 1e6 / peak}
+            results[name] = {"us": ms * 1e3, "gbs": alg / ms / 1e6, "hbm_frac": alg / ms / 1e6 / peak,
+                             "rows_read": rows, "rows_total": B * (2 * k + 1),
+                             "accepted_mean": float(n_acc.mean()), "drafts": "sampled from q"}
             if warp[0] > 0:  # draft-token sampling of one step: B rows
                 call = lambda: U.check(U.lib().ulb_sample(ctx.h, bq.ptr, B, V, k * V, C.byref(w), 1, 0, 0, 1, st.ptr))
                 call()
@@ -992,7 +1006,8 @@ def run_ops(args):
                 U.lib().ulb_graph_free(g)
                 results[name.replace("accept", "sample")] = {"us": ms * 1e3, "rows": B,
                                                              "gbs": B * V * 4 / ms / 1e6}
-        for b in (bp, bq, bd, ot, on, st):
+            bd.free()
+        for b in (bp, bq, ot, on, st):
             b.free()
     ctx.close()
     print(json.dumps({"mode": "ops", "peak_gbs": peak, "peak_source": peak_src, "results": results}), flush=True)

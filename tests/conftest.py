@@ -75,6 +75,16 @@ def tiny_draft(model_dir):
 
 
 @pytest.fixture(scope="session")
+def q4km_mix(model_dir):
+    """The tensor mix of llama.cpp's Q4_K_M files: Q4_K linears with Q6_K attn_v and ffn_down (and
+    here a Q8_0 attn_output), a Q6_K output.weight; GQA."""
+    spec = dict(n_layer=2, d_model=512, n_head=8, n_head_kv=2, d_ff=1536, n_vocab=4096, rms_eps=1e-5,
+                rope_base=5e5, wtype="q4_k", embd_type="q4_k", out_type="q6_k", v_type="q6_k", o_type="q8_0",
+                down_type="q6_k", seed=13, name="q4km-mix")
+    return _synth(model_dir, spec, "q4km_mix.gguf")
+
+
+@pytest.fixture(scope="session")
 def near_draft(model_dir):
     return _synth(model_dir, TINY_NEAR_DRAFT, "tiny_near_draft.gguf")
 

@@ -199,11 +199,13 @@ def test_mid_model_matches_oracle(ctx, mid_q40):
         gm.close()
 
 
-@pytest.mark.parametrize("fixture", ["llamacpp_q40", "q6k_embd_q80_head"])
+@pytest.mark.parametrize("fixture", ["llamacpp_q40", "q6k_embd_q80_head", "q4km_mix"])
 def test_quantised_embd_and_head_match_oracle(ctx, fixture, request):
-    """Q4_0 / Q6_K token_embd (rows dequantised inside the embedding kernel) and Q6_K / Q8_0
-    output.weight (the GGUF-row GEMV after a separate RMSNorm): one logits row of a 20-row
-    prefill, then a 12-row block (the head in chunks of 8 + 4 rows), against the oracle."""
+    """Q4_0 / Q6_K / Q4_K token_embd (rows dequantised inside the embedding kernel), Q6_K / Q8_0
+    output.weight (the GGUF-row GEMV after a separate RMSNorm), and (q4km_mix) Q6_K attn_v /
+    ffn_down and Q8_0 attn_output rows through the row GEMV's V-cache and residual epilogues: one
+    logits row of a 20-row prefill, then a 12-row block (rows in chunks of 8 + 4), against the
+    oracle."""
     path = request.getfixturevalue(fixture)
     gm = GpuModel(ctx, path)
     try:
@@ -224,15 +226,17 @@ def test_quantised_embd_and_head_match_oracle(ctx, fixture, request):
         gm.close()
 
 
-def test_llamacpp_layout_spec_stream_matches_oracle(llamacpp_q40):
+@pytest.mark.parametrize("fixture", ["llamacpp_q40", "q4km_mix"])
+def test_llamacpp_layout_spec_stream_matches_oracle(fixture, request):
     """The speculative loop through the public API on a llama.cpp-layout model (drafting with
     itself, so every draft is accepted): T=0 stream equal to the oracle's."""
+    path = request.getfixturevalue(fixture)
     prompt = _prompt(40, seed=5, vocab=4096)
-    api = _api(llamacpp_q40, llamacpp_q40, k=4)
+    api = _api(path, path, k=4)
     got = api.generate_tokens(prompt.tolist(), _cfg(48))
-    t = orc.Model(llamacpp_q40)
+    t = orc.Model(path)
     want, _, _, margin, tm = orc.spec_generate(t, t, [prompt], 48, 4, (0.0, 0, 1.0), seed=0, with_margins=True)
-    _match_greedy(got, want[0], tm[0], "llama.cpp-layout self-speculation")
+    _match_greedy(got, want[0], tm[0], "%s self-speculation" % fixture)
 
 
 def _api(target, draft=None, k=4):

@@ -181,6 +181,27 @@ def test_synthetic_embd_and_head_types(tmp_path, embd, out):
     mf.close()
 
 
+def test_synthetic_linear_type_mix(tmp_path):
+    """v_type / o_type / down_type write attn_v / attn_output / ffn_down of every layer in their
+    own types (llama.cpp's Q4_K_M mix), decoding through the oracle as through the gguf package."""
+    import vulkangguf as vg
+    p = str(tmp_path / "mix.gguf")
+    vg.write_synthetic_gguf(p, dict(n_layer=2, d_model=512, n_head=8, n_head_kv=2, d_ff=1536, n_vocab=512,
+                                    wtype="q4_k", v_type="q6_k", o_type="q8_0", down_type="q6_k", seed=9))
+    m = orc.Model(p)
+    gt = {orc.T_Q4_K: gguf.GGMLQuantizationType.Q4_K, 8: gguf.GGMLQuantizationType.Q8_0,
+          14: gguf.GGMLQuantizationType.Q6_K}
+    want = {"attn_q": orc.T_Q4_K, "attn_v": 14, "attn_output": 8, "ffn_gate": orc.T_Q4_K, "ffn_down": 14}
+    for l in range(2):
+        for nm, ty in want.items():
+            t, ne, raw = m.tensor("blk.%d.%s.weight" % (l, nm))
+            assert t == ty, (nm, t)
+            mine = orc.dequant(t, raw, ne[0] * ne[1])
+            ref = gguf.quants.dequantize(raw.reshape(ne[1], -1), gt[t]).ravel()
+            assert np.array_equal(mine.view(np.uint32), ref.view(np.uint32)), nm
+    m.close()
+
+
 # ---------------------------------------------------------------- GEMV structure
 @pytest.mark.parametrize("qt", ["q4_0", "q4_k", "q8_0", "q6_k"])
 @pytest.mark.parametrize("M", [1, 5, 8])

@@ -430,6 +430,13 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
   const int hd = sp.d_model / sp.n_head;
   const uint64_t nq = (uint64_t)sp.n_head * hd, nkv = (uint64_t)sp.n_head_kv * hd;
   if (sp.d_model % blk || sp.d_ff % blk || nq % blk) return fail("synthetic spec: dims must be multiples of the block size");
+  const int v_type = sp.v_type >= 0 ? sp.v_type : sp.wtype, o_type = sp.o_type >= 0 ? sp.o_type : sp.wtype,
+            down_type = sp.down_type >= 0 ? sp.down_type : sp.wtype;
+  auto blk_of = [](int t) { return t == 2 || t == 8 ? 32 : 256; };
+  if (!qtype_ok(v_type) || !qtype_ok(o_type) || !qtype_ok(down_type))
+    return fail("synthetic spec: v_type / o_type / down_type must be Q4_0, Q8_0, Q4_K or Q6_K");
+  if (sp.d_model % blk_of(v_type) || nq % blk_of(o_type) || sp.d_ff % blk_of(down_type))
+    return fail("synthetic spec: the inner dimension of attn_v / attn_output / ffn_down is not whole blocks");
   std::vector<PlannedTensor> plan;
   plan.push_back({"token_embd.weight", sp.embd_type, 2, {(uint64_t)sp.d_model, (uint64_t)sp.n_vocab}, PlannedTensor::NORMAL});
   for (int l = 0; l < sp.n_layer; ++l) {
@@ -438,12 +445,12 @@ bool write_synthetic_gguf(const std::string& path, const SynthSpec& sp, int thre
     plan.push_back({p + "attn_norm.weight", 0, 1, {d, 1}, PlannedTensor::ONES});
     plan.push_back({p + "attn_q.weight", sp.wtype, 2, {d, nq}, PlannedTensor::NORMAL});
     plan.push_back({p + "attn_k.weight", sp.wtype, 2, {d, nkv}, PlannedTensor::NORMAL});
-    plan.push_back({p + "attn_v.weight", sp.wtype, 2, {d, nkv}, PlannedTensor::NORMAL});
-    plan.push_back({p + "attn_output.weight", sp.wtype, 2, {nq, d}, PlannedTensor::NORMAL});
+    plan.push_back({p + "attn_v.weight", v_type, 2, {d, nkv}, PlannedTensor::NORMAL});
+    plan.push_back({p + "attn_output.weight", o_type, 2, {nq, d}, PlannedTensor::NORMAL});
     plan.push_back({p + "ffn_norm.weight", 0, 1, {d, 1}, PlannedTensor::ONES});
     plan.push_back({p + "ffn_gate.weight", sp.wtype, 2, {d, f}, PlannedTensor::NORMAL});
     plan.push_back({p + "ffn_up.weight", sp.wtype, 2, {d, f}, PlannedTensor::NORMAL});
-    plan.push_back({p + "ffn_down.weight", sp.wtype, 2, {f, d}, PlannedTensor::NORMAL});
+    plan.push_back({p + "ffn_down.weight", down_type, 2, {f, d}, PlannedTensor::NORMAL});
   }
   plan.push_back({"output_norm.weight", 0, 1, {(uint64_t)sp.d_model, 1}, PlannedTensor::ONES});
   if (!sp.tied)

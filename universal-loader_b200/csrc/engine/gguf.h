@@ -69,6 +69,9 @@ struct SynthSpec {
   int wtype = 2; /* Q4_0 = 2, Q4_K = 12 */
   int embd_type = 1;  /* token_embd: F32 = 0, F16 = 1, or Q4_0 / Q8_0 = 8 / Q4_K / Q6_K = 14 */
   int out_type = -1;  /* output.weight: Q4_0 / Q8_0 / Q4_K / Q6_K; -1 = wtype */
+  /* attn_v / attn_output / ffn_down of every layer: Q4_0 / Q8_0 / Q4_K / Q6_K, -1 = wtype (a
+     K-quant mix such as llama.cpp's Q4_K_M puts Q6_K in attn_v and ffn_down) */
+  int v_type = -1, o_type = -1, down_type = -1;
   bool tied = false;  /* no output.weight: the LM head is token_embd (tied embeddings) */
   uint64_t seed = 0;
   float stddev = 0.02f;

@@ -543,6 +543,9 @@ bool write_synthetic(const std::string& path, py::dict spec, int threads) {
   type_of("embd_type", s.embd_type);
   if (spec.contains("tied")) s.tied = spec["tied"].cast<bool>();
   type_of("out_type", s.out_type);
+  type_of("v_type", s.v_type);
+  type_of("o_type", s.o_type);
+  type_of("down_type", s.down_type);
   if (spec.contains("vocab")) {
     s.vocab = spec["vocab"].cast<std::vector<std::string>>();
     s.scores = spec.contains("scores") ? spec["scores"].cast<std::vector<float>>() : std::vector<float>(s.vocab.size(), 0.f);
@@ -728,7 +731,8 @@ PYBIND11_MODULE(vulkangguf, m) {
         "Write a synthetic LLaMA GGUF: Q4_0/Q4_K weights N(0, stddev), fp16 embeddings, unit norms; "
         "spec key tied=True writes no output.weight (the head is token_embd); "
         "spec keys embd_type / out_type pick other token_embd (f32, f16, q4_0, q8_0, q4_k, q6_k) and "
-        "output.weight (q4_0, q8_0, q4_k, q6_k) types; vocab / scores / token_types (+ merges, "
+        "output.weight (q4_0, q8_0, q4_k, q6_k) types, v_type / o_type / down_type other attn_v / "
+        "attn_output / ffn_down types (q4_0, q8_0, q4_k, q6_k); vocab / scores / token_types (+ merges, "
         "tokenizer_pre for byte-level BPE; add_bos, add_space_prefix) write a tokenizer.ggml.* vocabulary");
   m.def("synth_normal", &ulbe::synth_normal, "Sample i of the synthetic N(0,1) stream keyed by (seed, name)");
   m.attr("__version__") = "0.1";

@@ -16,6 +16,24 @@
 
 namespace ulb {
 
+/* element (kv head kvh, dimension dd) of token tok's row in this layer's V cache (fp16), through
+   the block table for a paged cache; nothing is written outside the cache or to an unmapped page */
+__device__ __forceinline__ void store_v_cache(const EpiArgs& e, int tok, int kvh, int dd, float v) {
+  const int pos = e.row_pos[tok];
+  const int seq = e.row_seq[tok];
+  if ((unsigned)pos >= (unsigned)e.cap || (unsigned)seq >= (unsigned)e.n_seq) return;
+  size_t row;
+  if (e.max_pages > 0) {
+    const int slot = seq * e.max_pages + pos / kKvPage;
+    const int page = e.bt ? e.bt[slot] : slot;
+    if (page < 0) return;
+    row = (((size_t)page * e.n_head_kv + kvh) * kKvPage + pos % kKvPage) * e.hd;
+  } else {
+    row = (((size_t)seq * e.n_head_kv + kvh) * e.cap + pos) * e.hd;
+  }
+  e.vc[row + dd] = __float2half_rn(v);
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue_token(const EpiArgs& e, int strip, int g, int tok, int M, int N, float vg,
                                                float vg8) {

@@ -33,6 +33,9 @@ struct Layer {
   float* attn_norm = nullptr;
   float* ffn_norm = nullptr;
   Tensor qkv, o, gateup, down;
+  /* attn_v kept as GGUF rows (Q8_0 / Q6_K / F16 / F32, as llama.cpp's K-quant mixes store it):
+     qkv then holds Q and K only and v writes the V cache through the row GEMV */
+  Tensor v;
 };
 
 struct Model {
@@ -362,7 +365,13 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     /* the QKV GEMV's tail prefetches attn_output and ffn_gate_up, which land in L2 while the
        attention kernel (which reads only the KV cache) leaves HBM mostly idle */
     hint(&L.o, &L.gateup);
-    ULB_TRY(launch_qgemv_rms(c, &L.qkv, m->x, d.d_model, L.attn_norm, d.rms_eps, m->x16, M, EPI_QKV, a));
+    if (L.v.dev) { /* V as GGUF rows: the normalised rows in x16 feed the Q / K GEMV and V's row GEMV */
+      ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, L.attn_norm, M, d.d_model, d.rms_eps, 0, m->x16, d.d_model));
+      ULB_TRY(launch_qgemv(c, &L.qkv, m->x16, M, d.d_model, EPI_QKV, a));
+      ULB_TRY(launch_qgemv(c, &L.v, m->x16, M, d.d_model, EPI_VCACHE, a));
+    } else {
+      ULB_TRY(launch_qgemv_rms(c, &L.qkv, m->x, d.d_model, L.attn_norm, d.rms_eps, m->x16, M, EPI_QKV, a));
+    }
     ULB_TRY(launch_attention(c, &ad, m->qb, m->nq, kc, vc, seq, pos, M, rps, m->att, kv->attn_scratch,
                              kv->attn_counters, kv->attn_floats, kv->n_counters, kv->identity ? nullptr : kv->bt,
                              kv->max_pages, tree ? tree->pref : nullptr, tree ? tree->mask : nullptr));
@@ -452,6 +461,16 @@ int build_plain(Ctx* c, const RawW& r, Tensor* out) {
   out->ne[0] = (uint64_t)K;
   out->ne[1] = (uint64_t)N;
   return ULB_OK;
+}
+
+/* a matrix kept as its GGUF rows, for the row GEMV */
+int build_raw(Ctx* c, const RawW& r, Tensor* out) {
+  out->type = r.type;
+  out->N = (int)r.ne[1];
+  out->K = (int)r.ne[0];
+  out->ne[0] = r.ne[0];
+  out->ne[1] = r.ne[1];
+  return upload_plain(c, r, &out->dev, &out->bytes);
 }
 
 void free_tensor(Ctx* c, Tensor& t) {
@@ -671,8 +690,21 @@ int ulb_model_finalize(ulb_model* mm) {
     ULB_TRY(expect(g, "ffn_gate", d.d_model, d.d_ff));
     ULB_TRY(expect(u, "ffn_up", d.d_model, d.d_ff));
     ULB_TRY(expect(dn, "ffn_down", d.d_ff, d.d_model));
-    for (const RawW* w : {q, k, v, o, g, u, dn})
-      ULB_CHECK(is_q4(w->type), ULB_EUNSUPPORTED, "%s linear weights must be Q4_0 or Q4_K", p.c_str());
+    for (const RawW* w : {q, k, g, u})
+      ULB_CHECK(is_q4(w->type), ULB_EUNSUPPORTED, "%s attn_q / attn_k / ffn_gate / ffn_up must be Q4_0 or Q4_K",
+                p.c_str());
+    /* attn_v, attn_output and ffn_down may also be GGUF rows of another type (llama.cpp's
+       Q4_K_M / Q5_K_M mixes put Q6_K there), multiplied by the row GEMV */
+    auto rows_ok = [&](const RawW* w) {
+      const int t = w->type;
+      const bool typ = t == ULB_TYPE_Q8_0 || t == ULB_TYPE_Q6_K || t == ULB_TYPE_F16 || t == ULB_TYPE_F32;
+      const uint64_t blk = t == ULB_TYPE_Q8_0 ? 32 : t == ULB_TYPE_Q6_K ? 256 : 8;
+      return typ && w->ne[0] % blk == 0;
+    };
+    for (const RawW* w : {v, o, dn})
+      ULB_CHECK(is_q4(w->type) || (rows_ok(w) && m->tp_world == 1), ULB_EUNSUPPORTED,
+                "%s attn_v / attn_output / ffn_down: type %d (Q4_0, Q4_K; or Q8_0, Q6_K, F16, F32 rows of whole "
+                "blocks without tensor parallelism)", p.c_str(), w->type);
     size_t b;
     ULB_TRY(upload_plain(c, *an, (void**)&L.attn_norm, &b));
     ULB_TRY(upload_plain(c, *fn, (void**)&L.ffn_norm, &b));
@@ -683,15 +715,21 @@ int ulb_model_finalize(ulb_model* mm) {
         const int f0 = s * 16;
         map[f0 + i] = f0 < nq + nkv ? (i < 8 ? f0 + 2 * i : f0 + 2 * (i - 8) + 1) : f0 + i;
       }
-    ULB_TRY(build_fused(c, {q, k, v}, map, &L.qkv));
-    ULB_TRY(build_plain(c, *o, &L.o));
+    if (is_q4(v->type)) {
+      ULB_TRY(build_fused(c, {q, k, v}, map, &L.qkv));
+    } else {
+      map.resize(nq + nkv);
+      ULB_TRY(build_fused(c, {q, k}, map, &L.qkv));
+      ULB_TRY(build_raw(c, *v, &L.v));
+    }
+    ULB_TRY(is_q4(o->type) ? build_plain(c, *o, &L.o) : build_raw(c, *o, &L.o));
     /* gate/up interleaved in strips: rows 0..7 gate 8s.., rows 8..15 up 8s.. */
     std::vector<int> gm(2 * d.d_ff);
     for (int s = 0; s < d.d_ff / 8; ++s)
       for (int i = 0; i < 16; ++i) gm[s * 16 + i] = i < 8 ? s * 8 + i : d.d_ff + s * 8 + (i - 8);
     ULB_TRY(build_fused(c, {g, u}, gm, &L.gateup));
-    ULB_TRY(build_plain(c, *dn, &L.down));
-    m->weight_bytes += L.qkv.bytes + L.o.bytes + L.gateup.bytes + L.down.bytes;
+    ULB_TRY(is_q4(dn->type) ? build_plain(c, *dn, &L.down) : build_raw(c, *dn, &L.down));
+    m->weight_bytes += L.qkv.bytes + L.v.bytes + L.o.bytes + L.gateup.bytes + L.down.bytes;
   }
   ULB_TRY(get("output_norm.weight", &r));
   ULB_CHECK(r->type == ULB_TYPE_F32 && r->ne[0] == (uint64_t)d.d_model, ULB_EFORMAT, "output_norm");
@@ -742,6 +780,7 @@ int ulb_model_free(ulb_model* mm) {
     dev_free(c, L.attn_norm, (size_t)m->d.d_model * 4);
     dev_free(c, L.ffn_norm, (size_t)m->d.d_model * 4);
     free_tensor(c, L.qkv); free_tensor(c, L.o); free_tensor(c, L.gateup); free_tensor(c, L.down);
+    free_tensor(c, L.v);
   }
   dev_free(c, m->out_norm, (size_t)m->d.d_model * 4);
   if (!m->out_shared) free_tensor(c, m->out);

@@ -636,10 +636,9 @@ __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
  * lane sums its integer dot products in fp32 and applies the block step with one fmaf; the
  * lanes' sums meet in a warp xor tree.
  */
-template <int QT>
+template <int QT, int EPI>
 __global__ void __launch_bounds__(256) rowgemv_kernel(const uint8_t* __restrict__ w, int N, int K,
-                                                      const __half* __restrict__ x, int ldx, int M,
-                                                      float* __restrict__ y, int ldy) {
+                                                      const __half* __restrict__ x, int ldx, int M, EpiArgs e) {
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
@@ -724,7 +723,14 @@ __global__ void __launch_bounds__(256) rowgemv_kernel(const uint8_t* __restrict_
     float v = acc[m];
 #pragma unroll
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0 && m < M) y[(size_t)m * ldy + n] = v;
+    if (lane == 0 && m < M) {
+      if (EPI == EPI_VCACHE) {
+        store_v_cache(e, m, n / e.hd, n % e.hd, v);
+      } else {
+        float* p = e.y + (size_t)m * e.ldy + n;
+        *p = EPI == EPI_RESID ? __ldcg(p) + v : v;
+      }
+    }
   }
 }
 
@@ -732,19 +738,34 @@ static bool raw_rows_type(int t) {
   return t == ULB_TYPE_Q8_0 || t == ULB_TYPE_Q6_K || t == ULB_TYPE_F16 || t == ULB_TYPE_F32;
 }
 
-static int launch_rowgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a) {
-  ULB_CHECK(epi == EPI_STORE && a.y, ULB_EUNSUPPORTED, "qgemv: a Q8_0 / Q6_K matrix takes the plain store epilogue only");
+template <int EPI>
+static auto rowgemv_for(int type) {
+  return type == ULB_TYPE_Q8_0   ? rowgemv_kernel<ULB_TYPE_Q8_0, EPI>
+         : type == ULB_TYPE_Q6_K ? rowgemv_kernel<ULB_TYPE_Q6_K, EPI>
+         : type == ULB_TYPE_F16  ? rowgemv_kernel<ULB_TYPE_F16, EPI>
+                                 : rowgemv_kernel<ULB_TYPE_F32, EPI>;
+}
+
+/* a matrix kept as GGUF rows (Q8_0 / Q6_K / F16 / F32): LM heads, and the attn_v / attn_output /
+   ffn_down projections llama.cpp's K-quant mixes store in Q6_K or Q8_0; 8 tokens per launch */
+static int launch_rowgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
+  ULB_CHECK(((epi == EPI_STORE || epi == EPI_RESID) && a0.y) || (epi == EPI_VCACHE && a0.vc && a0.row_pos && a0.row_seq),
+            ULB_EUNSUPPORTED, "qgemv: a Q8_0 / Q6_K / F16 / F32 matrix takes the store, residual or V-cache epilogue");
   ULB_CHECK(ldx % 8 == 0 && ((uintptr_t)x & 15) == 0, ULB_EINVAL, "qgemv: activations must be 16-byte aligned rows");
   ULB_CHECK(w->K % 8 == 0, ULB_EUNSUPPORTED, "row GEMV: K=%d not a multiple of 8", w->K);
   const dim3 grid((w->N + 7) / 8), block(256);
-  auto kern = w->type == ULB_TYPE_Q8_0   ? rowgemv_kernel<ULB_TYPE_Q8_0>
-              : w->type == ULB_TYPE_Q6_K ? rowgemv_kernel<ULB_TYPE_Q6_K>
-              : w->type == ULB_TYPE_F16  ? rowgemv_kernel<ULB_TYPE_F16>
-                                         : rowgemv_kernel<ULB_TYPE_F32>;
   for (int m0 = 0; m0 < M; m0 += 8) {
     const int mc = M - m0 < 8 ? M - m0 : 8;
-    cudaError_t e = launch_k(c, kern, grid, block, 0, (const uint8_t*)w->dev, w->N, w->K, x + (size_t)m0 * ldx, ldx, mc,
-                             a.y + (size_t)m0 * a.ldy, a.ldy);
+    EpiArgs a = a0;
+    if (a.y) a.y += (size_t)m0 * a.ldy;
+    if (a.row_seq) a.row_seq += m0;
+    if (a.row_pos) a.row_pos += m0;
+    cudaError_t e;
+    const uint8_t* wd = (const uint8_t*)w->dev;
+    const __half* xc = x + (size_t)m0 * ldx;
+    if (epi == EPI_STORE) e = launch_k(c, rowgemv_for<EPI_STORE>(w->type), grid, block, 0, wd, w->N, w->K, xc, ldx, mc, a);
+    else if (epi == EPI_RESID) e = launch_k(c, rowgemv_for<EPI_RESID>(w->type), grid, block, 0, wd, w->N, w->K, xc, ldx, mc, a);
+    else e = launch_k(c, rowgemv_for<EPI_VCACHE>(w->type), grid, block, 0, wd, w->N, w->K, xc, ldx, mc, a);
     if (e != cudaSuccess) return cuda_error(e, "row GEMV launch", __FILE__, __LINE__);
   }
   return ULB_OK;

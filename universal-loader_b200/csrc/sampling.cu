@@ -23,11 +23,14 @@
  * compacts that bin's elements into shared memory, and a radix select over the compacted
  * candidates finds the exact key.  Only a bin too large for the candidate buffer (a very flat
  * row) falls back to a radix select over the whole row.  The row is read from HBM once (the
- * argmax pass); the later passes find it in L2 (the stats grid keeps few rows in flight).
+ * argmax pass); the later passes find it in L2.
  *
- * Kernels: row_stats (one CTA per row: max, keep threshold, normaliser, argmax) over all
- * target and draft rows of a round in parallel; sample (stats + inverse CDF for the draft
- * tokens); decide (one CTA per sequence: accept test, residual / bonus sampling, commit).
+ * Kernels: accept (one CTA per sequence, a single kernel per round: the walk over the round's
+ * positions computes each p / q row's statistics -- max, keep threshold, normaliser, argmax --
+ * when it reaches the row, prefetching the next rows into L2, then the accept test, residual /
+ * bonus sampling and the commit; rows after the first rejection are never read); sample
+ * (statistics + inverse CDF for the draft tokens); for trees, row_stats over every p / q row of
+ * the trees in parallel and tree_decide (the walk of one sequence's tree).
  */
 #include <algorithm>
 
@@ -343,7 +346,7 @@ __device__ __forceinline__ double warped_e(const float* l, int i, float iT, cons
 
 /*
  * Inverse CDF in index order over weights produced by wfun(i) (fp64, >= 0): with W the
- * total weight (sum of per-thread contiguous segments, in segment order), returns the
+ * total weight (per-thread contiguous segments, summed by a scan over the block), returns the
  * smallest i whose cumulative weight exceeds u * W, and W in *total.  One pass over the
  * weights plus a scan of the one segment that holds the target.
  */
@@ -353,19 +356,27 @@ __device__ int block_inv_cdf(int V, float u, WF wfun, SmemRed<BT>& s, double* to
   const int b0 = threadIdx.x * seg, b1 = min(V, b0 + seg);
   double sum = 0.0;
   for (int i = b0; i < b1; ++i) sum += wfun(i);
+  /* the segments' exclusive prefix sums: a scan inside each warp, then the warps' totals */
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double inc = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  double exc = __shfl_up_sync(0xffffffffu, inc, 1);
+  if (lane == 0) exc = 0.0;
   __syncthreads();
-  s.seg[threadIdx.x] = sum;
+  if (lane == 31) s.d[warp] = inc;
   if (threadIdx.x == 0) s.found = 0x7fffffff;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    double c = 0.0;
-    for (int t = 0; t < BT; ++t) { const double v = s.seg[t]; s.seg[t] = c; c += v; }
-    s.above = c;
+  double W = 0.0, before = 0.0;
+  for (int w2 = 0; w2 < BT / 32; ++w2) {
+    if (w2 == warp) before = W;
+    W += s.d[w2];
   }
-  __syncthreads();
-  const double W = s.above;
   const double target = (double)u * W;
-  double cum = s.seg[threadIdx.x];
+  double cum = before + exc;
   if (b0 < b1 && cum + sum > target) {
     for (int i = b0; i < b1; ++i) {
       const double wv = wfun(i);
@@ -467,20 +478,39 @@ struct SpecCommit {
   int log_rounds, log_stride;
 };
 
-/* one CTA per sequence */
-__global__ void __launch_bounds__(DT) decide_kernel(const float* __restrict__ p, const float* __restrict__ q,
-                                                    const int32_t* __restrict__ draft, const RowStats* __restrict__ rs,
-                                                    int B, int k, int V, ulb_warp w, uint64_t seed,
-                                                    const uint32_t* dev_round, uint32_t round,
-                                                    int32_t* out_tokens, int32_t* out_n, SpecCommit cm) {
+/* the logits rows a walk may need next, on their way to L2 while it works on this one: the
+   16-byte-aligned part of the row (the bulk prefetch takes 16-byte-aligned addresses and
+   sizes; a row of a vocabulary that is not a multiple of 4 starts unaligned) */
+__device__ __forceinline__ void prefetch_row_l2(const float* row, int V) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(row), a1 = a0 + (uintptr_t)V * 4u;
+  const uintptr_t s0 = (a0 + 15u) & ~(uintptr_t)15u, e0 = a1 & ~(uintptr_t)15u;
+  for (uintptr_t o = s0 + (uintptr_t)threadIdx.x * 32768u; o < e0; o += (uintptr_t)blockDim.x * 32768u) {
+    const uint32_t len = e0 - o < 32768u ? (uint32_t)(e0 - o) : 32768u;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(o), "r"(len) : "memory");
+  }
+}
+
+/*
+ * Rejection sampling of one sequence's round in a single kernel (one CTA per sequence): the
+ * walk computes a row's warp statistics (max, keep threshold, normaliser, argmax) only when
+ * it reaches the row -- p_i, and q_i unless greedy -- and stops at the first rejection, so
+ * each row is read once and rows past the first rejection are never read.  The next
+ * position's rows are prefetched into L2 while this one is decided.
+ */
+__global__ void __launch_bounds__(DT) accept_kernel(const float* __restrict__ p, const float* __restrict__ q,
+                                                    const int32_t* __restrict__ draft, int B, int k, int V,
+                                                    ulb_warp w, uint64_t seed, const uint32_t* dev_round,
+                                                    uint32_t round, int32_t* out_tokens, int32_t* out_n,
+                                                    SpecCommit cm) {
   __shared__ SmemRed<DT> s;
+  __shared__ SelSmem sel;
+  __shared__ RowStats st_p, st_q;
   pdl_wait();
   pdl_trigger();
   const int b = blockIdx.x;
   const bool greedy = !(w.temperature > 0.f);
   const float iT = greedy ? 1.f : __fdiv_rn(1.0f, w.temperature); /* inverse temperature */
   const uint32_t rnd = dev_round ? dev_round[b] : round;
-  const int np = B * (k + 1);
   int n = 0, tok = -1;
   /* target probability (under the warp) of each committed token, for the round record (which
      the loop keeps for k <= kMaxLoggedK; ulb_spec_accept may pass a larger k and logs nothing) */
@@ -489,18 +519,29 @@ __global__ void __launch_bounds__(DT) decide_kernel(const float* __restrict__ p,
   auto note_p = [&](int j, float v) {
     if (j <= kMaxLoggedK) pcommit[j] = v;
   };
+  auto prow = [&](int i) { return p + ((size_t)b * (k + 1) + i) * V; };
+  auto qrow = [&](int i) { return q + ((size_t)b * k + i) * V; };
   for (int i = 0; i < k; ++i) {
     const int x = draft[b * k + i];
-    const RowStats sp = rs[b * (k + 1) + i];
+    const float* pl = prow(i);
+    prefetch_row_l2(prow(i + 1), V);
+    if (!greedy) {
+      prefetch_row_l2(qrow(i), V);
+      if (i + 1 < k) prefetch_row_l2(qrow(i + 1), V);
+    }
+    compute_row_stats(pl, V, w, st_p, s, sel);
+    __syncthreads();
+    const RowStats sp = st_p;
     if (greedy) {
       note_p(n, 1.0f);
       if (x == sp.amax) { ++n; continue; }
       tok = sp.amax;
       break;
     }
-    const RowStats sq = rs[np + b * k + i];
-    const float* pl = p + ((size_t)b * (k + 1) + i) * V;
-    const float* ql = q + ((size_t)b * k + i) * V;
+    const float* ql = qrow(i);
+    compute_row_stats(ql, V, w, st_q, s, sel);
+    __syncthreads();
+    const RowStats sq = st_q;
     const bool in_vocab = (unsigned)x < (unsigned)V; /* a token outside the vocabulary is rejected */
     const double px = in_vocab ? warped_e(pl, x, iT, sp) / sp.Z : 0.0;
     const double qx = in_vocab ? warped_e(ql, x, iT, sq) / sq.Z : 0.0;
@@ -520,12 +561,14 @@ __global__ void __launch_bounds__(DT) decide_kernel(const float* __restrict__ p,
     break;
   }
   if (tok < 0) {
-    const RowStats sp = rs[b * (k + 1) + k];
+    const float* pl = prow(k);
+    compute_row_stats(pl, V, w, st_p, s, sel);
+    __syncthreads();
+    const RowStats sp = st_p;
     if (greedy) {
       tok = sp.amax;
       note_p(n, 1.0f);
     } else {
-      const float* pl = p + ((size_t)b * (k + 1) + k) * V;
       const float u2 = rng_u(seed, rnd, (uint32_t)b, (uint32_t)k, ULB_RNG_RESID);
       tok = block_inv_cdf(V, u2, [&](int v) { return warped_e(pl, v, iT, sp); }, s, nullptr);
       note_p(n, (float)(warped_e(pl, tok, iT, sp) / sp.Z));
@@ -822,7 +865,7 @@ int launch_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* dr
                        int32_t* out_tokens, int32_t* out_n, void* stats_scratch, const void* commit);
 
 size_t sample_scratch_bytes(int, int) { return 0; }
-size_t accept_scratch_bytes(int B, int k, int) { return sizeof(RowStats) * (size_t)B * (2 * k + 1); }
+size_t accept_scratch_bytes(int, int, int) { return sizeof(RowStats); }
 
 int launch_sample(Ctx* c, const float* logits, int rows, int V, int ld, const ulb_warp* w, uint64_t seed,
                   const uint32_t* dev_round, uint32_t round, uint32_t slot, uint32_t tag, int32_t* out,
@@ -856,18 +899,12 @@ int launch_accept_impl(Ctx* c, const float* p, const float* q, const int32_t* dr
                        const ulb_warp* w, uint64_t seed, const uint32_t* dev_round, uint32_t round,
                        int32_t* out_tokens, int32_t* out_n, void* stats_scratch, const void* commit) {
   if (B == 0) return ULB_OK;
-  RowStats* rs = (RowStats*)stats_scratch;
-  const int rows = B * (k + 1) + B * k;
-  /* rows in flight (one per CTA): as many as keep ~60 MB of rows in L2, between 1 and 3 per SM */
-  const int fit = (int)std::min<long long>(3LL * c->n_sm, std::max<long long>(c->n_sm, 60000000LL / ((long long)V * 4)));
-  const int grid = std::min(rows, fit);
-  cudaError_t e = launch_k(c, stats_kernel, dim3(grid), dim3(ST), 0, p, q, B * (k + 1), B * k, V, *w, rs);
-  if (e != cudaSuccess) return cuda_error(e, "stats launch", __FILE__, __LINE__);
+  (void)stats_scratch; /* the walk keeps its row statistics in shared memory */
   SpecCommit cm = {};
   if (commit) cm = *(const SpecCommit*)commit;
-  e = launch_k(c, decide_kernel, dim3(B), dim3(DT), 0, p, q, draft, (const RowStats*)rs, B, k, V, *w, seed,
-               dev_round, round, out_tokens, out_n, cm);
-  if (e != cudaSuccess) return cuda_error(e, "decide launch", __FILE__, __LINE__);
+  cudaError_t e = launch_k(c, accept_kernel, dim3(B), dim3(DT), 0, p, q, draft, B, k, V, *w, seed, dev_round, round,
+                           out_tokens, out_n, cm);
+  if (e != cudaSuccess) return cuda_error(e, "accept launch", __FILE__, __LINE__);
   return ULB_OK;
 }
 

@@ -124,7 +124,9 @@ int repack_q4(Ctx* c, int type, const void* dev_raw, int raw_rows, int K, const 
               int packed_rows, Tensor* out);
 
 /* ------------------------------------------------------------------ kernels (launchers) */
-enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+/* EPI_VCACHE: the output rows are V features (the attn_v projection kept as GGUF rows), written
+   in fp16 straight into the V cache like the V strips of EPI_QKV */
+enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_VCACHE = 4 };
 
 /* KV cache pages: positions of a sequence are mapped to pages of kKvPage positions through a
    block table (bt[seq * max_pages + pos / kKvPage] = page, -1 = unmapped).  A page holds
