@@ -84,12 +84,28 @@ __device__ __forceinline__ void row_for_each(const float* __restrict__ l, int V,
         f(b, a[u].x); f(b + 1, a[u].y); f(b + 2, a[u].z); f(b + 3, a[u].w);
       }
     }
-    for (; i < V4; i += BT) {
-      const float4 a = __ldg(l4 + i);
-      f(4 * i, a.x); f(4 * i + 1, a.y); f(4 * i + 2, a.z); f(4 * i + 3, a.w);
+    if (i < V4) { /* the last up-to-eight float4s of the thread, all requested before any is used */
+      float4 a[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (i + u * BT < V4) a[u] = __ldg(l4 + i + u * BT);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (i + u * BT < V4) {
+          const int b = 4 * (i + u * BT);
+          f(b, a[u].x); f(b + 1, a[u].y); f(b + 2, a[u].z); f(b + 3, a[u].w);
+        }
     }
   } else {
-    for (int i = threadIdx.x; i < V; i += BT) f(i, l[i]);
+    int i = threadIdx.x;
+    for (; i + 7 * BT < V; i += 8 * BT) {
+      float a[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] = __ldg(l + i + u * BT);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) f(i + u * BT, a[u]);
+    }
+    for (; i < V; i += BT) f(i, __ldg(l + i));
   }
 }
 
@@ -355,6 +371,7 @@ __device__ int block_inv_cdf(int V, float u, WF wfun, SmemRed<BT>& s, double* to
   const int seg = (V + BT - 1) / BT;
   const int b0 = threadIdx.x * seg, b1 = min(V, b0 + seg);
   double sum = 0.0;
+#pragma unroll 8
   for (int i = b0; i < b1; ++i) sum += wfun(i);
   /* the segments' exclusive prefix sums: a scan inside each warp, then the warps' totals */
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -376,13 +393,30 @@ __device__ int block_inv_cdf(int V, float u, WF wfun, SmemRed<BT>& s, double* to
     W += s.d[w2];
   }
   const double target = (double)u * W;
-  double cum = before + exc;
-  if (b0 < b1 && cum + sum > target) {
-    for (int i = b0; i < b1; ++i) {
-      const double wv = wfun(i);
-      if (wv <= 0.0) continue;
-      cum += wv;
-      if (cum > target) { atomicMin(&s.found, i); break; }
+  const double cum = before + exc;
+  /* the first lane of each warp whose segment ends past the target starts a walk of the warp,
+     32 elements a step (a scan of their weights), through the rest of the warp's segments; the
+     lowest crossing of all warps is the result */
+  const unsigned past = __ballot_sync(0xffffffffu, b0 < b1 && cum + sum > target);
+  if (past) {
+    const int src = __ffs(past) - 1;
+    const int w0 = __shfl_sync(0xffffffffu, b0, src), w1 = min(V, (warp * 32 + 32) * seg);
+    double base = __shfl_sync(0xffffffffu, cum, src);
+    for (int g0 = w0; g0 < w1; g0 += 32) {
+      const int i = g0 + lane;
+      const double wv = i < w1 ? wfun(i) : 0.0;
+      double c = wv;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(0xffffffffu, c, o);
+        if (lane >= o) c += t;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, wv > 0.0 && base + c > target);
+      if (hit) {
+        if (lane == 0) atomicMin(&s.found, g0 + __ffs(hit) - 1);
+        break;
+      }
+      base += __shfl_sync(0xffffffffu, c, 31);
     }
   }
   __syncthreads();
