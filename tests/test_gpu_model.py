@@ -461,3 +461,18 @@ class GpuModelTied(GpuModel):
             U.check(U.lib().ulb_model_set_weight(h, nm.encode(), t, ne4, raw.ctypes.data_as(C.c_void_p), raw.nbytes))
         U.check(U.lib().ulb_model_finalize(h))
         self.om = om
+
+
+def test_long_prompts_prefill_in_chunks_of_any_attention_form(tiny_target, tiny_draft):
+    """Prompts past 2048 positions on 24 sequences: the 256-row prefill chunks run the streaming
+    attention form and the short last chunks the per-split form with its global split merge, whose
+    scratch the loop's workspaces must already hold.  Greedy streams against the oracle."""
+    prompts = [_prompt(n, seed=60 + n) for n in (2090, 2113)]
+    api = _api(tiny_target, tiny_draft, k=3)
+    got = api.generate_tokens([p.tolist() for p in prompts] * 12, _cfg(6))
+    assert len(got) == 24 and all(len(g) == 6 for g in got)
+    t, d = orc.Model(tiny_target), orc.Model(tiny_draft)
+    want, _, _, _, tm = orc.spec_generate(t, d, prompts, 6, 3, (0.0, 0, 1.0), seed=0, with_margins=True)
+    for i in range(2):
+        _match_greedy(got[i], want[i], tm[i], "prompt of %d tokens among 24 sequences" % len(prompts[i]))
+        assert all(got[i + 2 * j] == got[i] for j in range(12))

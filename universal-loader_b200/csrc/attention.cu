@@ -814,7 +814,7 @@ int validate_attn_desc(const ulb_attn_desc* d, int M, int rps) {
 }
 
 int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int max_pos, size_t* floats,
-                           int* n_counters, bool tree) {
+                           int* n_counters, bool tree, bool bound) {
   ULB_TRY(validate_attn_desc(d, M, rps));
   *floats = 0;
   *n_counters = 0;
@@ -822,7 +822,10 @@ int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int m
   AttnParams p{};
   int ng;
   attn_geometry(d, M, rps, max_pos, &p, &ng);
-  if (attn_use_stream(c, p, ng, tree) || p.max_splits == 1) return ULB_OK;
+  /* bound: what the per-split form would need, whatever this shape's form -- a workspace sized
+     by it serves every launch of up to this many rows, although the form of a smaller launch
+     (a short prefill chunk, fewer sequences) may differ from this one's */
+  if ((!bound && attn_use_stream(c, p, ng, tree)) || p.max_splits == 1) return ULB_OK;
   bool cl = false;
   const cudaError_t e = d->head_dim == 64 ? attn_cluster_merge<64>(p.max_splits, &cl)
                                           : attn_cluster_merge<128>(p.max_splits, &cl);

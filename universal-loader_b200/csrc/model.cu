@@ -221,7 +221,7 @@ static int ensure_attn(KV* kv, int M, int rps, bool tree) {
   ulb_attn_desc ad{d.n_head, d.n_head_kv, d.head_dim, kv->cap, kv->n_seq, 1.0f / std::sqrt((float)d.head_dim)};
   int nc = 0;
   size_t nf = 0;
-  ULB_TRY(attention_scratch_need(kv->m->c, &ad, M, rps, kv->cap - 1, &nf, &nc, tree));
+  ULB_TRY(attention_scratch_need(kv->m->c, &ad, M, rps, kv->cap - 1, &nf, &nc, tree, /*bound=*/true));
   if (nf <= kv->attn_floats && nc <= kv->n_counters) return ULB_OK;
   /* grow to the largest shape seen so far: every prepared shape must keep fitting */
   const size_t f2 = nf > kv->attn_floats ? nf : kv->attn_floats;

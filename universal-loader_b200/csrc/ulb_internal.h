@@ -210,10 +210,12 @@ int launch_attention(Ctx* c, const ulb_attn_desc* d, const float* q, int ldq, co
 /* argument checks shared by every attention entry point (no division by a zero head count) */
 int validate_attn_desc(const ulb_attn_desc* d, int M, int rps);
 /* split-merge scratch a launch of this shape needs: zero floats / counters when it has one key
-   split, or when its splits merge in a thread-block cluster (only a global-memory merge, over
-   caches longer than 2048 positions, reads the scratch and counters) */
+   split, when its splits merge in a thread-block cluster, or when it runs in the streaming form
+   (only a global-memory merge, over caches longer than 2048 positions, reads the scratch and
+   counters); bound = true: the per-split form's need whatever the form, which covers every
+   launch of up to M rows */
 int attention_scratch_need(Ctx* c, const ulb_attn_desc* d, int M, int rps, int max_pos, size_t* floats,
-                           int* n_counters, bool tree = false);
+                           int* n_counters, bool tree = false, bool bound = false);
 
 int launch_rmsnorm(Ctx* c, const float* x, int ldx, const float* g, int M, int d, float eps,
                    const int* row_select, __half* out, int ldo);
