@@ -932,30 +932,41 @@ def run_ops(args):
             ctx.free_tensor(h)
     # block-causal attention of the verify / draft rows against a KV cache (ulb_attention_noalloc:
     # no allocation or synchronisation inside the timed loop); bytes = the K/V rows read
-    for (label, H, Hkv, hd, rps, L) in (("attn:7b_verify", 32, 32, 128, 6, 768), ("attn:tinyllama_draft", 32, 4, 64, 2, 768),
-                                        ("attn:7b_verify_4k", 32, 32, 128, 6, 4096)):
+    # (label, heads, kv heads, head dim, rows per sequence, sequences, context): one sequence at the
+    # config-2 verify / draft shapes, and config 4's 64 sequences (contexts U[256, 4096] + 128, seed 1)
+    # for the verify (9 rows, hd 128) and the draft (1 row, hd 64)
+    c4_ctx = np.random.default_rng(1).integers(256, 4097, 64) + 128
+    for (label, H, Hkv, hd, rps, S, Ls) in (("attn:7b_verify", 32, 32, 128, 6, 1, [768]),
+                                            ("attn:tinyllama_draft", 32, 4, 64, 2, 1, [768]),
+                                            ("attn:7b_verify_4k", 32, 32, 128, 6, 1, [4096]),
+                                            ("attn:c4_verify", 32, 8, 128, 9, 64, c4_ctx),
+                                            ("attn:c4_draft", 32, 8, 64, 1, 64, c4_ctx)):
         if args.only and not label.startswith(args.only):
             continue
-        cap = L + 8
-        desc = U.AttnDesc(H, Hkv, hd, cap, 1, 1.0 / float(np.sqrt(hd)))
-        q = rng.standard_normal((rps, H * hd)).astype(np.float32)
-        kc = rng.standard_normal((1, Hkv, cap, hd)).astype(np.float16)
-        vc = rng.standard_normal((1, Hkv, cap, hd)).astype(np.float16)
-        rs = np.zeros(rps, np.int32)
-        rp = np.arange(L - rps, L, dtype=np.int32)
+        cap = int(max(Ls)) + 8
+        desc = U.AttnDesc(H, Hkv, hd, cap, S, 1.0 / float(np.sqrt(hd)))
+        M = S * rps
+        q = rng.standard_normal((M, H * hd)).astype(np.float32)
+        kc = (rng.standard_normal((S, Hkv, cap, hd), dtype=np.float32)).astype(np.float16)
+        vc = (rng.standard_normal((S, Hkv, cap, hd), dtype=np.float32)).astype(np.float16)
+        rs = np.repeat(np.arange(S, dtype=np.int32), rps)
+        rp = np.concatenate([np.arange(int(L) - rps, int(L), dtype=np.int32) for L in Ls])
         bufs = [ctx.buffer(a) for a in (q, kc, vc, rs, rp)]
-        out = ctx.buffer(nbytes=rps * H * hd * 2)
+        out = ctx.buffer(nbytes=M * H * hd * 2)
         call = lambda: U.check(U.lib().ulb_attention_noalloc(ctx.h, C.byref(desc), bufs[0].ptr, bufs[1].ptr, bufs[2].ptr,
-                                                             bufs[3].ptr, bufs[4].ptr, rps, rps, out.ptr))
+                                                             bufs[3].ptr, bufs[4].ptr, M, rps, out.ptr))
         for _ in range(max(1, args.warmup)):
             call()
         ctx.sync()
-        g = ctx.capture(lambda: [call() for _ in range(20)])  # each call: counter reset + kernel
-        ms = ctx.time_graph(g, max(args.steps, 3)) / 20
+        reps = 20 if S == 1 else 4
+        g = ctx.capture(lambda: [call() for _ in range(reps)])  # each call: counter reset + kernel
+        ms = ctx.time_graph(g, max(args.steps, 3)) / reps
         U.lib().ulb_graph_free(g)
-        alg = 2 * L * Hkv * hd * 2 + q.nbytes + rps * H * hd * 2
+        kv = 2 * int(sum(int(L) for L in Ls)) * Hkv * hd * 2
+        alg = kv + q.nbytes + M * H * hd * 2
         results[label] = {"us": ms * 1e3, "gbs": alg / ms / 1e6, "hbm_frac": alg / ms / 1e6 / peak,
-                          "note": "K/V of one sequence (%.1f MB) fit in L2: a latency figure" % (2 * L * Hkv * hd * 2 / 1e6)}
+                          "note": ("K/V of one sequence (%.1f MB) fit in L2: a latency figure" % (kv / 1e6)) if S == 1
+                          else "K/V of %d sequences: %.0f MB" % (S, kv / 1e6)}
         for b in bufs + [out]:
             b.free()
     # rejection sampling: config 3's [64, 9 | 8, 32000] at T = 1 and T = 0, and config 4's vocabulary
