@@ -514,33 +514,39 @@ __global__ void __launch_bounds__(AW * 32, 1)
 
 /*
  * Streaming form for large batches (many sequences x heads, long caches): one CTA per
- * (16-query tile, kv head, sequence) walks all of the tile's key splits in order, so a CTA
- * never exits between splits and the split partials never leave the SM.  Per split, warp w
- * scores its 64-key block exactly as attn_mma_kernel does (same staging, same block
- * arithmetic, same in-CTA merge), and each thread folds the split's partial of its (query,
- * output pair) items into a running merge in registers with merge_next, the arithmetic of
- * the other forms' split merges: a row gets the same bits from either kernel.
- * Each warp's K and V blocks are a pipeline: the next split's keys are requested as soon as
- * this split's scores are computed, its values as soon as P.V is done, and the blocks of the
- * split after that are prefetched into L2 (cp.async.bulk.prefetch), so HBM keeps streaming
- * while the SM computes.  Shared memory: K [4][64][HD] | V [4][64][HD] | warp partials
- * [4][16][HD + 2].  No scratch, no counters.
+ * (TT 16-query tiles, kv head, sequence) walks all of its key splits in order, so a CTA never
+ * exits between splits and the split partials never leave the SM.  Per split, warp (t, w)
+ * scores tile t against 64-key block w exactly as attn_mma_kernel does (same staging, same
+ * block arithmetic, same in-CTA merge), and each thread folds the split's partial of its
+ * (query, output pair) items into a running merge in registers with merge_next, the
+ * arithmetic of the other forms' split merges: a row gets the same bits from either kernel.
+ * (A split past a tile's last position adds exact zeros to its merge.)
+ * The warps of tile 0 stage each 64-key block once for all TT tiles; K and V are a pipeline:
+ * the next split's keys are requested as soon as this split's scores are computed, its values
+ * as soon as P.V is done, and the blocks of the split after that are prefetched into L2
+ * (cp.async.bulk.prefetch), so HBM keeps streaming while the SM computes.  The warps sharing a
+ * block meet on a named barrier of their own.  Shared memory: K [4][64][HD] | V [4][64][HD] |
+ * warp partials [TT][4][16][HD + 2].  No scratch, no counters.
  */
-template <int HD>
-__global__ void __launch_bounds__(AW * 32, 1)
+template <int HD, int TT>
+__global__ void __launch_bounds__(TT * AW * 32, 1)
     attn_stream_kernel(AttnParams p, const float* __restrict__ q, const __half* __restrict__ kc,
                        const __half* __restrict__ vc, const int* __restrict__ row_seq,
                        const int* __restrict__ row_pos, __half* __restrict__ out) {
   constexpr int KS = HD / 16, DN = HD / 8, PST = HD + 2;
-  constexpr int ITEMS = QT * (HD / 2) / (AW * 32); /* (query, output pair) items per thread */
+  constexpr int ITEMS = QT * (HD / 2) / (AW * 32); /* (query, output pair) items per thread of a tile */
   extern __shared__ __align__(128) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const int mt = blockIdx.x, kvh = blockIdx.y, gi = blockIdx.z;
-  const int Q = p.G * p.rps, q0 = mt * QT, nq = min(QT, Q - q0);
+  const int tw = warp / AW, bw = warp % AW, ttid = tid - tw * AW * 32; /* tile of the warp, its block */
+  const int mt = blockIdx.x * TT + tw, kvh = blockIdx.y, gi = blockIdx.z;
+  const int Q = p.G * p.rps, q0 = mt * QT, nq = min(QT, Q - q0); /* nq <= 0: no such tile */
+  const bool live = nq > 0;
   const int m0 = gi * p.rps;
   const int qa = q0 + g, qb = q0 + g + 8;
   const bool va = g < nq, vb = g + 8 < nq;
-  int last_pos = lane < nq ? row_pos[m0 + (q0 + lane) / p.G] : 0;
+  /* the CTA's last position: over the TT tiles' rows (at most 32, one per lane) */
+  const int cq0 = blockIdx.x * TT * QT, cnq = min(TT * QT, Q - cq0);
+  int last_pos = lane < cnq ? row_pos[m0 + (cq0 + lane) / p.G] : 0;
   const int seq = row_seq[m0];
   const int pa = va ? row_pos[m0 + qa / p.G] : -1, pb = vb ? row_pos[m0 + qb / p.G] : -1;
   int first_new = lane < p.rps ? row_pos[m0 + lane] : INT_MAX;
@@ -554,26 +560,33 @@ __global__ void __launch_bounds__(AW * 32, 1)
   const int n_splits = last_pos / SPLITK + 1;
   if ((unsigned)seq >= (unsigned)p.n_seq) return;
 
-  __half* const Ks = reinterpret_cast<__half*>(sm) + (size_t)warp * KB * HD;
-  __half* const Vs = reinterpret_cast<__half*>(sm) + (size_t)(AW + warp) * KB * HD;
-  float* const part = reinterpret_cast<float*>(sm + (size_t)2 * AW * KB * HD * sizeof(__half));
-  /* this warp's block of split s: its first key, cache offset and key count (<= 0: none) */
+  const bool stager = tw == 0; /* tile 0's warps stage the blocks for every tile */
+  __half* const Ks = reinterpret_cast<__half*>(sm) + (size_t)bw * KB * HD;
+  __half* const Vs = reinterpret_cast<__half*>(sm) + (size_t)(AW + bw) * KB * HD;
+  float* const part = reinterpret_cast<float*>(sm + (size_t)2 * AW * KB * HD * sizeof(__half)) +
+                      (size_t)tw * AW * QT * PST;
+  /* the warps sharing block bw (one per tile): their own barrier; one warp: the warp itself */
+  auto pair_sync = [&]() {
+    if (TT == 1) __syncwarp();
+    else asm volatile("bar.sync %0, %1;" ::"r"(1 + bw), "r"(TT * 32) : "memory");
+  };
+  /* block bw of split s: its first key, cache offset and key count (<= 0: none) */
   auto block_of = [&](int s, int& kb0, size_t& kvoff, int& nk) {
-    kb0 = (s * AW + warp) * KB;
+    kb0 = (s * AW + bw) * KB;
     int page_ok = 1;
     if (p.max_pages > 0) {
       const int slot = seq * p.max_pages + s;
       const int page = p.bt ? p.bt[slot] : slot;
       page_ok = page >= 0;
-      kvoff = (((size_t)max(page, 0) * p.Hkv + kvh) * kKvPage + warp * KB) * HD;
+      kvoff = (((size_t)max(page, 0) * p.Hkv + kvh) * kKvPage + bw * KB) * HD;
     } else {
       kvoff = (((size_t)seq * p.Hkv + kvh) * p.cap + max(kb0, 0)) * HD;
     }
     nk = page_ok ? min(KB, last_pos + 1 - kb0) : 0;
   };
-  /* the K / V rows of this warp's block of split s on their way to L2 */
+  /* the K / V rows of block bw of split s on their way to L2 */
   auto prefetch = [&](int s) {
-    if (s >= n_splits || lane != 0) return;
+    if (s >= n_splits || lane != 0 || !stager) return;
     int kb, n;
     size_t off;
     block_of(s, kb, off, n);
@@ -588,25 +601,25 @@ __global__ void __launch_bounds__(AW * 32, 1)
   {
     /* split 0: the rows that predate this forward before griddepcontrol.wait, the rest after */
     const int n_old = max(0, min(nk, first_new - kb0));
-    if (nk > 0) {
+    if (stager && nk > 0) {
       stage_rows<HD>(Ks, kc + kvoff, nk, 0, n_old, lane);
       stage_rows<HD>(Vs, vc + kvoff, nk, 0, n_old, lane);
     }
     prefetch(1); /* a hint into L2, the point of coherence: rows still to be written may go too */
     pdl_wait();
     pdl_trigger();
-    if (nk > 0) {
+    if (stager && nk > 0) {
       stage_rows<HD>(Ks, kc + kvoff, nk, n_old, KB, lane);
       stage_rows<HD>(Vs, vc + kvoff, nk, n_old, KB, lane);
     }
     cp_commit();
   }
-  const float* qpa = q + (size_t)(m0 + (va ? qa : q0) / p.G) * p.ldq + (kvh * p.G + (va ? qa : q0) % p.G) * HD;
-  const float* qpb = q + (size_t)(m0 + (vb ? qb : q0) / p.G) * p.ldq + (kvh * p.G + (vb ? qb : q0) % p.G) * HD;
+  const float* qpa = q + (size_t)(m0 + (va ? qa : 0) / p.G) * p.ldq + (kvh * p.G + (va ? qa : 0) % p.G) * HD;
+  const float* qpb = q + (size_t)(m0 + (vb ? qb : 0) / p.G) * p.ldq + (kvh * p.G + (vb ? qb : 0) % p.G) * HD;
   uint32_t qh[KS][4], ql[KS][4];
   q_frags<HD>(qpa, qpb, va, vb, t, qh, ql);
 
-  /* the running merge of the splits' partials: thread items it = tid + 128 j */
+  /* the running merge of the splits' partials: thread items it = ttid + 128 j of its tile */
   float RM[ITEMS], RL[ITEMS], RX[ITEMS], RY[ITEMS];
   for (int s = 0; s < n_splits; ++s) {
     float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
@@ -614,32 +627,32 @@ __global__ void __launch_bounds__(AW * 32, 1)
 #pragma unroll
     for (int d = 0; d < DN; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
     float sc[8][4];
-    /* keys of split s (groups pending: K_s, V_s; split 0: one group) */
+    /* keys of split s (the stager's groups pending: K_s, V_s; split 0: one group) */
     if (s == 0) asm volatile("cp.async.wait_group 0;" ::: "memory");
     else asm volatile("cp.async.wait_group 1;" ::: "memory");
-    __syncwarp();
-    if (nk > 0) score_block<HD>(Ks, qh, ql, kb0, pa, pb, p.scale2, lane, sc, mA, mB, lA, lB);
-    __syncwarp();
-    /* this warp's block of the next split: keys now, values once this split's are consumed */
+    pair_sync();
+    if (live && nk > 0) score_block<HD>(Ks, qh, ql, kb0, pa, pb, p.scale2, lane, sc, mA, mB, lA, lB);
+    pair_sync();
+    /* block bw of the next split: keys now, values once this split's are consumed */
     int kb1 = 0, nk1 = 0;
     size_t kvoff1 = 0;
     if (s + 1 < n_splits) {
       block_of(s + 1, kb1, kvoff1, nk1);
-      if (nk1 > 0) stage_rows<HD>(Ks, kc + kvoff1, nk1, 0, KB, lane);
+      if (stager && nk1 > 0) stage_rows<HD>(Ks, kc + kvoff1, nk1, 0, KB, lane);
     }
     cp_commit();
     prefetch(s + 2);
     asm volatile("cp.async.wait_group 1;" ::: "memory"); /* V_s */
-    __syncwarp();
-    if (nk > 0) pv_block<HD>(Vs, sc, lane, o);
-    __syncwarp();
-    if (s + 1 < n_splits && nk1 > 0) stage_rows<HD>(Vs, vc + kvoff1, nk1, 0, KB, lane);
+    pair_sync();
+    if (live && nk > 0) pv_block<HD>(Vs, sc, lane, o);
+    pair_sync();
+    if (stager && s + 1 < n_splits && nk1 > 0) stage_rows<HD>(Vs, vc + kvoff1, nk1, 0, KB, lane);
     cp_commit();
-    write_warp_partial<HD>(part + (size_t)warp * QT * PST, lane, mA, mB, lA, lB, o);
+    write_warp_partial<HD>(part + (size_t)bw * QT * PST, lane, mA, mB, lA, lB, o);
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
-      const int it = tid + j * AW * 32, qi = it / (HD / 2), d2 = it % (HD / 2);
+      const int it = ttid + j * AW * 32, qi = it / (HD / 2), d2 = it % (HD / 2);
       float M, L, ox, oy;
       cta_merge_item<HD>(part, (size_t)QT * PST, qi, d2, M, L, ox, oy);
       merge_next(s == 0, M, L, ox, oy, RM[j], RL[j], RX[j], RY[j]);
@@ -649,9 +662,10 @@ __global__ void __launch_bounds__(AW * 32, 1)
     nk = nk1;
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (!live) return;
 #pragma unroll
   for (int j = 0; j < ITEMS; ++j) {
-    const int it = tid + j * AW * 32, qi = it / (HD / 2), d2 = it % (HD / 2);
+    const int it = ttid + j * AW * 32, qi = it / (HD / 2), d2 = it % (HD / 2);
     if (qi < nq) {
       const float inv = RL[j] > 0.f ? 1.0f / RL[j] : 0.f;
       const int qq = q0 + qi;
@@ -681,10 +695,12 @@ size_t attn_smem(int hd) {
   const size_t part = (size_t)(AW + 1) * QT * (hd + 2) * sizeof(float); /* warp partials + the split's */
   return std::max(kv, part);
 }
-/* streaming form: K / V blocks of the 4 warps + their partials */
-size_t attn_stream_smem(int hd) {
-  return (size_t)AW * 2 * KB * hd * sizeof(__half) + (size_t)AW * QT * (hd + 2) * sizeof(float);
+/* streaming form: K / V blocks of the 4 warp columns + the partials of TT tiles' warps */
+size_t attn_stream_smem(int hd, int tt) {
+  return (size_t)AW * 2 * KB * hd * sizeof(__half) + (size_t)tt * AW * QT * (hd + 2) * sizeof(float);
 }
+/* tiles per streaming CTA: two once a (kv head, sequence) has two or more query tiles */
+int attn_stream_tiles(const AttnParams& p) { return p.n_mt >= 2 ? 2 : 1; }
 
 /* Which form runs a launch: one CTA per key split (short latency for a few sequences: every
    split of every head in flight at once) or one CTA walking all splits of its (tile, head,
@@ -698,10 +714,11 @@ bool attn_use_stream(const Ctx* c, const AttnParams& p, int ng, bool tree) {
   if (c && c->attn_form == ULB_ATTN_STREAM) return true;
   const int n_sm = c ? c->n_sm : 0;
   if (p.max_splits < 2) return false;
+  const int tt = attn_stream_tiles(p);
   const long long base = (long long)p.n_mt * p.Hkv * ng, sm = n_sm > 0 ? n_sm : 148;
-  const long long occ = p.hd == 64 ? 2 : 1;
+  const long long sbase = (long long)((p.n_mt + tt - 1) / tt) * p.Hkv * ng, occ = p.hd == 64 && tt == 1 ? 2 : 1;
   const double t_split = (double)((base * p.max_splits + sm - 1) / sm) * 12.0;
-  const double t_stream = (double)((base + sm * occ - 1) / (sm * occ)) * (6.0 + 2.5 * p.max_splits);
+  const double t_stream = (double)((sbase + sm * occ - 1) / (sm * occ)) * (6.0 + 2.5 * p.max_splits);
   return t_stream < 0.8 * t_split; /* a close call stays with the short-latency form */
 }
 
@@ -767,12 +784,18 @@ cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, con
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [] {
-      attr_err = cudaFuncSetAttribute(attn_stream_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)attn_stream_smem(HD));
+      attr_err = cudaFuncSetAttribute(attn_stream_kernel<HD, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)attn_stream_smem(HD, 1));
+      if (attr_err == cudaSuccess)
+        attr_err = cudaFuncSetAttribute(attn_stream_kernel<HD, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)attn_stream_smem(HD, 2));
     });
     if (attr_err != cudaSuccess) return attr_err;
-    return launch_k(c, attn_stream_kernel<HD>, dim3(p.n_mt, p.Hkv, ng), dim3(AW * 32), attn_stream_smem(HD), p, q, k,
-                    v, row_seq, row_pos, out);
+    if (attn_stream_tiles(p) == 2)
+      return launch_k(c, attn_stream_kernel<HD, 2>, dim3((p.n_mt + 1) / 2, p.Hkv, ng), dim3(2 * AW * 32),
+                      attn_stream_smem(HD, 2), p, q, k, v, row_seq, row_pos, out);
+    return launch_k(c, attn_stream_kernel<HD, 1>, dim3(p.n_mt, p.Hkv, ng), dim3(AW * 32), attn_stream_smem(HD, 1), p,
+                    q, k, v, row_seq, row_pos, out);
   }
   bool cl = false;
   const cudaError_t se = attn_cluster_merge<HD>(p.max_splits, &cl);
