@@ -158,11 +158,6 @@ __device__ __forceinline__ void epilogue(const EpiArgs& e, int strip, int nt, in
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ uint64_t gtimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
 
 /* 128-bit weight load: read once, so it neither allocates in L1 (kept for the activations)
    nor waits for the previous kernel (weights are constant) */
