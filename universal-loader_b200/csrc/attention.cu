@@ -255,10 +255,8 @@ __device__ __forceinline__ void write_warp_partial(float* pw, int lane, float mA
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int d = 0; d < HD / 8; ++d) {
-    pw[g * PST + 2 + d * 8 + 2 * t] = o[d][0];
-    pw[g * PST + 3 + d * 8 + 2 * t] = o[d][1];
-    pw[(g + 8) * PST + 2 + d * 8 + 2 * t] = o[d][2];
-    pw[(g + 8) * PST + 3 + d * 8 + 2 * t] = o[d][3];
+    *reinterpret_cast<float2*>(pw + g * PST + 2 + d * 8 + 2 * t) = make_float2(o[d][0], o[d][1]);
+    *reinterpret_cast<float2*>(pw + (g + 8) * PST + 2 + d * 8 + 2 * t) = make_float2(o[d][2], o[d][3]);
   }
   if (t == 0) {
     pw[g * PST] = mA;
@@ -268,47 +266,82 @@ __device__ __forceinline__ void write_warp_partial(float* pw, int lane, float mA
   }
 }
 
-/* the split's (max, sum, output pair d2) of query qi from the 4 warp partials, warp order;
-   warp w's partial starts at part + w * wstride */
+/*
+ * The merges, each split into a per-row step (the maxima, the sums and the factors, computed
+ * once per query row) and a per-pair step (the output pairs of the row, which only apply the
+ * row's factors), so no exponential is evaluated once per output element.
+ *
+ * In-CTA merge of a split's 4 warp partials, in warp order (warp w's partial starts at
+ * part + w * wstride): row_factors gives f = {M, L, e_0 .. e_3} with M = max_w m_w,
+ * e_w = exp2(m_w - M) (0 for a block without keys), L = the fmaf chain of l_w e_w;
+ * merge_pair the fmaf chain of o_w e_w for output pair d2.
+ */
+constexpr int RF = AW + 2; /* floats of a row's factor record */
 template <int HD>
-__device__ __forceinline__ void cta_merge_item(const float* part, size_t wstride, int qi, int d2, float& M, float& L,
-                                               float& ox, float& oy) {
+__device__ __forceinline__ void row_factors(const float* part, size_t wstride, int qi, float* f) {
   constexpr int PST = HD + 2;
-  M = -INFINITY;
-#pragma unroll
-  for (int w = 0; w < AW; ++w) M = fmaxf(M, part[w * wstride + (size_t)qi * PST]);
-  L = 0.f;
-  ox = 0.f;
-  oy = 0.f;
+  float mw[AW], lw[AW];
 #pragma unroll
   for (int w = 0; w < AW; ++w) {
-    const float* pw = part + w * wstride + (size_t)qi * PST;
-    const float e = pw[0] == -INFINITY ? 0.f : exp2f(pw[0] - M);
-    L = __fmaf_rn(pw[1], e, L);
-    ox = __fmaf_rn(pw[2 + 2 * d2], e, ox);
-    oy = __fmaf_rn(pw[3 + 2 * d2], e, oy);
+    mw[w] = part[w * wstride + (size_t)qi * PST];
+    lw[w] = part[w * wstride + (size_t)qi * PST + 1];
   }
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < AW; ++w) M = fmaxf(M, mw[w]);
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < AW; ++w) {
+    const float e = mw[w] == -INFINITY ? 0.f : exp2f(mw[w] - M);
+    L = __fmaf_rn(lw[w], e, L);
+    f[2 + w] = e;
+  }
+  f[0] = M;
+  f[1] = L;
+}
+template <int HD>
+__device__ __forceinline__ float2 merge_pair(const float* part, size_t wstride, int qi, int d2, const float* f) {
+  constexpr int PST = HD + 2;
+  float2 o[AW];
+#pragma unroll
+  for (int w = 0; w < AW; ++w) o[w] = *reinterpret_cast<const float2*>(part + w * wstride + (size_t)qi * PST + 2 + 2 * d2);
+  float ox = 0.f, oy = 0.f;
+#pragma unroll
+  for (int w = 0; w < AW; ++w) {
+    ox = __fmaf_rn(o[w].x, f[2 + w], ox);
+    oy = __fmaf_rn(o[w].y, f[2 + w], oy);
+  }
+  return make_float2(ox, oy);
 }
 
-/* the next split's partial (m, l, (oxs, oys)) into the running merge (M, L, ox, oy) of the
-   splits before it, in split order; split 0's partial is taken as it is.  Every form of the
-   kernel merges splits with exactly this arithmetic. */
-__device__ __forceinline__ void merge_next(bool first, float m, float l, float oxs, float oys, float& M, float& L,
-                                           float& ox, float& oy) {
+/* Merge of split partials in split order, every form of the kernel with exactly this
+   arithmetic: merge_row folds split partial (m, l) into the row's running (M, L) and returns
+   the factors of the running and the new output (split 0 is taken as it is); merge_pair_next
+   applies them to an output pair. */
+struct MergeFac {
+  float a, b;
+};
+__device__ __forceinline__ MergeFac merge_row(bool first, float m, float l, float& M, float& L) {
   if (first) {
     M = m;
     L = l;
-    ox = oxs;
-    oy = oys;
-    return;
+    return MergeFac{0.f, 1.f};
   }
   const float Mn = fmaxf(M, m);
   const float a = M == -INFINITY ? 0.f : exp2f(M - Mn);
   const float b = m == -INFINITY ? 0.f : exp2f(m - Mn);
   L = __fmaf_rn(l, b, L * a);
-  ox = __fmaf_rn(oxs, b, ox * a);
-  oy = __fmaf_rn(oys, b, oy * a);
   M = Mn;
+  return MergeFac{a, b};
+}
+__device__ __forceinline__ void merge_pair_next(bool first, MergeFac f, float oxs, float oys, float& ox, float& oy) {
+  if (first) {
+    ox = oxs;
+    oy = oys;
+    return;
+  }
+  ox = __fmaf_rn(oxs, f.b, ox * f.a);
+  oy = __fmaf_rn(oys, f.b, oy * f.a);
 }
 
 template <int HD, bool CL, bool TREE>
@@ -416,10 +449,16 @@ __global__ void __launch_bounds__(AW * 32, 1)
     pv_block<HD>(Vs, s, lane, o);
   }
 
-  /* merge the 4 warp blocks (shared memory, warp order) */
+  /* merge the 4 warp blocks (shared memory, warp order): each row's factors once, then its
+     output pairs; rows past the tile's queries are never merged */
   float* part = reinterpret_cast<float*>(sm); /* [AW][QT][PST], over the K / V staging */
+  __shared__ float rowf[QT][RF];
+  __shared__ MergeFac sfac[QT][MAXSPLIT]; /* split-merge factors of each row */
+  __shared__ float sinv[QT];
   __syncthreads();
   write_warp_partial<HD>(part + (size_t)warp * QT * PST, lane, mA, mB, lA, lB, o);
+  __syncthreads();
+  if (tid < nq) row_factors<HD>(part, (size_t)QT * PST, tid, rowf[tid]);
   __syncthreads();
   auto out_ptr = [&](int qi) {
     const int qq = q0 + qi;
@@ -429,23 +468,21 @@ __global__ void __launch_bounds__(AW * 32, 1)
   float* gbase = scratch + (size_t)ti * p.max_splits * QT * PST;
   /* CL: this split's partial stays in this CTA's shared memory, after the warp partials */
   float* cpart = part + (size_t)AW * QT * PST;
-  for (int it = tid; it < QT * (HD / 2); it += AW * 32) {
+  for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
     const int qi = it / (HD / 2), d2 = it % (HD / 2);
-    float M, L, ox, oy;
-    cta_merge_item<HD>(part, (size_t)QT * PST, qi, d2, M, L, ox, oy);
+    const float2 oo = merge_pair<HD>(part, (size_t)QT * PST, qi, d2, rowf[qi]);
     if (n_splits == 1) {
-      if (qi < nq) {
-        const float inv = L > 0.f ? 1.0f / L : 0.f;
-        out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
-      }
+      const float L = rowf[qi][1];
+      const float inv = L > 0.f ? 1.0f / L : 0.f;
+      out_ptr(qi)[d2] = __floats2half2_rn(oo.x * inv, oo.y * inv);
     } else {
       float* gp = (CL ? cpart : gbase + (size_t)split * QT * PST) + (size_t)qi * PST;
       if (d2 == 0) {
-        gp[0] = M;
-        gp[1] = L;
+        gp[0] = rowf[qi][0];
+        gp[1] = rowf[qi][1];
       }
-      gp[2 + 2 * d2] = ox;
-      gp[3 + 2 * d2] = oy;
+      gp[2 + 2 * d2] = oo.x;
+      gp[3 + 2 * d2] = oo.y;
     }
   }
   if (CL) {
@@ -455,24 +492,33 @@ __global__ void __launch_bounds__(AW * 32, 1)
        until it has */
     cluster_sync();
     if (split == 0 && n_splits > 1) {
-      for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
-        const int qi = it / (HD / 2), d2 = it % (HD / 2);
+      if (tid < nq) { /* the row's (max, sum) of every split, then the split-order merge */
+        const float* gp = cpart + (size_t)tid * PST;
         float mc[8], lc[8];
-        float2 oc[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u)
           if (u < n_splits) {
-            const float* gp = cpart + (size_t)qi * PST;
             mc[u] = ld_cluster(cluster_addr(gp, u));
             lc[u] = ld_cluster(cluster_addr(gp + 1, u));
-            oc[u] = ld_cluster2(cluster_addr(gp + 2 + 2 * d2, u));
           }
-        float M = -INFINITY, L = 0.f, ox = 0.f, oy = 0.f;
+        float M = -INFINITY, L = 0.f;
 #pragma unroll
         for (int u = 0; u < 8; ++u)
-          if (u < n_splits) merge_next(u == 0, mc[u], lc[u], oc[u].x, oc[u].y, M, L, ox, oy);
-        const float inv = L > 0.f ? 1.0f / L : 0.f;
-        out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
+          if (u < n_splits) sfac[tid][u] = merge_row(u == 0, mc[u], lc[u], M, L);
+        sinv[tid] = L > 0.f ? 1.0f / L : 0.f;
+      }
+      __syncthreads();
+      for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
+        const int qi = it / (HD / 2), d2 = it % (HD / 2);
+        float2 oc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (u < n_splits) oc[u] = ld_cluster2(cluster_addr(cpart + (size_t)qi * PST + 2 + 2 * d2, u));
+        float ox = 0.f, oy = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (u < n_splits) merge_pair_next(u == 0, sfac[qi][u], oc[u].x, oc[u].y, ox, oy);
+        out_ptr(qi)[d2] = __floats2half2_rn(ox * sinv[qi], oy * sinv[qi]);
       }
     }
     cluster_sync();
@@ -486,28 +532,40 @@ __global__ void __launch_bounds__(AW * 32, 1)
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  /* merge of the splits in split order, eight splits' loads per memory round trip: a thread
-     owns one (query, output pair) and loads the splits' (max, sum, output pair) together */
-  for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
-    const int qi = it / (HD / 2), d2 = it % (HD / 2);
-    float M = -INFINITY, L = 0.f, ox = 0.f, oy = 0.f;
+  /* merge of the splits in split order: each row's (max, sum) of every split and the factors
+     first, eight splits' loads per memory round trip, then a thread per (query, output pair) */
+  if (tid < nq) {
+    float M = -INFINITY, L = 0.f;
     for (int c0 = 0; c0 < n_splits; c0 += 8) {
       float mc[8], lc[8];
-      float2 oc[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
         if (c0 + u < n_splits) {
-          const float* gp = gbase + (size_t)(c0 + u) * QT * PST + (size_t)qi * PST;
+          const float* gp = gbase + (size_t)(c0 + u) * QT * PST + (size_t)tid * PST;
           mc[u] = __ldcg(gp);
           lc[u] = __ldcg(gp + 1);
-          oc[u] = __ldcg(reinterpret_cast<const float2*>(gp + 2) + d2);
         }
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (c0 + u < n_splits) merge_next(c0 + u == 0, mc[u], lc[u], oc[u].x, oc[u].y, M, L, ox, oy);
+        if (c0 + u < n_splits) sfac[tid][c0 + u] = merge_row(c0 + u == 0, mc[u], lc[u], M, L);
     }
-    const float inv = L > 0.f ? 1.0f / L : 0.f;
-    out_ptr(qi)[d2] = __floats2half2_rn(ox * inv, oy * inv);
+    sinv[tid] = L > 0.f ? 1.0f / L : 0.f;
+  }
+  __syncthreads();
+  for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
+    const int qi = it / (HD / 2), d2 = it % (HD / 2);
+    float ox = 0.f, oy = 0.f;
+    for (int c0 = 0; c0 < n_splits; c0 += 8) {
+      float2 oc[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + u < n_splits)
+          oc[u] = __ldcg(reinterpret_cast<const float2*>(gbase + (size_t)(c0 + u) * QT * PST + (size_t)qi * PST + 2) + d2);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + u < n_splits) merge_pair_next(c0 + u == 0, sfac[qi][c0 + u], oc[u].x, oc[u].y, ox, oy);
+    }
+    out_ptr(qi)[d2] = __floats2half2_rn(ox * sinv[qi], oy * sinv[qi]);
   }
   if (tid == 0) counters[ti] = 0; /* ready for the next launch / graph replay */
 }
@@ -518,9 +576,9 @@ __global__ void __launch_bounds__(AW * 32, 1)
  * exits between splits and the split partials never leave the SM.  Per split, warp (t, w)
  * scores tile t against 64-key block w exactly as attn_mma_kernel does (same staging, same
  * block arithmetic, same in-CTA merge), and each thread folds the split's partial of its
- * (query, output pair) items into a running merge in registers with merge_next, the
- * arithmetic of the other forms' split merges: a row gets the same bits from either kernel.
- * (A split past a tile's last position adds exact zeros to its merge.)
+ * (query, output pair) items into a running merge in registers with merge_row /
+ * merge_pair_next, the arithmetic of the other forms' split merges: a row gets the same bits
+ * from either kernel.  (A split past a tile's last position adds exact zeros to its merge.)
  * The warps of tile 0 stage each 64-key block once for all TT tiles; K and V are a pipeline:
  * the next split's keys are requested as soon as this split's scores are computed, its values
  * as soon as P.V is done, and the blocks of the split after that are prefetched into L2
@@ -619,8 +677,14 @@ __global__ void __launch_bounds__(TT * AW * 32, 1)
   uint32_t qh[KS][4], ql[KS][4];
   q_frags<HD>(qpa, qpb, va, vb, t, qh, ql);
 
-  /* the running merge of the splits' partials: thread items it = ttid + 128 j of its tile */
-  float RM[ITEMS], RL[ITEMS], RX[ITEMS], RY[ITEMS];
+  /* the running merge of the splits' partials: the row of thread ttid < nq keeps its (max,
+     sum) and leaves the split's factors in shared memory; thread items it = ttid + 128 j of
+     its tile keep their output pairs */
+  __shared__ float rowf[TT][QT][RF];
+  __shared__ MergeFac sfac[TT][QT];
+  __shared__ float sinv[TT][QT];
+  float RM = -INFINITY, RL = 0.f;
+  float RX[ITEMS], RY[ITEMS];
   for (int s = 0; s < n_splits; ++s) {
     float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
     float o[DN][4];
@@ -650,12 +714,18 @@ __global__ void __launch_bounds__(TT * AW * 32, 1)
     cp_commit();
     write_warp_partial<HD>(part + (size_t)bw * QT * PST, lane, mA, mB, lA, lB, o);
     __syncthreads();
+    if (ttid < nq) {
+      row_factors<HD>(part, (size_t)QT * PST, ttid, rowf[tw][ttid]);
+      sfac[tw][ttid] = merge_row(s == 0, rowf[tw][ttid][0], rowf[tw][ttid][1], RM, RL);
+    }
+    __syncthreads();
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
       const int it = ttid + j * AW * 32, qi = it / (HD / 2), d2 = it % (HD / 2);
-      float M, L, ox, oy;
-      cta_merge_item<HD>(part, (size_t)QT * PST, qi, d2, M, L, ox, oy);
-      merge_next(s == 0, M, L, ox, oy, RM[j], RL[j], RX[j], RY[j]);
+      if (qi < nq) {
+        const float2 oo = merge_pair<HD>(part, (size_t)QT * PST, qi, d2, rowf[tw][qi]);
+        merge_pair_next(s == 0, sfac[tw][qi], oo.x, oo.y, RX[j], RY[j]);
+      }
     }
     __syncthreads();
     kb0 = kb1;
@@ -663,11 +733,14 @@ __global__ void __launch_bounds__(TT * AW * 32, 1)
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   if (!live) return;
+  if (ttid < nq) sinv[tw][ttid] = RL > 0.f ? 1.0f / RL : 0.f;
+  /* the tile's own warps: a named barrier per tile (ids 1..4 are the block pairs') */
+  asm volatile("bar.sync %0, %1;" ::"r"(5 + tw), "r"(AW * 32) : "memory");
 #pragma unroll
   for (int j = 0; j < ITEMS; ++j) {
     const int it = ttid + j * AW * 32, qi = it / (HD / 2), d2 = it % (HD / 2);
     if (qi < nq) {
-      const float inv = RL[j] > 0.f ? 1.0f / RL[j] : 0.f;
+      const float inv = sinv[tw][qi];
       const int qq = q0 + qi;
       reinterpret_cast<__half2*>(out + (size_t)(m0 + qq / p.G) * p.H * HD + (kvh * p.G + qq % p.G) * HD)[d2] =
           __floats2half2_rn(RX[j] * inv, RY[j] * inv);

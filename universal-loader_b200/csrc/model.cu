@@ -135,18 +135,20 @@ __device__ __forceinline__ float embd_value(const uint8_t* __restrict__ row, int
   }
 }
 
+/* one thread per element: CTA (m, y) writes elements [256 y, 256 y + 256) of row m, so every
+   load of the row is in flight at once */
 __global__ void embed_kernel(const void* __restrict__ table, int table_type, size_t row_bytes, int d, int V,
                              const int* __restrict__ tokens, float* __restrict__ x, int* err) {
   pdl_wait();
   pdl_trigger();
-  const int m = blockIdx.x;
+  const int m = blockIdx.x, i = blockIdx.y * blockDim.x + threadIdx.x;
   int t = tokens[m];
   if (t < 0 || t >= V) {
-    if (threadIdx.x == 0) atomicOr(err, 1);
+    if (threadIdx.x == 0 && blockIdx.y == 0) atomicOr(err, 1);
     t = t < 0 ? 0 : V - 1;
   }
   const uint8_t* row = reinterpret_cast<const uint8_t*>(table) + (size_t)t * row_bytes;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) x[(size_t)m * d + i] = embd_value(row, table_type, i);
+  if (i < d) x[(size_t)m * d + i] = embd_value(row, table_type, i);
 }
 
 /* out[s] = fp16((x[row] * r) * g), r = 1 / sqrt(mean(x^2) + eps); row = s*sel + sel-1 if sel.
@@ -176,7 +178,8 @@ int launch_embed_t(Ctx* c, const void* table, int type, int d, int V, const int*
     default: break;
   }
   ULB_CHECK(row_bytes, ULB_EUNSUPPORTED, "embedding: table type %d with d=%d", type, d);
-  cudaError_t e = launch_k(c, embed_kernel, dim3(M), dim3(256), 0, table, type, row_bytes, d, V, tokens, x, err);
+  cudaError_t e = launch_k(c, embed_kernel, dim3(M, (d + 255) / 256), dim3(256), 0, table, type, row_bytes, d, V, tokens,
+                           x, err);
   if (e != cudaSuccess) return cuda_error(e, "embed launch", __FILE__, __LINE__);
   return ULB_OK;
 }

@@ -609,7 +609,11 @@ __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
   __shared__ float red[72];
   gemv_body<QT, NT, EPI, XS>(
       S, smem, wcnt, xzero,
-      [] {
+      [&] {
+        /* the norm weights are constant: on their way to L2 before the wait, so the
+           normalisation's second pass finds them there */
+        if (XS && threadIdx.x == 0 && ((uintptr_t)S.nin.g & 15) == 0)
+          prefetch_l2_bulk(S.nin.g, (uint32_t)S.sp.tiles * WTile<QT>::TK * sizeof(float));
         pdl_wait();
         pdl_trigger();
         return true;
