@@ -22,6 +22,8 @@ headline line:
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload c2|c4|c5] [--extras auto|none|c4|c5|c4,c5]
+  python bench.py --mode ops [--only CASE]     the config-3 kernel sweep
+  python bench.py --mode trace                 the CTA timeline of one C2 round
 """
 import argparse
 import json
@@ -883,6 +885,139 @@ def _rand_q4(rng, qt, N, K):
     return raw.reshape(N, -1)
 
 
+TRACE_UNITS = ("qgemv", "attention", "model", "sampling", "spec", "qgemm_tc", "runtime")
+TRACE_NAMES = {6000: "embed", 6100: "rmsnorm", 6200: "add", 7000: "sample", 7100: "stats", 7200: "accept",
+               7300: "tree_children", 7400: "tree_decide", 8000: "stage_draft", 8100: "stage_verify",
+               8200: "stage_prefill", 8300: "stage_tree_draft", 8301: "stage_tree_verify", 8350: "kv_tree_compact",
+               9000: "wait_flag"}
+
+
+def trace_kernel_name(tag, arg):
+    if 1000 <= tag < 2000:
+        epi = {0: "store", 1: "resid", 2: "swiglu", 3: "qkv"}.get((tag - 1000) // 100, "?")
+        return "qgemv_%s_N%d%s" % (epi, arg, "_rmsnorm" if tag % 10 else "")
+    if 2000 <= tag < 3000:
+        return "attn_split_hd%d%s%s" % (arg, "_cluster" if tag & 1 else "", "_tree" if tag & 2 else "")
+    if 3000 <= tag < 4000:
+        return "attn_stream_hd%d_tiles%d" % (arg, tag - 3000)
+    if 4000 <= tag < 5000:
+        return "qgemm_tc_epi%d_nt%d" % (tag - 4000, arg)
+    if 5000 <= tag < 6000:
+        return "rowgemv_N%d" % arg
+    return TRACE_NAMES.get(tag, str(tag))
+
+
+def trace_launches(rings):
+    """CTA records of every unit, within the window all busy rings still cover, grouped into
+    launches (consecutive entries of one kernel with distinct CTA indices)."""
+    import numpy as np
+    live = [r[r["t_entry"] > 0] for r in rings]
+    busy = [r for r in live if len(r) > 1000]
+    t_min = max(int(r["t_entry"].min()) for r in busy) if busy else 0
+    rec = np.concatenate(live)
+    rec = rec[rec["t_entry"] >= t_min]
+    rec = rec[np.argsort(rec["t_entry"], kind="stable")]
+    launches, cur, seen = [], None, set()
+    for x in rec:
+        key = (int(x["tag"]), int(x["arg"]), int(x["grid"]))
+        if cur is None or cur["key"] != key or int(x["cta"]) in seen or len(seen) >= key[2]:
+            cur, seen = {"key": key, "recs": []}, set()
+            launches.append(cur)
+        cur["recs"].append(x)
+        seen.add(int(x["cta"]))
+    out = []
+    for l in launches:
+        r = np.array(l["recs"], dtype=rec.dtype)
+        waits = r["t_wait"][r["t_wait"] > 0]
+        last = r[int(np.argmax(r["t_exit"]))]
+        out.append({"name": trace_kernel_name(*l["key"][:2]), "ctas": len(r), "entry": int(r["t_entry"].min()),
+                    "wait": int(waits.max()) if len(waits) else 0, "exit": int(r["t_exit"].max()),
+                    "last_marks": [int(m) - int(last["t_wait"]) if m and last["t_wait"] else None for m in last["mark"]]})
+    return out
+
+
+def run_trace(args):
+    """Timeline of one C2 round from the trace build (libulb_cuda_trace.so: every kernel's CTAs
+    record the global-timer times of their entry, of the return of their wait for the previous
+    kernel and of their exit, plus marks inside the GEMV and the per-split attention).  The
+    traced generation is the bench's C2 workload shortened to 64 tokens; its last complete
+    round is reported kernel by kernel: `exposed` = this launch's last CTA exit - the previous
+    launch's, `after_wait` = its last exit - its last wait, and the marks of the CTA that
+    exits last, relative to its own wait."""
+    import ctypes as C
+    import numpy as np
+    import build as pbuild
+    lib_path = pbuild.build_cuda(trace=True)
+    lib = C.CDLL(lib_path, mode=C.RTLD_GLOBAL)  # the Python module binds to it (same soname)
+    import vulkangguf as vg
+    maps = open("/proc/self/maps").read()
+    assert "/libulb_cuda.so" not in maps and "libulb_cuda_trace.so" in maps, "the trace build is not the one loaded"
+    rec_t = np.dtype([("tag", "<u4"), ("cta", "<u4"), ("grid", "<u4"), ("arg", "<u4"), ("t_entry", "<u8"),
+                      ("t_wait", "<u8"), ("t_exit", "<u8"), ("pad", "<u8"), ("mark", "<u8", (8,))])
+    cap = 1 << 18
+
+    def dump():
+        rings = []
+        for u in TRACE_UNITS:
+            buf = np.zeros(cap, rec_t)
+            n = C.c_uint(0)
+            rc = getattr(lib, "ulb_trace_dump_" + u)(buf.ctypes.data_as(C.c_void_p), C.byref(n))
+            assert rc == 0, (u, rc)
+            rings.append(buf)
+        return rings
+
+    tp, dp = ensure_models(0, lambda: None)
+    api = vg.InferenceAPI()
+    if not api.load_model(tp) or not api.load_draft_model(dp):
+        return 1
+    api.enable_speculative_decoding(True)
+    api.set_speculation_length(K_SPEC)
+    cfg = vg.GenerationConfig()
+    cfg.max_tokens = 64
+    cfg.temperature = 0.0
+    cfg.do_sample = False
+    prompt = prompt_for(0)
+    for _ in range(max(1, args.warmup)):
+        api.generate_tokens(prompt, cfg)
+    dump()
+    api.generate_tokens(prompt, cfg)
+    L = trace_launches(dump())
+    acc = [i for i, l in enumerate(L) if l["name"] == "accept"]
+    if len(acc) < 2:
+        print(json.dumps({"mode": "trace", "error": "fewer than two rounds in the trace"}))
+        return 1
+    a, b = acc[-2] + 1, acc[-1] + 1
+    rnd = L[a:b]
+    phase, prev, agg = "draft", L[a - 1]["exit"], {}
+    for l in rnd:
+        if l["name"] == "stage_verify":
+            phase = "verify"
+        if l["name"] == "accept":
+            phase = "accept"
+        exposed = (l["exit"] - prev) / 1e3
+        after = (l["exit"] - l["wait"]) / 1e3 if l["wait"] else 0.0
+        prev = l["exit"]
+        g = agg.setdefault((phase, l["name"]), {"phase": phase, "kernel": l["name"], "launches": 0, "ctas": l["ctas"],
+                                                "exposed_us": 0.0, "after_wait_us": 0.0, "marks": []})
+        g["launches"] += 1
+        g["exposed_us"] += exposed
+        g["after_wait_us"] += after
+        g["marks"].append(l["last_marks"])
+    kernels, phases = [], {}
+    for g in agg.values():
+        n = g["launches"]
+        mk = np.array([[np.nan if m is None else m / 1e3 for m in ms] for ms in g.pop("marks")])
+        means = [round(float(np.nanmean(mk[:, j])), 2) for j in range(8) if not np.all(np.isnan(mk[:, j]))]
+        g.update(exposed_us=round(g["exposed_us"], 1), mean_exposed_us=round(g["exposed_us"] / n, 2),
+                 mean_after_wait_us=round(g["after_wait_us"] / n, 2), last_cta_marks_after_wait_us=means)
+        phases[g["phase"]] = round(phases.get(g["phase"], 0.0) + g["exposed_us"], 1)
+        kernels.append(g)
+    print(json.dumps({"mode": "trace", "workload": "c2 round (k=5, T=0), 64-token generation after a 512-token prompt",
+                      "round_us": round((rnd[-1]["exit"] - L[a - 1]["exit"]) / 1e3, 1), "launches": len(rnd),
+                      "phases_us": phases, "kernels": kernels}), flush=True)
+    return 0
+
+
 def run_ops(args):
     """Config-3 op sweep on one GPU: fused Q4_0 / Q4_K dequant-GEMM for (N, K) in
     {(4096,4096), (11008,4096), (4096,11008)} x M in {1,5,8,16,64,256}, and the rejection
@@ -1031,8 +1166,9 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="spec", choices=["spec", "ops"],
-                    help="spec: the C2 speculative workload (default); ops: the config-3 kernel sweep")
+    ap.add_argument("--mode", default="spec", choices=["spec", "ops", "trace"],
+                    help="spec: the C2 speculative workload (default); ops: the config-3 kernel sweep; "
+                         "trace: the CTA timeline of one C2 round (trace build)")
     ap.add_argument("--only", default="", help="ops mode: run one case, e.g. q4_0:11008x4096:m5 or accept")
     ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5", "pgtest"],
                     help="c2: 7B + TinyLlama, B=1 (default, the headline); c4: Llama-3-8B + 3.2-1B, 64 sequences "
@@ -1048,6 +1184,8 @@ def main():
         return run_reference(args)
     if args.mode == "ops":
         return run_ops(args)
+    if args.mode == "trace":
+        return run_trace(args)
     if args.workload == "pgtest":
         return run_pgtest(args)
     if args.workload == "c4":

@@ -167,3 +167,23 @@ def test_gguf_with_overflowing_tensor_info_rejected(tmp_path, tiny_draft, field,
     import vulkangguf as vg
     api = vg.InferenceAPI()
     assert api.load_model(str(bad)) is False
+
+
+def test_trace_build_exports_its_dump_functions_and_the_product_build_none():
+    """The CTA timeline trace is compiled into libulb_cuda_trace.so only (bench.py --mode trace
+    reads one ring per translation unit); both builds carry the soname the Python module binds."""
+    import subprocess
+    import bench
+    import build as pbuild
+    pbuild.build_cuda(trace=True)
+
+    def dyn_symbols(path):
+        out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
+        return {line.split()[-1] for line in out.splitlines() if line.strip()}
+
+    tr = dyn_symbols(pbuild.CUDA_LIB_TRACE)
+    assert {"ulb_trace_dump_" + u for u in bench.TRACE_UNITS} <= tr
+    assert not {n for n in dyn_symbols(pbuild.CUDA_LIB) if n.startswith("ulb_trace_")}
+    for path in (pbuild.CUDA_LIB, pbuild.CUDA_LIB_TRACE):
+        dyn = subprocess.run(["readelf", "-d", path], capture_output=True, text=True, check=True).stdout
+        assert "Library soname: [libulb_cuda.so]" in dyn

@@ -22,6 +22,8 @@ CUDA_HOME = os.path.dirname(os.path.dirname(NVCC))
 
 CU_SOURCES = ["runtime.cu", "qgemv.cu", "qgemm_tc.cu", "attention.cu", "sampling.cu", "model.cu", "spec.cu"]
 CUDA_LIB = os.path.join(PKG, "libulb_cuda.so")
+BUILD_TRACE = os.path.join(PKG, "_build_trace")
+CUDA_LIB_TRACE = os.path.join(PKG, "libulb_cuda_trace.so")
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
               "-I" + INCLUDE, "-I" + CSRC]
@@ -46,27 +48,33 @@ def _run(cmd):
     return r.stdout + r.stderr
 
 
-def build_cuda(verbose=False):
-    os.makedirs(BUILD, exist_ok=True)
+def build_cuda(verbose=False, trace=False):
+    """libulb_cuda.so; trace=True: libulb_cuda_trace.so, the same sources with the CTA timeline
+    trace compiled in (-DULB_TRACE), under the same soname so the Python module binds to it
+    when it is loaded first (bench.py --mode trace)."""
+    bdir = BUILD_TRACE if trace else BUILD
+    lib_path = CUDA_LIB_TRACE if trace else CUDA_LIB
+    os.makedirs(bdir, exist_ok=True)
     hdrs = _headers()
     jobs = []
     objs = []
     for src in CU_SOURCES:
         s = os.path.join(CSRC, src)
-        o = os.path.join(BUILD, src + ".o")
+        o = os.path.join(bdir, src + ".o")
         objs.append(o)
         if _newer(o, [s] + hdrs):
-            extra = ["-Xptxas", "-v"] if verbose else []
+            extra = (["-Xptxas", "-v"] if verbose else []) + (["-DULB_TRACE"] if trace else [])
             jobs.append(([NVCC] + NVCC_FLAGS + extra + ["-c", s, "-o", o], src))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         for out, (cmd, src) in zip(ex.map(lambda j: _run(j[0]), jobs), jobs):
             if verbose and out.strip():
                 print("== %s\n%s" % (src, out))
-    if _newer(CUDA_LIB, objs):
-        tmp = CUDA_LIB + ".tmp"
-        _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", tmp] + objs + ["-lnccl"])
-        os.replace(tmp, CUDA_LIB)
-    return CUDA_LIB
+    if _newer(lib_path, objs):
+        tmp = lib_path + ".tmp"
+        _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-Xlinker", "-soname=libulb_cuda.so",
+              "-o", tmp] + objs + ["-lnccl"])
+        os.replace(tmp, lib_path)
+    return lib_path
 
 
 def pybind_module_path():
@@ -92,8 +100,10 @@ def build_engine():
     return out
 
 
-def build(verbose=False):
+def build(verbose=False, trace=True):
     lib = build_cuda(verbose=verbose)
+    if trace:
+        build_cuda(trace=True)
     mod = None
     if os.path.isdir(ENGINE) and any(f.endswith(".cpp") for f in os.listdir(ENGINE)):
         mod = build_engine()

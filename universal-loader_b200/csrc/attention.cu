@@ -102,21 +102,14 @@ __device__ __forceinline__ int swz(int j, int c) { return c ^ (j & 7); }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-/* a float (pair) of the shared memory of CTA `rank` of the cluster, at this CTA's offset p */
+/* the address in the shared memory of CTA `rank` of the cluster at this CTA's offset p */
 __device__ __forceinline__ uint32_t cluster_addr(const void* p, int rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr(p)), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float ld_cluster(uint32_t a) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
-  return v;
-}
-__device__ __forceinline__ float2 ld_cluster2(uint32_t a) {
-  float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a) : "memory");
-  return v;
+__device__ __forceinline__ void st_cluster2(uint32_t a, float2 v) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(v.x), "f"(v.y) : "memory");
 }
 
 /*
@@ -349,6 +342,7 @@ __global__ void __launch_bounds__(AW * 32, 1)
     attn_mma_kernel(AttnParams p, const float* __restrict__ q, const __half* __restrict__ kc,
                     const __half* __restrict__ vc, const int* __restrict__ row_seq, const int* __restrict__ row_pos,
                     __half* __restrict__ out, float* scratch, int* counters) {
+  ULB_TRACE_KERNEL(kTrAttnSplit + (CL ? 1 : 0) + (TREE ? 2 : 0), HD);
   constexpr int KS = HD / 16; /* k-steps of Q.K^T */
   constexpr int DN = HD / 8;  /* n-tiles of the output */
   constexpr int PST = HD + 2; /* floats per query of a partial: m, l, o[HD] */
@@ -393,11 +387,8 @@ __global__ void __launch_bounds__(AW * 32, 1)
   /* n_splits and seq are the same for every CTA of a cluster */
   const bool live = split < n_splits && (unsigned)seq < (unsigned)p.n_seq;
   if (!live) {
-    /* a cluster's CTAs all pass its two barriers (see the end of the kernel) */
-    if (CL) {
-      cluster_sync();
-      cluster_sync();
-    }
+    /* a cluster's CTAs all pass its barrier (see the end of the kernel) */
+    if (CL) cluster_sync();
     return;
   }
 
@@ -440,14 +431,17 @@ __global__ void __launch_bounds__(AW * 32, 1)
   const float* qpb = q + (size_t)(m0 + (vb ? qb : q0) / p.G) * p.ldq + (kvh * p.G + (vb ? qb : q0) % p.G) * HD;
   uint32_t qh[KS][4], ql[KS][4];
   q_frags<HD>(qpa, qpb, va, vb, t, qh, ql);
+  ULB_TRACE_MARK(0);
 
   if (nk > 0) {
     cp_wait_all();
     __syncwarp();
+    ULB_TRACE_MARK(1);
     float s[8][4];
     score_block<HD, TREE>(Ks, qh, ql, kb0, pa, pb, p.scale2, lane, s, mA, mB, lA, lB, prA, prB, mkA, mkB);
     pv_block<HD>(Vs, s, lane, o);
   }
+  ULB_TRACE_MARK(2);
 
   /* merge the 4 warp blocks (shared memory, warp order): each row's factors once, then its
      output pairs; rows past the tile's queries are never merged */
@@ -466,8 +460,10 @@ __global__ void __launch_bounds__(AW * 32, 1)
   };
   const int ti = (gi * p.n_mt + mt) * p.Hkv + kvh;
   float* gbase = scratch + (size_t)ti * p.max_splits * QT * PST;
-  /* CL: this split's partial stays in this CTA's shared memory, after the warp partials */
-  float* cpart = part + (size_t)AW * QT * PST;
+  /* CL: the cluster's split partials [8][QT][PST] in split 0's shared memory, after its K / V
+     staging and warp partials (which split 0 may still be using when the others write) */
+  float* cslots = reinterpret_cast<float*>(sm + std::max((size_t)AW * 2 * KB * HD * sizeof(__half),
+                                                         (size_t)AW * QT * PST * sizeof(float)));
   for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
     const int qi = it / (HD / 2), d2 = it % (HD / 2);
     const float2 oo = merge_pair<HD>(part, (size_t)QT * PST, qi, d2, rowf[qi]);
@@ -475,8 +471,18 @@ __global__ void __launch_bounds__(AW * 32, 1)
       const float L = rowf[qi][1];
       const float inv = L > 0.f ? 1.0f / L : 0.f;
       out_ptr(qi)[d2] = __floats2half2_rn(oo.x * inv, oo.y * inv);
+    } else if (CL) {
+      /* into split 0's slot of this split: local, or a store to distributed shared memory */
+      float* gp = cslots + ((size_t)split * QT + qi) * PST;
+      if (split == 0) {
+        if (d2 == 0) *reinterpret_cast<float2*>(gp) = make_float2(rowf[qi][0], rowf[qi][1]);
+        *reinterpret_cast<float2*>(gp + 2 + 2 * d2) = oo;
+      } else {
+        if (d2 == 0) st_cluster2(cluster_addr(gp, 0), make_float2(rowf[qi][0], rowf[qi][1]));
+        st_cluster2(cluster_addr(gp + 2 + 2 * d2, 0), oo);
+      }
     } else {
-      float* gp = (CL ? cpart : gbase + (size_t)split * QT * PST) + (size_t)qi * PST;
+      float* gp = gbase + (size_t)split * QT * PST + (size_t)qi * PST;
       if (d2 == 0) {
         gp[0] = rowf[qi][0];
         gp[1] = rowf[qi][1];
@@ -485,43 +491,43 @@ __global__ void __launch_bounds__(AW * 32, 1)
       gp[3 + 2 * d2] = oo.y;
     }
   }
+  ULB_TRACE_MARK(3);
   if (CL) {
-    /* the splits' partials merge through distributed shared memory: once every CTA of the
-       cluster has written its partial, split 0 reads them in split order (the arithmetic of
-       the global merge below), and the second barrier keeps the others' shared memory alive
-       until it has */
+    /* one cluster barrier: every CTA has written its split partial into split 0's shared
+       memory (release / acquire), after which no CTA's shared memory is read by another, so
+       the others exit and split 0 merges the partials in split order (the arithmetic of the
+       global merge below) */
     cluster_sync();
-    if (split == 0 && n_splits > 1) {
-      if (tid < nq) { /* the row's (max, sum) of every split, then the split-order merge */
-        const float* gp = cpart + (size_t)tid * PST;
-        float mc[8], lc[8];
+    ULB_TRACE_MARK(4);
+    if (split != 0 || n_splits == 1) return;
+    if (tid < nq) { /* the row's (max, sum) of every split, then the split-order merge */
+      float mc[8], lc[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (u < n_splits) {
-            mc[u] = ld_cluster(cluster_addr(gp, u));
-            lc[u] = ld_cluster(cluster_addr(gp + 1, u));
-          }
-        float M = -INFINITY, L = 0.f;
+      for (int u = 0; u < 8; ++u)
+        if (u < n_splits) {
+          const float2 ml = *reinterpret_cast<const float2*>(cslots + ((size_t)u * QT + tid) * PST);
+          mc[u] = ml.x;
+          lc[u] = ml.y;
+        }
+      float M = -INFINITY, L = 0.f;
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (u < n_splits) sfac[tid][u] = merge_row(u == 0, mc[u], lc[u], M, L);
-        sinv[tid] = L > 0.f ? 1.0f / L : 0.f;
-      }
-      __syncthreads();
-      for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
-        const int qi = it / (HD / 2), d2 = it % (HD / 2);
-        float2 oc[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (u < n_splits) oc[u] = ld_cluster2(cluster_addr(cpart + (size_t)qi * PST + 2 + 2 * d2, u));
-        float ox = 0.f, oy = 0.f;
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (u < n_splits) merge_pair_next(u == 0, sfac[qi][u], oc[u].x, oc[u].y, ox, oy);
-        out_ptr(qi)[d2] = __floats2half2_rn(ox * sinv[qi], oy * sinv[qi]);
-      }
+      for (int u = 0; u < 8; ++u)
+        if (u < n_splits) sfac[tid][u] = merge_row(u == 0, mc[u], lc[u], M, L);
+      sinv[tid] = L > 0.f ? 1.0f / L : 0.f;
     }
-    cluster_sync();
+    __syncthreads();
+    for (int it = tid; it < nq * (HD / 2); it += AW * 32) {
+      const int qi = it / (HD / 2), d2 = it % (HD / 2);
+      float2 oc[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (u < n_splits) oc[u] = *reinterpret_cast<const float2*>(cslots + ((size_t)u * QT + qi) * PST + 2 + 2 * d2);
+      float ox = 0.f, oy = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (u < n_splits) merge_pair_next(u == 0, sfac[qi][u], oc[u].x, oc[u].y, ox, oy);
+      out_ptr(qi)[d2] = __floats2half2_rn(ox * sinv[qi], oy * sinv[qi]);
+    }
     return;
   }
   if (n_splits == 1) return;
@@ -581,9 +587,9 @@ __global__ void __launch_bounds__(AW * 32, 1)
  * from either kernel.  (A split past a tile's last position adds exact zeros to its merge.)
  * The warps of tile 0 stage each 64-key block once for all TT tiles; K and V are a pipeline:
  * the next split's keys are requested as soon as this split's scores are computed, its values
- * as soon as P.V is done, and the blocks of the split after that are prefetched into L2
- * (cp.async.bulk.prefetch), so HBM keeps streaming while the SM computes.  The warps sharing a
- * block meet on a named barrier of their own.  Shared memory: K [4][64][HD] | V [4][64][HD] |
+ * as soon as P.V is done, so HBM keeps streaming while the SM computes.  (An L2 prefetch of
+ * the split after that was measured slower: a bulk prefetch holds its warp while it issues.)
+ * The warps sharing a block meet on a named barrier of their own.  Shared memory: K [4][64][HD] | V [4][64][HD] |
  * warp partials [TT][4][16][HD + 2].  No scratch, no counters.
  */
 template <int HD, int TT>
@@ -591,6 +597,7 @@ __global__ void __launch_bounds__(TT * AW * 32, 1)
     attn_stream_kernel(AttnParams p, const float* __restrict__ q, const __half* __restrict__ kc,
                        const __half* __restrict__ vc, const int* __restrict__ row_seq,
                        const int* __restrict__ row_pos, __half* __restrict__ out) {
+  ULB_TRACE_KERNEL(kTrAttnStream + TT, HD);
   constexpr int KS = HD / 16, DN = HD / 8, PST = HD + 2;
   constexpr int ITEMS = QT * (HD / 2) / (AW * 32); /* (query, output pair) items per thread of a tile */
   extern __shared__ __align__(128) uint8_t sm[];
@@ -642,17 +649,6 @@ __global__ void __launch_bounds__(TT * AW * 32, 1)
     }
     nk = page_ok ? min(KB, last_pos + 1 - kb0) : 0;
   };
-  /* the K / V rows of block bw of split s on their way to L2 */
-  auto prefetch = [&](int s) {
-    if (s >= n_splits || lane != 0 || !stager) return;
-    int kb, n;
-    size_t off;
-    block_of(s, kb, off, n);
-    if (n <= 0) return;
-    const uint32_t bytes = (uint32_t)n * HD * sizeof(__half);
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kc + off), "r"(bytes) : "memory");
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vc + off), "r"(bytes) : "memory");
-  };
   int kb0, nk;
   size_t kvoff;
   block_of(0, kb0, kvoff, nk);
@@ -663,7 +659,6 @@ __global__ void __launch_bounds__(TT * AW * 32, 1)
       stage_rows<HD>(Ks, kc + kvoff, nk, 0, n_old, lane);
       stage_rows<HD>(Vs, vc + kvoff, nk, 0, n_old, lane);
     }
-    prefetch(1); /* a hint into L2, the point of coherence: rows still to be written may go too */
     pdl_wait();
     pdl_trigger();
     if (stager && nk > 0) {
@@ -705,7 +700,6 @@ __global__ void __launch_bounds__(TT * AW * 32, 1)
       if (stager && nk1 > 0) stage_rows<HD>(Ks, kc + kvoff1, nk1, 0, KB, lane);
     }
     cp_commit();
-    prefetch(s + 2);
     asm volatile("cp.async.wait_group 1;" ::: "memory"); /* V_s */
     pair_sync();
     if (live && nk > 0) pv_block<HD>(Vs, sc, lane, o);
@@ -763,10 +757,12 @@ void attn_geometry(const ulb_attn_desc* d, int M, int rps, int max_pos, AttnPara
   p->n_groups = *n_groups;
 }
 
-size_t attn_smem(int hd) {
+/* per-split form: K / V staging, the warp partials over it; with a cluster merge (cl) the
+   cluster's split partials after both, written there by every CTA of the cluster */
+size_t attn_smem(int hd, bool cl) {
   const size_t kv = (size_t)AW * 2 * KB * hd * sizeof(__half);
-  const size_t part = (size_t)(AW + 1) * QT * (hd + 2) * sizeof(float); /* warp partials + the split's */
-  return std::max(kv, part);
+  const size_t part = (size_t)AW * QT * (hd + 2) * sizeof(float);
+  return std::max(kv, part) + (cl ? (size_t)8 * QT * (hd + 2) * sizeof(float) : 0);
 }
 /* streaming form: K / V blocks of the 4 warp columns + the partials of TT tiles' warps */
 size_t attn_stream_smem(int hd, int tt) {
@@ -810,21 +806,21 @@ cudaError_t attn_setup(const bool** cl_ok_out) {
   static bool cl_ok[9] = {false}; /* max_splits -> cluster form schedulable */
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)attn_smem(HD));
+                                    (int)attn_smem(HD, false));
     if (attr_err == cudaSuccess)
       attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)attn_smem(HD));
+                                      (int)attn_smem(HD, true));
     if (attr_err == cudaSuccess)
       attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)attn_smem(HD));
+                                      (int)attn_smem(HD, false));
     if (attr_err == cudaSuccess)
       attr_err = cudaFuncSetAttribute(attn_mma_kernel<HD, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)attn_smem(HD));
+                                      (int)attn_smem(HD, true));
     for (int s = 2; s <= 8 && attr_err == cudaSuccess; ++s) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(1, 1, s);
       cfg.blockDim = dim3(AW * 32);
-      cfg.dynamicSmemBytes = attn_smem(HD);
+      cfg.dynamicSmemBytes = attn_smem(HD, true);
       cudaLaunchAttribute a[1];
       a[0].id = cudaLaunchAttributeClusterDimension;
       a[0].val.clusterDim.x = 1;
@@ -876,7 +872,7 @@ cudaError_t launch_attn(Ctx* c, const AttnParams& p, int ng, const float* q, con
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_mt, p.Hkv, ng * p.max_splits);
   cfg.blockDim = dim3(AW * 32);
-  cfg.dynamicSmemBytes = attn_smem(HD);
+  cfg.dynamicSmemBytes = attn_smem(HD, cl);
   cfg.stream = c->stream;
   cudaLaunchAttribute a[2];
   a[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1097,3 +1093,5 @@ extern "C" int ulb_attention(ulb_ctx* ctx, const ulb_attn_desc* d, const float* 
   dev_free(c, scratch, nf * sizeof(float));
   return rc;
 }
+
+ULB_TRACE_UNIT(attention)

@@ -139,6 +139,7 @@ __device__ __forceinline__ float embd_value(const uint8_t* __restrict__ row, int
    load of the row is in flight at once */
 __global__ void embed_kernel(const void* __restrict__ table, int table_type, size_t row_bytes, int d, int V,
                              const int* __restrict__ tokens, float* __restrict__ x, int* err) {
+  ULB_TRACE_KERNEL(kTrEmbed, d);
   pdl_wait();
   pdl_trigger();
   const int m = blockIdx.x, i = blockIdx.y * blockDim.x + threadIdx.x;
@@ -155,6 +156,7 @@ __global__ void embed_kernel(const void* __restrict__ table, int table_type, siz
    256 threads (rms_row_256). */
 __global__ void rmsnorm_kernel(const float* __restrict__ x, int ldx, const float* __restrict__ g, int d, float eps,
                                int sel, __half* __restrict__ out, int ldo) {
+  ULB_TRACE_KERNEL(kTrRmsnorm, d);
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
@@ -251,6 +253,7 @@ int model_prepare(Model* m, KV* kv, int M, int rps, bool tree) {
 
 /* x += part, elementwise (the residual add after a tensor-parallel all-reduce) */
 __global__ void add_inplace_kernel(float* __restrict__ x, const float* __restrict__ part, size_t n) {
+  ULB_TRACE_KERNEL(kTrAdd, 0);
   pdl_wait();
   pdl_trigger();
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
@@ -291,6 +294,7 @@ static int forward_head(Model* m, int M, int rps, int logits_mode, float* logits
 __global__ void kv_tree_compact_kernel(__half* __restrict__ kc, __half* __restrict__ vc, size_t layer_elems, int Hkv,
                                        int hd, int cap, const int* __restrict__ bt, int max_pages,
                                        const int32_t* __restrict__ comp, int D) {
+  ULB_TRACE_KERNEL(kTrStageTree + 50, 0);
   pdl_wait();
   pdl_trigger();
   const int l = blockIdx.x, s = blockIdx.y;
@@ -357,17 +361,6 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     a.row_seq = seq; a.row_pos = pos; a.rope = kv->rope;
     a.bt = kv->identity ? nullptr : kv->bt; a.max_pages = kv->max_pages;
     a.row_rope = tree ? tree->rope : nullptr;
-    /* GEMV tails prefetch the weights of the GEMVs to come into L2 (the hint is set just
-       before the launch whose tail issues it) */
-    auto hint = [c](const Tensor* t, const Tensor* t2 = nullptr) {
-      c->pf_ptr = t ? t->dev : nullptr;
-      c->pf_bytes = t ? t->bytes : 0;
-      c->pf2_ptr = t2 ? t2->dev : nullptr;
-      c->pf2_bytes = t2 ? t2->bytes : 0;
-    };
-    /* the QKV GEMV's tail prefetches attn_output and ffn_gate_up, which land in L2 while the
-       attention kernel (which reads only the KV cache) leaves HBM mostly idle */
-    hint(&L.o, &L.gateup);
     if (L.v.dev) { /* V as GGUF rows: the normalised rows in x16 feed the Q / K GEMV and V's row GEMV */
       ULB_TRY(launch_rmsnorm_sel(c, m->x, d.d_model, L.attn_norm, M, d.d_model, d.rms_eps, 0, m->x16, d.d_model));
       ULB_TRY(launch_qgemv(c, &L.qkv, m->x16, M, d.d_model, EPI_QKV, a));
@@ -385,14 +378,11 @@ int model_forward(Model* m, KV* kv, int M, int rps, const int* tok, const int* s
     EpiArgs pr;
     pr.y = m->tp_part; pr.ldy = d.d_model;
     const bool tp = m->tp_world > 1;
-    hint(&L.down);
     ULB_TRY(launch_qgemv(c, &L.o, m->att, M, m->nq, tp ? EPI_STORE : EPI_RESID, tp ? pr : r));
     if (tp) ULB_TRY(tp_reduce_add(m, M));
     EpiArgs s;
     s.h = m->h16; s.ldh = d.d_ff;
-    hint(l + 1 < d.n_layer ? &m->layers[l + 1].qkv : &m->out);
     ULB_TRY(launch_qgemv_rms(c, &L.gateup, m->x, d.d_model, L.ffn_norm, d.rms_eps, m->x16, M, EPI_SWIGLU, s));
-    hint(nullptr);
     ULB_TRY(launch_qgemv(c, &L.down, m->h16, M, d.d_ff, tp ? EPI_STORE : EPI_RESID, tp ? pr : r));
     if (tp) ULB_TRY(tp_reduce_add(m, M));
   }
@@ -931,3 +921,5 @@ int ulb_model_forward(ulb_ctx* ctx, ulb_model* mm, ulb_kv* kvh, int M, int rps, 
 }
 
 }  // extern "C"
+
+ULB_TRACE_UNIT(model)

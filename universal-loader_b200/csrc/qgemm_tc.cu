@@ -213,6 +213,7 @@ template <int QT, int NT, int EPI>
 __global__ void __launch_bounds__(TCW * 32, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, TcArgs a,
                     EpiArgs ea) {
+  ULB_TRACE_KERNEL(kTrGemmTc + EPI, NT);
   using C = TcCfg<QT, NT>;
   constexpr int TB = C::TB;
   constexpr int TK = QT == ULB_TYPE_Q4_0 ? kQ40TileK : kQ4KTileK; /* k per packed tile */
@@ -601,3 +602,5 @@ int launch_qgemm_tc(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, in
 }
 
 }  // namespace ulb
+
+ULB_TRACE_UNIT(qgemm_tc)

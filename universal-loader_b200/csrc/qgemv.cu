@@ -24,9 +24,6 @@
  *    on (N, K, SM count) only, so a row's arithmetic never depends on M;
  *  - the fused epilogues write RoPE'd Q / K / V (K and V straight into the fp16 KV cache),
  *    SiLU(gate)*up in fp16, or the fp32 residual add;
- *  - a GEMV's tail prefetches the weights of GEMVs to come into L2 (up to two ranges the
- *    forward pass names), e.g. the QKV GEMV's tail brings attn_output and ffn_gate_up in while
- *    the attention kernel leaves HBM mostly idle;
  *  - Q8_0 / Q6_K matrices (LM heads of llama.cpp files) stay in GGUF rows and run through
  *    rowgemv_kernel, one warp per output row.
  * The tensor pipe is idle in this regime (<= 3.6 flop/B at M = 1); mma.sync is used as the
@@ -38,9 +35,6 @@ namespace ulb {
 
 namespace {
 
-__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 
 __device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
   uint32_t r;
@@ -356,11 +350,6 @@ struct GemvStep {
   int ldx = 0;
   NormIn nin;
   EpiArgs ea;
-  /* weights of the GEMVs to come (one or two ranges): prefetched into L2 from the tail */
-  const uint8_t* pf = nullptr;
-  uint32_t pf_bytes = 0;
-  const uint8_t* pf2 = nullptr;
-  uint32_t pf2_bytes = 0;
 };
 
 /* shared-memory layout of a GEMV CTA: warp partials | normalised activations (fp16 [M][K]) */
@@ -470,7 +459,6 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
   const uint32_t c = blockIdx.x;
   const uint32_t c0 = cta_begin(sp, c), c1 = cta_begin(sp, c + 1), tc = c1 - c0;
   uint32_t a = 0, b = 0;
-  const uint32_t u = c * sp.Wn + warp; /* working-warp index (when warp < Wn) */
   if ((uint32_t)warp < sp.Wn) {
     a = warp_begin(c0, tc, sp.Wn, warp);
     b = warp_begin(c0, tc, sp.Wn, warp + 1);
@@ -486,6 +474,7 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
   if (tid < W) wcnt[tid] = 0;
   if (!sync()) return;
   const XIn xin = prep();
+  ULB_TRACE_MARK(0);
   if (n == 0) return;
   const __half* xr[NT];
   /* tokens >= M only feed MMA columns the epilogue drops: in shared memory they may read row 0 */
@@ -581,20 +570,7 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
       ULB_GEMV_NEXT(u, j + u)
     }
 #undef ULB_GEMV_NEXT
-  if ((S.pf_bytes | S.pf2_bytes) && lane == 0) {
-    /* this warp's loads are all issued: start the weights of the kernels to come on their way
-       to L2, an equal share of the two ranges (back to back) per warp, so HBM stays busy
-       through this kernel's tail and what follows it */
-    const uint64_t nw = (uint64_t)sp.G * sp.Wn, tot = (uint64_t)S.pf_bytes + S.pf2_bytes;
-    const uint64_t lo = tot * u / nw & ~15ull, hi = tot * (u + 1) / nw & ~15ull;
-    for (uint64_t o = lo; o < hi;) {
-      const bool first = o < S.pf_bytes;
-      const uint64_t end = first && hi > S.pf_bytes ? S.pf_bytes : hi;
-      const uint32_t len = end - o < 32768 ? (uint32_t)(end - o) : 32768u;
-      prefetch_l2_bulk(first ? S.pf + o : S.pf2 + (o - S.pf_bytes), len);
-      o += len;
-    }
-  }
+  ULB_TRACE_MARK(1);
   if (kt != 0) flush(s); /* the range ends inside strip s */
 }
 
@@ -604,16 +580,13 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
 template <int QT, int NT, int EPI, bool XS>
 __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
     qgemv_kernel(GemvStep S, const __half* __restrict__ xzero) {
+  ULB_TRACE_KERNEL(kTrGemv + EPI * 100 + NT * 10 + (XS ? 1 : 0), S.N);
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t wcnt[GemvCfg<QT, NT>::W];
   __shared__ float red[72];
   gemv_body<QT, NT, EPI, XS>(
       S, smem, wcnt, xzero,
-      [&] {
-        /* the norm weights are constant: on their way to L2 before the wait, so the
-           normalisation's second pass finds them there */
-        if (XS && threadIdx.x == 0 && ((uintptr_t)S.nin.g & 15) == 0)
-          prefetch_l2_bulk(S.nin.g, (uint32_t)S.sp.tiles * WTile<QT>::TK * sizeof(float));
+      [] {
         pdl_wait();
         pdl_trigger();
         return true;
@@ -638,6 +611,7 @@ __global__ void __launch_bounds__(GemvCfg<QT, NT>::W * 32, 1)
 template <int QT, int EPI>
 __global__ void __launch_bounds__(256) rowgemv_kernel(const uint8_t* __restrict__ w, int N, int K,
                                                       const __half* __restrict__ x, int ldx, int M, EpiArgs e) {
+  ULB_TRACE_KERNEL(kTrRowGemv + EPI, N);
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
@@ -899,13 +873,6 @@ static int make_split(Ctx* c, const Tensor* w, Split* sp) {
   return ULB_OK;
 }
 
-/* the next-GEMV prefetch hint of the context, as kernel arguments */
-static void take_hint(Ctx* c, GemvStep* S) {
-  S->pf = (const uint8_t*)c->pf_ptr;
-  S->pf_bytes = c->pf_ptr ? (uint32_t)(std::min<size_t>(c->pf_bytes, kPrefetchMaxBytes) & ~(size_t)15) : 0u;
-  S->pf2 = (const uint8_t*)c->pf2_ptr;
-  S->pf2_bytes = c->pf2_ptr ? (uint32_t)(std::min<size_t>(c->pf2_bytes, kPrefetchMaxBytes) & ~(size_t)15) : 0u;
-}
 
 /* shared memory of the normalised activation rows: M x K fp16 */
 static size_t norm_bytes(int M, int K) { return ((size_t)M * K * sizeof(__half) + 15) / 16 * 16; }
@@ -922,7 +889,6 @@ int launch_q(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, const Epi
   S.ldx = ldx;
   S.nin = nin;
   S.ea = a;
-  take_hint(c, &S);
   const size_t smem = warp_part_bytes<QT, NT>() + (XS ? norm_bytes(M, w->K) : 0);
   ULB_CHECK(smem <= kGemvSmemBytes, ULB_EUNSUPPORTED, "qgemv: %d normalised rows of %d", M, w->K);
   static bool attr_set = false;
@@ -958,10 +924,7 @@ static int max_rows_per_launch(int) { return kGemvMaxRows; }
 static int launch_qgemv_impl(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0);
 
 int launch_qgemv(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
-  const int rc = launch_qgemv_impl(c, w, x, M, ldx, epi, a0);
-  c->pf_ptr = c->pf2_ptr = nullptr; /* the prefetch hint is for the launch that follows it only */
-  c->pf_bytes = c->pf2_bytes = 0;
-  return rc;
+  return launch_qgemv_impl(c, w, x, M, ldx, epi, a0);
 }
 
 static int launch_qgemv_impl(Ctx* c, const Tensor* w, const __half* x, int M, int ldx, int epi, const EpiArgs& a0) {
@@ -1024,8 +987,6 @@ int launch_qgemv_rms(Ctx* c, const Tensor* w, const float* x32, int ldx32, const
   else
     rc = q40 ? launch_q<ULB_TYPE_Q4_0, 1, EPI_STORE, true>(c, w, nullptr, M, w->K, a, nin)
              : launch_q<ULB_TYPE_Q4_K, 1, EPI_STORE, true>(c, w, nullptr, M, w->K, a, nin);
-  c->pf_ptr = c->pf2_ptr = nullptr;
-  c->pf_bytes = c->pf2_bytes = 0;
   return rc;
 }
 
@@ -1073,3 +1034,5 @@ int repack_q4(Ctx* c, int type, const void* dev_raw, int raw_rows, int K, const 
 }
 
 }  // namespace ulb
+
+ULB_TRACE_UNIT(qgemv)

@@ -63,6 +63,7 @@ void dev_free(Ctx* c, void* p, size_t bytes) {
    on the timeout it raises bit 4 of the device error word and returns (nothing is left in
    flight: the wait is a plain load loop) */
 __global__ void wait_flag_kernel(const int* flag, int value, unsigned long long timeout_ns, int* err) {
+  ULB_TRACE_KERNEL(kTrWaitFlag, 0);
   pdl_wait();
   if (threadIdx.x != 0) return;
   unsigned long long t0, t;
@@ -454,3 +455,5 @@ int ulb_qgemm(ulb_ctx* ctx, const ulb_tensor* w, const uint16_t* x, int M, float
 }
 
 }  // extern "C"
+
+ULB_TRACE_UNIT(runtime)

@@ -454,6 +454,7 @@ __global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ lo
                                                     uint64_t seed, const uint32_t* dev_round, uint32_t round,
                                                     uint32_t slot, uint32_t tag, uint32_t seq_base, int32_t* out,
                                                     int out_stride) {
+  ULB_TRACE_KERNEL(kTrSample, V);
   __shared__ SmemRed<BT> s;
   __shared__ SelSmem sel;
   __shared__ RowStats st;
@@ -480,6 +481,7 @@ __global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ lo
 /* stats for np p rows followed by nq q rows */
 __global__ void __launch_bounds__(ST) stats_kernel(const float* __restrict__ p, const float* __restrict__ q, int np,
                                                    int nq, int V, ulb_warp w, RowStats* __restrict__ out) {
+  ULB_TRACE_KERNEL(kTrStats, 0);
   __shared__ SmemRed<ST> s;
   __shared__ SelSmem sel;
   __shared__ RowStats st;
@@ -536,6 +538,7 @@ __global__ void __launch_bounds__(DT) accept_kernel(const float* __restrict__ p,
                                                     ulb_warp w, uint64_t seed, const uint32_t* dev_round,
                                                     uint32_t round, int32_t* out_tokens, int32_t* out_n,
                                                     SpecCommit cm) {
+  ULB_TRACE_KERNEL(kTrAccept, 0);
   __shared__ SmemRed<DT> s;
   __shared__ SelSmem sel;
   __shared__ RowStats st_p, st_q;
@@ -681,6 +684,7 @@ __global__ void __launch_bounds__(RT) tree_children_kernel(const float* __restri
                                                            ulb_warp wp, uint64_t seed,
                                                            const uint32_t* __restrict__ dev_round, int N,
                                                            int32_t* tokens) {
+  ULB_TRACE_KERNEL(kTrTreeChildren, 0);
   __shared__ SmemRed<RT> s;
   __shared__ SelSmem sel;
   __shared__ RowStats st;
@@ -753,6 +757,7 @@ __global__ void __launch_bounds__(DT) tree_decide_kernel(const float* __restrict
                                                          const RowStats* __restrict__ rs, TreeShape t, int V,
                                                          ulb_warp wp, uint64_t seed, const uint32_t* dev_round,
                                                          uint32_t round, TreeOut out, SpecCommit cm) {
+  ULB_TRACE_KERNEL(kTrTreeDecide, 0);
   __shared__ SmemRed<DT> s;
   pdl_wait();
   pdl_trigger();
@@ -1048,3 +1053,5 @@ extern "C" int ulb_spec_accept(ulb_ctx* ctx, const float* p, const float* q, con
   dev_free(c, scratch, bytes);
   return rc;
 }
+
+ULB_TRACE_UNIT(sampling)

@@ -55,6 +55,7 @@ namespace {
 
 __global__ void stage_draft_kernel(int S, int j, int k, const int* __restrict__ hist, int hl, const int* __restrict__ L,
                                    const int* __restrict__ draft, int* rtok, int* rseq, int* rpos) {
+  ULB_TRACE_KERNEL(kTrStageDraft, j);
   pdl_wait();
   pdl_trigger();
   const int rps = j == 0 ? 2 : 1;
@@ -76,6 +77,7 @@ __global__ void stage_draft_kernel(int S, int j, int k, const int* __restrict__ 
 
 __global__ void stage_verify_kernel(int S, int k, const int* __restrict__ hist, int hl, const int* __restrict__ L,
                                     const int* __restrict__ draft, int* rtok, int* rseq, int* rpos) {
+  ULB_TRACE_KERNEL(kTrStageVerify, 0);
   pdl_wait();
   pdl_trigger();
   const int R = k + 1;
@@ -89,6 +91,7 @@ __global__ void stage_verify_kernel(int S, int k, const int* __restrict__ hist, 
 
 __global__ void stage_prefill_kernel(int s, int c0, int n, const int* __restrict__ hist, int hl, int* rtok, int* rseq,
                                      int* rpos) {
+  ULB_TRACE_KERNEL(kTrStagePrefill, 0);
   pdl_wait();
   pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -104,6 +107,7 @@ __global__ void stage_prefill_kernel(int s, int c0, int n, const int* __restrict
 __global__ void stage_tree_draft_kernel(int S, int d, int w, int N, const int* __restrict__ hist, int hl,
                                         const int* __restrict__ L, const int* __restrict__ ttok, int* rtok, int* rseq,
                                         int* rpos, int* rrope, int* rpref, unsigned long long* rmask) {
+  ULB_TRACE_KERNEL(kTrStageTree, d);
   pdl_wait();
   pdl_trigger();
   int per = 1;
@@ -134,6 +138,7 @@ __global__ void stage_tree_draft_kernel(int S, int d, int w, int N, const int* _
 __global__ void stage_tree_verify_kernel(int S, int w, int N, const int* __restrict__ hist, int hl,
                                          const int* __restrict__ L, const int* __restrict__ ttok, int* rtok, int* rseq,
                                          int* rpos, int* rrope, int* rpref, unsigned long long* rmask) {
+  ULB_TRACE_KERNEL(kTrStageTree + 1, 0);
   pdl_wait();
   pdl_trigger();
   const int R = N + 1;
@@ -729,3 +734,5 @@ int ulb_spec_free(ulb_spec* h) {
 }
 
 }  // extern "C"
+
+ULB_TRACE_UNIT(spec)

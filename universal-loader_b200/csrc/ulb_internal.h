@@ -86,13 +86,6 @@ struct Ctx {
   int* tc_cnt = nullptr;               /* kTcCounters arrival counters, zero between launches */
   int tp_rank = 0, tp_world = 1;
   int attn_form = 0; /* ULB_ATTN_AUTO / SPLIT / STREAM */
-  /* hint: up to two byte ranges (weights of GEMVs to come) that the next GEMV launched on the
-     stream prefetches into L2 from its tail; set just before that launch by the forward
-     pass, cleared by every GEMV launch. */
-  const void* pf_ptr = nullptr;
-  size_t pf_bytes = 0;
-  const void* pf2_ptr = nullptr; /* a second range, prefetched after the first */
-  size_t pf2_bytes = 0;
   /* timing of the tensor-parallel all-reduces (on while a round is profiled): a CUDA event
      pair is recorded around each ncclAllReduce, events[2i] before and events[2i+1] after */
   /* host-side bound on waits for a stream holding tensor-parallel collectives (ms, 0 = none):
@@ -103,7 +96,6 @@ struct Ctx {
   std::vector<cudaEvent_t> ar_events;
   size_t ar_used = 0;
 };
-constexpr size_t kPrefetchMaxBytes = (size_t)48 << 20;
 /* fp32 sum over the communicator's ranks, in place, on the context stream */
 int tp_allreduce_sum(Ctx* c, float* buf, size_t n);
 constexpr int kZeroRowHalves = 65536 + 64;
@@ -280,9 +272,106 @@ struct ulb_tensor {
 /* device-side helpers shared by the .cu files */
 #ifdef __CUDACC__
 namespace ulb {
+/*
+ * CTA timeline trace, compiled into trace builds only (-DULB_TRACE, libulb_cuda_trace.so):
+ * each CTA of an instrumented kernel appends one record to a ring in device memory (one ring
+ * per translation unit): the kernel's tag and argument, the CTA index and grid size, and the
+ * global-timer times of the CTA's entry, of the return of its wait for the previous kernel
+ * (griddepcontrol.wait), of the last exit of its warps, and of up to 8 marks of its thread
+ * 0.  ulb_trace_dump_<unit> copies a ring out and clears it.  Product builds compile every
+ * ULB_TRACE_* macro to nothing.
+ */
+enum TraceTag : unsigned {
+  kTrGemv = 1000,       /* + 100 epilogue + 10 n-tiles + fused RMSNorm; argument N */
+  kTrAttnSplit = 2000,  /* + cluster merge + 2 tree; argument head dim */
+  kTrAttnStream = 3000, /* + tiles per CTA; argument head dim */
+  kTrGemmTc = 4000,     /* + epilogue; argument token tile */
+  kTrRowGemv = 5000,    /* + epilogue; argument N */
+  kTrEmbed = 6000,
+  kTrRmsnorm = 6100,
+  kTrAdd = 6200,
+  kTrSample = 7000,
+  kTrStats = 7100,
+  kTrAccept = 7200,
+  kTrTreeChildren = 7300,
+  kTrTreeDecide = 7400,
+  kTrStageDraft = 8000,
+  kTrStageVerify = 8100,
+  kTrStagePrefill = 8200,
+  kTrStageTree = 8300, /* + 1 verify rows, + 50 cache compaction */
+  kTrWaitFlag = 9000,
+};
+#ifdef ULB_TRACE
+struct TraceRec {
+  unsigned tag, cta, grid, arg;
+  unsigned long long t_entry, t_wait, t_exit, pad, mark[8];
+};
+constexpr unsigned kTraceCap = 1u << 18;
+static __device__ TraceRec g_trace[kTraceCap];
+static __device__ unsigned g_trace_n;
+__device__ __forceinline__ unsigned long long trace_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+/* the CTA's record slot (written by thread 0 at entry, read by every warp at exit) */
+__device__ __forceinline__ unsigned& trace_slot() {
+  __shared__ unsigned s;
+  return s;
+}
+struct TraceGuard {
+  __device__ __forceinline__ TraceGuard(unsigned tag, unsigned arg) {
+    if (threadIdx.x == 0) {
+      const unsigned s = atomicAdd(&g_trace_n, 1u) & (kTraceCap - 1);
+      trace_slot() = s;
+      TraceRec& r = g_trace[s];
+      r.tag = tag;
+      r.cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+      r.grid = gridDim.x * gridDim.y * gridDim.z;
+      r.arg = arg;
+      r.t_wait = r.t_exit = 0;
+      for (int k = 0; k < 8; ++k) r.mark[k] = 0;
+      r.t_entry = trace_now();
+    }
+  }
+  __device__ __forceinline__ ~TraceGuard() {
+    /* the slot index is masked: a warp that exits before thread 0 wrote it corrupts at most
+       one record, never memory outside the ring */
+    if ((threadIdx.x & 31) == 0)
+      atomicMax(&g_trace[*(volatile unsigned*)&trace_slot() & (kTraceCap - 1)].t_exit, trace_now());
+  }
+};
+#define ULB_TRACE_KERNEL(tag, arg) ::ulb::TraceGuard ulb_trace_guard_((unsigned)(tag), (unsigned)(arg))
+#define ULB_TRACE_MARK(k)                                                                            \
+  do {                                                                                               \
+    if (threadIdx.x == 0) ::ulb::g_trace[::ulb::trace_slot() & (::ulb::kTraceCap - 1)].mark[k] = ::ulb::trace_now(); \
+  } while (0)
+#define ULB_TRACE_UNIT(NAME)                                                                         \
+  extern "C" __attribute__((visibility("default"))) int ulb_trace_dump_##NAME(void* host, unsigned* n) { \
+    if (cudaDeviceSynchronize() != cudaSuccess) return ULB_ECUDA;                                    \
+    if (cudaMemcpyFromSymbol(n, ::ulb::g_trace_n, sizeof(unsigned)) != cudaSuccess) return ULB_ECUDA; \
+    if (cudaMemcpyFromSymbol(host, ::ulb::g_trace, sizeof(::ulb::g_trace)) != cudaSuccess) return ULB_ECUDA; \
+    const unsigned zero = 0;                                                                         \
+    if (cudaMemcpyToSymbol(::ulb::g_trace_n, &zero, sizeof zero) != cudaSuccess) return ULB_ECUDA;    \
+    return ULB_OK;                                                                                   \
+  }
+#else
+#define ULB_TRACE_KERNEL(tag, arg) ((void)0)
+#define ULB_TRACE_MARK(k) ((void)0)
+#define ULB_TRACE_UNIT(NAME)
+#endif
+
 /* Wait for the preceding kernel in the stream (programmatic dependent launch).  Every
  * kernel calls this before it touches data produced upstream, and before exiting. */
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#ifdef ULB_TRACE
+  if (threadIdx.x == 0) {
+    TraceRec& r = g_trace[trace_slot() & (kTraceCap - 1)];
+    if (r.t_wait == 0) r.t_wait = trace_now();
+  }
+#endif
+}
 /* Allow the next kernel in the stream to begin launching its CTAs. */
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
