@@ -130,7 +130,7 @@ __device__ __forceinline__ void block_colsum(const uint4& bx, float (&s)[4]) {
 template <int J>
 __device__ __forceinline__ void q4k_sm(uint32_t w0, uint32_t w1, uint32_t w2, float& sc, float& mn) {
   uint32_t s, m;
-  if (J < 4) {
+  if constexpr (J < 4) {
     s = (w0 >> (8 * J)) & 63u;
     m = (w1 >> (8 * J)) & 63u;
   } else {
@@ -142,13 +142,12 @@ __device__ __forceinline__ void q4k_sm(uint32_t w0, uint32_t w1, uint32_t w2, fl
 }
 
 /* ------------------------------------------------------------------ epilogues */
-/* lane (g, t) holds, for n-tile nt, rows (g, g + 8) of tokens nt*8 + 2t and + 1 */
+/* lane (g, t) holds, for n-tile nt, rows (g, g + 8) of tokens nt*8 + 2t and + 1; pre: those
+   tokens' cache rows when read ahead (QKV), else NULL */
 template <int EPI>
 __device__ __forceinline__ void epilogue(const EpiArgs& e, int strip, int nt, int g, int t, int M,
-                                         int N, const float4& v) {
-  const int tok0 = nt * 8 + 2 * t;
-  epilogue_token<EPI>(e, strip, g, tok0, M, N, v.x, v.z);
-  epilogue_token<EPI>(e, strip, g, tok0 + 1, M, N, v.y, v.w);
+                                         int N, const float4& v, const EpiRow* pre) {
+  epilogue_pair<EPI>(e, strip, g, nt * 8 + 2 * t, M, N, v, pre);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -364,6 +363,7 @@ template <int QT, int NT> __device__ __forceinline__ __half* smem_x(uint8_t* sme
  * per-thread fmaf chains over float4 j = i*256 + vt, a warp xor tree, and the eight virtual
  * warps in order.  Real warp w takes virtual warps w, w + NW, ... of the M * 8.
  */
+constexpr int kNormMaxRows = 8; /* rows a GEMV normalises itself (one n-tile) */
 template <int NW>
 __device__ __forceinline__ void norm_rows(const float* __restrict__ x, int ldx, const float* __restrict__ gw, int d,
                                           float eps, int M, __half* xs, float* red /* [8 * 8 + 8] */) {
@@ -401,17 +401,25 @@ __device__ __forceinline__ void norm_rows(const float* __restrict__ x, int ldx, 
     red[64 + m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
   }
   __syncthreads();
+  /* a thread takes float4 column j of every row at once (one memory round trip per column
+     it owns, the norm weights loaded once for all rows) */
   const float4* gv = reinterpret_cast<const float4*>(gw);
-  for (int idx = threadIdx.x; idx < M * n4; idx += NW * 32) {
-    const int m = idx / n4, j = idx - m * n4;
-    const float r = red[64 + m];
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(x + (size_t)m * ldx) + j);
+  for (int j = threadIdx.x; j < n4; j += NW * 32) {
     const float4 gg = __ldg(gv + j);
-    __half2* o2 = reinterpret_cast<__half2*>(xs + (size_t)m * d) + 2 * j;
-    o2[0] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v.x, r), gg.x)),
-                           __float2half_rn(__fmul_rn(__fmul_rn(v.y, r), gg.y)));
-    o2[1] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v.z, r), gg.z)),
-                           __float2half_rn(__fmul_rn(__fmul_rn(v.w, r), gg.w)));
+    float4 v[kNormMaxRows];
+#pragma unroll
+    for (int m = 0; m < kNormMaxRows; ++m)
+      if (m < M) v[m] = __ldcg(reinterpret_cast<const float4*>(x + (size_t)m * ldx) + j);
+#pragma unroll
+    for (int m = 0; m < kNormMaxRows; ++m)
+      if (m < M) {
+        const float r = red[64 + m];
+        __half2* o2 = reinterpret_cast<__half2*>(xs + (size_t)m * d) + 2 * j;
+        o2[0] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v[m].x, r), gg.x)),
+                               __float2half_rn(__fmul_rn(__fmul_rn(v[m].y, r), gg.y)));
+        o2[1] = __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(v[m].z, r), gg.z)),
+                               __float2half_rn(__fmul_rn(__fmul_rn(v[m].w, r), gg.w)));
+      }
   }
   __syncthreads();
 }
@@ -471,6 +479,19 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
 #pragma unroll
   for (int i = 0; i < D; ++i)
     if (i < n) ring[i].load(src + (size_t)i * TB + lane * 16, src + (size_t)i * TB + WTile<QT>::MO + g * 16);
+  /* QKV with one n-tile: the lane's two tokens' cache rows are read now, before the wait (see
+     EpiRow), so the epilogue pays one table lookup instead of a chain of them */
+  constexpr bool kPreRows = EPI == EPI_QKV && NT == 1;
+  EpiRow pre[NT][2];
+  if (kPreRows) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int tok = nt * 8 + 2 * t + i;
+        pre[nt][i] = tok < M ? epi_row(ea, tok) : EpiRow{-1, 0, 0};
+      }
+  }
   if (tid < W) wcnt[tid] = 0;
   if (!sync()) return;
   const XIn xin = prep();
@@ -524,8 +545,10 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
         }
       }
     }
+    ULB_TRACE_MARK_MAX(2);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) epilogue<EPI>(ea, (int)s, nt, g, t, M, N, v[nt]);
+    for (int nt = 0; nt < NT; ++nt) epilogue<EPI>(ea, (int)s, nt, g, t, M, N, v[nt], kPreRows ? pre[nt] : nullptr);
+    ULB_TRACE_MARK_MAX(3);
   };
 
   uint32_t s = first_strip;
@@ -571,6 +594,7 @@ __device__ __forceinline__ void gemv_body(const GemvStep& S, uint8_t* smem, uint
     }
 #undef ULB_GEMV_NEXT
   ULB_TRACE_MARK(1);
+  ULB_TRACE_MARK_MAX(4);
   if (kt != 0) flush(s); /* the range ends inside strip s */
 }
 

@@ -346,6 +346,12 @@ struct TraceGuard {
   do {                                                                                               \
     if (threadIdx.x == 0) ::ulb::g_trace[::ulb::trace_slot() & (::ulb::kTraceCap - 1)].mark[k] = ::ulb::trace_now(); \
   } while (0)
+/* the latest time any warp of the CTA reaches this point (lane 0 of each warp that does) */
+#define ULB_TRACE_MARK_MAX(k)                                                                        \
+  do {                                                                                               \
+    if ((threadIdx.x & 31) == 0)                                                                     \
+      atomicMax(&::ulb::g_trace[*(volatile unsigned*)&::ulb::trace_slot() & (::ulb::kTraceCap - 1)].mark[k], ::ulb::trace_now()); \
+  } while (0)
 #define ULB_TRACE_UNIT(NAME)                                                                         \
   extern "C" __attribute__((visibility("default"))) int ulb_trace_dump_##NAME(void* host, unsigned* n) { \
     if (cudaDeviceSynchronize() != cudaSuccess) return ULB_ECUDA;                                    \
@@ -358,6 +364,7 @@ struct TraceGuard {
 #else
 #define ULB_TRACE_KERNEL(tag, arg) ((void)0)
 #define ULB_TRACE_MARK(k) ((void)0)
+#define ULB_TRACE_MARK_MAX(k) ((void)0)
 #define ULB_TRACE_UNIT(NAME)
 #endif
 
