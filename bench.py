@@ -23,7 +23,7 @@ headline line:
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload c2|c4|c5] [--extras auto|none|c4|c5|c4,c5]
   python bench.py --mode ops [--only CASE]     the config-3 kernel sweep
-  python bench.py --mode trace                 the CTA timeline of one C2 round
+  python bench.py --mode trace [--workload c4] the CTA timeline of one C2 (C4) round
 """
 import argparse
 import json
@@ -917,14 +917,19 @@ def trace_launches(rings):
     rec = np.concatenate(live)
     rec = rec[rec["t_entry"] >= t_min]
     rec = rec[np.argsort(rec["t_entry"], kind="stable")]
-    launches, cur, seen = [], None, set()
+    # a record joins the open launch of its kernel (tag, argument, grid) unless that launch
+    # already holds its CTA index or is full; under programmatic dependent launch at most two
+    # consecutive launches overlap, and consecutive launches of one kernel do not
+    launches, open_l = [], {}
     for x in rec:
         key = (int(x["tag"]), int(x["arg"]), int(x["grid"]))
-        if cur is None or cur["key"] != key or int(x["cta"]) in seen or len(seen) >= key[2]:
-            cur, seen = {"key": key, "recs": []}, set()
+        cur = open_l.get(key)
+        if cur is None or int(x["cta"]) in cur["seen"] or len(cur["seen"]) >= key[2]:
+            cur = {"key": key, "recs": [], "seen": set()}
+            open_l[key] = cur
             launches.append(cur)
         cur["recs"].append(x)
-        seen.add(int(x["cta"]))
+        cur["seen"].add(int(x["cta"]))
     out = []
     for l in launches:
         r = np.array(l["recs"], dtype=rec.dtype)
@@ -933,6 +938,7 @@ def trace_launches(rings):
         out.append({"name": trace_kernel_name(*l["key"][:2]), "ctas": len(r), "entry": int(r["t_entry"].min()),
                     "wait": int(waits.max()) if len(waits) else 0, "exit": int(r["t_exit"].max()),
                     "last_marks": [int(m) - int(last["t_wait"]) if m and last["t_wait"] else None for m in last["mark"]]})
+    out.sort(key=lambda l: l["exit"])  # a kernel completes after the one before it in the stream
     return out
 
 
@@ -966,22 +972,28 @@ def run_trace(args):
             rings.append(buf)
         return rings
 
-    tp, dp = ensure_models(0, lambda: None)
+    c4 = args.workload == "c4"
+    tp, dp = ensure_models(0, lambda: None, *((C4_TARGET, C4_DRAFT) if c4 else ()))
     api = vg.InferenceAPI()
     if not api.load_model(tp) or not api.load_draft_model(dp):
         return 1
     api.enable_speculative_decoding(True)
-    api.set_speculation_length(K_SPEC)
+    api.set_speculation_length(C4_K if c4 else K_SPEC)
     cfg = vg.GenerationConfig()
-    cfg.max_tokens = 64
-    cfg.temperature = 0.0
-    cfg.do_sample = False
-    prompt = prompt_for(0)
+    if c4:  # config 4 on one GPU: 64 sequences, T = 0.8, top_p = 0.9, a few rounds
+        cfg.max_tokens, cfg.temperature, cfg.top_p, cfg.top_k, cfg.do_sample, cfg.seed = 24, 0.8, 0.9, 0, True, 0
+        prompt = c4_prompts()
+    else:
+        cfg.max_tokens, cfg.temperature, cfg.do_sample = 64, 0.0, False
+        prompt = prompt_for(0)
     for _ in range(max(1, args.warmup)):
         api.generate_tokens(prompt, cfg)
     dump()
     api.generate_tokens(prompt, cfg)
-    L = trace_launches(dump())
+    rings = dump()
+    if args.trace_dump:  # the raw records, for analyses of one's own
+        np.savez_compressed(args.trace_dump, **{u: r for u, r in zip(TRACE_UNITS, rings)})
+    L = trace_launches(rings)
     acc = [i for i, l in enumerate(L) if l["name"] == "accept"]
     if len(acc) < 2:
         print(json.dumps({"mode": "trace", "error": "fewer than two rounds in the trace"}))
@@ -1012,7 +1024,9 @@ def run_trace(args):
                  mean_after_wait_us=round(g["after_wait_us"] / n, 2), last_cta_marks_after_wait_us=means)
         phases[g["phase"]] = round(phases.get(g["phase"], 0.0) + g["exposed_us"], 1)
         kernels.append(g)
-    print(json.dumps({"mode": "trace", "workload": "c2 round (k=5, T=0), 64-token generation after a 512-token prompt",
+    wl = ("c4 round (64 sequences, k=8, T=0.8, top_p=0.9), 24-token generation" if c4 else
+          "c2 round (k=5, T=0), 64-token generation after a 512-token prompt")
+    print(json.dumps({"mode": "trace", "workload": wl,
                       "round_us": round((rnd[-1]["exit"] - L[a - 1]["exit"]) / 1e3, 1), "launches": len(rnd),
                       "phases_us": phases, "kernels": kernels}), flush=True)
     return 0
@@ -1169,6 +1183,7 @@ def main():
     ap.add_argument("--mode", default="spec", choices=["spec", "ops", "trace"],
                     help="spec: the C2 speculative workload (default); ops: the config-3 kernel sweep; "
                          "trace: the CTA timeline of one C2 round (trace build)")
+    ap.add_argument("--trace-dump", default="", help="trace mode: also save the raw CTA records (.npz)")
     ap.add_argument("--only", default="", help="ops mode: run one case, e.g. q4_0:11008x4096:m5 or accept")
     ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5", "pgtest"],
                     help="c2: 7B + TinyLlama, B=1 (default, the headline); c4: Llama-3-8B + 3.2-1B, 64 sequences "
