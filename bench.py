@@ -1122,7 +1122,7 @@ def run_ops(args):
     # (128256) at T = 0.8, top_p = 0.9; draft sampling of 64 rows at config 4's warp
     for (label, V, warps) in (("accept", 32000, ((1.0, 0, 1.0), (0.0, 0, 1.0))),
                               ("accept_c4", 128256, ((0.8, 0, 0.9),))):
-        if args.only and not label.startswith(args.only) and not args.only.startswith(label):
+        if args.only and not label.startswith(args.only) and args.only.split(":")[0] != label:
             continue
         B, k = 64, 8
         pl = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)

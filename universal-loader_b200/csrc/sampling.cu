@@ -265,6 +265,7 @@ __device__ uint32_t select_cut(const float* l, int V, float iT, float mx, uint32
     }
   });
   tot = block_sum_u64(tot, s);
+  ULB_TRACE_MARK(4);
   const unsigned long long R = MASS ? (unsigned long long)ulb_topp_target(top_p, tot) : (unsigned long long)k;
   /* the cut bin: block scan of the bins' weights (each thread a contiguous group of bins) */
   constexpr int PER = kSelBins / BT > 0 ? kSelBins / BT : 1;
@@ -295,6 +296,7 @@ __device__ uint32_t select_cut(const float* l, int V, float iT, float mx, uint32
     }
   }
   __syncthreads();
+  ULB_TRACE_MARK(5);
   const int cut = sel.bin;
   const unsigned long long before = sel.before;
   /* the cut bin's elements into shared memory */
@@ -310,6 +312,7 @@ __device__ uint32_t select_cut(const float* l, int V, float iT, float mx, uint32
     }
   });
   __syncthreads();
+  ULB_TRACE_MARK(6);
   const int n = sel.n;
   if (n <= kSelCap) {
     return radix_select<BT>([&](auto f) {
@@ -330,6 +333,7 @@ template <int BT>
 __device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowStats& out, SmemRed<BT>& s,
                                   SelSmem& sel) {
   const int amax = block_argmax(l, V, s);
+  ULB_TRACE_MARK(0);
   if (!(w.temperature > 0.f)) {
     if (threadIdx.x == 0) { out.mx = l[amax]; out.thr = -INFINITY; out.Z = 1.0; out.amax = amax; }
     return;
@@ -339,12 +343,14 @@ __device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowS
   uint32_t key_lo = 0;
   if (w.top_k > 0 && w.top_k < V) key_lo = select_cut<BT, false>(l, V, iT, mx, 0u, w.top_k, 0.f, s, sel);
   if (w.top_p > 0.f && w.top_p < 1.f) key_lo = select_cut<BT, true>(l, V, iT, mx, key_lo, 0, w.top_p, s, sel);
+  ULB_TRACE_MARK(1);
   double zs = 0.0;
   row_for_each<BT>(l, V, [&](int, float x) {
     const float z = zof(x, iT);
     if (fkey(z) >= key_lo) zs += (double)ulb_warp_exp(__fsub_rn(z, mx));
   });
   const double Z = block_sum_d(zs, s);
+  ULB_TRACE_MARK(2);
   if (threadIdx.x == 0) {
     out.mx = mx;
     out.thr = key_lo == 0 ? -INFINITY : unkey(key_lo);
@@ -475,6 +481,7 @@ __global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ lo
     const RowStats stc = st;
     tok = block_inv_cdf(V, u, [&](int i) { return warped_e(l, i, iT, stc); }, s, nullptr);
   }
+  ULB_TRACE_MARK(3);
   if (threadIdx.x == 0) out[(size_t)row * out_stride] = tok;
 }
 
