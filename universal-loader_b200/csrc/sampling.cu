@@ -18,10 +18,11 @@
  * same logits give the same kept set on host and device.
  *
  * Selection of the top-k / top-p cut (B200): one pass over the row histograms it into 1024
- * bins of max z - z (width 1/32) with integer atomics, which spread over many bins (no
- * contended fp64 atomics); the bin holding the cut is found by a block scan, a second pass
- * compacts that bin's elements into shared memory, and a radix select over the compacted
- * candidates finds the exact key.  Only a bin too large for the candidate buffer (a very flat
+ * bins of max z - z (the row's range spread over the bins, at least 32 bins per unit) with
+ * integer atomics, which spread over many bins (no contended fp64 atomics); the bin holding
+ * the cut is found by a block scan, a second pass compacts that bin's elements into shared
+ * memory (one counter update per warp), and a sort of the candidates with a scan of their
+ * weights finds the exact key.  Only a bin too large for the candidate buffer (a very flat
  * row) falls back to a radix select over the whole row.  The row is read from HBM once (the
  * argmax pass); the later passes find it in L2.
  *
@@ -137,6 +138,19 @@ struct SelSmem {
 };
 
 template <int BT>
+__device__ float block_min(float v, SmemRed<BT>& s) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) s.f[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = s.f[0];
+#pragma unroll
+  for (int w = 1; w < BT / 32; ++w) r = fminf(r, s.f[w]);
+  return r;
+}
+
+template <int BT>
 __device__ float block_max(float v, SmemRed<BT>& s) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -163,14 +177,16 @@ __device__ double block_sum_d(double v, SmemRed<BT>& s) {
   return r;
 }
 
-/* argmax, lowest index on ties */
+/* argmax, lowest index on ties; *lmin (if given): the smallest element, in the same pass */
 template <int BT>
-__device__ int block_argmax(const float* l, int V, SmemRed<BT>& s) {
-  float bv = -INFINITY;
+__device__ int block_argmax(const float* l, int V, SmemRed<BT>& s, float* lmin = nullptr) {
+  float bv = -INFINITY, mn = INFINITY;
   int bi = 0x7fffffff;
   row_for_each<BT>(l, V, [&](int i, float x) {
     if (x > bv || (x == bv && i < bi)) { bv = x; bi = i; }
+    mn = fminf(mn, x);
   });
+  if (lmin) *lmin = block_min(mn, s);
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -235,10 +251,82 @@ __device__ uint32_t radix_select(Visit visit, unsigned long long R, SmemRed<BT>&
   return prefix;
 }
 
-/* bin of z: floor((max z - z) * 32), clamped to the last bin (-inf and NaN land there) */
-__device__ __forceinline__ int sel_bin(float mx, float z) {
-  const float d = __fmul_rn(__fsub_rn(mx, z), kSelBinScale);
+/* bin of z: floor((max z - z) * scale), clamped to the last bin (-inf and NaN land there).
+   scale spreads the row's range over the bins (at least kSelBinScale bins per unit), so even a
+   flat row puts few elements in a bin: the bins only locate the cut, whose key is then found
+   exactly among the cut bin's elements */
+__device__ __forceinline__ int sel_bin(float mx, float z, float scale) {
+  const float d = __fmul_rn(__fsub_rn(mx, z), scale);
   return d < (float)(kSelBins - 1) ? (int)d : kSelBins - 1;
+}
+__device__ __forceinline__ float sel_scale(float mx, float zmin) {
+  const float range = __fsub_rn(mx, zmin);
+  const float sc = range > 0.f && range < INFINITY ? __fdiv_rn((float)(kSelBins - 1), range) : kSelBinScale;
+  return fmaxf(sc, kSelBinScale);
+}
+
+/*
+ * The key t of the cut among n (key, weight) candidates in shared memory: sorted by key,
+ * largest first (a bitonic sort), the first whose cumulative weight reaches R, so that the
+ * weight of the keys above t is below R and that of the keys from t up reaches it.  Weights
+ * add as integers: the result does not depend on the order of equal keys.
+ */
+template <int BT>
+__device__ uint32_t sorted_cut(uint32_t* ck, unsigned long long* cw, int n, unsigned long long R, SmemRed<BT>& s) {
+  int N = 1;
+  while (N < n) N <<= 1;
+  for (int i = n + threadIdx.x; i < N; i += BT) { /* padding sorts last and weighs nothing */
+    ck[i] = 0u;
+    cw[i] = 0ull;
+  }
+  __syncthreads();
+  for (int k = 2; k <= N; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < N; i += BT) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const bool desc = (i & k) == 0; /* descending runs first: the whole array ends descending */
+          const uint32_t a = ck[i], b = ck[ixj];
+          if (desc ? a < b : a > b) {
+            ck[i] = b;
+            ck[ixj] = a;
+            const unsigned long long t = cw[i];
+            cw[i] = cw[ixj];
+            cw[ixj] = t;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  /* prefix sums of the weights in sorted order: thread t owns a contiguous run of per items */
+  const int per = (N + BT - 1) / BT, i0 = threadIdx.x * per;
+  unsigned long long mine = 0;
+  for (int j = 0; j < per; ++j)
+    if (i0 + j < N) mine += cw[i0 + j];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned long long inc = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) s.u[warp] = inc;
+  if (threadIdx.x == 0) s.prefix = ck[0];
+  __syncthreads();
+  unsigned long long cum = inc - mine;
+  for (int w = 0; w < warp; ++w) cum += s.u[w];
+  if (cum < R && cum + mine >= R) /* exactly one thread holds the crossing */
+    for (int j = 0; j < per && i0 + j < N; ++j) {
+      if (cum + cw[i0 + j] >= R) {
+        s.prefix = ck[i0 + j];
+        break;
+      }
+      cum += cw[i0 + j];
+    }
+  __syncthreads();
+  const uint32_t t = s.prefix;
+  __syncthreads();
+  return t;
 }
 
 /*
@@ -247,8 +335,8 @@ __device__ __forceinline__ int sel_bin(float mx, float z) {
  * where R = k (count) or ulb_topp_target(top_p, total mass) (MASS).
  */
 template <int BT, bool MASS>
-__device__ uint32_t select_cut(const float* l, int V, float iT, float mx, uint32_t key_lo, int k, float top_p,
-                               SmemRed<BT>& s, SelSmem& sel) {
+__device__ uint32_t select_cut(const float* l, int V, float iT, float mx, float scale, uint32_t key_lo, int k,
+                               float top_p, SmemRed<BT>& s, SelSmem& sel) {
   auto weight = [&](float z) -> unsigned long long {
     return MASS ? (unsigned long long)ulb_mass_fix(ulb_warp_exp(__fsub_rn(z, mx))) : 1ull;
   };
@@ -261,7 +349,7 @@ __device__ uint32_t select_cut(const float* l, int V, float iT, float mx, uint32
     if (fkey(z) >= key_lo) {
       const unsigned long long w = weight(z);
       tot += w;
-      atomicAdd(&sel.bw[sel_bin(mx, z)], w);
+      atomicAdd(&sel.bw[sel_bin(mx, z, scale)], w);
     }
   });
   tot = block_sum_u64(tot, s);
@@ -299,26 +387,32 @@ __device__ uint32_t select_cut(const float* l, int V, float iT, float mx, uint32
   ULB_TRACE_MARK(5);
   const int cut = sel.bin;
   const unsigned long long before = sel.before;
-  /* the cut bin's elements into shared memory */
+  /* the cut bin's elements into shared memory (one slot counter update per warp and element
+     step: the lanes that hold a candidate take consecutive slots) */
   row_for_each<BT>(l, V, [&](int, float x) {
     const float z = zof(x, iT);
     const uint32_t key = fkey(z);
-    if (key >= key_lo && sel_bin(mx, z) == cut) {
-      const int slot = atomicAdd(&sel.n, 1);
-      if (slot < kSelCap) {
-        sel.ck[slot] = key;
-        sel.cw[slot] = weight(z);
+    const bool hit = key >= key_lo && sel_bin(mx, z, scale) == cut;
+    const unsigned act = __activemask();
+    const unsigned m = __ballot_sync(act, hit);
+    if (m) {
+      const int leader = __ffs(m) - 1, lane = threadIdx.x & 31;
+      int base = 0;
+      if (lane == leader) base = atomicAdd(&sel.n, __popc(m));
+      base = __shfl_sync(act, base, leader);
+      if (hit) {
+        const int slot = base + __popc(m & ((1u << lane) - 1u));
+        if (slot < kSelCap) {
+          sel.ck[slot] = key;
+          sel.cw[slot] = weight(z);
+        }
       }
     }
   });
   __syncthreads();
   ULB_TRACE_MARK(6);
   const int n = sel.n;
-  if (n <= kSelCap) {
-    return radix_select<BT>([&](auto f) {
-      for (int j = threadIdx.x; j < n; j += BT) f(sel.ck[j], sel.cw[j]);
-    }, R - before, s);
-  }
+  if (n <= kSelCap) return sorted_cut<BT>(sel.ck, sel.cw, n, R - before, s);
   /* a very flat row: the cut bin does not fit, select over the whole row */
   return radix_select<BT>([&](auto f) {
     row_for_each<BT>(l, V, [&](int, float x) {
@@ -332,7 +426,8 @@ __device__ uint32_t select_cut(const float* l, int V, float iT, float mx, uint32
 template <int BT>
 __device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowStats& out, SmemRed<BT>& s,
                                   SelSmem& sel) {
-  const int amax = block_argmax(l, V, s);
+  float lmin;
+  const int amax = block_argmax(l, V, s, &lmin);
   ULB_TRACE_MARK(0);
   if (!(w.temperature > 0.f)) {
     if (threadIdx.x == 0) { out.mx = l[amax]; out.thr = -INFINITY; out.Z = 1.0; out.amax = amax; }
@@ -340,9 +435,11 @@ __device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowS
   }
   const float iT = __fdiv_rn(1.0f, w.temperature); /* inverse temperature */
   const float mx = zof(l[amax], iT); /* scaling by 1/T > 0 is monotone: max z = z of the max logit */
+  const float scale = sel_scale(mx, zof(lmin, iT));
   uint32_t key_lo = 0;
-  if (w.top_k > 0 && w.top_k < V) key_lo = select_cut<BT, false>(l, V, iT, mx, 0u, w.top_k, 0.f, s, sel);
-  if (w.top_p > 0.f && w.top_p < 1.f) key_lo = select_cut<BT, true>(l, V, iT, mx, key_lo, 0, w.top_p, s, sel);
+  if (w.top_k > 0 && w.top_k < V) key_lo = select_cut<BT, false>(l, V, iT, mx, scale, 0u, w.top_k, 0.f, s, sel);
+  if (w.top_p > 0.f && w.top_p < 1.f)
+    key_lo = select_cut<BT, true>(l, V, iT, mx, scale, key_lo, 0, w.top_p, s, sel);
   ULB_TRACE_MARK(1);
   double zs = 0.0;
   row_for_each<BT>(l, V, [&](int, float x) {
