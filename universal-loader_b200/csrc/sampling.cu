@@ -423,7 +423,9 @@ __device__ uint32_t select_cut(const float* l, int V, float iT, float mx, float 
   }, R, s);
 }
 
-template <int BT>
+/* NEED_Z = false: the normaliser is not needed (draft sampling, whose inverse CDF sums the
+   weights itself) and out.Z is left at 0 */
+template <int BT, bool NEED_Z = true>
 __device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowStats& out, SmemRed<BT>& s,
                                   SelSmem& sel) {
   float lmin;
@@ -441,12 +443,15 @@ __device__ void compute_row_stats(const float* l, int V, const ulb_warp& w, RowS
   if (w.top_p > 0.f && w.top_p < 1.f)
     key_lo = select_cut<BT, true>(l, V, iT, mx, scale, key_lo, 0, w.top_p, s, sel);
   ULB_TRACE_MARK(1);
-  double zs = 0.0;
-  row_for_each<BT>(l, V, [&](int, float x) {
-    const float z = zof(x, iT);
-    if (fkey(z) >= key_lo) zs += (double)ulb_warp_exp(__fsub_rn(z, mx));
-  });
-  const double Z = block_sum_d(zs, s);
+  double Z = 0.0;
+  if (NEED_Z) {
+    double zs = 0.0;
+    row_for_each<BT>(l, V, [&](int, float x) {
+      const float z = zof(x, iT);
+      if (fkey(z) >= key_lo) zs += (double)ulb_warp_exp(__fsub_rn(z, mx));
+    });
+    Z = block_sum_d(zs, s);
+  }
   ULB_TRACE_MARK(2);
   if (threadIdx.x == 0) {
     out.mx = mx;
@@ -465,12 +470,13 @@ __device__ __forceinline__ double warped_e(const float* l, int i, float iT, cons
 
 /*
  * Inverse CDF in index order over weights produced by wfun(i) (fp64, >= 0): with W the
- * total weight (per-thread contiguous segments, summed by a scan over the block), returns the
- * smallest i whose cumulative weight exceeds u * W, and W in *total.  One pass over the
+ * total weight, returns the smallest i whose cumulative weight exceeds u * W, and W in
+ * *total.  This form, for rows longer than kInvCdfMax<BT>: per-thread contiguous segments,
+ * summed by a scan over the block.  One pass over the
  * weights plus a scan of the one segment that holds the target.
  */
 template <int BT, typename WF>
-__device__ int block_inv_cdf(int V, float u, WF wfun, SmemRed<BT>& s, double* total) {
+__device__ int block_inv_cdf_seg(int V, float u, WF wfun, SmemRed<BT>& s, double* total) {
   const int seg = (V + BT - 1) / BT;
   const int b0 = threadIdx.x * seg, b1 = min(V, b0 + seg);
   double sum = 0.0;
@@ -542,6 +548,115 @@ __device__ int block_inv_cdf(int V, float u, WF wfun, SmemRed<BT>& s, double* to
   return r;
 }
 
+/*
+ * Inverse CDF in index order, the form for rows of up to kInvCdfMax<BT> weights: each warp owns
+ * a contiguous range of super-chunks (kInvCdfS chunks of 32 consecutive elements) whose
+ * elements its lanes read together (coalesced, lane l the l-th of each chunk); a super-chunk's
+ * weight sum (the lanes' sums, then a fixed butterfly, identical on every lane) is kept by lane
+ * j of the warp for its j-th super-chunk, and the warp's total adds them in order.  A scan of
+ * the warps' totals finds the warp holding the target, a scan of its super-chunk sums the
+ * super-chunk, and a walk over that super-chunk's chunks (their weights computed again, a warp
+ * scan each) the element.  Where the scans' roundings put the target past a range's last
+ * positive weight, that weight's element is taken.
+ */
+constexpr int kInvCdfS = 8; /* chunks per super-chunk */
+template <int BT> constexpr int kInvCdfMax = (BT / 32) * 32 * kInvCdfS * 32;
+template <int BT, typename WF>
+__device__ int block_inv_cdf_chunked(int V, float u, WF wfun, SmemRed<BT>& s, double* total) {
+  constexpr int NW = BT / 32, SCE = kInvCdfS * 32; /* warps, elements per super-chunk */
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nsc = (V + SCE - 1) / SCE, spw = (nsc + NW - 1) / NW; /* super-chunks, per warp (<= 32) */
+  const int s0 = warp * spw, s1 = min(nsc, s0 + spw);
+  double mine = 0.0, wtot = 0.0;
+  for (int sc = s0; sc < s1; ++sc) { /* warp-uniform */
+    double v[kInvCdfS];
+#pragma unroll
+    for (int k = 0; k < kInvCdfS; ++k) {
+      const int i = sc * SCE + k * 32 + lane;
+      v[k] = i < V ? wfun(i) : 0.0;
+    }
+    double t = 0.0;
+#pragma unroll
+    for (int k = 0; k < kInvCdfS; ++k) t += v[k];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (sc - s0 == lane) mine = t;
+    wtot += t;
+  }
+  __syncthreads();
+  if (lane == 0) s.d[warp] = wtot;
+  if (threadIdx.x == 0) s.found = 0x7fffffff;
+  __syncthreads();
+  double W = 0.0, before = 0.0;
+  for (int w2 = 0; w2 < NW; ++w2) {
+    if (w2 == warp) before = W;
+    W += s.d[w2];
+  }
+  const double target = (double)u * W;
+  if (wtot > 0.0 && before <= target && target < before + wtot) { /* this warp holds the target */
+    double c = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double t = __shfl_up_sync(0xffffffffu, c, o);
+      if (lane >= o) c += t;
+    }
+    const unsigned pos = __ballot_sync(0xffffffffu, mine > 0.0);
+    const unsigned hit = __ballot_sync(0xffffffffu, mine > 0.0 && before + c > target);
+    int js;
+    double base;
+    if (hit) {
+      js = __ffs(hit) - 1;
+      base = before + __shfl_sync(0xffffffffu, c - mine, js); /* the super-chunks before it */
+    } else { /* rounding: the last super-chunk with weight, its last positive element */
+      js = pos ? 31 - __clz(pos) : 0;
+      base = -INFINITY;
+    }
+    const int e0 = (s0 + js) * SCE;
+    int found = -1, lastp = -1;
+    for (int k = 0; k < kInvCdfS && found < 0; ++k) {
+      const int i = e0 + k * 32 + lane;
+      const double wv = i < V ? wfun(i) : 0.0;
+      double cc = wv;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(0xffffffffu, cc, o);
+        if (lane >= o) cc += t;
+      }
+      const unsigned h = __ballot_sync(0xffffffffu, wv > 0.0 && base + cc > target);
+      const unsigned p = __ballot_sync(0xffffffffu, wv > 0.0);
+      if (p) lastp = e0 + k * 32 + 31 - __clz(p);
+      if (h) found = e0 + k * 32 + __ffs(h) - 1;
+      base += __shfl_sync(0xffffffffu, cc, 31);
+    }
+    if (lane == 0) s.found = found >= 0 ? found : (lastp >= 0 ? lastp : 0x7fffffff);
+  }
+  __syncthreads();
+  int r = s.found;
+  if (r == 0x7fffffff) { /* target at/above the total through rounding: last positive weight */
+    __syncthreads();
+    int last = -1;
+    for (int i = threadIdx.x; i < V; i += BT)
+      if (wfun(i) > 0.0) last = max(last, i);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+    if ((threadIdx.x & 31) == 0) s.i[threadIdx.x >> 5] = last;
+    __syncthreads();
+    r = s.i[0];
+    for (int w2 = 1; w2 < NW; ++w2) r = max(r, s.i[w2]);
+    if (r < 0) r = 0;
+  }
+  __syncthreads();
+  if (total) *total = W;
+  return r;
+}
+
+/* the inverse CDF of a row (see the two forms) */
+template <int BT, typename WF>
+__device__ int block_inv_cdf(int V, float u, WF wfun, SmemRed<BT>& s, double* total) {
+  if (V <= kInvCdfMax<BT>) return block_inv_cdf_chunked<BT>(V, u, wfun, s, total);
+  return block_inv_cdf_seg<BT>(V, u, wfun, s, total);
+}
+
 __device__ __forceinline__ float rng_u(uint64_t seed, uint32_t round, uint32_t seq, uint32_t slot, uint32_t tag) {
   return ulb_uniform(seed, round, seq, slot, tag);
 }
@@ -565,7 +680,7 @@ __global__ void __launch_bounds__(BT) sample_kernel(const float* __restrict__ lo
   pdl_trigger();
   const int row = blockIdx.x;
   const float* l = logits + (size_t)row * ld;
-  compute_row_stats(l, V, w, st, s, sel);
+  compute_row_stats<BT, false>(l, V, w, st, s, sel);
   __syncthreads();
   int tok;
   if (!(w.temperature > 0.f)) {
