@@ -148,6 +148,47 @@ __device__ __forceinline__ void epilogue_token(const EpiArgs& e, int strip, int 
   }
 }
 
+/* the tensor-core GEMM's epilogue of NTOK consecutive tokens tok0 .. of rows g (va) and g + 8
+   (vb) of strip `strip`; rows: the tokens' cache rows (QKV), read ahead into shared memory.
+   Every load of the group is issued before any store. */
+template <int EPI, int NTOK>
+__device__ __forceinline__ void epilogue_tokens(const EpiArgs& e, int strip, int g, int tok0, int M, int N,
+                                                const float (&va)[NTOK], const float (&vb)[NTOK], const EpiRow* rows) {
+  if (EPI == EPI_RESID) {
+    const int r0 = strip * 16 + g, r1 = r0 + 8;
+    const bool c0 = r0 < N, c1 = r1 < N;
+    float a0[NTOK], a1[NTOK];
+#pragma unroll
+    for (int i = 0; i < NTOK; ++i) {
+      const bool t = tok0 + i < M;
+      const float* p = e.y + (size_t)(tok0 + i) * e.ldy + r0;
+      a0[i] = t && c0 ? __ldcg(p) : 0.f;
+      a1[i] = t && c1 ? __ldcg(p + 8) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < NTOK; ++i) {
+      if (tok0 + i >= M) continue;
+      float* p = e.y + (size_t)(tok0 + i) * e.ldy + r0;
+      if (c0) p[0] = a0[i] + va[i];
+      if (c1) p[8] = a1[i] + vb[i];
+    }
+  } else if (EPI == EPI_QKV) {
+    int tk[NTOK];
+    bool ok[NTOK];
+    EpiRow r[NTOK];
+#pragma unroll
+    for (int i = 0; i < NTOK; ++i) {
+      tk[i] = tok0 + i;
+      ok[i] = tok0 + i < M;
+      r[i] = rows[i];
+    }
+    qkv_tokens<NTOK>(e, strip, g, tk, r, ok, va, vb);
+  } else {
+#pragma unroll
+    for (int i = 0; i < NTOK; ++i) epilogue_token<EPI>(e, strip, g, tok0 + i, M, N, va[i], vb[i]);
+  }
+}
+
 /* the GEMV's epilogue of one lane's two tokens tok0, tok0 + 1 (v = (tok0 row g, tok0 + 1 row g,
    tok0 row g + 8, tok0 + 1 row g + 8)); pre: their rows, read before the kernel's wait (QKV),
    or NULL.  Every load of the pair is issued before any store. */

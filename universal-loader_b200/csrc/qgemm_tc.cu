@@ -222,6 +222,7 @@ __global__ void __launch_bounds__(TCW * 32, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_raw[RT], free_raw[RT], full_a[SA], free_a[SA], full_b[SB], free_b[SB], acc_full;
   __shared__ uint32_t tmem_base_sh;
+  __shared__ EpiRow srow[EPI == EPI_QKV ? NT : 1]; /* QKV: the tile's tokens' cache rows */
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* const a_ring = smem;
   uint8_t* const b_ring = smem + SA * C::A_BYTES;
@@ -350,6 +351,10 @@ __global__ void __launch_bounds__(TCW * 32, 1)
     }
     pdl_wait(); /* the epilogue reads / writes buffers of earlier kernels */
     pdl_trigger();
+    if (EPI == EPI_QKV) { /* the tile's tokens' cache rows, once for all rows of the tile */
+      for (int t = d; t < NT; t += 256) srow[t] = tok0 + t < a.M ? epi_row(ea, tok0 + t) : EpiRow{-1, 0, 0};
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+    }
   } else if (warp == 10) {
     /* ------------------------------------------------ MMA issue (one lane) */
     pdl_trigger();
@@ -386,11 +391,19 @@ __global__ void __launch_bounds__(TCW * 32, 1)
     const int col0 = ((warp - 2) >> 2) * (NT / 2);  /* its half of the token columns */
     const int row = q4 * 32 + lane;                 /* row of the 128-row tile = TMEM lane */
     const int n = wt * BM + row;                    /* packed row */
+    /* eight tokens at a time, every load of the eight issued before any store */
     auto finish = [&](int c0, const float (&v)[32]) {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float v8 = __shfl_down_sync(0xffffffffu, v[c], 8);
-        if ((lane & 15) < 8) epilogue_token<EPI>(ea, n >> 4, lane & 7, tok0 + c0 + c, a.M, a.N, v[c], v8);
+      for (int cb = 0; cb < 32; cb += 8) {
+        float va[8], vb[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          va[c] = v[cb + c];
+          vb[c] = __shfl_down_sync(0xffffffffu, v[cb + c], 8);
+        }
+        if ((lane & 15) < 8)
+          epilogue_tokens<EPI, 8>(ea, n >> 4, lane & 7, tok0 + c0 + cb, a.M, a.N, va, vb,
+                                  EPI == EPI_QKV ? srow + c0 + cb : nullptr);
       }
     };
     if (a.splits == 1) {
