@@ -39,6 +39,7 @@ constexpr int AW = 4;               /* warps per CTA */
 constexpr int SPLITK = KB * AW;     /* keys per CTA = one split */
 constexpr int MAXSPLIT = 32;        /* capacity <= 8192 */
 constexpr int QT = 16;              /* queries per CTA: one m16 tile */
+constexpr int kSchedMax = 256;      /* streaming form: sequences ordered longest first, up to this many */
 constexpr float kLog2e = 1.44269504088896340736f;
 
 struct AttnParams {
@@ -603,7 +604,29 @@ __global__ void __launch_bounds__(TT * AW * 32, 1)
   extern __shared__ __align__(128) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int tw = warp / AW, bw = warp % AW, ttid = tid - tw * AW * 32; /* tile of the warp, its block */
-  const int mt = blockIdx.x * TT + tw, kvh = blockIdx.y, gi = blockIdx.z;
+  const int mt = blockIdx.x * TT + tw, kvh = blockIdx.y;
+  /* longest walks first: CTA z takes the sequence of rank z by (last position descending,
+     index ascending), so the long sequences start in the first wave and the short ones fill
+     the tail (for up to kSchedMax sequences; beyond that, launch order).  Only the order in
+     which the work runs changes, never a result. */
+  int gi = blockIdx.z;
+  if (p.n_groups <= kSchedMax) {
+    __shared__ int s_len[kSchedMax];
+    __shared__ int s_gi;
+    for (int u = tid; u < p.n_groups; u += TT * AW * 32) s_len[u] = row_pos[u * p.rps + p.rps - 1];
+    __syncthreads();
+    for (int u = tid; u < p.n_groups; u += TT * AW * 32) {
+      const int lu = s_len[u];
+      int rank = 0;
+      for (int u2 = 0; u2 < p.n_groups; ++u2) {
+        const int l2 = s_len[u2];
+        rank += (l2 > lu || (l2 == lu && u2 < u)) ? 1 : 0;
+      }
+      if (rank == (int)blockIdx.z) s_gi = u;
+    }
+    __syncthreads();
+    gi = s_gi;
+  }
   const int Q = p.G * p.rps, q0 = mt * QT, nq = min(QT, Q - q0); /* nq <= 0: no such tile */
   const bool live = nq > 0;
   const int m0 = gi * p.rps;
