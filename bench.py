@@ -886,6 +886,9 @@ def _rand_q4(rng, qt, N, K):
 
 
 TRACE_UNITS = ("qgemv", "attention", "model", "sampling", "spec", "qgemm_tc", "runtime")
+# one CTA record of the trace build (ulb::TraceRec)
+TRACE_REC = [("tag", "<u4"), ("cta", "<u4"), ("grid", "<u4"), ("arg", "<u4"), ("t_entry", "<u8"),
+             ("t_wait", "<u8"), ("t_exit", "<u8"), ("pad", "<u8"), ("mark", "<u8", (8,))]
 TRACE_NAMES = {6000: "embed", 6100: "rmsnorm", 6200: "add", 7000: "sample", 7100: "stats", 7200: "accept",
                7300: "tree_children", 7400: "tree_decide", 8000: "stage_draft", 8100: "stage_verify",
                8200: "stage_prefill", 8300: "stage_tree_draft", 8301: "stage_tree_verify", 8350: "kv_tree_compact",
@@ -958,8 +961,7 @@ def run_trace(args):
     import vulkangguf as vg
     maps = open("/proc/self/maps").read()
     assert "/libulb_cuda.so" not in maps and "libulb_cuda_trace.so" in maps, "the trace build is not the one loaded"
-    rec_t = np.dtype([("tag", "<u4"), ("cta", "<u4"), ("grid", "<u4"), ("arg", "<u4"), ("t_entry", "<u8"),
-                      ("t_wait", "<u8"), ("t_exit", "<u8"), ("pad", "<u8"), ("mark", "<u8", (8,))])
+    rec_t = np.dtype(TRACE_REC)
     cap = 1 << 18
 
     def dump():
